@@ -1,0 +1,130 @@
+/*
+ * recant_b200 -- C ABI of the B200 (sm_100a) GDN + NVFP4 hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*), launches
+ * asynchronously on that stream, never allocates or frees device memory (scratch comes in as
+ * `ws`/`ws_bytes`, sized by the matching *_workspace_size function) and returns a status code.
+ * On a non-zero status, rb2_last_error() returns a message (thread-local).
+ *
+ * Layouts (all contiguous, row-major):
+ *   q, k      [B*T, Hk, dk]     dtype RB2_F32 or RB2_BF16
+ *   v         [B*T, Hv, dv]     same dtype
+ *   g         [B*T, Hv]         float32 (log decay, <= 0)
+ *   beta      [B*T, Hv]         same dtype as q
+ *   o         [B*T, Hv, dv]     same dtype as q
+ *   h0, hT    [N, Hv, dk, dv]   float32 (N = number of sequences)
+ *   cu_seqlens int64 [N+1] on the DEVICE, or NULL for N = B fixed-length sequences of T
+ * Hk must divide Hv (GQA: head h of v uses key/query head h / (Hv/Hk)); dk = dv = 128.
+ */
+#ifndef RECANT_B200_H
+#define RECANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RB2_API __attribute__((visibility("default")))
+#else
+#define RB2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define RB2_OK 0
+#define RB2_EINVAL 1       /* bad argument: shape, dtype, null pointer, misalignment */
+#define RB2_EUNSUPPORTED 2 /* valid but not implemented here (e.g. head dim != 128) */
+#define RB2_ECUDA 3        /* a CUDA launch/runtime error */
+#define RB2_EWORKSPACE 4   /* ws_bytes smaller than the *_workspace_size result */
+#define RB2_ENOMEM 5       /* CUDA reported out of memory */
+#define RB2_EDEVICE 6      /* a kernel reported an error through its device status word */
+
+/* dtypes */
+#define RB2_F32 0
+#define RB2_BF16 1
+
+/* GDN precision paths */
+#define RB2_GDN_AUTO 0  /* bf16 inputs -> tensor-core path, f32 inputs -> exact fp32 path */
+#define RB2_GDN_EXACT 1 /* fp32 CUDA-core arithmetic throughout (fp32 parity path) */
+#define RB2_GDN_FAST 2  /* bf16 tensor-core path (bf16 inputs only) */
+
+RB2_API const char* rb2_last_error(void);
+RB2_API const char* rb2_version(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * Chunked Gated DeltaNet.
+ *
+ * Replaces recant.model.ops.gdn_torch / gdn_fla as registered in GDN_BACKENDS
+ * (recant/model/ops.py:21-60) and called by gdn_core (ops.py:62-67). Semantics are those of
+ * gdn_torch: q and k are L2-normalised per head with eps 1e-6 inside the rsqrt (ops.py:18-19),
+ * q is multiplied by `scale` (dk^-0.5 in the reference, ops.py:27), chunk size 64, state fp32.
+ *
+ * The forward stores everything the backward needs in `ws`; rb2_gdn_bwd must receive the same
+ * `ws` contents and the same arguments. n_seqs = B without cu_seqlens, else len(cu_seqlens)-1
+ * with B == 1.
+ * ------------------------------------------------------------------------------------------- */
+RB2_API size_t rb2_gdn_workspace_size(int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
+                              int dtype, int path);
+
+RB2_API int rb2_gdn_fwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
+                void* o, float* hT, void* ws, size_t ws_bytes, void* stream);
+
+/* Backward of rb2_gdn_fwd (the autograd of gdn_torch, ops.py:21-54): given dO (dtype) and
+ * optionally dhT (fp32, NULL = zero), writes dq, dk [B*T,Hk,dk], dv [B*T,Hv,dv], dbeta (dtype),
+ * dg (fp32) and, when dh0 != NULL, the gradient of the initial state (fp32). */
+RB2_API int rb2_gdn_bwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
+                const void* d_o, const float* dhT, void* dq, void* dk_out, void* dv_out,
+                float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * NVFP4 quantizer: codes/scales/gscale of quantize(rht(x)) (use_rht=1) or quantize(x),
+ * bit-exact with recant/model/nvfp4.py:23-31,59-91 for round-to-nearest; stochastic=1 is the
+ * unbiased rounding of nvfp4.py:62-68 driven by a Philox-4x32-10 stream keyed by `seed`.
+ * Replaces nvfp4.quantize_activation's fast hook (nvfp4.py:139-149, fp4_kernels.quantize_fast
+ * at recant/model/fp4_kernels.py:452-467). x [M,K] with K % 16 == 0, dtype F32 or BF16.
+ * Outputs: codes u8 [M, K/2] (even element in the low nibble), scales e4m3 bytes [M, K/16],
+ * optional scales_blocked (the 128x4 blocked swizzle of nvfp4._to_blocked, nvfp4.py:112-119,
+ * ceil(M/128)*ceil(K/64)*512 bytes, pad bytes zero) and gscale (1 float, device).
+ * ------------------------------------------------------------------------------------------- */
+RB2_API size_t rb2_nvfp4_quantize_workspace_size(int64_t M, int64_t K);
+
+RB2_API int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype, int use_rht, int stochastic,
+                       uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,
+                       float* gscale, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * NVFP4 block-scaled GEMM: out[M,N] = (A . B^T) * gA * gB where A = codes_a [M,K/2] with
+ * blocked scales (128x4 swizzle) and B = codes_b [N,K/2] likewise; fp32 accumulation.
+ * Replaces the GEMM_BACKENDS entries of recant/model/nvfp4.py:108-125 (_gemm_emulated and
+ * _gemm_scaled_mm = torch._scaled_mm on cuBLASLt). out_dtype RB2_F32 or RB2_BF16.
+ * Requires K % 64 == 0.
+ * ------------------------------------------------------------------------------------------- */
+RB2_API size_t rb2_nvfp4_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+
+RB2_API int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                   const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                   int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws,
+                   size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Launch profiler (no counterpart in the reference; measurement support for benchmarks).
+ * While enabled, each kernel launch of this library is bracketed by CUDA events on its stream.
+ * rb2_profile_read waits for them and writes up to max_records (name, milliseconds) pairs; names
+ * are NUL-terminated in slots of name_stride bytes. Not thread-safe.
+ * ------------------------------------------------------------------------------------------- */
+RB2_API int rb2_profile_enable(int max_launches);
+RB2_API int rb2_profile_disable(void);
+RB2_API int rb2_profile_read(int max_records, char* names, size_t name_stride, float* ms);
+RB2_API int rb2_profile_dropped(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RECANT_B200_H */

@@ -44,6 +44,10 @@ def gdn_forward(q, k, v, g, beta, initial_state=None, output_final_state=False,
     out_dtype = q.dtype
     B, T, H, dk = k.shape
     dv = v.shape[-1]
+    if T == 0:  # an empty segment passes its state through unchanged
+        S = torch.zeros(B, H, dk, dv, dtype=dtype) if initial_state is None else initial_state.to(dtype)
+        o = torch.zeros(B, 0, H, dv, dtype=out_dtype) + 0.0 * S.sum()
+        return o, (S.to(torch.float32) if output_final_state else None)
     # head-major working layout [B, H, T, d]
     qh, kh, vh = (t.permute(0, 2, 1, 3).to(dtype) for t in (q, k, v))
     bh, gh = (t.permute(0, 2, 1).to(dtype) for t in (beta, g))

@@ -1,0 +1,99 @@
+"""ctypes binding of the in-tree CUDA library (``recant_b200/_lib/librecant_b200.so``).
+
+The library has a plain C ABI (include/recant_b200.h); this module declares every entry point's
+argument types and turns non-zero status codes into Python exceptions. There is no fallback:
+if the library is missing, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "librecant_b200.so")
+
+OK, EINVAL, EUNSUPPORTED, ECUDA, EWORKSPACE, ENOMEM, EDEVICE = range(7)
+F32, BF16 = 0, 1
+GDN_AUTO, GDN_EXACT, GDN_FAST = 0, 1, 2
+
+_p, _i, _i64, _u64, _sz, _f = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
+
+SIGNATURES = {
+    "rb2_last_error": (C.c_char_p, []),
+    "rb2_version": (C.c_char_p, []),
+    "rb2_gdn_workspace_size": (_sz, [_i64, _i64, _i64, _i, _i, _i, _i, _i, _i]),
+    "rb2_gdn_fwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
+                         _p, _p, _p, _sz, _p]),
+    "rb2_gdn_bwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
+                         _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "rb2_nvfp4_quantize_workspace_size": (_sz, [_i64, _i64]),
+    "rb2_nvfp4_quantize": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p, _sz, _p]),
+    "rb2_nvfp4_gemm_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "rb2_nvfp4_gemm": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _p]),
+    "rb2_profile_enable": (_i, [_i]),
+    "rb2_profile_disable": (_i, []),
+    "rb2_profile_read": (_i, [_i, C.c_char_p, _sz, C.POINTER(C.c_float)]),
+    "rb2_profile_dropped": (_i, []),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class LibraryError(RuntimeError):
+    """A recant_b200 entry point returned a non-zero status."""
+
+
+def lib() -> C.CDLL:
+    """Load the library once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(f"recant_b200 CUDA library not built: {LIB_PATH} is missing "
+                                      "(run `python -m recant_b200.build`)")
+                h = C.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(h, name)
+                    fn.restype, fn.argtypes = res, args
+                _lib = h
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    msg = lib().rb2_last_error().decode(errors="replace")
+    if status == ENOMEM or "out of memory" in msg:
+        import torch
+        raise torch.cuda.OutOfMemoryError(f"recant_b200 {what}: {msg}")
+    raise LibraryError(f"recant_b200 {what} failed (status {status}): {msg}")
+
+
+class LaunchProfiler:
+    """Device time of every library kernel launch between start() and read(), measured with
+    CUDA events recorded on the launching stream."""
+
+    def __init__(self, capacity: int = 4096):
+        self.capacity = capacity
+
+    def start(self):
+        check(lib().rb2_profile_enable(self.capacity), "profile_enable")
+
+    def read(self):
+        lib().rb2_profile_disable()
+        stride = 64
+        names = C.create_string_buffer(self.capacity * stride)
+        ms = (C.c_float * self.capacity)()
+        n = lib().rb2_profile_read(self.capacity, names, stride, ms)
+        if n < 0:
+            check(ECUDA, "profile_read")
+        raw = names.raw
+        out = [(raw[i * stride:(i + 1) * stride].split(b"\0", 1)[0].decode(), float(ms[i])) for i in range(n)]
+        return out, int(lib().rb2_profile_dropped())
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()

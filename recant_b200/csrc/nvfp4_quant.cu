@@ -1,0 +1,242 @@
+// NVFP4 activation quantizer: randomized Hadamard (16-point) + e2m1 codes + e4m3 per-16 scales
+// + fp32 global scale, bit-exact with the reference quantize(rht(x)).
+//
+// Reference semantics (recant/model/nvfp4.py):
+//   rht            :23-31  sign flip by _SIGNS, butterflies with strides 1,2,4,8 as (a+b, a-b),
+//                          x0.25, re-round to the input dtype
+//   quantize       :76-91  s_g = max(|x|, 1e-30) / (6*448); s_b = min((amax16 / 6) / s_g, 448)
+//                          -> e4m3 (RNE); denom = (s8 == 0 ? 1 : s8) * s_g; q = x / denom
+//   _round_codes   :59-71  RN: idx = #{midpoints < |q|} (ties toward zero), +8 when q < 0;
+//                          SR: unbiased choice between the two neighbouring grid points
+//   _pack          :73-74  even element in the low nibble
+//
+// Design (HBM-bound, 2.5625 B/elt algorithmic for bf16): the global amax forces two passes.
+// Pass 1 reads x, transforms each 16-block in registers and reduces the amax to one word.
+// Pass 2 re-reads x in REVERSE block order so that the tail of x that pass 1 left in the
+// 126 MB L2 is consumed first, recomputes the transform and writes codes and scales.
+// One thread owns one 16-element block: a warp covers 512 contiguous elements of a row.
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+
+namespace rb2 {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ void load16(const T* __restrict__ p, float v[16]);
+
+template <>
+__device__ __forceinline__ void load16<float>(const float* __restrict__ p, float v[16]) {
+  const float4* p4 = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4 t = __ldg(p4 + i);
+    v[4 * i + 0] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* __restrict__ p, float v[16]) {
+  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    uint4 t = __ldg(p4 + i);
+    uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[8 * i + 2 * j + 0] = __uint_as_float(w[j] << 16);
+      v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+  }
+}
+
+// The 16-point randomized Hadamard transform of one block, with the reference's exact
+// operation order, followed by re-rounding to the input dtype.
+template <typename T>
+__device__ __forceinline__ void transform16(float v[16], bool rot) {
+  if (rot) {
+    // _SIGNS = [1,1,-1,1,-1,-1,-1,1,1,1,1,1,-1,-1,1,-1]
+    v[2] = -v[2]; v[4] = -v[4]; v[5] = -v[5]; v[6] = -v[6];
+    v[12] = -v[12]; v[13] = -v[13]; v[15] = -v[15];
+#pragma unroll
+    for (int s = 1; s < 16; s <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if ((i & s) == 0) {
+          float a = v[i], b = v[i + s];
+          v[i] = __fadd_rn(a, b);
+          v[i + s] = __fsub_rn(a, b);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], 0.25f);
+    if (sizeof(T) == 2) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+zero_word_kernel(unsigned int* w) { *w = 0u; }
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+amax_kernel(const T* __restrict__ x, int64_t n_blocks, int rot, unsigned int* __restrict__ gmax_bits) {
+  const int64_t b = int64_t(blockIdx.x) * kThreads + threadIdx.x;
+  float m = 0.f;
+  if (b < n_blocks) {
+    float v[16];
+    load16<T>(x + b * 16, v);
+    transform16<T>(v, rot != 0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+  }
+  m = warp_max(m);
+  __shared__ float red[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float r = threadIdx.x < kThreads / 32 ? red[threadIdx.x] : 0.f;
+    r = warp_max(r);
+    // non-negative floats order like their bit patterns
+    if (threadIdx.x == 0 && r > 0.f) atomicMax(gmax_bits, __float_as_uint(r));
+  }
+}
+
+// Philox-4x32-10 counter-based generator (Salmon, Moraes, Dror, Shaw; SC'11).
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += 0x9E3779B9u;
+    k.y += 0xBB67AE85u;
+  }
+  return c;
+}
+
+__device__ __forceinline__ float grid_value(int i) {
+  // e2m1 magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6
+  return i < 4 ? 0.5f * float(i) : (i == 4 ? 2.f : (i == 5 ? 3.f : (i == 6 ? 4.f : 6.f)));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+quant_kernel(const T* __restrict__ x, int64_t n_blocks, int64_t groups, int64_t rows, int rot,
+             int stochastic, uint64_t seed, const unsigned int* __restrict__ gmax_bits,
+             uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+             uint8_t* __restrict__ blocked, float* __restrict__ gscale_out) {
+  // reverse CTA order: consume what pass 1 left in L2 first
+  const int64_t cta = int64_t(gridDim.x) - 1 - blockIdx.x;
+  const int64_t b = cta * kThreads + threadIdx.x;
+  const float gmax = fmaxf(__uint_as_float(*gmax_bits), 1e-30f);
+  const float s_g = __fdiv_rn(gmax, 2688.0f);  // 6 * 448
+  if (blockIdx.x == 0 && threadIdx.x == 0) *gscale_out = s_g;
+  if (b >= n_blocks) return;
+  float v[16];
+  load16<T>(x + b * 16, v);
+  transform16<T>(v, rot != 0);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float s_b = fminf(__fdiv_rn(__fdiv_rn(amax, 6.0f), s_g), 448.0f);
+  const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(s_b, __NV_SATFINITE, __NV_E4M3);
+  const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
+  const float sq = __half2float(__half(hr));
+  const float denom = __fmul_rn(sq == 0.f ? 1.f : sq, s_g);
+
+  uint32_t rnd[16];
+  if (stochastic) {
+    const uint2 key = make_uint2(uint32_t(seed), uint32_t(seed >> 32));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 r = philox4x32_10(make_uint4(uint32_t(b), uint32_t(uint64_t(b) >> 32), uint32_t(j), 0u), key);
+      rnd[4 * j + 0] = r.x; rnd[4 * j + 1] = r.y; rnd[4 * j + 2] = r.z; rnd[4 * j + 3] = r.w;
+    }
+  }
+  uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float q = __fdiv_rn(v[i], denom);
+    const float a = fminf(fabsf(q), 6.0f);
+    int idx;
+    if (stochastic) {
+      int hi = (a > 0.f) + (a > 0.5f) + (a > 1.f) + (a > 1.5f) + (a > 2.f) + (a > 3.f) + (a > 4.f);
+      hi = hi < 1 ? 1 : hi;
+      const float glo = grid_value(hi - 1), ghi = grid_value(hi);
+      const float p = __fdiv_rn(__fsub_rn(a, glo), __fsub_rn(ghi, glo));
+      const float u = float(rnd[i] >> 8) * (1.0f / 16777216.0f);
+      idx = (u < p) ? hi : hi - 1;
+    } else {
+      idx = (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) + (a > 2.5f) + (a > 3.5f) + (a > 5.0f);
+    }
+    const uint32_t code = uint32_t(idx + (q < 0.f ? 8 : 0));
+    packed[i >> 3] |= code << (4 * (i & 7));
+  }
+  reinterpret_cast<uint2*>(codes)[b] = make_uint2(packed[0], packed[1]);
+  scales[b] = uint8_t(s8);
+  if (blocked) {
+    const int64_t r = b / groups, c = b % groups;
+    const int64_t ncb = (groups + 3) / 4;
+    const int64_t off = ((r >> 7) * ncb + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
+    blocked[off] = uint8_t(s8);
+  }
+  (void)rows;
+}
+
+}  // namespace
+}  // namespace rb2
+
+using namespace rb2;
+
+extern "C" size_t rb2_nvfp4_quantize_workspace_size(int64_t M, int64_t K) {
+  (void)M; (void)K;
+  return 256;
+}
+
+extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype, int use_rht,
+                                  int stochastic, uint64_t seed, uint8_t* codes, uint8_t* scales,
+                                  uint8_t* scales_blocked, float* gscale, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  RB2_CHECK_ARG(M > 0 && K > 0 && K % 16 == 0, "nvfp4_quantize: need M, K > 0 and K %% 16 == 0 (M=%lld K=%lld)",
+                (long long)M, (long long)K);
+  RB2_CHECK_ARG(dtype == RB2_F32 || dtype == RB2_BF16, "nvfp4_quantize: dtype must be F32 or BF16");
+  RB2_CHECK_ARG(x && codes && scales && gscale && ws, "nvfp4_quantize: null pointer");
+  RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(codes) & 7) == 0,
+                "nvfp4_quantize: x must be 16-byte and codes 8-byte aligned");
+  if (ws_bytes < rb2_nvfp4_quantize_workspace_size(M, K)) {
+    set_error("nvfp4_quantize: workspace too small");
+    return RB2_EWORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned int* gmax = static_cast<unsigned int*>(ws);
+  const int64_t n_blocks = M * (K / 16);
+  const int64_t groups = K / 16;
+  { ProfScope ps_("nvfp4_zero", s); zero_word_kernel<<<1, 1, 0, s>>>(gmax); }
+  RB2_CHECK_LAUNCH("nvfp4_quantize: zero");
+  if (scales_blocked && (M % 128 != 0 || groups % 4 != 0)) {
+    const size_t nb = size_t((M + 127) / 128) * size_t((groups + 3) / 4) * 512;
+    RB2_CUDA(cudaMemsetAsync(scales_blocked, 0, nb, s), "nvfp4_quantize: clear blocked pads");
+  }
+  const unsigned grid = unsigned((n_blocks + kThreads - 1) / kThreads);
+  if (dtype == RB2_BF16) {
+    auto xp = static_cast<const __nv_bfloat16*>(x);
+    { ProfScope ps_("nvfp4_amax", s); amax_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
+    ProfScope ps_("nvfp4_quant", s);
+    quant_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, n_blocks, groups, M, use_rht, stochastic, seed,
+                                                          gmax, codes, scales, scales_blocked, gscale);
+  } else {
+    auto xp = static_cast<const float*>(x);
+    { ProfScope ps_("nvfp4_amax", s); amax_kernel<float><<<grid, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
+    ProfScope ps_("nvfp4_quant", s);
+    quant_kernel<float><<<grid, kThreads, 0, s>>>(xp, n_blocks, groups, M, use_rht, stochastic, seed,
+                                                  gmax, codes, scales, scales_blocked, gscale);
+  }
+  RB2_CHECK_LAUNCH("nvfp4_quantize");
+  return RB2_OK;
+}

@@ -1,0 +1,135 @@
+"""Chunked Gated DeltaNet op on B200, shaped like the reference backend registry.
+
+Drop-in for ``recant.model.ops``'s GDN backends (recant/model/ops.py:5-10,56-67):
+
+* :func:`gdn_b200` has the signature of ``gdn_torch``/``gdn_fla``
+  ``fn(q, k, v, g, beta, initial_state=None, output_final_state=False) -> (o, final_state|None)``
+  and the semantics of ``gdn_torch`` (qk L2-norm and dk^-0.5 inside the op, chunk 64, fp32 state,
+  o in the input dtype); its backward is a ``torch.autograd.Function`` giving dq, dk, dv, dg,
+  dbeta and d(initial_state).
+* Extensions (defaults keep every reference call site unchanged): ``cu_seqlens`` (int64 [N+1],
+  B == 1, per-sequence state reset, the fla varlen convention), q/k with Hk < Hv heads (GQA
+  without repeat_interleave), ``scale`` and ``path`` ("auto" | "exact" | "fast").
+* :data:`GDN_BACKENDS`, :func:`set_gdn_backend`, :func:`get_gdn_backend`, :func:`gdn_core` mirror
+  ops.py's registry; :func:`register` adds ``'b200'`` to the reference's own registry.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+_PATHS = {"auto": L.GDN_AUTO, "exact": L.GDN_EXACT, "fast": L.GDN_FAST}
+_DT = {torch.float32: L.F32, torch.bfloat16: L.BF16}
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _Problem:
+    def __init__(self, q, k, v, g, beta, initial_state, cu_seqlens, scale, path):
+        if not q.is_cuda:
+            raise ValueError("recant_b200.gdn: inputs must be CUDA tensors (no CPU path)")
+        if q.dim() != 4 or k.shape != q.shape or v.dim() != 4:
+            raise ValueError(f"recant_b200.gdn: q/k must be [B,T,Hk,dk] and v [B,T,Hv,dv]; got "
+                             f"{tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+        B, T, Hk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+        if v.shape[:2] != (B, T) or g.shape != (B, T, Hv) or beta.shape != (B, T, Hv):
+            raise ValueError("recant_b200.gdn: g and beta must be [B,T,Hv] matching v")
+        if q.dtype not in _DT:
+            raise TypeError(f"recant_b200.gdn: dtype {q.dtype} unsupported (float32 or bfloat16)")
+        self.dtype = q.dtype
+        self.B, self.T, self.Hk, self.Hv, self.dk, self.dv = B, T, Hk, Hv, dk, dv
+        if cu_seqlens is not None:
+            if B != 1:
+                raise ValueError("recant_b200.gdn: cu_seqlens requires B == 1")
+            self.n_seqs = cu_seqlens.numel() - 1
+        else:
+            self.n_seqs = B
+        if initial_state is not None and initial_state.shape != (self.n_seqs, Hv, dk, dv):
+            raise ValueError(f"recant_b200.gdn: initial_state must be [{self.n_seqs},{Hv},{dk},{dv}]")
+        self.scale = float(dk ** -0.5 if scale is None else scale)
+        self.path = _PATHS[path]
+        self.ws_bytes = L.lib().rb2_gdn_workspace_size(B, T, self.n_seqs, Hk, Hv, dk, dv, _DT[q.dtype], self.path)
+        if self.ws_bytes == 0:
+            L.check(L.EINVAL if dk == dv == 128 else L.EUNSUPPORTED, "gdn_workspace_size")
+
+    def args(self):
+        return (self.B, self.T, self.n_seqs, self.Hk, self.Hv, self.dk, self.dv, _DT[self.dtype], self.path,
+                self.scale)
+
+
+class _GDNFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, initial_state, cu_seqlens, output_final_state, scale, path):
+        pb = _Problem(q, k, v, g, beta, initial_state, cu_seqlens, scale, path)
+        dt = pb.dtype
+        q, k, v = (t.contiguous() for t in (q, k, v))
+        g = g.to(torch.float32).contiguous()
+        beta_k = beta.to(dt).contiguous()
+        h0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+        cu = None if cu_seqlens is None else cu_seqlens.to(device=q.device, dtype=torch.int64).contiguous()
+        ws = torch.empty(pb.ws_bytes, dtype=torch.uint8, device=q.device)
+        o = torch.empty(pb.B, pb.T, pb.Hv, pb.dv, dtype=dt, device=q.device)
+        hT = torch.empty(pb.n_seqs, pb.Hv, pb.dk, pb.dv, dtype=torch.float32, device=q.device)
+        st = L.lib().rb2_gdn_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta_k), L.ptr(h0), L.ptr(cu),
+                                 *pb.args(), L.ptr(o), L.ptr(hT), L.ptr(ws), pb.ws_bytes, _stream(q.device))
+        L.check(st, "gdn_fwd")
+        ctx.save_for_backward(q, k, v, g, beta_k, h0, cu)
+        ctx.pb, ctx.ws = pb, ws
+        ctx.beta_dtype = beta.dtype
+        ctx.has_h0 = initial_state is not None
+        return o, hT
+
+    @staticmethod
+    def backward(ctx, do, dhT):
+        q, k, v, g, beta, h0, cu = ctx.saved_tensors
+        pb, ws = ctx.pb, ctx.ws
+        do = do.to(pb.dtype).contiguous()
+        dhT = None if dhT is None else dhT.to(torch.float32).contiguous()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        dg = torch.empty_like(g)
+        dbeta = torch.empty_like(beta)
+        dh0 = torch.empty_like(h0) if ctx.has_h0 and ctx.needs_input_grad[5] else None
+        st = L.lib().rb2_gdn_bwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta), L.ptr(h0), L.ptr(cu),
+                                 *pb.args(), L.ptr(do), L.ptr(dhT), L.ptr(dq), L.ptr(dk), L.ptr(dv), L.ptr(dg),
+                                 L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), pb.ws_bytes, _stream(q.device))
+        L.check(st, "gdn_bwd")
+        return dq, dk, dv, dg, dbeta.to(ctx.beta_dtype), dh0, None, None, None, None
+
+
+def gdn_b200(q, k, v, g, beta, initial_state=None, output_final_state=False, *, cu_seqlens=None,
+             scale=None, path="auto"):
+    """Chunked GDN on B200 with gdn_torch's contract (recant/model/ops.py:21-54)."""
+    o, hT = _GDNFunction.apply(q, k, v, g, beta, initial_state, cu_seqlens, output_final_state, scale, path)
+    return o, (hT if output_final_state else None)
+
+
+# ----- registry mirror of recant/model/ops.py:5-10,60-67 -------------------------------------
+GDN_BACKENDS = {"b200": gdn_b200}
+_state = {"gdn": "b200"}
+
+
+def set_gdn_backend(name: str) -> None:
+    if name not in GDN_BACKENDS:
+        raise KeyError(f"unknown GDN backend {name!r}; have {list(GDN_BACKENDS)}")
+    _state["gdn"] = name
+
+
+def get_gdn_backend() -> str:
+    return _state["gdn"]
+
+
+def gdn_core(q, k, v, g, beta, initial_state=None, output_final_state=False):
+    with torch.profiler.record_function("b:gdn"):
+        return GDN_BACKENDS[_state["gdn"]](q, k, v, g, beta, initial_state=initial_state,
+                                           output_final_state=output_final_state)
+
+
+def register(ref_ops_module, select: bool = False) -> None:
+    """Add ``'b200'`` to the reference's ``ops.GDN_BACKENDS`` (and optionally select it)."""
+    ref_ops_module.GDN_BACKENDS["b200"] = gdn_b200
+    if select:
+        ref_ops_module.set_gdn_backend("b200")

@@ -1,0 +1,115 @@
+"""NVFP4 quantizer and block-scaled GEMM on B200, shaped like recant/model/nvfp4.py.
+
+* :class:`FP4Tensor` has the reference's fields (codes u8 [M,K/2], scales float8_e4m3fn [M,K/16],
+  gscale fp32 0-d, shape) plus ``blocked``: the same scales in the 128x4 blocked swizzle that
+  the GEMM consumes (nvfp4._to_blocked, nvfp4.py:112-119), produced by the quantizer itself.
+* :func:`quantize_fast` is the drop-in for ``fp4_kernels.quantize_fast(x, use_rht, stochastic)``
+  (recant/model/fp4_kernels.py:452-467) behind ``nvfp4._fast['quantize']`` (nvfp4.py:139-149):
+  bit-exact codes/scales/gscale for round-to-nearest; stochastic rounding is unbiased.
+* :func:`gemm_b200` is the drop-in for a ``GEMM_BACKENDS`` entry (nvfp4.py:108-125):
+  ``fn(a, b) -> fp32 [M, N] = a . b^T * gA * gB``.
+"""
+from __future__ import annotations
+
+import random
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib as L
+
+BLOCK = 16
+_DT = {torch.float32: L.F32, torch.bfloat16: L.BF16}
+
+
+@dataclass
+class FP4Tensor:
+    codes: torch.Tensor
+    scales: torch.Tensor
+    gscale: torch.Tensor
+    shape: tuple
+    blocked: torch.Tensor | None = field(default=None, repr=False)
+
+
+def blocked_size(rows: int, cols: int) -> int:
+    return -(-rows // 128) * -(-cols // 4) * 512
+
+
+def quantize_fast(x: torch.Tensor, use_rht: bool = True, stochastic: bool = False, seed: int | None = None) -> FP4Tensor:
+    if not x.is_cuda or x.dim() != 2 or x.shape[1] % BLOCK or x.dtype not in _DT:
+        raise ValueError(f"recant_b200.quantize_fast: need a CUDA 2-D float32/bfloat16 tensor with K % 16 == 0, "
+                         f"got {x.dtype} {tuple(x.shape)} on {x.device}")
+    x = x.contiguous()
+    m, k = x.shape
+    g = k // BLOCK
+    codes = torch.empty(m, k // 2, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(m, g, dtype=torch.uint8, device=x.device)
+    blocked = torch.empty(blocked_size(m, g), dtype=torch.uint8, device=x.device)
+    gscale = torch.empty((), dtype=torch.float32, device=x.device)
+    lib = L.lib()
+    wsb = lib.rb2_nvfp4_quantize_workspace_size(m, k)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
+    if stochastic and seed is None:
+        seed = random.getrandbits(62)
+    st = lib.rb2_nvfp4_quantize(L.ptr(x), m, k, _DT[x.dtype], int(use_rht), int(stochastic), int(seed or 0),
+                                L.ptr(codes), L.ptr(scales), L.ptr(blocked), L.ptr(gscale), L.ptr(ws), wsb,
+                                torch.cuda.current_stream(x.device).cuda_stream)
+    L.check(st, "nvfp4_quantize")
+    return FP4Tensor(codes, scales.view(torch.float8_e4m3fn), gscale, (m, k), blocked)
+
+
+def _blocked_of(t) -> torch.Tensor:
+    b = getattr(t, "blocked", None)
+    if b is not None:
+        return b
+    raise ValueError("recant_b200.gemm_b200: operand has no blocked scales; quantize it with recant_b200")
+
+
+def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
+    """a . b^T * (gA gB) with a [M,K] and b [N,K] NVFP4 tensors; fp32 (or bf16) [M, N]."""
+    m, k = a.shape
+    n, kb = b.shape
+    if k != kb:
+        raise ValueError(f"recant_b200.gemm_b200: K mismatch {k} vs {kb}")
+    out = torch.empty(m, n, dtype=out_dtype, device=a.codes.device)
+    lib = L.lib()
+    wsb = lib.rb2_nvfp4_gemm_workspace_size(m, n, k)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=a.codes.device)
+    st = lib.rb2_nvfp4_gemm(L.ptr(a.codes), L.ptr(_blocked_of(a)), L.ptr(a.gscale), L.ptr(b.codes),
+                            L.ptr(_blocked_of(b)), L.ptr(b.gscale), m, n, k, L.ptr(out), _DT[out_dtype], L.ptr(ws),
+                            wsb, torch.cuda.current_stream(a.codes.device).cuda_stream)
+    L.check(st, "nvfp4_gemm")
+    return out
+
+
+# ----- registry mirror of recant/model/nvfp4.py:125-149 --------------------------------------
+GEMM_BACKENDS = {"b200": gemm_b200}
+_state = {"gemm": "b200"}
+_fast = {"quantize": True}
+
+
+def set_gemm_backend(name: str) -> None:
+    if name not in GEMM_BACKENDS:
+        raise KeyError(f"unknown FP4 GEMM backend {name!r}; have {list(GEMM_BACKENDS)}")
+    _state["gemm"] = name
+
+
+def get_gemm_backend() -> str:
+    return _state["gemm"]
+
+
+def gemm_fp4(a, b) -> torch.Tensor:
+    with torch.profiler.record_function("b:fp4_gemm"):
+        return GEMM_BACKENDS[_state["gemm"]](a, b)
+
+
+def quantize_activation(x: torch.Tensor, use_rht: bool = True, stochastic: bool = False) -> FP4Tensor:
+    with torch.profiler.record_function("b:quantize"):
+        return quantize_fast(x.contiguous(), use_rht, stochastic)
+
+
+def register(ref_nvfp4_module, select: bool = False) -> None:
+    """Add ``'b200'`` to the reference's GEMM_BACKENDS and install the fast quantizer hook."""
+    ref_nvfp4_module.GEMM_BACKENDS["b200"] = gemm_b200
+    if select:
+        ref_nvfp4_module.set_gemm_backend("b200")

@@ -1,0 +1,95 @@
+"""C-ABI boundary checks that need no GPU: the library loads, exports every declared symbol,
+sizes workspaces and rejects bad arguments before touching the device."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from recant_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    with open(os.path.join(ROOT, "include", "recant_b200.h")) as f:
+        return re.findall(r"RB2_API\s+[\w\s\*]+?\b(rb2_\w+)\s*\(", f.read())
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    names = declared_symbols()
+    assert len(names) >= 9
+    lib = L.lib()
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in L.SIGNATURES, f"{n} has no ctypes signature"
+    assert set(L.SIGNATURES) <= set(names)
+
+
+def test_version_string():
+    assert b"sm_100a" in L.lib().rb2_version()
+
+
+def test_gdn_workspace_size_scales_with_problem():
+    lib = L.lib()
+    small = lib.rb2_gdn_workspace_size(1, 1024, 1, 4, 8, 128, 128, L.F32, L.GDN_EXACT)
+    big = lib.rb2_gdn_workspace_size(4, 4096, 4, 16, 32, 128, 128, L.F32, L.GDN_EXACT)
+    assert 0 < small < big
+    # cu_seqlens form: B == 1 with N sequences
+    assert lib.rb2_gdn_workspace_size(1, 5000, 7, 16, 32, 128, 128, L.F32, L.GDN_EXACT) > 0
+
+
+@pytest.mark.parametrize("dk", [16, 64, 256])
+def test_gdn_rejects_unsupported_head_dim(dk):
+    lib = L.lib()
+    st = lib.rb2_gdn_fwd(None, None, None, None, None, None, None, 1, 64, 1, 1, 1, dk, dk, L.F32, 0, 1.0,
+                         None, None, C.c_void_p(256), 1 << 30, None)
+    assert st == L.EUNSUPPORTED
+    assert b"128" in lib.rb2_last_error()
+
+
+def test_gdn_rejects_bad_group_and_dtype():
+    lib = L.lib()
+    st = lib.rb2_gdn_fwd(None, None, None, None, None, None, None, 1, 64, 1, 3, 4, 128, 128, L.F32, 0, 1.0,
+                         None, None, C.c_void_p(256), 1 << 30, None)
+    assert st == L.EINVAL and b"multiple" in lib.rb2_last_error()
+    st = lib.rb2_gdn_fwd(None, None, None, None, None, None, None, 1, 64, 1, 1, 1, 128, 128, 7, 0, 1.0,
+                         None, None, C.c_void_p(256), 1 << 30, None)
+    assert st == L.EINVAL
+
+
+def test_gdn_rejects_small_workspace_before_launch():
+    lib = L.lib()
+    p = C.c_void_p(4096)
+    st = lib.rb2_gdn_fwd(p, p, p, p, p, None, None, 1, 64, 1, 1, 1, 128, 128, L.F32, L.GDN_EXACT, 1.0,
+                         p, None, p, 16, None)
+    assert st == L.EWORKSPACE
+
+
+def test_quantize_rejects_bad_shapes():
+    lib = L.lib()
+    p = C.c_void_p(4096)
+    assert lib.rb2_nvfp4_quantize(p, 4, 24, L.BF16, 1, 0, 0, p, p, None, p, p, 256, None) == L.EINVAL
+    assert lib.rb2_nvfp4_quantize(p, 0, 32, L.BF16, 1, 0, 0, p, p, None, p, p, 256, None) == L.EINVAL
+    assert lib.rb2_nvfp4_quantize(p, 4, 32, 5, 1, 0, 0, p, p, None, p, p, 256, None) == L.EINVAL
+    assert lib.rb2_nvfp4_quantize(C.c_void_p(4100), 4, 32, L.BF16, 1, 0, 0, p, p, None, p, p, 256, None) == L.EINVAL
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from recant_b200 import gdn_b200, quantize_fast
+    x = torch.zeros(1, 64, 1, 128)
+    with pytest.raises(ValueError):
+        gdn_b200(x, x, x, torch.zeros(1, 64, 1), torch.zeros(1, 64, 1))
+    with pytest.raises(ValueError):
+        quantize_fast(torch.zeros(4, 32))
+
+
+def test_registry_mirror():
+    from recant_b200 import gdn as G, nvfp4 as N
+    assert G.get_gdn_backend() == "b200" and "b200" in G.GDN_BACKENDS
+    with pytest.raises(KeyError):
+        G.set_gdn_backend("nope")
+    assert N.get_gemm_backend() == "b200"
+    with pytest.raises(KeyError):
+        N.set_gemm_backend("nope")
