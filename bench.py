@@ -1,0 +1,348 @@
+"""Benchmark of the GDN hot path: chunked Gated DeltaNet forward + backward at the 9B layer shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--path auto|exact|fast]
+
+Workload (config 1 of the benchmark spec): B=4, T=4096, Hk=16, Hv=32, dk=dv=128, chunk 64, bf16
+inputs, fp32 state; q, k ~ N(0,1) (L2-normalised inside the op), v ~ N(0,1),
+beta = sigmoid(N(0,1)), g = -exp(A_log) softplus(a) with A_log = log U(1,16), a ~ N(0,1); upstream
+dO ~ N(0,1). A step is one forward + backward over that batch. Multi-GPU runs are replicas (the
+path has no exchange at this config): every rank runs its own batch, value = all ranks' tokens
+divided by the slowest rank's time (weak scaling).
+
+Prints ONE JSON line (rank 0). `value` is device-timed with inputs resident in HBM (inputs are
+larger than L2, so no flush is needed); `e2e` is the same metric through the public op with
+inputs copied from pinned host memory and o plus all gradients copied back inside the timed
+region; `roofline` is for the dominant kernel, timed live with CUDA events on its stream;
+`cpu_baseline` is the CPU port of the reference op (oracle/gdn.py, the restatement of
+recant.model.ops.gdn_torch + autograd) on a bounded sample, on the host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(B=4, T=4096, Hk=16, Hv=32, d=128, chunk=64)
+METRIC = "GDN fwd+bwd tokens/s at the 9B layer shape (B4 T4096 Hk16 Hv32 d128, chunk 64)"
+# algorithmic FLOPs per token-head of the chunked GDN (C = 64, d = 128):
+# forward 10*C*d + 6*d^2 = 180,224; forward + backward = 3x
+FLOP_FWD_PER_TOKEN_HEAD = 10 * 64 * 128 + 6 * 128 * 128
+FLOP_PER_TOKEN_HEAD = 3 * FLOP_FWD_PER_TOKEN_HEAD
+# per-launch algorithmic matmul FLOPs of each kernel, per (chunk, value head)
+_MF = 2 * 64 * 64 * 128  # one 64x64x128 product
+KERNEL_FLOPS_PER_CH = {
+    "gdn_exact_fwd_prep": 4 * _MF, "gdn_exact_fwd_state": 4 * _MF, "gdn_exact_fwd_out": 3 * _MF,
+    "gdn_exact_bwd_state": 7 * _MF, "gdn_exact_bwd_mm": 7 * _MF, "gdn_exact_bwd_intra": 12 * _MF,
+}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return dict(hbm=float(p["hbm_gbs"]), bf16=float(p["bf16_tflops"]),
+                    bf16_sustained=float(p["bf16_tflops_sustained"]), source="measured")
+    except Exception:
+        return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+def algorithmic_bytes(B, T, Hk, Hv, d):
+    """Compulsory HBM bytes of one fwd+bwd: fwd reads q,k (Hk), v, beta (bf16), g (fp32) and writes
+    o (bf16) + final state (fp32); bwd reads the inputs plus dO and writes dq, dk, dv, dbeta, dg."""
+    n = B * T
+    qk = 2 * n * Hk * d * 2
+    vv = n * Hv * d * 2
+    gb = n * Hv * 4 + n * Hv * 2
+    fwd = qk + vv + gb + vv + B * Hv * d * d * 4
+    bwd = (qk + vv + gb + vv) + (qk + vv + gb)
+    return fwd + bwd
+
+
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(dev, rank, B, T, Hk, Hv, d):
+    import torch
+    import torch.nn.functional as F
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    bf = torch.bfloat16
+    q = torch.randn(B, T, Hk, d, device=dev, generator=gen).to(bf)
+    k = torch.randn(B, T, Hk, d, device=dev, generator=gen).to(bf)
+    v = torch.randn(B, T, Hv, d, device=dev, generator=gen).to(bf)
+    beta = torch.sigmoid(torch.randn(B, T, Hv, device=dev, generator=gen)).to(bf)
+    a_log = torch.log(torch.empty(Hv, device=dev).uniform_(1.0, 16.0, generator=gen))
+    g = (-a_log.exp() * F.softplus(torch.randn(B, T, Hv, device=dev, generator=gen))).float()
+    do = torch.randn(B, T, Hv, d, device=dev, generator=gen).to(bf)
+    return dict(q=q, k=k, v=v, g=g, beta=beta), do
+
+
+def cpu_reference_sample(B, T, Hk, Hv, d, reps):
+    """The reference op's CPU path (oracle port of gdn_torch + autograd) on a bounded sample.
+    Returns tokens/s, threads, the sample description and seconds."""
+    import torch
+
+    from oracle import gdn as OG
+    from oracle import inputs as I
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    inp = I.gdn_inputs(B, T, Hk, Hv, d, dtype=torch.bfloat16, seed=0)
+    do = I.grad_output(B, T, Hv, d, dtype=torch.bfloat16)
+    f32 = {n: t.float() for n, t in inp.items()}   # the reference upcasts to fp32 (ops.py:25)
+    OG.gdn_fwd_bwd(f32["q"][:, :64], f32["k"][:, :64], f32["v"][:, :64], f32["g"][:, :64],
+                   f32["beta"][:, :64], do[:, :64].float())
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        OG.gdn_fwd_bwd(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], do.float())
+    dt = (time.perf_counter() - t0) / reps
+    return B * T / dt, threads, f"B{B} T{T} Hk{Hk} Hv{Hv} d{d} fwd+bwd, fp32 compute, {reps} reps", dt
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the reference's own CPU implementation of the path (its torch op
+    restated in oracle/gdn.py) timed on the host cores. Rank 0 only."""
+    if rank != 0:
+        return 0
+    c = CFG
+    sample_T = 1024
+    steps = []
+    for i in range(args.warmup + args.steps):
+        tps, threads, sample, dt = cpu_reference_sample(1, sample_T, c["Hk"], c["Hv"], c["d"], 1)
+        if i >= args.warmup:
+            steps.append(dt)
+    dt = statistics.mean(steps)
+    value = sample_T / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "config1-sample: GDN fwd+bwd, B1 T1024 Hk16 Hv32 d128 "
+                                        "(a bounded sample of B4 T4096; tokens/s is size-independent for O(T) GDN)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"B1 T{sample_T} Hk16 Hv32 d128 fwd+bwd per step (oracle/gdn.py)"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import torch
+    import torch.distributed as dist
+
+    from recant_b200 import _lib as L
+    from recant_b200 import gdn_b200
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    c = CFG
+    B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
+    inp, do = make_inputs(dev, rank, B, T, Hk, Hv, d)
+    leaves = {n: t.clone().requires_grad_(True) for n, t in inp.items()}
+
+    def step():
+        for t in leaves.values():
+            t.grad = None
+        o, _ = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], path=args.path)
+        o.backward(do)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    prof = L.LaunchProfiler(capacity=64 * (args.steps + 1))
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    prof.start()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    records, dropped = prof.read()
+    barrier()
+    clock_info = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = B * T
+    value = world * tokens / (ms / 1e3)
+
+    # ---- end to end through the public op with host buffers ------------------------------
+    host_in = {n: t.detach().cpu().pin_memory() for n, t in inp.items()}
+    host_do = do.cpu().pin_memory()
+    outs_host = {n: torch.empty_like(t.detach().cpu()).pin_memory() for n, t in inp.items()}
+    o_host = torch.empty(B, T, Hv, d, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values()) + host_do.numel() * host_do.element_size()
+    d2h = o_host.numel() * o_host.element_size() + sum(t.numel() * t.element_size() for t in outs_host.values())
+
+    def e2e_step():
+        dev_in = {n: t.to(dev, non_blocking=True).requires_grad_(True) for n, t in host_in.items()}
+        ddo = host_do.to(dev, non_blocking=True)
+        o, _ = gdn_b200(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], path=args.path)
+        o.backward(ddo)
+        o_host.copy_(o.detach(), non_blocking=True)
+        for n, t in dev_in.items():
+            outs_host[n].copy_(t.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(stream)
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_value = world * tokens / (ms_e2e / 1e3)
+
+    # ---- roofline of the dominant kernel ----------------------------------------------------
+    pk = peaks()
+    per_kernel = {}
+    for name, t in records:
+        a = per_kernel.setdefault(name, [0, 0.0])
+        a[0] += 1
+        a[1] += t
+    total_k = sum(v[1] for v in per_kernel.values()) or 1.0
+    top = max(per_kernel, key=lambda n: per_kernel[n][1]) if per_kernel else None
+    n_ch = (tokens // 64 + (1 if tokens % 64 else 0)) * Hv
+    roof = None
+    if top is not None:
+        launches, tot = per_kernel[top]
+        avg_s = tot / launches / 1e3
+        flops = KERNEL_FLOPS_PER_CH.get(top, 0) * n_ch
+        achieved = flops / avg_s / 1e12
+        roof = {"kernel": top, "bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16"],
+                "unit": "TFLOP/s", "frac": round(achieved / pk["bf16"], 4), "traffic": None,
+                "peak_source": f"{pk['source']} bf16 burst (MEASURED_PEAKS.json)",
+                "share_of_kernel_time": round(tot / total_k, 3), "avg_launch_ms": round(avg_s * 1e3, 4)}
+    path_flops = FLOP_PER_TOKEN_HEAD * tokens * Hv
+    path_bytes = algorithmic_bytes(B, T, Hk, Hv, d)
+    t_roof = max(path_flops / (pk["bf16"] * 1e12), path_bytes / (pk["hbm"] * 1e9))
+    kernels = {n: {"launches": v[0], "ms_total": round(v[1], 3), "share": round(v[1] / total_k, 3)}
+               for n, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][1])}
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",
+                   "global_batch": B * world, "seq_len": T, "parallelism": f"replicas x{world}",
+                   "path": args.path, "l2": "inputs (q,k,v,dO ~ 470 MB) exceed the 126 MB L2; no flush"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": roof,
+        "path_roofline": {"flops": path_flops, "bytes": path_bytes, "t_roof_ms": round(t_roof * 1e3, 4),
+                          "frac": round(t_roof * 1e3 / ms, 4),
+                          "definition": "max(F / bf16 burst peak, bytes / HBM peak) / measured step time"},
+        "gpu_launches": len(records) + dropped,
+        "kernels": kernels,
+        "clocks": clock_info,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, threads, sample, _ = cpu_reference_sample(1, 2048, Hk, Hv, d, 1)
+        line["cpu_baseline"] = {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
