@@ -123,6 +123,12 @@ RB2_API int rb2_profile_disable(void);
 RB2_API int rb2_profile_read(int max_records, char* names, size_t name_stride, float* ms);
 RB2_API int rb2_profile_dropped(void);
 
+/* Diagnostic (no counterpart in the reference): one-tile tcgen05 product D[M,N] = A . B^T with
+ * bf16 A, B given K-major (a_mn/b_mn = 0: A[m*K+k]) or MN-major (1: A[k*M+m]); M in {64,128},
+ * N, K in {64,128}; fp32 D. Validates the tensor-core operand layouts on this device. */
+RB2_API int rb2_selftest_mma(const void* A, const void* B, float* D, int a_mn, int b_mn, int M, int N, int K,
+                             int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,7 @@ SIGNATURES = {
     "rb2_profile_disable": (_i, []),
     "rb2_profile_read": (_i, [_i, C.c_char_p, _sz, C.POINTER(C.c_float)]),
     "rb2_profile_dropped": (_i, []),
+    "rb2_selftest_mma": (_i, [_p, _p, _p, _i, _i, _i, _i, _i, _p, _p]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,143 @@
+// Blackwell (sm_100a) tensor-core plumbing in inline PTX: tcgen05 MMA with operands in shared
+// memory, accumulators in tensor memory (TMEM), mbarrier completion, TMEM loads, and the
+// 128-byte-swizzled shared-memory operand layouts the MMA descriptors describe.
+//
+// Operand layouts used throughout (bf16, "SW128" = 128-byte swizzle, 1024-byte atoms):
+//   K-major tile  R rows x 64 k   : byte(r, k) = r*128 + (((k*2)>>4) ^ (r&7))*16 + (k*2 & 15)
+//   A tile with more than 64 k is a sequence of such 64-k slabs, slab stride = R*128 bytes.
+//   The same bytes read as an MN-major operand (M or N = the 64 "k" elements of a slab, K = the
+//   R rows) have LBO = slab stride and SBO = 1024, so one tile written once serves both roles.
+// TMEM accumulator of an M=128 MMA: row m in lane m, column n at column (base + n), fp32.
+#pragma once
+
+#include "common.cuh"
+
+namespace rb2 {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ----- byte offset of element (r, k) in a K-major SW128 tile of `rows` rows -------------------
+__device__ __forceinline__ uint32_t sw128_offset(int r, int k, int rows) {
+  const int slab = k >> 6, kk = k & 63;
+  return uint32_t(slab * rows * 128 + r * 128 + ((((kk * 2) >> 4) ^ (r & 7)) << 4) + ((kk * 2) & 15));
+}
+
+// ----- shared-memory matrix descriptors ---------------------------------------------------------
+// K-major SW128: SBO = 1024 (8-row groups), LBO unused (1), version 1, layout type 2 (128B swizzle)
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFF);
+  d |= uint64_t(1) << 16;                   // LBO (ignored for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;           // SBO
+  d |= uint64_t(1) << 46;                   // version (sm100)
+  d |= uint64_t(2) << 61;                   // SWIZZLE_128B
+  return d;
+}
+// MN-major SW128: LBO = stride between 64-element MN blocks, SBO = stride between 8-row K groups
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFF);
+  d |= uint64_t((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+// ----- instruction descriptor: kind::f16, bf16 x bf16 -> f32 ----------------------------------
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major,
+                                                   bool negate_a = false) {
+  return (1u << 4)                          // D = f32
+         | (1u << 7) | (1u << 10)           // A, B = bf16
+         | (negate_a ? (1u << 13) : 0u)
+         | (a_mn_major ? (1u << 15) : 0u) | (b_mn_major ? (1u << 16) : 0u)
+         | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+// ----- tcgen05 ------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0));
+}
+// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Make this thread's generic-proxy shared-memory writes visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane (quarter*32 + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ----- mbarrier -----------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~2^26 polls (seconds), records `code` in *err and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  if (err) atomicExch(err, code);
+  return false;
+}
+
+// ----- bf16 packing -------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Write 8 consecutive k (16 bytes) of row r into a K-major SW128 tile; k0 % 8 == 0.
+__device__ __forceinline__ void sw128_store8(unsigned char* tile, int rows, int r, int k0, uint4 v) {
+  *reinterpret_cast<uint4*>(tile + sw128_offset(r, k0, rows)) = v;
+}
+
+}  // namespace tc
+}  // namespace rb2
