@@ -21,7 +21,6 @@ template <typename TIn>
 int exact_backward(const GdnProblem& p, ExactWs& ws, const TIn* d_o, const float* dhT, TIn* dq, TIn* dk,
                    TIn* dv, float* dg, TIn* dbeta, float* dh0, cudaStream_t s);
 
-int fast_workspace_bytes(const GdnProblem& p);
 int fast_forward(const GdnProblem& p, void* ws, void* o, float* hT, cudaStream_t s);
 int fast_backward(const GdnProblem& p, void* ws, const void* d_o, const float* dhT, void* dq, void* dk,
                   void* dv, float* dg, void* dbeta, float* dh0, cudaStream_t s);

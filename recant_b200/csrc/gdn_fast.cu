@@ -1,0 +1,523 @@
+// Chunked Gated DeltaNet, tensor-core path (bf16 operands, fp32 accumulation and state) on tcgen05.
+//
+// Same chunked factorisation as recant.model.ops.gdn_torch (recant/model/ops.py:21-54); see
+// gdn_exact.cu for the algebra. Every matmul runs on tcgen05 with M = 128 TMEM lanes by writing the
+// products TRANSPOSED, so that the 128-long head dimension is the MMA's M:
+//
+//   prep  (per chunk x head, parallel)
+//     [K; Q] K^T                   M=128 (64 key rows + 64 query rows), N=64, K=dk   -> kk, qk
+//     T = (I + strict(beta kk Gamma))^-1      fp32 on CUDA cores (blocked forward substitution)
+//     U^T = V^T (T beta)^T          M=dv, N=64, K=64
+//     W^T = K^T (T beta e^cum r_k)^T M=dk, N=64, K=64
+//   state (per sequence x head, sequential over chunks; S^T [dv][dk] fp32 in registers)
+//     V'^T = U^T - S^T W^T          M=dv, N=64,  K=dk
+//     O^T  = S^T q~^T + V'^T A_qk^T M=dv, N=64,  K=dk then K=64
+//     S^T <- gamma S^T + V'^T k~    M=dv, N=dk,  K=64
+//
+// Raw bf16 q/k/v feed the MMAs directly; the l2norm scales, decays and beta are folded into fp32
+// epilogues or into the small bf16 T-derived operands, so the only added roundings are those of
+// T beta, W, U, q~, k~, A_qk, the per-chunk S^T operand and V' (measured ~2.4e-3 relative on o).
+#include "gdn_common.cuh"
+#include "tc.cuh"
+
+namespace rb2 {
+
+struct FastWs {
+  ChunkTable ct;
+  float* stats;          // [ch][4][64] cum, rq, rk, beta
+  float* tinv;           // [ch][64][64]
+  __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal
+  __nv_bfloat16* w;      // [ch][64][128]
+  __nv_bfloat16* u;      // [ch][64][128]
+  __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q
+  __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k
+  __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk]
+  __nv_bfloat16* vp;     // [ch][64][128]  V'
+  int* err;              // device status word
+};
+
+size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks) {
+  const size_t nch = size_t(max_chunks) * Hv;
+  w.ct.tok0 = c.take<int>(max_chunks);
+  w.ct.len = c.take<int>(max_chunks);
+  w.ct.seq = c.take<int>(max_chunks);
+  w.ct.seq_chunk0 = c.take<int>(n_seqs + 1);
+  w.ct.n_chunks = c.take<int>(1);
+  w.err = c.take<int>(1);
+  w.stats = c.take<float>(nch * 256);
+  w.tinv = c.take<float>(nch * 4096);
+  w.aqk = c.take<__nv_bfloat16>(nch * 4096);
+  w.w = c.take<__nv_bfloat16>(nch * 8192);
+  w.u = c.take<__nv_bfloat16>(nch * 8192);
+  w.qt = c.take<__nv_bfloat16>(nch * 8192);
+  w.kt = c.take<__nv_bfloat16>(nch * 8192);
+  w.hs = c.take<__nv_bfloat16>(nch * 16384);
+  w.vp = c.take<__nv_bfloat16>(nch * 8192);
+  (void)tokens;
+  return c.bytes();
+}
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+  return p + ((1024 - (tc::smem_u32(p) & 1023)) & 1023);
+}
+
+// Copy `nrows` rows of 128 bf16 (row stride `stride` elements) into rows [r0, r0+nrows) of a
+// K-major SW128 tile with `tile_rows` rows; rows >= L are zero. All `nthr` threads participate.
+__device__ __forceinline__ void load_rows_sw128(unsigned char* tile, int tile_rows, int r0, const bf16* src,
+                                                int64_t stride, int nrows, int L, int nthr) {
+  for (int idx = threadIdx.x; idx < nrows * 16; idx += nthr) {
+    const int r = idx >> 4, c8 = idx & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < L) v = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r0 + r, c8 * 8, tile_rows)) = v;
+  }
+}
+
+// Same for a plain row-major [64][128] bf16 smem tile (no swizzle).
+__device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int64_t stride, int nthr) {
+  for (int idx = threadIdx.x; idx < 64 * 16; idx += nthr) {
+    const int r = idx >> 4, c8 = idx & 15;
+    *reinterpret_cast<uint4*>(tile + r * 128 + c8 * 8) = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
+  }
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
+
+// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65), 128 threads.
+__device__ void unit_lower_inverse128(const float* lm, float* tm, float* xbuf) {
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  for (int idx = tid; idx < 64 * 65; idx += 128) tm[idx] = 0.f;
+  __syncthreads();
+  if (l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
+    const int o = 16 * w;
+    float col[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float t = (i == l) ? 1.f : 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) t = fmaf(-lm[(o + i) * 65 + o + m], col[m], t);
+      col[i] = t;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tm[(o + i) * 65 + o + l] = col[i];
+  }
+  __syncthreads();
+  for (int bi = 1; bi < 4; ++bi) {
+    for (int e = tid; e < bi * 256; e += 128) {  // X_bj = sum_{m in [16bj, 16bi)} L[16bi+r][m] T[m][16bj+c]
+      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      float x = 0.f;
+      for (int m = 16 * bj; m < 16 * bi; ++m) x = fmaf(lm[(16 * bi + r) * 65 + m], tm[m * 65 + 16 * bj + c], x);
+      xbuf[e] = x;
+    }
+    __syncthreads();
+    for (int e = tid; e < bi * 256; e += 128) {  // T_bi,bj = -T_bi,bi X_bj
+      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      float t = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) t = fmaf(tm[(16 * bi + r) * 65 + 16 * bi + m], xbuf[bj * 256 + m * 16 + c], t);
+      tm[(16 * bi + r) * 65 + 16 * bj + c] = -t;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// prep: one CTA (128 threads) per (chunk, value head)
+// ------------------------------------------------------------------------------------------------
+constexpr int kPrepSmem = 32768 + 16384 + 8192 + 8192 + 2 * 64 * 65 * 4 + 768 * 4 + 6 * 64 * 4 + 2048;
+
+__global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = align1024(smem_raw);
+  unsigned char* kq = sm;                  // [K;Q] K-major SW128, 128 rows x 128   (32 KB)
+  unsigned char* vt = kq + 32768;          // V, 64 rows x 128 (as MN-major A)     (16 KB)
+  unsigned char* tb1 = vt + 16384;         // T diag(beta), 64 x 64 K-major         (8 KB)
+  unsigned char* tb2 = tb1 + 8192;         // T diag(beta e^cum rk)                 (8 KB)
+  float* lm = reinterpret_cast<float*>(tb2 + 8192);
+  float* tm = lm + 64 * 65;
+  float* xbuf = tm + 64 * 65;
+  float* cum = xbuf + 768;
+  float* rq = cum + 64;
+  float* rk = rq + 64;
+  float* beta = rk + 64;
+  float* ecum = beta + 64;
+  float* gv = ecum + 64;
+  __shared__ uint64_t bar[2];
+  __shared__ uint32_t tmem_base;
+
+  const int ci = blockIdx.x, h = blockIdx.y;
+  if (ci >= *ws.ct.n_chunks) return;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
+  const int64_t ch = int64_t(ci) * p.Hv + h;
+  const bf16* q = static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128;
+  const bf16* k = static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128;
+  const bf16* v = static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128;
+  const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
+
+  if (w == 0) tc::tmem_alloc(&tmem_base, 256);
+  if (tid == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  load_rows_sw128(kq, 128, 0, k, qs, 64, L, 128);
+  load_rows_sw128(kq, 128, 64, q, qs, 64, L, 128);
+  load_rows_sw128(vt, 64, 0, v, vs, 64, L, 128);
+  if (tid < 64) {
+    gv[tid] = tid < L ? p.g[int64_t(t0 + tid) * p.Hv + h] : 0.f;
+    beta[tid] = tid < L ? __bfloat162float(static_cast<const bf16*>(p.beta)[int64_t(t0 + tid) * p.Hv + h]) : 0.f;
+  }
+  tc::fence_proxy_async();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+  if (tid == 0) {  // [K;Q] K^T: M=128, N=64, K=128 -> TMEM cols [0, 64)
+    const uint32_t a0 = tc::smem_u32(kq);
+    const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+    for (int k0 = 0; k0 < 128; k0 += 16) {
+      const uint32_t off = (k0 >> 6) * 16384 + (k0 & 63) * 2;
+      tc::mma_bf16(tbase, tc::desc_kmajor_sw128(a0 + off), tc::desc_kmajor_sw128(a0 + off), idesc, k0 > 0);
+    }
+    tc::mma_commit(&bar[0]);
+  }
+  // norms of the 128 stacked rows (half-warp per row), cumulative gate in double
+  for (int r = w * 2 + (l >> 4); r < 128; r += 8) {
+    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(r, (l & 15) * 8, 128));
+    float s = 0.f;
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { const float a = bf_lo(xs[j]), b = bf_hi(xs[j]); s = fmaf(a, a, s); s = fmaf(b, b, s); }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((l & 15) == 0) {
+      const float rs = 1.0f / sqrtf(s + 1e-6f);
+      if (r < 64) rk[r] = rs; else rq[r - 64] = rs;
+    }
+  }
+  if (tid == 0) {
+    double acc = 0.0;
+    for (int i = 0; i < 64; ++i) { acc += double(gv[i]); cum[i] = float(acc); }
+  }
+  __syncthreads();
+  if (tid < 64) ecum[tid] = expf(cum[tid]);
+  float* st = ws.stats + ch * 256;
+  if (tid < 64) { st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid]; }
+
+  tc::mbar_wait(&bar[0], 0, ws.err, 101);
+  tc::fence_after_sync();
+  {
+    // lane tid of the accumulator: rows 0-63 = kk row i, rows 64-127 = qk row i
+    float row[64];
+    float tmp[32];
+    const uint32_t lane_addr = tbase + (uint32_t(w * 32) << 16);
+    tc::tmem_ld32(lane_addr + 0, tmp);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) row[j] = tmp[j];
+    tc::tmem_ld32(lane_addr + 32, tmp);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) row[32 + j] = tmp[j];
+    if (tid < 64) {
+      const int i = tid;
+      const float bi = beta[i] * rk[i], ci_ = cum[i];
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        lm[i * 65 + j] = j < i ? bi * rk[j] * row[j] * expf(ci_ - cum[j]) : 0.f;
+    } else {
+      const int i = tid - 64;
+      const float si = p.scale * rq[i], ci_ = cum[i];
+      uint32_t packed[32];
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) {
+        const float a = j <= i ? si * rk[j] * row[j] * expf(ci_ - cum[j]) : 0.f;
+        const float b = j + 1 <= i ? si * rk[j + 1] * row[j + 1] * expf(ci_ - cum[j + 1]) : 0.f;
+        packed[j >> 1] = tc::pack_bf16(a, b);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(ws.aqk + ch * 4096 + i * 64);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  unit_lower_inverse128(lm, tm, xbuf);
+  // T to the workspace (fp32, for the backward) and the two bf16 B operands
+  for (int idx = tid; idx < 4096; idx += 128) ws.tinv[ch * 4096 + idx] = tm[(idx >> 6) * 65 + (idx & 63)];
+  {
+    const int i = tid & 63;
+    unsigned char* dst = tid < 64 ? tb1 : tb2;
+#pragma unroll
+    for (int m0 = 0; m0 < 64; m0 += 8) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const int m = m0 + j;
+        float f0 = tm[i * 65 + m] * beta[m], f1 = tm[i * 65 + m + 1] * beta[m + 1];
+        if (tid >= 64) { f0 *= ecum[m] * rk[m]; f1 *= ecum[m + 1] * rk[m + 1]; }
+        pk[j >> 1] = tc::pack_bf16(f0, f1);
+      }
+      *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, m0, 64)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+  tc::fence_proxy_async();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (tid == 0) {
+    // U^T = V^T (T beta)^T: A = V as MN-major (M = dv, K = tok), B = tb1 K-major (N = 64, K = 64)
+    // W^T = K^T (T beta e^cum rk)^T: A = rows 0-63 of [K;Q] as MN-major (slab stride 16 KB)
+    const uint32_t idesc = tc::idesc_bf16(128, 64, true, false);
+    const uint32_t va = tc::smem_u32(vt), ka = tc::smem_u32(kq), b1 = tc::smem_u32(tb1), b2 = tc::smem_u32(tb2);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16) {
+      tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(va + k0 * 128, 8192), tc::desc_kmajor_sw128(b1 + k0 * 2), idesc, k0 > 0);
+      tc::mma_bf16(tbase + 128, tc::desc_mnmajor_sw128(ka + k0 * 128, 16384), tc::desc_kmajor_sw128(b2 + k0 * 2), idesc, k0 > 0);
+    }
+    tc::mma_commit(&bar[1]);
+  }
+  // q~ and k~ rows while the MMAs run: half-warp per row, 8 elements per lane
+  for (int r = w * 2 + (l >> 4); r < 128; r += 8) {
+    const int c8 = (l & 15) * 8;
+    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(r, c8, 128));
+    const int i = r & 63;
+    const float f = r < 64 ? expf(cum[63] - cum[i]) * rk[i] : p.scale * rq[i] * ecum[i];
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
+    bf16* dst = (r < 64 ? ws.kt : ws.qt) + ch * 8192 + i * 128 + c8;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  tc::mbar_wait(&bar[1], 0, ws.err, 102);
+  tc::fence_after_sync();
+  {
+    // lane tid = dv (for U) or dk (for W); 64 token columns each
+    const uint32_t lane_addr = tbase + (uint32_t(w * 32) << 16);
+    float tmp[32];
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      bf16* dst = (part == 0 ? ws.u : ws.w) + ch * 8192 + tid;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tc::tmem_ld32(lane_addr + 64 + 64 * part + 32 * half, tmp);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dst[(32 * half + j) * 128] = __float2bfloat16_rn(tmp[j]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (w == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+// ------------------------------------------------------------------------------------------------
+// forward state walk: one CTA (256 threads) per (sequence, value head)
+//   thread (w, l): TMEM lane / dv row r = 32 (w & 3) + l, dk half hh = w >> 2
+// ------------------------------------------------------------------------------------------------
+constexpr int kStateSmem = 32768 + 16384 * 3 + 8192 + 16384 + 16384 + 64 * 4 + 2048;
+
+__global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ o,
+                                                                 float* __restrict__ hT) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = align1024(smem_raw);
+  unsigned char* st = sm;                   // S^T bf16, K-major 128 rows (dv) x 128 (dk)   32 KB
+  unsigned char* wt = st + 32768;           // W   64 rows (tok) x 128 (dk)                 16 KB
+  unsigned char* qt = wt + 16384;           // q~  64 x 128                                 16 KB
+  unsigned char* kt = qt + 16384;           // k~  64 x 128 (used MN-major: N = dk)        16 KB
+  unsigned char* at = kt + 16384;           // A_qk 64 (i) x 64 (j)                          8 KB
+  unsigned char* vpt = at + 8192;           // V'^T 128 rows (dv) x 64 (tok)                16 KB
+  bf16* us = reinterpret_cast<bf16*>(vpt + 16384);  // U plain [64][128]                     16 KB
+  float* cum = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(us) + 16384);
+  __shared__ uint64_t bar[2];
+  __shared__ uint32_t tmem_base;
+
+  const int h = blockIdx.x, s = blockIdx.y;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int r = 32 * (w & 3) + l, hh = w >> 2;
+  if (w == 0) tc::tmem_alloc(&tmem_base, 512);
+  if (tid == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  // S^T[r][dk] for dk in [64 hh, 64 hh + 64): S[dk][r] of the [dk][dv] state
+  float S[64];
+  const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
+#pragma unroll
+  for (int j = 0; j < 64; ++j) S[j] = p.h0 ? p.h0[sbase + (64 * hh + j) * 128 + r] : 0.f;
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16);
+  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
+  uint32_t phase = 0;
+  for (int ci = c0; ci < c1; ++ci) {
+    const int64_t ch = int64_t(ci) * p.Hv + h;
+    const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
+    // S^T (bf16) -> smem operand and -> workspace (state entering this chunk)
+    {
+      uint32_t pk[32];
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) pk[j >> 1] = tc::pack_bf16(S[j], S[j + 1]);
+      uint4* gdst = reinterpret_cast<uint4*>(ws.hs + ch * 16384 + r * 128 + 64 * hh);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        *reinterpret_cast<uint4*>(st + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
+        gdst[j] = v4;
+      }
+    }
+    load_rows_sw128(wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
+    load_rows_sw128(qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
+    load_rows_sw128(kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
+    for (int idx = tid; idx < 64 * 8; idx += 256) {  // A_qk: 64 rows x 64 -> one 64-k slab
+      const int i = idx >> 3, c8 = idx & 7;
+      *reinterpret_cast<uint4*>(at + tc::sw128_offset(i, c8 * 8, 64)) =
+          __ldg(reinterpret_cast<const uint4*>(ws.aqk + ch * 4096 + i * 64 + c8 * 8));
+    }
+    load_rows_plain(us, ws.u + ch * 8192, 128, 256);
+    if (tid < 64) cum[tid] = ws.stats[ch * 256 + tid];
+    tc::fence_proxy_async();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (tid == 0) {
+      // D_vp = S^T W^T (cols [0,64)), D_o = S^T q~^T (cols [64,128)): M=128, N=64, K=128
+      const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t sa = tc::smem_u32(st), wa = tc::smem_u32(wt), qa = tc::smem_u32(qt);
+#pragma unroll
+      for (int k0 = 0; k0 < 128; k0 += 16) {
+        const uint32_t aoff = (k0 >> 6) * 16384 + (k0 & 63) * 2, boff = (k0 >> 6) * 8192 + (k0 & 63) * 2;
+        tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(wa + boff), idesc, k0 > 0);
+        tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(qa + boff), idesc, k0 > 0);
+      }
+      tc::mma_commit(&bar[0]);
+    }
+    tc::mbar_wait(&bar[0], phase, ws.err, 111);
+    tc::fence_after_sync();
+    {
+      // V'^T[r][tok] = U[tok][r] - D_vp[r][tok] for tok in [32 hh, 32 hh + 32)
+      float x[32];
+      tc::tmem_ld32(lane_addr + 32 * hh, x);
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const int tk = 32 * hh + j;
+        const float a = __bfloat162float(us[tk * 128 + r]) - x[j];
+        const float b = __bfloat162float(us[(tk + 1) * 128 + r]) - x[j + 1];
+        pk[j >> 1] = tc::pack_bf16(a, b);
+        const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(&pk[j >> 1]);
+        ws.vp[ch * 8192 + tk * 128 + r] = ab.x;
+        ws.vp[ch * 8192 + (tk + 1) * 128 + r] = ab.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
+            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+    }
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (tid == 0) {
+      // D_o += V'^T A_qk^T (M=128, N=64, K=64); D_s = V'^T k~ (M=128, N=128, K=64, k~ MN-major)
+      const uint32_t va = tc::smem_u32(vpt), aa = tc::smem_u32(at), ka = tc::smem_u32(kt);
+      const uint32_t id_o = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
+#pragma unroll
+      for (int k0 = 0; k0 < 64; k0 += 16) {
+        tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_kmajor_sw128(aa + k0 * 2), id_o, true);
+        tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_mnmajor_sw128(ka + k0 * 128, 8192), id_s,
+                     k0 > 0);
+      }
+      tc::mma_commit(&bar[1]);
+    }
+    tc::mbar_wait(&bar[1], phase, ws.err, 112);
+    tc::fence_after_sync();
+    {
+      float x[32];
+      tc::tmem_ld32(lane_addr + 64 + 32 * hh, x);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int tk = 32 * hh + j;
+        if (tk < L) o[(int64_t(t0 + tk) * p.Hv + h) * 128 + r] = __float2bfloat16_rn(x[j]);
+      }
+      const float gamma = expf(cum[63]);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tc::tmem_ld32(lane_addr + 256 + 64 * hh + 32 * half, x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) S[32 * half + j] = fmaf(gamma, S[32 * half + j], x[j]);
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    phase ^= 1;
+  }
+  if (hT) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) hT[sbase + (64 * hh + j) * 128 + r] = S[j];
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (w == 0) tc::tmem_dealloc(tbase, 512);
+}
+
+template <typename K>
+int smem_attr(K kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return RB2_ECUDA;
+  }
+  return RB2_OK;
+}
+
+}  // namespace
+
+size_t fast_workspace_size(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int max_chunks) {
+  (void)Hk;
+  Carver c(nullptr);
+  FastWs w;
+  return carve_fast(c, w, tokens, n_seqs, Hv, max_chunks);
+}
+
+static int check_err_word(const FastWs& w, cudaStream_t s, bool sync) {
+  (void)w; (void)s; (void)sync;
+  return RB2_OK;
+}
+
+int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_t s) {
+  Carver c(wsp);
+  FastWs w;
+  carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks);
+  int rc = launch_chunk_table(p, w.ct, s);
+  if (rc) return rc;
+  RB2_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), s), "gdn fast: clear status");
+  if (p.max_chunks > 0) {
+    if ((rc = smem_attr(fast_prep_kernel, kPrepSmem))) return rc;
+    ProfScope ps_("gdn_fast_prep", s);
+    fast_prep_kernel<<<dim3(p.max_chunks, p.Hv), 128, kPrepSmem, s>>>(p, w);
+    RB2_CHECK_LAUNCH("gdn fast prep");
+  }
+  if ((rc = smem_attr(fast_state_fwd_kernel, kStateSmem))) return rc;
+  {
+    ProfScope ps_("gdn_fast_state_fwd", s);
+    fast_state_fwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kStateSmem, s>>>(p, w, static_cast<bf16*>(o), hT);
+    RB2_CHECK_LAUNCH("gdn fast state fwd");
+  }
+  return check_err_word(w, s, false);
+}
+
+int fast_backward(const GdnProblem& p, void* ws, const void* d_o, const float* dhT, void* dq, void* dk, void* dv,
+                  float* dg, void* dbeta, float* dh0, cudaStream_t s) {
+  (void)p; (void)ws; (void)d_o; (void)dhT; (void)dq; (void)dk; (void)dv; (void)dg; (void)dbeta; (void)dh0; (void)s;
+  set_error("gdn: tensor-core backward not built yet");
+  return RB2_EUNSUPPORTED;
+}
+
+}  // namespace rb2

@@ -1,0 +1,50 @@
+"""Tensor-core (tcgen05) GDN path vs the fp32 oracle: bf16 inputs, tolerance 2e-2 relative Frobenius."""
+import pytest
+import torch
+
+from gpu_util import rel
+from oracle import gdn as OG
+from oracle import inputs as I
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _fwd(inp, h0=None, cu=None):
+    from recant_b200 import gdn_b200
+    d = {n: t.cuda() for n, t in inp.items()}
+    with torch.no_grad():
+        o, hT = gdn_b200(d["q"], d["k"], d["v"], d["g"], d["beta"], None if h0 is None else h0.cuda(), True,
+                         cu_seqlens=None if cu is None else cu.cuda(), path="fast")
+    torch.cuda.synchronize()
+    return o.cpu(), hT.cpu()
+
+
+@pytest.mark.parametrize("B,T,Hk,Hv", [(1, 64, 1, 1), (2, 300, 2, 4), (1, 1024, 4, 8)])
+def test_fast_forward(B, T, Hk, Hv):
+    inp = I.gdn_inputs(B, T, Hk, Hv, 128, dtype=torch.bfloat16, seed=T + Hv)
+    f32 = {n: t.float() for n, t in inp.items()}
+    ro, rhT = OG.gdn(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], None, True)
+    o, hT = _fwd(inp)
+    assert rel(o, ro) < TOL and rel(hT, rhT) < TOL, (rel(o, ro), rel(hT, rhT))
+
+
+def test_fast_forward_initial_state_and_mild_gates():
+    inp = I.gdn_inputs(2, 200, 2, 2, 128, dtype=torch.bfloat16, seed=3)
+    gen = torch.Generator().manual_seed(3)
+    inp["g"] = -torch.rand(2, 200, 2, generator=gen) * 0.1
+    h0 = torch.randn(2, 2, 128, 128, generator=gen) * 0.1
+    f32 = {n: t.float() for n, t in inp.items()}
+    ro, rhT = OG.gdn(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], h0, True)
+    o, hT = _fwd(inp, h0)
+    assert rel(o, ro) < TOL and rel(hT, rhT) < TOL, (rel(o, ro), rel(hT, rhT))
+
+
+def test_fast_forward_varlen():
+    lengths = [70, 1, 64, 0, 129, 33]
+    cu = I.cu_seqlens_of(lengths)
+    inp = I.gdn_inputs(1, int(cu[-1]), 2, 4, 128, dtype=torch.bfloat16, seed=5)
+    f32 = {n: t.float() for n, t in inp.items()}
+    ro, rhT = OG.gdn(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], None, True, cu_seqlens=cu)
+    o, hT = _fwd(inp, cu=cu)
+    assert rel(o, ro) < TOL and rel(hT, rhT) < TOL, (rel(o, ro), rel(hT, rhT))
