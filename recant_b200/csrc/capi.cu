@@ -29,7 +29,7 @@ size_t fast_workspace_size(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int m
 namespace {
 
 int resolve_path(int dtype, int path) {
-  if (path == RB2_GDN_AUTO) return RB2_GDN_EXACT;
+  if (path == RB2_GDN_AUTO) return dtype == RB2_BF16 ? RB2_GDN_FAST : RB2_GDN_EXACT;
   return path;
 }
 

@@ -17,26 +17,11 @@
 // Raw bf16 q/k/v feed the MMAs directly; the l2norm scales, decays and beta are folded into fp32
 // epilogues or into the small bf16 T-derived operands, so the only added roundings are those of
 // T beta, W, U, q~, k~, A_qk, the per-chunk S^T operand and V' (measured ~2.4e-3 relative on o).
-#include "gdn_common.cuh"
-#include "tc.cuh"
+#include "gdn_fast.cuh"
 
 namespace rb2 {
 
-struct FastWs {
-  ChunkTable ct;
-  float* stats;          // [ch][4][64] cum, rq, rk, beta
-  float* tinv;           // [ch][64][64]
-  __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal
-  __nv_bfloat16* w;      // [ch][64][128]
-  __nv_bfloat16* u;      // [ch][64][128]
-  __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q
-  __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k
-  __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk]
-  __nv_bfloat16* vp;     // [ch][64][128]  V'
-  int* err;              // device status word
-};
-
-size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks) {
+size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks, bool gqa) {
   const size_t nch = size_t(max_chunks) * Hv;
   w.ct.tok0 = c.take<int>(max_chunks);
   w.ct.len = c.take<int>(max_chunks);
@@ -53,78 +38,16 @@ size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, 
   w.kt = c.take<__nv_bfloat16>(nch * 8192);
   w.hs = c.take<__nv_bfloat16>(nch * 16384);
   w.vp = c.take<__nv_bfloat16>(nch * 8192);
-  (void)tokens;
+  w.dh = c.take<__nv_bfloat16>(nch * 16384);
+  w.dvp = c.take<__nv_bfloat16>(nch * 8192);
+  w.dqh = c.take<float>(gqa ? size_t(tokens) * Hv * 128 : 0);
+  w.dkh = c.take<float>(gqa ? size_t(tokens) * Hv * 128 : 0);
   return c.bytes();
 }
 
 namespace {
 
-using bf16 = __nv_bfloat16;
-
-__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
-  return p + ((1024 - (tc::smem_u32(p) & 1023)) & 1023);
-}
-
-// Copy `nrows` rows of 128 bf16 (row stride `stride` elements) into rows [r0, r0+nrows) of a
-// K-major SW128 tile with `tile_rows` rows; rows >= L are zero. All `nthr` threads participate.
-__device__ __forceinline__ void load_rows_sw128(unsigned char* tile, int tile_rows, int r0, const bf16* src,
-                                                int64_t stride, int nrows, int L, int nthr) {
-  for (int idx = threadIdx.x; idx < nrows * 16; idx += nthr) {
-    const int r = idx >> 4, c8 = idx & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < L) v = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
-    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r0 + r, c8 * 8, tile_rows)) = v;
-  }
-}
-
-// Same for a plain row-major [64][128] bf16 smem tile (no swizzle).
-__device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int64_t stride, int nthr) {
-  for (int idx = threadIdx.x; idx < 64 * 16; idx += nthr) {
-    const int r = idx >> 4, c8 = idx & 15;
-    *reinterpret_cast<uint4*>(tile + r * 128 + c8 * 8) = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
-  }
-}
-
-__device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
-
-// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65), 128 threads.
-__device__ void unit_lower_inverse128(const float* lm, float* tm, float* xbuf) {
-  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
-  for (int idx = tid; idx < 64 * 65; idx += 128) tm[idx] = 0.f;
-  __syncthreads();
-  if (l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
-    const int o = 16 * w;
-    float col[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float t = (i == l) ? 1.f : 0.f;
-#pragma unroll
-      for (int m = 0; m < i; ++m) t = fmaf(-lm[(o + i) * 65 + o + m], col[m], t);
-      col[i] = t;
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) tm[(o + i) * 65 + o + l] = col[i];
-  }
-  __syncthreads();
-  for (int bi = 1; bi < 4; ++bi) {
-    for (int e = tid; e < bi * 256; e += 128) {  // X_bj = sum_{m in [16bj, 16bi)} L[16bi+r][m] T[m][16bj+c]
-      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      float x = 0.f;
-      for (int m = 16 * bj; m < 16 * bi; ++m) x = fmaf(lm[(16 * bi + r) * 65 + m], tm[m * 65 + 16 * bj + c], x);
-      xbuf[e] = x;
-    }
-    __syncthreads();
-    for (int e = tid; e < bi * 256; e += 128) {  // T_bi,bj = -T_bi,bi X_bj
-      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      float t = 0.f;
-#pragma unroll
-      for (int m = 0; m < 16; ++m) t = fmaf(tm[(16 * bi + r) * 65 + 16 * bi + m], xbuf[bj * 256 + m * 16 + c], t);
-      tm[(16 * bi + r) * 65 + 16 * bj + c] = -t;
-    }
-    __syncthreads();
-  }
-}
+using namespace fast;
 
 // ------------------------------------------------------------------------------------------------
 // prep: one CTA (128 threads) per (chunk, value head)
@@ -480,10 +403,9 @@ int smem_attr(K kernel, int bytes) {
 }  // namespace
 
 size_t fast_workspace_size(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int max_chunks) {
-  (void)Hk;
   Carver c(nullptr);
   FastWs w;
-  return carve_fast(c, w, tokens, n_seqs, Hv, max_chunks);
+  return carve_fast(c, w, tokens, n_seqs, Hv, max_chunks, Hk != Hv);
 }
 
 static int check_err_word(const FastWs& w, cudaStream_t s, bool sync) {
@@ -494,7 +416,7 @@ static int check_err_word(const FastWs& w, cudaStream_t s, bool sync) {
 int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_t s) {
   Carver c(wsp);
   FastWs w;
-  carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks);
+  carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks, p.group > 1);
   int rc = launch_chunk_table(p, w.ct, s);
   if (rc) return rc;
   RB2_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), s), "gdn fast: clear status");
@@ -513,11 +435,5 @@ int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_
   return check_err_word(w, s, false);
 }
 
-int fast_backward(const GdnProblem& p, void* ws, const void* d_o, const float* dhT, void* dq, void* dk, void* dv,
-                  float* dg, void* dbeta, float* dh0, cudaStream_t s) {
-  (void)p; (void)ws; (void)d_o; (void)dhT; (void)dq; (void)dk; (void)dv; (void)dg; (void)dbeta; (void)dh0; (void)s;
-  set_error("gdn: tensor-core backward not built yet");
-  return RB2_EUNSUPPORTED;
-}
 
 }  // namespace rb2

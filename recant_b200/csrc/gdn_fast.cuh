@@ -1,0 +1,99 @@
+// Shared declarations of the tensor-core GDN path (gdn_fast.cu forward, gdn_fast_bwd.cu backward).
+#pragma once
+
+#include "gdn_common.cuh"
+#include "tc.cuh"
+
+namespace rb2 {
+
+struct FastWs {
+  ChunkTable ct;
+  float* stats;          // [ch][4][64] cum, rq, rk, beta
+  float* tinv;           // [ch][64][64]
+  __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal
+  __nv_bfloat16* w;      // [ch][64][128]
+  __nv_bfloat16* u;      // [ch][64][128]
+  __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q
+  __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k
+  __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk]
+  __nv_bfloat16* vp;     // [ch][64][128]  V'
+  __nv_bfloat16* dh;     // [ch][128][128] dS^T of the state leaving the chunk, [dv][dk]
+  __nv_bfloat16* dvp;    // [ch][64][128]  dV'
+  float* dqh;            // [tokens][Hv][128] per-value-head dq (GQA only)
+  float* dkh;            // [tokens][Hv][128]
+  int* err;              // device status word
+};
+
+size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks, bool gqa);
+
+namespace fast {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+  return p + ((1024 - (tc::smem_u32(p) & 1023)) & 1023);
+}
+
+// Copy `nrows` rows of 128 bf16 (row stride `stride` elements) into rows [r0, r0+nrows) of a
+// K-major SW128 tile with `tile_rows` rows; rows >= L are zero. All `nthr` threads participate.
+__device__ __forceinline__ void load_rows_sw128(unsigned char* tile, int tile_rows, int r0, const bf16* src,
+                                                int64_t stride, int nrows, int L, int nthr) {
+  for (int idx = threadIdx.x; idx < nrows * 16; idx += nthr) {
+    const int r = idx >> 4, c8 = idx & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < L) v = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r0 + r, c8 * 8, tile_rows)) = v;
+  }
+}
+
+// Same for a plain row-major [64][128] bf16 smem tile (no swizzle).
+__device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int64_t stride, int nthr) {
+  for (int idx = threadIdx.x; idx < 64 * 16; idx += nthr) {
+    const int r = idx >> 4, c8 = idx & 15;
+    *reinterpret_cast<uint4*>(tile + r * 128 + c8 * 8) = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
+  }
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
+
+// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65), 128 threads.
+__device__ inline void unit_lower_inverse128(const float* lm, float* tm, float* xbuf) {
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  for (int idx = tid; idx < 64 * 65; idx += 128) tm[idx] = 0.f;
+  __syncthreads();
+  if (l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
+    const int o = 16 * w;
+    float col[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float t = (i == l) ? 1.f : 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) t = fmaf(-lm[(o + i) * 65 + o + m], col[m], t);
+      col[i] = t;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tm[(o + i) * 65 + o + l] = col[i];
+  }
+  __syncthreads();
+  for (int bi = 1; bi < 4; ++bi) {
+    for (int e = tid; e < bi * 256; e += 128) {  // X_bj = sum_{m in [16bj, 16bi)} L[16bi+r][m] T[m][16bj+c]
+      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      float x = 0.f;
+      for (int m = 16 * bj; m < 16 * bi; ++m) x = fmaf(lm[(16 * bi + r) * 65 + m], tm[m * 65 + 16 * bj + c], x);
+      xbuf[e] = x;
+    }
+    __syncthreads();
+    for (int e = tid; e < bi * 256; e += 128) {  // T_bi,bj = -T_bi,bi X_bj
+      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      float t = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) t = fmaf(tm[(16 * bi + r) * 65 + 16 * bi + m], xbuf[bj * 256 + m * 16 + c], t);
+      tm[(16 * bi + r) * 65 + 16 * bj + c] = -t;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace fast
+}  // namespace rb2

@@ -1,0 +1,655 @@
+// Chunked Gated DeltaNet backward on tcgen05 (the autograd of recant.model.ops.gdn_torch,
+// recant/model/ops.py:21-54, written out by hand).
+//
+// Per chunk, with S the state entering it and dS the gradient of the state leaving it:
+//   reversed walk (per sequence x head, sequential):
+//     dV'^T = dO^T A_qk + dS^T k~^T                         M=dv, N=64, K=64 and K=dk
+//     dS^T  <- gamma dS^T + dO^T q~ - dV'^T W               M=dv, N=dk, K=64 (negated A)
+//   chunk backward (per chunk x head, parallel), transposed so d is the MMA's M wherever the
+//   output is [d][tok]; 64x64 token-by-token products use M=64 (rows in lanes 0-15 of each
+//   32-lane quarter):
+//     dq~^T = S dO^T, dW^T = -S dV'^T, dk~^T = dS V'^T, dA_qk = dO V'^T      (G1)
+//     dT = dV' (beta V)^T + dW (beta e^cum r_k K)^T, dBv^T = dV'^T T, dBk^T = dW^T T   (G2)
+//     Y = T^T dT (G3);  dL = -Y T^T (G4)
+//     dk^ += diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^,  dq^ += Qm k^   (G5)
+//       with P = dL * Gamma (strictly lower) and Qm = dA_qk * Gamma
+//   then the decay factors, beta, the cumulative gate (reverse cumsum -> dg) and the l2norm.
+#include "gdn_fast.cuh"
+
+namespace rb2 {
+namespace {
+
+using namespace fast;
+
+// Sum v[0..63] over the 32 lanes of the warp by a halving butterfly; afterwards this lane holds
+// the totals of columns c0 and c0 + 1 in v[0], v[1] (c0 from colsum_base()).
+__device__ __forceinline__ void warp_colsum64(float (&v)[64]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int s = 16 >> step, c = 64 >> step;
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < c / 2; ++j) {
+      const float send = up ? v[j] : v[j + c / 2];
+      const float keep = up ? v[j + c / 2] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+}
+__device__ __forceinline__ int colsum_base() {
+  const int l = threadIdx.x & 31;
+  return ((l & 16) ? 32 : 0) + ((l & 8) ? 16 : 0) + ((l & 4) ? 8 : 0) + ((l & 2) ? 4 : 0) + ((l & 1) ? 2 : 0);
+}
+// Column sums of a 128 x 64 matrix held one row per thread (128 threads); out[64] in smem.
+__device__ __forceinline__ void block_colsum64(float (&v)[64], float* red, float* out) {
+  warp_colsum64(v);
+  const int w = threadIdx.x >> 5, c0 = colsum_base();
+  red[w * 64 + c0] = v[0];
+  red[w * 64 + c0 + 1] = v[1];
+  __syncthreads();
+  if (threadIdx.x < 64) out[threadIdx.x] = red[threadIdx.x] + red[64 + threadIdx.x] + red[128 + threadIdx.x] + red[192 + threadIdx.x];
+  __syncthreads();
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t addr, float (&v)[64]) {
+  float a[32];
+  tc::tmem_ld32(addr, a);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = a[j];
+  tc::tmem_ld32(addr + 32, a);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[32 + j] = a[j];
+}
+
+// Write 64 fp32 values as one bf16 row (64 elements) of a K-major SW128 tile with `rows` rows.
+__device__ __forceinline__ void store_row64(unsigned char* tile, int rows, int r, const float (&v)[64]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                               tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, 8 * j, rows)) = x;
+  }
+}
+
+__device__ __forceinline__ float tile_elem(const unsigned char* tile, int rows, int r, int k) {
+  return __bfloat162float(*reinterpret_cast<const bf16*>(tile + tc::sw128_offset(r, k, rows)));
+}
+
+__device__ __forceinline__ void sync_for_mma() {
+  tc::fence_proxy_async();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+}
+
+// ------------------------------------------------------------------------------------------------
+// reversed state walk: one CTA (256 threads) per (sequence, value head); thread = (dv row, dk half)
+// ------------------------------------------------------------------------------------------------
+constexpr int kBStateSmem = 32768 + 16384 + 8192 + 16384 * 3 + 16384 + 64 * 4 + 2048;
+
+__global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
+                                                                 const float* __restrict__ dhT, float* __restrict__ dh0) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = align1024(smem_raw);
+  unsigned char* dst = sm;              // dS^T bf16, rows dv (128) x dk               32 KB
+  unsigned char* dot = dst + 32768;     // dO rows tok (64) x dv                        16 KB
+  unsigned char* at = dot + 16384;      // A_qk rows i x c                               8 KB
+  unsigned char* kt = at + 8192;        // k~ rows tok x dk                             16 KB
+  unsigned char* qt = kt + 16384;       // q~                                           16 KB
+  unsigned char* wt = qt + 16384;       // W                                            16 KB
+  unsigned char* dvt = wt + 16384;      // dV'^T rows dv x tok                          16 KB
+  float* cum = reinterpret_cast<float*>(dvt + 16384);
+  __shared__ uint64_t bar[2];
+  __shared__ uint32_t tmem_base;
+
+  const int h = blockIdx.x, s = blockIdx.y;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int r = 32 * (w & 3) + l, hh = w >> 2;
+  if (w == 0) tc::tmem_alloc(&tmem_base, 512);
+  if (tid == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  float dS[64];
+  const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
+#pragma unroll
+  for (int j = 0; j < 64; ++j) dS[j] = dhT ? dhT[sbase + (64 * hh + j) * 128 + r] : 0.f;
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16);
+  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
+  uint32_t phase = 0;
+  for (int ci = c1 - 1; ci >= c0; --ci) {
+    const int64_t ch = int64_t(ci) * p.Hv + h;
+    const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
+    {
+      uint32_t pk[32];
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) pk[j >> 1] = tc::pack_bf16(dS[j], dS[j + 1]);
+      uint4* gdst = reinterpret_cast<uint4*>(ws.dh + ch * 16384 + r * 128 + 64 * hh);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        *reinterpret_cast<uint4*>(dst + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
+        gdst[j] = v4;
+      }
+    }
+    load_rows_sw128(dot, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, 64, L, 256);
+    for (int idx = tid; idx < 64 * 8; idx += 256) {
+      const int i = idx >> 3, c8 = idx & 7;
+      *reinterpret_cast<uint4*>(at + tc::sw128_offset(i, c8 * 8, 64)) =
+          __ldg(reinterpret_cast<const uint4*>(ws.aqk + ch * 4096 + i * 64 + c8 * 8));
+    }
+    load_rows_sw128(kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
+    load_rows_sw128(qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
+    load_rows_sw128(wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
+    if (tid < 64) cum[tid] = ws.stats[ch * 256 + tid];
+    sync_for_mma();
+    if (tid == 0) {
+      const uint32_t doa = tc::smem_u32(dot), aa = tc::smem_u32(at), da = tc::smem_u32(dst), ka = tc::smem_u32(kt),
+                     qa = tc::smem_u32(qt);
+      // dV'^T = dO^T A_qk (A = dO MN-major: M = dv, K = tok; B = A_qk MN-major: N = c, K = i)
+      const uint32_t id_a = tc::idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int k0 = 0; k0 < 64; k0 += 16)
+        tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(doa + k0 * 128, 8192), tc::desc_mnmajor_sw128(aa + k0 * 128, 8192),
+                     id_a, k0 > 0);
+      // dV'^T += dS^T k~^T (A = dS^T K-major: M = dv, K = dk; B = k~ K-major: N = tok, K = dk)
+      const uint32_t id_b = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+      for (int k0 = 0; k0 < 128; k0 += 16)
+        tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(da + (k0 >> 6) * 16384 + (k0 & 63) * 2),
+                     tc::desc_kmajor_sw128(ka + (k0 >> 6) * 8192 + (k0 & 63) * 2), id_b, true);
+      // D_s = dO^T q~ (A = dO MN-major; B = q~ MN-major: N = dk, K = tok)
+      const uint32_t id_s = tc::idesc_bf16(128, 128, true, true);
+#pragma unroll
+      for (int k0 = 0; k0 < 64; k0 += 16)
+        tc::mma_bf16(tbase + 256, tc::desc_mnmajor_sw128(doa + k0 * 128, 8192), tc::desc_mnmajor_sw128(qa + k0 * 128, 8192),
+                     id_s, k0 > 0);
+      tc::mma_commit(&bar[0]);
+    }
+    tc::mbar_wait(&bar[0], phase, ws.err, 121);
+    tc::fence_after_sync();
+    {
+      float x[32];
+      tc::tmem_ld32(lane_addr + 32 * hh, x);
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
+        const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(&pk[j >> 1]);
+        const int tk = 32 * hh + j;
+        ws.dvp[ch * 8192 + tk * 128 + r] = ab.x;
+        ws.dvp[ch * 8192 + (tk + 1) * 128 + r] = ab.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(dvt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
+            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+    }
+    sync_for_mma();
+    if (tid == 0) {
+      // D_s -= dV'^T W (A = dV'^T K-major: M = dv, K = tok, negated; B = W MN-major: N = dk, K = tok)
+      const uint32_t va = tc::smem_u32(dvt), wa = tc::smem_u32(wt);
+      const uint32_t id_w = tc::idesc_bf16(128, 128, false, true, true);
+#pragma unroll
+      for (int k0 = 0; k0 < 64; k0 += 16)
+        tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_mnmajor_sw128(wa + k0 * 128, 8192), id_w, true);
+      tc::mma_commit(&bar[1]);
+    }
+    tc::mbar_wait(&bar[1], phase, ws.err, 122);
+    tc::fence_after_sync();
+    {
+      const float gamma = expf(cum[63]);
+      float x[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tc::tmem_ld32(lane_addr + 256 + 64 * hh + 32 * half, x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dS[32 * half + j] = fmaf(gamma, dS[32 * half + j], x[j]);
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    phase ^= 1;
+  }
+  if (dh0) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) dh0[sbase + (64 * hh + j) * 128 + r] = dS[j];
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (w == 0) tc::tmem_dealloc(tbase, 512);
+}
+
+// ------------------------------------------------------------------------------------------------
+// chunk backward: one CTA (128 threads) per (chunk, value head)
+// ------------------------------------------------------------------------------------------------
+namespace lay {  // shared-memory map (bytes from the 1024-aligned base)
+constexpr int KQ = 0, VT = 32768, DVP = 49152;
+constexpr int ST = 65536, DHT = 98304, DOT = 131072, VPT = 147456;           // phase 1
+constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  // phase 2 (over phase 1)
+              YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
+constexpr int QB2 = VT;                                                        // over V once consumed
+constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
+constexpr int VEC = DAQF + 16640;                                              // 8 x 64 floats
+constexpr int RED = VEC + 8 * 256;                                             // 4 x 64 floats
+constexpr int END = RED + 1024 + 64;
+}  // namespace lay
+constexpr int kBChunkSmem = lay::END + 1024;
+
+__global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
+                                                                 bf16* __restrict__ dq, bf16* __restrict__ dk,
+                                                                 bf16* __restrict__ dv, float* __restrict__ dg,
+                                                                 bf16* __restrict__ dbeta) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = align1024(smem_raw);
+  float* kkf = reinterpret_cast<float*>(sm + lay::KKF);
+  float* qkf = reinterpret_cast<float*>(sm + lay::QKF);
+  float* daqf = reinterpret_cast<float*>(sm + lay::DAQF);
+  float* vec = reinterpret_cast<float*>(sm + lay::VEC);
+  float *cum = vec, *rq = vec + 64, *rk = vec + 128, *beta = vec + 192, *ecum = vec + 256, *edec = vec + 320,
+        *dbeta_acc = vec + 384, *dcum_acc = vec + 448;
+  float* red = reinterpret_cast<float*>(sm + lay::RED);
+  float* scal = red + 256;  // [0] = dgamma, [1..] scratch
+  __shared__ float colbuf[64];
+  __shared__ uint64_t bar[5];
+  __shared__ uint32_t tmem_base;
+
+  const int ci = blockIdx.x, h = blockIdx.y;
+  if (ci >= *ws.ct.n_chunks) return;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
+  const int64_t ch = int64_t(ci) * p.Hv + h;
+  const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
+
+  if (w == 0) tc::tmem_alloc(&tmem_base, 512);
+  if (tid == 0) {
+    for (int i = 0; i < 5; ++i) tc::mbar_init(&bar[i], 1);
+    tc::fence_mbar_init();
+  }
+  // ---- loads ---------------------------------------------------------------------------------
+  load_rows_sw128(sm + lay::KQ, 128, 0, static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 128);
+  load_rows_sw128(sm + lay::KQ, 128, 64, static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 128);
+  load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 128);
+  load_rows_sw128(sm + lay::DVP, 64, 0, ws.dvp + ch * 8192, 128, 64, 64, 128);
+  load_rows_sw128(sm + lay::ST, 128, 0, ws.hs + ch * 16384, 128, 128, 128, 128);
+  load_rows_sw128(sm + lay::DHT, 128, 0, ws.dh + ch * 16384, 128, 128, 128, 128);
+  load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 128);
+  load_rows_sw128(sm + lay::VPT, 64, 0, ws.vp + ch * 8192, 128, 64, 64, 128);
+  if (tid < 64) {
+    const float* st = ws.stats + ch * 256;
+    cum[tid] = st[tid]; rq[tid] = st[64 + tid]; rk[tid] = st[128 + tid]; beta[tid] = st[192 + tid];
+    ecum[tid] = expf(st[tid]);
+    edec[tid] = expf(st[63] - st[tid]);
+    dbeta_acc[tid] = 0.f;
+    dcum_acc[tid] = 0.f;
+  }
+  sync_for_mma();
+  const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + (uint32_t(32 * w) << 16);
+  const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
+  if (tid == 0) {  // ---- G1 ----
+    const uint32_t sta = tc::smem_u32(sm + lay::ST), dha = tc::smem_u32(sm + lay::DHT), doa = tc::smem_u32(sm + lay::DOT),
+                   vpa = tc::smem_u32(sm + lay::VPT), dva = tc::smem_u32(sm + lay::DVP);
+    const uint32_t id_kk = tc::idesc_bf16(128, 64, false, false);
+    const uint32_t id_s = tc::idesc_bf16(128, 64, true, false);
+    const uint32_t id_sn = tc::idesc_bf16(128, 64, true, false, true);
+    const uint32_t id_64 = tc::idesc_bf16(64, 64, false, false);
+#pragma unroll
+    for (int k0 = 0; k0 < 128; k0 += 16) {
+      const uint32_t o16 = (k0 >> 6) * 16384 + (k0 & 63) * 2, o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
+      const bool acc = k0 > 0;
+      tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(kqa + o16), tc::desc_kmajor_sw128(kqa + o16), id_kk, acc);
+      tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_kmajor_sw128(doa + o8), id_s, acc);
+      tc::mma_bf16(tbase + 128, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_kmajor_sw128(dva + o8), id_sn, acc);
+      tc::mma_bf16(tbase + 192, tc::desc_mnmajor_sw128(dha + k0 * 128, 16384), tc::desc_kmajor_sw128(vpa + o8), id_s, acc);
+      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(doa + o8), tc::desc_kmajor_sw128(vpa + o8), id_64, acc);
+    }
+    tc::mma_commit(&bar[0]);
+  }
+  {  // dgamma = sum S^T * dS^T while G1 runs (both tiles share one layout)
+    float part = 0.f;
+    for (int idx = tid; idx < 128 * 16; idx += 128) {
+      const uint32_t off = uint32_t(idx) * 16;
+      const uint4 a = *reinterpret_cast<const uint4*>(sm + lay::ST + off);
+      const uint4 b = *reinterpret_cast<const uint4*>(sm + lay::DHT + off);
+      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) part += bf_lo(av[j]) * bf_lo(bv[j]) + bf_hi(av[j]) * bf_hi(bv[j]);
+    }
+    part = warp_sum(part);
+    if (l == 0) red[w] = part;
+  }
+  __syncthreads();
+  if (tid == 0) scal[0] = red[0] + red[1] + red[2] + red[3];
+  tc::mbar_wait(&bar[0], 0, ws.err, 131);
+  tc::fence_after_sync();
+  // ---- E1 ------------------------------------------------------------------------------------
+  {
+    float v[64];
+    tmem_ld64(lane_addr + 0, v);  // lanes 0-63: kk rows, 64-127: qk rows
+    float* dstf = tid < 64 ? kkf + tid * 65 : qkf + (tid - 64) * 65;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) dstf[j] = v[j];
+    tmem_ld64(lane_addr + 128, v);  // dW^T row dk = tid
+    store_row64(sm + lay::DWT, 128, tid, v);
+    tmem_ld64(lane_addr + 256, v);  // dA_qk (M = 64): lanes 0-15 of each quarter
+    if (l < 16) {
+      const int i = 16 * w + l;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) daqf[i * 65 + j] = j <= i ? v[j] : 0.f;
+    }
+  }
+  for (int idx = tid; idx < 64 * 16; idx += 128) {  // beta V and beta e^cum rk K (rows m)
+    const int m = idx >> 4, c8 = (idx & 15) * 8;
+    const uint4 xv = *reinterpret_cast<const uint4*>(sm + lay::VT + tc::sw128_offset(m, c8, 64));
+    const uint4 xk = *reinterpret_cast<const uint4*>(sm + lay::KQ + tc::sw128_offset(m, c8, 128));
+    const float fv = beta[m], fk = beta[m] * ecum[m] * rk[m];
+    const uint32_t av[4] = {xv.x, xv.y, xv.z, xv.w}, ak[4] = {xk.x, xk.y, xk.z, xk.w};
+    uint32_t ov[4], ok[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ov[j] = tc::pack_bf16(bf_lo(av[j]) * fv, bf_hi(av[j]) * fv);
+      ok[j] = tc::pack_bf16(bf_lo(ak[j]) * fk, bf_hi(ak[j]) * fk);
+    }
+    *reinterpret_cast<uint4*>(sm + lay::BV + tc::sw128_offset(m, c8, 64)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+    *reinterpret_cast<uint4*>(sm + lay::BK + tc::sw128_offset(m, c8, 64)) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
+  }
+  for (int idx = tid; idx < 64 * 8; idx += 128) {  // T (bf16) rows i
+    const int i = idx >> 3, c8 = (idx & 7) * 8;
+    const float4 a = *reinterpret_cast<const float4*>(ws.tinv + ch * 4096 + i * 64 + c8);
+    const float4 b = *reinterpret_cast<const float4*>(ws.tinv + ch * 4096 + i * 64 + c8 + 4);
+    *reinterpret_cast<uint4*>(sm + lay::TT + tc::sw128_offset(i, c8, 64)) =
+        make_uint4(tc::pack_bf16(a.x, a.y), tc::pack_bf16(a.z, a.w), tc::pack_bf16(b.x, b.y), tc::pack_bf16(b.z, b.w));
+  }
+  sync_for_mma();
+  const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
+  if (tid == 0) {  // ---- G2 ----
+    const uint32_t dva = tc::smem_u32(sm + lay::DVP), bva = tc::smem_u32(sm + lay::BV), bka = tc::smem_u32(sm + lay::BK);
+    const uint32_t id_t1 = tc::idesc_bf16(64, 64, false, false), id_t2 = tc::idesc_bf16(64, 64, true, false);
+#pragma unroll
+    for (int k0 = 0; k0 < 128; k0 += 16) {
+      const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
+      tc::mma_bf16(tbase + 320, tc::desc_kmajor_sw128(dva + o8), tc::desc_kmajor_sw128(bva + o8), id_t1, k0 > 0);
+    }
+#pragma unroll
+    for (int k0 = 0; k0 < 128; k0 += 16) {
+      const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
+      tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dwa + k0 * 128, 16384), tc::desc_kmajor_sw128(bka + o8), id_t2, true);
+    }
+    const uint32_t id_bv = tc::idesc_bf16(128, 64, true, true), id_bk = tc::idesc_bf16(128, 64, false, true);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16) {
+      tc::mma_bf16(tbase + 384, tc::desc_mnmajor_sw128(dva + k0 * 128, 8192), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192),
+                   id_bv, k0 > 0);
+      tc::mma_bf16(tbase + 448, tc::desc_kmajor_sw128(dwa + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bk,
+                   k0 > 0);
+    }
+    tc::mma_commit(&bar[1]);
+  }
+  tc::mbar_wait(&bar[1], 0, ws.err, 132);
+  tc::fence_after_sync();
+  // ---- E2 ------------------------------------------------------------------------------------
+  {
+    float v[64];
+    tmem_ld64(lane_addr + 320, v);  // dT (M = 64)
+    if (l < 16) {
+      const int i = 16 * w + l;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] = j <= i ? v[j] : 0.f;
+      store_row64(sm + lay::DTT, 64, i, v);
+    }
+    tmem_ld64(lane_addr + 384, v);  // dBv^T row dv = tid
+    const int r = tid;
+#pragma unroll
+    for (int m = 0; m < 64; ++m) {
+      if (m < L) dv[(int64_t(t0 + m) * p.Hv + h) * 128 + r] = __float2bfloat16_rn(beta[m] * v[m]);
+      v[m] *= tile_elem(sm + lay::VT, 64, m, r);
+    }
+    block_colsum64(v, red, colbuf);
+    if (tid < 64) dbeta_acc[tid] += colbuf[tid];
+  }
+  sync_for_mma();
+  if (tid == 0) {  // ---- G3: Y = T^T dT ----
+    const uint32_t dta = tc::smem_u32(sm + lay::DTT);
+    const uint32_t id_y = tc::idesc_bf16(64, 64, true, true);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16)
+      tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), tc::desc_mnmajor_sw128(dta + k0 * 128, 8192),
+                   id_y, k0 > 0);
+    tc::mma_commit(&bar[2]);
+  }
+  tc::mbar_wait(&bar[2], 0, ws.err, 133);
+  tc::fence_after_sync();
+  {
+    float v[64];
+    tmem_ld64(lane_addr + 0, v);
+    if (l < 16) store_row64(sm + lay::YT, 64, 16 * w + l, v);
+  }
+  sync_for_mma();
+  if (tid == 0) {  // ---- G4: dL' = Y T^T ----
+    const uint32_t ya = tc::smem_u32(sm + lay::YT);
+    const uint32_t id_l = tc::idesc_bf16(64, 64, false, false);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16)
+      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
+    tc::mma_commit(&bar[3]);
+  }
+  tc::mbar_wait(&bar[3], 0, ws.err, 134);
+  tc::fence_after_sync();
+  // ---- E4: P, Qm, R and the B operands of G5 -------------------------------------------------
+  {
+    float v[64];
+    tmem_ld64(lane_addr + 256, v);
+    if (l < 16) {
+      const int i = 16 * w + l;
+      const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
+      float db = 0.f;
+      float pb1[64], qb1[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const float gam = j <= i ? expf(ci_ - cum[j]) : 0.f;
+        const float dl = j < i ? -v[j] : 0.f;
+        const float P = dl * gam;
+        const float kkn = kkf[i * 65 + j] * rki * rk[j];
+        const float qkn = qkf[i * 65 + j] * sqi * rk[j];
+        const float daq = daqf[i * 65 + j];
+        db = fmaf(P, kkn, db);
+        kkf[i * 65 + j] = P * bi * kkn + daq * qkn * gam;  // R
+        const float qm = daq * gam;
+        v[j] = P;
+        pb1[j] = bi * rk[j] * P;
+        qb1[j] = rk[j] * qm;
+        daqf[i * 65 + j] = qm;
+      }
+      dbeta_acc[i] += db;
+      store_row64(sm + lay::PB1, 64, i, pb1);
+      store_row64(sm + lay::QB1, 64, i, qb1);
+#pragma unroll
+      for (int j = 0; j < 64; ++j) { pb1[j] = bi * rki * v[j]; qb1[j] = sqi * daqf[i * 65 + j]; }
+      store_row64(sm + lay::PB2, 64, i, pb1);
+      store_row64(sm + lay::QB2, 64, i, qb1);
+    }
+  }
+  sync_for_mma();
+  if (tid == 0) {  // ---- G5 ----
+    const uint32_t p1 = tc::smem_u32(sm + lay::PB1), p2 = tc::smem_u32(sm + lay::PB2), q1 = tc::smem_u32(sm + lay::QB1),
+                   q2 = tc::smem_u32(sm + lay::QB2);
+    const uint32_t id_k = tc::idesc_bf16(128, 64, true, false), id_m = tc::idesc_bf16(128, 64, true, true);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16) {
+      const uint64_t ka = tc::desc_mnmajor_sw128(kqa + k0 * 128, 16384);         // K rows as (M = dk, K = j)
+      const uint64_t qa = tc::desc_mnmajor_sw128(kqa + 8192 + k0 * 128, 16384);  // Q rows (start at row 64)
+      tc::mma_bf16(tbase + 320, ka, tc::desc_kmajor_sw128(p1 + k0 * 2), id_k, k0 > 0);
+      tc::mma_bf16(tbase + 320, ka, tc::desc_mnmajor_sw128(p2 + k0 * 128, 8192), id_m, true);
+      tc::mma_bf16(tbase + 320, qa, tc::desc_mnmajor_sw128(q2 + k0 * 128, 8192), id_m, true);
+      tc::mma_bf16(tbase + 0, ka, tc::desc_kmajor_sw128(q1 + k0 * 2), id_k, k0 > 0);
+    }
+    tc::mma_commit(&bar[4]);
+  }
+  if (tid < 64) {  // dcum_i += sum_j R_ij - sum_j R_ji
+    float a = 0.f;
+    for (int j = 0; j < 64; ++j) a += kkf[tid * 65 + j] - kkf[j * 65 + tid];
+    dcum_acc[tid] += a;
+  }
+  tc::mbar_wait(&bar[4], 0, ws.err, 135);
+  tc::fence_after_sync();
+  // ---- final epilogue: thread = head-dim row r; columns = tokens -----------------------------
+  const int r = tid;
+  float qr[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) qr[i] = tile_elem(sm + lay::KQ, 128, 64 + i, r);
+  float a1_mine;
+  {
+    float v[64];
+    tmem_ld64(lane_addr + 64, v);  // dq~^T
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] *= qr[i];
+    block_colsum64(v, red, colbuf);
+    a1_mine = tid < 64 ? colbuf[tid] : 0.f;
+  }
+  {
+    float dqh[64], v[64];
+    tmem_ld64(lane_addr + 0, dqh);   // (Qm k^)^T
+    tmem_ld64(lane_addr + 64, v);    // dq~^T
+#pragma unroll
+    for (int i = 0; i < 64; ++i) { dqh[i] = p.scale * fmaf(ecum[i], v[i], dqh[i]); v[i] = dqh[i] * qr[i]; }
+    block_colsum64(v, red, colbuf);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      if (i < L) {
+        const float rqi = rq[i];
+        const float gq = rqi * dqh[i] - qr[i] * rqi * rqi * rqi * colbuf[i];
+        if (p.group == 1) dq[(int64_t(t0 + i) * p.Hk + hk) * 128 + r] = __float2bfloat16_rn(gq);
+        else ws.dqh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gq;
+      }
+    }
+  }
+  __syncthreads();
+  float kr[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) kr[i] = tile_elem(sm + lay::KQ, 128, i, r);
+  float a2_mine, a3_mine;
+  {
+    float v[64];
+    tmem_ld64(lane_addr + 192, v);  // dk~^T
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] *= kr[i];
+    block_colsum64(v, red, colbuf);
+    a2_mine = tid < 64 ? colbuf[tid] : 0.f;
+    tmem_ld64(lane_addr + 448, v);  // dBk^T
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] *= kr[i];
+    block_colsum64(v, red, colbuf);
+    a3_mine = tid < 64 ? colbuf[tid] : 0.f;
+  }
+  {
+    float dkh[64], v[64];
+    tmem_ld64(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
+    tmem_ld64(lane_addr + 192, v);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) dkh[i] = fmaf(edec[i], v[i], dkh[i]);
+    tmem_ld64(lane_addr + 448, v);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) { dkh[i] = fmaf(beta[i] * ecum[i], v[i], dkh[i]); v[i] = dkh[i] * kr[i]; }
+    block_colsum64(v, red, colbuf);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      if (i < L) {
+        const float rki = rk[i];
+        const float gk = rki * dkh[i] - kr[i] * rki * rki * rki * colbuf[i];
+        if (p.group == 1) dk[(int64_t(t0 + i) * p.Hk + hk) * 128 + r] = __float2bfloat16_rn(gk);
+        else ws.dkh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gk;
+      }
+    }
+  }
+  // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------
+  if (tid < 64) {
+    const int i = tid;
+    const float z = edec[i] * rk[i] * a2_mine;
+    const float colk = rk[i] * a3_mine;
+    dcum_acc[i] += ecum[i] * p.scale * rq[i] * a1_mine - z + beta[i] * ecum[i] * colk;
+    dbeta_acc[i] += ecum[i] * colk;
+    red[i] = z;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float dcl = scal[0] * expf(cum[63]);
+    for (int i = 0; i < 64; ++i) dcl += red[i];
+    dcum_acc[63] += dcl;
+    double acc = 0.0;
+    for (int i = 63; i >= 0; --i) {
+      acc += double(dcum_acc[i]);
+      if (i < L) dg[int64_t(t0 + i) * p.Hv + h] = float(acc);
+    }
+  }
+  if (tid < L && tid < 64) dbeta[int64_t(t0 + tid) * p.Hv + h] = __float2bfloat16_rn(dbeta_acc[tid]);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (w == 0) tc::tmem_dealloc(tbase, 512);
+}
+
+__global__ void __launch_bounds__(256) fast_gqa_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ dq,
+                                                       bf16* __restrict__ dk) {
+  const int64_t n = p.tokens * p.Hk * 128;
+  for (int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * 256) {
+    const int64_t c = idx & 127, th = idx >> 7, hk = th % p.Hk, tok = th / p.Hk;
+    float aq = 0.f, ak = 0.f;
+    for (int g = 0; g < p.group; ++g) {
+      const int64_t src = (tok * p.Hv + hk * p.group + g) * 128 + c;
+      aq += ws.dqh[src];
+      ak += ws.dkh[src];
+    }
+    dq[idx] = __float2bfloat16_rn(aq);
+    dk[idx] = __float2bfloat16_rn(ak);
+  }
+}
+
+template <typename K>
+int smem_attr_b(K kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return RB2_ECUDA;
+  }
+  return RB2_OK;
+}
+
+}  // namespace
+
+int fast_backward(const GdnProblem& p, void* wsp, const void* d_o, const float* dhT, void* dq, void* dk, void* dv,
+                  float* dg, void* dbeta, float* dh0, cudaStream_t s) {
+  Carver c(wsp);
+  FastWs w;
+  carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks, p.group > 1);
+  int rc;
+  if ((rc = smem_attr_b(fast_state_bwd_kernel, kBStateSmem))) return rc;
+  {
+    ProfScope ps_("gdn_fast_state_bwd", s);
+    fast_state_bwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kBStateSmem, s>>>(p, w, static_cast<const bf16*>(d_o),
+                                                                                    dhT, dh0);
+    RB2_CHECK_LAUNCH("gdn fast state bwd");
+  }
+  if (p.max_chunks > 0) {
+    if ((rc = smem_attr_b(fast_chunk_bwd_kernel, kBChunkSmem))) return rc;
+    {
+      ProfScope ps_("gdn_fast_chunk_bwd", s);
+      fast_chunk_bwd_kernel<<<dim3(p.max_chunks, p.Hv), 128, kBChunkSmem, s>>>(
+          p, w, static_cast<const bf16*>(d_o), static_cast<bf16*>(dq), static_cast<bf16*>(dk), static_cast<bf16*>(dv), dg,
+          static_cast<bf16*>(dbeta));
+      RB2_CHECK_LAUNCH("gdn fast chunk bwd");
+    }
+    if (p.group > 1) {
+      ProfScope ps_("gdn_fast_gqa", s);
+      fast_gqa_kernel<<<148 * 8, 256, 0, s>>>(p, w, static_cast<bf16*>(dq), static_cast<bf16*>(dk));
+      RB2_CHECK_LAUNCH("gdn fast gqa");
+    }
+  }
+  return RB2_OK;
+}
+
+}  // namespace rb2

@@ -48,3 +48,46 @@ def test_fast_forward_varlen():
     ro, rhT = OG.gdn(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], None, True, cu_seqlens=cu)
     o, hT = _fwd(inp, cu=cu)
     assert rel(o, ro) < TOL and rel(hT, rhT) < TOL, (rel(o, ro), rel(hT, rhT))
+
+
+def _check_grads(inp, do, h0=None, dht=None, cu=None):
+    from gpu_util import run_b200
+    f32 = {n: t.float() for n, t in inp.items()}
+    ro, rhT, rg = OG.gdn_fwd_bwd(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], do.float(), h0, dht,
+                                 cu_seqlens=cu)
+    o, hT, gr = run_b200(inp, do, h0, dht, cu=cu, path="fast")
+    errs = {"o": rel(o, ro), "hT": rel(hT, rhT)}
+    errs.update({"d" + n: rel(gr[n], rg[n]) for n in ("q", "k", "v", "g", "beta")})
+    if h0 is not None:
+        errs["dh0"] = rel(gr["h0"], rg["h0"])
+    bad = {k: v for k, v in errs.items() if not v < TOL}
+    assert not bad, (bad, errs)
+
+
+@pytest.mark.parametrize("B,T,Hk,Hv", [(1, 64, 1, 1), (2, 300, 2, 4), (1, 1024, 4, 8), (2, 130, 2, 2)])
+def test_fast_backward(B, T, Hk, Hv):
+    inp = I.gdn_inputs(B, T, Hk, Hv, 128, dtype=torch.bfloat16, seed=T + 7 * Hv)
+    do = I.grad_output(B, T, Hv, 128, dtype=torch.bfloat16, seed=T + 1)
+    _check_grads(inp, do)
+
+
+def test_fast_backward_state_grads_and_mild_gates():
+    inp = I.gdn_inputs(2, 200, 2, 2, 128, dtype=torch.bfloat16, seed=13)
+    gen = torch.Generator().manual_seed(13)
+    inp["g"] = -torch.rand(2, 200, 2, generator=gen) * 0.1
+    do = I.grad_output(2, 200, 2, 128, dtype=torch.bfloat16, seed=14)
+    h0 = torch.randn(2, 2, 128, 128, generator=gen) * 0.1
+    dht = torch.randn(2, 2, 128, 128, generator=gen) * 0.1
+    _check_grads(inp, do, h0, dht)
+
+
+def test_fast_backward_varlen():
+    lengths = [70, 1, 64, 0, 129, 33]
+    cu = I.cu_seqlens_of(lengths)
+    T = int(cu[-1])
+    inp = I.gdn_inputs(1, T, 2, 4, 128, dtype=torch.bfloat16, seed=21)
+    do = I.grad_output(1, T, 4, 128, dtype=torch.bfloat16, seed=22)
+    gen = torch.Generator().manual_seed(23)
+    h0 = torch.randn(len(lengths), 4, 128, 128, generator=gen) * 0.1
+    dht = torch.randn(len(lengths), 4, 128, 128, generator=gen) * 0.1
+    _check_grads(inp, do, h0, dht, cu)
