@@ -41,7 +41,7 @@ _MF = 2 * 64 * 64 * 128  # one 64x64x128 product
 KERNEL_FLOPS_PER_CH = {
     # tensor-core path: algorithmic matmul FLOPs each kernel performs per (chunk, head)
     "gdn_fast_prep": 4 * _MF, "gdn_fast_state_fwd": 7 * _MF, "gdn_fast_state_bwd": 7 * _MF,
-    "gdn_fast_chunk_bwd": 17 * _MF,
+    "gdn_fast_chunk_bwd": 18 * _MF,
     "gdn_exact_fwd_prep": 4 * _MF, "gdn_exact_fwd_state": 4 * _MF, "gdn_exact_fwd_out": 3 * _MF,
     "gdn_exact_bwd_state": 7 * _MF, "gdn_exact_bwd_mm": 7 * _MF, "gdn_exact_bwd_intra": 12 * _MF,
 }

@@ -92,10 +92,12 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
   load_rows_sw128(kq, 128, 0, k, qs, 64, L, 128);
   load_rows_sw128(kq, 128, 64, q, qs, 64, L, 128);
   load_rows_sw128(vt, 64, 0, v, vs, 64, L, 128);
+  tc::cp_async_commit();
   if (tid < 64) {
     gv[tid] = tid < L ? p.g[int64_t(t0 + tid) * p.Hv + h] : 0.f;
     beta[tid] = tid < L ? __bfloat162float(static_cast<const bf16*>(p.beta)[int64_t(t0 + tid) * p.Hv + h]) : 0.f;
   }
+  tc::cp_async_wait<0>();
   tc::fence_proxy_async();
   __syncthreads();
   tc::fence_after_sync();
@@ -242,20 +244,47 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
 // forward state walk: one CTA (256 threads) per (sequence, value head)
 //   thread (w, l): TMEM lane / dv row r = 32 (w & 3) + l, dk half hh = w >> 2
 // ------------------------------------------------------------------------------------------------
-constexpr int kStateSmem = 32768 + 16384 * 3 + 8192 + 16384 + 16384 + 64 * 4 + 2048;
+constexpr int kStageBytes = 16384 * 4 + 8192 + 1024;  // W, q~, k~, U, A_qk, cum (1024-byte multiple)
+constexpr int kStateSmem = 32768 + 16384 + 2 * kStageBytes + 2048;
+
+struct FwdStage {
+  unsigned char* wt;   // W   64 rows (tok) x 128 (dk)        16 KB
+  unsigned char* qt;   // q~  64 x 128                         16 KB
+  unsigned char* kt;   // k~  64 x 128 (used MN-major: N = dk) 16 KB
+  bf16* us;            // U plain [64][128]                    16 KB
+  unsigned char* at;   // A_qk 64 (i) x 64 (j)                  8 KB
+  float* cum;          // 64 floats
+};
+
+__device__ __forceinline__ FwdStage fwd_stage(unsigned char* base, int stg) {
+  unsigned char* b = base + stg * kStageBytes;
+  FwdStage st;
+  st.wt = b;
+  st.qt = b + 16384;
+  st.kt = b + 32768;
+  st.us = reinterpret_cast<bf16*>(b + 49152);
+  st.at = b + 65536;
+  st.cum = reinterpret_cast<float*>(b + 65536 + 8192);
+  return st;
+}
+
+__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch) {
+  load_rows_sw128(st.wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
+  load_rows_sw128(st.qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
+  load_rows_sw128(st.kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
+  load_rows64_sw128(st.at, ws.aqk + ch * 4096, 256);
+  load_rows_plain(st.us, ws.u + ch * 8192, 128, 256);
+  if (threadIdx.x < 16) tc::cp_async16(st.cum + 4 * threadIdx.x, ws.stats + ch * 256 + 4 * threadIdx.x, true);
+  tc::cp_async_commit();
+}
 
 __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ o,
                                                                  float* __restrict__ hT) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* st = sm;                   // S^T bf16, K-major 128 rows (dv) x 128 (dk)   32 KB
-  unsigned char* wt = st + 32768;           // W   64 rows (tok) x 128 (dk)                 16 KB
-  unsigned char* qt = wt + 16384;           // q~  64 x 128                                 16 KB
-  unsigned char* kt = qt + 16384;           // k~  64 x 128 (used MN-major: N = dk)        16 KB
-  unsigned char* at = kt + 16384;           // A_qk 64 (i) x 64 (j)                          8 KB
-  unsigned char* vpt = at + 8192;           // V'^T 128 rows (dv) x 64 (tok)                16 KB
-  bf16* us = reinterpret_cast<bf16*>(vpt + 16384);  // U plain [64][128]                     16 KB
-  float* cum = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(us) + 16384);
+  unsigned char* vpt = st + 32768;          // V'^T 128 rows (dv) x 64 (tok)                16 KB
+  unsigned char* stages = vpt + 16384;      // 2 x FwdStage
   __shared__ uint64_t bar[2];
   __shared__ uint32_t tmem_base;
 
@@ -268,6 +297,8 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     tc::mbar_init(&bar[1], 1);
     tc::fence_mbar_init();
   }
+  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
+  if (c0 < c1) fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h);
   // S^T[r][dk] for dk in [64 hh, 64 hh + 64): S[dk][r] of the [dk][dv] state
   float S[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
@@ -277,11 +308,18 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16);
-  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
   uint32_t phase = 0;
   for (int ci = c0; ci < c1; ++ci) {
     const int64_t ch = int64_t(ci) * p.Hv + h;
     const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
+    const int stg = (ci - c0) & 1;
+    const FwdStage cur = fwd_stage(stages, stg);
+    if (ci + 1 < c1) {
+      fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv);
+      tc::cp_async_wait<1>();
+    } else {
+      tc::cp_async_wait<0>();
+    }
     // S^T (bf16) -> smem operand and -> workspace (state entering this chunk)
     {
       uint32_t pk[32];
@@ -295,23 +333,13 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
         gdst[j] = v4;
       }
     }
-    load_rows_sw128(wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
-    load_rows_sw128(qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
-    load_rows_sw128(kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
-    for (int idx = tid; idx < 64 * 8; idx += 256) {  // A_qk: 64 rows x 64 -> one 64-k slab
-      const int i = idx >> 3, c8 = idx & 7;
-      *reinterpret_cast<uint4*>(at + tc::sw128_offset(i, c8 * 8, 64)) =
-          __ldg(reinterpret_cast<const uint4*>(ws.aqk + ch * 4096 + i * 64 + c8 * 8));
-    }
-    load_rows_plain(us, ws.u + ch * 8192, 128, 256);
-    if (tid < 64) cum[tid] = ws.stats[ch * 256 + tid];
     tc::fence_proxy_async();
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {
       // D_vp = S^T W^T (cols [0,64)), D_o = S^T q~^T (cols [64,128)): M=128, N=64, K=128
       const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
-      const uint32_t sa = tc::smem_u32(st), wa = tc::smem_u32(wt), qa = tc::smem_u32(qt);
+      const uint32_t sa = tc::smem_u32(st), wa = tc::smem_u32(cur.wt), qa = tc::smem_u32(cur.qt);
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16) {
         const uint32_t aoff = (k0 >> 6) * 16384 + (k0 & 63) * 2, boff = (k0 >> 6) * 8192 + (k0 & 63) * 2;
@@ -330,8 +358,8 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
         const int tk = 32 * hh + j;
-        const float a = __bfloat162float(us[tk * 128 + r]) - x[j];
-        const float b = __bfloat162float(us[(tk + 1) * 128 + r]) - x[j + 1];
+        const float a = __bfloat162float(cur.us[tk * 128 + r]) - x[j];
+        const float b = __bfloat162float(cur.us[(tk + 1) * 128 + r]) - x[j + 1];
         pk[j >> 1] = tc::pack_bf16(a, b);
         const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(&pk[j >> 1]);
         ws.vp[ch * 8192 + tk * 128 + r] = ab.x;
@@ -348,7 +376,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     tc::fence_after_sync();
     if (tid == 0) {
       // D_o += V'^T A_qk^T (M=128, N=64, K=64); D_s = V'^T k~ (M=128, N=128, K=64, k~ MN-major)
-      const uint32_t va = tc::smem_u32(vpt), aa = tc::smem_u32(at), ka = tc::smem_u32(kt);
+      const uint32_t va = tc::smem_u32(vpt), aa = tc::smem_u32(cur.at), ka = tc::smem_u32(cur.kt);
       const uint32_t id_o = tc::idesc_bf16(128, 64, false, false);
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
 #pragma unroll
@@ -369,7 +397,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
         const int tk = 32 * hh + j;
         if (tk < L) o[(int64_t(t0 + tk) * p.Hv + h) * 128 + r] = __float2bfloat16_rn(x[j]);
       }
-      const float gamma = expf(cum[63]);
+      const float gamma = expf(cur.cum[63]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         tc::tmem_ld32(lane_addr + 256 + 64 * hh + 32 * half, x);

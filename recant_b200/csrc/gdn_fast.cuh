@@ -34,15 +34,23 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
   return p + ((1024 - (tc::smem_u32(p) & 1023)) & 1023);
 }
 
-// Copy `nrows` rows of 128 bf16 (row stride `stride` elements) into rows [r0, r0+nrows) of a
-// K-major SW128 tile with `tile_rows` rows; rows >= L are zero. All `nthr` threads participate.
+// Asynchronously copy `nrows` rows of 128 bf16 (row stride `stride` elements) into rows
+// [r0, r0+nrows) of a K-major SW128 tile with `tile_rows` rows; rows >= L are zero-filled. All
+// `nthr` threads participate; completion via cp_async_commit / cp_async_wait.
 __device__ __forceinline__ void load_rows_sw128(unsigned char* tile, int tile_rows, int r0, const bf16* src,
                                                 int64_t stride, int nrows, int L, int nthr) {
   for (int idx = threadIdx.x; idx < nrows * 16; idx += nthr) {
     const int r = idx >> 4, c8 = idx & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < L) v = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
-    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r0 + r, c8 * 8, tile_rows)) = v;
+    const bool ok = r < L;
+    tc::cp_async16(tile + tc::sw128_offset(r0 + r, c8 * 8, tile_rows), src + (ok ? r * stride + c8 * 8 : 0), ok);
+  }
+}
+
+// Rows of 64 bf16 (e.g. a 64x64 A_qk block, row stride 64) into a one-slab SW128 tile.
+__device__ __forceinline__ void load_rows64_sw128(unsigned char* tile, const bf16* src, int nthr) {
+  for (int idx = threadIdx.x; idx < 64 * 8; idx += nthr) {
+    const int i = idx >> 3, c8 = idx & 7;
+    tc::cp_async16(tile + tc::sw128_offset(i, c8 * 8, 64), src + i * 64 + c8 * 8, true);
   }
 }
 
@@ -50,7 +58,7 @@ __device__ __forceinline__ void load_rows_sw128(unsigned char* tile, int tile_ro
 __device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int64_t stride, int nthr) {
   for (int idx = threadIdx.x; idx < 64 * 16; idx += nthr) {
     const int r = idx >> 4, c8 = idx & 15;
-    *reinterpret_cast<uint4*>(tile + r * 128 + c8 * 8) = __ldg(reinterpret_cast<const uint4*>(src + r * stride + c8 * 8));
+    tc::cp_async16(tile + r * 128 + c8 * 8, src + r * stride + c8 * 8, true);
   }
 }
 

@@ -86,20 +86,50 @@ __device__ __forceinline__ void sync_for_mma() {
 // ------------------------------------------------------------------------------------------------
 // reversed state walk: one CTA (256 threads) per (sequence, value head); thread = (dv row, dk half)
 // ------------------------------------------------------------------------------------------------
-constexpr int kBStateSmem = 32768 + 16384 + 8192 + 16384 * 3 + 16384 + 64 * 4 + 2048;
+constexpr int kBStageBytes = 16384 * 4 + 8192 + 1024;  // dO, k~, q~, W, A_qk, cum (1024-byte multiple)
+constexpr int kBStateSmem = 32768 + 16384 + 2 * kBStageBytes + 2048;
+
+struct BwdStage {
+  unsigned char* dot;  // dO rows tok (64) x dv
+  unsigned char* kt;   // k~ rows tok x dk
+  unsigned char* qt;   // q~
+  unsigned char* wt;   // W
+  unsigned char* at;   // A_qk rows i x c
+  float* cum;
+};
+
+__device__ __forceinline__ BwdStage bwd_stage(unsigned char* base, int stg) {
+  unsigned char* b = base + stg * kBStageBytes;
+  BwdStage st;
+  st.dot = b;
+  st.kt = b + 16384;
+  st.qt = b + 32768;
+  st.wt = b + 49152;
+  st.at = b + 65536;
+  st.cum = reinterpret_cast<float*>(b + 65536 + 8192);
+  return st;
+}
+
+__device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& p, const FastWs& ws, const bf16* d_o,
+                                          int ci, int h) {
+  const int64_t ch = int64_t(ci) * p.Hv + h;
+  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
+  load_rows_sw128(st.dot, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, 64, L, 256);
+  load_rows_sw128(st.kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
+  load_rows_sw128(st.qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
+  load_rows_sw128(st.wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
+  load_rows64_sw128(st.at, ws.aqk + ch * 4096, 256);
+  if (threadIdx.x < 16) tc::cp_async16(st.cum + 4 * threadIdx.x, ws.stats + ch * 256 + 4 * threadIdx.x, true);
+  tc::cp_async_commit();
+}
 
 __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  const float* __restrict__ dhT, float* __restrict__ dh0) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* dst = sm;              // dS^T bf16, rows dv (128) x dk               32 KB
-  unsigned char* dot = dst + 32768;     // dO rows tok (64) x dv                        16 KB
-  unsigned char* at = dot + 16384;      // A_qk rows i x c                               8 KB
-  unsigned char* kt = at + 8192;        // k~ rows tok x dk                             16 KB
-  unsigned char* qt = kt + 16384;       // q~                                           16 KB
-  unsigned char* wt = qt + 16384;       // W                                            16 KB
-  unsigned char* dvt = wt + 16384;      // dV'^T rows dv x tok                          16 KB
-  float* cum = reinterpret_cast<float*>(dvt + 16384);
+  unsigned char* dvt = dst + 32768;     // dV'^T rows dv x tok                          16 KB
+  unsigned char* stages = dvt + 16384;  // 2 x BwdStage
   __shared__ uint64_t bar[2];
   __shared__ uint32_t tmem_base;
 
@@ -112,6 +142,8 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     tc::mbar_init(&bar[1], 1);
     tc::fence_mbar_init();
   }
+  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
+  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, d_o, c1 - 1, h);
   float dS[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
 #pragma unroll
@@ -120,11 +152,17 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16);
-  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
   uint32_t phase = 0;
   for (int ci = c1 - 1; ci >= c0; --ci) {
     const int64_t ch = int64_t(ci) * p.Hv + h;
-    const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
+    const int stg = (c1 - 1 - ci) & 1;
+    const BwdStage cur = bwd_stage(stages, stg);
+    if (ci - 1 >= c0) {
+      bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, d_o, ci - 1, h);
+      tc::cp_async_wait<1>();
+    } else {
+      tc::cp_async_wait<0>();
+    }
     {
       uint32_t pk[32];
 #pragma unroll
@@ -137,20 +175,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
         gdst[j] = v4;
       }
     }
-    load_rows_sw128(dot, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, 64, L, 256);
-    for (int idx = tid; idx < 64 * 8; idx += 256) {
-      const int i = idx >> 3, c8 = idx & 7;
-      *reinterpret_cast<uint4*>(at + tc::sw128_offset(i, c8 * 8, 64)) =
-          __ldg(reinterpret_cast<const uint4*>(ws.aqk + ch * 4096 + i * 64 + c8 * 8));
-    }
-    load_rows_sw128(kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
-    load_rows_sw128(qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
-    load_rows_sw128(wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
-    if (tid < 64) cum[tid] = ws.stats[ch * 256 + tid];
     sync_for_mma();
     if (tid == 0) {
-      const uint32_t doa = tc::smem_u32(dot), aa = tc::smem_u32(at), da = tc::smem_u32(dst), ka = tc::smem_u32(kt),
-                     qa = tc::smem_u32(qt);
+      const uint32_t doa = tc::smem_u32(cur.dot), aa = tc::smem_u32(cur.at), da = tc::smem_u32(dst),
+                     ka = tc::smem_u32(cur.kt), qa = tc::smem_u32(cur.qt);
       // dV'^T = dO^T A_qk (A = dO MN-major: M = dv, K = tok; B = A_qk MN-major: N = c, K = i)
       const uint32_t id_a = tc::idesc_bf16(128, 64, true, true);
 #pragma unroll
@@ -193,7 +221,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     sync_for_mma();
     if (tid == 0) {
       // D_s -= dV'^T W (A = dV'^T K-major: M = dv, K = tok, negated; B = W MN-major: N = dk, K = tok)
-      const uint32_t va = tc::smem_u32(dvt), wa = tc::smem_u32(wt);
+      const uint32_t va = tc::smem_u32(dvt), wa = tc::smem_u32(cur.wt);
       const uint32_t id_w = tc::idesc_bf16(128, 128, false, true, true);
 #pragma unroll
       for (int k0 = 0; k0 < 64; k0 += 16)
@@ -203,7 +231,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     tc::mbar_wait(&bar[1], phase, ws.err, 122);
     tc::fence_after_sync();
     {
-      const float gamma = expf(cum[63]);
+      const float gamma = expf(cur.cum[63]);
       float x[32];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -280,6 +308,7 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   load_rows_sw128(sm + lay::DHT, 128, 0, ws.dh + ch * 16384, 128, 128, 128, 128);
   load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 128);
   load_rows_sw128(sm + lay::VPT, 64, 0, ws.vp + ch * 8192, 128, 64, 64, 128);
+  tc::cp_async_commit();
   if (tid < 64) {
     const float* st = ws.stats + ch * 256;
     cum[tid] = st[tid]; rq[tid] = st[64 + tid]; rk[tid] = st[128 + tid]; beta[tid] = st[192 + tid];
@@ -288,6 +317,7 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     dbeta_acc[tid] = 0.f;
     dcum_acc[tid] = 0.f;
   }
+  tc::cp_async_wait<0>();
   sync_for_mma();
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * w) << 16);
