@@ -21,57 +21,6 @@ namespace {
 
 using namespace fast;
 
-// Sum v[0..63] over the 32 lanes of the warp by a halving butterfly; afterwards this lane holds
-// the totals of columns c0 and c0 + 1 in v[0], v[1] (c0 from colsum_base()).
-__device__ __forceinline__ void warp_colsum64(float (&v)[64]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int step = 0; step < 5; ++step) {
-    const int s = 16 >> step, c = 64 >> step;
-    const bool up = (lane & s) != 0;
-#pragma unroll
-    for (int j = 0; j < c / 2; ++j) {
-      const float send = up ? v[j] : v[j + c / 2];
-      const float keep = up ? v[j + c / 2] : v[j];
-      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
-    }
-  }
-}
-__device__ __forceinline__ int colsum_base() {
-  const int l = threadIdx.x & 31;
-  return ((l & 16) ? 32 : 0) + ((l & 8) ? 16 : 0) + ((l & 4) ? 8 : 0) + ((l & 2) ? 4 : 0) + ((l & 1) ? 2 : 0);
-}
-// Column sums of a 128 x 64 matrix held one row per thread (128 threads); out[64] in smem.
-__device__ __forceinline__ void block_colsum64(float (&v)[64], float* red, float* out) {
-  warp_colsum64(v);
-  const int w = threadIdx.x >> 5, c0 = colsum_base();
-  red[w * 64 + c0] = v[0];
-  red[w * 64 + c0 + 1] = v[1];
-  __syncthreads();
-  if (threadIdx.x < 64) out[threadIdx.x] = red[threadIdx.x] + red[64 + threadIdx.x] + red[128 + threadIdx.x] + red[192 + threadIdx.x];
-  __syncthreads();
-}
-
-__device__ __forceinline__ void tmem_ld64(uint32_t addr, float (&v)[64]) {
-  float a[32];
-  tc::tmem_ld32(addr, a);
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = a[j];
-  tc::tmem_ld32(addr + 32, a);
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[32 + j] = a[j];
-}
-
-// Write 64 fp32 values as one bf16 row (64 elements) of a K-major SW128 tile with `rows` rows.
-__device__ __forceinline__ void store_row64(unsigned char* tile, int rows, int r, const float (&v)[64]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
-                               tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
-    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, 8 * j, rows)) = x;
-  }
-}
-
 __device__ __forceinline__ float tile_elem(const unsigned char* tile, int rows, int r, int k) {
   return __bfloat162float(*reinterpret_cast<const bf16*>(tile + tc::sw128_offset(r, k, rows)));
 }
@@ -254,7 +203,9 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
 }
 
 // ------------------------------------------------------------------------------------------------
-// chunk backward: one CTA (128 threads) per (chunk, value head)
+// chunk backward: one CTA (256 threads) per (chunk, value head). Thread (w, l): TMEM lane quarter
+// q = w & 3, lane r = 32 q + l (head-dim row of an M=128 accumulator; for M=64 accumulators lanes
+// l < 16 hold token rows 16 q + l), column half hh = w >> 2 (columns [32 hh, 32 hh + 32)).
 // ------------------------------------------------------------------------------------------------
 namespace lay {  // shared-memory map (bytes from the 1024-aligned base)
 constexpr int KQ = 0, VT = 32768, DVP = 49152;
@@ -262,14 +213,58 @@ constexpr int ST = 65536, DHT = 98304, DOT = 131072, VPT = 147456;           // 
 constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  // phase 2 (over phase 1)
               YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
 constexpr int QB2 = VT;                                                        // over V once consumed
+constexpr int QCOL = 65536, KCOL = QCOL + 128 * 66 * 2;                        // final: over phase 2
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
-constexpr int VEC = DAQF + 16640;                                              // 8 x 64 floats
-constexpr int RED = VEC + 8 * 256;                                             // 4 x 64 floats
-constexpr int END = RED + 1024 + 64;
+constexpr int VEC = DAQF + 16640;                                              // 12 x 64 floats
+constexpr int RED = VEC + 12 * 256;                                            // 5 x 4 x 64 floats
+constexpr int END = RED + 5 * 1024 + 64;
 }  // namespace lay
 constexpr int kBChunkSmem = lay::END + 1024;
+constexpr int kColStride = 66;  // bf16 elements per row of the transposed q / k column tiles
 
-__global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
+// Sum v[0..31] over the 32 lanes; afterwards lane l holds the total of column l.
+__device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int s = 16 >> step, c = 32 >> step;
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < c / 2; ++j) {
+      const float send = up ? v[j] : v[j + c / 2];
+      const float keep = up ? v[j + c / 2] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ void tmem_ld32f(uint32_t addr, float (&v)[32]) { tc::tmem_ld32(addr, v); }
+
+// 32 bf16 (64 bytes) of row r starting at element e0 of a K-major SW128 tile -> fp32
+__device__ __forceinline__ void store_row32(unsigned char* tile, int rows, int r, int e0, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                               tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0 + 8 * j, rows)) = x;
+  }
+}
+
+// Write 32 per-token values of head-dim column r (tokens 32 hh + j) as bf16 to dst[(tok) * row + r],
+// pairing lanes r, r^1 so that every store is one 4-byte bf16x2.
+__device__ __forceinline__ void store_cols32(bf16* dst, int64_t row, int r, int t_base, int L, const float (&v)[32]) {
+  const bool odd = (r & 1) != 0;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+    const int tk = t_base + j + (odd ? 1 : 0);
+    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
+    if (tk < L) *reinterpret_cast<uint32_t*>(dst + int64_t(tk) * row + (r & ~1)) = tc::pack_bf16(lo, hi);
+  }
+}
+
+__global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  bf16* __restrict__ dq, bf16* __restrict__ dk,
                                                                  bf16* __restrict__ dv, float* __restrict__ dg,
                                                                  bf16* __restrict__ dbeta) {
@@ -280,34 +275,37 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   float* daqf = reinterpret_cast<float*>(sm + lay::DAQF);
   float* vec = reinterpret_cast<float*>(sm + lay::VEC);
   float *cum = vec, *rq = vec + 64, *rk = vec + 128, *beta = vec + 192, *ecum = vec + 256, *edec = vec + 320,
-        *dbeta_acc = vec + 384, *dcum_acc = vec + 448;
-  float* red = reinterpret_cast<float*>(sm + lay::RED);
-  float* scal = red + 256;  // [0] = dgamma, [1..] scratch
-  __shared__ float colbuf[64];
+        *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [2][64] */, *scal = vec + 640;
+  float* red = reinterpret_cast<float*>(sm + lay::RED);  // [5][4][64]
+  bf16* qcol = reinterpret_cast<bf16*>(sm + lay::QCOL);
+  bf16* kcol = reinterpret_cast<bf16*>(sm + lay::KCOL);
   __shared__ uint64_t bar[5];
   __shared__ uint32_t tmem_base;
 
   const int ci = blockIdx.x, h = blockIdx.y;
   if (ci >= *ws.ct.n_chunks) return;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int q4 = w & 3, hh = w >> 2, r = 32 * q4 + l, c0 = 32 * hh;
+  const bool mrow = l < 16;            // this lane holds a row of an M=64 accumulator
+  const int i64 = 16 * q4 + l;          // ... and it is token row i64
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
   const int64_t ch = int64_t(ci) * p.Hv + h;
   const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
 
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) tc::mbar_init(&bar[i], 1);
+    for (int b = 0; b < 5; ++b) tc::mbar_init(&bar[b], 1);
     tc::fence_mbar_init();
   }
   // ---- loads ---------------------------------------------------------------------------------
-  load_rows_sw128(sm + lay::KQ, 128, 0, static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 128);
-  load_rows_sw128(sm + lay::KQ, 128, 64, static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 128);
-  load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 128);
-  load_rows_sw128(sm + lay::DVP, 64, 0, ws.dvp + ch * 8192, 128, 64, 64, 128);
-  load_rows_sw128(sm + lay::ST, 128, 0, ws.hs + ch * 16384, 128, 128, 128, 128);
-  load_rows_sw128(sm + lay::DHT, 128, 0, ws.dh + ch * 16384, 128, 128, 128, 128);
-  load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 128);
-  load_rows_sw128(sm + lay::VPT, 64, 0, ws.vp + ch * 8192, 128, 64, 64, 128);
+  load_rows_sw128(sm + lay::KQ, 128, 0, static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
+  load_rows_sw128(sm + lay::KQ, 128, 64, static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
+  load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 256);
+  load_rows_sw128(sm + lay::DVP, 64, 0, ws.dvp + ch * 8192, 128, 64, 64, 256);
+  load_rows_sw128(sm + lay::ST, 128, 0, ws.hs + ch * 16384, 128, 128, 128, 256);
+  load_rows_sw128(sm + lay::DHT, 128, 0, ws.dh + ch * 16384, 128, 128, 128, 256);
+  load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 256);
+  load_rows_sw128(sm + lay::VPT, 64, 0, ws.vp + ch * 8192, 128, 64, 64, 256);
   tc::cp_async_commit();
   if (tid < 64) {
     const float* st = ws.stats + ch * 256;
@@ -320,7 +318,7 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::cp_async_wait<0>();
   sync_for_mma();
   const uint32_t tbase = tmem_base;
-  const uint32_t lane_addr = tbase + (uint32_t(32 * w) << 16);
+  const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
   if (tid == 0) {  // ---- G1 ----
     const uint32_t sta = tc::smem_u32(sm + lay::ST), dha = tc::smem_u32(sm + lay::DHT), doa = tc::smem_u32(sm + lay::DOT),
@@ -343,7 +341,7 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   {  // dgamma = sum S^T * dS^T while G1 runs (both tiles share one layout)
     float part = 0.f;
-    for (int idx = tid; idx < 128 * 16; idx += 128) {
+    for (int idx = tid; idx < 128 * 16; idx += 256) {
       const uint32_t off = uint32_t(idx) * 16;
       const uint4 a = *reinterpret_cast<const uint4*>(sm + lay::ST + off);
       const uint4 b = *reinterpret_cast<const uint4*>(sm + lay::DHT + off);
@@ -355,26 +353,29 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     if (l == 0) red[w] = part;
   }
   __syncthreads();
-  if (tid == 0) scal[0] = red[0] + red[1] + red[2] + red[3];
+  if (tid == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    scal[0] = t;
+  }
   tc::mbar_wait(&bar[0], 0, ws.err, 131);
   tc::fence_after_sync();
   // ---- E1 ------------------------------------------------------------------------------------
   {
-    float v[64];
-    tmem_ld64(lane_addr + 0, v);  // lanes 0-63: kk rows, 64-127: qk rows
-    float* dstf = tid < 64 ? kkf + tid * 65 : qkf + (tid - 64) * 65;
+    float v[32];
+    tmem_ld32f(lane_addr + 0, v);  // lanes 0-63: kk rows, 64-127: qk rows
+    float* dstf = r < 64 ? kkf + r * 65 + c0 : qkf + (r - 64) * 65 + c0;
 #pragma unroll
-    for (int j = 0; j < 64; ++j) dstf[j] = v[j];
-    tmem_ld64(lane_addr + 128, v);  // dW^T row dk = tid
-    store_row64(sm + lay::DWT, 128, tid, v);
-    tmem_ld64(lane_addr + 256, v);  // dA_qk (M = 64): lanes 0-15 of each quarter
-    if (l < 16) {
-      const int i = 16 * w + l;
+    for (int j = 0; j < 32; ++j) dstf[j] = v[j];
+    tmem_ld32f(lane_addr + 128, v);  // dW^T row dk = r
+    store_row32(sm + lay::DWT, 128, r, c0, v);
+    tmem_ld32f(lane_addr + 256, v);  // dA_qk (M = 64)
+    if (mrow) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) daqf[i * 65 + j] = j <= i ? v[j] : 0.f;
+      for (int j = 0; j < 32; ++j) daqf[i64 * 65 + c0 + j] = c0 + j <= i64 ? v[j] : 0.f;
     }
   }
-  for (int idx = tid; idx < 64 * 16; idx += 128) {  // beta V and beta e^cum rk K (rows m)
+  for (int idx = tid; idx < 64 * 16; idx += 256) {  // beta V and beta e^cum rk K (rows m)
     const int m = idx >> 4, c8 = (idx & 15) * 8;
     const uint4 xv = *reinterpret_cast<const uint4*>(sm + lay::VT + tc::sw128_offset(m, c8, 64));
     const uint4 xk = *reinterpret_cast<const uint4*>(sm + lay::KQ + tc::sw128_offset(m, c8, 128));
@@ -389,7 +390,7 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     *reinterpret_cast<uint4*>(sm + lay::BV + tc::sw128_offset(m, c8, 64)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
     *reinterpret_cast<uint4*>(sm + lay::BK + tc::sw128_offset(m, c8, 64)) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
   }
-  for (int idx = tid; idx < 64 * 8; idx += 128) {  // T (bf16) rows i
+  for (int idx = tid; idx < 64 * 8; idx += 256) {  // T (bf16) rows i
     const int i = idx >> 3, c8 = (idx & 7) * 8;
     const float4 a = *reinterpret_cast<const float4*>(ws.tinv + ch * 4096 + i * 64 + c8);
     const float4 b = *reinterpret_cast<const float4*>(ws.tinv + ch * 4096 + i * 64 + c8 + 4);
@@ -425,24 +426,25 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::fence_after_sync();
   // ---- E2 ------------------------------------------------------------------------------------
   {
-    float v[64];
-    tmem_ld64(lane_addr + 320, v);  // dT (M = 64)
-    if (l < 16) {
-      const int i = 16 * w + l;
+    float v[32];
+    tmem_ld32f(lane_addr + 320, v);  // dT (M = 64)
+    if (mrow) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) v[j] = j <= i ? v[j] : 0.f;
-      store_row64(sm + lay::DTT, 64, i, v);
+      for (int j = 0; j < 32; ++j) v[j] = c0 + j <= i64 ? v[j] : 0.f;
+      store_row32(sm + lay::DTT, 64, i64, c0, v);
     }
-    tmem_ld64(lane_addr + 384, v);  // dBv^T row dv = tid
-    const int r = tid;
+    tmem_ld32f(lane_addr + 384, v);  // dBv^T row dv = r, columns m = c0 + j
+    float x[32];
 #pragma unroll
-    for (int m = 0; m < 64; ++m) {
-      if (m < L) dv[(int64_t(t0 + m) * p.Hv + h) * 128 + r] = __float2bfloat16_rn(beta[m] * v[m]);
-      v[m] *= tile_elem(sm + lay::VT, 64, m, r);
+    for (int j = 0; j < 32; ++j) {
+      x[j] = beta[c0 + j] * v[j];
+      v[j] *= tile_elem(sm + lay::VT, 64, c0 + j, r);
     }
-    block_colsum64(v, red, colbuf);
-    if (tid < 64) dbeta_acc[tid] += colbuf[tid];
+    store_cols32(dv + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, c0, L, x);
+    red[q4 * 64 + c0 + l] = warp_colsum32(v);
   }
+  __syncthreads();
+  if (tid < 64) dbeta_acc[tid] += red[tid] + red[64 + tid] + red[128 + tid] + red[192 + tid];
   sync_for_mma();
   if (tid == 0) {  // ---- G3: Y = T^T dT ----
     const uint32_t dta = tc::smem_u32(sm + lay::DTT);
@@ -456,9 +458,9 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::mbar_wait(&bar[2], 0, ws.err, 133);
   tc::fence_after_sync();
   {
-    float v[64];
-    tmem_ld64(lane_addr + 0, v);
-    if (l < 16) store_row64(sm + lay::YT, 64, 16 * w + l, v);
+    float v[32];
+    tmem_ld32f(lane_addr + 0, v);
+    if (mrow) store_row32(sm + lay::YT, 64, i64, c0, v);
   }
   sync_for_mma();
   if (tid == 0) {  // ---- G4: dL' = Y T^T ----
@@ -471,38 +473,36 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   tc::mbar_wait(&bar[3], 0, ws.err, 134);
   tc::fence_after_sync();
-  // ---- E4: P, Qm, R and the B operands of G5 -------------------------------------------------
+  // ---- E4: P, Qm, R and the B operands of G5 (row i64, columns c0..c0+31) ---------------------
   {
-    float v[64];
-    tmem_ld64(lane_addr + 256, v);
-    if (l < 16) {
-      const int i = 16 * w + l;
+    float v[32];
+    tmem_ld32f(lane_addr + 256, v);
+    if (mrow) {
+      const int i = i64;
       const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
       float db = 0.f;
-      float pb1[64], qb1[64];
+      float pb1[32], qb1[32], pb2[32], qb2[32];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const float gam = j <= i ? expf(ci_ - cum[j]) : 0.f;
-        const float dl = j < i ? -v[j] : 0.f;
-        const float P = dl * gam;
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = c0 + jj;
+        const float gam = j <= i ? __expf(ci_ - cum[j]) : 0.f;
+        const float P = j < i ? -v[jj] * gam : 0.f;
         const float kkn = kkf[i * 65 + j] * rki * rk[j];
         const float qkn = qkf[i * 65 + j] * sqi * rk[j];
         const float daq = daqf[i * 65 + j];
+        const float qm = daq * gam;
         db = fmaf(P, kkn, db);
         kkf[i * 65 + j] = P * bi * kkn + daq * qkn * gam;  // R
-        const float qm = daq * gam;
-        v[j] = P;
-        pb1[j] = bi * rk[j] * P;
-        qb1[j] = rk[j] * qm;
-        daqf[i * 65 + j] = qm;
+        pb1[jj] = bi * rk[j] * P;
+        qb1[jj] = rk[j] * qm;
+        pb2[jj] = bi * rki * P;
+        qb2[jj] = sqi * qm;
       }
-      dbeta_acc[i] += db;
-      store_row64(sm + lay::PB1, 64, i, pb1);
-      store_row64(sm + lay::QB1, 64, i, qb1);
-#pragma unroll
-      for (int j = 0; j < 64; ++j) { pb1[j] = bi * rki * v[j]; qb1[j] = sqi * daqf[i * 65 + j]; }
-      store_row64(sm + lay::PB2, 64, i, pb1);
-      store_row64(sm + lay::QB2, 64, i, qb1);
+      dbp[hh * 64 + i] = db;
+      store_row32(sm + lay::PB1, 64, i, c0, pb1);
+      store_row32(sm + lay::QB1, 64, i, c0, qb1);
+      store_row32(sm + lay::PB2, 64, i, c0, pb2);
+      store_row32(sm + lay::QB2, 64, i, c0, qb2);
     }
   }
   sync_for_mma();
@@ -521,95 +521,123 @@ __global__ void __launch_bounds__(128, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     }
     tc::mma_commit(&bar[4]);
   }
-  if (tid < 64) {  // dcum_i += sum_j R_ij - sum_j R_ji
+  if (tid < 64) {  // dcum_i += sum_j R_ij - sum_j R_ji;  dbeta partials
     float a = 0.f;
     for (int j = 0; j < 64; ++j) a += kkf[tid * 65 + j] - kkf[j * 65 + tid];
     dcum_acc[tid] += a;
+    dbeta_acc[tid] += dbp[tid] + dbp[64 + tid];
   }
   tc::mbar_wait(&bar[4], 0, ws.err, 135);
   tc::fence_after_sync();
-  // ---- final epilogue: thread = head-dim row r; columns = tokens -----------------------------
-  const int r = tid;
-  float qr[64];
+  __syncthreads();  // region A (the phase-2 tiles) is free once G5 has completed
+  // ---- transposed copies of q and k: col[r][i] = x[i][r] ------------------------------------------
+  for (int idx = tid; idx < 128 * 16; idx += 256) {
+    const int t = idx >> 4, c8 = (idx & 15) * 8;
+    const uint4 x = *reinterpret_cast<const uint4*>(sm + lay::KQ + tc::sw128_offset(t, c8, 128));
+    bf16* col = t < 64 ? kcol : qcol;
+    const int i = t & 63;
+    const bf16* e = reinterpret_cast<const bf16*>(&x);
 #pragma unroll
-  for (int i = 0; i < 64; ++i) qr[i] = tile_elem(sm + lay::KQ, 128, 64 + i, r);
-  float a1_mine;
-  {
-    float v[64];
-    tmem_ld64(lane_addr + 64, v);  // dq~^T
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] *= qr[i];
-    block_colsum64(v, red, colbuf);
-    a1_mine = tid < 64 ? colbuf[tid] : 0.f;
+    for (int j = 0; j < 8; ++j) col[(c8 + j) * kColStride + i] = e[j];
   }
+  __syncthreads();
+  // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j -----------------------------
+  float xr[32];
   {
-    float dqh[64], v[64];
-    tmem_ld64(lane_addr + 0, dqh);   // (Qm k^)^T
-    tmem_ld64(lane_addr + 64, v);    // dq~^T
+    const uint32_t* qp = reinterpret_cast<const uint32_t*>(qcol + r * kColStride + c0);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) { dqh[i] = p.scale * fmaf(ecum[i], v[i], dqh[i]); v[i] = dqh[i] * qr[i]; }
-    block_colsum64(v, red, colbuf);
+    for (int j = 0; j < 16; ++j) { const uint32_t u = qp[j]; xr[2 * j] = bf_lo(u); xr[2 * j + 1] = bf_hi(u); }
+  }
+  float* red1 = red;            // a1: sum_r dq~^T q
+  float* red2 = red + 256;      // a4: sum_r dq^^T q   (l2norm)
+  float* red3 = red + 512;      // a2: sum_r dk~^T k
+  float* red4 = red + 768;      // a3: sum_r dBk^T k
+  float* red5 = red + 1024;     // a5: sum_r dk^^T k   (l2norm)
+  float dqh[32];
+  {
+    float t1[32], v[32];
+    tmem_ld32f(lane_addr + 0, dqh);   // (Qm k^)^T
+    tmem_ld32f(lane_addr + 64, t1);   // dq~^T
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      if (i < L) {
-        const float rqi = rq[i];
-        const float gq = rqi * dqh[i] - qr[i] * rqi * rqi * rqi * colbuf[i];
-        if (p.group == 1) dq[(int64_t(t0 + i) * p.Hk + hk) * 128 + r] = __float2bfloat16_rn(gq);
-        else ws.dqh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gq;
-      }
+    for (int j = 0; j < 32; ++j) {
+      dqh[j] = p.scale * fmaf(ecum[c0 + j], t1[j], dqh[j]);
+      v[j] = t1[j] * xr[j];
+      t1[j] = dqh[j] * xr[j];
+    }
+    red1[q4 * 64 + c0 + l] = warp_colsum32(v);
+    red2[q4 * 64 + c0 + l] = warp_colsum32(t1);
+  }
+  float kr_[32];
+  {
+    const uint32_t* kp = reinterpret_cast<const uint32_t*>(kcol + r * kColStride + c0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) { const uint32_t u = kp[j]; kr_[2 * j] = bf_lo(u); kr_[2 * j + 1] = bf_hi(u); }
+  }
+  float dkh[32];
+  {
+    float t2[32], t3[32];
+    tmem_ld32f(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
+    tmem_ld32f(lane_addr + 192, t2);   // dk~^T
+    tmem_ld32f(lane_addr + 448, t3);   // dBk^T
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int i = c0 + j;
+      dkh[j] = fmaf(edec[i], t2[j], fmaf(beta[i] * ecum[i], t3[j], dkh[j]));
+      t2[j] *= kr_[j];
+      t3[j] *= kr_[j];
+    }
+    red3[q4 * 64 + c0 + l] = warp_colsum32(t2);
+    red4[q4 * 64 + c0 + l] = warp_colsum32(t3);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t2[j] = dkh[j] * kr_[j];
+    red5[q4 * 64 + c0 + l] = warp_colsum32(t2);
+  }
+  __syncthreads();
+  if (tid < 64) {  // combine the four lane quarters
+#pragma unroll
+    for (int b = 0; b < 5; ++b) {
+      float* rb = red + 256 * b;
+      rb[tid] = rb[tid] + rb[64 + tid] + rb[128 + tid] + rb[192 + tid];
     }
   }
   __syncthreads();
-  float kr[64];
-#pragma unroll
-  for (int i = 0; i < 64; ++i) kr[i] = tile_elem(sm + lay::KQ, 128, i, r);
-  float a2_mine, a3_mine;
   {
-    float v[64];
-    tmem_ld64(lane_addr + 192, v);  // dk~^T
+    float gq[32], gk[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] *= kr[i];
-    block_colsum64(v, red, colbuf);
-    a2_mine = tid < 64 ? colbuf[tid] : 0.f;
-    tmem_ld64(lane_addr + 448, v);  // dBk^T
+    for (int j = 0; j < 32; ++j) {
+      const int i = c0 + j;
+      const float rqi = rq[i], rki = rk[i];
+      gq[j] = rqi * dqh[j] - xr[j] * rqi * rqi * rqi * red2[i];
+      gk[j] = rki * dkh[j] - kr_[j] * rki * rki * rki * red5[i];
+    }
+    if (p.group == 1) {
+      const int64_t row = int64_t(p.Hk) * 128;
+      store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
+      store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] *= kr[i];
-    block_colsum64(v, red, colbuf);
-    a3_mine = tid < 64 ? colbuf[tid] : 0.f;
-  }
-  {
-    float dkh[64], v[64];
-    tmem_ld64(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
-    tmem_ld64(lane_addr + 192, v);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) dkh[i] = fmaf(edec[i], v[i], dkh[i]);
-    tmem_ld64(lane_addr + 448, v);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) { dkh[i] = fmaf(beta[i] * ecum[i], v[i], dkh[i]); v[i] = dkh[i] * kr[i]; }
-    block_colsum64(v, red, colbuf);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      if (i < L) {
-        const float rki = rk[i];
-        const float gk = rki * dkh[i] - kr[i] * rki * rki * rki * colbuf[i];
-        if (p.group == 1) dk[(int64_t(t0 + i) * p.Hk + hk) * 128 + r] = __float2bfloat16_rn(gk);
-        else ws.dkh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gk;
+      for (int j = 0; j < 32; ++j) {
+        const int i = c0 + j;
+        if (i < L) {
+          ws.dqh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gq[j];
+          ws.dkh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gk[j];
+        }
       }
     }
   }
   // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------
   if (tid < 64) {
     const int i = tid;
-    const float z = edec[i] * rk[i] * a2_mine;
-    const float colk = rk[i] * a3_mine;
-    dcum_acc[i] += ecum[i] * p.scale * rq[i] * a1_mine - z + beta[i] * ecum[i] * colk;
+    const float z = edec[i] * rk[i] * red3[i];
+    const float colk = rk[i] * red4[i];
+    dcum_acc[i] += ecum[i] * p.scale * rq[i] * red1[i] - z + beta[i] * ecum[i] * colk;
     dbeta_acc[i] += ecum[i] * colk;
-    red[i] = z;
+    scal[1 + i] = z;
   }
   __syncthreads();
   if (tid == 0) {
     float dcl = scal[0] * expf(cum[63]);
-    for (int i = 0; i < 64; ++i) dcl += red[i];
+    for (int i = 0; i < 64; ++i) dcl += scal[1 + i];
     dcum_acc[63] += dcl;
     double acc = 0.0;
     for (int i = 63; i >= 0; --i) {
@@ -668,7 +696,7 @@ int fast_backward(const GdnProblem& p, void* wsp, const void* d_o, const float* 
     if ((rc = smem_attr_b(fast_chunk_bwd_kernel, kBChunkSmem))) return rc;
     {
       ProfScope ps_("gdn_fast_chunk_bwd", s);
-      fast_chunk_bwd_kernel<<<dim3(p.max_chunks, p.Hv), 128, kBChunkSmem, s>>>(
+      fast_chunk_bwd_kernel<<<dim3(p.max_chunks, p.Hv), 256, kBChunkSmem, s>>>(
           p, w, static_cast<const bf16*>(d_o), static_cast<bf16*>(dq), static_cast<bf16*>(dk), static_cast<bf16*>(dv), dg,
           static_cast<bf16*>(dbeta));
       RB2_CHECK_LAUNCH("gdn fast chunk bwd");
