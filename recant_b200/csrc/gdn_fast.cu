@@ -50,11 +50,12 @@ namespace {
 using namespace fast;
 
 // ------------------------------------------------------------------------------------------------
-// prep: one CTA (128 threads) per (chunk, value head)
+// prep: one CTA (256 threads) per (chunk, value head). Thread (w, l): TMEM lane r = 32 (w & 3) + l,
+// column half hh = w >> 2 (columns [32 hh, 32 hh + 32) of the 64-wide accumulators).
 // ------------------------------------------------------------------------------------------------
 constexpr int kPrepSmem = 32768 + 16384 + 8192 + 8192 + 2 * 64 * 65 * 4 + 768 * 4 + 6 * 64 * 4 + 2048;
 
-__global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws) {
+__global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* kq = sm;                  // [K;Q] K-major SW128, 128 rows x 128   (32 KB)
@@ -76,6 +77,7 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
   const int ci = blockIdx.x, h = blockIdx.y;
   if (ci >= *ws.ct.n_chunks) return;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int r = 32 * (w & 3) + l, hh = w >> 2, c0 = 32 * hh;
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
   const int64_t ch = int64_t(ci) * p.Hv + h;
   const bf16* q = static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128;
@@ -89,9 +91,9 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
     tc::mbar_init(&bar[1], 1);
     tc::fence_mbar_init();
   }
-  load_rows_sw128(kq, 128, 0, k, qs, 64, L, 128);
-  load_rows_sw128(kq, 128, 64, q, qs, 64, L, 128);
-  load_rows_sw128(vt, 64, 0, v, vs, 64, L, 128);
+  load_rows_sw128(kq, 128, 0, k, qs, 64, L, 256);
+  load_rows_sw128(kq, 128, 64, q, qs, 64, L, 256);
+  load_rows_sw128(vt, 64, 0, v, vs, 64, L, 256);
   tc::cp_async_commit();
   if (tid < 64) {
     gv[tid] = tid < L ? p.g[int64_t(t0 + tid) * p.Hv + h] : 0.f;
@@ -102,6 +104,7 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16) + c0;
   if (tid == 0) {  // [K;Q] K^T: M=128, N=64, K=128 -> TMEM cols [0, 64)
     const uint32_t a0 = tc::smem_u32(kq);
     const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
@@ -113,8 +116,8 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
     tc::mma_commit(&bar[0]);
   }
   // norms of the 128 stacked rows (half-warp per row), cumulative gate in double
-  for (int r = w * 2 + (l >> 4); r < 128; r += 8) {
-    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(r, (l & 15) * 8, 128));
+  for (int row = w * 2 + (l >> 4); row < 128; row += 16) {
+    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row, (l & 15) * 8, 128));
     float s = 0.f;
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
     for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((l & 15) == 0) {
       const float rs = 1.0f / sqrtf(s + 1e-6f);
-      if (r < 64) rk[r] = rs; else rq[r - 64] = rs;
+      if (row < 64) rk[row] = rs; else rq[row - 64] = rs;
     }
   }
   if (tid == 0) {
@@ -131,63 +134,63 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
     for (int i = 0; i < 64; ++i) { acc += double(gv[i]); cum[i] = float(acc); }
   }
   __syncthreads();
-  if (tid < 64) ecum[tid] = expf(cum[tid]);
+  if (tid < 64) ecum[tid] = __expf(cum[tid]);
   float* st = ws.stats + ch * 256;
   if (tid < 64) { st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid]; }
 
   tc::mbar_wait(&bar[0], 0, ws.err, 101);
   tc::fence_after_sync();
   {
-    // lane tid of the accumulator: rows 0-63 = kk row i, rows 64-127 = qk row i
-    float row[64];
-    float tmp[32];
-    const uint32_t lane_addr = tbase + (uint32_t(w * 32) << 16);
-    tc::tmem_ld32(lane_addr + 0, tmp);
+    // lane r of the accumulator: rows 0-63 = kk row i, rows 64-127 = qk row i; columns c0..c0+31
+    float row[32];
+    tc::tmem_ld32(lane_addr, row);
+    const int i = r & 63;
+    const float ci_ = cum[i];
+    if (r < 64) {
+      const float bi = beta[i] * rk[i];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) row[j] = tmp[j];
-    tc::tmem_ld32(lane_addr + 32, tmp);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) row[32 + j] = tmp[j];
-    if (tid < 64) {
-      const int i = tid;
-      const float bi = beta[i] * rk[i], ci_ = cum[i];
-#pragma unroll
-      for (int j = 0; j < 64; ++j)
-        lm[i * 65 + j] = j < i ? bi * rk[j] * row[j] * expf(ci_ - cum[j]) : 0.f;
-    } else {
-      const int i = tid - 64;
-      const float si = p.scale * rq[i], ci_ = cum[i];
-      uint32_t packed[32];
-#pragma unroll
-      for (int j = 0; j < 64; j += 2) {
-        const float a = j <= i ? si * rk[j] * row[j] * expf(ci_ - cum[j]) : 0.f;
-        const float b = j + 1 <= i ? si * rk[j + 1] * row[j + 1] * expf(ci_ - cum[j + 1]) : 0.f;
-        packed[j >> 1] = tc::pack_bf16(a, b);
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = c0 + jj;
+        lm[i * 65 + j] = j < i ? bi * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
       }
-      uint4* dst = reinterpret_cast<uint4*>(ws.aqk + ch * 4096 + i * 64);
+    } else {
+      const float si = p.scale * rq[i];
+      uint32_t packed[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+      for (int jj = 0; jj < 32; jj += 2) {
+        const int j = c0 + jj;
+        const float a = j <= i ? si * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
+        const float b = j + 1 <= i ? si * rk[j + 1] * row[jj + 1] * __expf(ci_ - cum[j + 1]) : 0.f;
+        packed[jj >> 1] = tc::pack_bf16(a, b);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(ws.aqk + ch * 4096 + i * 64 + c0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  unit_lower_inverse128(lm, tm, xbuf);
+  unit_lower_inverse(lm, tm, xbuf, 256);
   // T to the workspace (fp32, for the backward) and the two bf16 B operands
-  for (int idx = tid; idx < 4096; idx += 128) ws.tinv[ch * 4096 + idx] = tm[(idx >> 6) * 65 + (idx & 63)];
+  for (int idx = tid; idx < 1024; idx += 256) {
+    const int i = idx >> 4, c4 = (idx & 15) * 4;
+    *reinterpret_cast<float4*>(ws.tinv + ch * 4096 + i * 64 + c4) =
+        make_float4(tm[i * 65 + c4], tm[i * 65 + c4 + 1], tm[i * 65 + c4 + 2], tm[i * 65 + c4 + 3]);
+  }
   {
-    const int i = tid & 63;
-    unsigned char* dst = tid < 64 ? tb1 : tb2;
+    const int i = tid & 63, which = (tid >> 6) & 1, m0 = 32 * (tid >> 7);
+    unsigned char* dst = which == 0 ? tb1 : tb2;
 #pragma unroll
-    for (int m0 = 0; m0 < 64; m0 += 8) {
+    for (int mb = 0; mb < 32; mb += 8) {
       uint32_t pk[4];
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
-        const int m = m0 + j;
+        const int m = m0 + mb + j;
         float f0 = tm[i * 65 + m] * beta[m], f1 = tm[i * 65 + m + 1] * beta[m + 1];
-        if (tid >= 64) { f0 *= ecum[m] * rk[m]; f1 *= ecum[m + 1] * rk[m + 1]; }
+        if (which) { f0 *= ecum[m] * rk[m]; f1 *= ecum[m + 1] * rk[m + 1]; }
         pk[j >> 1] = tc::pack_bf16(f0, f1);
       }
-      *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, m0, 64)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, m0 + mb, 64)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
   }
   tc::fence_proxy_async();
@@ -206,34 +209,27 @@ __global__ void __launch_bounds__(128) fast_prep_kernel(GdnProblem p, FastWs ws)
     tc::mma_commit(&bar[1]);
   }
   // q~ and k~ rows while the MMAs run: half-warp per row, 8 elements per lane
-  for (int r = w * 2 + (l >> 4); r < 128; r += 8) {
+  for (int row = w * 2 + (l >> 4); row < 128; row += 16) {
     const int c8 = (l & 15) * 8;
-    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(r, c8, 128));
-    const int i = r & 63;
-    const float f = r < 64 ? expf(cum[63] - cum[i]) * rk[i] : p.scale * rq[i] * ecum[i];
+    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row, c8, 128));
+    const int i = row & 63;
+    const float f = row < 64 ? __expf(cum[63] - cum[i]) * rk[i] : p.scale * rq[i] * ecum[i];
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
-    bf16* dst = (r < 64 ? ws.kt : ws.qt) + ch * 8192 + i * 128 + c8;
+    bf16* dst = (row < 64 ? ws.kt : ws.qt) + ch * 8192 + i * 128 + c8;
     *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   tc::mbar_wait(&bar[1], 0, ws.err, 102);
   tc::fence_after_sync();
   {
-    // lane tid = dv (for U) or dk (for W); 64 token columns each
-    const uint32_t lane_addr = tbase + (uint32_t(w * 32) << 16);
+    // lane r = dv (for U) or dk (for W); tokens c0..c0+31
     float tmp[32];
-#pragma unroll
-    for (int part = 0; part < 2; ++part) {
-      bf16* dst = (part == 0 ? ws.u : ws.w) + ch * 8192 + tid;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tc::tmem_ld32(lane_addr + 64 + 64 * part + 32 * half, tmp);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) dst[(32 * half + j) * 128] = __float2bfloat16_rn(tmp[j]);
-      }
-    }
+    tc::tmem_ld32(lane_addr + 64, tmp);
+    store_cols32(ws.u + ch * 8192, 128, r, c0, 64, tmp);
+    tc::tmem_ld32(lane_addr + 128, tmp);
+    store_cols32(ws.w + ch * 8192, 128, r, c0, 64, tmp);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -451,7 +447,7 @@ int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_
   if (p.max_chunks > 0) {
     if ((rc = smem_attr(fast_prep_kernel, kPrepSmem))) return rc;
     ProfScope ps_("gdn_fast_prep", s);
-    fast_prep_kernel<<<dim3(p.max_chunks, p.Hv), 128, kPrepSmem, s>>>(p, w);
+    fast_prep_kernel<<<dim3(p.max_chunks, p.Hv), 256, kPrepSmem, s>>>(p, w);
     RB2_CHECK_LAUNCH("gdn fast prep");
   }
   if ((rc = smem_attr(fast_state_fwd_kernel, kStateSmem))) return rc;

@@ -65,12 +65,14 @@ __device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int
 __device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
 
-// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65), 128 threads.
-__device__ inline void unit_lower_inverse128(const float* lm, float* tm, float* xbuf) {
+// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65); `nthr` threads
+// (a multiple of 128). The four 16x16 diagonal blocks by forward substitution (warps 0-3, lane =
+// column), then the off-diagonal blocks by block rows: T_ij = -T_ii sum_{j<=m<i} L_im T_mj.
+__device__ inline void unit_lower_inverse(const float* lm, float* tm, float* xbuf, int nthr) {
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
-  for (int idx = tid; idx < 64 * 65; idx += 128) tm[idx] = 0.f;
+  for (int idx = tid; idx < 64 * 65; idx += nthr) tm[idx] = 0.f;
   __syncthreads();
-  if (l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
+  if (w < 4 && l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
     const int o = 16 * w;
     float col[16];
 #pragma unroll
@@ -85,14 +87,14 @@ __device__ inline void unit_lower_inverse128(const float* lm, float* tm, float* 
   }
   __syncthreads();
   for (int bi = 1; bi < 4; ++bi) {
-    for (int e = tid; e < bi * 256; e += 128) {  // X_bj = sum_{m in [16bj, 16bi)} L[16bi+r][m] T[m][16bj+c]
+    for (int e = tid; e < bi * 256; e += nthr) {  // X_bj = sum_{m in [16bj, 16bi)} L[16bi+r][m] T[m][16bj+c]
       const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
       float x = 0.f;
       for (int m = 16 * bj; m < 16 * bi; ++m) x = fmaf(lm[(16 * bi + r) * 65 + m], tm[m * 65 + 16 * bj + c], x);
       xbuf[e] = x;
     }
     __syncthreads();
-    for (int e = tid; e < bi * 256; e += 128) {  // T_bi,bj = -T_bi,bi X_bj
+    for (int e = tid; e < bi * 256; e += nthr) {  // T_bi,bj = -T_bi,bi X_bj
       const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
       float t = 0.f;
 #pragma unroll
@@ -100,6 +102,29 @@ __device__ inline void unit_lower_inverse128(const float* lm, float* tm, float* 
       tm[(16 * bi + r) * 65 + 16 * bj + c] = -t;
     }
     __syncthreads();
+  }
+}
+
+// 32 bf16 (64 bytes) of row r starting at element e0 of a K-major SW128 tile -> fp32
+__device__ __forceinline__ void store_row32(unsigned char* tile, int rows, int r, int e0, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                               tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0 + 8 * j, rows)) = x;
+  }
+}
+
+// Write 32 per-token values of head-dim column r (tokens 32 hh + j) as bf16 to dst[(tok) * row + r],
+// pairing lanes r, r^1 so that every store is one 4-byte bf16x2.
+__device__ __forceinline__ void store_cols32(bf16* dst, int64_t row, int r, int t_base, int L, const float (&v)[32]) {
+  const bool odd = (r & 1) != 0;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+    const int tk = t_base + j + (odd ? 1 : 0);
+    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
+    if (tk < L) *reinterpret_cast<uint32_t*>(dst + int64_t(tk) * row + (r & ~1)) = tc::pack_bf16(lo, hi);
   }
 }
 

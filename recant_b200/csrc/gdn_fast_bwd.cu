@@ -241,29 +241,6 @@ __device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
 
 __device__ __forceinline__ void tmem_ld32f(uint32_t addr, float (&v)[32]) { tc::tmem_ld32(addr, v); }
 
-// 32 bf16 (64 bytes) of row r starting at element e0 of a K-major SW128 tile -> fp32
-__device__ __forceinline__ void store_row32(unsigned char* tile, int rows, int r, int e0, const float (&v)[32]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
-                               tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
-    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0 + 8 * j, rows)) = x;
-  }
-}
-
-// Write 32 per-token values of head-dim column r (tokens 32 hh + j) as bf16 to dst[(tok) * row + r],
-// pairing lanes r, r^1 so that every store is one 4-byte bf16x2.
-__device__ __forceinline__ void store_cols32(bf16* dst, int64_t row, int r, int t_base, int L, const float (&v)[32]) {
-  const bool odd = (r & 1) != 0;
-#pragma unroll
-  for (int j = 0; j < 32; j += 2) {
-    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
-    const int tk = t_base + j + (odd ? 1 : 0);
-    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
-    if (tk < L) *reinterpret_cast<uint32_t*>(dst + int64_t(tk) * row + (r & ~1)) = tc::pack_bf16(lo, hi);
-  }
-}
-
 __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  bf16* __restrict__ dq, bf16* __restrict__ dk,
                                                                  bf16* __restrict__ dv, float* __restrict__ dg,
