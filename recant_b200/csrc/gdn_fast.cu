@@ -51,7 +51,8 @@ using namespace fast;
 
 // ------------------------------------------------------------------------------------------------
 // prep: one CTA (256 threads) per (chunk, value head). Thread (w, l): TMEM lane r = 32 (w & 3) + l,
-// column half hh = w >> 2 (columns [32 hh, 32 hh + 32) of the 64-wide accumulators).
+// column half hh = w >> 2 (columns [32 hh, 32 hh + 32) of the 64-wide accumulators). 128 TMEM columns:
+// [K;Q] K^T in [0, 64) is read before U^T / W^T overwrite [0, 128), so two CTAs share an SM.
 // ------------------------------------------------------------------------------------------------
 constexpr int kPrepSmem = 32768 + 16384 + 8192 + 8192 + 2 * 64 * 65 * 4 + 768 * 4 + 6 * 64 * 4 + 2048;
 
@@ -85,7 +86,10 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   const bf16* v = static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128;
   const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
 
-  if (w == 0) tc::tmem_alloc(&tmem_base, 256);
+  if (w == 0) {
+    tc::tmem_alloc(&tmem_base, 128);
+    tc::tmem_relinquish();
+  }
   if (tid == 0) {
     tc::mbar_init(&bar[0], 1);
     tc::mbar_init(&bar[1], 1);
@@ -203,8 +207,8 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
     const uint32_t va = tc::smem_u32(vt), ka = tc::smem_u32(kq), b1 = tc::smem_u32(tb1), b2 = tc::smem_u32(tb2);
 #pragma unroll
     for (int k0 = 0; k0 < 64; k0 += 16) {
-      tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(va + k0 * 128, 8192), tc::desc_kmajor_sw128(b1 + k0 * 2), idesc, k0 > 0);
-      tc::mma_bf16(tbase + 128, tc::desc_mnmajor_sw128(ka + k0 * 128, 16384), tc::desc_kmajor_sw128(b2 + k0 * 2), idesc, k0 > 0);
+      tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(va + k0 * 128, 8192), tc::desc_kmajor_sw128(b1 + k0 * 2), idesc, k0 > 0);
+      tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(ka + k0 * 128, 16384), tc::desc_kmajor_sw128(b2 + k0 * 2), idesc, k0 > 0);
     }
     tc::mma_commit(&bar[1]);
   }
@@ -226,14 +230,14 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   {
     // lane r = dv (for U) or dk (for W); tokens c0..c0+31
     float tmp[32];
-    tc::tmem_ld32(lane_addr + 64, tmp);
+    tc::tmem_ld32(lane_addr + 0, tmp);
     store_cols32(ws.u + ch * 8192, 128, r, c0, 64, tmp);
-    tc::tmem_ld32(lane_addr + 128, tmp);
+    tc::tmem_ld32(lane_addr + 64, tmp);
     store_cols32(ws.w + ch * 8192, 128, r, c0, 64, tmp);
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (w == 0) tc::tmem_dealloc(tbase, 256);
+  if (w == 0) tc::tmem_dealloc(tbase, 128);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -352,15 +356,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       tc::tmem_ld32(lane_addr + 32 * hh, x);
       uint32_t pk[16];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const int tk = 32 * hh + j;
-        const float a = __bfloat162float(cur.us[tk * 128 + r]) - x[j];
-        const float b = __bfloat162float(cur.us[(tk + 1) * 128 + r]) - x[j + 1];
-        pk[j >> 1] = tc::pack_bf16(a, b);
-        const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(&pk[j >> 1]);
-        ws.vp[ch * 8192 + tk * 128 + r] = ab.x;
-        ws.vp[ch * 8192 + (tk + 1) * 128 + r] = ab.y;
-      }
+      for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(cur.us[(32 * hh + j) * 128 + r]) - x[j];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
+      store_cols32(ws.vp + ch * 8192, 128, r, 32 * hh, 64, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -388,11 +387,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     {
       float x[32];
       tc::tmem_ld32(lane_addr + 64 + 32 * hh, x);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int tk = 32 * hh + j;
-        if (tk < L) o[(int64_t(t0 + tk) * p.Hv + h) * 128 + r] = __float2bfloat16_rn(x[j]);
-      }
+      store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, 32 * hh, L, x);
       const float gamma = expf(cur.cum[63]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {

@@ -155,13 +155,8 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       tc::tmem_ld32(lane_addr + 32 * hh, x);
       uint32_t pk[16];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-        const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(&pk[j >> 1]);
-        const int tk = 32 * hh + j;
-        ws.dvp[ch * 8192 + tk * 128 + r] = ab.x;
-        ws.dvp[ch * 8192 + (tk + 1) * 128 + r] = ab.y;
-      }
+      for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
+      store_cols32(ws.dvp + ch * 8192, 128, r, 32 * hh, 64, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(dvt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
