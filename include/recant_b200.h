@@ -98,6 +98,11 @@ RB2_API int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype, i
                        uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,
                        float* gscale, void* ws, size_t ws_bytes, void* stream);
 
+/* Scale bytes [rows, cols] (e4m3) -> the 128x4 blocked swizzle of nvfp4._to_blocked
+ * (recant/model/nvfp4.py:112-119), ceil(rows/128)*ceil(cols/4)*512 bytes, pad bytes zero. Lets
+ * FP4 tensors quantized elsewhere (e.g. by the reference's quantize_weight) feed the GEMM. */
+RB2_API int rb2_nvfp4_block_scales(const uint8_t* scales, int64_t rows, int64_t cols, uint8_t* blocked, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * NVFP4 block-scaled GEMM: out[M,N] = (A . B^T) * gA * gB where A = codes_a [M,K/2] with
  * blocked scales (128x4 swizzle) and B = codes_b [N,K/2] likewise; fp32 accumulation.

@@ -1,9 +1,273 @@
-// NVFP4 block-scaled GEMM (placeholder until the tcgen05 kind::mxf4nvf4 kernel lands).
-#include "common.cuh"
+// NVFP4 block-scaled GEMM on tcgen05: out[M,N] = (A . B^T) * gA * gB.
+//
+// Replaces the GEMM_BACKENDS of recant/model/nvfp4.py:108-125 (_gemm_emulated, and
+// _gemm_scaled_mm = torch._scaled_mm on cuBLASLt with the 128x4 blocked scale swizzle of
+// _to_blocked, nvfp4.py:112-119). A = codes [M, K/2] (two e2m1 per byte, even element in the low
+// nibble), B = codes [N, K/2]; per-16 e4m3 scales in the blocked layout; fp32 accumulation.
+//
+// One CTA computes a 128 x 256 output tile (grid = ceil(M/128) x ceil(N/256)), warp-specialised:
+//   warp 0     producer: TMA (cp.async.bulk.tensor, SW128, no multicast) of the A and B code tiles
+//              (128 bytes = 256 K-elements per row per stage) and 1-D bulk copies of the scale
+//              atoms into a 4-stage ring; completion via mbarrier transaction counts;
+//   warp 1     MMA: per 64-element K step, tcgen05.cp of the scale atoms into TMEM (32x128b.warpx4:
+//              lane m%32 of every sub-partition, 32-bit column m/32, one byte per 16-element block)
+//              and one tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64);
+//   warps 2-5  epilogue: TMEM -> registers -> * gA gB -> fp32 or bf16 rows.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
-extern "C" size_t rb2_nvfp4_gemm_workspace_size(int64_t, int64_t, int64_t) { return 0; }
-extern "C" int rb2_nvfp4_gemm(const uint8_t*, const uint8_t*, const float*, const uint8_t*, const uint8_t*,
-                              const float*, int64_t, int64_t, int64_t, void*, int, void*, size_t, void*) {
-  rb2::set_error("nvfp4_gemm: not built");
-  return RB2_EUNSUPPORTED;
+#include "tc.cuh"
+
+namespace rb2 {
+namespace {
+
+constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, cols, K bytes per stage (= 256 e2m1)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;       // 16 KB, 32 KB
+constexpr int SFA_BYTES = (BM / 128) * 4 * 512;               // 4 atoms of 128 rows x 4 scales
+constexpr int SFB_BYTES = (BN / 128) * 4 * 512;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int kGemmSmem = STAGES * STAGE_BYTES + 1024;
+constexpr int kThreads = 192;
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(tc::smem_u32(smem_dst)),
+      "l"(map), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   tc::smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+// smem descriptor of one 512-byte scale atom (32 rows x 16 bytes, no swizzle) for tcgen05.cp
+__device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFF);
+  d |= uint64_t(128 >> 4) << 16;  // LBO (single 16-byte column)
+  d |= uint64_t(128 >> 4) << 32;  // SBO: 8-row core matrices 128 bytes apart
+  d |= uint64_t(1) << 46;
+  return d;                       // layout type 0 = no swizzle
+}
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// kind::mxf4nvf4 instruction descriptor: e2m1 x e2m1, ue4m3 scales, K-major A and B, dense K=64
+__host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
+  return (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                  const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, const float* __restrict__ ga,
+                  const float* __restrict__ gb, int M, int N, int K, void* __restrict__ out, int out_bf16,
+                  int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023);
+  __shared__ uint64_t full[STAGES], empty[STAGES], accum_full;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int tm = blockIdx.x, tn = blockIdx.y;
+  const int ksteps = K / 64;                       // 64-element MMA steps
+  const int nstages = (ksteps + 3) / 4;            // 4 steps per stage
+  const int ncb = (K / 16 + 3) / 4;                // scale atoms per 128-row block
+
+  if (w == 1) {
+    tc::tmem_alloc(&tmem_base, 512);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(&accum_full, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+
+  if (w == 0) {
+    if (l == 0) {  // ---------------- producer ----------------
+      for (int kt = 0; kt < nstages; ++kt) {
+        const int s = kt % STAGES;
+        if (!tc::mbar_wait(&empty[s], ((kt / STAGES) & 1) ^ 1, err, 201)) break;
+        unsigned char* st = sm + s * STAGE_BYTES;
+        const int steps = min(4, ksteps - 4 * kt);
+        // B row blocks of this tile that exist in the blocked scale buffer (ceil(N/128) blocks)
+        const int nrb = min(BN / 128, (N + 127) / 128 - tn * (BN / 128));
+        const uint32_t sfa_bytes = steps * 512, sfb_bytes = steps * 512 * nrb;
+        mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sfa_bytes + sfb_bytes);
+        tma_load_2d(st, &map_a, kt * BKB, tm * BM, &full[s]);
+        tma_load_2d(st + A_BYTES, &map_b, kt * BKB, tn * BN, &full[s]);
+        bulk_load(st + A_BYTES + B_BYTES, sfa + (size_t(tm) * ncb + 4 * kt) * 512, sfa_bytes, &full[s]);
+        for (int rb = 0; rb < nrb; ++rb)
+          bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + rb * 2048,
+                    sfb + (size_t(tn * (BN / 128) + rb) * ncb + 4 * kt) * 512, steps * 512, &full[s]);
+      }
+    }
+  } else if (w == 1) {
+    if (l == 0) {  // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_nvf4(BM, BN);
+      const uint32_t t_acc = tbase, t_sfa = tbase + 256, t_sfb = tbase + 256 + 16;
+      for (int kt = 0; kt < nstages; ++kt) {
+        const int s = kt % STAGES;
+        if (!tc::mbar_wait(&full[s], (kt / STAGES) & 1, err, 202)) break;
+        tc::fence_after_sync();
+        const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
+        const uint32_t sa = st, sb = st + A_BYTES, ssfa = st + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
+        const int steps = min(4, ksteps - 4 * kt);
+        for (int kk = 0; kk < steps; ++kk) {
+          tmem_cp_sf(t_sfa + 4 * kk, desc_sf_atom(ssfa + 512 * kk));
+#pragma unroll
+          for (int rb = 0; rb < BN / 128; ++rb) tmem_cp_sf(t_sfb + 8 * kk + 4 * rb, desc_sf_atom(ssfb + rb * 2048 + 512 * kk));
+        }
+        for (int kk = 0; kk < steps; ++kk) {
+          mma_nvf4(t_acc, tc::desc_kmajor_sw128(sa + 32 * kk), tc::desc_kmajor_sw128(sb + 32 * kk), idesc, t_sfa + 4 * kk,
+                   t_sfb + 8 * kk, kt > 0 || kk > 0);
+        }
+        tc::mma_commit(&empty[s]);
+      }
+      tc::mma_commit(&accum_full);
+    }
+  } else {  // ---------------- epilogue: warps 2..5 ----------------
+    tc::mbar_wait(&accum_full, 0, err, 203);
+    tc::fence_after_sync();
+    const int q = w & 3;
+    const int row = tm * BM + 32 * q + l;
+    const float scale = ga[0] * gb[0];
+    const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tc::tmem_ld32(lane_addr + c0, v);
+      const int col0 = tn * BN + c0;
+      if (row < M) {
+        if (out_bf16) {
+          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
+          if (col0 + 32 <= N && (N % 8) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk = make_uint4(tc::pack_bf16(v[j] * scale, v[j + 1] * scale), tc::pack_bf16(v[j + 2] * scale, v[j + 3] * scale),
+                                    tc::pack_bf16(v[j + 4] * scale, v[j + 5] * scale), tc::pack_bf16(v[j + 6] * scale, v[j + 7] * scale));
+              *reinterpret_cast<uint4*>(o + j) = pk;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) o[j] = __float2bfloat16_rn(v[j] * scale);
+          }
+        } else {
+          float* o = static_cast<float*>(out) + size_t(row) * N + col0;
+          if (col0 + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(o + j) = make_float4(v[j] * scale, v[j + 1] * scale, v[j + 2] * scale, v[j + 3] * scale);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) o[j] = v[j] * scale;
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (w == 1) tc::tmem_dealloc(tbase, 512);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D byte tensor [rows][cols_bytes], box [box_rows][128 bytes], 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_bytes, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("nvfp4_gemm: cuTensorMapEncodeTiled unavailable");
+    return RB2_ECUDA;
+  }
+  cuuint64_t dims[2] = {cuuint64_t(cols_bytes), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols_bytes)};
+  cuuint32_t box[2] = {128u, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("nvfp4_gemm: cuTensorMapEncodeTiled failed (%d)", int(r));
+    return RB2_ECUDA;
+  }
+  return RB2_OK;
+}
+
+}  // namespace
+}  // namespace rb2
+
+using namespace rb2;
+
+extern "C" size_t rb2_nvfp4_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  (void)M; (void)N; (void)K;
+  return 256;  // device status word
+}
+
+extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                              const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                              int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws, size_t ws_bytes,
+                              void* stream) {
+  RB2_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % 64 == 0, "nvfp4_gemm: need M, N > 0 and K %% 64 == 0 (K=%lld)",
+                (long long)K);
+  RB2_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31), "nvfp4_gemm: size");
+  RB2_CHECK_ARG(a_codes && b_codes && a_scales_blocked && b_scales_blocked && a_gscale && b_gscale && out && ws,
+                "nvfp4_gemm: null pointer");
+  RB2_CHECK_ARG(out_dtype == RB2_F32 || out_dtype == RB2_BF16, "nvfp4_gemm: out_dtype");
+  RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(a_codes) & 15) == 0 && (reinterpret_cast<uintptr_t>(b_codes) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(a_scales_blocked) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(b_scales_blocked) & 15) == 0,
+                "nvfp4_gemm: operands must be 16-byte aligned");
+  if (ws_bytes < rb2_nvfp4_gemm_workspace_size(M, N, K)) {
+    set_error("nvfp4_gemm: workspace too small");
+    return RB2_EWORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_map(&ma, a_codes, M, K / 2, BM))) return rc;
+  if ((rc = make_map(&mb, b_codes, N, K / 2, BN))) return rc;
+  RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem),
+           "nvfp4_gemm: smem attribute");
+  RB2_CUDA(cudaMemsetAsync(ws, 0, sizeof(int), s), "nvfp4_gemm: clear status");
+  dim3 grid(unsigned((M + BM - 1) / BM), unsigned((N + BN - 1) / BN));
+  {
+    ProfScope ps_("nvfp4_gemm", s);
+    nvfp4_gemm_kernel<<<grid, kThreads, kGemmSmem, s>>>(ma, mb, a_scales_blocked, b_scales_blocked, a_gscale, b_gscale,
+                                                        int(M), int(N), int(K), out, out_dtype == RB2_BF16,
+                                                        static_cast<int*>(ws));
+  }
+  RB2_CHECK_LAUNCH("nvfp4_gemm");
+  return RB2_OK;
 }

@@ -240,3 +240,30 @@ extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype
   RB2_CHECK_LAUNCH("nvfp4_quantize");
   return RB2_OK;
 }
+
+namespace rb2 {
+namespace {
+__global__ void __launch_bounds__(256) block_scales_kernel(const uint8_t* __restrict__ scales, int64_t rows, int64_t cols,
+                                                           uint8_t* __restrict__ blocked) {
+  const int64_t n = rows * cols, ncb = (cols + 3) / 4;
+  for (int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x; i < n; i += int64_t(gridDim.x) * 256) {
+    const int64_t r = i / cols, c = i % cols;
+    blocked[((r >> 7) * ncb + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3)] = scales[i];
+  }
+}
+}  // namespace
+}  // namespace rb2
+
+extern "C" int rb2_nvfp4_block_scales(const uint8_t* scales, int64_t rows, int64_t cols, uint8_t* blocked,
+                                      void* stream) {
+  RB2_CHECK_ARG(rows > 0 && cols > 0 && scales && blocked, "nvfp4_block_scales: bad arguments");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t nb = size_t((rows + 127) / 128) * size_t((cols + 3) / 4) * 512;
+  RB2_CUDA(cudaMemsetAsync(blocked, 0, nb, s), "nvfp4_block_scales: clear");
+  {
+    ProfScope ps_("nvfp4_block_scales", s);
+    block_scales_kernel<<<148 * 4, 256, 0, s>>>(scales, rows, cols, blocked);
+  }
+  RB2_CHECK_LAUNCH("nvfp4_block_scales");
+  return RB2_OK;
+}

@@ -58,11 +58,17 @@ def quantize_fast(x: torch.Tensor, use_rht: bool = True, stochastic: bool = Fals
     return FP4Tensor(codes, scales.view(torch.float8_e4m3fn), gscale, (m, k), blocked)
 
 
-def _blocked_of(t) -> torch.Tensor:
+def blocked_scales(t) -> torch.Tensor:
+    """The 128x4 blocked swizzle of an FP4 tensor's scales (computed on the GPU if absent)."""
     b = getattr(t, "blocked", None)
     if b is not None:
         return b
-    raise ValueError("recant_b200.gemm_b200: operand has no blocked scales; quantize it with recant_b200")
+    rows, k = t.shape
+    sc = t.scales.contiguous().view(torch.uint8)
+    b = torch.empty(blocked_size(rows, k // BLOCK), dtype=torch.uint8, device=sc.device)
+    L.check(L.lib().rb2_nvfp4_block_scales(L.ptr(sc), rows, k // BLOCK, L.ptr(b),
+                                           torch.cuda.current_stream(sc.device).cuda_stream), "nvfp4_block_scales")
+    return b
 
 
 def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
@@ -71,15 +77,64 @@ def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
     n, kb = b.shape
     if k != kb:
         raise ValueError(f"recant_b200.gemm_b200: K mismatch {k} vs {kb}")
+    if not a.codes.is_cuda:
+        raise ValueError("recant_b200.gemm_b200: operands must be CUDA tensors (no CPU path)")
     out = torch.empty(m, n, dtype=out_dtype, device=a.codes.device)
     lib = L.lib()
     wsb = lib.rb2_nvfp4_gemm_workspace_size(m, n, k)
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=a.codes.device)
-    st = lib.rb2_nvfp4_gemm(L.ptr(a.codes), L.ptr(_blocked_of(a)), L.ptr(a.gscale), L.ptr(b.codes),
-                            L.ptr(_blocked_of(b)), L.ptr(b.gscale), m, n, k, L.ptr(out), _DT[out_dtype], L.ptr(ws),
-                            wsb, torch.cuda.current_stream(a.codes.device).cuda_stream)
+    ga = a.gscale.reshape(1).to(torch.float32).contiguous()
+    gb = b.gscale.reshape(1).to(torch.float32).contiguous()
+    st = lib.rb2_nvfp4_gemm(L.ptr(a.codes.contiguous()), L.ptr(blocked_scales(a)), L.ptr(ga),
+                            L.ptr(b.codes.contiguous()), L.ptr(blocked_scales(b)), L.ptr(gb), m, n, k, L.ptr(out),
+                            _DT[out_dtype], L.ptr(ws), wsb, torch.cuda.current_stream(a.codes.device).cuda_stream)
     L.check(st, "nvfp4_gemm")
     return out
+
+
+@dataclass
+class FP4Weight:
+    """Frozen NVFP4 weight with its fprop (Q(rht(W)) [N,K]) and dgrad (Q(rht(W^T)) [K,N]) copies,
+    as recant/model/nvfp4.py:93-106."""
+    fprop: FP4Tensor
+    dgrad: FP4Tensor
+    out_features: int
+    in_features: int
+    use_rht: bool
+
+
+def quantize_weight(w: torch.Tensor, use_rht: bool = True) -> FP4Weight:
+    """GPU quantize_weight (nvfp4.py:101-106): fp32 RHT, no re-rounding; bit-exact."""
+    n, k = w.shape
+    wf = w.detach().to(torch.float32).contiguous()
+    fp = quantize_fast(wf, use_rht, False)
+    dg = quantize_fast(wf.t().contiguous(), use_rht, False)
+    return FP4Weight(fp, dg, n, k, use_rht)
+
+
+class FP4Linear(torch.autograd.Function):
+    """fwd: Q(rht(x)) RN -> GEMM(fprop) -> x dtype; bwd: Q(rht(dy)) SR -> GEMM(dgrad); no weight
+    grad (recant/model/nvfp4.py:151-170)."""
+
+    @staticmethod
+    def forward(ctx, x, w: FP4Weight):
+        ctx.w = w
+        x2 = x.reshape(-1, w.in_features)
+        a = quantize_activation(x2, w.use_rht)
+        y = gemm_fp4(a, w.fprop)
+        return y.reshape(*x.shape[:-1], w.out_features).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        w = ctx.w
+        d2 = dy.reshape(-1, w.out_features)
+        d = quantize_activation(d2, w.use_rht, stochastic=True)
+        dx = gemm_fp4(d, w.dgrad)
+        return dx.reshape(*dy.shape[:-1], w.in_features).to(dy.dtype), None
+
+
+def fp4_linear(x: torch.Tensor, w: FP4Weight) -> torch.Tensor:
+    return FP4Linear.apply(x, w)
 
 
 # ----- registry mirror of recant/model/nvfp4.py:125-149 --------------------------------------

@@ -1,0 +1,96 @@
+"""NVFP4 block-scaled GEMM parity: tcgen05 kind::mxf4nvf4 vs the emulated reference GEMM
+(dequantise both operands, fp32 matmul; recant/model/nvfp4.py:108-110). Tolerance 5e-3 relative
+Frobenius (the reference's own check, recant/backends.py:21-35, allows 3e-2)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nvfp4 as ON
+
+pytestmark = pytest.mark.gpu
+TOL = 5e-3
+
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def _fp4(x_gpu, rht=True):
+    from recant_b200 import quantize_fast
+    return quantize_fast(x_gpu, rht, False)
+
+
+def _oracle(t, k):
+    return (t.codes.cpu().numpy(), t.scales.view(torch.uint8).cpu().numpy(), float(t.gscale.cpu()), (t.shape[0], k))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (300, 2048, 1024), (257, 384, 320), (64, 100, 64), (512, 1024, 4096)])
+def test_gemm_matches_emulated(M, N, K):
+    from recant_b200 import gemm_b200
+    gen = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    a, b = _fp4(x), _fp4(w)
+    out = gemm_b200(a, b).cpu().numpy()
+    ref = ON.gemm_emulated(_oracle(a, K), _oracle(b, K))
+    assert _rel(out, ref) < TOL, _rel(out, ref)
+    out16 = gemm_b200(a, b, out_dtype=torch.bfloat16).float().cpu().numpy()
+    assert _rel(out16, ref) < 1e-2
+
+
+def test_gemm_on_reference_layout_scales():
+    """Operands without pre-blocked scales (e.g. quantized by the reference) get blocked on the GPU."""
+    from recant_b200 import nvfp4 as N
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(200, 512, generator=gen)
+    c, s, g = ON.quantize_activation(x.numpy(), "f32", True)
+    t = N.FP4Tensor(torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda().view(torch.float8_e4m3fn),
+                    torch.tensor(g).cuda(), (200, 512))
+    out = N.gemm_b200(t, t).cpu().numpy()
+    ref = ON.gemm_emulated((c, s, g, (200, 512)), (c, s, g, (200, 512)))
+    assert _rel(out, ref) < TOL
+
+
+def test_reference_select_fp4_gemm_check():
+    """The reference's backend check (recant/backends.py:21-35): fprop and dgrad at 300x1024 @ 2048x1024
+    against the emulated GEMM, rel err < 0.03."""
+    from recant_b200 import nvfp4 as N
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(300, 1024, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(2048, 1024, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    W = N.quantize_weight(w)
+    a = N.quantize_fast(x, True, False)
+    e1 = _rel(N.gemm_b200(a, W.fprop).cpu().numpy(), ON.gemm_emulated(_oracle(a, 1024), _oracle(W.fprop, 1024)))
+    dy = torch.randn(300, 2048, generator=gen).to(torch.bfloat16).cuda()
+    d = N.quantize_fast(dy, True, True)
+    e2 = _rel(N.gemm_b200(d, W.dgrad).cpu().numpy(), ON.gemm_emulated(_oracle(d, 2048), _oracle(W.dgrad, 2048)))
+    assert e1 < 0.03 and e2 < 0.03 and e1 < TOL and e2 < TOL, (e1, e2)
+
+
+def test_quantize_weight_bit_exact():
+    """GPU quantize_weight equals the reference's (fp32 RHT, fprop and dgrad copies)."""
+    from recant_b200 import nvfp4 as N
+    gen = torch.Generator().manual_seed(21)
+    w = torch.randn(512, 256, generator=gen) * 0.02
+    W = N.quantize_weight(w.cuda())
+    fp, dg = ON.quantize_weight(w.numpy())
+    assert np.array_equal(W.fprop.codes.cpu().numpy(), fp[0]) and np.array_equal(W.dgrad.codes.cpu().numpy(), dg[0])
+    assert np.array_equal(W.fprop.scales.view(torch.uint8).cpu().numpy(), fp[1])
+    assert float(W.dgrad.gscale.cpu()) == float(dg[2])
+
+
+def test_fp4_linear_fwd_bwd():
+    """FP4Linear: forward = RN-quantized activations through fprop; backward = SR-quantized dy through dgrad."""
+    from recant_b200 import nvfp4 as N
+    gen = torch.Generator().manual_seed(5)
+    w = (torch.randn(512, 256, generator=gen) * 0.02).cuda()
+    W = N.quantize_weight(w)
+    x = torch.randn(4, 32, 256, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    y = N.fp4_linear(x, W)
+    ref = ON.gemm_emulated(_oracle(N.quantize_fast(x.detach().reshape(-1, 256), True, False), 256), _oracle(W.fprop, 256))
+    assert _rel(y.detach().float().reshape(-1, 512).cpu().numpy(), ref) < 1e-2
+    dy = torch.randn(4, 32, 512, generator=gen).to(torch.bfloat16).cuda()
+    y.backward(dy)
+    exact = (dy.float().reshape(-1, 512) @ w.float()).cpu().numpy()
+    assert x.grad.shape == x.shape and _rel(x.grad.float().reshape(-1, 256).cpu().numpy(), exact) < 0.2
