@@ -5,7 +5,7 @@
 // _to_blocked, nvfp4.py:112-119). A = codes [M, K/2] (two e2m1 per byte, even element in the low
 // nibble), B = codes [N, K/2]; per-16 e4m3 scales in the blocked layout; fp32 accumulation.
 //
-// One CTA computes a 128 x 256 output tile (grid = ceil(M/128) x ceil(N/256)), warp-specialised:
+// Persistent CTAs (one per SM) walk 128 x 256 output tiles, warp-specialised:
 //   warp 0     producer: TMA (cp.async.bulk.tensor, SW128, no multicast) of the A and B code tiles
 //              (128 bytes = 256 K-elements per row per stage) and 1-D bulk copies of the scale
 //              atoms into a 4-stage ring; completion via mbarrier transaction counts;
@@ -21,14 +21,22 @@
 namespace rb2 {
 namespace {
 
-constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, cols, K bytes per stage (= 256 e2m1)
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;       // 16 KB, 32 KB
-constexpr int SFA_BYTES = (BM / 128) * 4 * 512;               // 4 atoms of 128 rows x 4 scales
-constexpr int SFB_BYTES = (BN / 128) * 4 * 512;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-constexpr int kGemmSmem = STAGES * STAGE_BYTES + 1024;
+constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (= 256 e2m1)
 constexpr int kThreads = 192;
+
+// Tile shape: BN output columns, STAGES smem stages, ACC TMEM accumulator buffers.
+template <int BN_, int STAGES_, int ACC_>
+struct GemmCfg {
+  static constexpr int BN = BN_, STAGES = STAGES_, ACC = ACC_;
+  static constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;
+  static constexpr int SFA_BYTES = (BM / 128) * 4 * 512;  // 4 atoms of 128 rows x 4 scales
+  static constexpr int SFB_BYTES = (BN / 128) * 4 * 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int SF_COL0 = ACC * BN;                  // TMEM: accumulators, then scale factors
+  static_assert(SF_COL0 + 16 + 8 * (BN / 128) * 4 <= 512, "TMEM budget");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+};
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
@@ -73,6 +81,15 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0), "r"(sfa_tmem), "r"(sfb_tmem));
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+
+// Persistent: CTA c handles tiles c, c + gridDim.x, ... (tile t -> row block t / ntn, column block
+// t % ntn, so concurrently running CTAs share A row blocks in L2). The producer streams stages
+// across tile boundaries; the single TMEM accumulator is handed between the MMA warp and the
+// epilogue warps with acc_full / acc_empty.
+template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, const float* __restrict__ ga,
@@ -80,13 +97,15 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                   int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023);
-  __shared__ uint64_t full[STAGES], empty[STAGES], accum_full;
+  constexpr int BN = C::BN, STAGES = C::STAGES, ACC = C::ACC;
+  constexpr int A_BYTES = C::A_BYTES, B_BYTES = C::B_BYTES, SFA_BYTES = C::SFA_BYTES, STAGE_BYTES = C::STAGE_BYTES;
+  __shared__ uint64_t full[STAGES], empty[STAGES], acc_full[ACC], acc_empty[ACC];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
-  const int tm = blockIdx.x, tn = blockIdx.y;
   const int ksteps = K / 64;                       // 64-element MMA steps
   const int nstages = (ksteps + 3) / 4;            // 4 steps per stage
   const int ncb = (K / 16 + 3) / 4;                // scale atoms per 128-row block
+  const int ntm = (M + BM - 1) / BM, ntn = (N + BN - 1) / BN, ntiles = ntm * ntn;
 
   if (w == 1) {
     tc::tmem_alloc(&tmem_base, 512);
@@ -97,7 +116,10 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
-    tc::mbar_init(&accum_full, 1);
+    for (int b = 0; b < ACC; ++b) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], 4);   // one arrival per epilogue warp
+    }
     tc::fence_mbar_init();
   }
   __syncthreads();
@@ -106,85 +128,105 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
 
   if (w == 0) {
     if (l == 0) {  // ---------------- producer ----------------
-      for (int kt = 0; kt < nstages; ++kt) {
-        const int s = kt % STAGES;
-        if (!tc::mbar_wait(&empty[s], ((kt / STAGES) & 1) ^ 1, err, 201)) break;
-        unsigned char* st = sm + s * STAGE_BYTES;
-        const int steps = min(4, ksteps - 4 * kt);
-        // B row blocks of this tile that exist in the blocked scale buffer (ceil(N/128) blocks)
+      int g = 0;   // global stage counter
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int tm = t / ntn, tn = t % ntn;
         const int nrb = min(BN / 128, (N + 127) / 128 - tn * (BN / 128));
-        const uint32_t sfa_bytes = steps * 512, sfb_bytes = steps * 512 * nrb;
-        mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sfa_bytes + sfb_bytes);
-        tma_load_2d(st, &map_a, kt * BKB, tm * BM, &full[s]);
-        tma_load_2d(st + A_BYTES, &map_b, kt * BKB, tn * BN, &full[s]);
-        bulk_load(st + A_BYTES + B_BYTES, sfa + (size_t(tm) * ncb + 4 * kt) * 512, sfa_bytes, &full[s]);
-        for (int rb = 0; rb < nrb; ++rb)
-          bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + rb * 2048,
-                    sfb + (size_t(tn * (BN / 128) + rb) * ncb + 4 * kt) * 512, steps * 512, &full[s]);
+        for (int kt = 0; kt < nstages; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = tc::mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, err, 201))) break;
+          unsigned char* st = sm + s * STAGE_BYTES;
+          const int steps = min(4, ksteps - 4 * kt);
+          const uint32_t sfa_bytes = steps * 512, sfb_bytes = steps * 512 * nrb;
+          mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sfa_bytes + sfb_bytes);
+          tma_load_2d(st, &map_a, kt * BKB, tm * BM, &full[s]);
+          tma_load_2d(st + A_BYTES, &map_b, kt * BKB, tn * BN, &full[s]);
+          bulk_load(st + A_BYTES + B_BYTES, sfa + (size_t(tm) * ncb + 4 * kt) * 512, sfa_bytes, &full[s]);
+          for (int rb = 0; rb < nrb; ++rb)
+            bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + rb * 2048,
+                      sfb + (size_t(tn * (BN / 128) + rb) * ncb + 4 * kt) * 512, steps * 512, &full[s]);
+        }
       }
     }
   } else if (w == 1) {
     if (l == 0) {  // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_nvf4(BM, BN);
-      const uint32_t t_acc = tbase, t_sfa = tbase + 256, t_sfb = tbase + 256 + 16;
-      for (int kt = 0; kt < nstages; ++kt) {
-        const int s = kt % STAGES;
-        if (!tc::mbar_wait(&full[s], (kt / STAGES) & 1, err, 202)) break;
+      constexpr uint32_t idesc = idesc_nvf4(BM, BN);
+      const uint32_t t_sfa = tbase + C::SF_COL0, t_sfb = t_sfa + 16;
+      int g = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++local) {
+        const int ab = local % ACC;
+        const uint32_t t_acc = tbase + ab * BN;
+        if (!(ok = tc::mbar_wait(&acc_empty[ab], ((local / ACC) & 1) ^ 1, err, 204))) break;
         tc::fence_after_sync();
-        const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
-        const uint32_t sa = st, sb = st + A_BYTES, ssfa = st + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
-        const int steps = min(4, ksteps - 4 * kt);
-        for (int kk = 0; kk < steps; ++kk) {
-          tmem_cp_sf(t_sfa + 4 * kk, desc_sf_atom(ssfa + 512 * kk));
+        for (int kt = 0; kt < nstages; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = tc::mbar_wait(&full[s], (g / STAGES) & 1, err, 202))) break;
+          tc::fence_after_sync();
+          const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
+          const uint32_t sa = st, sb = st + A_BYTES, ssfa = st + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
+          const int steps = min(4, ksteps - 4 * kt);
+          for (int kk = 0; kk < steps; ++kk) {
+            tmem_cp_sf(t_sfa + 4 * kk, desc_sf_atom(ssfa + 512 * kk));
 #pragma unroll
-          for (int rb = 0; rb < BN / 128; ++rb) tmem_cp_sf(t_sfb + 8 * kk + 4 * rb, desc_sf_atom(ssfb + rb * 2048 + 512 * kk));
+            for (int rb = 0; rb < BN / 128; ++rb)
+              tmem_cp_sf(t_sfb + 4 * (BN / 128) * kk + 4 * rb, desc_sf_atom(ssfb + rb * 2048 + 512 * kk));
+          }
+          for (int kk = 0; kk < steps; ++kk)
+            mma_nvf4(t_acc, tc::desc_kmajor_sw128(sa + 32 * kk), tc::desc_kmajor_sw128(sb + 32 * kk), idesc,
+                     t_sfa + 4 * kk, t_sfb + 4 * (BN / 128) * kk, kt > 0 || kk > 0);
+          tc::mma_commit(&empty[s]);
         }
-        for (int kk = 0; kk < steps; ++kk) {
-          mma_nvf4(t_acc, tc::desc_kmajor_sw128(sa + 32 * kk), tc::desc_kmajor_sw128(sb + 32 * kk), idesc, t_sfa + 4 * kk,
-                   t_sfb + 8 * kk, kt > 0 || kk > 0);
-        }
-        tc::mma_commit(&empty[s]);
+        tc::mma_commit(&acc_full[ab]);
       }
-      tc::mma_commit(&accum_full);
     }
   } else {  // ---------------- epilogue: warps 2..5 ----------------
-    tc::mbar_wait(&accum_full, 0, err, 203);
-    tc::fence_after_sync();
     const int q = w & 3;
-    const int row = tm * BM + 32 * q + l;
     const float scale = ga[0] * gb[0];
-    const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16);
+    int local = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
+      const int tm = t / ntn, tn = t % ntn;
+      const int ab = local % ACC;
+      const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16) + ab * BN;
+      if (!tc::mbar_wait(&acc_full[ab], (local / ACC) & 1, err, 203)) break;
+      tc::fence_after_sync();
+      const int row = tm * BM + 32 * q + l;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      tc::tmem_ld32(lane_addr + c0, v);
-      const int col0 = tn * BN + c0;
-      if (row < M) {
-        if (out_bf16) {
-          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
-          if (col0 + 32 <= N && (N % 8) == 0) {
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(lane_addr + c0, v);
+        const int col0 = tn * BN + c0;
+        if (row < M && col0 < N) {
+          if (out_bf16) {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
+            if (col0 + 32 <= N && (N % 8) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 pk = make_uint4(tc::pack_bf16(v[j] * scale, v[j + 1] * scale), tc::pack_bf16(v[j + 2] * scale, v[j + 3] * scale),
-                                    tc::pack_bf16(v[j + 4] * scale, v[j + 5] * scale), tc::pack_bf16(v[j + 6] * scale, v[j + 7] * scale));
-              *reinterpret_cast<uint4*>(o + j) = pk;
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk = make_uint4(tc::pack_bf16(v[j] * scale, v[j + 1] * scale), tc::pack_bf16(v[j + 2] * scale, v[j + 3] * scale),
+                                      tc::pack_bf16(v[j + 4] * scale, v[j + 5] * scale), tc::pack_bf16(v[j + 6] * scale, v[j + 7] * scale));
+                *reinterpret_cast<uint4*>(o + j) = pk;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) o[j] = __float2bfloat16_rn(v[j] * scale);
             }
           } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) o[j] = __float2bfloat16_rn(v[j] * scale);
-          }
-        } else {
-          float* o = static_cast<float*>(out) + size_t(row) * N + col0;
-          if (col0 + 32 <= N && (N % 4) == 0) {
+            float* o = static_cast<float*>(out) + size_t(row) * N + col0;
+            if (col0 + 32 <= N && (N % 4) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(o + j) = make_float4(v[j] * scale, v[j + 1] * scale, v[j + 2] * scale, v[j + 3] * scale);
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) o[j] = v[j] * scale;
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(o + j) = make_float4(v[j] * scale, v[j + 1] * scale, v[j + 2] * scale, v[j + 3] * scale);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) o[j] = v[j] * scale;
+            }
           }
         }
       }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (l == 0) mbar_arrive(&acc_empty[ab]);
     }
   }
   tc::fence_before_sync();
@@ -256,17 +298,23 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CUtensorMap ma, mb;
   int rc;
+  using Wide = GemmCfg<256, 4, 1>;
+  const int BN = Wide::BN;
   if ((rc = make_map(&ma, a_codes, M, K / 2, BM))) return rc;
   if ((rc = make_map(&mb, b_codes, N, K / 2, BN))) return rc;
-  RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem),
-           "nvfp4_gemm: smem attribute");
   RB2_CUDA(cudaMemsetAsync(ws, 0, sizeof(int), s), "nvfp4_gemm: clear status");
-  dim3 grid(unsigned((M + BM - 1) / BM), unsigned((N + BN - 1) / BN));
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ntiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  dim3 grid(unsigned(ntiles < sms ? ntiles : sms));
   {
     ProfScope ps_("nvfp4_gemm", s);
-    nvfp4_gemm_kernel<<<grid, kThreads, kGemmSmem, s>>>(ma, mb, a_scales_blocked, b_scales_blocked, a_gscale, b_gscale,
-                                                        int(M), int(N), int(K), out, out_dtype == RB2_BF16,
-                                                        static_cast<int*>(ws));
+      RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide>, cudaFuncAttributeMaxDynamicSharedMemorySize, Wide::SMEM),
+             "nvfp4_gemm: smem attribute");
+    nvfp4_gemm_kernel<Wide><<<grid, kThreads, Wide::SMEM, s>>>(ma, mb, a_scales_blocked, b_scales_blocked, a_gscale,
+                                                               b_gscale, int(M), int(N), int(K), out,
+                                                               out_dtype == RB2_BF16, static_cast<int*>(ws));
   }
   RB2_CHECK_LAUNCH("nvfp4_gemm");
   return RB2_OK;
