@@ -98,6 +98,19 @@ RB2_API int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype, i
                        uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,
                        float* gscale, void* ws, size_t ws_bytes, void* stream);
 
+/* Allocation-free rb2_nvfp4_quantize (no counterpart in the reference). For callers that cannot
+ * provide device scratch -- C/C++ embedders without a device allocator, serving loops whose
+ * allocator is frozen, code where a cudaMalloc would synchronise or break a memory cap -- the
+ * quantizer's one scratch word (the global |x| maximum) lives in a 256-byte file-scope device
+ * array that every GPU loading the library keeps until exit. Same arguments and results as
+ * rb2_nvfp4_quantize minus ws/ws_bytes; returns RB2_EWORKSPACE if a size would need more than the
+ * 256-byte buffer. The first call on each device looks the buffer's address up (make it before any
+ * stream capture). All calls share the buffer and each call clears it first; calls that overlap on
+ * the GPU (concurrent streams) race on it. Never allocates or frees device memory. */
+RB2_API int rb2_nvfp4_quantize_noalloc(const void* x, int64_t M, int64_t K, int dtype, int use_rht, int stochastic,
+                                       uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,
+                                       float* gscale, void* stream);
+
 /* Scale bytes [rows, cols] (e4m3) -> the 128x4 blocked swizzle of nvfp4._to_blocked
  * (recant/model/nvfp4.py:112-119), ceil(rows/128)*ceil(cols/4)*512 bytes, pad bytes zero. Lets
  * FP4 tensors quantized elsewhere (e.g. by the reference's quantize_weight) feed the GEMM. */

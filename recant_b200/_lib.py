@@ -28,6 +28,7 @@ SIGNATURES = {
                          _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "rb2_nvfp4_quantize_workspace_size": (_sz, [_i64, _i64]),
     "rb2_nvfp4_quantize": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p, _sz, _p]),
+    "rb2_nvfp4_quantize_noalloc": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p]),
     "rb2_nvfp4_block_scales": (_i, [_p, _i64, _i64, _p, _p]),
     "rb2_nvfp4_gemm_workspace_size": (_sz, [_i64, _i64, _i64]),
     "rb2_nvfp4_gemm": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _p]),

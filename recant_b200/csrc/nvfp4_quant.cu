@@ -267,3 +267,64 @@ extern "C" int rb2_nvfp4_block_scales(const uint8_t* scales, int64_t rows, int64
   RB2_CHECK_LAUNCH("nvfp4_block_scales");
   return RB2_OK;
 }
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free variant of rb2_nvfp4_quantize.
+//
+// Some callers cannot hand the library a workspace: C or C++ code that embeds the library without
+// a device allocator of its own, serving loops that run with the caching allocator frozen, and
+// code paths where a cudaMalloc would synchronise the device or fail under a memory cap. For them
+// the quantizer's only scratch -- the word that collects the global |x| maximum -- lives in a
+// file-scope device array instead. That array exists once per GPU that loads the library and stays
+// allocated until the process exits. Every call shares it: the kernel clears the word at the start
+// of each call, and calls whose kernels overlap on the GPU (two streams at once) race on it.
+// ------------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace rb2 {
+namespace {
+constexpr size_t kQuantStaticScratchBytes = 256;
+__device__ __align__(256) unsigned char g_quant_scratch[kQuantStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// Device address of g_quant_scratch on the current device. The name g_quant_scratch is only a
+// host-side stand-in in host code, so the address is looked up once per device, with that device
+// current, on the first call that runs there.
+int static_scratch(void** out) {
+  int dev = 0;
+  RB2_CUDA(cudaGetDevice(&dev), "nvfp4_quantize_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("nvfp4_quantize_noalloc: device ordinal %d out of range", dev);
+    return RB2_EINVAL;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    RB2_CUDA(cudaGetSymbolAddress(&p, g_quant_scratch), "nvfp4_quantize_noalloc: cudaGetSymbolAddress");
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return RB2_OK;
+}
+}  // namespace
+}  // namespace rb2
+
+extern "C" int rb2_nvfp4_quantize_noalloc(const void* x, int64_t M, int64_t K, int dtype, int use_rht,
+                                          int stochastic, uint64_t seed, uint8_t* codes, uint8_t* scales,
+                                          uint8_t* scales_blocked, float* gscale, void* stream) {
+  const size_t need = rb2_nvfp4_quantize_workspace_size(M, K);
+  if (need > rb2::kQuantStaticScratchBytes) {
+    rb2::set_error("nvfp4_quantize_noalloc: M=%lld K=%lld needs %zu bytes of scratch, more than the %zu-byte static "
+                   "buffer; use rb2_nvfp4_quantize with a workspace",
+                   (long long)M, (long long)K, need, rb2::kQuantStaticScratchBytes);
+    return RB2_EWORKSPACE;
+  }
+  void* scratch = nullptr;
+  const int rc = rb2::static_scratch(&scratch);
+  if (rc) return rc;
+  return rb2_nvfp4_quantize(x, M, K, dtype, use_rht, stochastic, seed, codes, scales, scales_blocked, gscale, scratch,
+                            rb2::kQuantStaticScratchBytes, stream);
+}
