@@ -138,6 +138,14 @@ def make_inputs(dev, rank, B, T, Hk, Hv, d):
     return dict(q=q, k=k, v=v, g=g, beta=beta), do
 
 
+def config3_lengths(n=64, lo=128, hi=8192, seed=0):
+    """Config 3: 64 sequence lengths uniform in [128, 8192] from a seeded CPU generator
+    (243,613 tokens at seed 0)."""
+    import torch
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(lo, hi + 1, (n,), generator=gen).tolist()
+
+
 def cpu_reference_sample(B, T, Hk, Hv, d, reps):
     """The reference op's CPU path (oracle port of gdn_torch + autograd) on a bounded sample.
     Returns tokens/s, threads, the sample description and seconds."""
@@ -195,6 +203,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[1, 3], default=1,
+                    help="1: B4 T4096 replicas (the headline); 3: packed varlen, data-parallel by tokens")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -217,14 +227,29 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     c = CFG
     B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
+    cu = None
+    bucket = None
+    total_tokens = B * T * world
+    if args.config == 3:
+        from recant_b200 import parallel as P
+        lengths = config3_lengths()
+        parts, loads = P.lpt_partition(lengths, world)
+        mine = [lengths[i] for i in parts[rank]]
+        B, T = 1, sum(mine)
+        cu = P.cu_seqlens_of(mine, device=dev)
+        total_tokens = sum(lengths)
+        bucket = torch.ones(P.lora_bucket_numel(), dtype=torch.float32, device=dev)
     inp, do = make_inputs(dev, rank, B, T, Hk, Hv, d)
     leaves = {n: t.clone().requires_grad_(True) for n, t in inp.items()}
 
     def step():
         for t in leaves.values():
             t.grad = None
-        o, _ = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], path=args.path)
+        o, _ = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], cu_seqlens=cu,
+                        path=args.path)
         o.backward(do)
+        if bucket is not None and world > 1:
+            dist.all_reduce(bucket)
 
     def barrier():
         if world > 1:
@@ -256,7 +281,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     tokens = B * T
-    value = world * tokens / (ms / 1e3)
+    value = total_tokens / (ms / 1e3)
 
     # ---- end to end through the public op with host buffers ------------------------------
     host_in = {n: t.detach().cpu().pin_memory() for n, t in inp.items()}
@@ -269,8 +294,11 @@ def main():
     def e2e_step():
         dev_in = {n: t.to(dev, non_blocking=True).requires_grad_(True) for n, t in host_in.items()}
         ddo = host_do.to(dev, non_blocking=True)
-        o, _ = gdn_b200(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], path=args.path)
+        o, _ = gdn_b200(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], cu_seqlens=cu,
+                        path=args.path)
         o.backward(ddo)
+        if bucket is not None and world > 1:
+            dist.all_reduce(bucket)
         o_host.copy_(o.detach(), non_blocking=True)
         for n, t in dev_in.items():
             outs_host[n].copy_(t.grad, non_blocking=True)
@@ -290,7 +318,7 @@ def main():
         t = torch.tensor([ms_e2e], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_e2e = float(t.item())
-    e2e_value = world * tokens / (ms_e2e / 1e3)
+    e2e_value = total_tokens / (ms_e2e / 1e3)
 
     # ---- roofline of the dominant kernel ----------------------------------------------------
     pk = peaks()
@@ -301,7 +329,7 @@ def main():
         a[1] += t
     total_k = sum(v[1] for v in per_kernel.values()) or 1.0
     top = max(per_kernel, key=lambda n: per_kernel[n][1]) if per_kernel else None
-    n_ch = (tokens // 64 + (1 if tokens % 64 else 0)) * Hv
+    n_ch = (sum(-(-n // 64) for n in mine) if args.config == 3 else B * (-(-T // 64))) * Hv
     roof = None
     if top is not None:
         launches, tot = per_kernel[top]
@@ -313,18 +341,25 @@ def main():
                 "peak_source": f"{pk['source']} bf16 burst (MEASURED_PEAKS.json)",
                 "share_of_kernel_time": round(tot / total_k, 3), "avg_launch_ms": round(avg_s * 1e3, 4)}
     path_flops = FLOP_PER_TOKEN_HEAD * tokens * Hv
-    path_bytes = algorithmic_bytes(B, T, Hk, Hv, d)
+    path_bytes = algorithmic_bytes(B, T, Hk, Hv, d) if args.config == 1 else algorithmic_bytes(1, T, Hk, Hv, d)
     t_roof = max(path_flops / (pk["bf16"] * 1e12), path_bytes / (pk["hbm"] * 1e9))
     kernels = {n: {"launches": v[0], "ms_total": round(v[1], 3), "share": round(v[1] / total_k, 3)}
                for n, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][1])}
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak" if args.config == 1 else "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",
-                   "global_batch": B * world, "seq_len": T, "parallelism": f"replicas x{world}",
-                   "path": args.path, "l2": "inputs (q,k,v,dO ~ 470 MB) exceed the 126 MB L2; no flush"},
+        "config": ({"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",
+                    "global_batch": B * world, "seq_len": T, "parallelism": f"replicas x{world}",
+                    "path": args.path, "l2": "inputs (q,k,v,dO ~ 470 MB) exceed the 126 MB L2; no flush"}
+                   if args.config == 1 else
+                   {"workload": "config3: packed varlen GDN fwd+bwd, 64 sequences U[128,8192] (243,613 tokens), "
+                                "Hk16 Hv32 d128, LPT token balance + 44 MB fp32 LoRA-bucket NCCL all-reduce per step",
+                    "global_batch": 64, "tokens": total_tokens, "tokens_this_rank": tokens,
+                    "parallelism": f"dp{world}", "path": args.path,
+                    "l2": "per-rank inputs exceed the 126 MB L2; no flush"}),
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": roof,
@@ -335,7 +370,7 @@ def main():
         "kernels": kernels,
         "clocks": clock_info,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and args.config == 1 and not args.no_cpu_baseline:
         tps, threads, sample, _ = cpu_reference_sample(1, 2048, Hk, Hv, d, 1)
         line["cpu_baseline"] = {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                                 "sample": sample}
