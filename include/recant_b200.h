@@ -82,6 +82,25 @@ RB2_API int rb2_gdn_bwd(const void* q, const void* k, const void* v, const float
                 const void* d_o, const float* dhT, void* dq, void* dk_out, void* dv_out,
                 float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* stream);
 
+/* Stage-selecting forms of rb2_gdn_fwd / rb2_gdn_bwd for segmented and context-parallel runs
+ * (no counterpart in the reference op; tensor-core path only). fwd stages: 1 = chunk table + per-
+ * chunk prep, 2 = state walk, 3 = both. bwd stages: 1 = reversed state walk, 2 = chunk backward.
+ * walk = 0: normal; 1: state only (final state / initial-state gradient, no per-chunk outputs);
+ * 2 (fwd): transition -- U = 0 and S_0 = I for every sequence, so hT receives each sequence's
+ * state-transition matrix M with S_out = M S_in + S_out(S_in = 0), and M^T maps the gradient of
+ * the final state to that of the initial state. A later stage must see the same ws and arguments
+ * (except h0 / dhT) as the stage-1 call that filled ws. */
+RB2_API int rb2_gdn_fwd_ex(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                           const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                           int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
+                           void* o, float* hT, void* ws, size_t ws_bytes, void* stream, int stages, int walk);
+RB2_API int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                           const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                           int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
+                           const void* d_o, const float* dhT, void* dq, void* dk_out, void* dv_out,
+                           float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* stream,
+                           int stages, int walk);
+
 /* ---------------------------------------------------------------------------------------------
  * NVFP4 quantizer: codes/scales/gscale of quantize(rht(x)) (use_rht=1) or quantize(x),
  * bit-exact with recant/model/nvfp4.py:23-31,59-91 for round-to-nearest; stochastic=1 is the

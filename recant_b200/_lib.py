@@ -26,6 +26,10 @@ SIGNATURES = {
                          _p, _p, _p, _sz, _p]),
     "rb2_gdn_bwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
                          _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "rb2_gdn_fwd_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
+                            _p, _p, _p, _sz, _p, _i, _i]),
+    "rb2_gdn_bwd_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
+                            _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p, _i, _i]),
     "rb2_nvfp4_quantize_workspace_size": (_sz, [_i64, _i64]),
     "rb2_nvfp4_quantize": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p, _sz, _p]),
     "rb2_nvfp4_quantize_noalloc": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p]),

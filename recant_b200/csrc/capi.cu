@@ -90,15 +90,21 @@ extern "C" size_t rb2_gdn_workspace_size(int64_t B, int64_t T, int64_t n_seqs, i
   return exact_ws_bytes(p, nullptr, nullptr);
 }
 
-extern "C" int rb2_gdn_fwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
-                           const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
-                           int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, void* o,
-                           float* hT, void* ws, size_t ws_bytes, void* stream) {
+namespace rb2 {
+namespace {
+int gdn_fwd_impl(const void* q, const void* k, const void* v, const float* g, const void* beta, const float* h0,
+                 const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
+                 int dtype, int path, float scale, void* o, float* hT, void* ws, size_t ws_bytes, void* stream,
+                 int stages, int walk) {
   int rc = check_problem(B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, cu_seqlens != nullptr);
   if (rc) return rc;
   RB2_CHECK_ARG(ws != nullptr, "gdn_fwd: null workspace");
-  RB2_CHECK_ARG(B * T == 0 || (q && k && v && g && beta && o), "gdn_fwd: null input/output pointer");
+  RB2_CHECK_ARG(stages >= 1 && stages <= 3 && walk >= 0 && walk <= 2, "gdn_fwd: bad stages/walk");
+  RB2_CHECK_ARG(B * T == 0 || (q && k && v && g && beta && (o || walk != 0 || !(stages & 2))),
+                "gdn_fwd: null input/output pointer");
   GdnProblem p = make_problem(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dtype, path, scale);
+  p.stages = stages;
+  p.walk = walk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.path == RB2_GDN_FAST) {
     if (ws_bytes < fast_workspace_size(p.tokens, p.n_seqs, Hk, Hv, p.max_chunks)) {
@@ -106,6 +112,10 @@ extern "C" int rb2_gdn_fwd(const void* q, const void* k, const void* v, const fl
       return RB2_EWORKSPACE;
     }
     return fast_forward(p, ws, o, hT, s);
+  }
+  if (stages != 3 || walk != 0) {
+    set_error("gdn_fwd: stage/walk selection needs the tensor-core path");
+    return RB2_EUNSUPPORTED;
   }
   ExactWs w;
   if (ws_bytes < exact_ws_bytes(p, &w, ws)) {
@@ -116,16 +126,20 @@ extern "C" int rb2_gdn_fwd(const void* q, const void* k, const void* v, const fl
   return exact_forward<float>(p, w, static_cast<float*>(o), hT, s);
 }
 
-extern "C" int rb2_gdn_bwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
-                           const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
-                           int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, const void* d_o,
-                           const float* dhT, void* dq, void* dk_out, void* dv_out, float* dg, void* dbeta,
-                           float* dh0, void* ws, size_t ws_bytes, void* stream) {
+int gdn_bwd_impl(const void* q, const void* k, const void* v, const float* g, const void* beta, const float* h0,
+                 const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
+                 int dtype, int path, float scale, const void* d_o, const float* dhT, void* dq, void* dk_out,
+                 void* dv_out, float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* stream,
+                 int stages, int walk) {
   int rc = check_problem(B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, cu_seqlens != nullptr);
   if (rc) return rc;
   RB2_CHECK_ARG(ws != nullptr, "gdn_bwd: null workspace");
-  RB2_CHECK_ARG(B * T == 0 || (d_o && dq && dk_out && dv_out && dg && dbeta), "gdn_bwd: null gradient pointer");
+  RB2_CHECK_ARG(stages >= 1 && stages <= 3 && walk >= 0 && walk <= 1, "gdn_bwd: bad stages/walk");
+  RB2_CHECK_ARG(B * T == 0 || d_o, "gdn_bwd: null dO");
+  RB2_CHECK_ARG(B * T == 0 || !(stages & 2) || (dq && dk_out && dv_out && dg && dbeta), "gdn_bwd: null gradient pointer");
   GdnProblem p = make_problem(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dtype, path, scale);
+  p.stages = stages;
+  p.walk = walk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.path == RB2_GDN_FAST) {
     if (ws_bytes < fast_workspace_size(p.tokens, p.n_seqs, Hk, Hv, p.max_chunks)) {
@@ -133,6 +147,10 @@ extern "C" int rb2_gdn_bwd(const void* q, const void* k, const void* v, const fl
       return RB2_EWORKSPACE;
     }
     return fast_backward(p, ws, d_o, dhT, dq, dk_out, dv_out, dg, dbeta, dh0, s);
+  }
+  if (stages != 3 || walk != 0) {
+    set_error("gdn_bwd: stage/walk selection needs the tensor-core path");
+    return RB2_EUNSUPPORTED;
   }
   ExactWs w;
   if (ws_bytes < exact_ws_bytes(p, &w, ws)) {
@@ -148,4 +166,40 @@ extern "C" int rb2_gdn_bwd(const void* q, const void* k, const void* v, const fl
   return exact_backward<float>(p, w, static_cast<const float*>(d_o), dhT, static_cast<float*>(dq),
                                static_cast<float*>(dk_out), static_cast<float*>(dv_out), dg,
                                static_cast<float*>(dbeta), dh0, s);
+}
+}  // namespace
+}  // namespace rb2
+
+extern "C" int rb2_gdn_fwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                           const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                           int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, void* o,
+                           float* hT, void* ws, size_t ws_bytes, void* stream) {
+  return gdn_fwd_impl(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, scale, o, hT, ws,
+                      ws_bytes, stream, 3, 0);
+}
+
+extern "C" int rb2_gdn_fwd_ex(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                              const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                              int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, void* o,
+                              float* hT, void* ws, size_t ws_bytes, void* stream, int stages, int walk) {
+  return gdn_fwd_impl(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, scale, o, hT, ws,
+                      ws_bytes, stream, stages, walk);
+}
+
+extern "C" int rb2_gdn_bwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                           const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                           int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, const void* d_o,
+                           const float* dhT, void* dq, void* dk_out, void* dv_out, float* dg, void* dbeta,
+                           float* dh0, void* ws, size_t ws_bytes, void* stream) {
+  return gdn_bwd_impl(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, scale, d_o, dhT,
+                      dq, dk_out, dv_out, dg, dbeta, dh0, ws, ws_bytes, stream, 3, 0);
+}
+
+extern "C" int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                              const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
+                              int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, const void* d_o,
+                              const float* dhT, void* dq, void* dk_out, void* dv_out, float* dg, void* dbeta,
+                              float* dh0, void* ws, size_t ws_bytes, void* stream, int stages, int walk) {
+  return gdn_bwd_impl(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, scale, d_o, dhT,
+                      dq, dk_out, dv_out, dg, dbeta, dh0, ws, ws_bytes, stream, stages, walk);
 }

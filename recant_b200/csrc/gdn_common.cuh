@@ -16,6 +16,9 @@ struct GdnProblem {
   int dtype, path;
   float scale;
   int max_chunks;              // bound on the chunk count: tokens/64 + n_seqs
+  int stages = 3;              // fwd: 1 = chunk table + prep, 2 = state walk; bwd: 1 = walk, 2 = chunks
+  int walk = 0;                // 0 normal; 1 state only (no per-chunk outputs); 2 transition (fwd):
+                               // U = 0 and S_0 = I, so the final "state" is the segment's matrix M
 };
 
 // Chunk table built on the device from cu_seqlens (or from B, T): chunk ci covers tokens

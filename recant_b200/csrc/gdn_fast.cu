@@ -268,12 +268,14 @@ __device__ __forceinline__ FwdStage fwd_stage(unsigned char* base, int stg) {
   return st;
 }
 
-__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch) {
+__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch, int walk) {
   load_rows_sw128(st.wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
-  load_rows_sw128(st.qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
   load_rows_sw128(st.kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
-  load_rows64_sw128(st.at, ws.aqk + ch * 4096, 256);
-  load_rows_plain(st.us, ws.u + ch * 8192, 128, 256);
+  if (walk == 0) {  // outputs need q~ and A_qk
+    load_rows_sw128(st.qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
+    load_rows64_sw128(st.at, ws.aqk + ch * 4096, 256);
+  }
+  if (walk != 2) load_rows_plain(st.us, ws.u + ch * 8192, 128, 256);
   if (threadIdx.x < 16) tc::cp_async16(st.cum + 4 * threadIdx.x, ws.stats + ch * 256 + 4 * threadIdx.x, true);
   tc::cp_async_commit();
 }
@@ -298,16 +300,18 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     tc::fence_mbar_init();
   }
   const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
-  if (c0 < c1) fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h);
+  if (c0 < c1) fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h, p.walk);
   // S^T[r][dk] for dk in [64 hh, 64 hh + 64): S[dk][r] of the [dk][dv] state
   float S[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
 #pragma unroll
-  for (int j = 0; j < 64; ++j) S[j] = p.h0 ? p.h0[sbase + (64 * hh + j) * 128 + r] : 0.f;
+  for (int j = 0; j < 64; ++j)
+    S[j] = p.walk == 2 ? (64 * hh + j == r ? 1.f : 0.f) : (p.h0 ? p.h0[sbase + (64 * hh + j) * 128 + r] : 0.f);
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16);
+  const bool outs = p.walk == 0;  // per-chunk outputs (o, S, V') only in the normal walk
   uint32_t phase = 0;
   for (int ci = c0; ci < c1; ++ci) {
     const int64_t ch = int64_t(ci) * p.Hv + h;
@@ -315,7 +319,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     const int stg = (ci - c0) & 1;
     const FwdStage cur = fwd_stage(stages, stg);
     if (ci + 1 < c1) {
-      fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv);
+      fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv, p.walk);
       tc::cp_async_wait<1>();
     } else {
       tc::cp_async_wait<0>();
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       for (int j = 0; j < 8; ++j) {
         const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
         *reinterpret_cast<uint4*>(st + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
-        gdst[j] = v4;
+        if (outs) gdst[j] = v4;
       }
     }
     tc::fence_proxy_async();
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       for (int k0 = 0; k0 < 128; k0 += 16) {
         const uint32_t aoff = (k0 >> 6) * 16384 + (k0 & 63) * 2, boff = (k0 >> 6) * 8192 + (k0 & 63) * 2;
         tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(wa + boff), idesc, k0 > 0);
-        tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(qa + boff), idesc, k0 > 0);
+        if (outs) tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(qa + boff), idesc, k0 > 0);
       }
       tc::mma_commit(&bar[0]);
     }
@@ -355,11 +359,16 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       float x[32];
       tc::tmem_ld32(lane_addr + 32 * hh, x);
       uint32_t pk[16];
+      if (p.walk == 2) {  // transition: U = 0
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(cur.us[(32 * hh + j) * 128 + r]) - x[j];
+        for (int j = 0; j < 32; ++j) x[j] = -x[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(cur.us[(32 * hh + j) * 128 + r]) - x[j];
+      }
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-      store_cols32(ws.vp + ch * 8192, 128, r, 32 * hh, 64, x);
+      if (outs) store_cols32(ws.vp + ch * 8192, 128, r, 32 * hh, 64, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -376,7 +385,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
 #pragma unroll
       for (int k0 = 0; k0 < 64; k0 += 16) {
-        tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_kmajor_sw128(aa + k0 * 2), id_o, true);
+        if (outs) tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_kmajor_sw128(aa + k0 * 2), id_o, true);
         tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_mnmajor_sw128(ka + k0 * 128, 8192), id_s,
                      k0 > 0);
       }
@@ -386,8 +395,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     tc::fence_after_sync();
     {
       float x[32];
-      tc::tmem_ld32(lane_addr + 64 + 32 * hh, x);
-      store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, 32 * hh, L, x);
+      if (outs) {
+        tc::tmem_ld32(lane_addr + 64 + 32 * hh, x);
+        store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, 32 * hh, L, x);
+      }
       const float gamma = expf(cur.cum[63]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -436,15 +447,18 @@ int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_
   Carver c(wsp);
   FastWs w;
   carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks, p.group > 1);
-  int rc = launch_chunk_table(p, w.ct, s);
-  if (rc) return rc;
-  RB2_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), s), "gdn fast: clear status");
-  if (p.max_chunks > 0) {
+  int rc = RB2_OK;
+  if (p.stages & 1) {
+    if ((rc = launch_chunk_table(p, w.ct, s))) return rc;
+    RB2_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), s), "gdn fast: clear status");
+  }
+  if ((p.stages & 1) && p.max_chunks > 0) {
     if ((rc = smem_attr(fast_prep_kernel, kPrepSmem))) return rc;
     ProfScope ps_("gdn_fast_prep", s);
     fast_prep_kernel<<<dim3(p.max_chunks, p.Hv), 256, kPrepSmem, s>>>(p, w);
     RB2_CHECK_LAUNCH("gdn fast prep");
   }
+  if (!(p.stages & 2)) return RB2_OK;
   if ((rc = smem_attr(fast_state_fwd_kernel, kStateSmem))) return rc;
   {
     ProfScope ps_("gdn_fast_state_fwd", s);

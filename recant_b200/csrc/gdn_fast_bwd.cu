@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       for (int j = 0; j < 8; ++j) {
         const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
         *reinterpret_cast<uint4*>(dst + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
-        gdst[j] = v4;
+        if (p.walk == 0) gdst[j] = v4;
       }
     }
     sync_for_mma();
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-      store_cols32(ws.dvp + ch * 8192, 128, r, 32 * hh, 64, x);
+      if (p.walk == 0) store_cols32(ws.dvp + ch * 8192, 128, r, 32 * hh, 64, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(dvt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -657,14 +657,14 @@ int fast_backward(const GdnProblem& p, void* wsp, const void* d_o, const float* 
   FastWs w;
   carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks, p.group > 1);
   int rc;
-  if ((rc = smem_attr_b(fast_state_bwd_kernel, kBStateSmem))) return rc;
-  {
+  if ((p.stages & 1) && (rc = smem_attr_b(fast_state_bwd_kernel, kBStateSmem))) return rc;
+  if (p.stages & 1) {
     ProfScope ps_("gdn_fast_state_bwd", s);
     fast_state_bwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kBStateSmem, s>>>(p, w, static_cast<const bf16*>(d_o),
                                                                                     dhT, dh0);
     RB2_CHECK_LAUNCH("gdn fast state bwd");
   }
-  if (p.max_chunks > 0) {
+  if ((p.stages & 2) && p.max_chunks > 0) {
     if ((rc = smem_attr_b(fast_chunk_bwd_kernel, kBChunkSmem))) return rc;
     {
       ProfScope ps_("gdn_fast_chunk_bwd", s);

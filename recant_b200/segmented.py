@@ -1,0 +1,195 @@
+"""Segmented and context-parallel GDN: the affine state hand-off.
+
+Per chunk the state update is affine in the incoming state,
+    S_{c+1} = A_c S_c + b_c,   A_c = gamma_c I - k~_c^T W_c,   b_c = k~_c^T U_c,
+so a run of chunks (a *segment*) maps S_in to  S_out = M S_in + S0  with  M = A_n ... A_1  and
+S0 = S_out(S_in = 0). The backward is the transposed map: dS_in = M^T dS_out + dS0 with dS0 the
+initial-state gradient for dS_out = 0.
+
+Forward of one long sequence split into segments (all on the tensor-core path, chunk-aligned
+segment boundaries so the chunking equals the unsegmented op's):
+  1. per-chunk prep once (rb2_gdn_fwd_ex stage 1, segments passed as cu_seqlens);
+  2. state-only walk  -> S0 of every segment (in parallel over segments);
+  3. transition walk  -> M of every segment (U = 0, S_0 = I);
+  4. prefix over segments (and, with a process group, over ranks via all_gather of the rank's
+     composed (M_r, S0_r)) -> the true S_in of every segment;
+  5. normal walk from those S_in -> o, per-chunk states, final state.
+Backward: state-only reversed walk -> dS0; suffix over segments (and ranks, all_gather of d_r);
+normal reversed walk from the true dS_out; chunk backward.
+
+With a process group (context parallelism), each rank passes its contiguous token shard of the
+sequence; only rank 0's ``initial_state`` and the last rank's final-state gradient are used.
+The collectives per layer are one all_gather of 2 x Hv x 128 x 128 fp32 in the forward and one
+of Hv x 128 x 128 fp32 in the backward.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from .gdn import _PATHS, _stream
+
+
+def _compose(Ms, cs):
+    """(M_{n-1} ... M_0, fold of c) for segments applied in order 0..n-1."""
+    M = torch.eye(Ms.shape[-1], dtype=Ms.dtype, device=Ms.device).expand_as(Ms[0]).clone()
+    c = torch.zeros_like(cs[0])
+    for k in range(Ms.shape[0]):
+        M = Ms[k] @ M
+        c = Ms[k] @ c + cs[k]
+    return M, c
+
+
+def _prefix(Ms, cs, s0):
+    """S_in of every segment: S_in[0] = s0, S_in[k] = M[k-1] S_in[k-1] + c[k-1]."""
+    out = [s0]
+    for k in range(1, Ms.shape[0]):
+        out.append(Ms[k - 1] @ out[-1] + cs[k - 1])
+    return torch.stack(out, 0)
+
+
+def _suffix(Ms, ds, d_last):
+    """dS_out of every segment: dS_out[n-1] = d_last, dS_out[k] = M[k+1]^T dS_out[k+1] + ds[k+1]."""
+    n = Ms.shape[0]
+    out = [None] * n
+    out[n - 1] = d_last
+    for k in range(n - 2, -1, -1):
+        out[k] = Ms[k + 1].transpose(-1, -2) @ out[k + 1] + ds[k + 1]
+    return torch.stack(out, 0)
+
+
+def rank_input_state(M_all, c_all, rank, s0):
+    """Context parallelism: the state entering ``rank``'s shard, folding ranks 0..rank-1's
+    composed maps (M_all[j], c_all[j]) onto the sequence's initial state s0."""
+    s = s0
+    for j in range(rank):
+        s = M_all[j] @ s + c_all[j]
+    return s
+
+
+def rank_output_grad(M_all, d_all, rank, d_final):
+    """Context parallelism: the gradient of the state leaving ``rank``'s shard, folding ranks
+    world-1..rank+1 (dS_in = M^T dS_out + d) onto the gradient of the sequence's final state."""
+    s = d_final
+    for j in range(M_all.shape[0] - 1, rank, -1):
+        s = M_all[j].transpose(-1, -2) @ s + d_all[j]
+    return s
+
+
+class _SegmentedGDN(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, initial_state, seg_len, group, scale):
+        if q.shape[0] != 1 or q.dtype != torch.bfloat16:
+            raise ValueError("recant_b200.gdn_segmented: needs B == 1 and bfloat16 inputs (tensor-core path)")
+        if seg_len % 64:
+            raise ValueError("recant_b200.gdn_segmented: segment length must be a multiple of 64")
+        _, T, Hk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+        dev = q.device
+        q, k, v = (t.contiguous() for t in (q, k, v))
+        g = g.to(torch.float32).contiguous()
+        beta = beta.to(torch.bfloat16).contiguous()
+        bounds = list(range(0, T, seg_len)) + [T]
+        cu = torch.tensor(bounds, dtype=torch.int64, device=dev)
+        n = len(bounds) - 1
+        scale = float(dk ** -0.5 if scale is None else scale)
+        lib = L.lib()
+        path = _PATHS["fast"]
+        wsb = lib.rb2_gdn_workspace_size(1, T, n, Hk, Hv, dk, dv, L.BF16, path)
+        if wsb == 0:
+            L.check(L.EINVAL, "gdn_workspace_size")
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        common = lambda: (L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta))
+        dims = (1, T, n, Hk, Hv, dk, dv, L.BF16, path, scale)
+        st = _stream(dev)
+
+        def fwd(h0, o, hT, stages, walk):
+            L.check(lib.rb2_gdn_fwd_ex(*common(), L.ptr(h0), L.ptr(cu), *dims, L.ptr(o), L.ptr(hT), L.ptr(ws), wsb,
+                                       st, stages, walk), "gdn_fwd_ex")
+
+        S0 = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
+        Ms = torch.empty(n, Hv, dk, dk, dtype=torch.float32, device=dev)
+        fwd(None, None, S0, 1 | 2, 1)     # prep + state-only walk
+        fwd(None, None, Ms, 2, 2)         # transition walk
+        s0 = torch.zeros(Hv, dk, dv, dtype=torch.float32, device=dev)
+        world, rank = 1, 0
+        if group is not None:
+            import torch.distributed as dist
+            world, rank = dist.get_world_size(group), dist.get_rank(group)
+        if initial_state is not None and rank == 0:
+            s0 = initial_state.reshape(Hv, dk, dv).to(torch.float32)
+        M_all = None
+        if world > 1:
+            import torch.distributed as dist
+            Mr, cr = _compose(Ms, S0)
+            packed = torch.stack([Mr, cr], 0).contiguous()
+            gathered = [torch.empty_like(packed) for _ in range(world)]
+            dist.all_gather(gathered, packed, group=group)
+            M_all = torch.stack([x[0] for x in gathered], 0)
+            c_all = torch.stack([x[1] for x in gathered], 0)
+            s0 = rank_input_state(M_all, c_all, rank, s0)
+        S_in = _prefix(Ms, S0, s0).contiguous()
+        o = torch.empty(1, T, Hv, dv, dtype=torch.bfloat16, device=dev)
+        hT = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
+        fwd(S_in, o, hT, 2, 0)            # normal walk from the true segment inputs
+        final = hT[n - 1].unsqueeze(0).clone()
+        if world > 1:
+            import torch.distributed as dist
+            dist.broadcast(final, src=world - 1, group=group)
+        ctx.save_for_backward(q, k, v, g, beta, cu, S_in)
+        ctx.ws, ctx.wsb, ctx.Ms, ctx.M_all = ws, wsb, Ms, M_all
+        ctx.dims, ctx.n, ctx.group, ctx.world, ctx.rank = dims, n, group, world, rank
+        ctx.has_h0 = initial_state is not None
+        return o, final
+
+    @staticmethod
+    def backward(ctx, do, dfinal):
+        q, k, v, g, beta, cu, S_in = ctx.saved_tensors
+        ws, wsb, Ms, dims, n = ctx.ws, ctx.wsb, ctx.Ms, ctx.dims, ctx.n
+        dev = q.device
+        lib = L.lib()
+        st = _stream(dev)
+        do = do.to(torch.bfloat16).contiguous()
+        _, T, Hv, dv = do.shape
+        dk = q.shape[-1]
+        common = (L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta), L.ptr(S_in), L.ptr(cu))
+        dq, dkk, dvv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        dg = torch.empty_like(g)
+        dbeta = torch.empty_like(beta)
+        dS0 = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
+
+        def bwd(dhT, dh0, stages, walk):
+            L.check(lib.rb2_gdn_bwd_ex(*common, *dims, L.ptr(do), L.ptr(dhT), L.ptr(dq), L.ptr(dkk), L.ptr(dvv),
+                                       L.ptr(dg), L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), wsb, st, stages, walk),
+                    "gdn_bwd_ex")
+
+        bwd(None, dS0, 1, 1)              # state-only reversed walk: dS_in for dS_out = 0
+        # gradient of the whole sequence's final state: the last rank's
+        d_last = torch.zeros(Hv, dk, dv, dtype=torch.float32, device=dev)
+        if dfinal is not None:
+            d_last = dfinal.reshape(Hv, dk, dv).to(torch.float32).clone()
+        if ctx.world > 1:
+            import torch.distributed as dist
+            dist.broadcast(d_last, src=ctx.world - 1, group=ctx.group)
+            # this rank's left-boundary gradient for a zero right-boundary gradient
+            d = torch.zeros(Hv, dk, dv, dtype=torch.float32, device=dev)
+            for kk in range(n - 1, -1, -1):
+                d = Ms[kk].transpose(-1, -2) @ d + dS0[kk]
+            gathered = [torch.empty_like(d) for _ in range(ctx.world)]
+            dist.all_gather(gathered, d.contiguous(), group=ctx.group)
+            d_last = rank_output_grad(ctx.M_all, torch.stack(gathered, 0), ctx.rank, d_last)
+        dS_out = _suffix(Ms, dS0, d_last).contiguous()
+        dh0 = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
+        bwd(dS_out, dh0, 1, 0)            # normal reversed walk
+        bwd(None, None, 2, 0)             # chunk backward
+        d_init = dh0[0].unsqueeze(0) if (ctx.has_h0 and ctx.rank == 0) else None
+        return dq, dkk, dvv, dg, dbeta, d_init, None, None, None
+
+
+def gdn_segmented(q, k, v, g, beta, initial_state=None, output_final_state=False, *, segment_len=1024,
+                  group=None, scale=None):
+    """GDN over one long sequence (B == 1) in chunk-aligned segments processed in parallel, with
+    the affine hand-off; with ``group`` (a torch.distributed process group) the sequence is
+    context-parallel: every rank passes its contiguous shard. Same semantics as ``gdn_b200``."""
+    o, final = _SegmentedGDN.apply(q, k, v, g, beta, initial_state, int(segment_len), group, scale)
+    return o, (final if output_final_state else None)
