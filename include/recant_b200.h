@@ -68,6 +68,14 @@ RB2_API const char* rb2_version(void);
 RB2_API size_t rb2_gdn_workspace_size(int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
                               int dtype, int path);
 
+/* The workspace's two parts (no reference counterpart): `saved_bytes` is what the forward fills
+ * and the backward reads -- the forward needs only this much -- and `scratch_bytes` is used only
+ * inside the backward, which takes it either after the saved part of one buffer of
+ * rb2_gdn_workspace_size bytes or as a separate buffer (rb2_gdn_bwd_ex), so one scratch buffer
+ * can serve every layer of a model. Exact path: scratch 0. Returns a status code. */
+RB2_API int rb2_gdn_workspace_split(int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
+                                    int dtype, int path, size_t* saved_bytes, size_t* scratch_bytes);
+
 RB2_API int rb2_gdn_fwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
                 const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
                 int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
@@ -89,7 +97,8 @@ RB2_API int rb2_gdn_bwd(const void* q, const void* k, const void* v, const float
  * 2 (fwd): transition -- U = 0 and S_0 = I for every sequence, so hT receives each sequence's
  * state-transition matrix M with S_out = M S_in + S_out(S_in = 0), and M^T maps the gradient of
  * the final state to that of the initial state. A later stage must see the same ws and arguments
- * (except h0 / dhT) as the stage-1 call that filled ws. */
+ * (except h0 / dhT) as the stage-1 call that filled ws. bwd_ex's `scratch` (NULL = the part of ws
+ * after the saved bytes) is the backward-only part of rb2_gdn_workspace_split. */
 RB2_API int rb2_gdn_fwd_ex(const void* q, const void* k, const void* v, const float* g, const void* beta,
                            const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
                            int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
@@ -98,8 +107,8 @@ RB2_API int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const fl
                            const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
                            int Hk, int Hv, int dk, int dv, int dtype, int path, float scale,
                            const void* d_o, const float* dhT, void* dq, void* dk_out, void* dv_out,
-                           float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* stream,
-                           int stages, int walk);
+                           float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* scratch,
+                           size_t scratch_bytes, void* stream, int stages, int walk);
 
 /* ---------------------------------------------------------------------------------------------
  * NVFP4 quantizer: codes/scales/gscale of quantize(rht(x)) (use_rht=1) or quantize(x),

@@ -22,6 +22,7 @@ SIGNATURES = {
     "rb2_last_error": (C.c_char_p, []),
     "rb2_version": (C.c_char_p, []),
     "rb2_gdn_workspace_size": (_sz, [_i64, _i64, _i64, _i, _i, _i, _i, _i, _i]),
+    "rb2_gdn_workspace_split": (_i, [_i64, _i64, _i64, _i, _i, _i, _i, _i, _i, C.POINTER(_sz), C.POINTER(_sz)]),
     "rb2_gdn_fwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
                          _p, _p, _p, _sz, _p]),
     "rb2_gdn_bwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
@@ -29,7 +30,7 @@ SIGNATURES = {
     "rb2_gdn_fwd_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
                             _p, _p, _p, _sz, _p, _i, _i]),
     "rb2_gdn_bwd_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
-                            _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p, _i, _i]),
+                            _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p, _sz, _p, _i, _i]),
     "rb2_nvfp4_quantize_workspace_size": (_sz, [_i64, _i64]),
     "rb2_nvfp4_quantize": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p, _sz, _p]),
     "rb2_nvfp4_quantize_noalloc": (_i, [_p, _i64, _i64, _i, _i, _i, _u64, _p, _p, _p, _p, _p]),

@@ -22,9 +22,10 @@ int exact_backward(const GdnProblem& p, ExactWs& ws, const TIn* d_o, const float
                    TIn* dv, float* dg, TIn* dbeta, float* dh0, cudaStream_t s);
 
 int fast_forward(const GdnProblem& p, void* ws, void* o, float* hT, cudaStream_t s);
-int fast_backward(const GdnProblem& p, void* ws, const void* d_o, const float* dhT, void* dq, void* dk,
+int fast_backward(const GdnProblem& p, void* ws, void* scratch, const void* d_o, const float* dhT, void* dq, void* dk,
                   void* dv, float* dg, void* dbeta, float* dh0, cudaStream_t s);
-size_t fast_workspace_size(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int max_chunks);
+void fast_workspace_split(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int max_chunks, size_t* saved,
+                          size_t* scratch);
 
 namespace {
 
@@ -81,13 +82,40 @@ using namespace rb2;
 extern "C" const char* rb2_last_error(void) { return g_err; }
 extern "C" const char* rb2_version(void) { return "recant_b200 0.1 (sm_100a)"; }
 
+namespace rb2 {
+namespace {
+// Bytes of the workspace part the forward fills and the backward reads ("saved") and of the part
+// only the backward uses ("scratch"); the single-buffer layout is saved followed by scratch.
+void ws_split(const GdnProblem& p, size_t* saved, size_t* scratch) {
+  if (p.path == RB2_GDN_FAST) {
+    fast_workspace_split(p.tokens, p.n_seqs, p.Hk, p.Hv, p.max_chunks, saved, scratch);
+  } else {
+    *saved = exact_ws_bytes(p, nullptr, nullptr);
+    *scratch = 0;
+  }
+}
+}  // namespace
+}  // namespace rb2
+
 extern "C" size_t rb2_gdn_workspace_size(int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
                                          int dtype, int path) {
   if (check_problem(B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, n_seqs != B || B == 1)) return 0;
   GdnProblem p = make_problem(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, B, T, n_seqs, Hk,
                               Hv, dtype, path, 1.f);
-  if (p.path == RB2_GDN_FAST) return fast_workspace_size(p.tokens, n_seqs, Hk, Hv, p.max_chunks);
-  return exact_ws_bytes(p, nullptr, nullptr);
+  size_t saved, scratch;
+  ws_split(p, &saved, &scratch);
+  return saved + scratch;
+}
+
+extern "C" int rb2_gdn_workspace_split(int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
+                                       int dtype, int path, size_t* saved_bytes, size_t* scratch_bytes) {
+  int rc = check_problem(B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, n_seqs != B || B == 1);
+  if (rc) return rc;
+  RB2_CHECK_ARG(saved_bytes && scratch_bytes, "gdn_workspace_split: null output pointer");
+  GdnProblem p = make_problem(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, B, T, n_seqs, Hk,
+                              Hv, dtype, path, 1.f);
+  ws_split(p, saved_bytes, scratch_bytes);
+  return RB2_OK;
 }
 
 namespace rb2 {
@@ -106,8 +134,10 @@ int gdn_fwd_impl(const void* q, const void* k, const void* v, const float* g, co
   p.stages = stages;
   p.walk = walk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  size_t saved, scratch;
+  ws_split(p, &saved, &scratch);
   if (p.path == RB2_GDN_FAST) {
-    if (ws_bytes < fast_workspace_size(p.tokens, p.n_seqs, Hk, Hv, p.max_chunks)) {
+    if (ws_bytes < saved) {
       set_error("gdn_fwd: workspace too small");
       return RB2_EWORKSPACE;
     }
@@ -129,8 +159,8 @@ int gdn_fwd_impl(const void* q, const void* k, const void* v, const float* g, co
 int gdn_bwd_impl(const void* q, const void* k, const void* v, const float* g, const void* beta, const float* h0,
                  const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs, int Hk, int Hv, int dk, int dv,
                  int dtype, int path, float scale, const void* d_o, const float* dhT, void* dq, void* dk_out,
-                 void* dv_out, float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* stream,
-                 int stages, int walk) {
+                 void* dv_out, float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* scratch,
+                 size_t scratch_bytes, void* stream, int stages, int walk) {
   int rc = check_problem(B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, cu_seqlens != nullptr);
   if (rc) return rc;
   RB2_CHECK_ARG(ws != nullptr, "gdn_bwd: null workspace");
@@ -141,12 +171,14 @@ int gdn_bwd_impl(const void* q, const void* k, const void* v, const float* g, co
   p.stages = stages;
   p.walk = walk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  size_t saved, need_scratch;
+  ws_split(p, &saved, &need_scratch);
   if (p.path == RB2_GDN_FAST) {
-    if (ws_bytes < fast_workspace_size(p.tokens, p.n_seqs, Hk, Hv, p.max_chunks)) {
+    if (scratch ? (ws_bytes < saved || scratch_bytes < need_scratch) : ws_bytes < saved + need_scratch) {
       set_error("gdn_bwd: workspace too small");
       return RB2_EWORKSPACE;
     }
-    return fast_backward(p, ws, d_o, dhT, dq, dk_out, dv_out, dg, dbeta, dh0, s);
+    return fast_backward(p, ws, scratch, d_o, dhT, dq, dk_out, dv_out, dg, dbeta, dh0, s);
   }
   if (stages != 3 || walk != 0) {
     set_error("gdn_bwd: stage/walk selection needs the tensor-core path");
@@ -192,14 +224,16 @@ extern "C" int rb2_gdn_bwd(const void* q, const void* k, const void* v, const fl
                            const float* dhT, void* dq, void* dk_out, void* dv_out, float* dg, void* dbeta,
                            float* dh0, void* ws, size_t ws_bytes, void* stream) {
   return gdn_bwd_impl(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, scale, d_o, dhT,
-                      dq, dk_out, dv_out, dg, dbeta, dh0, ws, ws_bytes, stream, 3, 0);
+                      dq, dk_out, dv_out, dg, dbeta, dh0, ws, ws_bytes, nullptr, 0, stream, 3, 0);
 }
 
 extern "C" int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const float* g, const void* beta,
                               const float* h0, const int64_t* cu_seqlens, int64_t B, int64_t T, int64_t n_seqs,
                               int Hk, int Hv, int dk, int dv, int dtype, int path, float scale, const void* d_o,
                               const float* dhT, void* dq, void* dk_out, void* dv_out, float* dg, void* dbeta,
-                              float* dh0, void* ws, size_t ws_bytes, void* stream, int stages, int walk) {
+                              float* dh0, void* ws, size_t ws_bytes, void* scratch, size_t scratch_bytes,
+                              void* stream, int stages, int walk) {
   return gdn_bwd_impl(q, k, v, g, beta, h0, cu_seqlens, B, T, n_seqs, Hk, Hv, dk, dv, dtype, path, scale, d_o, dhT,
-                      dq, dk_out, dv_out, dg, dbeta, dh0, ws, ws_bytes, stream, stages, walk);
+                      dq, dk_out, dv_out, dg, dbeta, dh0, ws, ws_bytes, scratch, scratch_bytes, stream,
+                      stages, walk);
 }

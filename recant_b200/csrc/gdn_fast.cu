@@ -21,7 +21,7 @@
 
 namespace rb2 {
 
-size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks, bool gqa) {
+size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_chunks) {
   const size_t nch = size_t(max_chunks) * Hv;
   w.ct.tok0 = c.take<int>(max_chunks);
   w.ct.len = c.take<int>(max_chunks);
@@ -30,7 +30,7 @@ size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, 
   w.ct.n_chunks = c.take<int>(1);
   w.err = c.take<int>(1);
   w.stats = c.take<float>(nch * 256);
-  w.tinv = c.take<float>(nch * 4096);
+  w.tinv = c.take<__nv_bfloat16>(nch * 4096);
   w.aqk = c.take<__nv_bfloat16>(nch * 4096);
   w.w = c.take<__nv_bfloat16>(nch * 8192);
   w.u = c.take<__nv_bfloat16>(nch * 8192);
@@ -38,6 +38,11 @@ size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, 
   w.kt = c.take<__nv_bfloat16>(nch * 8192);
   w.hs = c.take<__nv_bfloat16>(nch * 16384);
   w.vp = c.take<__nv_bfloat16>(nch * 8192);
+  return c.bytes();
+}
+
+size_t carve_fast_scratch(Carver& c, FastWs& w, int64_t tokens, int Hv, int max_chunks, bool gqa) {
+  const size_t nch = size_t(max_chunks) * Hv;
   w.dh = c.take<__nv_bfloat16>(nch * 16384);
   w.dvp = c.take<__nv_bfloat16>(nch * 8192);
   w.dqh = c.take<float>(gqa ? size_t(tokens) * Hv * 128 : 0);
@@ -175,11 +180,13 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   tc::fence_before_sync();
   __syncthreads();
   unit_lower_inverse(lm, tm, xbuf, 256);
-  // T to the workspace (fp32, for the backward) and the two bf16 B operands
-  for (int idx = tid; idx < 1024; idx += 256) {
-    const int i = idx >> 4, c4 = (idx & 15) * 4;
-    *reinterpret_cast<float4*>(ws.tinv + ch * 4096 + i * 64 + c4) =
-        make_float4(tm[i * 65 + c4], tm[i * 65 + c4 + 1], tm[i * 65 + c4 + 2], tm[i * 65 + c4 + 3]);
+  // T to the workspace (bf16 rows, the backward's MMA operand) and the two bf16 B operands
+  for (int idx = tid; idx < 512; idx += 256) {
+    const int i = idx >> 3, c8 = (idx & 7) * 8;
+    const float* t = tm + i * 65 + c8;
+    *reinterpret_cast<uint4*>(ws.tinv + ch * 4096 + i * 64 + c8) =
+        make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
+                   tc::pack_bf16(t[6], t[7]));
   }
   {
     const int i = tid & 63, which = (tid >> 6) & 1, m0 = 32 * (tid >> 7);
@@ -432,10 +439,12 @@ int smem_attr(K kernel, int bytes) {
 
 }  // namespace
 
-size_t fast_workspace_size(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int max_chunks) {
-  Carver c(nullptr);
+void fast_workspace_split(int64_t tokens, int64_t n_seqs, int Hk, int Hv, int max_chunks, size_t* saved,
+                          size_t* scratch) {
   FastWs w;
-  return carve_fast(c, w, tokens, n_seqs, Hv, max_chunks, Hk != Hv);
+  Carver a(nullptr), b(nullptr);
+  *saved = carve_fast_saved(a, w, n_seqs, Hv, max_chunks);
+  *scratch = carve_fast_scratch(b, w, tokens, Hv, max_chunks, Hk != Hv);
 }
 
 static int check_err_word(const FastWs& w, cudaStream_t s, bool sync) {
@@ -446,7 +455,7 @@ static int check_err_word(const FastWs& w, cudaStream_t s, bool sync) {
 int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_t s) {
   Carver c(wsp);
   FastWs w;
-  carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks, p.group > 1);
+  carve_fast_saved(c, w, p.n_seqs, p.Hv, p.max_chunks);
   int rc = RB2_OK;
   if (p.stages & 1) {
     if ((rc = launch_chunk_table(p, w.ct, s))) return rc;

@@ -9,7 +9,7 @@ namespace rb2 {
 struct FastWs {
   ChunkTable ct;
   float* stats;          // [ch][4][64] cum, rq, rk, beta
-  float* tinv;           // [ch][64][64]
+  __nv_bfloat16* tinv;   // [ch][64][64]   T = (I + L)^-1
   __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal
   __nv_bfloat16* w;      // [ch][64][128]
   __nv_bfloat16* u;      // [ch][64][128]
@@ -24,7 +24,11 @@ struct FastWs {
   int* err;              // device status word
 };
 
-size_t carve_fast(Carver& c, FastWs& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks, bool gqa);
+// The workspace has two parts: "saved" (written by the forward, read by the backward: chunk table,
+// status word, per-chunk prep outputs, states and V') and "scratch" (backward only: dS, dV' and the
+// per-value-head dq / dk of GQA), which the caller may pass separately and reuse across layers.
+size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_chunks);
+size_t carve_fast_scratch(Carver& c, FastWs& w, int64_t tokens, int Hv, int max_chunks, bool gqa);
 
 namespace fast {
 

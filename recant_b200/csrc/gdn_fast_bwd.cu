@@ -332,6 +332,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   tc::mbar_wait(&bar[0], 0, ws.err, 131);
   tc::fence_after_sync();
+  load_rows64_sw128(sm + lay::TT, ws.tinv + ch * 4096, 256);  // T (bf16) over dS^T, consumed by G1
+  tc::cp_async_commit();
   // ---- E1 ------------------------------------------------------------------------------------
   {
     float v[32];
@@ -362,13 +364,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     *reinterpret_cast<uint4*>(sm + lay::BV + tc::sw128_offset(m, c8, 64)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
     *reinterpret_cast<uint4*>(sm + lay::BK + tc::sw128_offset(m, c8, 64)) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
   }
-  for (int idx = tid; idx < 64 * 8; idx += 256) {  // T (bf16) rows i
-    const int i = idx >> 3, c8 = (idx & 7) * 8;
-    const float4 a = *reinterpret_cast<const float4*>(ws.tinv + ch * 4096 + i * 64 + c8);
-    const float4 b = *reinterpret_cast<const float4*>(ws.tinv + ch * 4096 + i * 64 + c8 + 4);
-    *reinterpret_cast<uint4*>(sm + lay::TT + tc::sw128_offset(i, c8, 64)) =
-        make_uint4(tc::pack_bf16(a.x, a.y), tc::pack_bf16(a.z, a.w), tc::pack_bf16(b.x, b.y), tc::pack_bf16(b.z, b.w));
-  }
+  tc::cp_async_wait<0>();
   sync_for_mma();
   const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
   if (tid == 0) {  // ---- G2 ----
@@ -651,11 +647,13 @@ int smem_attr_b(K kernel, int bytes) {
 
 }  // namespace
 
-int fast_backward(const GdnProblem& p, void* wsp, const void* d_o, const float* dhT, void* dq, void* dk, void* dv,
-                  float* dg, void* dbeta, float* dh0, cudaStream_t s) {
+int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o, const float* dhT, void* dq, void* dk,
+                  void* dv, float* dg, void* dbeta, float* dh0, cudaStream_t s) {
   Carver c(wsp);
   FastWs w;
-  carve_fast(c, w, p.tokens, p.n_seqs, p.Hv, p.max_chunks, p.group > 1);
+  const size_t saved = carve_fast_saved(c, w, p.n_seqs, p.Hv, p.max_chunks);
+  Carver c2(scratch ? scratch : static_cast<char*>(wsp) + saved);
+  carve_fast_scratch(c2, w, p.tokens, p.Hv, p.max_chunks, p.group > 1);
   int rc;
   if ((p.stages & 1) && (rc = smem_attr_b(fast_state_bwd_kernel, kBStateSmem))) return rc;
   if (p.stages & 1) {

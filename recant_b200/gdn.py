@@ -15,6 +15,8 @@ Drop-in for ``recant.model.ops``'s GDN backends (recant/model/ops.py:5-10,56-67)
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import _lib as L
@@ -52,9 +54,12 @@ class _Problem:
             raise ValueError(f"recant_b200.gdn: initial_state must be [{self.n_seqs},{Hv},{dk},{dv}]")
         self.scale = float(dk ** -0.5 if scale is None else scale)
         self.path = _PATHS[path]
-        self.ws_bytes = L.lib().rb2_gdn_workspace_size(B, T, self.n_seqs, Hk, Hv, dk, dv, _DT[q.dtype], self.path)
-        if self.ws_bytes == 0:
-            L.check(L.EINVAL if dk == dv == 128 else L.EUNSUPPORTED, "gdn_workspace_size")
+        saved, scratch = C.c_size_t(0), C.c_size_t(0)
+        L.check(L.lib().rb2_gdn_workspace_split(B, T, self.n_seqs, Hk, Hv, dk, dv, _DT[q.dtype], self.path,
+                                                C.byref(saved), C.byref(scratch)), "gdn_workspace_split")
+        # the forward keeps only the saved part alive until the backward; the backward-only
+        # scratch is allocated inside the backward (the caching allocator recycles it)
+        self.ws_bytes, self.scratch_bytes = saved.value, scratch.value
 
     def args(self):
         return (self.B, self.T, self.n_seqs, self.Hk, self.Hv, self.dk, self.dv, _DT[self.dtype], self.path,
@@ -93,9 +98,11 @@ class _GDNFunction(torch.autograd.Function):
         dg = torch.empty_like(g)
         dbeta = torch.empty_like(beta)
         dh0 = torch.empty_like(h0) if ctx.has_h0 and ctx.needs_input_grad[5] else None
-        st = L.lib().rb2_gdn_bwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta), L.ptr(h0), L.ptr(cu),
-                                 *pb.args(), L.ptr(do), L.ptr(dhT), L.ptr(dq), L.ptr(dk), L.ptr(dv), L.ptr(dg),
-                                 L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), pb.ws_bytes, _stream(q.device))
+        scratch = torch.empty(max(pb.scratch_bytes, 1), dtype=torch.uint8, device=q.device)
+        st = L.lib().rb2_gdn_bwd_ex(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta), L.ptr(h0), L.ptr(cu),
+                                    *pb.args(), L.ptr(do), L.ptr(dhT), L.ptr(dq), L.ptr(dk), L.ptr(dv), L.ptr(dg),
+                                    L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), pb.ws_bytes, L.ptr(scratch),
+                                    pb.scratch_bytes, _stream(q.device), 3, 0)
         L.check(st, "gdn_bwd")
         return dq, dk, dv, dg, dbeta.to(ctx.beta_dtype), dh0, None, None, None, None
 

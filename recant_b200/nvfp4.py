@@ -121,7 +121,7 @@ class FP4Linear(torch.autograd.Function):
         ctx.w = w
         x2 = x.reshape(-1, w.in_features)
         a = quantize_activation(x2, w.use_rht)
-        y = gemm_fp4(a, w.fprop)
+        y = _gemm_to(a, w.fprop, x.dtype)
         return y.reshape(*x.shape[:-1], w.out_features).to(x.dtype)
 
     @staticmethod
@@ -129,8 +129,17 @@ class FP4Linear(torch.autograd.Function):
         w = ctx.w
         d2 = dy.reshape(-1, w.out_features)
         d = quantize_activation(d2, w.use_rht, stochastic=True)
-        dx = gemm_fp4(d, w.dgrad)
+        dx = _gemm_to(d, w.dgrad, dy.dtype)
         return dx.reshape(*dy.shape[:-1], w.in_features).to(dy.dtype), None
+
+
+def _gemm_to(a, b, dtype):
+    """The selected GEMM backend; with this package's own backend and a bf16 activation the
+    epilogue writes bf16 directly (one rounding of acc * gA * gB) instead of fp32 then a cast."""
+    if _state["gemm"] == "b200" and dtype == torch.bfloat16:
+        with torch.profiler.record_function("b:fp4_gemm"):
+            return gemm_b200(a, b, out_dtype=torch.bfloat16)
+    return gemm_fp4(a, b)
 
 
 def fp4_linear(x: torch.Tensor, w: FP4Weight) -> torch.Tensor:

@@ -24,6 +24,8 @@ of Hv x 128 x 128 fp32 in the backward.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import _lib as L
@@ -95,9 +97,10 @@ class _SegmentedGDN(torch.autograd.Function):
         scale = float(dk ** -0.5 if scale is None else scale)
         lib = L.lib()
         path = _PATHS["fast"]
-        wsb = lib.rb2_gdn_workspace_size(1, T, n, Hk, Hv, dk, dv, L.BF16, path)
-        if wsb == 0:
-            L.check(L.EINVAL, "gdn_workspace_size")
+        saved, scratch = C.c_size_t(0), C.c_size_t(0)
+        L.check(lib.rb2_gdn_workspace_split(1, T, n, Hk, Hv, dk, dv, L.BF16, path, C.byref(saved), C.byref(scratch)),
+                "gdn_workspace_split")
+        wsb = saved.value
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
         common = lambda: (L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta))
         dims = (1, T, n, Hk, Hv, dk, dv, L.BF16, path, scale)
@@ -137,7 +140,7 @@ class _SegmentedGDN(torch.autograd.Function):
             import torch.distributed as dist
             dist.broadcast(final, src=world - 1, group=group)
         ctx.save_for_backward(q, k, v, g, beta, cu, S_in)
-        ctx.ws, ctx.wsb, ctx.Ms, ctx.M_all = ws, wsb, Ms, M_all
+        ctx.ws, ctx.wsb, ctx.scratch_bytes, ctx.Ms, ctx.M_all = ws, wsb, scratch.value, Ms, M_all
         ctx.dims, ctx.n, ctx.group, ctx.world, ctx.rank = dims, n, group, world, rank
         ctx.has_h0 = initial_state is not None
         return o, final
@@ -157,11 +160,12 @@ class _SegmentedGDN(torch.autograd.Function):
         dg = torch.empty_like(g)
         dbeta = torch.empty_like(beta)
         dS0 = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
+        scratch = torch.empty(max(ctx.scratch_bytes, 1), dtype=torch.uint8, device=dev)
 
         def bwd(dhT, dh0, stages, walk):
             L.check(lib.rb2_gdn_bwd_ex(*common, *dims, L.ptr(do), L.ptr(dhT), L.ptr(dq), L.ptr(dkk), L.ptr(dvv),
-                                       L.ptr(dg), L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), wsb, st, stages, walk),
-                    "gdn_bwd_ex")
+                                       L.ptr(dg), L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), wsb, L.ptr(scratch),
+                                       ctx.scratch_bytes, st, stages, walk), "gdn_bwd_ex")
 
         bwd(None, dS0, 1, 1)              # state-only reversed walk: dS_in for dS_out = 0
         # gradient of the whole sequence's final state: the last rank's

@@ -39,6 +39,26 @@ def test_gdn_workspace_size_scales_with_problem():
     assert lib.rb2_gdn_workspace_size(1, 5000, 7, 16, 32, 128, 128, L.F32, L.GDN_EXACT) > 0
 
 
+@pytest.mark.parametrize("Hk,Hv,path", [(16, 32, L.GDN_FAST), (32, 32, L.GDN_FAST), (4, 8, L.GDN_EXACT)])
+def test_gdn_workspace_split_sums_to_total(Hk, Hv, path):
+    lib = L.lib()
+    dt = L.BF16 if path == L.GDN_FAST else L.F32
+    total = lib.rb2_gdn_workspace_size(4, 4096, 4, Hk, Hv, 128, 128, dt, path)
+    saved, scratch = C.c_size_t(0), C.c_size_t(0)
+    assert lib.rb2_gdn_workspace_split(4, 4096, 4, Hk, Hv, 128, 128, dt, path, C.byref(saved),
+                                       C.byref(scratch)) == L.OK
+    assert saved.value + scratch.value == total and saved.value > 0
+    if path == L.GDN_FAST:
+        # scratch holds dS (32 KB) and dV' (16 KB) per (chunk, head) for the chunk bound
+        # tokens / 64 + n_seqs, plus fp32 dq/dk per value head for GQA
+        per_ch = (4 * 4096 // 64 + 4) * Hv * (32768 + 16384)
+        gqa = 2 * 4 * 4096 * Hv * 128 * 4 if Hk != Hv else 0
+        assert per_ch + gqa <= scratch.value <= per_ch + gqa + 4096
+    else:
+        assert scratch.value == 0
+    assert lib.rb2_gdn_workspace_split(4, 4096, 4, Hk, Hv, 128, 128, dt, path, None, None) == L.EINVAL
+
+
 @pytest.mark.parametrize("dk", [16, 64, 256])
 def test_gdn_rejects_unsupported_head_dim(dk):
     lib = L.lib()
