@@ -195,6 +195,186 @@ def reference_arm(args, rank, world):
     return 0
 
 
+METRIC4 = "GDN stack fwd+bwd sequence tokens/s (8 GDN layers + NVFP4 out_proj, B1 T131072, context-parallel)"
+C4 = dict(T=131072, layers=8, Hk=16, Hv=32, d=128, hidden=4096, segments_per_rank=4)
+# NVFP4 GEMM roofline: 4x the measured dense bf16 rate (the tcgen05 FP4 : bf16 dense ratio)
+FP4_PER_BF16 = 4.0
+
+
+def _timed(step, steps, stream, world, dev):
+    """Device time per step (CUDA events on `stream`), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_config4(args, rank, world, local, dev):
+    """Config 4: 8 stacked layers, each a chunked GDN whose values are the previous layer's output
+    (v = x viewed as [1, T, Hv, d]) followed by an NVFP4 4096x4096 out_proj, on one sequence of
+    131072 tokens split into contiguous shards of T / N tokens (context parallelism). Per layer and
+    rank the GDN runs as segmented walks with the affine state hand-off (segments_per_rank
+    segments per shard); the ranks exchange their composed state maps with one all_gather in the
+    forward and one in the backward. A step is the forward of all layers plus the backward from a
+    synthetic upstream gradient, computing dq, dk, dv, dg, dbeta of every layer and dx of the input."""
+    import torch
+    import torch.distributed as dist
+
+    from recant_b200 import _lib as L
+    from recant_b200 import gdn_segmented
+    from recant_b200 import nvfp4 as N
+
+    c = C4
+    T, Hk, Hv, d, layers = c["T"], c["Hk"], c["Hv"], c["d"], c["layers"]
+    if T % (64 * world):
+        raise SystemExit(f"config 4: T={T} does not split into {world} chunk-aligned shards")
+    Tr = T // world
+    seg = max(64, (Tr // c["segments_per_rank"]) // 64 * 64)
+    group = dist.group.WORLD if world > 1 else None
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+    bf = torch.bfloat16
+    per_layer = []
+    for _ in range(layers):
+        q = torch.randn(1, Tr, Hk, d, device=dev, generator=gen).to(bf)
+        k = torch.randn(1, Tr, Hk, d, device=dev, generator=gen).to(bf)
+        beta = torch.sigmoid(torch.randn(1, Tr, Hv, device=dev, generator=gen)).to(bf)
+        a_log = torch.log(torch.empty(Hv, device=dev).uniform_(1.0, 16.0, generator=gen))
+        g = (-a_log.exp() * torch.nn.functional.softplus(torch.randn(1, Tr, Hv, device=dev, generator=gen))).float()
+        w = torch.randn(c["hidden"], c["hidden"], device=dev, generator=gen) * 0.02
+        per_layer.append(dict(q=q, k=k, g=g, beta=beta, W=N.quantize_weight(w)))
+        del w
+    x0 = torch.randn(1, Tr, c["hidden"], device=dev, generator=gen).to(bf)
+    dy = torch.randn(1, Tr, c["hidden"], device=dev, generator=gen).to(bf)
+
+    def forward_backward(x_in, layer_inputs, d_out):
+        x = x_in
+        for lp in layer_inputs:
+            o, _ = gdn_segmented(lp["q"], lp["k"], x.view(1, Tr, Hv, d), lp["g"], lp["beta"], segment_len=seg,
+                                 group=group)
+            x = N.fp4_linear(o.view(1, Tr, c["hidden"]), lp["W"])
+        x.backward(d_out)
+        return x
+
+    leaves = [{n: lp[n].clone().requires_grad_(True) for n in ("q", "k", "g", "beta")} for lp in per_layer]
+    for lv, lp in zip(leaves, per_layer):
+        lv["W"] = lp["W"]
+    x_leaf = x0.clone().requires_grad_(True)
+
+    def clear_grads():
+        x_leaf.grad = None
+        for lv in leaves:
+            for n in ("q", "k", "g", "beta"):
+                lv[n].grad = None
+
+    def step():
+        clear_grads()
+        forward_backward(x_leaf, leaves, dy)
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(local)
+    clocks.start()
+    prof = L.LaunchProfiler(capacity=256 * layers * (args.steps + 1))
+    prof.start()
+    ms = _timed(step, args.steps, stream, world, dev)
+    records, dropped = prof.read()
+    clock_info = clocks.stop()
+    value = T / (ms / 1e3)
+    clear_grads()
+
+    # ---- end to end: every step copies its inputs from pinned host memory and reads back the
+    # stack's output and the input gradient
+    host = [{n: lp[n].cpu().pin_memory() for n in ("q", "k", "g", "beta")} for lp in per_layer]
+    hx, hdy = x0.cpu().pin_memory(), dy.cpu().pin_memory()
+    out_host = torch.empty(1, Tr, c["hidden"], dtype=bf).pin_memory()
+    dx_host = torch.empty(1, Tr, c["hidden"], dtype=bf).pin_memory()
+    h2d = hx.numel() * 2 + hdy.numel() * 2 + sum(t.numel() * t.element_size() for hl in host for t in hl.values())
+    d2h = out_host.numel() * 2 + dx_host.numel() * 2
+
+    def e2e_step():
+        lin = []
+        for hl, lp in zip(host, per_layer):
+            e = {n: t.to(dev, non_blocking=True).requires_grad_(True) for n, t in hl.items()}
+            e["W"] = lp["W"]
+            lin.append(e)
+        xl = hx.to(dev, non_blocking=True).requires_grad_(True)
+        out = forward_backward(xl, lin, hdy.to(dev, non_blocking=True))
+        out_host.copy_(out.detach(), non_blocking=True)
+        dx_host.copy_(xl.grad, non_blocking=True)
+
+    e2e_step()
+    e2e_steps = max(2, args.steps // 2)
+    ms_e2e = _timed(e2e_step, e2e_steps, stream, world, dev)
+
+    pk = peaks()
+    per_kernel = {}
+    for name, t in records:
+        a = per_kernel.setdefault(name, [0, 0.0])
+        a[0] += 1
+        a[1] += t
+    total_k = sum(v[1] for v in per_kernel.values()) or 1.0
+    kernels = {n: {"launches": v[0], "ms_total": round(v[1], 3), "share": round(v[1] / total_k, 3)}
+               for n, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][1])}
+    top = max(per_kernel, key=lambda n: per_kernel[n][1]) if per_kernel else None
+    n_ch = (Tr // 64) * Hv                 # chunk-heads per GDN launch on this rank
+    roof = None
+    if top is not None:
+        launches, tot = per_kernel[top]
+        avg_s = tot / launches / 1e3
+        if top == "nvfp4_gemm":
+            flops, peak = 2.0 * Tr * c["hidden"] * c["hidden"], pk["bf16"] * FP4_PER_BF16
+        else:
+            flops, peak = KERNEL_FLOPS_PER_CH.get(top, 0) * n_ch, pk["bf16"]
+        achieved = flops / avg_s / 1e12
+        roof = {"kernel": top, "bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "peak_source": f"{pk['source']} bf16 burst (MEASURED_PEAKS.json)" +
+                               (" x4 for FP4" if top == "nvfp4_gemm" else ""),
+                "share_of_kernel_time": round(tot / total_k, 3), "avg_launch_ms": round(avg_s * 1e3, 4)}
+    f_gdn = layers * FLOP_PER_TOKEN_HEAD * T * Hv
+    f_gemm = layers * 2 * (2.0 * T * c["hidden"] * c["hidden"])   # fprop + dgrad
+    t_roof = f_gdn / (pk["bf16"] * 1e12) + f_gemm / (pk["bf16"] * FP4_PER_BF16 * 1e12)
+    line = {
+        "metric": METRIC4, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config4: 8 x (GDN Hk16 Hv32 d128 chunk64 + NVFP4 4096x4096 out_proj) fwd+bwd "
+                               "on one sequence, B1 T131072, context-parallel in contiguous shards",
+                   "seq_len": T, "layers": layers, "tokens_this_rank": Tr, "segment_len": seg,
+                   "parallelism": f"cp{world}", "layer_tokens_per_s": round(value * layers, 1),
+                   "l2": "per-rank inputs exceed the 126 MB L2; no flush"},
+        "e2e": {"value": round(T / (ms_e2e / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": roof,
+        "path_roofline": {"flops_gdn": f_gdn, "flops_fp4_gemm": f_gemm, "t_roof_ms": round(t_roof * 1e3 / world, 3),
+                          "frac": round(t_roof * 1e3 / world / ms, 4),
+                          "definition": "(GDN F / bf16 burst peak + GEMM F / (4 x bf16 peak)) / N / step time"},
+        "gpu_launches": len(records) + dropped,
+        "kernels": kernels,
+        "clocks": clock_info,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -203,8 +383,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[1, 3], default=1,
-                    help="1: B4 T4096 replicas (the headline); 3: packed varlen, data-parallel by tokens")
+    ap.add_argument("--config", type=int, choices=[1, 3, 4], default=1,
+                    help="1: B4 T4096 replicas (the headline); 3: packed varlen, data-parallel by tokens; "
+                         "4: 8-layer GDN + NVFP4 out_proj stack on one T=131072 sequence, context-parallel")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -225,6 +406,8 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    if args.config == 4:
+        return run_config4(args, rank, world, local, dev)
     c = CFG
     B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
     cu = None

@@ -110,6 +110,16 @@ RB2_API int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const fl
                            float* dg, void* dbeta, float* dh0, void* ws, size_t ws_bytes, void* scratch,
                            size_t scratch_bytes, void* stream, int stages, int walk);
 
+/* Affine state fold of segmented / context-parallel GDN (no reference counterpart: the reference
+ * walks one sequence's chunks in order, ops.py:49-52; a run of chunks maps S_out = M S_in + c and
+ * dS_in = M^T dS_out + d). M, c: [n, H, d, d] fp32 (c NULL = 0); s0: [H, d, d] (NULL = zero, or
+ * the identity when identity_init). transpose = 0: x_0 = s0, x_{k+1} = M_k x_k + c_k; transpose
+ * = 1: from k = n-1 down to 0, x <- M_k^T x + c_k. states (optional, [n, H, d, d]) receives the
+ * value entering every map, final_out (optional, [H, d, d]) the value after the last. d = 128;
+ * pointers 16-byte aligned; n may be 0 (final_out = s0). */
+RB2_API int rb2_gdn_state_fold(const float* M, const float* c, const float* s0, int64_t n, int H, int d,
+                               int transpose, int identity_init, float* states, float* final_out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * NVFP4 quantizer: codes/scales/gscale of quantize(rht(x)) (use_rht=1) or quantize(x),
  * bit-exact with recant/model/nvfp4.py:23-31,59-91 for round-to-nearest; stochastic=1 is the

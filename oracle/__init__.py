@@ -9,6 +9,8 @@ reference RECANT package that the B200 kernels replace:
 * ``oracle.nvfp4``  -- randomized-Hadamard + NVFP4 quantizer, the 128x4 blocked
                       scale swizzle, dequantisation and the emulated GEMM
                       (recant/model/nvfp4.py:6-124), in numpy, bit-exact.
+* ``oracle.segments`` -- the affine state folds (prefix / suffix / composition) of the
+                      segmented and context-parallel op, as plain torch loops;
 * ``oracle.inputs`` -- the seeded synthetic inputs of the benchmark configs.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and

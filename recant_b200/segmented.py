@@ -12,7 +12,8 @@ segment boundaries so the chunking equals the unsegmented op's):
   2. state-only walk  -> S0 of every segment (in parallel over segments);
   3. transition walk  -> M of every segment (U = 0, S_0 = I);
   4. prefix over segments (and, with a process group, over ranks via all_gather of the rank's
-     composed (M_r, S0_r)) -> the true S_in of every segment;
+     composed (M_r, S0_r)) -> the true S_in of every segment; every fold is one launch of the
+     fold kernel (rb2_gdn_state_fold);
   5. normal walk from those S_in -> o, per-chunk states, final state.
 Backward: state-only reversed walk -> dS0; suffix over segments (and ranks, all_gather of d_r);
 normal reversed walk from the true dS_out; chunk backward.
@@ -32,50 +33,18 @@ from . import _lib as L
 from .gdn import _PATHS, _stream
 
 
-def _compose(Ms, cs):
-    """(M_{n-1} ... M_0, fold of c) for segments applied in order 0..n-1."""
-    M = torch.eye(Ms.shape[-1], dtype=Ms.dtype, device=Ms.device).expand_as(Ms[0]).clone()
-    c = torch.zeros_like(cs[0])
-    for k in range(Ms.shape[0]):
-        M = Ms[k] @ M
-        c = Ms[k] @ c + cs[k]
-    return M, c
-
-
-def _prefix(Ms, cs, s0):
-    """S_in of every segment: S_in[0] = s0, S_in[k] = M[k-1] S_in[k-1] + c[k-1]."""
-    out = [s0]
-    for k in range(1, Ms.shape[0]):
-        out.append(Ms[k - 1] @ out[-1] + cs[k - 1])
-    return torch.stack(out, 0)
-
-
-def _suffix(Ms, ds, d_last):
-    """dS_out of every segment: dS_out[n-1] = d_last, dS_out[k] = M[k+1]^T dS_out[k+1] + ds[k+1]."""
-    n = Ms.shape[0]
-    out = [None] * n
-    out[n - 1] = d_last
-    for k in range(n - 2, -1, -1):
-        out[k] = Ms[k + 1].transpose(-1, -2) @ out[k + 1] + ds[k + 1]
-    return torch.stack(out, 0)
-
-
-def rank_input_state(M_all, c_all, rank, s0):
-    """Context parallelism: the state entering ``rank``'s shard, folding ranks 0..rank-1's
-    composed maps (M_all[j], c_all[j]) onto the sequence's initial state s0."""
-    s = s0
-    for j in range(rank):
-        s = M_all[j] @ s + c_all[j]
-    return s
-
-
-def rank_output_grad(M_all, d_all, rank, d_final):
-    """Context parallelism: the gradient of the state leaving ``rank``'s shard, folding ranks
-    world-1..rank+1 (dS_in = M^T dS_out + d) onto the gradient of the sequence's final state."""
-    s = d_final
-    for j in range(M_all.shape[0] - 1, rank, -1):
-        s = M_all[j].transpose(-1, -2) @ s + d_all[j]
-    return s
+def state_fold(M, c=None, s0=None, *, transpose=False, identity=False, states=True):
+    """Fold the affine maps M [n, H, 128, 128] (offsets c, same shape, None = 0) from the start
+    value s0 [H, 128, 128] (None = zero, or the identity with ``identity``) on the GPU.
+    Forward: x_0 = s0, x_{k+1} = M_k x_k + c_k; transposed: from k = n-1 down, x = M_k^T x + c_k.
+    Returns (values entering every map [n, H, 128, 128] or None, value after the last map)."""
+    n, H = int(M.shape[0]), int(M.shape[1])
+    dev = M.device
+    out_states = torch.empty_like(M) if states else None
+    out_final = torch.empty(H, 128, 128, dtype=torch.float32, device=dev)
+    L.check(L.lib().rb2_gdn_state_fold(L.ptr(M), L.ptr(c), L.ptr(s0), n, H, 128, int(transpose), int(identity),
+                                       L.ptr(out_states), L.ptr(out_final), _stream(dev)), "gdn_state_fold")
+    return out_states, out_final
 
 
 class _SegmentedGDN(torch.autograd.Function):
@@ -124,14 +93,15 @@ class _SegmentedGDN(torch.autograd.Function):
         M_all = None
         if world > 1:
             import torch.distributed as dist
-            Mr, cr = _compose(Ms, S0)
-            packed = torch.stack([Mr, cr], 0).contiguous()
-            gathered = [torch.empty_like(packed) for _ in range(world)]
-            dist.all_gather(gathered, packed, group=group)
-            M_all = torch.stack([x[0] for x in gathered], 0)
-            c_all = torch.stack([x[1] for x in gathered], 0)
-            s0 = rank_input_state(M_all, c_all, rank, s0)
-        S_in = _prefix(Ms, S0, s0).contiguous()
+            packed = torch.empty(2, Hv, dk, dk, dtype=torch.float32, device=dev)
+            _, packed[0] = state_fold(Ms, identity=True, states=False)      # M_r = M_{n-1} ... M_0
+            _, packed[1] = state_fold(Ms, S0, states=False)                 # c_r = S_out(S_in = 0)
+            gathered = torch.empty(world, 2, Hv, dk, dk, dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(gathered, packed, group=group)
+            M_all = gathered[:, 0].contiguous()
+            c_all = gathered[:, 1].contiguous()
+            _, s0 = state_fold(M_all[:rank], c_all[:rank], s0.contiguous(), states=False)
+        S_in, _ = state_fold(Ms, S0, s0.contiguous())
         o = torch.empty(1, T, Hv, dv, dtype=torch.bfloat16, device=dev)
         hT = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
         fwd(S_in, o, hT, 2, 0)            # normal walk from the true segment inputs
@@ -176,13 +146,12 @@ class _SegmentedGDN(torch.autograd.Function):
             import torch.distributed as dist
             dist.broadcast(d_last, src=ctx.world - 1, group=ctx.group)
             # this rank's left-boundary gradient for a zero right-boundary gradient
-            d = torch.zeros(Hv, dk, dv, dtype=torch.float32, device=dev)
-            for kk in range(n - 1, -1, -1):
-                d = Ms[kk].transpose(-1, -2) @ d + dS0[kk]
-            gathered = [torch.empty_like(d) for _ in range(ctx.world)]
-            dist.all_gather(gathered, d.contiguous(), group=ctx.group)
-            d_last = rank_output_grad(ctx.M_all, torch.stack(gathered, 0), ctx.rank, d_last)
-        dS_out = _suffix(Ms, dS0, d_last).contiguous()
+            _, d = state_fold(Ms, dS0, transpose=True, states=False)
+            d_all = torch.empty(ctx.world, Hv, dk, dv, dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(d_all, d, group=ctx.group)
+            _, d_last = state_fold(ctx.M_all[ctx.rank + 1:], d_all[ctx.rank + 1:], d_last, transpose=True,
+                                   states=False)
+        dS_out, _ = state_fold(Ms, dS0, d_last, transpose=True)
         dh0 = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
         bwd(dS_out, dh0, 1, 0)            # normal reversed walk
         bwd(None, None, 2, 0)             # chunk backward

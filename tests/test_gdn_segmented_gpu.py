@@ -80,3 +80,24 @@ def test_context_parallel_two_ranks():
     res = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "CP OK" in res.stdout, res.stdout[-3000:]
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+@pytest.mark.parametrize("n", [0, 1, 5])
+def test_state_fold_kernel_matches_oracle(n, transpose):
+    from oracle import segments as OS
+    from recant_b200.segmented import state_fold
+    gen = torch.Generator().manual_seed(n + 10 * transpose)
+    H = 3
+    M = torch.randn(n, H, 128, 128, generator=gen) / 128 ** 0.5
+    c = torch.randn(n, H, 128, 128, generator=gen)
+    s0 = torch.randn(H, 128, 128, generator=gen)
+    states, final = state_fold(M.cuda(), c.cuda(), s0.cuda(), transpose=transpose)
+    rs, rf = OS.fold(M.double(), c.double(), s0.double(), transpose=transpose)
+    assert rel(final, rf) < 1e-5
+    if n:
+        assert rel(states, rs) < 1e-5
+        # identity start without offsets composes the maps
+        _, prod = state_fold(M.cuda(), identity=True, states=False, transpose=transpose)
+        eye = torch.eye(128, dtype=torch.float64).expand(H, 128, 128)
+        assert rel(prod, OS.fold(M.double(), None, eye, transpose=transpose)[1]) < 1e-5

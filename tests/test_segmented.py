@@ -8,7 +8,7 @@ import torch.multiprocessing as mp
 
 from oracle import gdn as OG
 from oracle import inputs as I
-from recant_b200 import segmented as SG
+from oracle import segments as SG
 
 
 def _problem(T=320, d=8, H=2, seed=0):
@@ -36,13 +36,13 @@ def test_prefix_reproduces_unsegmented_forward():
     bounds = [0, 64, 192, 256, 320]
     Ms, S0 = _seg_maps(inp, bounds, d, H)
     h0 = torch.randn(H, d, d, dtype=torch.float64) * 0.1
-    S_in = SG._prefix(Ms, S0, h0)
+    S_in = SG.prefix(Ms, S0, h0)
     o_full, hT_full = OG.gdn_forward(*(inp[n] for n in ("q", "k", "v", "g", "beta")), h0[None], True, dtype=torch.float64)
     for kk, (s, e) in enumerate(zip(bounds[:-1], bounds[1:])):
         o, hT = OG.gdn_forward(*(inp[n][:, s:e] for n in ("q", "k", "v", "g", "beta")), S_in[kk][None], True,
                                dtype=torch.float64)
         assert torch.allclose(o, o_full[:, s:e], atol=1e-5)
-    M, c = SG._compose(Ms, S0)
+    M, c = SG.compose(Ms, S0)
     assert torch.allclose(M @ h0 + c, hT_full[0].double(), atol=1e-5)
 
 
@@ -53,8 +53,8 @@ def test_suffix_matches_autograd_state_gradient():
     Ms, S0 = _seg_maps(inp, bounds, d, H)
     d_final = torch.randn(H, d, d, dtype=torch.float64)
     # gradient of <S_final, d_final> w.r.t. the initial state through the composed map = M^T d_final
-    M, _ = SG._compose(Ms, S0)
-    dS_out = SG._suffix(Ms, torch.zeros_like(S0), d_final)
+    M, _ = SG.compose(Ms, S0)
+    dS_out = SG.suffix(Ms, torch.zeros_like(S0), d_final)
     assert torch.allclose(Ms[0].transpose(-1, -2) @ dS_out[0], M.transpose(-1, -2) @ d_final, atol=1e-8)
     h0 = torch.zeros(1, H, d, d, dtype=torch.float64, requires_grad=True)
     _, hT = OG.gdn_forward(*(inp[n] for n in ("q", "k", "v", "g", "beta")), h0, True, dtype=torch.float64)
@@ -72,7 +72,7 @@ def _rank_main(rank, world, port, out):
         inp = _problem(d=d, H=H, seed=5)
         shards = [[0, 64, 128], [128, 192, 320]]           # two segments per rank
         Ms, S0 = _seg_maps(inp, shards[rank], d, H)
-        Mr, cr = SG._compose(Ms, S0)
+        Mr, cr = SG.compose(Ms, S0)
         packed = torch.stack([Mr, cr], 0)
         gathered = [torch.empty_like(packed) for _ in range(world)]
         dist.all_gather(gathered, packed)
@@ -80,7 +80,7 @@ def _rank_main(rank, world, port, out):
         c_all = torch.stack([x[1] for x in gathered])
         h0 = torch.full((H, d, d), 0.05, dtype=torch.float64)
         s_in = SG.rank_input_state(M_all, c_all, rank, h0)
-        S_in = SG._prefix(Ms, S0, s_in)
+        S_in = SG.prefix(Ms, S0, s_in)
         outs = []
         for kk, (s, e) in enumerate(zip(shards[rank][:-1], shards[rank][1:])):
             o, _ = OG.gdn_forward(*(inp[n][:, s:e] for n in ("q", "k", "v", "g", "beta")), S_in[kk][None], True,
@@ -119,7 +119,7 @@ def test_context_parallel_rank_folds_gloo():
     assert torch.allclose(out[1][0], o_full[:, 128:], atol=1e-5)
     # rank 0's outgoing-state gradient = rank 1's map transposed applied to d_final
     Ms1, S01 = _seg_maps(inp, [128, 192, 320], d, H)
-    M1, _ = SG._compose(Ms1, S01)
+    M1, _ = SG.compose(Ms1, S01)
     d_final = torch.full((H, d, d), 0.3, dtype=torch.float64)
     assert torch.allclose(out[0][1], M1.transpose(-1, -2) @ d_final, atol=1e-6)
     assert torch.allclose(out[1][1], d_final)
