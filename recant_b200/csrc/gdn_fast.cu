@@ -138,9 +138,16 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
       if (row < 64) rk[row] = rs; else rq[row - 64] = rs;
     }
   }
-  if (tid == 0) {
-    double acc = 0.0;
-    for (int i = 0; i < 64; ++i) { acc += double(gv[i]); cum[i] = float(acc); }
+  if (w == 0) {  // cum = cumulative sum of g in double (the reference's fp32 cumsum accumulates in double)
+    double lo = gv[l], hi = gv[32 + l];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const double tl = __shfl_up_sync(0xffffffffu, lo, off), th = __shfl_up_sync(0xffffffffu, hi, off);
+      if (l >= off) { lo += tl; hi += th; }
+    }
+    hi += __shfl_sync(0xffffffffu, lo, 31);
+    cum[l] = float(lo);
+    cum[32 + l] = float(hi);
   }
   __syncthreads();
   if (tid < 64) ecum[tid] = __expf(cum[tid]);
@@ -172,9 +179,11 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
         const float b = j + 1 <= i ? si * rk[j + 1] * row[jj + 1] * __expf(ci_ - cum[j + 1]) : 0.f;
         packed[jj >> 1] = tc::pack_bf16(a, b);
       }
-      uint4* dst = reinterpret_cast<uint4*>(ws.aqk + ch * 4096 + i * 64 + c0);
+      unsigned char* dst = img(ws.aqk + ch * 4096);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, c0 + 8 * j, 64)) =
+            make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
     }
   }
   tc::fence_before_sync();
@@ -184,7 +193,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   for (int idx = tid; idx < 512; idx += 256) {
     const int i = idx >> 3, c8 = (idx & 7) * 8;
     const float* t = tm + i * 65 + c8;
-    *reinterpret_cast<uint4*>(ws.tinv + ch * 4096 + i * 64 + c8) =
+    *reinterpret_cast<uint4*>(img(ws.tinv + ch * 4096) + tc::sw128_offset(i, c8, 64)) =
         make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
                    tc::pack_bf16(t[6], t[7]));
   }
@@ -229,7 +238,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
-    bf16* dst = (row < 64 ? ws.kt : ws.qt) + ch * 8192 + i * 128 + c8;
+    unsigned char* dst = img((row < 64 ? ws.kt : ws.qt) + ch * 8192) + tc::sw128_offset(i, c8, 64);
     *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   tc::mbar_wait(&bar[1], 0, ws.err, 102);
@@ -240,7 +249,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
     tc::tmem_ld32(lane_addr + 0, tmp);
     store_cols32(ws.u + ch * 8192, 128, r, c0, 64, tmp);
     tc::tmem_ld32(lane_addr + 64, tmp);
-    store_cols32(ws.w + ch * 8192, 128, r, c0, 64, tmp);
+    store_cols32_img(img(ws.w + ch * 8192), 64, r, c0, tmp);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -275,16 +284,19 @@ __device__ __forceinline__ FwdStage fwd_stage(unsigned char* base, int stg) {
   return st;
 }
 
-__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch, int walk) {
-  load_rows_sw128(st.wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
-  load_rows_sw128(st.kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
+// One thread: bulk copies of the chunk's tile images (and U, cum) into a stage, counted on `bar`.
+__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch, int walk, uint64_t* bar) {
+  const uint32_t bytes = 16384 * 2 + 256 + (walk == 0 ? 16384 + 8192 : 0) + (walk != 2 ? 16384 : 0);
+  tc::fence_proxy_async();  // the stage's previous generic reads are ordered before these writes
+  tc::mbar_expect_tx(bar, bytes);
+  tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
+  tc::bulk_load(st.kt, ws.kt + ch * 8192, 16384, bar);
   if (walk == 0) {  // outputs need q~ and A_qk
-    load_rows_sw128(st.qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
-    load_rows64_sw128(st.at, ws.aqk + ch * 4096, 256);
+    tc::bulk_load(st.qt, ws.qt + ch * 8192, 16384, bar);
+    tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
   }
-  if (walk != 2) load_rows_plain(st.us, ws.u + ch * 8192, 128, 256);
-  if (threadIdx.x < 16) tc::cp_async16(st.cum + 4 * threadIdx.x, ws.stats + ch * 256 + 4 * threadIdx.x, true);
-  tc::cp_async_commit();
+  if (walk != 2) tc::bulk_load(st.us, ws.u + ch * 8192, 16384, bar);
+  tc::bulk_load(st.cum, ws.stats + ch * 256, 256, bar);
 }
 
 __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ o,
@@ -295,19 +307,22 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
   unsigned char* vpt = st + 32768;          // V'^T 128 rows (dv) x 64 (tok)                16 KB
   unsigned char* stages = vpt + 16384;      // 2 x FwdStage
   __shared__ uint64_t bar[2];
+  __shared__ uint64_t ldbar[2];   // stage loads
   __shared__ uint32_t tmem_base;
 
   const int h = blockIdx.x, s = blockIdx.y;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int r = 32 * (w & 3) + l, hh = w >> 2;
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
+  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
   if (tid == 0) {
     tc::mbar_init(&bar[0], 1);
     tc::mbar_init(&bar[1], 1);
+    tc::mbar_init(&ldbar[0], 1);
+    tc::mbar_init(&ldbar[1], 1);
     tc::fence_mbar_init();
+    if (c0 < c1) fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h, p.walk, &ldbar[0]);
   }
-  const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
-  if (c0 < c1) fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h, p.walk);
   // S^T[r][dk] for dk in [64 hh, 64 hh + 64): S[dk][r] of the [dk][dv] state
   float S[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
@@ -325,23 +340,20 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
     const int stg = (ci - c0) & 1;
     const FwdStage cur = fwd_stage(stages, stg);
-    if (ci + 1 < c1) {
-      fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv, p.walk);
-      tc::cp_async_wait<1>();
-    } else {
-      tc::cp_async_wait<0>();
-    }
+    if (tid == 0 && ci + 1 < c1) fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv, p.walk, &ldbar[stg ^ 1]);
+    tc::mbar_wait(&ldbar[stg], ((ci - c0) >> 1) & 1, ws.err, 110);
     // S^T (bf16) -> smem operand and -> workspace (state entering this chunk)
     {
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 64; j += 2) pk[j >> 1] = tc::pack_bf16(S[j], S[j + 1]);
-      uint4* gdst = reinterpret_cast<uint4*>(ws.hs + ch * 16384 + r * 128 + 64 * hh);
+      unsigned char* gdst = img(ws.hs + ch * 16384);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-        *reinterpret_cast<uint4*>(st + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
-        if (outs) gdst[j] = v4;
+        const uint32_t off = tc::sw128_offset(r, 64 * hh + 8 * j, 128);
+        *reinterpret_cast<uint4*>(st + off) = v4;
+        if (outs) *reinterpret_cast<uint4*>(gdst + off) = v4;
       }
     }
     tc::fence_proxy_async();
@@ -375,7 +387,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       }
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-      if (outs) store_cols32(ws.vp + ch * 8192, 128, r, 32 * hh, 64, x);
+      if (outs) store_cols32_img(img(ws.vp + ch * 8192), 64, r, 32 * hh, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =

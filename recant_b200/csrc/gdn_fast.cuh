@@ -9,16 +9,16 @@ namespace rb2 {
 struct FastWs {
   ChunkTable ct;
   float* stats;          // [ch][4][64] cum, rq, rk, beta
-  __nv_bfloat16* tinv;   // [ch][64][64]   T = (I + L)^-1
-  __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal
-  __nv_bfloat16* w;      // [ch][64][128]
-  __nv_bfloat16* u;      // [ch][64][128]
-  __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q
-  __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k
-  __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk]
-  __nv_bfloat16* vp;     // [ch][64][128]  V'
-  __nv_bfloat16* dh;     // [ch][128][128] dS^T of the state leaving the chunk, [dv][dk]
-  __nv_bfloat16* dvp;    // [ch][64][128]  dV'
+  __nv_bfloat16* tinv;   // [ch][64][64]   T = (I + L)^-1                      (tile image)
+  __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal (image)
+  __nv_bfloat16* w;      // [ch][64][128]                                      (tile image)
+  __nv_bfloat16* u;      // [ch][64][128]   plain row-major
+  __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q           (tile image)
+  __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k          (tile image)
+  __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk] (tile image)
+  __nv_bfloat16* vp;     // [ch][64][128]  V' (tile image)
+  __nv_bfloat16* dh;     // [ch][128][128] dS^T of the state leaving the chunk, [dv][dk] (image)
+  __nv_bfloat16* dvp;    // [ch][64][128]  dV' (tile image)
   float* dqh;            // [tokens][Hv][128] per-value-head dq (GQA only)
   float* dkh;            // [tokens][Hv][128]
   int* err;              // device status word
@@ -129,6 +129,24 @@ __device__ __forceinline__ void store_cols32(bf16* dst, int64_t row, int r, int 
     const int tk = t_base + j + (odd ? 1 : 0);
     const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
     if (tk < L) *reinterpret_cast<uint32_t*>(dst + int64_t(tk) * row + (r & ~1)) = tc::pack_bf16(lo, hi);
+  }
+}
+
+// Workspace tiles that a later kernel loads as an MMA operand are stored as "images": the exact
+// bytes of the K-major SW128 shared-memory tile (tc::sw128_offset), so that one linear bulk copy
+// into a 1024-byte-aligned buffer reproduces the swizzled operand.
+__device__ __forceinline__ unsigned char* img(void* base) { return static_cast<unsigned char*>(base); }
+
+// store_cols32 into a tile image with `rows` rows: token t_base + j, head-dim column r.
+__device__ __forceinline__ void store_cols32_img(unsigned char* image, int rows, int r, int t_base,
+                                                 const float (&v)[32]) {
+  const bool odd = (r & 1) != 0;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+    const int tk = t_base + j + (odd ? 1 : 0);
+    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
+    *reinterpret_cast<uint32_t*>(image + tc::sw128_offset(tk, r & ~1, rows)) = tc::pack_bf16(lo, hi);
   }
 }
 

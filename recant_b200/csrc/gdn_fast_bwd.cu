@@ -59,17 +59,23 @@ __device__ __forceinline__ BwdStage bwd_stage(unsigned char* base, int stg) {
   return st;
 }
 
+// dO rows of the chunk (rows >= len zero-filled) by cp.async from all threads; the workspace tile
+// images (k~, q~, W, A_qk, cum) by bulk copies from thread 0, counted on `bar`.
 __device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& p, const FastWs& ws, const bf16* d_o,
-                                          int ci, int h) {
+                                          int ci, int h, uint64_t* bar) {
   const int64_t ch = int64_t(ci) * p.Hv + h;
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
   load_rows_sw128(st.dot, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, 64, L, 256);
-  load_rows_sw128(st.kt, 64, 0, ws.kt + ch * 8192, 128, 64, 64, 256);
-  load_rows_sw128(st.qt, 64, 0, ws.qt + ch * 8192, 128, 64, 64, 256);
-  load_rows_sw128(st.wt, 64, 0, ws.w + ch * 8192, 128, 64, 64, 256);
-  load_rows64_sw128(st.at, ws.aqk + ch * 4096, 256);
-  if (threadIdx.x < 16) tc::cp_async16(st.cum + 4 * threadIdx.x, ws.stats + ch * 256 + 4 * threadIdx.x, true);
   tc::cp_async_commit();
+  if (threadIdx.x == 0) {
+    tc::fence_proxy_async();
+    tc::mbar_expect_tx(bar, 3 * 16384 + 8192 + 256);
+    tc::bulk_load(st.kt, ws.kt + ch * 8192, 16384, bar);
+    tc::bulk_load(st.qt, ws.qt + ch * 8192, 16384, bar);
+    tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
+    tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
+    tc::bulk_load(st.cum, ws.stats + ch * 256, 256, bar);
+  }
 }
 
 __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
@@ -80,6 +86,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
   unsigned char* dvt = dst + 32768;     // dV'^T rows dv x tok                          16 KB
   unsigned char* stages = dvt + 16384;  // 2 x BwdStage
   __shared__ uint64_t bar[2];
+  __shared__ uint64_t ldbar[2];   // stage loads (bulk part)
   __shared__ uint32_t tmem_base;
 
   const int h = blockIdx.x, s = blockIdx.y;
@@ -89,10 +96,12 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
   if (tid == 0) {
     tc::mbar_init(&bar[0], 1);
     tc::mbar_init(&bar[1], 1);
+    tc::mbar_init(&ldbar[0], 1);
+    tc::mbar_init(&ldbar[1], 1);
     tc::fence_mbar_init();
   }
   const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
-  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, d_o, c1 - 1, h);
+  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, d_o, c1 - 1, h, &ldbar[0]);
   float dS[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
 #pragma unroll
@@ -107,21 +116,23 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     const int stg = (c1 - 1 - ci) & 1;
     const BwdStage cur = bwd_stage(stages, stg);
     if (ci - 1 >= c0) {
-      bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, d_o, ci - 1, h);
+      bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, d_o, ci - 1, h, &ldbar[stg ^ 1]);
       tc::cp_async_wait<1>();
     } else {
       tc::cp_async_wait<0>();
     }
+    tc::mbar_wait(&ldbar[stg], ((c1 - 1 - ci) >> 1) & 1, ws.err, 120);
     {
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 64; j += 2) pk[j >> 1] = tc::pack_bf16(dS[j], dS[j + 1]);
-      uint4* gdst = reinterpret_cast<uint4*>(ws.dh + ch * 16384 + r * 128 + 64 * hh);
+      unsigned char* gdst = img(ws.dh + ch * 16384);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-        *reinterpret_cast<uint4*>(dst + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
-        if (p.walk == 0) gdst[j] = v4;
+        const uint32_t off = tc::sw128_offset(r, 64 * hh + 8 * j, 128);
+        *reinterpret_cast<uint4*>(dst + off) = v4;
+        if (p.walk == 0) *reinterpret_cast<uint4*>(gdst + off) = v4;
       }
     }
     sync_for_mma();
@@ -156,7 +167,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-      if (p.walk == 0) store_cols32(ws.dvp + ch * 8192, 128, r, 32 * hh, 64, x);
+      if (p.walk == 0) store_cols32_img(img(ws.dvp + ch * 8192), 64, r, 32 * hh, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(dvt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -252,6 +263,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   bf16* qcol = reinterpret_cast<bf16*>(sm + lay::QCOL);
   bf16* kcol = reinterpret_cast<bf16*>(sm + lay::KCOL);
   __shared__ uint64_t bar[5];
+  __shared__ uint64_t ldbar[2];   // bulk loads: workspace tile images, then T
   __shared__ uint32_t tmem_base;
 
   const int ci = blockIdx.x, h = blockIdx.y;
@@ -267,17 +279,21 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
   if (tid == 0) {
     for (int b = 0; b < 5; ++b) tc::mbar_init(&bar[b], 1);
+    tc::mbar_init(&ldbar[0], 1);
+    tc::mbar_init(&ldbar[1], 1);
     tc::fence_mbar_init();
+    // ---- loads: workspace tile images by bulk copy ---------------------------------------------
+    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2);
+    tc::bulk_load(sm + lay::DVP, ws.dvp + ch * 8192, 16384, &ldbar[0]);
+    tc::bulk_load(sm + lay::ST, ws.hs + ch * 16384, 32768, &ldbar[0]);
+    tc::bulk_load(sm + lay::DHT, ws.dh + ch * 16384, 32768, &ldbar[0]);
+    tc::bulk_load(sm + lay::VPT, ws.vp + ch * 8192, 16384, &ldbar[0]);
   }
-  // ---- loads ---------------------------------------------------------------------------------
+  // ---- loads: the caller's q, k, v, dO rows (rows >= len zero-filled) --------------------------
   load_rows_sw128(sm + lay::KQ, 128, 0, static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
   load_rows_sw128(sm + lay::KQ, 128, 64, static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
   load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 256);
-  load_rows_sw128(sm + lay::DVP, 64, 0, ws.dvp + ch * 8192, 128, 64, 64, 256);
-  load_rows_sw128(sm + lay::ST, 128, 0, ws.hs + ch * 16384, 128, 128, 128, 256);
-  load_rows_sw128(sm + lay::DHT, 128, 0, ws.dh + ch * 16384, 128, 128, 128, 256);
   load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 256);
-  load_rows_sw128(sm + lay::VPT, 64, 0, ws.vp + ch * 8192, 128, 64, 64, 256);
   tc::cp_async_commit();
   if (tid < 64) {
     const float* st = ws.stats + ch * 256;
@@ -289,6 +305,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   tc::cp_async_wait<0>();
   sync_for_mma();
+  tc::mbar_wait(&ldbar[0], 0, ws.err, 130);
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
@@ -332,8 +349,11 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   tc::mbar_wait(&bar[0], 0, ws.err, 131);
   tc::fence_after_sync();
-  load_rows64_sw128(sm + lay::TT, ws.tinv + ch * 4096, 256);  // T (bf16) over dS^T, consumed by G1
-  tc::cp_async_commit();
+  if (tid == 0) {  // T (tile image) over dS^T, which G1 and the dgamma sum have consumed
+    tc::fence_proxy_async();
+    tc::mbar_expect_tx(&ldbar[1], 8192);
+    tc::bulk_load(sm + lay::TT, ws.tinv + ch * 4096, 8192, &ldbar[1]);
+  }
   // ---- E1 ------------------------------------------------------------------------------------
   {
     float v[32];
@@ -364,8 +384,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     *reinterpret_cast<uint4*>(sm + lay::BV + tc::sw128_offset(m, c8, 64)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
     *reinterpret_cast<uint4*>(sm + lay::BK + tc::sw128_offset(m, c8, 64)) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
   }
-  tc::cp_async_wait<0>();
   sync_for_mma();
+  tc::mbar_wait(&ldbar[1], 0, ws.err, 136);
   const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
   if (tid == 0) {  // ---- G2 ----
     const uint32_t dva = tc::smem_u32(sm + lay::DVP), bva = tc::smem_u32(sm + lay::BV), bka = tc::smem_u32(sm + lay::BK);
@@ -603,15 +623,17 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     scal[1 + i] = z;
   }
   __syncthreads();
-  if (tid == 0) {
-    float dcl = scal[0] * expf(cum[63]);
-    for (int i = 0; i < 64; ++i) dcl += scal[1 + i];
-    dcum_acc[63] += dcl;
-    double acc = 0.0;
-    for (int i = 63; i >= 0; --i) {
-      acc += double(dcum_acc[i]);
-      if (i < L) dg[int64_t(t0 + i) * p.Hv + h] = float(acc);
+  if (w == 0) {  // dg = reverse cumulative sum of dcum (in double), lane l: tokens l and 32 + l
+    const float dcl = scal[0] * expf(cum[63]) + warp_sum(scal[1 + l] + scal[33 + l]);
+    double lo = dcum_acc[l], hi = l == 31 ? double(dcum_acc[63] + dcl) : double(dcum_acc[32 + l]);
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const double tl = __shfl_down_sync(0xffffffffu, lo, off), th = __shfl_down_sync(0xffffffffu, hi, off);
+      if (l + off < 32) { lo += tl; hi += th; }
     }
+    lo += __shfl_sync(0xffffffffu, hi, 0);
+    if (l < L) dg[int64_t(t0 + l) * p.Hv + h] = float(lo);
+    if (32 + l < L) dg[int64_t(t0 + 32 + l) * p.Hv + h] = float(hi);
   }
   if (tid < L && tid < 64) dbeta[int64_t(t0 + tid) * p.Hv + h] = __float2bfloat16_rn(dbeta_acc[tid]);
   tc::fence_before_sync();

@@ -38,22 +38,12 @@ struct GemmCfg {
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
 };
 
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
           "r"(tc::smem_u32(smem_dst)),
       "l"(map), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
       : "memory");
-}
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   tc::smem_u32(smem_dst)),
-               "l"(gsrc), "r"(bytes), "r"(tc::smem_u32(bar))
-               : "memory");
 }
 // smem descriptor of one 512-byte scale atom (32 rows x 16 bytes, no swizzle) for tcgen05.cp
 __device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
@@ -139,12 +129,12 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           unsigned char* st = sm + s * STAGE_BYTES;
           const int steps = min(4, ksteps - 4 * kt);
           const uint32_t sfa_bytes = steps * 512, sfb_bytes = steps * 512 * nrb;
-          mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sfa_bytes + sfb_bytes);
+          tc::mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sfa_bytes + sfb_bytes);
           tma_load_2d(st, &map_a, kt * BKB, tm * BM, &full[s]);
           tma_load_2d(st + A_BYTES, &map_b, kt * BKB, tn * BN, &full[s]);
-          bulk_load(st + A_BYTES + B_BYTES, sfa + (size_t(tm) * ncb + 4 * kt) * 512, sfa_bytes, &full[s]);
+          tc::bulk_load(st + A_BYTES + B_BYTES, sfa + (size_t(tm) * ncb + 4 * kt) * 512, sfa_bytes, &full[s]);
           for (int rb = 0; rb < nrb; ++rb)
-            bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + rb * 2048,
+            tc::bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + rb * 2048,
                       sfb + (size_t(tn * (BN / 128) + rb) * ncb + 4 * kt) * 512, steps * 512, &full[s]);
         }
       }
