@@ -66,6 +66,10 @@ GdnProblem make_problem(const void* q, const void* k, const void* v, const float
   return p;
 }
 
+// The tensor-core path moves rows of q, k, v, dO, o with 16-byte (bulk) copies and writes dq, dk,
+// dv in 4-byte pairs.
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 size_t exact_ws_bytes(const GdnProblem& p, ExactWs* out, void* base) {
   Carver c(base);
   ExactWs w;
@@ -137,6 +141,8 @@ int gdn_fwd_impl(const void* q, const void* k, const void* v, const float* g, co
   size_t saved, scratch;
   ws_split(p, &saved, &scratch);
   if (p.path == RB2_GDN_FAST) {
+    RB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && aligned16(ws),
+                  "gdn_fwd: q, k, v, o and ws must be 16-byte aligned on the tensor-core path");
     if (ws_bytes < saved) {
       set_error("gdn_fwd: workspace too small");
       return RB2_EWORKSPACE;
@@ -174,6 +180,9 @@ int gdn_bwd_impl(const void* q, const void* k, const void* v, const float* g, co
   size_t saved, need_scratch;
   ws_split(p, &saved, &need_scratch);
   if (p.path == RB2_GDN_FAST) {
+    RB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(d_o) && aligned16(dq) &&
+                      aligned16(dk_out) && aligned16(dv_out) && aligned16(ws) && aligned16(scratch),
+                  "gdn_bwd: q, k, v, dO, dq, dk, dv, ws and scratch must be 16-byte aligned on the tensor-core path");
     if (scratch ? (ws_bytes < saved || scratch_bytes < need_scratch) : ws_bytes < saved + need_scratch) {
       set_error("gdn_bwd: workspace too small");
       return RB2_EWORKSPACE;

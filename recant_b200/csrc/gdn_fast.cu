@@ -124,8 +124,9 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
     }
     tc::mma_commit(&bar[0]);
   }
-  // norms of the 128 stacked rows (half-warp per row), cumulative gate in double
-  for (int row = w * 2 + (l >> 4); row < 128; row += 16) {
+  // norms of the 128 stacked rows (half-warp per row, warps 1-7 while thread 0 issues the MMA),
+  // cumulative gate in double
+  for (int row = (w - 1) * 2 + (l >> 4); w > 0 && row < 128; row += 14) {
     const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row, (l & 15) * 8, 128));
     float s = 0.f;
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((l & 15) == 0) {
-      const float rs = 1.0f / sqrtf(s + 1e-6f);
+      const float rs = rsqrtf(s + 1e-6f);
       if (row < 64) rk[row] = rs; else rq[row - 64] = rs;
     }
   }
@@ -228,8 +229,8 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
     }
     tc::mma_commit(&bar[1]);
   }
-  // q~ and k~ rows while the MMAs run: half-warp per row, 8 elements per lane
-  for (int row = w * 2 + (l >> 4); row < 128; row += 16) {
+  // q~ and k~ rows while the MMAs run: half-warp per row, 8 elements per lane (warps 1-7)
+  for (int row = (w - 1) * 2 + (l >> 4); w > 0 && row < 128; row += 14) {
     const int c8 = (l & 15) * 8;
     const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row, c8, 128));
     const int i = row & 63;
@@ -347,13 +348,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 64; j += 2) pk[j >> 1] = tc::pack_bf16(S[j], S[j + 1]);
-      unsigned char* gdst = img(ws.hs + ch * 16384);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-        const uint32_t off = tc::sw128_offset(r, 64 * hh + 8 * j, 128);
-        *reinterpret_cast<uint4*>(st + off) = v4;
-        if (outs) *reinterpret_cast<uint4*>(gdst + off) = v4;
+        *reinterpret_cast<uint4*>(st + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
       }
     }
     tc::fence_proxy_async();
@@ -370,6 +368,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
         if (outs) tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(qa + boff), idesc, k0 > 0);
       }
       tc::mma_commit(&bar[0]);
+      if (outs) {  // the state entering the chunk: the S^T tile is its workspace image
+        tc::bulk_store(ws.hs + ch * 16384, st, 32768);
+        tc::bulk_commit();
+      }
     }
     tc::mbar_wait(&bar[0], phase, ws.err, 111);
     tc::fence_after_sync();
@@ -387,7 +389,6 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       }
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-      if (outs) store_cols32_img(img(ws.vp + ch * 8192), 64, r, 32 * hh, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -409,15 +410,17 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
                      k0 > 0);
       }
       tc::mma_commit(&bar[1]);
+      if (outs) {  // V'^T [dv][tok]: the tile is the workspace image
+        tc::bulk_store(ws.vp + ch * 8192, vpt, 16384);
+        tc::bulk_commit();
+      }
     }
     tc::mbar_wait(&bar[1], phase, ws.err, 112);
     tc::fence_after_sync();
+    float ox[32];  // o rows of this chunk, stored after the barrier below (stores ahead of a fence stall it)
     {
       float x[32];
-      if (outs) {
-        tc::tmem_ld32(lane_addr + 64 + 32 * hh, x);
-        store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, 32 * hh, L, x);
-      }
+      if (outs) tc::tmem_ld32(lane_addr + 64 + 32 * hh, ox);
       const float gamma = expf(cur.cum[63]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -426,14 +429,17 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
         for (int j = 0; j < 32; ++j) S[32 * half + j] = fmaf(gamma, S[32 * half + j], x[j]);
       }
     }
+    if (tid == 0) tc::bulk_wait_read();  // the S^T and V'^T tiles are rewritten next step
     tc::fence_before_sync();
     __syncthreads();
+    if (outs) store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, 32 * hh, L, ox);
     phase ^= 1;
   }
   if (hT) {
 #pragma unroll
     for (int j = 0; j < 64; ++j) hT[sbase + (64 * hh + j) * 128 + r] = S[j];
   }
+  if (tid == 0) tc::bulk_wait_all();
   tc::fence_before_sync();
   __syncthreads();
   if (w == 0) tc::tmem_dealloc(tbase, 512);

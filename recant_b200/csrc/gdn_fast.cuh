@@ -16,9 +16,9 @@ struct FastWs {
   __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q           (tile image)
   __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k          (tile image)
   __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk] (tile image)
-  __nv_bfloat16* vp;     // [ch][64][128]  V' (tile image)
+  __nv_bfloat16* vp;     // [ch][128][64]  V'^T [dv][tok] (tile image)
   __nv_bfloat16* dh;     // [ch][128][128] dS^T of the state leaving the chunk, [dv][dk] (image)
-  __nv_bfloat16* dvp;    // [ch][64][128]  dV' (tile image)
+  __nv_bfloat16* dvp;    // [ch][128][64]  dV'^T [dv][tok] (tile image)
   float* dqh;            // [tokens][Hv][128] per-value-head dq (GQA only)
   float* dkh;            // [tokens][Hv][128]
   int* err;              // device status word
@@ -113,6 +113,16 @@ __device__ inline void unit_lower_inverse(const float* lm, float* tm, float* xbu
 __device__ __forceinline__ void store_row32(unsigned char* tile, int rows, int r, int e0, const float (&v)[32]) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
+    const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                               tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0 + 8 * j, rows)) = x;
+  }
+}
+
+// 16 values of row r starting at element e0 (a multiple of 8) of a K-major SW128 tile -> bf16
+__device__ __forceinline__ void store_row16(unsigned char* tile, int rows, int r, int e0, const float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
     const uint4 x = make_uint4(tc::pack_bf16(v[8 * j], v[8 * j + 1]), tc::pack_bf16(v[8 * j + 2], v[8 * j + 3]),
                                tc::pack_bf16(v[8 * j + 4], v[8 * j + 5]), tc::pack_bf16(v[8 * j + 6], v[8 * j + 7]));
     *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0 + 8 * j, rows)) = x;

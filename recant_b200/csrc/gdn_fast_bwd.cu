@@ -126,13 +126,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 64; j += 2) pk[j >> 1] = tc::pack_bf16(dS[j], dS[j + 1]);
-      unsigned char* gdst = img(ws.dh + ch * 16384);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint4 v4 = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-        const uint32_t off = tc::sw128_offset(r, 64 * hh + 8 * j, 128);
-        *reinterpret_cast<uint4*>(dst + off) = v4;
-        if (p.walk == 0) *reinterpret_cast<uint4*>(gdst + off) = v4;
+        *reinterpret_cast<uint4*>(dst + tc::sw128_offset(r, 64 * hh + 8 * j, 128)) = v4;
       }
     }
     sync_for_mma();
@@ -158,6 +155,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
         tc::mma_bf16(tbase + 256, tc::desc_mnmajor_sw128(doa + k0 * 128, 8192), tc::desc_mnmajor_sw128(qa + k0 * 128, 8192),
                      id_s, k0 > 0);
       tc::mma_commit(&bar[0]);
+      if (p.walk == 0) {  // the gradient of the state leaving the chunk: the dS^T tile is its image
+        tc::bulk_store(ws.dh + ch * 16384, dst, 32768);
+        tc::bulk_commit();
+      }
     }
     tc::mbar_wait(&bar[0], phase, ws.err, 121);
     tc::fence_after_sync();
@@ -167,7 +168,6 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
-      if (p.walk == 0) store_cols32_img(img(ws.dvp + ch * 8192), 64, r, 32 * hh, x);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(dvt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -182,6 +182,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       for (int k0 = 0; k0 < 64; k0 += 16)
         tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_mnmajor_sw128(wa + k0 * 128, 8192), id_w, true);
       tc::mma_commit(&bar[1]);
+      if (p.walk == 0) {  // dV'^T [dv][tok]: the tile is the workspace image
+        tc::bulk_store(ws.dvp + ch * 8192, dvt, 16384);
+        tc::bulk_commit();
+      }
     }
     tc::mbar_wait(&bar[1], phase, ws.err, 122);
     tc::fence_after_sync();
@@ -195,6 +199,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
         for (int j = 0; j < 32; ++j) dS[32 * half + j] = fmaf(gamma, dS[32 * half + j], x[j]);
       }
     }
+    if (tid == 0) tc::bulk_wait_read();  // the dS^T tile is rewritten next step
     tc::fence_before_sync();
     __syncthreads();
     phase ^= 1;
@@ -203,6 +208,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
 #pragma unroll
     for (int j = 0; j < 64; ++j) dh0[sbase + (64 * hh + j) * 128 + r] = dS[j];
   }
+  if (tid == 0) tc::bulk_wait_all();
   tc::fence_before_sync();
   __syncthreads();
   if (w == 0) tc::tmem_dealloc(tbase, 512);
@@ -219,14 +225,12 @@ constexpr int ST = 65536, DHT = 98304, DOT = 131072, VPT = 147456;           // 
 constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  // phase 2 (over phase 1)
               YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
 constexpr int QB2 = VT;                                                        // over V once consumed
-constexpr int QCOL = 65536, KCOL = QCOL + 128 * 66 * 2;                        // final: over phase 2
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
-constexpr int VEC = DAQF + 16640;                                              // 12 x 64 floats
-constexpr int RED = VEC + 12 * 256;                                            // 5 x 4 x 64 floats
+constexpr int VEC = DAQF + 16640;                                              // 14 x 64 floats
+constexpr int RED = VEC + 14 * 256;                                            // 5 x 4 x 64 floats
 constexpr int END = RED + 5 * 1024 + 64;
 }  // namespace lay
 constexpr int kBChunkSmem = lay::END + 1024;
-constexpr int kColStride = 66;  // bf16 elements per row of the transposed q / k column tiles
 
 // Sum v[0..31] over the 32 lanes; afterwards lane l holds the total of column l.
 __device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
@@ -258,10 +262,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   float* daqf = reinterpret_cast<float*>(sm + lay::DAQF);
   float* vec = reinterpret_cast<float*>(sm + lay::VEC);
   float *cum = vec, *rq = vec + 64, *rk = vec + 128, *beta = vec + 192, *ecum = vec + 256, *edec = vec + 320,
-        *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [2][64] */, *scal = vec + 640;
+        *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [4][64] */, *scal = vec + 768;
   float* red = reinterpret_cast<float*>(sm + lay::RED);  // [5][4][64]
-  bf16* qcol = reinterpret_cast<bf16*>(sm + lay::QCOL);
-  bf16* kcol = reinterpret_cast<bf16*>(sm + lay::KCOL);
   __shared__ uint64_t bar[5];
   __shared__ uint64_t ldbar[2];   // bulk loads: workspace tile images, then T
   __shared__ uint32_t tmem_base;
@@ -312,25 +314,29 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   if (tid == 0) {  // ---- G1 ----
     const uint32_t sta = tc::smem_u32(sm + lay::ST), dha = tc::smem_u32(sm + lay::DHT), doa = tc::smem_u32(sm + lay::DOT),
                    vpa = tc::smem_u32(sm + lay::VPT), dva = tc::smem_u32(sm + lay::DVP);
+    // V'^T and dV'^T arrive as [dv][tok] tiles: read MN-major as the N = tok operand
     const uint32_t id_kk = tc::idesc_bf16(128, 64, false, false);
     const uint32_t id_s = tc::idesc_bf16(128, 64, true, false);
-    const uint32_t id_sn = tc::idesc_bf16(128, 64, true, false, true);
-    const uint32_t id_64 = tc::idesc_bf16(64, 64, false, false);
+    const uint32_t id_ss = tc::idesc_bf16(128, 64, true, true);
+    const uint32_t id_sn = tc::idesc_bf16(128, 64, true, true, true);
+    const uint32_t id_64 = tc::idesc_bf16(64, 64, false, true);
 #pragma unroll
     for (int k0 = 0; k0 < 128; k0 += 16) {
       const uint32_t o16 = (k0 >> 6) * 16384 + (k0 & 63) * 2, o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
       const bool acc = k0 > 0;
       tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(kqa + o16), tc::desc_kmajor_sw128(kqa + o16), id_kk, acc);
       tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_kmajor_sw128(doa + o8), id_s, acc);
-      tc::mma_bf16(tbase + 128, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_kmajor_sw128(dva + o8), id_sn, acc);
-      tc::mma_bf16(tbase + 192, tc::desc_mnmajor_sw128(dha + k0 * 128, 16384), tc::desc_kmajor_sw128(vpa + o8), id_s, acc);
-      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(doa + o8), tc::desc_kmajor_sw128(vpa + o8), id_64, acc);
+      tc::mma_bf16(tbase + 128, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_mnmajor_sw128(dva + k0 * 128, 8192),
+                   id_sn, acc);
+      tc::mma_bf16(tbase + 192, tc::desc_mnmajor_sw128(dha + k0 * 128, 16384), tc::desc_mnmajor_sw128(vpa + k0 * 128, 8192),
+                   id_ss, acc);
+      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(doa + o8), tc::desc_mnmajor_sw128(vpa + k0 * 128, 8192), id_64, acc);
     }
     tc::mma_commit(&bar[0]);
   }
-  {  // dgamma = sum S^T * dS^T while G1 runs (both tiles share one layout)
+  {  // dgamma = sum S^T * dS^T while G1 runs (both tiles share one layout); warp 0 issues G1
     float part = 0.f;
-    for (int idx = tid; idx < 128 * 16; idx += 256) {
+    for (int idx = tid - 32; w > 0 && idx < 128 * 16; idx += 224) {
       const uint32_t off = uint32_t(idx) * 16;
       const uint4 a = *reinterpret_cast<const uint4*>(sm + lay::ST + off);
       const uint4 b = *reinterpret_cast<const uint4*>(sm + lay::DHT + off);
@@ -389,22 +395,23 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
   if (tid == 0) {  // ---- G2 ----
     const uint32_t dva = tc::smem_u32(sm + lay::DVP), bva = tc::smem_u32(sm + lay::BV), bka = tc::smem_u32(sm + lay::BK);
-    const uint32_t id_t1 = tc::idesc_bf16(64, 64, false, false), id_t2 = tc::idesc_bf16(64, 64, true, false);
+    const uint32_t id_t1 = tc::idesc_bf16(64, 64, true, false), id_t2 = tc::idesc_bf16(64, 64, true, false);
 #pragma unroll
-    for (int k0 = 0; k0 < 128; k0 += 16) {
+    for (int k0 = 0; k0 < 128; k0 += 16) {  // dT = dV' (beta V)^T, dV' read MN-major from the dV'^T tile
       const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
-      tc::mma_bf16(tbase + 320, tc::desc_kmajor_sw128(dva + o8), tc::desc_kmajor_sw128(bva + o8), id_t1, k0 > 0);
+      tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dva + k0 * 128, 8192), tc::desc_kmajor_sw128(bva + o8), id_t1,
+                   k0 > 0);
     }
 #pragma unroll
     for (int k0 = 0; k0 < 128; k0 += 16) {
       const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
       tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dwa + k0 * 128, 16384), tc::desc_kmajor_sw128(bka + o8), id_t2, true);
     }
-    const uint32_t id_bv = tc::idesc_bf16(128, 64, true, true), id_bk = tc::idesc_bf16(128, 64, false, true);
+    const uint32_t id_bv = tc::idesc_bf16(128, 64, false, true), id_bk = tc::idesc_bf16(128, 64, false, true);
 #pragma unroll
     for (int k0 = 0; k0 < 64; k0 += 16) {
-      tc::mma_bf16(tbase + 384, tc::desc_mnmajor_sw128(dva + k0 * 128, 8192), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192),
-                   id_bv, k0 > 0);
+      tc::mma_bf16(tbase + 384, tc::desc_kmajor_sw128(dva + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bv,
+                   k0 > 0);
       tc::mma_bf16(tbase + 448, tc::desc_kmajor_sw128(dwa + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bk,
                    k0 > 0);
     }
@@ -448,12 +455,15 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   {
     float v[32];
     tmem_ld32f(lane_addr + 0, v);
-    if (mrow) store_row32(sm + lay::YT, 64, i64, c0, v);
+    if (mrow) {  // [Y; Y]: G4 runs with M = 128 so that E4 has a row in every lane
+      store_row32(sm + lay::YT, 128, i64, c0, v);
+      store_row32(sm + lay::YT, 128, 64 + i64, c0, v);
+    }
   }
   sync_for_mma();
   if (tid == 0) {  // ---- G4: dL' = Y T^T ----
     const uint32_t ya = tc::smem_u32(sm + lay::YT);
-    const uint32_t id_l = tc::idesc_bf16(64, 64, false, false);
+    const uint32_t id_l = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
     for (int k0 = 0; k0 < 64; k0 += 16)
       tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
@@ -461,37 +471,36 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   tc::mbar_wait(&bar[3], 0, ws.err, 134);
   tc::fence_after_sync();
-  // ---- E4: P, Qm, R and the B operands of G5 (row i64, columns c0..c0+31) ---------------------
+  // ---- E4: P, Qm, R and the B operands of G5. dL' is an M = 128 accumulator of [Y; Y] T^T, so
+  // lane 32 q4 + l holds token row i = (32 q4 + l) & 63; the thread takes 16 columns, cb..cb+15.
   {
-    float v[32];
-    tmem_ld32f(lane_addr + 256, v);
-    if (mrow) {
-      const int i = i64;
-      const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
-      float db = 0.f;
-      float pb1[32], qb1[32], pb2[32], qb2[32];
+    const int i = r & 63, cb = c0 + 16 * (q4 >> 1);
+    float v[16];
+    tc::tmem_ld16(tbase + (uint32_t(32 * q4) << 16) + 256 + cb, v);
+    const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
+    float db = 0.f;
+    float pb1[16], qb1[16], pb2[16], qb2[16];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = c0 + jj;
-        const float gam = j <= i ? __expf(ci_ - cum[j]) : 0.f;
-        const float P = j < i ? -v[jj] * gam : 0.f;
-        const float kkn = kkf[i * 65 + j] * rki * rk[j];
-        const float qkn = qkf[i * 65 + j] * sqi * rk[j];
-        const float daq = daqf[i * 65 + j];
-        const float qm = daq * gam;
-        db = fmaf(P, kkn, db);
-        kkf[i * 65 + j] = P * bi * kkn + daq * qkn * gam;  // R
-        pb1[jj] = bi * rk[j] * P;
-        qb1[jj] = rk[j] * qm;
-        pb2[jj] = bi * rki * P;
-        qb2[jj] = sqi * qm;
-      }
-      dbp[hh * 64 + i] = db;
-      store_row32(sm + lay::PB1, 64, i, c0, pb1);
-      store_row32(sm + lay::QB1, 64, i, c0, qb1);
-      store_row32(sm + lay::PB2, 64, i, c0, pb2);
-      store_row32(sm + lay::QB2, 64, i, c0, qb2);
+    for (int jj = 0; jj < 16; ++jj) {
+      const int j = cb + jj;
+      const float gam = j <= i ? __expf(ci_ - cum[j]) : 0.f;
+      const float P = j < i ? -v[jj] * gam : 0.f;
+      const float kkn = kkf[i * 65 + j] * rki * rk[j];
+      const float qkn = qkf[i * 65 + j] * sqi * rk[j];
+      const float daq = daqf[i * 65 + j];
+      const float qm = daq * gam;
+      db = fmaf(P, kkn, db);
+      kkf[i * 65 + j] = P * bi * kkn + daq * qkn * gam;  // R
+      pb1[jj] = bi * rk[j] * P;
+      qb1[jj] = rk[j] * qm;
+      pb2[jj] = bi * rki * P;
+      qb2[jj] = sqi * qm;
     }
+    dbp[(2 * hh + (q4 >> 1)) * 64 + i] = db;
+    store_row16(sm + lay::PB1, 64, i, cb, pb1);
+    store_row16(sm + lay::QB1, 64, i, cb, qb1);
+    store_row16(sm + lay::PB2, 64, i, cb, pb2);
+    store_row16(sm + lay::QB2, 64, i, cb, qb2);
   }
   sync_for_mma();
   if (tid == 0) {  // ---- G5 ----
@@ -509,33 +518,21 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     }
     tc::mma_commit(&bar[4]);
   }
-  if (tid < 64) {  // dcum_i += sum_j R_ij - sum_j R_ji;  dbeta partials
+  if (tid >= 64 && tid < 128) {  // dcum_i += sum_j R_ij - sum_j R_ji; dbeta partials (warp 0 issues G5)
+    const int i = tid - 64;
     float a = 0.f;
-    for (int j = 0; j < 64; ++j) a += kkf[tid * 65 + j] - kkf[j * 65 + tid];
-    dcum_acc[tid] += a;
-    dbeta_acc[tid] += dbp[tid] + dbp[64 + tid];
+    for (int j = 0; j < 64; ++j) a += kkf[i * 65 + j] - kkf[j * 65 + i];
+    dcum_acc[i] += a;
+    dbeta_acc[i] += dbp[i] + dbp[64 + i] + dbp[128 + i] + dbp[192 + i];
   }
   tc::mbar_wait(&bar[4], 0, ws.err, 135);
   tc::fence_after_sync();
   __syncthreads();  // region A (the phase-2 tiles) is free once G5 has completed
-  // ---- transposed copies of q and k: col[r][i] = x[i][r] ------------------------------------------
-  for (int idx = tid; idx < 128 * 16; idx += 256) {
-    const int t = idx >> 4, c8 = (idx & 15) * 8;
-    const uint4 x = *reinterpret_cast<const uint4*>(sm + lay::KQ + tc::sw128_offset(t, c8, 128));
-    bf16* col = t < 64 ? kcol : qcol;
-    const int i = t & 63;
-    const bf16* e = reinterpret_cast<const bf16*>(&x);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) col[(c8 + j) * kColStride + i] = e[j];
-  }
-  __syncthreads();
-  // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j -----------------------------
+  // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j; q[i][r], k[i][r] read from the
+  // [K;Q] tile (consecutive lanes read consecutive columns of one row: no bank conflicts) -----------
   float xr[32];
-  {
-    const uint32_t* qp = reinterpret_cast<const uint32_t*>(qcol + r * kColStride + c0);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) { const uint32_t u = qp[j]; xr[2 * j] = bf_lo(u); xr[2 * j + 1] = bf_hi(u); }
-  }
+  for (int j = 0; j < 32; ++j) xr[j] = tile_elem(sm + lay::KQ, 128, 64 + c0 + j, r);
   float* red1 = red;            // a1: sum_r dq~^T q
   float* red2 = red + 256;      // a4: sum_r dq^^T q   (l2norm)
   float* red3 = red + 512;      // a2: sum_r dk~^T k
@@ -556,11 +553,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     red2[q4 * 64 + c0 + l] = warp_colsum32(t1);
   }
   float kr_[32];
-  {
-    const uint32_t* kp = reinterpret_cast<const uint32_t*>(kcol + r * kColStride + c0);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) { const uint32_t u = kp[j]; kr_[2 * j] = bf_lo(u); kr_[2 * j + 1] = bf_hi(u); }
-  }
+  for (int j = 0; j < 32; ++j) kr_[j] = tile_elem(sm + lay::KQ, 128, c0 + j, r);
   float dkh[32];
   {
     float t2[32], t3[32];

@@ -113,3 +113,11 @@ def test_registry_mirror():
     assert N.get_gemm_backend() == "b200"
     with pytest.raises(KeyError):
         N.set_gemm_backend("nope")
+
+
+def test_gdn_fast_path_rejects_misaligned_pointers():
+    lib = L.lib()
+    ok, bad = C.c_void_p(1 << 20), C.c_void_p((1 << 20) + 2)
+    st = lib.rb2_gdn_fwd(bad, ok, ok, ok, ok, None, None, 1, 64, 1, 1, 1, 128, 128, L.BF16, L.GDN_FAST, 1.0,
+                         ok, ok, ok, 1 << 40, None)
+    assert st == L.EINVAL and b"aligned" in lib.rb2_last_error()
