@@ -39,7 +39,8 @@ def test_gdn_workspace_size_scales_with_problem():
     assert lib.rb2_gdn_workspace_size(1, 5000, 7, 16, 32, 128, 128, L.F32, L.GDN_EXACT) > 0
 
 
-@pytest.mark.parametrize("Hk,Hv,path", [(16, 32, L.GDN_FAST), (32, 32, L.GDN_FAST), (4, 8, L.GDN_EXACT)])
+@pytest.mark.parametrize("Hk,Hv,path", [(16, 32, L.GDN_FAST), (32, 32, L.GDN_FAST), (2, 32, L.GDN_FAST),
+                                        (4, 8, L.GDN_EXACT)])
 def test_gdn_workspace_split_sums_to_total(Hk, Hv, path):
     lib = L.lib()
     dt = L.BF16 if path == L.GDN_FAST else L.F32

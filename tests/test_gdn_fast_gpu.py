@@ -64,8 +64,10 @@ def _check_grads(inp, do, h0=None, dht=None, cu=None):
     assert not bad, (bad, errs)
 
 
-@pytest.mark.parametrize("B,T,Hk,Hv", [(1, 64, 1, 1), (2, 300, 2, 4), (1, 1024, 4, 8), (2, 130, 2, 2)])
+@pytest.mark.parametrize("B,T,Hk,Hv", [(1, 64, 1, 1), (2, 300, 2, 4), (1, 1024, 4, 8), (2, 130, 2, 2),
+                                       (1, 200, 2, 8), (1, 150, 1, 8), (1, 100, 1, 16)])
 def test_fast_backward(B, T, Hk, Hv):
+    """Includes GQA groups of 2, 4, 8 and 16 value heads per key head."""
     inp = I.gdn_inputs(B, T, Hk, Hv, 128, dtype=torch.bfloat16, seed=T + 7 * Hv)
     do = I.grad_output(B, T, Hv, 128, dtype=torch.bfloat16, seed=T + 1)
     _check_grads(inp, do)
