@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -45,6 +44,13 @@ KERNEL_FLOPS_PER_CH = {
     "gdn_exact_fwd_prep": 4 * _MF, "gdn_exact_fwd_state": 4 * _MF, "gdn_exact_fwd_out": 3 * _MF,
     "gdn_exact_bwd_state": 7 * _MF, "gdn_exact_bwd_mm": 7 * _MF, "gdn_exact_bwd_intra": 12 * _MF,
 }
+
+
+# DRAM bytes (read + write) per chunk-head of each tensor-core kernel, from the ncu capture in
+# profiles/gdn_fast_kernels_B1T4096_ncu.md (per launch at B1 T4096 / 2048 chunk-heads); traffic scales
+# with the number of chunk-heads
+TRAFFIC_PER_CH = {"gdn_fast_prep": 183.9168e6 / 2048, "gdn_fast_state_fwd": 244.369408e6 / 2048,
+                  "gdn_fast_state_bwd": 217.417728e6 / 2048, "gdn_fast_chunk_bwd": 457.457152e6 / 2048}
 
 
 def peaks():
@@ -71,56 +77,47 @@ def algorithmic_bytes(B, T, Hk, Hv, d):
 
 # ------------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and throttle reasons of one GPU, polled through NVML every ~2 ms while running
+    (read-only queries); falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.reasons = set()
+        self.smax = None
+        self._stop = threading.Event()
+        self.t = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for nm, b in self.REASONS.items():
+                        if bits & b:
+                            self.reasons.add(nm)
+                    time.sleep(0.002)
+            self.t = threading.Thread(target=poll, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.t = None
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.3)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
-            except ValueError:
-                continue
-            for nm, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.t is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        self._stop.set()
+        self.t.join(timeout=2)
+        sm = self.samples
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                "reasons": sorted(self.reasons), "samples": len(sm), "source": "NVML, 2 ms polling"}
 
 
 def make_inputs(dev, rank, B, T, Hk, Hv, d):
@@ -165,6 +162,46 @@ def cpu_reference_sample(B, T, Hk, Hv, d, reps):
         OG.gdn_fwd_bwd(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], do.float())
     dt = (time.perf_counter() - t0) / reps
     return B * T / dt, threads, f"B{B} T{T} Hk{Hk} Hv{Hv} d{d} fwd+bwd, fp32 compute, {reps} reps", dt
+
+
+def nvfp4_leg(dev, pk, reps=10):
+    """The NVFP4 half of the path at config 2's in_proj shapes: quantize (RHT, round-to-nearest) of a
+    [16384, 4096] bf16 activation and the fprop GEMM [16384 x 4096] . [12288 x 4096]^T (qkv + z)
+    with a bf16 epilogue, each timed from the library's per-launch CUDA events. Quantize bytes are
+    the algorithmic 2.5625 per element (2 read, 0.5 codes, 1/16 scales); GEMM FLOPs are 2MNK
+    against 4 x the measured dense bf16 peak (the tcgen05 FP4 : bf16 rate)."""
+    import torch
+
+    from recant_b200 import _lib as L
+    from recant_b200 import nvfp4 as N
+    M, K, Nn = 16384, 4096, 12288
+    gen = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    W = N.quantize_weight(torch.randn(Nn, K, device=dev, generator=gen) * 0.02)
+    for _ in range(3):
+        a = N.quantize_fast(x)
+        y = N.gemm_b200(a, W.fprop, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    prof = L.LaunchProfiler(capacity=16 * reps)
+    prof.start()
+    for _ in range(reps):
+        a = N.quantize_fast(x)
+    for _ in range(reps):
+        y = N.gemm_b200(a, W.fprop, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    recs, _ = prof.read()
+    del y
+    q_ms = sum(t for n, t in recs if n in ("nvfp4_amax", "nvfp4_quant", "nvfp4_zero")) / reps
+    g_ms = sum(t for n, t in recs if n == "nvfp4_gemm") / reps
+    gbs = M * K * 2.5625 / (q_ms / 1e3) / 1e9
+    tfl = 2.0 * M * Nn * K / (g_ms / 1e3) / 1e12
+    fp4_peak = FP4_PER_BF16 * pk["bf16"]
+    return {"quantize": {"shape": [M, K], "ms": round(q_ms, 4), "achieved": round(gbs, 1), "unit": "GB/s",
+                         "peak": pk["hbm"], "frac": round(gbs / pk["hbm"], 4), "bytes_per_elt": 2.5625,
+                         "peak_source": f"{pk['source']} HBM copy (MEASURED_PEAKS.json)"},
+            "gemm": {"shape": [M, Nn, K], "ms": round(g_ms, 4), "achieved": round(tfl, 1), "unit": "TFLOP/s",
+                     "peak": round(fp4_peak, 1), "frac": round(tfl / fp4_peak, 4),
+                     "peak_source": f"4 x {pk['source']} bf16 burst (MEASURED_PEAKS.json)"}}
 
 
 def reference_arm(args, rank, world):
@@ -378,11 +415,13 @@ def run_config4(args, rank, world, local, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="config 1 only: batch B (default 4, the headline); smaller B for profiling captures")
     ap.add_argument("--config", type=int, choices=[1, 3, 4], default=1,
                     help="1: B4 T4096 replicas (the headline); 3: packed varlen, data-parallel by tokens; "
                          "4: 8-layer GDN + NVFP4 out_proj stack on one T=131072 sequence, context-parallel")
@@ -410,6 +449,8 @@ def main():
         return run_config4(args, rank, world, local, dev)
     c = CFG
     B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
+    if args.batch is not None and args.config == 1:
+        B = args.batch
     cu = None
     bucket = None
     total_tokens = B * T * world
@@ -519,8 +560,13 @@ def main():
         avg_s = tot / launches / 1e3
         flops = KERNEL_FLOPS_PER_CH.get(top, 0) * n_ch
         achieved = flops / avg_s / 1e12
+        traffic = TRAFFIC_PER_CH.get(top)
         roof = {"kernel": top, "bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16"],
-                "unit": "TFLOP/s", "frac": round(achieved / pk["bf16"], 4), "traffic": None,
+                "unit": "TFLOP/s", "frac": round(achieved / pk["bf16"], 4),
+                "traffic": None if traffic is None else round(traffic * n_ch),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per chunk-head x chunk-heads "
+                                  "(profiles/gdn_fast_kernels_B1T4096_ncu.md)",
+                "dram_gbs_at_traffic": None if traffic is None else round(traffic * n_ch / avg_s / 1e9, 1),
                 "peak_source": f"{pk['source']} bf16 burst (MEASURED_PEAKS.json)",
                 "share_of_kernel_time": round(tot / total_k, 3), "avg_launch_ms": round(avg_s * 1e3, 4)}
     path_flops = FLOP_PER_TOKEN_HEAD * tokens * Hv
@@ -553,6 +599,8 @@ def main():
         "kernels": kernels,
         "clocks": clock_info,
     }
+    if rank == 0 and world == 1 and args.config == 1:
+        line["nvfp4"] = nvfp4_leg(dev, pk)
     if rank == 0 and world == 1 and args.config == 1 and not args.no_cpu_baseline:
         tps, threads, sample, _ = cpu_reference_sample(1, 2048, Hk, Hv, d, 1)
         line["cpu_baseline"] = {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "port",

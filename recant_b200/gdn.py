@@ -82,6 +82,7 @@ class _GDNFunction(torch.autograd.Function):
         st = L.lib().rb2_gdn_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta_k), L.ptr(h0), L.ptr(cu),
                                  *pb.args(), L.ptr(o), L.ptr(hT), L.ptr(ws), pb.ws_bytes, _stream(q.device))
         L.check(st, "gdn_fwd")
+        ctx.set_materialize_grads(False)  # an unused final state needs no zero gradient
         ctx.save_for_backward(q, k, v, g, beta_k, h0, cu)
         ctx.pb, ctx.ws = pb, ws
         ctx.beta_dtype = beta.dtype
@@ -92,6 +93,8 @@ class _GDNFunction(torch.autograd.Function):
     def backward(ctx, do, dhT):
         q, k, v, g, beta, h0, cu = ctx.saved_tensors
         pb, ws = ctx.pb, ctx.ws
+        if do is None:
+            do = torch.zeros(pb.B, pb.T, pb.Hv, pb.dv, dtype=pb.dtype, device=q.device)
         do = do.to(pb.dtype).contiguous()
         dhT = None if dhT is None else dhT.to(torch.float32).contiguous()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)

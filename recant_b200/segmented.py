@@ -113,6 +113,7 @@ class _SegmentedGDN(torch.autograd.Function):
         ctx.ws, ctx.wsb, ctx.scratch_bytes, ctx.Ms, ctx.M_all = ws, wsb, scratch.value, Ms, M_all
         ctx.dims, ctx.n, ctx.group, ctx.world, ctx.rank = dims, n, group, world, rank
         ctx.has_h0 = initial_state is not None
+        ctx.set_materialize_grads(False)
         return o, final
 
     @staticmethod
@@ -122,6 +123,8 @@ class _SegmentedGDN(torch.autograd.Function):
         dev = q.device
         lib = L.lib()
         st = _stream(dev)
+        if do is None:
+            do = torch.zeros(1, q.shape[1], v.shape[2], v.shape[3], dtype=torch.bfloat16, device=dev)
         do = do.to(torch.bfloat16).contiguous()
         _, T, Hv, dv = do.shape
         dk = q.shape[-1]
