@@ -120,26 +120,59 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
   return c;
 }
 
+// e2m1 index for round-to-nearest with ties toward zero: the number of decision points 0.25, 0.75,
+// 1.25, 1.75, 2.5, 3.5, 5 strictly below a = min(|q|, 6). Each point has at most two mantissa bits
+// after the leading one, so with key = ceil(bits(a) / 2^21) (sign 0, 8 exponent bits, 2 mantissa
+// bits, rounded up) a > point <=> key > key(point); the keys of the points are 500, 506, 509, 511,
+// 513, 515, 517, and the index is a step function of key in [500, 518], read from a packed table
+// of 4-bit entries.
+__device__ __forceinline__ int e2m1_index(float a) {
+  const uint32_t key = (__float_as_uint(a) + 0x1FFFFFu) >> 21;
+  const uint32_t k = min(max(key, 500u), 518u) - 500u;  // 0 .. 18
+  // entry k = #{points with key < 500 + k}
+  constexpr uint64_t lo = 0x5544332221111110ull;        // k = 0 .. 15
+  constexpr uint32_t hi = 0x766u;                        // k = 16 .. 18
+  return k < 16 ? int((lo >> (4 * k)) & 0xF) : int((hi >> (4 * (k - 16))) & 0xF);
+}
+
 __device__ __forceinline__ float grid_value(int i) {
   // e2m1 magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6
   return i < 4 ? 0.5f * float(i) : (i == 4 ? 2.f : (i == 5 ? 3.f : (i == 6 ? 4.f : 6.f)));
 }
 
+// floor(n / d) for n < 2^32 by one multiply and shift (Granlund & Montgomery, PLDI 1994):
+// s = ceil(log2 d), m = ceil(2^(32+s) / d)
+struct Divider {
+  uint64_t m;
+  uint32_t s;
+};
+inline Divider make_divider(uint32_t d) {
+  uint32_t s = 0;
+  while ((uint64_t(1) << s) < d) ++s;
+  const unsigned __int128 num = (static_cast<unsigned __int128>(1) << (32 + s));
+  return Divider{uint64_t((num + d - 1) / d), s};
+}
+__device__ __forceinline__ uint32_t divide(uint32_t n, Divider dv) {
+  // m < 2^33: floor(n m / 2^32) = floor(n m_lo / 2^32) + n m_hi
+  const uint64_t hi32 = ((uint64_t(n) * uint32_t(dv.m)) >> 32) + uint64_t(n) * (dv.m >> 32);
+  return uint32_t(hi32 >> dv.s);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-quant_kernel(const T* __restrict__ x, int64_t n_blocks, int64_t groups, int64_t rows, int rot,
+quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divider by_groups, int rot,
              int stochastic, uint64_t seed, const unsigned int* __restrict__ gmax_bits,
              uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
              uint8_t* __restrict__ blocked, float* __restrict__ gscale_out) {
   // reverse CTA order: consume what pass 1 left in L2 first
-  const int64_t cta = int64_t(gridDim.x) - 1 - blockIdx.x;
-  const int64_t b = cta * kThreads + threadIdx.x;
+  const uint32_t cta = gridDim.x - 1 - blockIdx.x;
+  const uint32_t b = cta * kThreads + threadIdx.x;
   const float gmax = fmaxf(__uint_as_float(*gmax_bits), 1e-30f);
   const float s_g = __fdiv_rn(gmax, 2688.0f);  // 6 * 448
   if (blockIdx.x == 0 && threadIdx.x == 0) *gscale_out = s_g;
   if (b >= n_blocks) return;
   float v[16];
-  load16<T>(x + b * 16, v);
+  load16<T>(x + size_t(b) * 16, v);
   transform16<T>(v, rot != 0);
   float amax = 0.f;
 #pragma unroll
@@ -155,7 +188,7 @@ quant_kernel(const T* __restrict__ x, int64_t n_blocks, int64_t groups, int64_t 
     const uint2 key = make_uint2(uint32_t(seed), uint32_t(seed >> 32));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint4 r = philox4x32_10(make_uint4(uint32_t(b), uint32_t(uint64_t(b) >> 32), uint32_t(j), 0u), key);
+      uint4 r = philox4x32_10(make_uint4(b, 0u, uint32_t(j), 0u), key);
       rnd[4 * j + 0] = r.x; rnd[4 * j + 1] = r.y; rnd[4 * j + 2] = r.z; rnd[4 * j + 3] = r.w;
     }
   }
@@ -173,7 +206,7 @@ quant_kernel(const T* __restrict__ x, int64_t n_blocks, int64_t groups, int64_t 
       const float u = float(rnd[i] >> 8) * (1.0f / 16777216.0f);
       idx = (u < p) ? hi : hi - 1;
     } else {
-      idx = (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) + (a > 2.5f) + (a > 3.5f) + (a > 5.0f);
+      idx = e2m1_index(a);
     }
     const uint32_t code = uint32_t(idx + (q < 0.f ? 8 : 0));
     packed[i >> 3] |= code << (4 * (i & 7));
@@ -181,12 +214,11 @@ quant_kernel(const T* __restrict__ x, int64_t n_blocks, int64_t groups, int64_t 
   reinterpret_cast<uint2*>(codes)[b] = make_uint2(packed[0], packed[1]);
   scales[b] = uint8_t(s8);
   if (blocked) {
-    const int64_t r = b / groups, c = b % groups;
-    const int64_t ncb = (groups + 3) / 4;
-    const int64_t off = ((r >> 7) * ncb + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
+    const uint32_t r = divide(b, by_groups), c = b - r * groups;
+    const size_t ncb = (groups + 3) / 4;
+    const size_t off = ((r >> 7) * ncb + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
     blocked[off] = uint8_t(s8);
   }
-  (void)rows;
 }
 
 }  // namespace
@@ -206,6 +238,8 @@ extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype
   RB2_CHECK_ARG(M > 0 && K > 0 && K % 16 == 0, "nvfp4_quantize: need M, K > 0 and K %% 16 == 0 (M=%lld K=%lld)",
                 (long long)M, (long long)K);
   RB2_CHECK_ARG(dtype == RB2_F32 || dtype == RB2_BF16, "nvfp4_quantize: dtype must be F32 or BF16");
+  RB2_CHECK_ARG(M * (K / 16) < (int64_t(1) << 31), "nvfp4_quantize: more than 2^31 blocks of 16 (M=%lld K=%lld)",
+                (long long)M, (long long)K);
   RB2_CHECK_ARG(x && codes && scales && gscale && ws, "nvfp4_quantize: null pointer");
   RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(codes) & 7) == 0,
                 "nvfp4_quantize: x must be 16-byte and codes 8-byte aligned");
@@ -224,18 +258,20 @@ extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype
     RB2_CUDA(cudaMemsetAsync(scales_blocked, 0, nb, s), "nvfp4_quantize: clear blocked pads");
   }
   const unsigned grid = unsigned((n_blocks + kThreads - 1) / kThreads);
+  const Divider div = make_divider(uint32_t(groups));
   if (dtype == RB2_BF16) {
     auto xp = static_cast<const __nv_bfloat16*>(x);
     { ProfScope ps_("nvfp4_amax", s); amax_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
     ProfScope ps_("nvfp4_quant", s);
-    quant_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, n_blocks, groups, M, use_rht, stochastic, seed,
-                                                          gmax, codes, scales, scales_blocked, gscale);
+    quant_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, uint32_t(n_blocks), uint32_t(groups), div, use_rht,
+                                                          stochastic, seed, gmax, codes, scales, scales_blocked,
+                                                          gscale);
   } else {
     auto xp = static_cast<const float*>(x);
     { ProfScope ps_("nvfp4_amax", s); amax_kernel<float><<<grid, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
     ProfScope ps_("nvfp4_quant", s);
-    quant_kernel<float><<<grid, kThreads, 0, s>>>(xp, n_blocks, groups, M, use_rht, stochastic, seed,
-                                                  gmax, codes, scales, scales_blocked, gscale);
+    quant_kernel<float><<<grid, kThreads, 0, s>>>(xp, uint32_t(n_blocks), uint32_t(groups), div, use_rht, stochastic,
+                                                  seed, gmax, codes, scales, scales_blocked, gscale);
   }
   RB2_CHECK_LAUNCH("nvfp4_quantize");
   return RB2_OK;
