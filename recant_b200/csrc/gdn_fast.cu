@@ -114,30 +114,15 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16) + c0;
-  if (tid == 0) {  // [K;Q] K^T: M=128, N=64, K=128 -> TMEM cols [0, 64)
+  if (tid == 0) {  // [K;Q][K;Q]^T: M=128, N=128, K=128 -> TMEM cols [0, 128)
     const uint32_t a0 = tc::smem_u32(kq);
-    const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
+    const uint32_t idesc = tc::idesc_bf16(128, 128, false, false);
 #pragma unroll
     for (int k0 = 0; k0 < 128; k0 += 16) {
       const uint32_t off = (k0 >> 6) * 16384 + (k0 & 63) * 2;
       tc::mma_bf16(tbase, tc::desc_kmajor_sw128(a0 + off), tc::desc_kmajor_sw128(a0 + off), idesc, k0 > 0);
     }
     tc::mma_commit(&bar[0]);
-  }
-  // norms of the 128 stacked rows (half-warp per row, warps 1-7 while thread 0 issues the MMA),
-  // cumulative gate in double
-  for (int row = (w - 1) * 2 + (l >> 4); w > 0 && row < 128; row += 14) {
-    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row, (l & 15) * 8, 128));
-    float s = 0.f;
-    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) { const float a = bf_lo(xs[j]), b = bf_hi(xs[j]); s = fmaf(a, a, s); s = fmaf(b, b, s); }
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((l & 15) == 0) {
-      const float rs = rsqrtf(s + 1e-6f);
-      if (row < 64) rk[row] = rs; else rq[row - 64] = rs;
-    }
   }
   if (w == 0) {  // cum = cumulative sum of g in double (the reference's fp32 cumsum accumulates in double)
     double lo = gv[l], hi = gv[32 + l];
@@ -150,17 +135,39 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
     cum[l] = float(lo);
     cum[32 + l] = float(hi);
   }
-  __syncthreads();
+  tc::mbar_wait(&bar[0], 0, ws.err, 101);
+  tc::fence_after_sync();
+  // lane r of the accumulator: rows 0-63 = k_i . [k; q], rows 64-127 = q_i . [k; q]; this thread's
+  // columns c0..c0+31 of the first 64 (K K^T and Q K^T). The squared norms are diagonals: |k_i|^2 at
+  // (i, i), |q_i|^2 at (64 + i, 64 + i), i.e. column 32 q4 + l of lane 32 q4 + l.
+  float row[32];
+  tc::tmem_ld32(lane_addr, row);
+  {
+    const int q4 = w & 3;
+    float dg[32];
+    bool mine = false;
+    if (q4 < 2 && hh == q4) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) dg[j] = row[j];
+      mine = true;
+    } else if (q4 >= 2 && hh == 0) {
+      tc::tmem_ld32(tbase + (uint32_t(32 * q4) << 16) + 32 * q4, dg);
+      mine = true;
+    }
+    if (mine) {
+      float d = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) d = j == l ? dg[j] : d;
+      const float rs = rsqrtf(d + 1e-6f);
+      if (r < 64) rk[r] = rs; else rq[r - 64] = rs;
+    }
+  }
+  __syncthreads();  // cum, rk, rq
   if (tid < 64) ecum[tid] = __expf(cum[tid]);
   float* st = ws.stats + ch * 256;
   if (tid < 64) { st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid]; }
-
-  tc::mbar_wait(&bar[0], 0, ws.err, 101);
-  tc::fence_after_sync();
+  uint32_t apk[16];  // A_qk row i (bf16 pairs), stored after the proxy fence below
   {
-    // lane r of the accumulator: rows 0-63 = kk row i, rows 64-127 = qk row i; columns c0..c0+31
-    float row[32];
-    tc::tmem_ld32(lane_addr, row);
     const int i = r & 63;
     const float ci_ = cum[i];
     if (r < 64) {
@@ -172,32 +179,18 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
       }
     } else {
       const float si = p.scale * rq[i];
-      uint32_t packed[16];
 #pragma unroll
       for (int jj = 0; jj < 32; jj += 2) {
         const int j = c0 + jj;
         const float a = j <= i ? si * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
         const float b = j + 1 <= i ? si * rk[j + 1] * row[jj + 1] * __expf(ci_ - cum[j + 1]) : 0.f;
-        packed[jj >> 1] = tc::pack_bf16(a, b);
+        apk[jj >> 1] = tc::pack_bf16(a, b);
       }
-      unsigned char* dst = img(ws.aqk + ch * 4096);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, c0 + 8 * j, 64)) =
-            make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
     }
   }
   tc::fence_before_sync();
   __syncthreads();
   unit_lower_inverse(lm, tm, xbuf, 256);
-  // T to the workspace (bf16 rows, the backward's MMA operand) and the two bf16 B operands
-  for (int idx = tid; idx < 512; idx += 256) {
-    const int i = idx >> 3, c8 = (idx & 7) * 8;
-    const float* t = tm + i * 65 + c8;
-    *reinterpret_cast<uint4*>(img(ws.tinv + ch * 4096) + tc::sw128_offset(i, c8, 64)) =
-        make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
-                   tc::pack_bf16(t[6], t[7]));
-  }
   {
     const int i = tid & 63, which = (tid >> 6) & 1, m0 = 32 * (tid >> 7);
     unsigned char* dst = which == 0 ? tb1 : tb2;
@@ -228,6 +221,22 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
       tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(ka + k0 * 128, 16384), tc::desc_kmajor_sw128(b2 + k0 * 2), idesc, k0 > 0);
     }
     tc::mma_commit(&bar[1]);
+  }
+  // workspace images of A_qk and T (global stores kept behind the proxy fence above)
+  if (r >= 64) {
+    unsigned char* dst = img(ws.aqk + ch * 4096);
+    const int i = r & 63;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, c0 + 8 * j, 64)) =
+          make_uint4(apk[4 * j], apk[4 * j + 1], apk[4 * j + 2], apk[4 * j + 3]);
+  }
+  for (int idx = tid; idx < 512; idx += 256) {
+    const int i = idx >> 3, c8 = (idx & 7) * 8;
+    const float* t = tm + i * 65 + c8;
+    *reinterpret_cast<uint4*>(img(ws.tinv + ch * 4096) + tc::sw128_offset(i, c8, 64)) =
+        make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
+                   tc::pack_bf16(t[6], t[7]));
   }
   // q~ and k~ rows while the MMAs run: half-warp per row, 8 elements per lane (warps 1-7)
   for (int row = (w - 1) * 2 + (l >> 4); w > 0 && row < 128; row += 14) {
