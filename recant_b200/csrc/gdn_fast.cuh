@@ -147,6 +147,35 @@ __device__ __forceinline__ void store_cols32(bf16* dst, int64_t row, int r, int 
 // into a 1024-byte-aligned buffer reproduces the swizzled operand.
 __device__ __forceinline__ unsigned char* img(void* base) { return static_cast<unsigned char*>(base); }
 
+// 32 per-token values of head-dim column r (tokens t_base + j) into a plain [64][128] tile in shared
+// memory: bf16 pairs from lanes r, r^1, or fp32 words
+__device__ __forceinline__ void stage_cols32(bf16* tile, int r, int t_base, const float (&v)[32]) {
+  const bool odd = (r & 1) != 0;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+    const int tk = t_base + j + (odd ? 1 : 0);
+    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
+    *reinterpret_cast<uint32_t*>(tile + tk * 128 + (r & ~1)) = tc::pack_bf16(lo, hi);
+  }
+}
+__device__ __forceinline__ void stage_cols32(float* tile, int r, int t_base, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) tile[(t_base + j) * 128 + r] = v[j];
+}
+// Rows [0, L) of a plain [64][row_elems] shared tile to dst + i * stride (16-byte chunks by nthr
+// threads starting at thread `first`; row_bytes a multiple of 16)
+__device__ __forceinline__ void copy_rows_out(void* dst, int64_t stride_bytes, const void* tile, int row_bytes, int L,
+                                              int first, int nthr) {
+  const int chunks = row_bytes / 16;
+  for (int idx = int(threadIdx.x) - first; idx >= 0 && idx < 64 * chunks; idx += nthr) {
+    const int i = idx / chunks, c = idx - i * chunks;
+    if (i < L)
+      *reinterpret_cast<uint4*>(static_cast<char*>(dst) + i * stride_bytes + c * 16) =
+          *reinterpret_cast<const uint4*>(static_cast<const char*>(tile) + i * row_bytes + c * 16);
+  }
+}
+
 // store_cols32 into a tile image with `rows` rows: token t_base + j, head-dim column r.
 __device__ __forceinline__ void store_cols32_img(unsigned char* image, int rows, int r, int t_base,
                                                  const float (&v)[32]) {

@@ -225,6 +225,8 @@ constexpr int ST = 65536, DHT = 98304, DOT = 131072, VPT = 147456;           // 
 constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  // phase 2 (over phase 1)
               YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
 constexpr int QB2 = VT;                                                        // over V once consumed
+constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 is issued
+constexpr int GQS = 65536;   // GQA dq / dk rows, fp32 [2][64][128], in the final epilogue (after G5)
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
 constexpr int VEC = DAQF + 16640;                                              // 14 x 64 floats
 constexpr int RED = VEC + 14 * 256;                                            // 5 x 4 x 64 floats
@@ -435,7 +437,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       x[j] = beta[c0 + j] * v[j];
       v[j] *= tile_elem(sm + lay::VT, 64, c0 + j, r);
     }
-    store_cols32(dv + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, c0, L, x);
+    // dv rows are staged over dW^T (dead after G2) and written out after the last proxy fence
+    stage_cols32(reinterpret_cast<bf16*>(sm + lay::DVS), r, c0, x);
     red[q4 * 64 + c0 + l] = warp_colsum32(v);
   }
   __syncthreads();
@@ -503,6 +506,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     store_row16(sm + lay::QB2, 64, i, cb, qb2);
   }
   sync_for_mma();
+  // dv rows of the chunk: coalesced 16-byte stores by warps 4-7 while G5 runs
+  copy_rows_out(dv + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 256, sm + lay::DVS, 256, L, 128, 128);
   if (tid == 0) {  // ---- G5 ----
     const uint32_t p1 = tc::smem_u32(sm + lay::PB1), p2 = tc::smem_u32(sm + lay::PB2), q1 = tc::smem_u32(sm + lay::QB1),
                    q2 = tc::smem_u32(sm + lay::QB2);
@@ -596,15 +601,9 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       const int64_t row = int64_t(p.Hk) * 128;
       store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
       store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int i = c0 + j;
-        if (i < L) {
-          ws.dqh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gq[j];
-          ws.dkh[(int64_t(t0 + i) * p.Hv + h) * 128 + r] = gk[j];
-        }
-      }
+    } else {  // per-value-head fp32 rows, staged for coalesced stores below
+      stage_cols32(reinterpret_cast<float*>(sm + lay::GQS), r, c0, gq);
+      stage_cols32(reinterpret_cast<float*>(sm + lay::GQS) + 8192, r, c0, gk);
     }
   }
   // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------
@@ -630,6 +629,11 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     if (32 + l < L) dg[int64_t(t0 + 32 + l) * p.Hv + h] = float(hi);
   }
   if (tid < L && tid < 64) dbeta[int64_t(t0 + tid) * p.Hv + h] = __float2bfloat16_rn(dbeta_acc[tid]);
+  if (p.group > 1) {  // the staged rows are visible after the __syncthreads above
+    const int64_t rs = int64_t(p.Hv) * 512;
+    copy_rows_out(ws.dqh + (int64_t(t0) * p.Hv + h) * 128, rs, sm + lay::GQS, 512, L, 0, 256);
+    copy_rows_out(ws.dkh + (int64_t(t0) * p.Hv + h) * 128, rs, sm + lay::GQS + 32768, 512, L, 0, 256);
+  }
   tc::fence_before_sync();
   __syncthreads();
   if (w == 0) tc::tmem_dealloc(tbase, 512);
