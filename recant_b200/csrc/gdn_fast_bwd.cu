@@ -226,7 +226,7 @@ constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  /
               YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
 constexpr int QB2 = VT;                                                        // over V once consumed
 constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 is issued
-constexpr int GQS = 65536;   // GQA dq / dk rows, fp32 [2][64][128], in the final epilogue (after G5)
+constexpr int GQS = 163840;  // GQA dq then dk rows, fp32 [64][128], over the fp32 scratch after G5
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
 constexpr int VEC = DAQF + 16640;                                              // 14 x 64 floats
 constexpr int RED = VEC + 14 * 256;                                            // 5 x 4 x 64 floats
@@ -270,15 +270,12 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   __shared__ uint64_t ldbar[2];   // bulk loads: workspace tile images, then T
   __shared__ uint32_t tmem_base;
 
-  const int ci = blockIdx.x, h = blockIdx.y;
-  if (ci >= *ws.ct.n_chunks) return;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int q4 = w & 3, hh = w >> 2, r = 32 * q4 + l, c0 = 32 * hh;
   const bool mrow = l < 16;            // this lane holds a row of an M=64 accumulator
   const int i64 = 16 * q4 + l;          // ... and it is token row i64
-  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
-  const int64_t ch = int64_t(ci) * p.Hv + h;
   const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
+  const int64_t n_items = int64_t(*ws.ct.n_chunks) * p.Hv;  // (chunk, head) pairs, head fastest
 
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
   if (tid == 0) {
@@ -286,18 +283,41 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     tc::mbar_init(&ldbar[0], 1);
     tc::mbar_init(&ldbar[1], 1);
     tc::fence_mbar_init();
-    // ---- loads: workspace tile images by bulk copy ---------------------------------------------
-    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2);
-    tc::bulk_load(sm + lay::DVP, ws.dvp + ch * 8192, 16384, &ldbar[0]);
-    tc::bulk_load(sm + lay::ST, ws.hs + ch * 16384, 32768, &ldbar[0]);
-    tc::bulk_load(sm + lay::DHT, ws.dh + ch * 16384, 32768, &ldbar[0]);
-    tc::bulk_load(sm + lay::VPT, ws.vp + ch * 8192, 16384, &ldbar[0]);
   }
-  // ---- loads: the caller's q, k, v, dO rows (rows >= len zero-filled) --------------------------
+  // Phase-1 tiles of one (chunk, head) other than [K;Q]: workspace images by bulk copy (thread 0,
+  // counted on ldbar[0]) and the caller's v, dO rows by cp.async (rows >= len zero-filled).
+  auto issue_phase1 = [&](int64_t item) {
+    const int ci_ = int(item / p.Hv), h_ = int(item % p.Hv);
+    const int64_t ch_ = int64_t(ci_) * p.Hv + h_;
+    const int t0_ = ws.ct.tok0[ci_], L_ = ws.ct.len[ci_];
+    if (tid == 0) {
+      tc::fence_proxy_async();
+      tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2);
+      tc::bulk_load(sm + lay::DVP, ws.dvp + ch_ * 8192, 16384, &ldbar[0]);
+      tc::bulk_load(sm + lay::ST, ws.hs + ch_ * 16384, 32768, &ldbar[0]);
+      tc::bulk_load(sm + lay::DHT, ws.dh + ch_ * 16384, 32768, &ldbar[0]);
+      tc::bulk_load(sm + lay::VPT, ws.vp + ch_ * 8192, 16384, &ldbar[0]);
+    }
+    load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0_) * p.Hv + h_) * 128, vs, 64, L_, 256);
+    load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0_) * p.Hv + h_) * 128, vs, 64, L_, 256);
+    tc::cp_async_commit();
+  };
+  tc::fence_before_sync();
+  __syncthreads();  // barrier init and the TMEM address visible
+  tc::fence_after_sync();
+  if (int64_t(blockIdx.x) < n_items) issue_phase1(blockIdx.x);
+  const uint32_t tbase = tmem_base;
+  const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
+  const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
+  int it = 0;
+  for (int64_t item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+  const uint32_t ph = uint32_t(it & 1);  // parity of every barrier (each completes once per item)
+  const int ci = int(item / p.Hv), h = int(item % p.Hv);
+  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
+  const int64_t ch = int64_t(ci) * p.Hv + h;
+  // [K;Q] rows of this chunk (the previous item's final epilogue read this region)
   load_rows_sw128(sm + lay::KQ, 128, 0, static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
   load_rows_sw128(sm + lay::KQ, 128, 64, static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
-  load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 256);
-  load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, vs, 64, L, 256);
   tc::cp_async_commit();
   if (tid < 64) {
     const float* st = ws.stats + ch * 256;
@@ -309,10 +329,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   tc::cp_async_wait<0>();
   sync_for_mma();
-  tc::mbar_wait(&ldbar[0], 0, ws.err, 130);
-  const uint32_t tbase = tmem_base;
-  const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
-  const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
+  tc::mbar_wait(&ldbar[0], ph, ws.err, 130);
   if (tid == 0) {  // ---- G1 ----
     const uint32_t sta = tc::smem_u32(sm + lay::ST), dha = tc::smem_u32(sm + lay::DHT), doa = tc::smem_u32(sm + lay::DOT),
                    vpa = tc::smem_u32(sm + lay::VPT), dva = tc::smem_u32(sm + lay::DVP);
@@ -355,7 +372,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     for (int i = 0; i < 8; ++i) t += red[i];
     scal[0] = t;
   }
-  tc::mbar_wait(&bar[0], 0, ws.err, 131);
+  tc::mbar_wait(&bar[0], ph, ws.err, 131);
   tc::fence_after_sync();
   if (tid == 0) {  // T (tile image) over dS^T, which G1 and the dgamma sum have consumed
     tc::fence_proxy_async();
@@ -393,7 +410,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     *reinterpret_cast<uint4*>(sm + lay::BK + tc::sw128_offset(m, c8, 64)) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
   }
   sync_for_mma();
-  tc::mbar_wait(&ldbar[1], 0, ws.err, 136);
+  tc::mbar_wait(&ldbar[1], ph, ws.err, 136);
   const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
   if (tid == 0) {  // ---- G2 ----
     const uint32_t dva = tc::smem_u32(sm + lay::DVP), bva = tc::smem_u32(sm + lay::BV), bka = tc::smem_u32(sm + lay::BK);
@@ -419,7 +436,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     }
     tc::mma_commit(&bar[1]);
   }
-  tc::mbar_wait(&bar[1], 0, ws.err, 132);
+  tc::mbar_wait(&bar[1], ph, ws.err, 132);
   tc::fence_after_sync();
   // ---- E2 ------------------------------------------------------------------------------------
   {
@@ -453,7 +470,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
                    id_y, k0 > 0);
     tc::mma_commit(&bar[2]);
   }
-  tc::mbar_wait(&bar[2], 0, ws.err, 133);
+  tc::mbar_wait(&bar[2], ph, ws.err, 133);
   tc::fence_after_sync();
   {
     float v[32];
@@ -472,7 +489,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
     tc::mma_commit(&bar[3]);
   }
-  tc::mbar_wait(&bar[3], 0, ws.err, 134);
+  tc::mbar_wait(&bar[3], ph, ws.err, 134);
   tc::fence_after_sync();
   // ---- E4: P, Qm, R and the B operands of G5. dL' is an M = 128 accumulator of [Y; Y] T^T, so
   // lane 32 q4 + l holds token row i = (32 q4 + l) & 63; the thread takes 16 columns, cb..cb+15.
@@ -530,9 +547,10 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     dcum_acc[i] += a;
     dbeta_acc[i] += dbp[i] + dbp[64 + i] + dbp[128 + i] + dbp[192 + i];
   }
-  tc::mbar_wait(&bar[4], 0, ws.err, 135);
+  tc::mbar_wait(&bar[4], ph, ws.err, 135);
   tc::fence_after_sync();
   __syncthreads();  // region A (the phase-2 tiles) is free once G5 has completed
+  if (item + gridDim.x < n_items) issue_phase1(item + gridDim.x);  // next item's tiles, behind this epilogue
   // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j; q[i][r], k[i][r] read from the
   // [K;Q] tile (consecutive lanes read consecutive columns of one row: no bank conflicts) -----------
   float xr[32];
@@ -601,9 +619,16 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       const int64_t row = int64_t(p.Hk) * 128;
       store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
       store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
-    } else {  // per-value-head fp32 rows, staged for coalesced stores below
-      stage_cols32(reinterpret_cast<float*>(sm + lay::GQS), r, c0, gq);
-      stage_cols32(reinterpret_cast<float*>(sm + lay::GQS) + 8192, r, c0, gk);
+    } else {  // per-value-head fp32 rows, staged for coalesced 16-byte stores (dq, then dk)
+      const int64_t rs = int64_t(p.Hv) * 512;
+      float* stg = reinterpret_cast<float*>(sm + lay::GQS);
+      stage_cols32(stg, r, c0, gq);
+      __syncthreads();
+      copy_rows_out(ws.dqh + (int64_t(t0) * p.Hv + h) * 128, rs, stg, 512, L, 0, 256);
+      __syncthreads();
+      stage_cols32(stg, r, c0, gk);
+      __syncthreads();
+      copy_rows_out(ws.dkh + (int64_t(t0) * p.Hv + h) * 128, rs, stg, 512, L, 0, 256);
     }
   }
   // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------
@@ -629,13 +654,9 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     if (32 + l < L) dg[int64_t(t0 + 32 + l) * p.Hv + h] = float(hi);
   }
   if (tid < L && tid < 64) dbeta[int64_t(t0 + tid) * p.Hv + h] = __float2bfloat16_rn(dbeta_acc[tid]);
-  if (p.group > 1) {  // the staged rows are visible after the __syncthreads above
-    const int64_t rs = int64_t(p.Hv) * 512;
-    copy_rows_out(ws.dqh + (int64_t(t0) * p.Hv + h) * 128, rs, sm + lay::GQS, 512, L, 0, 256);
-    copy_rows_out(ws.dkh + (int64_t(t0) * p.Hv + h) * 128, rs, sm + lay::GQS + 32768, 512, L, 0, 256);
-  }
   tc::fence_before_sync();
-  __syncthreads();
+  __syncthreads();  // this item's TMEM and shared reads are done before the next item's MMAs and loads
+  }
   if (w == 0) tc::tmem_dealloc(tbase, 512);
 }
 
@@ -686,7 +707,11 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
     if ((rc = smem_attr_b(fast_chunk_bwd_kernel, kBChunkSmem))) return rc;
     {
       ProfScope ps_("gdn_fast_chunk_bwd", s);
-      fast_chunk_bwd_kernel<<<dim3(p.max_chunks, p.Hv), 256, kBChunkSmem, s>>>(
+      int dev = 0, sms = 148;
+      RB2_CUDA(cudaGetDevice(&dev), "gdn fast chunk bwd: device");
+      RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "gdn fast chunk bwd: SM count");
+      const int64_t items = int64_t(p.max_chunks) * p.Hv;
+      fast_chunk_bwd_kernel<<<unsigned(items < sms ? items : sms), 256, kBChunkSmem, s>>>(
           p, w, static_cast<const bf16*>(d_o), static_cast<bf16*>(dq), static_cast<bf16*>(dk), static_cast<bf16*>(dv), dg,
           static_cast<bf16*>(dbeta));
       RB2_CHECK_LAUNCH("gdn fast chunk bwd");
