@@ -18,6 +18,7 @@
 // epilogues or into the small bf16 T-derived operands, so the only added roundings are those of
 // T beta, W, U, q~, k~, A_qk, the per-chunk S^T operand and V' (measured ~2.4e-3 relative on o).
 #include "gdn_fast.cuh"
+#include "tmap.cuh"
 
 namespace rb2 {
 
@@ -61,7 +62,9 @@ using namespace fast;
 // ------------------------------------------------------------------------------------------------
 constexpr int kPrepSmem = 32768 + 16384 + 8192 + 8192 + 2 * 64 * 65 * 4 + 768 * 4 + 6 * 64 * 4 + 2048;
 
-__global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws) {
+__global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws, const __grid_constant__ CUtensorMap map_q,
+                                                        const __grid_constant__ CUtensorMap map_k,
+                                                        const __grid_constant__ CUtensorMap map_v) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* kq = sm;                  // [K;Q] K-major SW128, 128 rows x 128   (32 KB)
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   float* beta = rk + 64;
   float* ecum = beta + 64;
   float* gv = ecum + 64;
-  __shared__ uint64_t bar[2];
+  __shared__ uint64_t bar[3];  // [K;Q] K^T, U/W, loads
   __shared__ uint32_t tmem_base;
 
   const int ci = blockIdx.x, h = blockIdx.y;
@@ -86,30 +89,34 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws)
   const int r = 32 * (w & 3) + l, hh = w >> 2, c0 = 32 * hh;
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
   const int64_t ch = int64_t(ci) * p.Hv + h;
-  const bf16* q = static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128;
-  const bf16* k = static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128;
-  const bf16* v = static_cast<const bf16*>(p.v) + (int64_t(t0) * p.Hv + h) * 128;
-  const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
 
   if (w == 0) {
     tc::tmem_alloc(&tmem_base, 128);
     tc::tmem_relinquish();
   }
-  if (tid == 0) {
+  if (tid == 0) {  // k, q, v rows of the chunk by TMA
     tc::mbar_init(&bar[0], 1);
     tc::mbar_init(&bar[1], 1);
+    tc::mbar_init(&bar[2], 1);
     tc::fence_mbar_init();
+    tc::mbar_expect_tx(&bar[2], 3 * 16384);
+    tc::tma_rows128(kq, 16384, 0, &map_k, hk, t0, &bar[2]);
+    tc::tma_rows128(kq, 16384, 64, &map_q, hk, t0, &bar[2]);
+    tc::tma_rows128(vt, 8192, 0, &map_v, h, t0, &bar[2]);
   }
-  load_rows_sw128(kq, 128, 0, k, qs, 64, L, 256);
-  load_rows_sw128(kq, 128, 64, q, qs, 64, L, 256);
-  load_rows_sw128(vt, 64, 0, v, vs, 64, L, 256);
-  tc::cp_async_commit();
   if (tid < 64) {
     gv[tid] = tid < L ? p.g[int64_t(t0 + tid) * p.Hv + h] : 0.f;
     beta[tid] = tid < L ? __bfloat162float(static_cast<const bf16*>(p.beta)[int64_t(t0 + tid) * p.Hv + h]) : 0.f;
   }
-  tc::cp_async_wait<0>();
+  __syncthreads();  // barrier init visible
+  tc::mbar_wait(&bar[2], 0, ws.err, 100);
+  if (L < 64) {  // rows past the end of the sequence
+    tc::zero_rows_tail(kq, 16384, 0, L, 256);
+    tc::zero_rows_tail(kq, 16384, 64, L, 256);
+    tc::zero_rows_tail(vt, 8192, 0, L, 256);
+  }
   tc::fence_proxy_async();
+  tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
@@ -491,7 +498,11 @@ int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_
   if ((p.stages & 1) && p.max_chunks > 0) {
     if ((rc = smem_attr(fast_prep_kernel, kPrepSmem))) return rc;
     ProfScope ps_("gdn_fast_prep", s);
-    fast_prep_kernel<<<dim3(p.max_chunks, p.Hv), 256, kPrepSmem, s>>>(p, w);
+    CUtensorMap mq, mk, mv;
+    if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk)) ||
+        (rc = make_rows_map(&mv, p.v, p.tokens, p.Hv)))
+      return rc;
+    fast_prep_kernel<<<dim3(p.max_chunks, p.Hv), 256, kPrepSmem, s>>>(p, w, mq, mk, mv);
     RB2_CHECK_LAUNCH("gdn fast prep");
   }
   if (!(p.stages & 2)) return RB2_OK;

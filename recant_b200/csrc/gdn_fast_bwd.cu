@@ -15,6 +15,7 @@
 //       with P = dL * Gamma (strictly lower) and Qm = dA_qk * Gamma
 //   then the decay factors, beta, the cumulative gate (reverse cumsum -> dg) and the l2norm.
 #include "gdn_fast.cuh"
+#include "tmap.cuh"
 
 namespace rb2 {
 namespace {
@@ -59,17 +60,16 @@ __device__ __forceinline__ BwdStage bwd_stage(unsigned char* base, int stg) {
   return st;
 }
 
-// dO rows of the chunk (rows >= len zero-filled) by cp.async from all threads; the workspace tile
-// images (k~, q~, W, A_qk, cum) by bulk copies from thread 0, counted on `bar`.
-__device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& p, const FastWs& ws, const bf16* d_o,
-                                          int ci, int h, uint64_t* bar) {
+// Thread 0: the chunk's dO rows by TMA (rows past the sequence are zeroed after the wait) and the
+// workspace tile images (k~, q~, W, A_qk, cum) by bulk copies, counted on `bar`.
+__device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& p, const FastWs& ws,
+                                          const CUtensorMap* map_do, int ci, int h, uint64_t* bar) {
   const int64_t ch = int64_t(ci) * p.Hv + h;
-  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
-  load_rows_sw128(st.dot, 64, 0, d_o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, 64, L, 256);
-  tc::cp_async_commit();
+  const int t0 = ws.ct.tok0[ci];
   if (threadIdx.x == 0) {
     tc::fence_proxy_async();
-    tc::mbar_expect_tx(bar, 3 * 16384 + 8192 + 256);
+    tc::mbar_expect_tx(bar, 4 * 16384 + 8192 + 256);
+    tc::tma_rows128(st.dot, 8192, 0, map_do, h, t0, bar);
     tc::bulk_load(st.kt, ws.kt + ch * 8192, 16384, bar);
     tc::bulk_load(st.qt, ws.qt + ch * 8192, 16384, bar);
     tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
@@ -78,7 +78,7 @@ __device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& 
   }
 }
 
-__global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
+__global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, FastWs ws, const __grid_constant__ CUtensorMap map_do,
                                                                  const float* __restrict__ dhT, float* __restrict__ dh0) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     tc::fence_mbar_init();
   }
   const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
-  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, d_o, c1 - 1, h, &ldbar[0]);
+  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, &map_do, c1 - 1, h, &ldbar[0]);
   float dS[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
 #pragma unroll
@@ -115,13 +115,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     const int64_t ch = int64_t(ci) * p.Hv + h;
     const int stg = (c1 - 1 - ci) & 1;
     const BwdStage cur = bwd_stage(stages, stg);
-    if (ci - 1 >= c0) {
-      bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, d_o, ci - 1, h, &ldbar[stg ^ 1]);
-      tc::cp_async_wait<1>();
-    } else {
-      tc::cp_async_wait<0>();
-    }
+    if (ci - 1 >= c0) bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, &map_do, ci - 1, h, &ldbar[stg ^ 1]);
     tc::mbar_wait(&ldbar[stg], ((c1 - 1 - ci) >> 1) & 1, ws.err, 120);
+    const int Lc = ws.ct.len[ci];
+    if (Lc < 64) tc::zero_rows_tail(cur.dot, 8192, 0, Lc, 256);  // dO rows past the sequence
     {
       uint32_t pk[32];
 #pragma unroll
@@ -256,7 +253,11 @@ __device__ __forceinline__ void tmem_ld32f(uint32_t addr, float (&v)[32]) { tc::
 __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  bf16* __restrict__ dq, bf16* __restrict__ dk,
                                                                  bf16* __restrict__ dv, float* __restrict__ dg,
-                                                                 bf16* __restrict__ dbeta) {
+                                                                 bf16* __restrict__ dbeta,
+                                                                 const __grid_constant__ CUtensorMap map_q,
+                                                                 const __grid_constant__ CUtensorMap map_k,
+                                                                 const __grid_constant__ CUtensorMap map_v,
+                                                                 const __grid_constant__ CUtensorMap map_do) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   float* kkf = reinterpret_cast<float*>(sm + lay::KKF);
@@ -267,40 +268,37 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
         *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [4][64] */, *scal = vec + 768;
   float* red = reinterpret_cast<float*>(sm + lay::RED);  // [5][4][64]
   __shared__ uint64_t bar[5];
-  __shared__ uint64_t ldbar[2];   // bulk loads: workspace tile images, then T
+  __shared__ uint64_t ldbar[3];   // loads: phase-1 tiles (bulk + TMA), T, [K;Q] (TMA)
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int q4 = w & 3, hh = w >> 2, r = 32 * q4 + l, c0 = 32 * hh;
   const bool mrow = l < 16;            // this lane holds a row of an M=64 accumulator
   const int i64 = 16 * q4 + l;          // ... and it is token row i64
-  const int64_t qs = int64_t(p.Hk) * 128, vs = int64_t(p.Hv) * 128;
   const int64_t n_items = int64_t(*ws.ct.n_chunks) * p.Hv;  // (chunk, head) pairs, head fastest
 
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
   if (tid == 0) {
     for (int b = 0; b < 5; ++b) tc::mbar_init(&bar[b], 1);
-    tc::mbar_init(&ldbar[0], 1);
-    tc::mbar_init(&ldbar[1], 1);
+    for (int b = 0; b < 3; ++b) tc::mbar_init(&ldbar[b], 1);
     tc::fence_mbar_init();
   }
-  // Phase-1 tiles of one (chunk, head) other than [K;Q]: workspace images by bulk copy (thread 0,
-  // counted on ldbar[0]) and the caller's v, dO rows by cp.async (rows >= len zero-filled).
+  // Phase-1 tiles of one (chunk, head) other than [K;Q], issued by thread 0 on ldbar[0]: the
+  // workspace images by bulk copy and the caller's v, dO rows by TMA (rows past the sequence are
+  // zeroed after the wait).
   auto issue_phase1 = [&](int64_t item) {
+    if (tid != 0) return;
     const int ci_ = int(item / p.Hv), h_ = int(item % p.Hv);
     const int64_t ch_ = int64_t(ci_) * p.Hv + h_;
-    const int t0_ = ws.ct.tok0[ci_], L_ = ws.ct.len[ci_];
-    if (tid == 0) {
-      tc::fence_proxy_async();
-      tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2);
-      tc::bulk_load(sm + lay::DVP, ws.dvp + ch_ * 8192, 16384, &ldbar[0]);
-      tc::bulk_load(sm + lay::ST, ws.hs + ch_ * 16384, 32768, &ldbar[0]);
-      tc::bulk_load(sm + lay::DHT, ws.dh + ch_ * 16384, 32768, &ldbar[0]);
-      tc::bulk_load(sm + lay::VPT, ws.vp + ch_ * 8192, 16384, &ldbar[0]);
-    }
-    load_rows_sw128(sm + lay::VT, 64, 0, static_cast<const bf16*>(p.v) + (int64_t(t0_) * p.Hv + h_) * 128, vs, 64, L_, 256);
-    load_rows_sw128(sm + lay::DOT, 64, 0, d_o + (int64_t(t0_) * p.Hv + h_) * 128, vs, 64, L_, 256);
-    tc::cp_async_commit();
+    const int t0_ = ws.ct.tok0[ci_];
+    tc::fence_proxy_async();
+    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2 + 2 * 16384);
+    tc::bulk_load(sm + lay::DVP, ws.dvp + ch_ * 8192, 16384, &ldbar[0]);
+    tc::bulk_load(sm + lay::ST, ws.hs + ch_ * 16384, 32768, &ldbar[0]);
+    tc::bulk_load(sm + lay::DHT, ws.dh + ch_ * 16384, 32768, &ldbar[0]);
+    tc::bulk_load(sm + lay::VPT, ws.vp + ch_ * 8192, 16384, &ldbar[0]);
+    tc::tma_rows128(sm + lay::VT, 8192, 0, &map_v, h_, t0_, &ldbar[0]);
+    tc::tma_rows128(sm + lay::DOT, 8192, 0, &map_do, h_, t0_, &ldbar[0]);
   };
   tc::fence_before_sync();
   __syncthreads();  // barrier init and the TMEM address visible
@@ -315,10 +313,12 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   const int ci = int(item / p.Hv), h = int(item % p.Hv);
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
   const int64_t ch = int64_t(ci) * p.Hv + h;
-  // [K;Q] rows of this chunk (the previous item's final epilogue read this region)
-  load_rows_sw128(sm + lay::KQ, 128, 0, static_cast<const bf16*>(p.k) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
-  load_rows_sw128(sm + lay::KQ, 128, 64, static_cast<const bf16*>(p.q) + (int64_t(t0) * p.Hk + hk) * 128, qs, 64, L, 256);
-  tc::cp_async_commit();
+  if (tid == 0) {  // [K;Q] rows of this chunk by TMA (the previous item's final epilogue read this region)
+    tc::fence_proxy_async();
+    tc::mbar_expect_tx(&ldbar[2], 32768);
+    tc::tma_rows128(sm + lay::KQ, 16384, 0, &map_k, hk, t0, &ldbar[2]);
+    tc::tma_rows128(sm + lay::KQ, 16384, 64, &map_q, hk, t0, &ldbar[2]);
+  }
   if (tid < 64) {
     const float* st = ws.stats + ch * 256;
     cum[tid] = st[tid]; rq[tid] = st[64 + tid]; rk[tid] = st[128 + tid]; beta[tid] = st[192 + tid];
@@ -327,9 +327,15 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     dbeta_acc[tid] = 0.f;
     dcum_acc[tid] = 0.f;
   }
-  tc::cp_async_wait<0>();
-  sync_for_mma();
+  tc::mbar_wait(&ldbar[2], ph, ws.err, 137);
   tc::mbar_wait(&ldbar[0], ph, ws.err, 130);
+  if (L < 64) {  // rows past the end of the sequence: zero (TMA fills only past the tensor's end)
+    tc::zero_rows_tail(sm + lay::KQ, 16384, 0, L, 256);
+    tc::zero_rows_tail(sm + lay::KQ, 16384, 64, L, 256);
+    tc::zero_rows_tail(sm + lay::VT, 8192, 0, L, 256);
+    tc::zero_rows_tail(sm + lay::DOT, 8192, 0, L, 256);
+  }
+  sync_for_mma();
   if (tid == 0) {  // ---- G1 ----
     const uint32_t sta = tc::smem_u32(sm + lay::ST), dha = tc::smem_u32(sm + lay::DHT), doa = tc::smem_u32(sm + lay::DOT),
                    vpa = tc::smem_u32(sm + lay::VPT), dva = tc::smem_u32(sm + lay::DVP);
@@ -699,8 +705,9 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
   if ((p.stages & 1) && (rc = smem_attr_b(fast_state_bwd_kernel, kBStateSmem))) return rc;
   if (p.stages & 1) {
     ProfScope ps_("gdn_fast_state_bwd", s);
-    fast_state_bwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kBStateSmem, s>>>(p, w, static_cast<const bf16*>(d_o),
-                                                                                    dhT, dh0);
+    CUtensorMap mdo;
+    if ((rc = make_rows_map(&mdo, d_o, p.tokens, p.Hv))) return rc;
+    fast_state_bwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kBStateSmem, s>>>(p, w, mdo, dhT, dh0);
     RB2_CHECK_LAUNCH("gdn fast state bwd");
   }
   if ((p.stages & 2) && p.max_chunks > 0) {
@@ -711,9 +718,13 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
       RB2_CUDA(cudaGetDevice(&dev), "gdn fast chunk bwd: device");
       RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "gdn fast chunk bwd: SM count");
       const int64_t items = int64_t(p.max_chunks) * p.Hv;
+      CUtensorMap mq, mk, mv, mdo;
+      if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk)) ||
+          (rc = make_rows_map(&mv, p.v, p.tokens, p.Hv)) || (rc = make_rows_map(&mdo, d_o, p.tokens, p.Hv)))
+        return rc;
       fast_chunk_bwd_kernel<<<unsigned(items < sms ? items : sms), 256, kBChunkSmem, s>>>(
           p, w, static_cast<const bf16*>(d_o), static_cast<bf16*>(dq), static_cast<bf16*>(dk), static_cast<bf16*>(dv), dg,
-          static_cast<bf16*>(dbeta));
+          static_cast<bf16*>(dbeta), mq, mk, mv, mdo);
       RB2_CHECK_LAUNCH("gdn fast chunk bwd");
     }
     if (p.group > 1) {

@@ -13,10 +13,8 @@
 //              lane m%32 of every sub-partition, 32-bit column m/32, one byte per 16-element block)
 //              and one tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64);
 //   warps 2-5  epilogue: TMEM -> registers -> * gA gB -> fp32 or bf16 rows.
-#include <cuda.h>
-#include <cudaTypedefs.h>
 
-#include "tc.cuh"
+#include "tmap.cuh"
 
 namespace rb2 {
 namespace {
@@ -224,21 +222,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
   if (w == 1) tc::tmem_dealloc(tbase, 512);
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // 2-D byte tensor [rows][cols_bytes], box [box_rows][128 bytes], 128-byte swizzle.
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_bytes, int box_rows) {
-  auto fn = encode_fn();
+  auto fn = tmap_encoder();
   if (!fn) {
     set_error("nvfp4_gemm: cuTensorMapEncodeTiled unavailable");
     return RB2_ECUDA;
