@@ -259,6 +259,129 @@ def _timed(step, steps, stream, world, dev):
     return ms
 
 
+METRIC2 = "GDN block fwd+bwd tokens/s (config 2: hidden 4096, B2 T8192, Hk16 Hv32, NVFP4 + LoRA r16)"
+
+
+def run_config2(args, rank, world, local, dev):
+    """Config 2: the full GDN block (recant/model/layers.py:148-182) forward + backward on x [2, 8192,
+    4096] bf16 ~ N(0, 1): NVFP4 in_proj_qkv (8192 x 4096) and in_proj_z (4096 x 4096) from N(0, 0.02)
+    weights, bf16 in_proj_a / in_proj_b (N = 32), causal conv(4) + SiLU, gates, chunked GDN (Hk 16,
+    Hv 32), gated RMSNorm, NVFP4 out_proj (4096 x 4096); LoRA rank 16 (alpha 32) on qkv, z and out
+    with A ~ N(0, 1/r), B = 0. Gradients flow to the LoRA weights only (x needs none), so the in_proj
+    dgrad GEMMs are not run, as in the reference. Multi-GPU runs are replicas (no exchange)."""
+    import torch
+    import torch.distributed as dist
+
+    from recant_b200 import _lib as L
+    from recant_b200.block import GDNBlock
+
+    B, T, hidden, Hk, Hv = 2, 8192, 4096, 16, 32
+    gen = torch.Generator(device=dev).manual_seed(777 + rank)
+    blk = GDNBlock(hidden, Hk, Hv).to(dev)
+    for lin in blk.projections():
+        lin.load_weight(torch.randn(lin.out_features, lin.in_features, device=dev, generator=gen) * 0.02)
+    for lin in (blk.in_proj_qkv, blk.in_proj_z, blk.out_proj):
+        lin.add_lora(16, 32, dev)
+        with torch.no_grad():
+            lin.lora_A.copy_(torch.randn(lin.lora_A.shape, device=dev, generator=gen) * (1 / 16) ** 0.5)
+    with torch.no_grad():
+        blk.conv_weight.copy_((torch.randn(blk.conv_weight.shape, device=dev, generator=gen) * 0.4).to(torch.bfloat16))
+        blk.A_log.copy_(torch.log(torch.empty(Hv, device=dev).uniform_(1.0, 16.0, generator=gen)))
+        blk.dt_bias.zero_()
+    x = torch.randn(B, T, hidden, device=dev, generator=gen).to(torch.bfloat16)
+    dy = torch.randn(B, T, hidden, device=dev, generator=gen).to(torch.bfloat16)
+    loras = [p for lin in (blk.in_proj_qkv, blk.in_proj_z, blk.out_proj) for p in (lin.lora_A, lin.lora_B)]
+
+    def step(xin=x, dyin=dy):
+        for p in loras:
+            p.grad = None
+        blk(xin).backward(dyin)
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(local)
+    clocks.start()
+    prof = L.LaunchProfiler(capacity=64 * (args.steps + 1))
+    prof.start()
+    ms = _timed(step, args.steps, stream, world, dev)
+    records, dropped = prof.read()
+    clock_info = clocks.stop()
+    tokens = B * T
+    value = tokens * world / (ms / 1e3)
+
+    hx, hdy = x.cpu().pin_memory(), dy.cpu().pin_memory()
+    out_host = torch.empty(B, T, hidden, dtype=torch.bfloat16).pin_memory()
+    grads_host = [torch.empty(p.shape, dtype=torch.float32).pin_memory() for p in loras]
+
+    def e2e_step():
+        xd = hx.to(dev, non_blocking=True)
+        for p in loras:
+            p.grad = None
+        out = blk(xd)
+        out.backward(hdy.to(dev, non_blocking=True))
+        out_host.copy_(out.detach(), non_blocking=True)
+        for gh, p in zip(grads_host, loras):
+            gh.copy_(p.grad, non_blocking=True)
+
+    e2e_step()
+    ms_e2e = _timed(e2e_step, max(3, args.steps // 2), stream, world, dev)
+    h2d = hx.numel() * 2 + hdy.numel() * 2
+    d2h = out_host.numel() * 2 + sum(g.numel() * 4 for g in grads_host)
+
+    pk = peaks()
+    per_kernel = {}
+    for name, t in records:
+        a = per_kernel.setdefault(name, [0, 0.0])
+        a[0] += 1
+        a[1] += t
+    total_k = sum(v[1] for v in per_kernel.values()) or 1.0
+    kernels = {n: {"launches": v[0], "ms_total": round(v[1], 3), "share": round(v[1] / total_k, 3)}
+               for n, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][1])}
+    top = max(per_kernel, key=lambda n: per_kernel[n][1]) if per_kernel else None
+    roof = None
+    if top is not None:
+        launches, tot = per_kernel[top]
+        avg_s = tot / launches / 1e3
+        if top == "nvfp4_gemm":   # mean over the fprop qkv / z / out and the out dgrad GEMMs
+            flops = (2.0 * tokens * hidden * (blk.conv_dim + blk.value_dim + hidden + blk.value_dim)) / 4
+            peak = pk["bf16"] * FP4_PER_BF16
+        else:
+            flops, peak = KERNEL_FLOPS_PER_CH.get(top, 0) * (tokens // 64) * Hv, pk["bf16"]
+        achieved = flops / avg_s / 1e12
+        roof = {"kernel": top, "bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                "share_of_kernel_time": round(tot / total_k, 3), "avg_launch_ms": round(avg_s * 1e3, 4),
+                "peak_source": f"{pk['source']} bf16 burst (MEASURED_PEAKS.json)" +
+                               (" x4 for FP4" if top == "nvfp4_gemm" else "")}
+    f_gemm = 2.0 * tokens * hidden * (blk.conv_dim + blk.value_dim + hidden) + 2.0 * tokens * blk.value_dim * hidden
+    f_gdn = FLOP_PER_TOKEN_HEAD * tokens * Hv
+    t_roof = f_gdn / (pk["bf16"] * 1e12) + f_gemm / (pk["bf16"] * FP4_PER_BF16 * 1e12)
+    line = {
+        "metric": METRIC2, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2: GDN block fwd+bwd, x [2, 8192, 4096] bf16, NVFP4 in/out projections, "
+                               "LoRA r16 alpha32, grads to LoRA only", "global_batch": B * world, "seq_len": T,
+                   "parallelism": f"replicas x{world}", "l2": "activations exceed the 126 MB L2; no flush"},
+        "e2e": {"value": round(tokens * world / (ms_e2e / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": roof,
+        "path_roofline": {"flops_gdn": f_gdn, "flops_fp4_gemm": f_gemm, "t_roof_ms": round(t_roof * 1e3, 3),
+                          "frac": round(t_roof * 1e3 / ms, 4),
+                          "definition": "(GDN F / bf16 burst peak + GEMM F / (4 x bf16 peak)) / step time"},
+        "gpu_launches": len(records) + dropped,
+        "kernels": kernels,
+        "clocks": clock_info,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_config4(args, rank, world, local, dev):
     """Config 4: 8 stacked layers, each a chunked GDN whose values are the previous layer's output
     (v = x viewed as [1, T, Hv, d]) followed by an NVFP4 4096x4096 out_proj, on one sequence of
@@ -422,9 +545,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="config 1 only: batch B (default 4, the headline); smaller B for profiling captures")
-    ap.add_argument("--config", type=int, choices=[1, 3, 4], default=1,
-                    help="1: B4 T4096 replicas (the headline); 3: packed varlen, data-parallel by tokens; "
-                         "4: 8-layer GDN + NVFP4 out_proj stack on one T=131072 sequence, context-parallel")
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4], default=1,
+                    help="1: B4 T4096 replicas (the headline); 2: the full GDN block (NVFP4 + LoRA projections, "
+                         "conv, gates, gated norm), B2 T8192 hidden 4096; 3: packed varlen, data-parallel by "
+                         "tokens; 4: 8-layer GDN + NVFP4 out_proj stack on one T=131072 sequence, context-parallel")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -447,6 +571,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     if args.config == 4:
         return run_config4(args, rank, world, local, dev)
+    if args.config == 2:
+        return run_config2(args, rank, world, local, dev)
     c = CFG
     B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
     if args.batch is not None and args.config == 1:

@@ -121,6 +121,33 @@ RB2_API int rb2_gdn_state_fold(const float* M, const float* c, const float* s0, 
                                int transpose, int identity_init, float* states, float* final_out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Element-wise stages of the GDN block (recant/model/layers.py:148-182), bf16 activations:
+ *
+ * rb2_conv_silu_fwd: y = silu(bf16(causal depthwise conv1d(x, w))), x [B, T, C], w [C, K] (K = 4,
+ *   zero prefix; layers.py:157-168). The output channels go to y0 (all C when y1 = y2 = NULL) or are
+ *   split into y0 [B, T, s1], y1 [B, T, s2 - s1], y2 [B, T, C - s2] -- the block's q, k, v
+ *   (layers.py:169). rb2_conv_silu_bwd: dx from x, w and the output gradient (same split).
+ * rb2_gdn_gates_fwd: g = -exp(A_log[h]) softplus(a + dt_bias[h]) (fp32) and beta = sigmoid(b)
+ *   (bf16) over n = B*T*H entries (fused_ops.py:32-33, layers.py:154); _bwd gives da, db.
+ * rb2_gated_rmsnorm_fwd: per row of dim = 128, y = bf16(w * bf16(x rsqrt(mean x^2 + eps))) *
+ *   silu(z) (fused_ops.py:11-16), rstd [rows] saved for rb2_gated_rmsnorm_bwd (dx, dz).
+ * The block's conv, gate and norm weights are frozen (the reference trains LoRA only), so only
+ * input gradients are produced.
+ * ------------------------------------------------------------------------------------------- */
+RB2_API int rb2_conv_silu_fwd(const void* x, const void* w, int B, int T, int C, int K, void* y0, void* y1,
+                              void* y2, int s1, int s2, void* stream);
+RB2_API int rb2_conv_silu_bwd(const void* x, const void* w, const void* dy0, const void* dy1, const void* dy2,
+                              int s1, int s2, int B, int T, int C, int K, void* dx, void* stream);
+RB2_API int rb2_gdn_gates_fwd(const void* a, const void* b, const float* A_log, const float* dt_bias, int64_t n,
+                              int H, float* g, void* beta, void* stream);
+RB2_API int rb2_gdn_gates_bwd(const void* a, const void* beta, const float* A_log, const float* dt_bias,
+                              const float* dg, const void* dbeta, int64_t n, int H, void* da, void* db, void* stream);
+RB2_API int rb2_gated_rmsnorm_fwd(const void* x, const void* z, const float* w, int64_t rows, int dim, float eps,
+                                  void* y, float* rstd, void* stream);
+RB2_API int rb2_gated_rmsnorm_bwd(const void* x, const void* z, const float* w, const float* rstd, const void* dout,
+                                  int64_t rows, int dim, void* dx, void* dz, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * NVFP4 quantizer: codes/scales/gscale of quantize(rht(x)) (use_rht=1) or quantize(x),
  * bit-exact with recant/model/nvfp4.py:23-31,59-91 for round-to-nearest; stochastic=1 is the
  * unbiased rounding of nvfp4.py:62-68 driven by a Philox-4x32-10 stream keyed by `seed`.

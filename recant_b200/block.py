@@ -1,0 +1,291 @@
+"""The GDN block on B200: recant/model/layers.py:148-182 (``GatedDeltaNet``) with the reference's
+parameter names, built from this package's kernels.
+
+x [B, T, hidden] bf16 ->
+  qkv, z      = NVFP4 in_proj_qkv / in_proj_z (+ LoRA), one shared activation quantize
+                (layers.py:152, grouped_linear layers.py:72-97; QLinear layers.py:36-70)
+  beta, a     = sigmoid(in_proj_b(x)), in_proj_a(x): bf16 dense, N = Hv < 256, never quantized
+                (layers.py:154-155, 47-48)
+  conv        = silu(causal depthwise conv1d, kernel 4, zero prefix)       (layers.py:157-168)
+  q, k, v     = split(conv) into [Hk*128, Hk*128, Hv*128]                  (layers.py:169-172)
+  g           = -exp(A_log) softplus(a + dt_bias)                          (fused_ops.py:32-33)
+  core        = chunked GDN (``gdn_b200``; Hk < Hv handled without repeat_interleave)
+  y           = out_proj(RMSNormGated(core, z))  (NVFP4 + LoRA)            (layers.py:23-34,181)
+
+Kernels: ``rb2_conv_silu_*``, ``rb2_gdn_gates_*``, ``rb2_gated_rmsnorm_*`` (csrc/gdn_block.cu), the
+NVFP4 quantizer and GEMM, the GDN op; the LoRA products (rank 16) and the N = Hv projections are
+plain GEMMs through torch (cuBLAS). Frozen weights get no gradients; LoRA A and B do.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from . import _lib as L
+from . import nvfp4 as N
+from .gdn import _stream, gdn_b200
+
+
+def _p(t):
+    return L.ptr(t)
+
+
+class _ConvSiLU(torch.autograd.Function):
+    """Returns the conv output split into contiguous [B, T, s1], [B, T, s2 - s1], [B, T, C - s2]
+    tensors (q, k, v of the block) written directly by the kernel."""
+
+    @staticmethod
+    def forward(ctx, x, w, s1, s2):
+        B, T, C = x.shape
+        x = x.contiguous()
+        w4 = w.reshape(C, 4).to(torch.bfloat16).contiguous()
+        outs = [torch.empty(B, T, n, dtype=torch.bfloat16, device=x.device) for n in (s1, s2 - s1, C - s2)]
+        L.check(L.lib().rb2_conv_silu_fwd(_p(x), _p(w4), B, T, C, 4, *[_p(o) for o in outs], s1, s2,
+                                          _stream(x.device)), "conv_silu_fwd")
+        ctx.save_for_backward(x, w4)
+        ctx.s1, ctx.s2 = s1, s2
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *dys):
+        x, w4 = ctx.saved_tensors
+        B, T, C = x.shape
+        widths = (ctx.s1, ctx.s2 - ctx.s1, C - ctx.s2)
+        dys = [torch.zeros(B, T, n, dtype=torch.bfloat16, device=x.device) if d is None
+               else d.to(torch.bfloat16).contiguous() for d, n in zip(dys, widths)]
+        dx = torch.empty_like(x)
+        L.check(L.lib().rb2_conv_silu_bwd(_p(x), _p(w4), *[_p(d) for d in dys], ctx.s1, ctx.s2, B, T, C, 4, _p(dx),
+                                          _stream(x.device)), "conv_silu_bwd")
+        return dx, None, None, None
+
+
+class _Gates(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, A_log, dt_bias):
+        H = a.shape[-1]
+        a, b = a.to(torch.bfloat16).contiguous(), b.to(torch.bfloat16).contiguous()
+        al, db_ = A_log.float().contiguous(), dt_bias.float().contiguous()
+        g = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+        beta = torch.empty_like(b)
+        L.check(L.lib().rb2_gdn_gates_fwd(_p(a), _p(b), _p(al), _p(db_), a.numel(), H, _p(g), _p(beta),
+                                          _stream(a.device)), "gdn_gates_fwd")
+        ctx.save_for_backward(a, beta, al, db_)
+        return g, beta
+
+    @staticmethod
+    def backward(ctx, dg, dbeta):
+        a, beta, al, db_ = ctx.saved_tensors
+        H = a.shape[-1]
+        dg = torch.zeros_like(a, dtype=torch.float32) if dg is None else dg.float().contiguous()
+        dbeta = torch.zeros_like(beta) if dbeta is None else dbeta.to(torch.bfloat16).contiguous()
+        da, db = torch.empty_like(a), torch.empty_like(beta)
+        L.check(L.lib().rb2_gdn_gates_bwd(_p(a), _p(beta), _p(al), _p(db_), _p(dg), _p(dbeta), a.numel(), H, _p(da),
+                                          _p(db), _stream(a.device)), "gdn_gates_bwd")
+        return da, db, None, None
+
+
+class _GatedRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, z, w, eps):
+        x, z = x.to(torch.bfloat16).contiguous(), z.to(torch.bfloat16).contiguous()
+        wf = w.float().contiguous()
+        rows = x.numel() // 128
+        y = torch.empty_like(x)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        L.check(L.lib().rb2_gated_rmsnorm_fwd(_p(x), _p(z), _p(wf), rows, 128, float(eps), _p(y), _p(rstd),
+                                              _stream(x.device)), "gated_rmsnorm_fwd")
+        ctx.save_for_backward(x, z, wf, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, z, wf, rstd = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16).contiguous()
+        dx, dz = torch.empty_like(x), torch.empty_like(z)
+        L.check(L.lib().rb2_gated_rmsnorm_bwd(_p(x), _p(z), _p(wf), _p(rstd), _p(dy), x.numel() // 128, 128, _p(dx),
+                                              _p(dz), _stream(x.device)), "gated_rmsnorm_bwd")
+        return dx, dz, None, None
+
+
+def conv_silu(x, weight, s1, s2):
+    """silu(causal depthwise conv1d(x, weight [C, 1, 4])), x [B, T, C] bf16 (layers.py:157-168), split
+    into channels [0, s1), [s1, s2), [s2, C) as three contiguous tensors (layers.py:169)."""
+    return _ConvSiLU.apply(x, weight, s1, s2)
+
+
+def gdn_gates(a, b, A_log, dt_bias):
+    """(g, beta) = (-exp(A_log) softplus(a + dt_bias) fp32, sigmoid(b))  (fused_ops.py:32-33, layers.py:154)."""
+    return _Gates.apply(a, b, A_log, dt_bias)
+
+
+def gated_rmsnorm(x, z, weight, eps=1e-6):
+    """RMSNormGated over rows of 128 (fused_ops.py:11-16, layers.py:23-34)."""
+    return _GatedRMSNorm.apply(x, z, weight, eps)
+
+
+class _FP4Group(torch.autograd.Function):
+    """y_i = x . W_i^T for NVFP4 weights sharing one quantization of x (RN); backward: dx = sum_i
+    Q(rht(dy_i)) . dgrad_i^T with stochastic rounding, as FP4Linear (nvfp4.py:151-170)."""
+
+    @staticmethod
+    def forward(ctx, x, stochastic, *weights):
+        x2 = x.reshape(-1, weights[0].in_features)
+        a = N.quantize_activation(x2, weights[0].use_rht)
+        ys = tuple(N._gemm_to(a, w.fprop, x.dtype).reshape(*x.shape[:-1], w.out_features) for w in weights)
+        ctx.weights, ctx.stochastic, ctx.xshape = weights, stochastic, x.shape
+        return ys
+
+    @staticmethod
+    def backward(ctx, *dys):
+        dx = None
+        for w, dy in zip(ctx.weights, dys):
+            if dy is None:
+                continue
+            d = N.quantize_activation(dy.reshape(-1, w.out_features), w.use_rht, stochastic=ctx.stochastic)
+            part = N._gemm_to(d, w.dgrad, dy.dtype)
+            dx = part if dx is None else dx + part
+        return (None if dx is None else dx.reshape(ctx.xshape), None, *([None] * len(ctx.weights)))
+
+
+class QLinear(nn.Module):
+    """layers.py:36-70: NVFP4 base when quantizable (in, out % 16 == 0 and out >= 256), else a bf16
+    dense weight; optional LoRA y += (alpha / r) (x A^T) B^T with fp32 A [r, in], B [out, r]."""
+
+    def __init__(self, in_f, out_f):
+        super().__init__()
+        self.in_features, self.out_features = in_f, out_f
+        self.weight = None          # bf16 dense weight when not quantized
+        self.fp4 = None
+        self.lora_A = self.lora_B = None
+        self.lora_scale = 1.0
+        self.stochastic_backward = True
+
+    @property
+    def quantizable(self):
+        return self.in_features % 16 == 0 and self.out_features % 16 == 0 and self.out_features >= 256
+
+    def load_weight(self, w, use_rht=True):
+        if self.quantizable:
+            self.fp4 = N.quantize_weight(w.detach(), use_rht)
+            self.weight = None
+        else:
+            self.weight = w.detach().to(torch.bfloat16).contiguous()
+
+    def add_lora(self, r, alpha, device):
+        self.lora_A = nn.Parameter(torch.empty(r, self.in_features, device=device, dtype=torch.float32))
+        nn.init.kaiming_uniform_(self.lora_A, a=math.sqrt(5))
+        self.lora_B = nn.Parameter(torch.zeros(self.out_features, r, device=device, dtype=torch.float32))
+        self.lora_scale = alpha / r
+
+    def lora(self, x, y, grouped=False):
+        """y + (alpha / r) (x A^T) B^T: three bf16 ops as QLinear.forward (layers.py:65-70), or one
+        addmm as grouped_linear's default path (layers.py:86-97)."""
+        if self.lora_A is None:
+            return y
+        h = x @ self.lora_A.to(x.dtype).t()
+        if grouped:
+            o = torch.addmm(y.reshape(-1, y.shape[-1]), h.reshape(-1, h.shape[-1]), self.lora_B.to(x.dtype).t(),
+                            alpha=self.lora_scale)
+            return o.reshape(*y.shape)
+        return y + (h @ self.lora_B.to(x.dtype).t()) * self.lora_scale
+
+    def forward(self, x):
+        if self.fp4 is not None:
+            (y,) = _FP4Group.apply(x, self.stochastic_backward, self.fp4)
+        else:
+            y = x @ self.weight.t()
+        return self.lora(x, y)
+
+
+def grouped_linear(x, lins):
+    """layers.py:72-97 with the activation quantized once for all NVFP4 members."""
+    fp4 = [l for l in lins if l.fp4 is not None]
+    outs = {}
+    if fp4:
+        ys = _FP4Group.apply(x, fp4[0].stochastic_backward, *[l.fp4 for l in fp4])
+        outs = {id(l): y for l, y in zip(fp4, ys)}
+    return [l.lora(x, outs[id(l)] if id(l) in outs else x @ l.weight.t(), grouped=True) for l in lins]
+
+
+class GDNBlock(nn.Module):
+    """``GatedDeltaNet`` (layers.py:133-182) on B200. Parameters keep the reference's names;
+    :meth:`from_reference` copies a reference block's weights (and LoRA) into it."""
+
+    def __init__(self, hidden, Hk, Hv, d=128, conv_k=4, eps=1e-6):
+        super().__init__()
+        if d != 128 or conv_k != 4:
+            raise ValueError("recant_b200.GDNBlock: head dim 128 and conv kernel 4 only")
+        self.hidden, self.Hk, self.Hv, self.d, self.eps = hidden, Hk, Hv, d, eps
+        self.key_dim, self.value_dim = Hk * d, Hv * d
+        self.conv_dim = 2 * self.key_dim + self.value_dim
+        self.in_proj_qkv = QLinear(hidden, self.conv_dim)
+        self.in_proj_z = QLinear(hidden, self.value_dim)
+        self.in_proj_b = QLinear(hidden, Hv)
+        self.in_proj_a = QLinear(hidden, Hv)
+        self.out_proj = QLinear(self.value_dim, hidden)
+        self.register_buffer("conv_weight", torch.zeros(self.conv_dim, 1, conv_k, dtype=torch.bfloat16))
+        self.register_buffer("dt_bias", torch.ones(Hv))
+        self.register_buffer("A_log", torch.zeros(Hv))
+        self.register_buffer("norm_weight", torch.ones(d))
+
+    def projections(self):
+        return [self.in_proj_qkv, self.in_proj_z, self.in_proj_b, self.in_proj_a, self.out_proj]
+
+    def set_stochastic_backward(self, on: bool):
+        for l in self.projections():
+            l.stochastic_backward = on
+
+    @classmethod
+    def from_reference(cls, ref, device="cuda"):
+        """Build from a reference ``GatedDeltaNet`` (unquantized weights, optional LoRA)."""
+        c = ref.c
+        blk = cls(c.hidden_size, c.linear_num_key_heads, c.linear_num_value_heads, c.linear_value_head_dim,
+                  c.linear_conv_kernel_dim, c.rms_norm_eps).to(device)
+        for name in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+            src, dst = getattr(ref, name), getattr(blk, name)
+            if src.weight is None:
+                raise ValueError("from_reference needs the reference block's unquantized weights")
+            dst.load_weight(src.weight.data.to(device))
+            if src.lora_A is not None:
+                dst.lora_A = nn.Parameter(src.lora_A.detach().float().to(device).clone())
+                dst.lora_B = nn.Parameter(src.lora_B.detach().float().to(device).clone())
+                dst.lora_scale = src.lora_scale
+        blk.conv_weight.copy_(ref.conv1d.weight.detach().to(device, torch.bfloat16))
+        blk.dt_bias.copy_(ref.dt_bias.detach().float())
+        blk.A_log.copy_(ref.A_log.detach().float())
+        blk.norm_weight.copy_(ref.norm.weight.detach().float())
+        return blk
+
+    @classmethod
+    def from_state(cls, sd, hidden, Hk, Hv, lora_scale=2.0, device="cuda"):
+        """Build from reference-named tensors: ``<proj>.weight`` (unquantized), optional
+        ``<proj>.lora_A`` / ``.lora_B``, ``conv1d.weight``, ``dt_bias``, ``A_log``, ``norm.weight``."""
+        blk = cls(hidden, Hk, Hv).to(device)
+        for name in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+            dst = getattr(blk, name)
+            dst.load_weight(sd[name + ".weight"].to(device, torch.bfloat16))
+            if name + ".lora_A" in sd:
+                dst.lora_A = nn.Parameter(sd[name + ".lora_A"].float().to(device).clone())
+                dst.lora_B = nn.Parameter(sd[name + ".lora_B"].float().to(device).clone())
+                dst.lora_scale = lora_scale
+        blk.conv_weight.copy_(sd["conv1d.weight"].to(device, torch.bfloat16))
+        blk.dt_bias.copy_(sd["dt_bias"].to(device, torch.bfloat16).float())
+        blk.A_log.copy_(sd["A_log"].to(device, torch.bfloat16).float())
+        blk.norm_weight.copy_(sd["norm.weight"].to(device, torch.bfloat16).float())
+        return blk
+
+    def forward(self, x):
+        B, T, _ = x.shape
+        d = self.d
+        qkv, z = grouped_linear(x, [self.in_proj_qkv, self.in_proj_z])
+        b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
+        q, k, v = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim)
+        q = q.view(B, T, self.Hk, d)
+        k = k.view(B, T, self.Hk, d)
+        v = v.view(B, T, self.Hv, d)
+        g, beta = gdn_gates(a, b_lin, self.A_log, self.dt_bias)
+        core, _ = gdn_b200(q, k, v, g, beta)
+        y = gated_rmsnorm(core.reshape(-1, d), z.reshape(-1, d), self.norm_weight, self.eps)
+        return self.out_proj(y.reshape(B, T, -1))

@@ -1,0 +1,384 @@
+// Element-wise kernels of the GDN block around the chunked op (recant/model/layers.py:148-182):
+//   causal depthwise conv (kernel 4, zero prefix) + SiLU over the qkv channels   layers.py:157-168
+//   gates g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)               fused_ops.py:32-33,
+//                                                                                 layers.py:154
+//   gated RMSNorm y = w * bf16(x rsqrt(mean x^2 + eps)) * silu(z) per 128-row     fused_ops.py:11-16
+// with the backward of each (the block's conv, gate and norm weights are frozen: only input
+// gradients). All are HBM-bound: 16-byte loads and stores, fp32 arithmetic, the reference's
+// roundings to bf16 where its eager code casts.
+#include "common.cuh"
+
+namespace rb2 {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return x * sigm(x); }
+
+__device__ __forceinline__ void load8(const bf16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void store8(bf16* p, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+constexpr int kConvK = 4;
+
+// The conv's C channels, written to (or their gradients read from) up to three contiguous tensors:
+// channels [0, s1) -> p0 (width s1), [s1, s2) -> p1, [s2, C) -> p2 (s1 = s2 = C: one tensor).
+struct Split {
+  bf16* p[3];
+  int s1, s2, C;
+  __device__ __forceinline__ bf16* at(int64_t tok, int c) const {
+    if (c < s1) return p[0] + tok * s1 + c;
+    if (c < s2) return p[1] + tok * (s2 - s1) + (c - s1);
+    return p[2] + tok * (C - s2) + (c - s2);
+  }
+};
+constexpr int kTStrip = 32;  // tokens per thread
+
+// y[b, t, c] = bf16(silu(bf16(sum_j w[c, j] x[b, t - 3 + j, c]))); one thread: 8 channels x 32 tokens
+__global__ void __launch_bounds__(256) conv_silu_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                            int B, int T, int C, Split y) {
+  const int c8 = C / 8, strips = (T + kTStrip - 1) / kTStrip;
+  const int64_t n = int64_t(B) * strips * c8;
+  for (int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * 256) {
+    const int cc = int(idx % c8), s = int((idx / c8) % strips), b = int(idx / (int64_t(c8) * strips));
+    const int c = cc * 8, t0 = s * kTStrip;
+    float wt[kConvK][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint2 u = *reinterpret_cast<const uint2*>(w + int64_t(c + i) * kConvK);
+      wt[0][i] = __uint_as_float(u.x << 16); wt[1][i] = __uint_as_float(u.x & 0xffff0000u);
+      wt[2][i] = __uint_as_float(u.y << 16); wt[3][i] = __uint_as_float(u.y & 0xffff0000u);
+    }
+    const bf16* xb = x + int64_t(b) * T * C + c;
+    float win[kConvK - 1][8];
+#pragma unroll
+    for (int j = 0; j < kConvK - 1; ++j) {
+      const int t = t0 - (kConvK - 1) + j;
+      if (t >= 0) load8(xb + int64_t(t) * C, win[j]);
+      else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
+      }
+    }
+    const int t1 = min(T, t0 + kTStrip);
+    for (int t = t0; t < t1; ++t) {
+      float cur[8], out[8];
+      load8(xb + int64_t(t) * C, cur);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float a = wt[0][i] * win[0][i];
+        a = fmaf(wt[1][i], win[1][i], a);
+        a = fmaf(wt[2][i], win[2][i], a);
+        a = fmaf(wt[3][i], cur[i], a);
+        out[i] = silu(bfr(a));
+        win[0][i] = win[1][i]; win[1][i] = win[2][i]; win[2][i] = cur[i];
+      }
+      store8(y.at(int64_t(b) * T + t, c), out);
+    }
+  }
+}
+
+// du[t] = dy[t] silu'(u[t]) (u recomputed, bf16 as in the forward); dx[t] = sum_j w[c, j] du[t + 3 - j]
+__global__ void __launch_bounds__(256) conv_silu_bwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                            Split dy, int B, int T, int C, bf16* __restrict__ dx) {
+  const int c8 = C / 8, strips = (T + kTStrip - 1) / kTStrip;
+  const int64_t n = int64_t(B) * strips * c8;
+  for (int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * 256) {
+    const int cc = int(idx % c8), s = int((idx / c8) % strips), b = int(idx / (int64_t(c8) * strips));
+    const int c = cc * 8, t0 = s * kTStrip;
+    float wt[kConvK][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint2 u = *reinterpret_cast<const uint2*>(w + int64_t(c + i) * kConvK);
+      wt[0][i] = __uint_as_float(u.x << 16); wt[1][i] = __uint_as_float(u.x & 0xffff0000u);
+      wt[2][i] = __uint_as_float(u.y << 16); wt[3][i] = __uint_as_float(u.y & 0xffff0000u);
+    }
+    const bf16* xb = x + int64_t(b) * T * C + c;
+    // du at t needs x[t-3 .. t]; dx at t needs du[t .. t+3]: walk t' = t0 .. t1+2, keeping x and du windows
+    float xw[kConvK - 1][8], dw[kConvK - 1][8];  // x[t'-3..t'-1], du[t'-3..t'-1]
+#pragma unroll
+    for (int j = 0; j < kConvK - 1; ++j) {
+      const int t = t0 - (kConvK - 1) + j;
+      if (t >= 0) load8(xb + int64_t(t) * C, xw[j]);
+      else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xw[j][i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dw[j][i] = 0.f;
+    }
+    const int t1 = min(T, t0 + kTStrip);
+    // first bring the x window to t0 (du for t < t0 is not needed)
+    for (int tp = t0; tp < t1 + kConvK - 1; ++tp) {
+      float xc[8], du[8];
+      if (tp < T) {
+        load8(xb + int64_t(tp) * C, xc);
+        float g[8];
+        load8(dy.at(int64_t(b) * T + tp, c), g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = wt[0][i] * xw[0][i];
+          a = fmaf(wt[1][i], xw[1][i], a);
+          a = fmaf(wt[2][i], xw[2][i], a);
+          a = fmaf(wt[3][i], xc[i], a);
+          const float u = bfr(a), sg = sigm(u);
+          du[i] = bfr(g[i] * sg * (1.f + u * (1.f - sg)));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { xc[i] = 0.f; du[i] = 0.f; }
+      }
+      const int t = tp - (kConvK - 1);  // dx[t] = w0 du[t+3] + w1 du[t+2] + w2 du[t+1] + w3 du[t]
+      if (t >= t0) {
+        float out[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = wt[0][i] * du[i];
+          a = fmaf(wt[1][i], dw[2][i], a);
+          a = fmaf(wt[2][i], dw[1][i], a);
+          a = fmaf(wt[3][i], dw[0][i], a);
+          out[i] = a;
+        }
+        store8(dx + (int64_t(b) * T + t) * C + c, out);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xw[0][i] = xw[1][i]; xw[1][i] = xw[2][i]; xw[2][i] = xc[i];
+        dw[0][i] = dw[1][i]; dw[1][i] = dw[2][i]; dw[2][i] = du[i];
+      }
+    }
+  }
+}
+
+// g = -exp(A_log[h]) softplus(a + dt_bias[h]) (fp32), beta = bf16(sigmoid(b)); softplus as torch
+// (threshold 20: x > 20 -> x)
+__global__ void __launch_bounds__(256) gates_fwd_kernel(const bf16* __restrict__ a, const bf16* __restrict__ b,
+                                                        const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                                                        int64_t n, int H, float* __restrict__ g, bf16* __restrict__ beta) {
+  for (int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x; i < n; i += int64_t(gridDim.x) * 256) {
+    const int h = int(i % H);
+    const float x = __bfloat162float(a[i]) + dt_bias[h];
+    const float sp = x > 20.f ? x : log1pf(expf(x));
+    g[i] = -expf(A_log[h]) * sp;
+    beta[i] = __float2bfloat16_rn(1.f / (1.f + expf(-__bfloat162float(b[i]))));
+  }
+}
+// da = dg (-exp(A_log)) sigmoid(a + dt_bias); db = dbeta beta (1 - beta) with the forward's bf16 beta
+__global__ void __launch_bounds__(256) gates_bwd_kernel(const bf16* __restrict__ a, const bf16* __restrict__ beta,
+                                                        const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                                                        const float* __restrict__ dg, const bf16* __restrict__ dbeta,
+                                                        int64_t n, int H, bf16* __restrict__ da, bf16* __restrict__ db) {
+  for (int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x; i < n; i += int64_t(gridDim.x) * 256) {
+    const int h = int(i % H);
+    const float x = __bfloat162float(a[i]) + dt_bias[h];
+    const float ds = x > 20.f ? 1.f : 1.f / (1.f + expf(-x));
+    da[i] = __float2bfloat16_rn(dg[i] * -expf(A_log[h]) * ds);
+    const float bt = __bfloat162float(beta[i]);
+    db[i] = __float2bfloat16_rn(__bfloat162float(dbeta[i]) * bt * (1.f - bt));
+  }
+}
+
+// one warp per row of 128 (4 per lane); rstd kept for the backward
+__global__ void __launch_bounds__(256) gated_norm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z,
+                                                             const float* __restrict__ w, int64_t rows, float eps,
+                                                             bf16* __restrict__ y, float* __restrict__ rstd) {
+  const int lane = threadIdx.x & 31;
+  const float4 wv = reinterpret_cast<const float4*>(w)[lane];
+  for (int64_t row = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5; row < rows; row += int64_t(gridDim.x) * 8) {
+    const uint2 ux = reinterpret_cast<const uint2*>(x + row * 128)[lane];
+    const uint2 uz = reinterpret_cast<const uint2*>(z + row * 128)[lane];
+    const float xv[4] = {__uint_as_float(ux.x << 16), __uint_as_float(ux.x & 0xffff0000u),
+                         __uint_as_float(ux.y << 16), __uint_as_float(ux.y & 0xffff0000u)};
+    const float zv[4] = {__uint_as_float(uz.x << 16), __uint_as_float(uz.x & 0xffff0000u),
+                         __uint_as_float(uz.y << 16), __uint_as_float(uz.y & 0xffff0000u)};
+    float ss = xv[0] * xv[0] + xv[1] * xv[1] + xv[2] * xv[2] + xv[3] * xv[3];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * (1.f / 128.f) + eps);
+    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = bfr(wa[i] * bfr(xv[i] * r)) * silu(zv[i]);
+    const __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]), p1 = __floats2bfloat162_rn(o[2], o[3]);
+    reinterpret_cast<uint2*>(y + row * 128)[lane] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1));
+    if (lane == 0 && rstd) rstd[row] = r;
+  }
+}
+// out = bf16(w n) silu(z), n = bf16(x r): dz = dout bf16(w n) silu'(z); dn = dout w silu(z);
+// dx = r (dn - xh mean(dn xh)), xh = x r
+__global__ void __launch_bounds__(256) gated_norm_bwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z,
+                                                             const float* __restrict__ w, const float* __restrict__ rstd,
+                                                             const bf16* __restrict__ dout, int64_t rows,
+                                                             bf16* __restrict__ dx, bf16* __restrict__ dz) {
+  const int lane = threadIdx.x & 31;
+  const float4 wv = reinterpret_cast<const float4*>(w)[lane];
+  const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+  for (int64_t row = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5; row < rows; row += int64_t(gridDim.x) * 8) {
+    const uint2 ux = reinterpret_cast<const uint2*>(x + row * 128)[lane];
+    const uint2 uz = reinterpret_cast<const uint2*>(z + row * 128)[lane];
+    const uint2 ud = reinterpret_cast<const uint2*>(dout + row * 128)[lane];
+    const float xv[4] = {__uint_as_float(ux.x << 16), __uint_as_float(ux.x & 0xffff0000u),
+                         __uint_as_float(ux.y << 16), __uint_as_float(ux.y & 0xffff0000u)};
+    const float zv[4] = {__uint_as_float(uz.x << 16), __uint_as_float(uz.x & 0xffff0000u),
+                         __uint_as_float(uz.y << 16), __uint_as_float(uz.y & 0xffff0000u)};
+    const float gv[4] = {__uint_as_float(ud.x << 16), __uint_as_float(ud.x & 0xffff0000u),
+                         __uint_as_float(ud.y << 16), __uint_as_float(ud.y & 0xffff0000u)};
+    const float r = rstd[row];
+    float dn[4], dzv[4], dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float s = sigm(zv[i]);
+      const float wn = bfr(wa[i] * bfr(xv[i] * r));
+      dzv[i] = gv[i] * wn * s * (1.f + zv[i] * (1.f - s));
+      dn[i] = gv[i] * wa[i] * zv[i] * s;
+      dot += dn[i] * xv[i] * r;
+    }
+    dot = warp_sum(dot) * (1.f / 128.f);
+    float dxv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dxv[i] = r * (dn[i] - xv[i] * r * dot);
+    const __nv_bfloat162 a0 = __floats2bfloat162_rn(dxv[0], dxv[1]), a1 = __floats2bfloat162_rn(dxv[2], dxv[3]);
+    const __nv_bfloat162 b0 = __floats2bfloat162_rn(dzv[0], dzv[1]), b1 = __floats2bfloat162_rn(dzv[2], dzv[3]);
+    reinterpret_cast<uint2*>(dx + row * 128)[lane] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a0), *reinterpret_cast<const uint32_t*>(&a1));
+    reinterpret_cast<uint2*>(dz + row * 128)[lane] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
+  }
+}
+
+unsigned grid_for(int64_t n, int per_block) {
+  const int64_t g = (n + per_block - 1) / per_block;
+  return unsigned(g < 148 * 16 ? (g > 0 ? g : 1) : 148 * 16);
+}
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace rb2
+
+using namespace rb2;
+
+namespace rb2 {
+namespace {
+int make_split(void* p0, void* p1, void* p2, int s1, int s2, int C, Split* out) {
+  RB2_CHECK_ARG(p0 && aligned16(p0), "conv_silu: null or misaligned output pointer");
+  if (p1 == nullptr && p2 == nullptr) {
+    *out = Split{{static_cast<bf16*>(p0), nullptr, nullptr}, C, C, C};
+    return RB2_OK;
+  }
+  RB2_CHECK_ARG(p1 && p2 && aligned16(p1) && aligned16(p2), "conv_silu: null or misaligned split pointer");
+  RB2_CHECK_ARG(0 < s1 && s1 < s2 && s2 < C && s1 % 8 == 0 && s2 % 8 == 0,
+                "conv_silu: split points must be multiples of 8 with 0 < s1 < s2 < C");
+  *out = Split{{static_cast<bf16*>(p0), static_cast<bf16*>(p1), static_cast<bf16*>(p2)}, s1, s2, C};
+  return RB2_OK;
+}
+}  // namespace
+}  // namespace rb2
+
+extern "C" int rb2_conv_silu_fwd(const void* x, const void* w, int B, int T, int C, int K, void* y0, void* y1,
+                                 void* y2, int s1, int s2, void* stream) {
+  RB2_CHECK_ARG(K == kConvK, "conv_silu: kernel size must be 4 (got %d)", K);
+  RB2_CHECK_ARG(B >= 1 && T >= 1 && C >= 8 && C % 8 == 0, "conv_silu: bad sizes B=%d T=%d C=%d", B, T, C);
+  RB2_CHECK_ARG(x && w && aligned16(x) && (reinterpret_cast<uintptr_t>(w) & 7) == 0,
+                "conv_silu: null or misaligned pointer");
+  Split y;
+  int rc = make_split(y0, y1, y2, s1, s2, C, &y);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n = int64_t(B) * ((T + kTStrip - 1) / kTStrip) * (C / 8);
+  ProfScope ps_("block_conv_silu_fwd", s);
+  conv_silu_fwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), B, T,
+                                                          C, y);
+  RB2_CHECK_LAUNCH("conv_silu_fwd");
+  return RB2_OK;
+}
+
+extern "C" int rb2_conv_silu_bwd(const void* x, const void* w, const void* dy0, const void* dy1, const void* dy2,
+                                 int s1, int s2, int B, int T, int C, int K, void* dx, void* stream) {
+  RB2_CHECK_ARG(K == kConvK, "conv_silu: kernel size must be 4 (got %d)", K);
+  RB2_CHECK_ARG(B >= 1 && T >= 1 && C >= 8 && C % 8 == 0, "conv_silu: bad sizes B=%d T=%d C=%d", B, T, C);
+  RB2_CHECK_ARG(x && w && dx && aligned16(x) && aligned16(dx) && (reinterpret_cast<uintptr_t>(w) & 7) == 0,
+                "conv_silu: null or misaligned pointer");
+  Split dy;
+  int rc = make_split(const_cast<void*>(dy0), const_cast<void*>(dy1), const_cast<void*>(dy2), s1, s2, C, &dy);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n = int64_t(B) * ((T + kTStrip - 1) / kTStrip) * (C / 8);
+  ProfScope ps_("block_conv_silu_bwd", s);
+  conv_silu_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), dy, B, T,
+                                                          C, static_cast<bf16*>(dx));
+  RB2_CHECK_LAUNCH("conv_silu_bwd");
+  return RB2_OK;
+}
+
+extern "C" int rb2_gdn_gates_fwd(const void* a, const void* b, const float* A_log, const float* dt_bias, int64_t n,
+                                 int H, float* g, void* beta, void* stream) {
+  RB2_CHECK_ARG(n >= 0 && H >= 1 && n % H == 0, "gdn_gates: bad sizes n=%lld H=%d", (long long)n, H);
+  RB2_CHECK_ARG(n == 0 || (a && b && A_log && dt_bias && g && beta), "gdn_gates: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope ps_("block_gates_fwd", s);
+  gates_fwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(a), static_cast<const bf16*>(b), A_log,
+                                                      dt_bias, n, H, g, static_cast<bf16*>(beta));
+  RB2_CHECK_LAUNCH("gdn_gates_fwd");
+  return RB2_OK;
+}
+
+extern "C" int rb2_gdn_gates_bwd(const void* a, const void* beta, const float* A_log, const float* dt_bias,
+                                 const float* dg, const void* dbeta, int64_t n, int H, void* da, void* db,
+                                 void* stream) {
+  RB2_CHECK_ARG(n >= 0 && H >= 1 && n % H == 0, "gdn_gates: bad sizes n=%lld H=%d", (long long)n, H);
+  RB2_CHECK_ARG(n == 0 || (a && beta && A_log && dt_bias && dg && dbeta && da && db), "gdn_gates: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope ps_("block_gates_bwd", s);
+  gates_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(a), static_cast<const bf16*>(beta), A_log,
+                                                      dt_bias, dg, static_cast<const bf16*>(dbeta), n, H,
+                                                      static_cast<bf16*>(da), static_cast<bf16*>(db));
+  RB2_CHECK_LAUNCH("gdn_gates_bwd");
+  return RB2_OK;
+}
+
+extern "C" int rb2_gated_rmsnorm_fwd(const void* x, const void* z, const float* w, int64_t rows, int dim, float eps,
+                                     void* y, float* rstd, void* stream) {
+  RB2_CHECK_ARG(dim == 128, "gated_rmsnorm: row length must be 128 (got %d)", dim);
+  RB2_CHECK_ARG(rows >= 0, "gated_rmsnorm: bad row count");
+  RB2_CHECK_ARG(rows == 0 || (x && z && w && y && aligned16(x) && aligned16(z) && aligned16(w) && aligned16(y)),
+                "gated_rmsnorm: null or misaligned pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope ps_("block_gated_norm_fwd", s);
+  gated_norm_fwd_kernel<<<grid_for(rows, 8), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(z), w,
+                                                           rows, eps, static_cast<bf16*>(y), rstd);
+  RB2_CHECK_LAUNCH("gated_rmsnorm_fwd");
+  return RB2_OK;
+}
+
+extern "C" int rb2_gated_rmsnorm_bwd(const void* x, const void* z, const float* w, const float* rstd, const void* dout,
+                                     int64_t rows, int dim, void* dx, void* dz, void* stream) {
+  RB2_CHECK_ARG(dim == 128, "gated_rmsnorm: row length must be 128 (got %d)", dim);
+  RB2_CHECK_ARG(rows >= 0, "gated_rmsnorm: bad row count");
+  RB2_CHECK_ARG(rows == 0 || (x && z && w && rstd && dout && dx && dz && aligned16(x) && aligned16(z) &&
+                              aligned16(w) && aligned16(dout) && aligned16(dx) && aligned16(dz)),
+                "gated_rmsnorm: null or misaligned pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope ps_("block_gated_norm_bwd", s);
+  gated_norm_bwd_kernel<<<grid_for(rows, 8), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(z), w,
+                                                           rstd, static_cast<const bf16*>(dout), rows,
+                                                           static_cast<bf16*>(dx), static_cast<bf16*>(dz));
+  RB2_CHECK_LAUNCH("gated_rmsnorm_bwd");
+  return RB2_OK;
+}

@@ -89,5 +89,48 @@ def main(ref_root: str) -> None:
     print("wrote", sorted(arrays))
 
 
+def block_main(ref_root: str) -> None:
+    """``tests/golden/block_golden.npz``: the reference ``GatedDeltaNet`` (recant/model/layers.py:
+    133-182) at a small bf16 configuration (hidden 256, Hk 1, Hv 2, head dim 128) with NVFP4
+    projections and rank-16 LoRA (random B so that LoRA contributes): its weights (as fp32 values of
+    the bf16 parameters, taken before quantisation), a seeded input and the forward output."""
+    sys.path.insert(0, ref_root)
+    from recant.model import layers
+    from recant.model.config import TextConfig
+    c = TextConfig(hidden_size=256, linear_key_head_dim=128, linear_value_head_dim=128, linear_num_key_heads=1,
+                   linear_num_value_heads=2, num_hidden_layers=1)
+    torch.manual_seed(11)
+    gen = torch.Generator().manual_seed(11)
+    blk = layers.GatedDeltaNet(c)
+    with torch.no_grad():
+        for name in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+            lin = getattr(blk, name)
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=gen) * 0.06)
+        blk.conv1d.weight.copy_(torch.randn(blk.conv1d.weight.shape, generator=gen) * 0.4)
+        blk.A_log.copy_(torch.log(torch.empty(2).uniform_(1.0, 16.0, generator=gen)))
+        blk.dt_bias.copy_(torch.randn(2, generator=gen) * 0.5)
+        blk.norm.weight.copy_(1.0 + 0.1 * torch.randn(128, generator=gen))
+    blk = blk.to(torch.bfloat16)
+    arrays = {}
+    for name, prm in blk.named_parameters():
+        arrays[name] = prm.detach().float().numpy()
+    for name in ("in_proj_qkv", "in_proj_z", "out_proj"):
+        lin = getattr(blk, name)
+        lin.quantize_(True)
+        lin.add_lora(16, 32)
+        with torch.no_grad():
+            lin.lora_B.copy_(torch.randn(lin.lora_B.shape, generator=gen) * 0.02)
+        arrays[name + ".lora_A"] = lin.lora_A.detach().numpy()
+        arrays[name + ".lora_B"] = lin.lora_B.detach().numpy()
+    x = torch.randn(1, 70, 256, generator=gen).to(torch.bfloat16)
+    with torch.no_grad():
+        out = blk(x)
+    arrays["x"] = x.float().numpy()
+    arrays["out"] = out.float().numpy()
+    np.savez_compressed(os.path.join(HERE, "block_golden.npz"), **arrays)
+    print("block golden: out", tuple(out.shape), float(out.float().abs().mean()))
+
+
 if __name__ == "__main__":
     main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    block_main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
