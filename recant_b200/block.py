@@ -200,13 +200,30 @@ class QLinear(nn.Module):
 
 
 def grouped_linear(x, lins):
-    """layers.py:72-97 with the activation quantized once for all NVFP4 members."""
+    """layers.py:72-97 with the activation quantized once for all NVFP4 members; the LoRA
+    down-projections of all members come from one GEMM over x (x . cat(A_i)^T, as the reference's
+    default path, layers.py:86-88), each member then adds one addmm."""
     fp4 = [l for l in lins if l.fp4 is not None]
     outs = {}
     if fp4:
         ys = _FP4Group.apply(x, fp4[0].stochastic_backward, *[l.fp4 for l in fp4])
         outs = {id(l): y for l, y in zip(fp4, ys)}
-    return [l.lora(x, outs[id(l)] if id(l) in outs else x @ l.weight.t(), grouped=True) for l in lins]
+    base = [outs[id(l)] if id(l) in outs else x @ l.weight.t() for l in lins]
+    act = [l for l in lins if l.lora_A is not None]
+    if not act:
+        return base
+    h = x @ torch.cat([l.lora_A for l in act], 0).to(x.dtype).t()
+    res, off = [], 0
+    for l, y in zip(lins, base):
+        if l.lora_A is None:
+            res.append(y)
+            continue
+        r = l.lora_A.shape[0]
+        hi = h[..., off:off + r].reshape(-1, r)
+        off += r
+        o = torch.addmm(y.reshape(-1, l.out_features), hi, l.lora_B.to(x.dtype).t(), alpha=l.lora_scale)
+        res.append(o.reshape(*y.shape))
+    return res
 
 
 class GDNBlock(nn.Module):
@@ -280,7 +297,11 @@ class GDNBlock(nn.Module):
         B, T, _ = x.shape
         d = self.d
         qkv, z = grouped_linear(x, [self.in_proj_qkv, self.in_proj_z])
-        b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
+        if self.in_proj_b.weight is not None and self.in_proj_a.weight is not None:  # one N = 2 Hv GEMM
+            ba = x @ torch.cat([self.in_proj_b.weight, self.in_proj_a.weight], 0).t()
+            b_lin, a = ba[..., :self.Hv], ba[..., self.Hv:]
+        else:
+            b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
         q, k, v = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim)
         q = q.view(B, T, self.Hk, d)
         k = k.view(B, T, self.Hk, d)

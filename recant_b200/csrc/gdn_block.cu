@@ -49,121 +49,167 @@ struct Split {
     return p[2] + tok * (C - s2) + (c - s2);
   }
 };
-constexpr int kTStrip = 32;  // tokens per thread
+// One CTA: a tile of kTileT tokens x kTileC channels of one sequence. The tile and its 3-row halo
+// are copied to shared memory with 16-byte cp.async (zero-filled before token 0 and past T), all
+// copies in flight at once; each thread then works on one 4-channel group and a run of 8 rows
+// (64 threads per row, 4 row groups; few registers, so 4 CTAs share an SM and hide the copies).
+constexpr int kTileT = 32, kTileC = 256, kChunks = kTileC / 8, kGroups = kTileC / 4;
+constexpr int kHalo = kConvK - 1;
+constexpr int kRowGroups = 256 / kGroups, kRowsPer = kTileT / kRowGroups;
 
-// y[b, t, c] = bf16(silu(bf16(sum_j w[c, j] x[b, t - 3 + j, c]))); one thread: 8 channels x 32 tokens
-__global__ void __launch_bounds__(256) conv_silu_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                            int B, int T, int C, Split y) {
-  const int c8 = C / 8, strips = (T + kTStrip - 1) / kTStrip;
-  const int64_t n = int64_t(B) * strips * c8;
-  for (int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * 256) {
-    const int cc = int(idx % c8), s = int((idx / c8) % strips), b = int(idx / (int64_t(c8) * strips));
-    const int c = cc * 8, t0 = s * kTStrip;
-    float wt[kConvK][8];
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+__device__ __forceinline__ void load4(const bf16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
+  v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
+}
+__device__ __forceinline__ void store4(bf16* p, const float (&v)[4]) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+__device__ __forceinline__ void load_taps4(const bf16* w, int c, float (&wt)[kConvK][4]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint2 u = *reinterpret_cast<const uint2*>(w + int64_t(c + i) * kConvK);
-      wt[0][i] = __uint_as_float(u.x << 16); wt[1][i] = __uint_as_float(u.x & 0xffff0000u);
-      wt[2][i] = __uint_as_float(u.y << 16); wt[3][i] = __uint_as_float(u.y & 0xffff0000u);
+  for (int i = 0; i < 4; ++i) {
+    const uint2 u = *reinterpret_cast<const uint2*>(w + int64_t(c + i) * kConvK);
+    wt[0][i] = __uint_as_float(u.x << 16); wt[1][i] = __uint_as_float(u.x & 0xffff0000u);
+    wt[2][i] = __uint_as_float(u.y << 16); wt[3][i] = __uint_as_float(u.y & 0xffff0000u);
+  }
+}
+// silu with a fast reciprocal (sigmoid to a few ulp; the output is rounded to bf16)
+__device__ __forceinline__ float fsigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+struct TileIdx {
+  int b, t0, c0, nchunk;
+};
+__device__ __forceinline__ TileIdx tile_of(int64_t tile, int T, int C) {
+  const int ct = (C + kTileC - 1) / kTileC, tt = (T + kTileT - 1) / kTileT;
+  TileIdx r;
+  r.c0 = int(tile % ct) * kTileC;
+  r.t0 = int((tile / ct) % tt) * kTileT;
+  r.b = int(tile / (int64_t(ct) * tt));
+  r.nchunk = min(kChunks, (C - r.c0) / 8);
+  return r;
+}
+
+// y[b, t, c] = bf16(silu(bf16(sum_j w[c, j] x[b, t - 3 + j, c])))
+__global__ void __launch_bounds__(256, 4) conv_silu_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                               int B, int T, int C, Split y) {
+  __shared__ __align__(16) bf16 xs[kTileT + kHalo][kTileC];  // row i = token t0 - 3 + i
+  const TileIdx ti = tile_of(blockIdx.x, T, C);
+  const bf16* xb = x + int64_t(ti.b) * T * C + ti.c0;
+  for (int e = threadIdx.x; e < (kTileT + kHalo) * kChunks; e += 256) {
+    const int r = e / kChunks, ch = e % kChunks, t = ti.t0 - kHalo + r;
+    const bool ok = ch < ti.nchunk && t >= 0 && t < T;
+    cp_async16(&xs[r][ch * 8], ok ? xb + int64_t(t) * C + ch * 8 : x, ok);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int g = threadIdx.x % kGroups, r0 = (threadIdx.x / kGroups) * kRowsPer;
+  if (g >= 2 * ti.nchunk) return;
+  const int c = ti.c0 + g * 4;
+  float wt[kConvK][4];
+  load_taps4(w, c, wt);
+  float win[kConvK][4];
+#pragma unroll
+  for (int j = 0; j < kHalo; ++j) load4(&xs[r0 + j][g * 4], win[j]);
+#pragma unroll
+  for (int k = 0; k < kRowsPer; ++k) {
+    const int t = ti.t0 + r0 + k;
+    load4(&xs[r0 + k + kHalo][g * 4], win[kHalo]);
+    float out[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a = wt[0][i] * win[0][i];
+      a = fmaf(wt[1][i], win[1][i], a);
+      a = fmaf(wt[2][i], win[2][i], a);
+      a = fmaf(wt[3][i], win[3][i], a);
+      const float u = bfr(a);
+      out[i] = u * fsigm(u);
+      win[0][i] = win[1][i]; win[1][i] = win[2][i]; win[2][i] = win[3][i];
     }
-    const bf16* xb = x + int64_t(b) * T * C + c;
-    float win[kConvK - 1][8];
-#pragma unroll
-    for (int j = 0; j < kConvK - 1; ++j) {
-      const int t = t0 - (kConvK - 1) + j;
-      if (t >= 0) load8(xb + int64_t(t) * C, win[j]);
-      else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
-      }
-    }
-    const int t1 = min(T, t0 + kTStrip);
-    for (int t = t0; t < t1; ++t) {
-      float cur[8], out[8];
-      load8(xb + int64_t(t) * C, cur);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float a = wt[0][i] * win[0][i];
-        a = fmaf(wt[1][i], win[1][i], a);
-        a = fmaf(wt[2][i], win[2][i], a);
-        a = fmaf(wt[3][i], cur[i], a);
-        out[i] = silu(bfr(a));
-        win[0][i] = win[1][i]; win[1][i] = win[2][i]; win[2][i] = cur[i];
-      }
-      store8(y.at(int64_t(b) * T + t, c), out);
-    }
+    if (t < T) store4(y.at(int64_t(ti.b) * T + t, c), out);
   }
 }
 
-// du[t] = dy[t] silu'(u[t]) (u recomputed, bf16 as in the forward); dx[t] = sum_j w[c, j] du[t + 3 - j]
-__global__ void __launch_bounds__(256) conv_silu_bwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                            Split dy, int B, int T, int C, bf16* __restrict__ dx) {
-  const int c8 = C / 8, strips = (T + kTStrip - 1) / kTStrip;
-  const int64_t n = int64_t(B) * strips * c8;
-  for (int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * 256) {
-    const int cc = int(idx % c8), s = int((idx / c8) % strips), b = int(idx / (int64_t(c8) * strips));
-    const int c = cc * 8, t0 = s * kTStrip;
-    float wt[kConvK][8];
+// du[t] = bf16(dy[t] silu'(u[t])) (u recomputed, bf16 as in the forward) for t in [t0, t0 + 35);
+// dx[t] = sum_j w[c, j] du[t + 3 - j] for t in [t0, t0 + 32)
+__global__ void __launch_bounds__(256, 4) conv_silu_bwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                               Split dy, int B, int T, int C, bf16* __restrict__ dx) {
+  __shared__ __align__(16) bf16 xs[kTileT + 2 * kHalo][kTileC];  // row i = token t0 - 3 + i
+  __shared__ __align__(16) bf16 ds[kTileT + kHalo][kTileC];      // row i = token t0 + i: dy, then du
+  const TileIdx ti = tile_of(blockIdx.x, T, C);
+  const bf16* xb = x + int64_t(ti.b) * T * C + ti.c0;
+  for (int e = threadIdx.x; e < (kTileT + 2 * kHalo) * kChunks; e += 256) {
+    const int r = e / kChunks, ch = e % kChunks, t = ti.t0 - kHalo + r;
+    const bool ok = ch < ti.nchunk && t >= 0 && t < T;
+    cp_async16(&xs[r][ch * 8], ok ? xb + int64_t(t) * C + ch * 8 : x, ok);
+  }
+  for (int e = threadIdx.x; e < (kTileT + kHalo) * kChunks; e += 256) {
+    const int r = e / kChunks, ch = e % kChunks, t = ti.t0 + r;
+    const bool ok = ch < ti.nchunk && t < T;
+    cp_async16(&ds[r][ch * 8], ok ? static_cast<const bf16*>(dy.at(int64_t(ti.b) * T + t, ti.c0 + ch * 8)) : x, ok);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int g = threadIdx.x % kGroups, grp = threadIdx.x / kGroups;
+  const bool active = g < 2 * ti.nchunk;
+  const int c = ti.c0 + g * 4;
+  float wt[kConvK][4];
+  if (active) load_taps4(w, c, wt);
+  // phase 1: 35 du rows over the row groups (9 rows each, the last one short); zero-filled dy gives du = 0
+  constexpr int kDuRows = kTileT + kHalo, kPer = (kDuRows + kRowGroups - 1) / kRowGroups;
+  if (active) {
+    const int r0 = grp * kPer;
+    float win[kConvK][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint2 u = *reinterpret_cast<const uint2*>(w + int64_t(c + i) * kConvK);
-      wt[0][i] = __uint_as_float(u.x << 16); wt[1][i] = __uint_as_float(u.x & 0xffff0000u);
-      wt[2][i] = __uint_as_float(u.y << 16); wt[3][i] = __uint_as_float(u.y & 0xffff0000u);
+    for (int j = 0; j < kHalo; ++j) load4(&xs[r0 + j][g * 4], win[j]);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int r = r0 + k;
+      if (r >= kDuRows) break;
+      load4(&xs[r + kHalo][g * 4], win[kHalo]);
+      float gr[4], du[4];
+      load4(&ds[r][g * 4], gr);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float a = wt[0][i] * win[0][i];
+        a = fmaf(wt[1][i], win[1][i], a);
+        a = fmaf(wt[2][i], win[2][i], a);
+        a = fmaf(wt[3][i], win[3][i], a);
+        const float pre = bfr(a), sg = fsigm(pre);
+        du[i] = gr[i] * sg * (1.f + pre * (1.f - sg));
+        win[0][i] = win[1][i]; win[1][i] = win[2][i]; win[2][i] = win[3][i];
+      }
+      store4(&ds[r][g * 4], du);
     }
-    const bf16* xb = x + int64_t(b) * T * C + c;
-    // du at t needs x[t-3 .. t]; dx at t needs du[t .. t+3]: walk t' = t0 .. t1+2, keeping x and du windows
-    float xw[kConvK - 1][8], dw[kConvK - 1][8];  // x[t'-3..t'-1], du[t'-3..t'-1]
+  }
+  __syncthreads();
+  // phase 2: dx rows r0 .. r0 + 7 from du rows r0 .. r0 + 10
+  if (!active) return;
+  const int r0 = grp * kRowsPer;
+  float dw[kConvK][4];
 #pragma unroll
-    for (int j = 0; j < kConvK - 1; ++j) {
-      const int t = t0 - (kConvK - 1) + j;
-      if (t >= 0) load8(xb + int64_t(t) * C, xw[j]);
-      else {
+  for (int j = 0; j < kHalo; ++j) load4(&ds[r0 + j][g * 4], dw[j]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xw[j][i] = 0.f;
-      }
+  for (int k = 0; k < kRowsPer; ++k) {
+    const int t = ti.t0 + r0 + k;
+    load4(&ds[r0 + k + kHalo][g * 4], dw[kHalo]);
+    float out[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) dw[j][i] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+      float a = wt[0][i] * dw[3][i];
+      a = fmaf(wt[1][i], dw[2][i], a);
+      a = fmaf(wt[2][i], dw[1][i], a);
+      a = fmaf(wt[3][i], dw[0][i], a);
+      out[i] = a;
+      dw[0][i] = dw[1][i]; dw[1][i] = dw[2][i]; dw[2][i] = dw[3][i];
     }
-    const int t1 = min(T, t0 + kTStrip);
-    // first bring the x window to t0 (du for t < t0 is not needed)
-    for (int tp = t0; tp < t1 + kConvK - 1; ++tp) {
-      float xc[8], du[8];
-      if (tp < T) {
-        load8(xb + int64_t(tp) * C, xc);
-        float g[8];
-        load8(dy.at(int64_t(b) * T + tp, c), g);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float a = wt[0][i] * xw[0][i];
-          a = fmaf(wt[1][i], xw[1][i], a);
-          a = fmaf(wt[2][i], xw[2][i], a);
-          a = fmaf(wt[3][i], xc[i], a);
-          const float u = bfr(a), sg = sigm(u);
-          du[i] = bfr(g[i] * sg * (1.f + u * (1.f - sg)));
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { xc[i] = 0.f; du[i] = 0.f; }
-      }
-      const int t = tp - (kConvK - 1);  // dx[t] = w0 du[t+3] + w1 du[t+2] + w2 du[t+1] + w3 du[t]
-      if (t >= t0) {
-        float out[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float a = wt[0][i] * du[i];
-          a = fmaf(wt[1][i], dw[2][i], a);
-          a = fmaf(wt[2][i], dw[1][i], a);
-          a = fmaf(wt[3][i], dw[0][i], a);
-          out[i] = a;
-        }
-        store8(dx + (int64_t(b) * T + t) * C + c, out);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        xw[0][i] = xw[1][i]; xw[1][i] = xw[2][i]; xw[2][i] = xc[i];
-        dw[0][i] = dw[1][i]; dw[1][i] = dw[2][i]; dw[2][i] = du[i];
-      }
-    }
+    if (t < T) store4(dx + (int64_t(ti.b) * T + t) * C + c, out);
   }
 }
 
@@ -301,9 +347,10 @@ extern "C" int rb2_conv_silu_fwd(const void* x, const void* w, int B, int T, int
   int rc = make_split(y0, y1, y2, s1, s2, C, &y);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t n = int64_t(B) * ((T + kTStrip - 1) / kTStrip) * (C / 8);
+  const int64_t n = int64_t(B) * ((T + kTileT - 1) / kTileT) * ((C + kTileC - 1) / kTileC);
+  RB2_CHECK_ARG(n < (int64_t(1) << 31), "conv_silu: too many tiles (%lld)", (long long)n);
   ProfScope ps_("block_conv_silu_fwd", s);
-  conv_silu_fwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), B, T,
+  conv_silu_fwd_kernel<<<unsigned(n), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), B, T,
                                                           C, y);
   RB2_CHECK_LAUNCH("conv_silu_fwd");
   return RB2_OK;
@@ -319,9 +366,10 @@ extern "C" int rb2_conv_silu_bwd(const void* x, const void* w, const void* dy0, 
   int rc = make_split(const_cast<void*>(dy0), const_cast<void*>(dy1), const_cast<void*>(dy2), s1, s2, C, &dy);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t n = int64_t(B) * ((T + kTStrip - 1) / kTStrip) * (C / 8);
+  const int64_t n = int64_t(B) * ((T + kTileT - 1) / kTileT) * ((C + kTileC - 1) / kTileC);
+  RB2_CHECK_ARG(n < (int64_t(1) << 31), "conv_silu: too many tiles (%lld)", (long long)n);
   ProfScope ps_("block_conv_silu_bwd", s);
-  conv_silu_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), dy, B, T,
+  conv_silu_bwd_kernel<<<unsigned(n), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), dy, B, T,
                                                           C, static_cast<bf16*>(dx));
   RB2_CHECK_LAUNCH("conv_silu_bwd");
   return RB2_OK;
