@@ -232,6 +232,101 @@ def reference_arm(args, rank, world):
     return 0
 
 
+# fla 0.5.1 on B200 (Triton 3.6 / TileLang): its chunk_gated_delta_rule fwd+bwd on valid contiguous
+# config-1 inputs raised a device fault before any kernel of this library had run; it is not run again.
+FLA_FAULT = ("not run: fla 0.5.1 chunk_gated_delta_rule fwd+bwd at config 1 raised 'CUDA error: misaligned "
+             "address' on B200 (a TileLang kernel had just been compiled)")
+
+
+def comparator_arm(args):
+    """--comparators: the GPU implementations the reference selects on a CUDA box, timed on this
+    GPU beside this library on the same shapes (CUDA events, median of the timed steps):
+      * fla's chunk_gated_delta_rule (recant/model/ops.py:56-59, chosen by backends.select_gdn) is not
+        run: on this GPU it faulted (FLA_FAULT); this library's GDN op fwd+bwd at config 1 on q and k
+        repeated to Hv as GatedDeltaNet does (layers.py:174-176) and on the unrepeated Hk = 16 ones;
+      * torch._scaled_mm NVFP4 (recant/model/nvfp4.py:112-124, the cuBLASLt GEMM backend) on config
+        2's fused in_proj fprop [16384 x 4096] . [12288 x 4096]^T with bf16 output, kernel alone and
+        with the backend's fp32 global-scale epilogue, beside this library's GEMM on the same codes.
+    Prints one JSON line; not part of the driver contract."""
+    import torch
+
+    from recant_b200 import gdn_b200
+    from recant_b200 import nvfp4 as N
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+
+    def med(fn, steps):
+        ts = []
+        for _ in range(3):
+            fn()
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    c = CFG
+    B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
+    inp, do = make_inputs(dev, 0, B, T, Hk, Hv, d)
+    rep = Hv // Hk
+    rq, rk = (inp[n].repeat_interleave(rep, dim=2).contiguous() for n in ("q", "k"))
+    out = {"impl": "comparators", "config": "config1 B4 T4096 Hk16 Hv32 d128 fwd+bwd; config2 in_proj GEMM",
+           "steps": args.steps}
+
+    def gdn_step(fn, q, k):
+        leaves = [t.detach().clone().requires_grad_(True) for t in (q, k, inp["v"], inp["g"], inp["beta"])]
+
+        def step():
+            for t in leaves:
+                t.grad = None
+            o = fn(*leaves)
+            o.backward(do)
+        return step
+
+    tokens = B * T
+    out["fla_gdn"] = {"unavailable": FLA_FAULT}
+    for name, (q, k) in (("b200_gdn_repeated", (rq, rk)), ("b200_gdn_gqa", (inp["q"], inp["k"]))):
+        ms = med(gdn_step(lambda *a: gdn_b200(*a)[0], q, k), args.steps)
+        out[name] = {"ms": round(ms, 4), "tokens_per_s": round(tokens / ms * 1e3, 1)}
+
+    M, K, Nn = 16384, 4096, 12288
+    gen = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    W = N.quantize_weight(torch.randn(Nn, K, device=dev, generator=gen) * 0.02)
+    a = N.quantize_fast(x)
+    b = W.fprop
+    flop = 2.0 * M * Nn * K
+    try:
+        fa = a.codes.view(torch.float4_e2m1fn_x2)
+        fb = b.codes.view(torch.float4_e2m1fn_x2)
+        sa, sb = a.blocked.view(torch.float8_e4m3fn), b.blocked.view(torch.float8_e4m3fn)
+
+        def smm():
+            return torch._scaled_mm(fa, fb.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+
+        def smm_backend():
+            return smm().float() * (a.gscale * b.gscale)
+        y_ref = smm_backend()
+        y_ours = N.gemm_b200(a, b)
+        agree = float((y_ours - y_ref).norm() / y_ref.norm())
+        ms_k, ms_b = med(smm, args.steps), med(smm_backend, args.steps)
+        out["scaled_mm_nvfp4"] = {"ms": round(ms_k, 4), "tflops": round(flop / ms_k / 1e9, 1),
+                                  "ms_with_fp32_epilogue": round(ms_b, 4),
+                                  "rel_diff_vs_b200_fp32": agree}
+    except Exception as e:
+        out["scaled_mm_nvfp4"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+    ms_o = med(lambda: N.gemm_b200(a, b, out_dtype=torch.bfloat16), args.steps)
+    ms_of = med(lambda: N.gemm_b200(a, b), args.steps)
+    out["b200_nvfp4_gemm"] = {"ms": round(ms_o, 4), "tflops": round(flop / ms_o / 1e9, 1),
+                              "ms_fp32_out": round(ms_of, 4)}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 METRIC4 = "GDN stack fwd+bwd sequence tokens/s (8 GDN layers + NVFP4 out_proj, B1 T131072, context-parallel)"
 C4 = dict(T=131072, layers=8, Hk=16, Hv=32, d=128, hidden=4096, segments_per_rank=4)
 # NVFP4 GEMM roofline: 4x the measured dense bf16 rate (the tcgen05 FP4 : bf16 dense ratio)
@@ -543,6 +638,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--comparators", action="store_true",
+                    help="time torch._scaled_mm NVFP4 (and record the fla fault) beside this library "
+                         "(one JSON line; outside the driver contract)")
     ap.add_argument("--batch", type=int, default=None,
                     help="config 1 only: batch B (default 4, the headline); smaller B for profiling captures")
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 4], default=1,
@@ -557,6 +655,8 @@ def main():
         return reference_arm(args, rank, world)
     if args.warmup < 3:
         args.warmup = 3
+    if args.comparators:
+        return comparator_arm(args)
 
     import torch
     import torch.distributed as dist

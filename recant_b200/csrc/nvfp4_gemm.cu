@@ -12,7 +12,8 @@
 //   warp 1     MMA: per 64-element K step, tcgen05.cp of the scale atoms into TMEM (32x128b.warpx4:
 //              lane m%32 of every sub-partition, 32-bit column m/32, one byte per 16-element block)
 //              and one tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64);
-//   warps 2-5  epilogue: TMEM -> registers -> * gA gB -> fp32 or bf16 rows.
+//   warps 2-9  epilogue: TMEM -> registers (each warp: its sub-partition's 32 rows x 128 columns),
+//              accumulator released, then * gA gB -> fp32 or bf16 rows while the next tile runs.
 
 #include "tmap.cuh"
 
@@ -20,7 +21,7 @@ namespace rb2 {
 namespace {
 
 constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (= 256 e2m1)
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 
 // Tile shape: BN output columns, STAGES smem stages, ACC TMEM accumulator buffers.
 template <int BN_, int STAGES_, int ACC_>
@@ -69,6 +70,18 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0), "r"(sfa_tmem), "r"(sfb_tmem));
 }
 
+// 32 lanes x 32 columns of 32-bit TMEM into registers, without waiting (tcgen05.wait::ld follows)
+__device__ __forceinline__ void tmem_ld32_raw(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
 }
@@ -106,7 +119,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
     }
     for (int b = 0; b < ACC; ++b) {
       tc::mbar_init(&acc_full[b], 1);
-      tc::mbar_init(&acc_empty[b], 4);   // one arrival per epilogue warp
+      tc::mbar_init(&acc_empty[b], 8);   // one arrival per epilogue warp
     }
     tc::fence_mbar_init();
   }
@@ -169,52 +182,65 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         tc::mma_commit(&acc_full[ab]);
       }
     }
-  } else {  // ---------------- epilogue: warps 2..5 ----------------
-    const int q = w & 3;
+  } else {  // ---------------- epilogue: warps 2..9 ----------------
+    // warp w reads TMEM lanes 32 (w % 4) .. + 31 (its sub-partition) and half (w - 2) / 4 of the
+    // columns into registers, hands the accumulator back at once, then scales and stores, so the
+    // stores overlap the next tile's main loop
+    const int q = w & 3, half = (w - 2) >> 2;
+    constexpr int HC = BN / 2;
     const float scale = ga[0] * gb[0];
     int local = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
       const int tm = t / ntn, tn = t % ntn;
       const int ab = local % ACC;
-      const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16) + ab * BN;
+      const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16) + ab * BN + half * HC;
       if (!tc::mbar_wait(&acc_full[ab], (local / ACC) & 1, err, 203)) break;
       tc::fence_after_sync();
-      const int row = tm * BM + 32 * q + l;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32];
-        tc::tmem_ld32(lane_addr + c0, v);
-        const int col0 = tn * BN + c0;
-        if (row < M && col0 < N) {
-          if (out_bf16) {
-            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
-            if (col0 + 32 <= N && (N % 8) == 0) {
+      uint32_t r[HC / 32][32];
 #pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk = make_uint4(tc::pack_bf16(v[j] * scale, v[j + 1] * scale), tc::pack_bf16(v[j + 2] * scale, v[j + 3] * scale),
-                                      tc::pack_bf16(v[j + 4] * scale, v[j + 5] * scale), tc::pack_bf16(v[j + 6] * scale, v[j + 7] * scale));
-                *reinterpret_cast<uint4*>(o + j) = pk;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < N) o[j] = __float2bfloat16_rn(v[j] * scale);
-            }
-          } else {
-            float* o = static_cast<float*>(out) + size_t(row) * N + col0;
-            if (col0 + 32 <= N && (N % 4) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(o + j) = make_float4(v[j] * scale, v[j + 1] * scale, v[j + 2] * scale, v[j + 3] * scale);
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < N) o[j] = v[j] * scale;
-            }
-          }
-        }
-      }
+      for (int c = 0; c < HC / 32; ++c) tmem_ld32_raw(lane_addr + 32 * c, r[c]);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       tc::fence_before_sync();
       __syncwarp();
       if (l == 0) mbar_arrive(&acc_empty[ab]);
+      const int row = tm * BM + 32 * q + l;
+      if (row >= M) continue;
+#pragma unroll
+      for (int c = 0; c < HC / 32; ++c) {
+        const int col0 = tn * BN + half * HC + 32 * c;
+        if (col0 >= N) break;
+        if (out_bf16) {
+          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
+          if (col0 + 32 <= N && (N % 8) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              const uint4 pk = make_uint4(
+                  tc::pack_bf16(__uint_as_float(r[c][j]) * scale, __uint_as_float(r[c][j + 1]) * scale),
+                  tc::pack_bf16(__uint_as_float(r[c][j + 2]) * scale, __uint_as_float(r[c][j + 3]) * scale),
+                  tc::pack_bf16(__uint_as_float(r[c][j + 4]) * scale, __uint_as_float(r[c][j + 5]) * scale),
+                  tc::pack_bf16(__uint_as_float(r[c][j + 6]) * scale, __uint_as_float(r[c][j + 7]) * scale));
+              *reinterpret_cast<uint4*>(o + j) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) o[j] = __float2bfloat16_rn(__uint_as_float(r[c][j]) * scale);
+          }
+        } else {
+          float* o = static_cast<float*>(out) + size_t(row) * N + col0;
+          if (col0 + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(o + j) =
+                  make_float4(__uint_as_float(r[c][j]) * scale, __uint_as_float(r[c][j + 1]) * scale,
+                              __uint_as_float(r[c][j + 2]) * scale, __uint_as_float(r[c][j + 3]) * scale);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) o[j] = __uint_as_float(r[c][j]) * scale;
+          }
+        }
+      }
     }
   }
   tc::fence_before_sync();
