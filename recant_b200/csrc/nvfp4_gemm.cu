@@ -6,12 +6,18 @@
 // nibble), B = codes [N, K/2]; per-16 e4m3 scales in the blocked layout; fp32 accumulation.
 //
 // Persistent CTAs (one per SM) walk 128 x 256 output tiles, warp-specialised:
+//   (before)   a small kernel expands both operands' blocked scales into workspace images: every
+//              512-byte atom (32 rows x 16 bytes: row r = the 4 scales of rows r, r+32, r+64, r+96 for
+//              one 64-element K step) written 4 times in a row, i.e. the 128-lane picture the MMA
+//              reads (row m of the image = atom row m % 32); B's two 128-row halves interleaved per
+//              K step;
 //   warp 0     producer: TMA (cp.async.bulk.tensor, SW128, no multicast) of the A and B code tiles
-//              (128 bytes = 256 K-elements per row per stage) and 1-D bulk copies of the scale
-//              atoms into a 4-stage ring; completion via mbarrier transaction counts;
-//   warp 1     MMA: per 64-element K step, tcgen05.cp of the scale atoms into TMEM (32x128b.warpx4:
-//              lane m%32 of every sub-partition, 32-bit column m/32, one byte per 16-element block)
-//              and one tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64);
+//              (128 bytes = 256 K-elements per row per stage) and one 1-D bulk copy per operand of
+//              its scale images into a 3-stage ring; completion via mbarrier transaction counts;
+//   warp 1     MMA: tcgen05.cp.128x256b of the images into TMEM (lane m, 32-bit column m / 32 of a
+//              4-column group holds row m's scales; one copy fills two groups: two K steps of A,
+//              or both halves of B for one K step: 6 copies per 4 K steps), then one
+//              tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64) per K step;
 //   warps 2-9  epilogue: TMEM -> registers (each warp: its sub-partition's 32 rows x 128 columns),
 //              accumulator released, then * gA gB -> fp32 or bf16 rows while the next tile runs.
 
@@ -23,19 +29,48 @@ namespace {
 constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (= 256 e2m1)
 constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 
-// Tile shape: BN output columns, STAGES smem stages, ACC TMEM accumulator buffers.
+// Tile shape: BN output columns, STAGES smem stages, ACC TMEM accumulator buffers. A stage is
+// [A scale images | B scale images | A codes | B codes]: the images first, so that every scale
+// copy reads well inside its own stage.
+constexpr int kImg = 4 * 512;  // one atom repeated over 128 rows
+
 template <int BN_, int STAGES_, int ACC_>
 struct GemmCfg {
   static constexpr int BN = BN_, STAGES = STAGES_, ACC = ACC_;
   static constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;
-  static constexpr int SFA_BYTES = (BM / 128) * 4 * 512;  // 4 atoms of 128 rows x 4 scales
-  static constexpr int SFB_BYTES = (BN / 128) * 4 * 512;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int SFA_BYTES = 4 * kImg;                 // 4 K steps
+  static constexpr int SFB_BYTES = 4 * 2 * kImg;             // 4 K steps x 2 halves
+  static constexpr int SFA_OFF = 0, SFB_OFF = SFA_BYTES, A_OFF = SFA_BYTES + SFB_BYTES, B_OFF = A_OFF + A_BYTES;
+  static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
-  static constexpr int SF_COL0 = ACC * BN;                  // TMEM: accumulators, then scale factors
-  static_assert(SF_COL0 + 16 + 8 * (BN / 128) * 4 <= 512, "TMEM budget");
-  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+  static constexpr int SF_COL0 = ACC * BN;                   // TMEM: accumulators, then scale factors
+  static_assert(BN == 256, "a B scale copy moves exactly two 128-row halves");
+  static_assert(SF_COL0 + 16 + 32 <= 512, "TMEM budget");
+  static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && STAGE_BYTES % 1024 == 0, "SW128 alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
+
+// Scale images in the workspace: A: [row block][K step (padded to 4)][kImg]; B: [256-row block]
+// [K step (padded to 4)][half][kImg]. ksp = K steps rounded up to a multiple of 4.
+__global__ void sf_images_kernel(const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int ntm, int nrb,
+                                 int ncb, int ksp, uint8_t* __restrict__ img_a, uint8_t* __restrict__ img_b) {
+  const int64_t na = int64_t(ntm) * ksp * (kImg / 16), nb = int64_t((nrb + 1) / 2) * ksp * 2 * (kImg / 16);
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < na + nb; i += int64_t(gridDim.x) * blockDim.x) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (i < na) {
+      const int within = int(i % 32), ks = int((i / 128) % ksp);
+      const int64_t tm = i / (int64_t(128) * ksp);
+      if (ks < ncb) v = reinterpret_cast<const uint4*>(sfa + (tm * ncb + ks) * 512)[within];
+      reinterpret_cast<uint4*>(img_a)[i] = v;
+    } else {
+      const int64_t j = i - na;
+      const int within = int(j % 32), h = int((j / 128) % 2), ks = int((j / 256) % ksp);
+      const int64_t rb = (j / (int64_t(256) * ksp)) * 2 + h;
+      if (ks < ncb && rb < nrb) v = reinterpret_cast<const uint4*>(sfb + (rb * ncb + ks) * 512)[within];
+      reinterpret_cast<uint4*>(img_b)[j] = v;
+    }
+  }
+}
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -44,17 +79,19 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "l"(map), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
       : "memory");
 }
-// smem descriptor of one 512-byte scale atom (32 rows x 16 bytes, no swizzle) for tcgen05.cp
-__device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
+// smem descriptor of a 128-row x 32-byte scale source for tcgen05.cp.128x256b, no swizzle: 8-row x
+// 16-byte core matrices, consecutive row groups 128 bytes apart (SBO), the second 16-byte column
+// kImg bytes after the first (LBO)
+__device__ __forceinline__ uint64_t desc_sf_pair(uint32_t saddr) {
   uint64_t d = 0;
   d |= uint64_t((saddr >> 4) & 0x3FFF);
-  d |= uint64_t(128 >> 4) << 16;  // LBO (single 16-byte column)
-  d |= uint64_t(128 >> 4) << 32;  // SBO: 8-row core matrices 128 bytes apart
+  d |= uint64_t((kImg >> 4) & 0x3FFF) << 16;  // LBO
+  d |= uint64_t(128 >> 4) << 32;              // SBO
   d |= uint64_t(1) << 46;
-  return d;                       // layout type 0 = no swizzle
+  return d;                                   // layout type 0 = no swizzle
 }
-__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+__device__ __forceinline__ void tmem_cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 // kind::mxf4nvf4 instruction descriptor: e2m1 x e2m1, ue4m3 scales, K-major A and B, dense K=64
 __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
@@ -93,19 +130,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                  const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, const float* __restrict__ ga,
+                  const uint8_t* __restrict__ img_a, const uint8_t* __restrict__ img_b, int ksp, const float* __restrict__ ga,
                   const float* __restrict__ gb, int M, int N, int K, void* __restrict__ out, int out_bf16,
                   int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023);
   constexpr int BN = C::BN, STAGES = C::STAGES, ACC = C::ACC;
-  constexpr int A_BYTES = C::A_BYTES, B_BYTES = C::B_BYTES, SFA_BYTES = C::SFA_BYTES, STAGE_BYTES = C::STAGE_BYTES;
+  constexpr int A_BYTES = C::A_BYTES, B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES;
   __shared__ uint64_t full[STAGES], empty[STAGES], acc_full[ACC], acc_empty[ACC];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int ksteps = K / 64;                       // 64-element MMA steps
   const int nstages = (ksteps + 3) / 4;            // 4 steps per stage
-  const int ncb = (K / 16 + 3) / 4;                // scale atoms per 128-row block
   const int ntm = (M + BM - 1) / BM, ntn = (N + BN - 1) / BN, ntiles = ntm * ntn;
 
   if (w == 1) {
@@ -133,20 +169,16 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         const int tm = t / ntn, tn = t % ntn;
-        const int nrb = min(BN / 128, (N + 127) / 128 - tn * (BN / 128));
         for (int kt = 0; kt < nstages; ++kt, ++g) {
           const int s = g % STAGES;
           if (!(ok = tc::mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, err, 201))) break;
           unsigned char* st = sm + s * STAGE_BYTES;
           const int steps = min(4, ksteps - 4 * kt);
-          const uint32_t sfa_bytes = steps * 512, sfb_bytes = steps * 512 * nrb;
-          tc::mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sfa_bytes + sfb_bytes);
-          tma_load_2d(st, &map_a, kt * BKB, tm * BM, &full[s]);
-          tma_load_2d(st + A_BYTES, &map_b, kt * BKB, tn * BN, &full[s]);
-          tc::bulk_load(st + A_BYTES + B_BYTES, sfa + (size_t(tm) * ncb + 4 * kt) * 512, sfa_bytes, &full[s]);
-          for (int rb = 0; rb < nrb; ++rb)
-            tc::bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + rb * 2048,
-                      sfb + (size_t(tn * (BN / 128) + rb) * ncb + 4 * kt) * 512, steps * 512, &full[s]);
+          tc::mbar_expect_tx(&full[s], A_BYTES + B_BYTES + uint32_t(steps) * 3 * kImg);
+          tma_load_2d(st + C::A_OFF, &map_a, kt * BKB, tm * BM, &full[s]);
+          tma_load_2d(st + C::B_OFF, &map_b, kt * BKB, tn * BN, &full[s]);
+          tc::bulk_load(st + C::SFA_OFF, img_a + (size_t(tm) * ksp + 4 * kt) * kImg, steps * kImg, &full[s]);
+          tc::bulk_load(st + C::SFB_OFF, img_b + (size_t(tn) * ksp + 4 * kt) * 2 * kImg, steps * 2 * kImg, &full[s]);
         }
       }
     }
@@ -166,17 +198,15 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           if (!(ok = tc::mbar_wait(&full[s], (g / STAGES) & 1, err, 202))) break;
           tc::fence_after_sync();
           const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
-          const uint32_t sa = st, sb = st + A_BYTES, ssfa = st + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
+          const uint32_t sa = st + C::A_OFF, sb = st + C::B_OFF, ssfa = st + C::SFA_OFF, ssfb = st + C::SFB_OFF;
           const int steps = min(4, ksteps - 4 * kt);
-          for (int kk = 0; kk < steps; ++kk) {
-            tmem_cp_sf(t_sfa + 4 * kk, desc_sf_atom(ssfa + 512 * kk));
-#pragma unroll
-            for (int rb = 0; rb < BN / 128; ++rb)
-              tmem_cp_sf(t_sfb + 4 * (BN / 128) * kk + 4 * rb, desc_sf_atom(ssfb + rb * 2048 + 512 * kk));
-          }
+          for (int kk = 0; kk < steps; kk += 2)  // A: K steps kk, kk + 1 -> columns 4kk .. 4kk + 7
+            tmem_cp_sf_pair(t_sfa + 4 * kk, desc_sf_pair(ssfa + kk * kImg));
+          for (int kk = 0; kk < steps; ++kk)     // B: both halves of K step kk -> columns 8kk .. 8kk + 7
+            tmem_cp_sf_pair(t_sfb + 8 * kk, desc_sf_pair(ssfb + 2 * kk * kImg));
           for (int kk = 0; kk < steps; ++kk)
             mma_nvf4(t_acc, tc::desc_kmajor_sw128(sa + 32 * kk), tc::desc_kmajor_sw128(sb + 32 * kk), idesc,
-                     t_sfa + 4 * kk, t_sfb + 4 * (BN / 128) * kk, kt > 0 || kk > 0);
+                     t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
           tc::mma_commit(&empty[s]);
         }
         tc::mma_commit(&acc_full[ab]);
@@ -274,9 +304,24 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_byte
 
 using namespace rb2;
 
+namespace {
+// workspace: [status word, padded to 1 KB][A scale images][B scale images]
+struct GemmWs {
+  int64_t ksp, img_a, img_b, total;
+};
+GemmWs gemm_ws(int64_t M, int64_t N, int64_t K) {
+  GemmWs w;
+  w.ksp = (K / 64 + 3) / 4 * 4;
+  w.img_a = (M + 127) / 128 * w.ksp * kImg;
+  w.img_b = (N + 255) / 256 * w.ksp * 2 * kImg;
+  w.total = 1024 + w.img_a + w.img_b;
+  return w;
+}
+}  // namespace
+
 extern "C" size_t rb2_nvfp4_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
-  (void)M; (void)N; (void)K;
-  return 256;  // device status word
+  if (M <= 0 || N <= 0 || K <= 0) return 1024;
+  return size_t(gemm_ws(M, N, K).total);
 }
 
 extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
@@ -300,7 +345,7 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CUtensorMap ma, mb;
   int rc;
-  using Wide = GemmCfg<256, 4, 1>;
+  using Wide = GemmCfg<256, 3, 1>;
   const int BN = Wide::BN;
   if ((rc = make_map(&ma, a_codes, M, K / 2, BM))) return rc;
   if ((rc = make_map(&mb, b_codes, N, K / 2, BN))) return rc;
@@ -310,11 +355,22 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t ntiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   dim3 grid(unsigned(ntiles < sms ? ntiles : sms));
+  const GemmWs gw = gemm_ws(M, N, K);
+  uint8_t* img_a = static_cast<uint8_t*>(ws) + 1024;
+  uint8_t* img_b = img_a + gw.img_a;
+  {
+    ProfScope ps_("nvfp4_sf_images", s);
+    const int64_t n16 = (gw.img_a + gw.img_b) / 16;
+    sf_images_kernel<<<unsigned(std::min<int64_t>((n16 + 255) / 256, int64_t(sms) * 16)), 256, 0, s>>>(
+        a_scales_blocked, b_scales_blocked, int((M + 127) / 128), int((N + 127) / 128), int(K / 64), int(gw.ksp), img_a,
+        img_b);
+  }
+  RB2_CHECK_LAUNCH("nvfp4_sf_images");
   {
     ProfScope ps_("nvfp4_gemm", s);
       RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide>, cudaFuncAttributeMaxDynamicSharedMemorySize, Wide::SMEM),
              "nvfp4_gemm: smem attribute");
-    nvfp4_gemm_kernel<Wide><<<grid, kThreads, Wide::SMEM, s>>>(ma, mb, a_scales_blocked, b_scales_blocked, a_gscale,
+    nvfp4_gemm_kernel<Wide><<<grid, kThreads, Wide::SMEM, s>>>(ma, mb, img_a, img_b, int(gw.ksp), a_gscale,
                                                                b_gscale, int(M), int(N), int(K), out,
                                                                out_dtype == RB2_BF16, static_cast<int*>(ws));
   }
