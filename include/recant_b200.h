@@ -120,13 +120,27 @@ RB2_API int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const fl
 RB2_API int rb2_gdn_state_fold(const float* M, const float* c, const float* s0, int64_t n, int H, int d,
                                int transpose, int identity_init, float* states, float* final_out, void* stream);
 
+/* Recurrent (token-by-token) forward for short calls with a carried state: the decode step of
+ * GatedDeltaNet.forward with a LayerCache (layers.py:177-180; serve/engine.py:107-119), the same
+ * arithmetic as gdn_torch on one padded chunk (ops.py:21-54). Arguments as rb2_gdn_fwd without
+ * path / workspace; no backward (the serving path runs under no_grad). h0, hT: [n_seqs, Hv, 128,
+ * 128] fp32, either may be NULL, hT may equal h0 (updated in place). Cost: one read and one write
+ * of the state per call, O(T) sequential steps. */
+RB2_API int rb2_gdn_recurrent_fwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                                  const float* h0, const int64_t* cu_seqlens, int B, int T, int n_seqs, int Hk,
+                                  int Hv, int dk, int dv, int dtype, float scale, void* o, float* hT, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Element-wise stages of the GDN block (recant/model/layers.py:148-182), bf16 activations:
  *
  * rb2_conv_silu_fwd: y = silu(bf16(causal depthwise conv1d(x, w))), x [B, T, C], w [C, K] (K = 4,
  *   zero prefix; layers.py:157-168). The output channels go to y0 (all C when y1 = y2 = NULL) or are
  *   split into y0 [B, T, s1], y1 [B, T, s2 - s1], y2 [B, T, C - s2] -- the block's q, k, v
- *   (layers.py:169). rb2_conv_silu_bwd: dx from x, w and the output gradient (same split).
+ *   (layers.py:169). prev (NULL = zeros) is the cached prefix [B, C, 3] of the decode path
+ *   (LayerCache.conv_state: token -3 + j in column j, layers.py:159-166); new_state (optional,
+ *   [B, C, 3]) receives the last 3 tokens of cat(prev, x), the next call's prefix.
+ *   rb2_conv_silu_bwd: dx from x, prev, w and the output gradient (same split; prev gets no gradient,
+ *   as the reference's cache is detached).
  * rb2_gdn_gates_fwd: g = -exp(A_log[h]) softplus(a + dt_bias[h]) (fp32) and beta = sigmoid(b)
  *   (bf16) over n = B*T*H entries (fused_ops.py:32-33, layers.py:154); _bwd gives da, db.
  * rb2_gated_rmsnorm_fwd: per row of dim = 128, y = bf16(w * bf16(x rsqrt(mean x^2 + eps))) *
@@ -134,10 +148,10 @@ RB2_API int rb2_gdn_state_fold(const float* M, const float* c, const float* s0, 
  * The block's conv, gate and norm weights are frozen (the reference trains LoRA only), so only
  * input gradients are produced.
  * ------------------------------------------------------------------------------------------- */
-RB2_API int rb2_conv_silu_fwd(const void* x, const void* w, int B, int T, int C, int K, void* y0, void* y1,
-                              void* y2, int s1, int s2, void* stream);
-RB2_API int rb2_conv_silu_bwd(const void* x, const void* w, const void* dy0, const void* dy1, const void* dy2,
-                              int s1, int s2, int B, int T, int C, int K, void* dx, void* stream);
+RB2_API int rb2_conv_silu_fwd(const void* x, const void* w, const void* prev, int B, int T, int C, int K, void* y0,
+                              void* y1, void* y2, int s1, int s2, void* new_state, void* stream);
+RB2_API int rb2_conv_silu_bwd(const void* x, const void* w, const void* prev, const void* dy0, const void* dy1,
+                              const void* dy2, int s1, int s2, int B, int T, int C, int K, void* dx, void* stream);
 RB2_API int rb2_gdn_gates_fwd(const void* a, const void* b, const float* A_log, const float* dt_bias, int64_t n,
                               int H, float* g, void* beta, void* stream);
 RB2_API int rb2_gdn_gates_bwd(const void* a, const void* beta, const float* A_log, const float* dt_bias,

@@ -7,14 +7,16 @@ CPU ops, for a bf16 block:
              activation dtype -- plus LoRA as one addmm y + (alpha / r) (x A^T) B^T (the default
              fused path, layers.py:86-97)
   beta, a  = sigmoid(x Wb^T), x Wa^T (bf16 dense: N < 256 is never quantized, layers.py:47-48)
-  conv     = silu(conv1d(cat(zeros, qkv^T), w, groups=C))^T              (layers.py:162-166)
+  conv     = silu(conv1d(cat(prefix, qkv^T), w, groups=C))^T             (layers.py:157-166)
+             prefix = zeros, or a cache's conv_state, which then becomes cat[..., -3:]
   q, k, v  = split(conv); g = -exp(A_log) softplus(a + dt_bias)          (fused_ops.py:32-33)
   core     = gdn_torch(q, k, v, g, beta) with q, k repeated to Hv        (layers.py:174-178; oracle.gdn)
+             (with a cache: initial_state = rec_state, which becomes the final state)
   out      = QLinear_out(rmsnorm_gated(core, z))                          (fused_ops.py:11-16)
 The backward is autograd over this graph. The NVFP4 linear's backward quantizes dy with
 round-to-nearest here, where the reference draws stochastic rounding from torch's RNG: the B200
 block is compared with stochastic rounding switched off. NVFP4 arithmetic comes from oracle.nvfp4
-(bit-exact quantizer) in float64 matmuls.
+(bit-exact quantizer) and its emulated GEMM, the same float32 torch matmul as the reference.
 """
 from __future__ import annotations
 
@@ -79,10 +81,12 @@ def quantized(weight: torch.Tensor, lora=None) -> dict:
     return p
 
 
-def block_forward(x, P, Hk, Hv, d=128, eps=1e-6):
+def block_forward(x, P, Hk, Hv, d=128, eps=1e-6, cache=None):
     """x [B, T, hidden] bf16; P: {"in_proj_qkv", "in_proj_z", "out_proj": qlinear dicts,
     "in_proj_b", "in_proj_a": {"weight"}, "conv": [C, 1, 4], "A_log", "dt_bias": [Hv],
-    "norm": [d]} -> [B, T, hidden]."""
+    "norm": [d]} -> [B, T, hidden]. ``cache``: an object with ``conv_state`` / ``rec_state`` (None
+    at first), read and replaced as GatedDeltaNet.forward does with a LayerCache (layers.py:158-166,
+    177-180)."""
     b, t, _ = x.shape
     key_dim, value_dim = Hk * d, Hv * d
     conv_dim = 2 * key_dim + value_dim
@@ -91,15 +95,21 @@ def block_forward(x, P, Hk, Hv, d=128, eps=1e-6):
     beta = qlinear(x, P["in_proj_b"]).sigmoid()
     a = qlinear(x, P["in_proj_a"])
     mixed = qkv.transpose(1, 2)
-    prev = torch.zeros(b, conv_dim, 3, dtype=mixed.dtype)
-    cat = torch.cat([prev, mixed], dim=-1)
+    prev = cache.conv_state if cache is not None else None
+    prev = prev if prev is not None else torch.zeros(b, conv_dim, 3, dtype=mixed.dtype)
+    cat = torch.cat([prev.to(mixed.dtype), mixed], dim=-1)
     conv = F.silu(F.conv1d(cat, P["conv"].to(mixed.dtype), groups=conv_dim)).transpose(1, 2)
+    if cache is not None:
+        cache.conv_state = cat[..., -3:].detach().clone()
     q, k, v = torch.split(conv, [key_dim, key_dim, value_dim], dim=-1)
     q = q.reshape(b, t, Hk, d)
     k = k.reshape(b, t, Hk, d)
     v = v.reshape(b, t, Hv, d)
     g = -P["A_log"].float().exp() * F.softplus(a.float() + P["dt_bias"].float())
-    core, _ = OG.gdn(q, k, v, g, beta)
+    init = cache.rec_state if cache is not None else None
+    core, state = OG.gdn(q, k, v, g, beta, initial_state=init, output_final_state=cache is not None)
+    if cache is not None:
+        cache.rec_state = state.detach()
     core = core.to(x.dtype)
     xf = core.reshape(-1, d).float()
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)

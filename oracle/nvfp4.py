@@ -159,11 +159,15 @@ def dequant(codes: np.ndarray, scales_u8: np.ndarray, gscale, k: int) -> np.ndar
 
 
 def gemm_emulated(a, b) -> np.ndarray:
-    """a, b: (codes, scales, gscale, (rows, k)) -> a . b^T in float32 (nvfp4.py:108-110)."""
+    """a, b: (codes, scales, gscale, (rows, k)) -> a . b^T in float32 (nvfp4.py:108-110): both
+    operands dequantised to float32 and multiplied by torch's CPU float32 matmul with the second
+    operand transposed, the same call the reference's emulated backend makes, so that the sums run
+    in the same order."""
+    import torch
     ka, kb = a[3][1], b[3][1]
-    da = dequant(a[0], a[1], a[2], ka).astype(np.float64)
-    db = dequant(b[0], b[1], b[2], kb).astype(np.float64)
-    return (da @ db.T).astype(np.float32)
+    da = torch.from_numpy(np.ascontiguousarray(dequant(a[0], a[1], a[2], ka), dtype=np.float32))
+    db = torch.from_numpy(np.ascontiguousarray(dequant(b[0], b[1], b[2], kb), dtype=np.float32))
+    return (da @ db.t()).float().numpy()
 
 
 def quantize_weight(w: np.ndarray, use_rht: bool = True):

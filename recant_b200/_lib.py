@@ -32,8 +32,9 @@ SIGNATURES = {
     "rb2_gdn_bwd_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
                             _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p, _sz, _p, _i, _i]),
     "rb2_gdn_state_fold": (_i, [_p, _p, _p, _i64, _i, _i, _i, _i, _p, _p, _p]),
-    "rb2_conv_silu_fwd": (_i, [_p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p]),
-    "rb2_conv_silu_bwd": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
+    "rb2_gdn_recurrent_fwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _f, _p, _p, _p]),
+    "rb2_conv_silu_fwd": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _p]),
+    "rb2_conv_silu_bwd": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
     "rb2_gdn_gates_fwd": (_i, [_p, _p, _p, _p, _i64, _i, _p, _p, _p]),
     "rb2_gdn_gates_bwd": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i, _p, _p, _p]),
     "rb2_gated_rmsnorm_fwd": (_i, [_p, _p, _p, _i64, _i, _f, _p, _p, _p]),

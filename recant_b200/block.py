@@ -6,10 +6,13 @@ x [B, T, hidden] bf16 ->
                 (layers.py:152, grouped_linear layers.py:72-97; QLinear layers.py:36-70)
   beta, a     = sigmoid(in_proj_b(x)), in_proj_a(x): bf16 dense, N = Hv < 256, never quantized
                 (layers.py:154-155, 47-48)
-  conv        = silu(causal depthwise conv1d, kernel 4, zero prefix)       (layers.py:157-168)
+  conv        = silu(causal depthwise conv1d, kernel 4; zero prefix, or the cached one when a
+                LayerCache is given, which then receives the next prefix)  (layers.py:157-168)
   q, k, v     = split(conv) into [Hk*128, Hk*128, Hv*128]                  (layers.py:169-172)
   g           = -exp(A_log) softplus(a + dt_bias)                          (fused_ops.py:32-33)
-  core        = chunked GDN (``gdn_b200``; Hk < Hv handled without repeat_interleave)
+  core        = GDN (``gdn_b200``; Hk < Hv handled without repeat_interleave); with a cache the
+                recurrent state is carried in and out (layers.py:177-180): short calls take the
+                token-by-token kernel, longer ones the chunked op
   y           = out_proj(RMSNormGated(core, z))  (NVFP4 + LoRA)            (layers.py:23-34,181)
 
 Kernels: ``rb2_conv_silu_*``, ``rb2_gdn_gates_*``, ``rb2_gated_rmsnorm_*`` (csrc/gdn_block.cu), the
@@ -19,6 +22,7 @@ plain GEMMs through torch (cuBLAS). Frozen weights get no gradients; LoRA A and 
 from __future__ import annotations
 
 import math
+from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
@@ -34,31 +38,39 @@ def _p(t):
 
 class _ConvSiLU(torch.autograd.Function):
     """Returns the conv output split into contiguous [B, T, s1], [B, T, s2 - s1], [B, T, C - s2]
-    tensors (q, k, v of the block) written directly by the kernel."""
+    tensors (q, k, v of the block) written directly by the kernel, and (with ``want_state``) the
+    next call's prefix [B, C, 3]. ``prev`` is the cached prefix (None = zeros); it gets no gradient."""
 
     @staticmethod
-    def forward(ctx, x, w, s1, s2):
+    def forward(ctx, x, w, s1, s2, prev, want_state):
         B, T, C = x.shape
         x = x.contiguous()
         w4 = w.reshape(C, 4).to(torch.bfloat16).contiguous()
+        if prev is not None:
+            prev = prev.to(device=x.device, dtype=torch.bfloat16).contiguous()
+            if prev.shape != (B, C, 3):
+                raise ValueError(f"recant_b200.conv_silu: conv state must be [{B}, {C}, 3], got {tuple(prev.shape)}")
         outs = [torch.empty(B, T, n, dtype=torch.bfloat16, device=x.device) for n in (s1, s2 - s1, C - s2)]
-        L.check(L.lib().rb2_conv_silu_fwd(_p(x), _p(w4), B, T, C, 4, *[_p(o) for o in outs], s1, s2,
-                                          _stream(x.device)), "conv_silu_fwd")
-        ctx.save_for_backward(x, w4)
+        state = torch.empty(B, C, 3, dtype=torch.bfloat16, device=x.device) if want_state else None
+        L.check(L.lib().rb2_conv_silu_fwd(_p(x), _p(w4), _p(prev), B, T, C, 4, *[_p(o) for o in outs], s1, s2,
+                                          _p(state), _stream(x.device)), "conv_silu_fwd")
+        ctx.save_for_backward(x, w4, prev)
         ctx.s1, ctx.s2 = s1, s2
-        return tuple(outs)
+        if state is not None:
+            ctx.mark_non_differentiable(state)
+        return (*outs, state)
 
     @staticmethod
-    def backward(ctx, *dys):
-        x, w4 = ctx.saved_tensors
+    def backward(ctx, *grads):
+        x, w4, prev = ctx.saved_tensors
         B, T, C = x.shape
         widths = (ctx.s1, ctx.s2 - ctx.s1, C - ctx.s2)
         dys = [torch.zeros(B, T, n, dtype=torch.bfloat16, device=x.device) if d is None
-               else d.to(torch.bfloat16).contiguous() for d, n in zip(dys, widths)]
+               else d.to(torch.bfloat16).contiguous() for d, n in zip(grads[:3], widths)]
         dx = torch.empty_like(x)
-        L.check(L.lib().rb2_conv_silu_bwd(_p(x), _p(w4), *[_p(d) for d in dys], ctx.s1, ctx.s2, B, T, C, 4, _p(dx),
-                                          _stream(x.device)), "conv_silu_bwd")
-        return dx, None, None, None
+        L.check(L.lib().rb2_conv_silu_bwd(_p(x), _p(w4), _p(prev), *[_p(d) for d in dys], ctx.s1, ctx.s2, B, T, C, 4,
+                                          _p(dx), _stream(x.device)), "conv_silu_bwd")
+        return dx, None, None, None, None, None
 
 
 class _Gates(torch.autograd.Function):
@@ -109,10 +121,13 @@ class _GatedRMSNorm(torch.autograd.Function):
         return dx, dz, None, None
 
 
-def conv_silu(x, weight, s1, s2):
+def conv_silu(x, weight, s1, s2, prev=None, want_state=False):
     """silu(causal depthwise conv1d(x, weight [C, 1, 4])), x [B, T, C] bf16 (layers.py:157-168), split
-    into channels [0, s1), [s1, s2), [s2, C) as three contiguous tensors (layers.py:169)."""
-    return _ConvSiLU.apply(x, weight, s1, s2)
+    into channels [0, s1), [s1, s2), [s2, C) as three contiguous tensors (layers.py:169). ``prev``:
+    the cached prefix [B, C, 3] (None = zeros). With ``want_state`` a fourth result is the next
+    prefix, the last 3 tokens of cat(prev, x) (layers.py:165-166); otherwise it is None."""
+    q, k, v, state = _ConvSiLU.apply(x, weight, s1, s2, prev, want_state)
+    return (q, k, v, state) if want_state else (q, k, v)
 
 
 def gdn_gates(a, b, A_log, dt_bias):
@@ -293,7 +308,12 @@ class GDNBlock(nn.Module):
         blk.norm_weight.copy_(sd["norm.weight"].to(device, torch.bfloat16).float())
         return blk
 
-    def forward(self, x):
+    def forward(self, x, cache=None, pos_offset=0):
+        """x [B, T, hidden] -> [B, T, hidden]. ``cache``: any object with ``conv_state`` ([B, C, 3]
+        bf16 or None) and ``rec_state`` ([B, Hv, 128, 128] fp32 or None) attributes -- the
+        reference's ``LayerCache`` (layers.py:111-130) or :class:`LayerCache` here; both are read
+        and replaced as GatedDeltaNet.forward does (layers.py:158-166, 177-180). ``pos_offset`` is
+        accepted for the reference's signature and unused (the block has no positions)."""
         B, T, _ = x.shape
         d = self.d
         qkv, z = grouped_linear(x, [self.in_proj_qkv, self.in_proj_z])
@@ -302,11 +322,32 @@ class GDNBlock(nn.Module):
             b_lin, a = ba[..., :self.Hv], ba[..., self.Hv:]
         else:
             b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
-        q, k, v = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim)
+        if cache is None:
+            q, k, v = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim)
+        else:
+            q, k, v, state = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim,
+                                       prev=cache.conv_state, want_state=True)
+            cache.conv_state = state
         q = q.view(B, T, self.Hk, d)
         k = k.view(B, T, self.Hk, d)
         v = v.view(B, T, self.Hv, d)
         g, beta = gdn_gates(a, b_lin, self.A_log, self.dt_bias)
-        core, _ = gdn_b200(q, k, v, g, beta)
+        if cache is None:
+            core, _ = gdn_b200(q, k, v, g, beta)
+        else:
+            core, rec = gdn_b200(q, k, v, g, beta, initial_state=cache.rec_state, output_final_state=True)
+            cache.rec_state = rec.detach()
         y = gated_rmsnorm(core.reshape(-1, d), z.reshape(-1, d), self.norm_weight, self.eps)
         return self.out_proj(y.reshape(B, T, -1))
+
+
+@dataclass
+class LayerCache:
+    """Per-layer decode state with the reference's fields (layers.py:111-130): the conv prefix
+    [B, conv_dim, 3] and the recurrent state [B, Hv, 128, 128] fp32 (None before the first call)."""
+    conv_state: torch.Tensor | None = None
+    rec_state: torch.Tensor | None = None
+
+    def fork(self) -> "LayerCache":
+        return LayerCache(None if self.conv_state is None else self.conv_state.clone(),
+                          None if self.rec_state is None else self.rec_state.clone())

@@ -83,6 +83,19 @@ __device__ __forceinline__ void load_taps4(const bf16* w, int c, float (&wt)[kCo
 // silu with a fast reciprocal (sigmoid to a few ulp; the output is rounded to bf16)
 __device__ __forceinline__ float fsigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
+// 8 channels of token t < 0 from the cached prefix prev [B, C, 3] (token t = column 3 + t; the
+// reference's LayerCache.conv_state, layers.py:159-166), or zeros without one
+__device__ __forceinline__ void halo_from_prev(bf16* dst, const bf16* prev, int b, int C, int c, int t) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bf16 lo = prev[(int64_t(b) * C + c + 2 * i) * kHalo + kHalo + t];
+    const bf16 hi = prev[(int64_t(b) * C + c + 2 * i + 1) * kHalo + kHalo + t];
+    w[i] = uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 struct TileIdx {
   int b, t0, c0, nchunk;
 };
@@ -98,12 +111,17 @@ __device__ __forceinline__ TileIdx tile_of(int64_t tile, int T, int C) {
 
 // y[b, t, c] = bf16(silu(bf16(sum_j w[c, j] x[b, t - 3 + j, c])))
 __global__ void __launch_bounds__(256, 4) conv_silu_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                               int B, int T, int C, Split y) {
+                                                               const bf16* __restrict__ prev, int B, int T, int C,
+                                                               Split y) {
   __shared__ __align__(16) bf16 xs[kTileT + kHalo][kTileC];  // row i = token t0 - 3 + i
   const TileIdx ti = tile_of(blockIdx.x, T, C);
   const bf16* xb = x + int64_t(ti.b) * T * C + ti.c0;
   for (int e = threadIdx.x; e < (kTileT + kHalo) * kChunks; e += 256) {
     const int r = e / kChunks, ch = e % kChunks, t = ti.t0 - kHalo + r;
+    if (t < 0 && prev && ch < ti.nchunk) {
+      halo_from_prev(&xs[r][ch * 8], prev, ti.b, C, ti.c0 + ch * 8, t);
+      continue;
+    }
     const bool ok = ch < ti.nchunk && t >= 0 && t < T;
     cp_async16(&xs[r][ch * 8], ok ? xb + int64_t(t) * C + ch * 8 : x, ok);
   }
@@ -139,13 +157,18 @@ __global__ void __launch_bounds__(256, 4) conv_silu_fwd_kernel(const bf16* __res
 // du[t] = bf16(dy[t] silu'(u[t])) (u recomputed, bf16 as in the forward) for t in [t0, t0 + 35);
 // dx[t] = sum_j w[c, j] du[t + 3 - j] for t in [t0, t0 + 32)
 __global__ void __launch_bounds__(256, 4) conv_silu_bwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                               Split dy, int B, int T, int C, bf16* __restrict__ dx) {
+                                                               const bf16* __restrict__ prev, Split dy, int B, int T,
+                                                               int C, bf16* __restrict__ dx) {
   __shared__ __align__(16) bf16 xs[kTileT + 2 * kHalo][kTileC];  // row i = token t0 - 3 + i
   __shared__ __align__(16) bf16 ds[kTileT + kHalo][kTileC];      // row i = token t0 + i: dy, then du
   const TileIdx ti = tile_of(blockIdx.x, T, C);
   const bf16* xb = x + int64_t(ti.b) * T * C + ti.c0;
   for (int e = threadIdx.x; e < (kTileT + 2 * kHalo) * kChunks; e += 256) {
     const int r = e / kChunks, ch = e % kChunks, t = ti.t0 - kHalo + r;
+    if (t < 0 && prev && ch < ti.nchunk) {
+      halo_from_prev(&xs[r][ch * 8], prev, ti.b, C, ti.c0 + ch * 8, t);
+      continue;
+    }
     const bool ok = ch < ti.nchunk && t >= 0 && t < T;
     cp_async16(&xs[r][ch * 8], ok ? xb + int64_t(t) * C + ch * 8 : x, ok);
   }
@@ -210,6 +233,23 @@ __global__ void __launch_bounds__(256, 4) conv_silu_bwd_kernel(const bf16* __res
       dw[0][i] = dw[1][i]; dw[1][i] = dw[2][i]; dw[2][i] = dw[3][i];
     }
     if (t < T) store4(dx + (int64_t(ti.b) * T + t) * C + c, out);
+  }
+}
+
+// The next call's prefix: the last 3 tokens of cat(prev, x) per channel, [B, C, 3] (layers.py:165-166)
+__global__ void conv_state_kernel(const bf16* __restrict__ x, const bf16* __restrict__ prev, int B, int T, int C,
+                                  bf16* __restrict__ out) {
+  const int64_t n = int64_t(B) * C;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = int(i % C), b = int(i / C);
+#pragma unroll
+    for (int j = 0; j < kHalo; ++j) {
+      const int p = T + j;  // position in cat(prev, x)
+      bf16 val = __float2bfloat16_rn(0.f);
+      if (p >= kHalo) val = x[(int64_t(b) * T + p - kHalo) * C + c];
+      else if (prev) val = prev[i * kHalo + p];
+      out[i * kHalo + j] = val;
+    }
   }
 }
 
@@ -337,8 +377,8 @@ int make_split(void* p0, void* p1, void* p2, int s1, int s2, int C, Split* out) 
 }  // namespace
 }  // namespace rb2
 
-extern "C" int rb2_conv_silu_fwd(const void* x, const void* w, int B, int T, int C, int K, void* y0, void* y1,
-                                 void* y2, int s1, int s2, void* stream) {
+extern "C" int rb2_conv_silu_fwd(const void* x, const void* w, const void* prev, int B, int T, int C, int K, void* y0,
+                                 void* y1, void* y2, int s1, int s2, void* new_state, void* stream) {
   RB2_CHECK_ARG(K == kConvK, "conv_silu: kernel size must be 4 (got %d)", K);
   RB2_CHECK_ARG(B >= 1 && T >= 1 && C >= 8 && C % 8 == 0, "conv_silu: bad sizes B=%d T=%d C=%d", B, T, C);
   RB2_CHECK_ARG(x && w && aligned16(x) && (reinterpret_cast<uintptr_t>(w) & 7) == 0,
@@ -349,15 +389,23 @@ extern "C" int rb2_conv_silu_fwd(const void* x, const void* w, int B, int T, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t n = int64_t(B) * ((T + kTileT - 1) / kTileT) * ((C + kTileC - 1) / kTileC);
   RB2_CHECK_ARG(n < (int64_t(1) << 31), "conv_silu: too many tiles (%lld)", (long long)n);
-  ProfScope ps_("block_conv_silu_fwd", s);
-  conv_silu_fwd_kernel<<<unsigned(n), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), B, T,
-                                                          C, y);
+  {
+    ProfScope ps_("block_conv_silu_fwd", s);
+    conv_silu_fwd_kernel<<<unsigned(n), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w),
+                                                      static_cast<const bf16*>(prev), B, T, C, y);
+  }
   RB2_CHECK_LAUNCH("conv_silu_fwd");
+  if (new_state) {
+    ProfScope ps_("block_conv_state", s);
+    conv_state_kernel<<<grid_for(int64_t(B) * C, 256), 256, 0, s>>>(
+        static_cast<const bf16*>(x), static_cast<const bf16*>(prev), B, T, C, static_cast<bf16*>(new_state));
+    RB2_CHECK_LAUNCH("conv_state");
+  }
   return RB2_OK;
 }
 
-extern "C" int rb2_conv_silu_bwd(const void* x, const void* w, const void* dy0, const void* dy1, const void* dy2,
-                                 int s1, int s2, int B, int T, int C, int K, void* dx, void* stream) {
+extern "C" int rb2_conv_silu_bwd(const void* x, const void* w, const void* prev, const void* dy0, const void* dy1,
+                                 const void* dy2, int s1, int s2, int B, int T, int C, int K, void* dx, void* stream) {
   RB2_CHECK_ARG(K == kConvK, "conv_silu: kernel size must be 4 (got %d)", K);
   RB2_CHECK_ARG(B >= 1 && T >= 1 && C >= 8 && C % 8 == 0, "conv_silu: bad sizes B=%d T=%d C=%d", B, T, C);
   RB2_CHECK_ARG(x && w && dx && aligned16(x) && aligned16(dx) && (reinterpret_cast<uintptr_t>(w) & 7) == 0,
@@ -369,8 +417,8 @@ extern "C" int rb2_conv_silu_bwd(const void* x, const void* w, const void* dy0, 
   const int64_t n = int64_t(B) * ((T + kTileT - 1) / kTileT) * ((C + kTileC - 1) / kTileC);
   RB2_CHECK_ARG(n < (int64_t(1) << 31), "conv_silu: too many tiles (%lld)", (long long)n);
   ProfScope ps_("block_conv_silu_bwd", s);
-  conv_silu_bwd_kernel<<<unsigned(n), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w), dy, B, T,
-                                                          C, static_cast<bf16*>(dx));
+  conv_silu_bwd_kernel<<<unsigned(n), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w),
+                                                    static_cast<const bf16*>(prev), dy, B, T, C, static_cast<bf16*>(dx));
   RB2_CHECK_LAUNCH("conv_silu_bwd");
   return RB2_OK;
 }

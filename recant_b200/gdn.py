@@ -9,7 +9,9 @@ Drop-in for ``recant.model.ops``'s GDN backends (recant/model/ops.py:5-10,56-67)
   dbeta and d(initial_state).
 * Extensions (defaults keep every reference call site unchanged): ``cu_seqlens`` (int64 [N+1],
   B == 1, per-sequence state reset, the fla varlen convention), q/k with Hk < Hv heads (GQA
-  without repeat_interleave), ``scale`` and ``path`` ("auto" | "exact" | "fast").
+  without repeat_interleave), ``scale`` and ``path`` ("auto" | "exact" | "fast" | "recurrent").
+* :func:`gdn_recurrent`: the token-by-token forward of the decode step (short calls with a carried
+  state and no gradient), chosen automatically by ``gdn_b200`` for such calls.
 * :data:`GDN_BACKENDS`, :func:`set_gdn_backend`, :func:`get_gdn_backend`, :func:`gdn_core` mirror
   ops.py's registry; :func:`register` adds ``'b200'`` to the reference's own registry.
 """
@@ -110,9 +112,57 @@ class _GDNFunction(torch.autograd.Function):
         return dq, dk, dv, dg, dbeta.to(ctx.beta_dtype), dh0, None, None, None, None
 
 
+# Calls of at most this many tokens that need no gradient (the decode step) take the recurrent kernel
+RECURRENT_MAX_T = 16
+
+
+def _needs_grad(*ts):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
+
+
+def gdn_recurrent(q, k, v, g, beta, initial_state=None, output_final_state=False, *, cu_seqlens=None, scale=None):
+    """Forward only, token by token, with a carried fp32 state: the decode step (layers.py:177-180 under
+    serve/engine.py:107-119). Same contract and arithmetic as gdn_torch on one padded chunk
+    (ops.py:21-54); no autograd graph."""
+    if not q.is_cuda:
+        raise ValueError("recant_b200.gdn: inputs must be CUDA tensors (no CPU path)")
+    if q.dim() != 4 or k.shape != q.shape or v.dim() != 4:
+        raise ValueError(f"recant_b200.gdn: q/k must be [B,T,Hk,dk] and v [B,T,Hv,dv]; got "
+                         f"{tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+    B, T, Hk, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    if v.shape[:2] != (B, T) or g.shape != (B, T, Hv) or beta.shape != (B, T, Hv):
+        raise ValueError("recant_b200.gdn: g and beta must be [B,T,Hv] matching v")
+    if q.dtype not in _DT:
+        raise TypeError(f"recant_b200.gdn: dtype {q.dtype} unsupported (float32 or bfloat16)")
+    n_seqs = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    if initial_state is not None and initial_state.shape != (n_seqs, Hv, dk, dv):
+        raise ValueError(f"recant_b200.gdn: initial_state must be [{n_seqs},{Hv},{dk},{dv}]")
+    dt = q.dtype
+    q, k, v = (t.detach().contiguous() for t in (q, k, v))
+    g = g.detach().to(torch.float32).contiguous()
+    beta_k = beta.detach().to(dt).contiguous()
+    h0 = None if initial_state is None else initial_state.detach().to(torch.float32).contiguous()
+    cu = None if cu_seqlens is None else cu_seqlens.to(device=q.device, dtype=torch.int64).contiguous()
+    o = torch.empty(B, T, Hv, dv, dtype=dt, device=q.device)
+    hT = torch.empty(n_seqs, Hv, dk, dv, dtype=torch.float32, device=q.device) if output_final_state else None
+    sc = float(dk ** -0.5 if scale is None else scale)
+    L.check(L.lib().rb2_gdn_recurrent_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta_k), L.ptr(h0),
+                                          L.ptr(cu), B, T, n_seqs, Hk, Hv, dk, dv, _DT[dt], sc, L.ptr(o), L.ptr(hT),
+                                          _stream(q.device)), "gdn_recurrent_fwd")
+    return o, hT
+
+
 def gdn_b200(q, k, v, g, beta, initial_state=None, output_final_state=False, *, cu_seqlens=None,
              scale=None, path="auto"):
-    """Chunked GDN on B200 with gdn_torch's contract (recant/model/ops.py:21-54)."""
+    """GDN on B200 with gdn_torch's contract (recant/model/ops.py:21-54): the chunked op, or for a
+    call of at most RECURRENT_MAX_T tokens that needs no gradient (``path="auto"``), or always with
+    ``path="recurrent"``, the token-by-token forward."""
+    if path == "recurrent" or (path == "auto" and q.shape[1] <= RECURRENT_MAX_T
+                               and not _needs_grad(q, k, v, g, beta, initial_state)):
+        o, hT = gdn_recurrent(q, k, v, g, beta, initial_state, output_final_state, cu_seqlens=cu_seqlens,
+                              scale=scale)
+        return o, (hT if output_final_state else None)
     o, hT = _GDNFunction.apply(q, k, v, g, beta, initial_state, cu_seqlens, output_final_state, scale, path)
     return o, (hT if output_final_state else None)
 

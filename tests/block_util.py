@@ -30,3 +30,18 @@ def oracle_params(G, requires_grad=False):
     P["A_log"], P["dt_bias"] = G["A_log"].to(bf), G["dt_bias"].to(bf)
     P["norm"] = G["norm.weight"].to(bf)
     return P
+
+
+def decode_golden():
+    """tests/golden/block_decode_golden.npz: the reference block with a LayerCache over a prefill,
+    three single-token steps and a 5-token chunk (tests/golden/make_golden.py:decode_main)."""
+    z = np.load(os.path.join(HERE, "golden", "block_decode_golden.npz"))
+    return {k: torch.from_numpy(z[k]) for k in z.files}
+
+
+class Cache:
+    """A LayerCache stand-in: the two fields GatedDeltaNet.forward reads and replaces."""
+
+    def __init__(self):
+        self.conv_state = None
+        self.rec_state = None

@@ -89,11 +89,11 @@ def main(ref_root: str) -> None:
     print("wrote", sorted(arrays))
 
 
-def block_main(ref_root: str) -> None:
-    """``tests/golden/block_golden.npz``: the reference ``GatedDeltaNet`` (recant/model/layers.py:
-    133-182) at a small bf16 configuration (hidden 256, Hk 1, Hv 2, head dim 128) with NVFP4
-    projections and rank-16 LoRA (random B so that LoRA contributes): its weights (as fp32 values of
-    the bf16 parameters, taken before quantisation), a seeded input and the forward output."""
+def _reference_block(ref_root: str):
+    """The reference ``GatedDeltaNet`` (recant/model/layers.py:133-182) at a small bf16
+    configuration (hidden 256, Hk 1, Hv 2, head dim 128) with NVFP4 projections and rank-16 LoRA
+    (random B so that LoRA contributes), and its weights (fp32 values of the bf16 parameters, taken
+    before quantisation). Returns (block, arrays, generator, layers module)."""
     sys.path.insert(0, ref_root)
     from recant.model import layers
     from recant.model.config import TextConfig
@@ -122,6 +122,13 @@ def block_main(ref_root: str) -> None:
             lin.lora_B.copy_(torch.randn(lin.lora_B.shape, generator=gen) * 0.02)
         arrays[name + ".lora_A"] = lin.lora_A.detach().numpy()
         arrays[name + ".lora_B"] = lin.lora_B.detach().numpy()
+    return blk, arrays, gen, layers
+
+
+def block_main(ref_root: str) -> None:
+    """``tests/golden/block_golden.npz``: the reference block's weights, a seeded input [1, 70, 256]
+    and the forward output."""
+    blk, arrays, gen, _ = _reference_block(ref_root)
     x = torch.randn(1, 70, 256, generator=gen).to(torch.bfloat16)
     with torch.no_grad():
         out = blk(x)
@@ -131,6 +138,32 @@ def block_main(ref_root: str) -> None:
     print("block golden: out", tuple(out.shape), float(out.float().abs().mean()))
 
 
+def decode_main(ref_root: str) -> None:
+    """``tests/golden/block_decode_golden.npz``: the same reference block (weights in
+    block_golden.npz) driven as the serving engine drives it (serve/engine.py:107-119), with a
+    ``LayerCache`` (layers.py:111-130) over 2 sequences of a seeded input [2, 48, 256]: a 40-token
+    prefill, three single-token steps, then a 5-token chunk. Stores every output, the cache's conv
+    state after each call and its recurrent state after the prefill and at the end."""
+    blk, _, _, layers = _reference_block(ref_root)
+    gen = torch.Generator().manual_seed(12)
+    x = torch.randn(2, 48, 256, generator=gen).to(torch.bfloat16)
+    cache = layers.LayerCache()
+    calls = [(0, 40), (40, 41), (41, 42), (42, 43), (43, 48)]
+    arrays = {"x": x.float().numpy()}
+    with torch.no_grad():
+        for i, (s, e) in enumerate(calls):
+            out = blk(x[:, s:e], cache, s)
+            arrays[f"out{i}"] = out.float().numpy()
+            arrays[f"conv_state{i}"] = cache.conv_state.float().numpy()
+            if i in (0, len(calls) - 1):  # after the prefill and at the end
+                arrays[f"rec_state{i}"] = cache.rec_state.float().numpy()
+    arrays["calls"] = np.array(calls, dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "block_decode_golden.npz"), **arrays)
+    print("decode golden:", [tuple(arrays[f"out{i}"].shape) for i in range(len(calls))])
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-    block_main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    main(root)
+    block_main(root)
+    decode_main(root)
