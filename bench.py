@@ -327,6 +327,89 @@ def comparator_arm(args):
     return 0
 
 
+def decode_arm(args):
+    """--decode: the serving step (serve/engine.py:107-119 -> GatedDeltaNet.forward with a LayerCache):
+    one GDN block (hidden 4096, Hk 16, Hv 32, NVFP4 + LoRA r16 projections) fed one new token per
+    sequence with the conv prefix and the fp32 recurrent state carried in the cache, at B = 1 (the
+    engine's per-sequence call) and B = 64 (a batch of sequences). Reports ms per step (CUDA events,
+    median), tokens/s, the same for the step replayed from a CUDA graph (DecodeGraph), and for the
+    recurrent GDN kernel the state bytes it must move (read + write
+    of B x Hv x 128 x 128 fp32) over its launch time against the measured HBM copy peak. One JSON line;
+    outside the driver contract."""
+    import torch
+
+    from recant_b200 import _lib as L
+    from recant_b200.block import GDNBlock, LayerCache
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hidden, Hk, Hv = 4096, 16, 32
+    gen = torch.Generator(device=dev).manual_seed(3)
+    blk = GDNBlock(hidden, Hk, Hv).to(dev)
+    for lin in blk.projections():
+        lin.load_weight(torch.randn(lin.out_features, lin.in_features, device=dev, generator=gen) * 0.02)
+    for lin in (blk.in_proj_qkv, blk.in_proj_z, blk.out_proj):
+        lin.add_lora(16, 32, dev)
+    blk.conv_weight.copy_(torch.randn(blk.conv_weight.shape, device=dev, generator=gen) * 0.3)
+    blk.A_log.copy_(torch.log(torch.empty(Hv, device=dev).uniform_(1.0, 16.0, generator=gen)))
+    pk = peaks()
+    out = {"impl": "decode", "config": "GDN block decode step, hidden 4096, Hk16 Hv32 d128, NVFP4 + LoRA r16, "
+                                       "one token per sequence with cached conv prefix and fp32 state",
+           "steps": args.steps}
+    stream = torch.cuda.current_stream()
+    for B in (1, 64):
+        x_pre = torch.randn(B, 64, hidden, device=dev, generator=gen).to(torch.bfloat16)
+        xs = torch.randn(B, args.steps + 3, hidden, device=dev, generator=gen).to(torch.bfloat16)
+        with torch.no_grad():
+            cache = LayerCache()
+            blk(x_pre, cache)
+            ts = []
+            prof = L.LaunchProfiler(capacity=256 * (args.steps + 3))
+            for i in range(args.steps + 3):
+                if i == 3:
+                    prof.start()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                blk(xs[:, i:i + 1], cache)
+                e1.record(stream)
+                e1.synchronize()
+                if i >= 3:
+                    ts.append(e0.elapsed_time(e1))
+            recs, _ = prof.read()
+        ms = statistics.median(ts)
+        # the same step captured once in a CUDA graph and replayed (DecodeGraph)
+        from recant_b200.block import DecodeGraph
+        with torch.no_grad():
+            step = DecodeGraph(blk, cache, B)
+            tg = []
+            for i in range(args.steps + 3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                step(xs[:, i:i + 1])
+                e1.record(stream)
+                e1.synchronize()
+                if i >= 3:
+                    tg.append(e0.elapsed_time(e1))
+            del step
+        ms_graph = statistics.median(tg)
+        rec = [t for n, t in recs if n == "gdn_recurrent"]
+        rec_ms = statistics.median(rec) if rec else None
+        state_bytes = 2 * B * Hv * 128 * 128 * 4
+        kern = {}
+        for n, t in recs:
+            kern[n] = kern.get(n, 0.0) + t / args.steps
+        out[f"B{B}"] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(B / ms * 1e3, 1),
+                        "graph_ms_per_step": round(ms_graph, 4), "graph_tokens_per_s": round(B / ms_graph * 1e3, 1),
+                        "launches_per_step": round(len(recs) / args.steps, 1),
+                        "kernel_ms_per_step": round(sum(kern.values()), 4),
+                        "gdn_recurrent": None if rec_ms is None else {
+                            "ms": round(rec_ms, 4), "state_bytes": state_bytes,
+                            "achieved_gbs": round(state_bytes / rec_ms / 1e6, 1), "peak_gbs": pk["hbm"],
+                            "frac": round(state_bytes / rec_ms / 1e6 / pk["hbm"], 4)},
+                        "top_kernels": {n: round(t, 4) for n, t in sorted(kern.items(), key=lambda kv: -kv[1])[:6]}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 METRIC4 = "GDN stack fwd+bwd sequence tokens/s (8 GDN layers + NVFP4 out_proj, B1 T131072, context-parallel)"
 C4 = dict(T=131072, layers=8, Hk=16, Hv=32, d=128, hidden=4096, segments_per_rank=4)
 # NVFP4 GEMM roofline: 4x the measured dense bf16 rate (the tcgen05 FP4 : bf16 dense ratio)
@@ -638,6 +721,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode", action="store_true",
+                    help="time the GDN block's decode step (one token per sequence with a cache) at B = 1 and 64 "
+                         "(one JSON line; outside the driver contract)")
     ap.add_argument("--comparators", action="store_true",
                     help="time torch._scaled_mm NVFP4 (and record the fla fault) beside this library "
                          "(one JSON line; outside the driver contract)")
@@ -657,6 +743,8 @@ def main():
         args.warmup = 3
     if args.comparators:
         return comparator_arm(args)
+    if args.decode:
+        return decode_arm(args)
 
     import torch
     import torch.distributed as dist

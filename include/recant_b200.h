@@ -138,7 +138,8 @@ RB2_API int rb2_gdn_recurrent_fwd(const void* q, const void* k, const void* v, c
  *   split into y0 [B, T, s1], y1 [B, T, s2 - s1], y2 [B, T, C - s2] -- the block's q, k, v
  *   (layers.py:169). prev (NULL = zeros) is the cached prefix [B, C, 3] of the decode path
  *   (LayerCache.conv_state: token -3 + j in column j, layers.py:159-166); new_state (optional,
- *   [B, C, 3]) receives the last 3 tokens of cat(prev, x), the next call's prefix.
+ *   [B, C, 3]) receives the last 3 tokens of cat(prev, x), the next call's prefix; it may be prev
+ *   itself (updated in place).
  *   rb2_conv_silu_bwd: dx from x, prev, w and the output gradient (same split; prev gets no gradient,
  *   as the reference's cache is detached).
  * rb2_gdn_gates_fwd: g = -exp(A_log[h]) softplus(a + dt_bias[h]) (fp32) and beta = sigmoid(b)
@@ -208,6 +209,18 @@ RB2_API int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_block
                    const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
                    int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws,
                    size_t ws_bytes, void* stream);
+/* rb2_nvfp4_gemm with B's scale images precomputed (b_images from rb2_nvfp4_gemm_b_images, NULL =
+ * built per call as rb2_nvfp4_gemm does): for frozen weights, whose images are built once. The
+ * images are B's blocked scales laid out as the kernel moves them into tensor memory (each 512-byte
+ * atom repeated 4 times, the two 128-row halves of a 256-row tile interleaved per K step), 16-byte
+ * aligned, rb2_nvfp4_gemm_b_images_size(N, K) bytes. */
+RB2_API int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                              const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                              const uint8_t* b_images, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
+                              void* ws, size_t ws_bytes, void* stream);
+RB2_API size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K);
+RB2_API int rb2_nvfp4_gemm_b_images(const uint8_t* b_scales_blocked, int64_t N, int64_t K, void* out,
+                                    size_t out_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Launch profiler (no counterpart in the reference; measurement support for benchmarks).

@@ -29,7 +29,7 @@ import torch.nn as nn
 
 from . import _lib as L
 from . import nvfp4 as N
-from .gdn import _stream, gdn_b200
+from .gdn import RECURRENT_MAX_T, _stream, gdn_b200, gdn_recurrent
 
 
 def _p(t):
@@ -42,7 +42,7 @@ class _ConvSiLU(torch.autograd.Function):
     next call's prefix [B, C, 3]. ``prev`` is the cached prefix (None = zeros); it gets no gradient."""
 
     @staticmethod
-    def forward(ctx, x, w, s1, s2, prev, want_state):
+    def forward(ctx, x, w, s1, s2, prev, want_state, state_out):
         B, T, C = x.shape
         x = x.contiguous()
         w4 = w.reshape(C, 4).to(torch.bfloat16).contiguous()
@@ -51,7 +51,12 @@ class _ConvSiLU(torch.autograd.Function):
             if prev.shape != (B, C, 3):
                 raise ValueError(f"recant_b200.conv_silu: conv state must be [{B}, {C}, 3], got {tuple(prev.shape)}")
         outs = [torch.empty(B, T, n, dtype=torch.bfloat16, device=x.device) for n in (s1, s2 - s1, C - s2)]
-        state = torch.empty(B, C, 3, dtype=torch.bfloat16, device=x.device) if want_state else None
+        if state_out is not None:
+            if state_out.shape != (B, C, 3) or state_out.dtype != torch.bfloat16 or not state_out.is_contiguous():
+                raise ValueError(f"recant_b200.conv_silu: state_out must be a contiguous bf16 [{B}, {C}, 3] tensor")
+            state = state_out
+        else:
+            state = torch.empty(B, C, 3, dtype=torch.bfloat16, device=x.device) if want_state else None
         L.check(L.lib().rb2_conv_silu_fwd(_p(x), _p(w4), _p(prev), B, T, C, 4, *[_p(o) for o in outs], s1, s2,
                                           _p(state), _stream(x.device)), "conv_silu_fwd")
         ctx.save_for_backward(x, w4, prev)
@@ -70,7 +75,7 @@ class _ConvSiLU(torch.autograd.Function):
         dx = torch.empty_like(x)
         L.check(L.lib().rb2_conv_silu_bwd(_p(x), _p(w4), _p(prev), *[_p(d) for d in dys], ctx.s1, ctx.s2, B, T, C, 4,
                                           _p(dx), _stream(x.device)), "conv_silu_bwd")
-        return dx, None, None, None, None, None
+        return dx, None, None, None, None, None, None
 
 
 class _Gates(torch.autograd.Function):
@@ -121,12 +126,13 @@ class _GatedRMSNorm(torch.autograd.Function):
         return dx, dz, None, None
 
 
-def conv_silu(x, weight, s1, s2, prev=None, want_state=False):
+def conv_silu(x, weight, s1, s2, prev=None, want_state=False, state_out=None):
     """silu(causal depthwise conv1d(x, weight [C, 1, 4])), x [B, T, C] bf16 (layers.py:157-168), split
     into channels [0, s1), [s1, s2), [s2, C) as three contiguous tensors (layers.py:169). ``prev``:
     the cached prefix [B, C, 3] (None = zeros). With ``want_state`` a fourth result is the next
-    prefix, the last 3 tokens of cat(prev, x) (layers.py:165-166); otherwise it is None."""
-    q, k, v, state = _ConvSiLU.apply(x, weight, s1, s2, prev, want_state)
+    prefix, the last 3 tokens of cat(prev, x) (layers.py:165-166), written to ``state_out`` when
+    given (which may be ``prev`` itself: updated in place); otherwise it is None."""
+    q, k, v, state = _ConvSiLU.apply(x, weight, s1, s2, prev, want_state, state_out)
     return (q, k, v, state) if want_state else (q, k, v)
 
 
@@ -308,12 +314,14 @@ class GDNBlock(nn.Module):
         blk.norm_weight.copy_(sd["norm.weight"].to(device, torch.bfloat16).float())
         return blk
 
-    def forward(self, x, cache=None, pos_offset=0):
+    def forward(self, x, cache=None, pos_offset=0, inplace_cache=False):
         """x [B, T, hidden] -> [B, T, hidden]. ``cache``: any object with ``conv_state`` ([B, C, 3]
         bf16 or None) and ``rec_state`` ([B, Hv, 128, 128] fp32 or None) attributes -- the
         reference's ``LayerCache`` (layers.py:111-130) or :class:`LayerCache` here; both are read
-        and replaced as GatedDeltaNet.forward does (layers.py:158-166, 177-180). ``pos_offset`` is
-        accepted for the reference's signature and unused (the block has no positions)."""
+        and replaced as GatedDeltaNet.forward does (layers.py:158-166, 177-180). With
+        ``inplace_cache`` (a short call without gradient, both states present) the states are
+        updated in their own storage instead, so their addresses stay fixed (what a captured CUDA
+        graph needs). ``pos_offset`` is accepted for the reference's signature and unused."""
         B, T, _ = x.shape
         d = self.d
         qkv, z = grouped_linear(x, [self.in_proj_qkv, self.in_proj_z])
@@ -322,18 +330,24 @@ class GDNBlock(nn.Module):
             b_lin, a = ba[..., :self.Hv], ba[..., self.Hv:]
         else:
             b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
+        inplace = (inplace_cache and cache is not None and cache.conv_state is not None
+                   and cache.rec_state is not None and T <= RECURRENT_MAX_T and not torch.is_grad_enabled())
         if cache is None:
             q, k, v = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim)
         else:
             q, k, v, state = conv_silu(qkv, self.conv_weight, self.key_dim, 2 * self.key_dim,
-                                       prev=cache.conv_state, want_state=True)
-            cache.conv_state = state
+                                       prev=cache.conv_state, want_state=True,
+                                       state_out=cache.conv_state if inplace else None)
+            if not inplace:  # in place, the cache keeps its own tensor (state aliases it)
+                cache.conv_state = state
         q = q.view(B, T, self.Hk, d)
         k = k.view(B, T, self.Hk, d)
         v = v.view(B, T, self.Hv, d)
         g, beta = gdn_gates(a, b_lin, self.A_log, self.dt_bias)
         if cache is None:
             core, _ = gdn_b200(q, k, v, g, beta)
+        elif inplace:
+            core, _ = gdn_recurrent(q, k, v, g, beta, cache.rec_state, True, final_state_out=cache.rec_state)
         else:
             core, rec = gdn_b200(q, k, v, g, beta, initial_state=cache.rec_state, output_final_state=True)
             cache.rec_state = rec.detach()
@@ -351,3 +365,47 @@ class LayerCache:
     def fork(self) -> "LayerCache":
         return LayerCache(None if self.conv_state is None else self.conv_state.clone(),
                           None if self.rec_state is None else self.rec_state.clone())
+
+
+class DecodeGraph:
+    """The decode step of a :class:`GDNBlock` captured once in a CUDA graph and replayed per token: a
+    fixed batch of B sequences, one new token each, the cache's conv prefix and fp32 recurrent
+    state held in static tensors and updated in place by the kernels. A step is one copy of the new
+    token into the static input and one graph replay, where the reference's engine runs the block's
+    Python and torch ops for every token (serve/engine.py:107-119 -> layers.py:148-182).
+
+    ``cache`` (fields ``conv_state`` / ``rec_state``, None = zeros) is adopted: after construction
+    its two fields are the static tensors, holding the same values as before."""
+
+    def __init__(self, blk: GDNBlock, cache, B: int):
+        dev = blk.conv_weight.device
+        bf = torch.bfloat16
+        conv = torch.zeros(B, blk.conv_dim, 3, dtype=bf, device=dev)
+        rec = torch.zeros(B, blk.Hv, blk.d, blk.d, dtype=torch.float32, device=dev)
+        if cache.conv_state is not None:
+            conv.copy_(cache.conv_state)
+        if cache.rec_state is not None:
+            rec.copy_(cache.rec_state)
+        cache.conv_state, cache.rec_state = conv, rec
+        self.blk, self.cache = blk, cache
+        self.x = torch.zeros(B, 1, blk.hidden, dtype=bf, device=dev)
+        saved = (conv.clone(), rec.clone())
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.no_grad(), torch.cuda.stream(side):
+            for _ in range(2):  # warm-up (allocations, one-time attributes) outside the capture
+                blk(self.x, cache, inplace_cache=True)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.out = blk(self.x, cache, inplace_cache=True)
+        if cache.conv_state.data_ptr() != conv.data_ptr() or cache.rec_state.data_ptr() != rec.data_ptr():
+            raise RuntimeError("recant_b200.DecodeGraph: the block did not update the cache in place")
+        conv.copy_(saved[0])  # the warm-up steps advanced the states
+        rec.copy_(saved[1])
+
+    def __call__(self, x_t: torch.Tensor) -> torch.Tensor:
+        """x_t [B, 1, hidden] -> [B, 1, hidden] (a view of a static buffer, valid until the next call)."""
+        self.x.copy_(x_t)
+        self.graph.replay()
+        return self.out

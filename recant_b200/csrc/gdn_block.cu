@@ -236,9 +236,10 @@ __global__ void __launch_bounds__(256, 4) conv_silu_bwd_kernel(const bf16* __res
   }
 }
 
-// The next call's prefix: the last 3 tokens of cat(prev, x) per channel, [B, C, 3] (layers.py:165-166)
-__global__ void conv_state_kernel(const bf16* __restrict__ x, const bf16* __restrict__ prev, int B, int T, int C,
-                                  bf16* __restrict__ out) {
+// The next call's prefix: the last 3 tokens of cat(prev, x) per channel, [B, C, 3] (layers.py:165-166).
+// out may be prev (in-place update): a thread owns one channel and reads prev[T + j] before writing
+// out[j], j ascending, so no entry is overwritten before it is read (no __restrict__ on the two).
+__global__ void conv_state_kernel(const bf16* __restrict__ x, const bf16* prev, int B, int T, int C, bf16* out) {
   const int64_t n = int64_t(B) * C;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     const int c = int(i % C), b = int(i / C);

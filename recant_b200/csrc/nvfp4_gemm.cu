@@ -324,10 +324,10 @@ extern "C" size_t rb2_nvfp4_gemm_workspace_size(int64_t M, int64_t N, int64_t K)
   return size_t(gemm_ws(M, N, K).total);
 }
 
-extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
-                              const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
-                              int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws, size_t ws_bytes,
-                              void* stream) {
+extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                                 const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                                 const uint8_t* b_images, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
+                                 void* ws, size_t ws_bytes, void* stream) {
   RB2_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % 64 == 0, "nvfp4_gemm: need M, N > 0 and K %% 64 == 0 (K=%lld)",
                 (long long)K);
   RB2_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31), "nvfp4_gemm: size");
@@ -358,13 +358,16 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
   const GemmWs gw = gemm_ws(M, N, K);
   uint8_t* img_a = static_cast<uint8_t*>(ws) + 1024;
   uint8_t* img_b = img_a + gw.img_a;
+  RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(b_images) & 15) == 0, "nvfp4_gemm: b_images must be 16-byte aligned");
   {
     ProfScope ps_("nvfp4_sf_images", s);
-    const int64_t n16 = (gw.img_a + gw.img_b) / 16;
+    // with precomputed B images (rb2_nvfp4_gemm_b_images) only A's are built (nrb = 0)
+    const int64_t n16 = (gw.img_a + (b_images ? 0 : gw.img_b)) / 16;
     sf_images_kernel<<<unsigned(std::min<int64_t>((n16 + 255) / 256, int64_t(sms) * 16)), 256, 0, s>>>(
-        a_scales_blocked, b_scales_blocked, int((M + 127) / 128), int((N + 127) / 128), int(K / 64), int(gw.ksp), img_a,
-        img_b);
+        a_scales_blocked, b_scales_blocked, int((M + 127) / 128), b_images ? 0 : int((N + 127) / 128), int(K / 64),
+        int(gw.ksp), img_a, img_b);
   }
+  if (b_images) img_b = const_cast<uint8_t*>(b_images);
   RB2_CHECK_LAUNCH("nvfp4_sf_images");
   {
     ProfScope ps_("nvfp4_gemm", s);
@@ -375,5 +378,40 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
                                                                out_dtype == RB2_BF16, static_cast<int*>(ws));
   }
   RB2_CHECK_LAUNCH("nvfp4_gemm");
+  return RB2_OK;
+}
+
+extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                              const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                              int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws, size_t ws_bytes,
+                              void* stream) {
+  return rb2_nvfp4_gemm_ex(a_codes, a_scales_blocked, a_gscale, b_codes, b_scales_blocked, b_gscale, nullptr, M, N, K,
+                           out, out_dtype, ws, ws_bytes, stream);
+}
+
+extern "C" size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0) return 0;
+  return size_t(gemm_ws(1, N, K).img_b);
+}
+
+extern "C" int rb2_nvfp4_gemm_b_images(const uint8_t* b_scales_blocked, int64_t N, int64_t K, void* out,
+                                       size_t out_bytes, void* stream) {
+  RB2_CHECK_ARG(N > 0 && K > 0 && K % 64 == 0 && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
+                "nvfp4_gemm_b_images: need N > 0 and K %% 64 == 0");
+  RB2_CHECK_ARG(b_scales_blocked && out && (reinterpret_cast<uintptr_t>(b_scales_blocked) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                "nvfp4_gemm_b_images: null or misaligned pointer");
+  const GemmWs gw = gemm_ws(1, N, K);
+  if (out_bytes < size_t(gw.img_b)) {
+    set_error("nvfp4_gemm_b_images: output too small");
+    return RB2_EWORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n16 = gw.img_b / 16;
+  ProfScope ps_("nvfp4_sf_images", s);
+  // the prep kernel with no A rows: only the B part
+  sf_images_kernel<<<unsigned(std::min<int64_t>((n16 + 255) / 256, int64_t(148) * 16)), 256, 0, s>>>(
+      nullptr, b_scales_blocked, 0, int((N + 127) / 128), int(K / 64), int(gw.ksp), nullptr, static_cast<uint8_t*>(out));
+  RB2_CHECK_LAUNCH("nvfp4_gemm_b_images");
   return RB2_OK;
 }

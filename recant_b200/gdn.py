@@ -120,10 +120,12 @@ def _needs_grad(*ts):
     return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
 
 
-def gdn_recurrent(q, k, v, g, beta, initial_state=None, output_final_state=False, *, cu_seqlens=None, scale=None):
+def gdn_recurrent(q, k, v, g, beta, initial_state=None, output_final_state=False, *, cu_seqlens=None, scale=None,
+                  final_state_out=None):
     """Forward only, token by token, with a carried fp32 state: the decode step (layers.py:177-180 under
     serve/engine.py:107-119). Same contract and arithmetic as gdn_torch on one padded chunk
-    (ops.py:21-54); no autograd graph."""
+    (ops.py:21-54); no autograd graph. ``final_state_out``: a contiguous fp32 [n_seqs, Hv, dk, dv]
+    tensor to receive the final state (it may be ``initial_state`` itself: updated in place)."""
     if not q.is_cuda:
         raise ValueError("recant_b200.gdn: inputs must be CUDA tensors (no CPU path)")
     if q.dim() != 4 or k.shape != q.shape or v.dim() != 4:
@@ -145,7 +147,14 @@ def gdn_recurrent(q, k, v, g, beta, initial_state=None, output_final_state=False
     h0 = None if initial_state is None else initial_state.detach().to(torch.float32).contiguous()
     cu = None if cu_seqlens is None else cu_seqlens.to(device=q.device, dtype=torch.int64).contiguous()
     o = torch.empty(B, T, Hv, dv, dtype=dt, device=q.device)
-    hT = torch.empty(n_seqs, Hv, dk, dv, dtype=torch.float32, device=q.device) if output_final_state else None
+    if final_state_out is not None:
+        if (final_state_out.shape != (n_seqs, Hv, dk, dv) or final_state_out.dtype != torch.float32
+                or not final_state_out.is_contiguous()):
+            raise ValueError("recant_b200.gdn_recurrent: final_state_out must be a contiguous fp32 "
+                             f"[{n_seqs},{Hv},{dk},{dv}] tensor")
+        hT = final_state_out
+    else:
+        hT = torch.empty(n_seqs, Hv, dk, dv, dtype=torch.float32, device=q.device) if output_final_state else None
     sc = float(dk ** -0.5 if scale is None else scale)
     L.check(L.lib().rb2_gdn_recurrent_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta_k), L.ptr(h0),
                                           L.ptr(cu), B, T, n_seqs, Hk, Hv, dk, dv, _DT[dt], sc, L.ptr(o), L.ptr(hT),

@@ -19,6 +19,9 @@ import torch
 from . import _lib as L
 
 BLOCK = 16
+# Frozen weights keep the GEMM's B-operand scale images (built once at quantisation) instead of
+# rebuilding them every call
+CACHE_WEIGHT_IMAGES = True
 _DT = {torch.float32: L.F32, torch.bfloat16: L.BF16}
 
 
@@ -29,6 +32,7 @@ class FP4Tensor:
     gscale: torch.Tensor
     shape: tuple
     blocked: torch.Tensor | None = field(default=None, repr=False)
+    gemm_images: torch.Tensor | None = field(default=None, repr=False)  # B-operand scale images
 
 
 def blocked_size(rows: int, cols: int) -> int:
@@ -71,6 +75,21 @@ def blocked_scales(t) -> torch.Tensor:
     return b
 
 
+def gemm_images(t) -> torch.Tensor:
+    """The scale images the GEMM kernel reads for ``t`` as its B operand, built once and kept on the
+    tensor (frozen weights; about 4x the size of the scales)."""
+    if t.gemm_images is None:
+        rows, k = t.shape
+        lib = L.lib()
+        nb = lib.rb2_nvfp4_gemm_b_images_size(rows, k)
+        img = torch.empty(nb, dtype=torch.uint8, device=t.codes.device)
+        L.check(lib.rb2_nvfp4_gemm_b_images(L.ptr(blocked_scales(t)), rows, k, L.ptr(img), nb,
+                                            torch.cuda.current_stream(t.codes.device).cuda_stream),
+                "nvfp4_gemm_b_images")
+        t.gemm_images = img
+    return t.gemm_images
+
+
 def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
     """a . b^T * (gA gB) with a [M,K] and b [N,K] NVFP4 tensors; fp32 (or bf16) [M, N]."""
     m, k = a.shape
@@ -85,9 +104,11 @@ def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=a.codes.device)
     ga = a.gscale.reshape(1).to(torch.float32).contiguous()
     gb = b.gscale.reshape(1).to(torch.float32).contiguous()
-    st = lib.rb2_nvfp4_gemm(L.ptr(a.codes.contiguous()), L.ptr(blocked_scales(a)), L.ptr(ga),
-                            L.ptr(b.codes.contiguous()), L.ptr(blocked_scales(b)), L.ptr(gb), m, n, k, L.ptr(out),
-                            _DT[out_dtype], L.ptr(ws), wsb, torch.cuda.current_stream(a.codes.device).cuda_stream)
+    img = getattr(b, "gemm_images", None)
+    st = lib.rb2_nvfp4_gemm_ex(L.ptr(a.codes.contiguous()), L.ptr(blocked_scales(a)), L.ptr(ga),
+                               L.ptr(b.codes.contiguous()), L.ptr(blocked_scales(b)), L.ptr(gb), L.ptr(img), m, n, k,
+                               L.ptr(out), _DT[out_dtype], L.ptr(ws), wsb,
+                               torch.cuda.current_stream(a.codes.device).cuda_stream)
     L.check(st, "nvfp4_gemm")
     return out
 
@@ -109,6 +130,9 @@ def quantize_weight(w: torch.Tensor, use_rht: bool = True) -> FP4Weight:
     wf = w.detach().to(torch.float32).contiguous()
     fp = quantize_fast(wf, use_rht, False)
     dg = quantize_fast(wf.t().contiguous(), use_rht, False)
+    if CACHE_WEIGHT_IMAGES:
+        gemm_images(fp)
+        gemm_images(dg)
     return FP4Weight(fp, dg, n, k, use_rht)
 
 

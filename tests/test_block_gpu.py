@@ -220,3 +220,23 @@ def test_cache_pieces_equal_one_call():
             o, h = gdn_b200(**piece, initial_state=h, output_final_state=True)
             outs.append(o)
     assert rel(torch.cat(outs, 1), o_full) < 1e-4 and rel(h, h_full) < 1e-4
+
+
+def test_decode_graph_replays_the_eager_decode_step():
+    """The CUDA-graph decode step (static cache, updated in place) gives exactly the eager cache path's
+    outputs and states, step after step."""
+    from recant_b200.block import DecodeGraph, LayerCache
+    G, blk = _block()
+    gen = torch.Generator().manual_seed(13)
+    x = torch.randn(3, 12, HIDDEN, generator=gen).to(torch.bfloat16).cuda()
+    with torch.no_grad():
+        eager = LayerCache()
+        blk(x[:, :6], eager)
+        graphed = eager.fork()
+        step = DecodeGraph(blk, graphed, B=3)
+        for t in range(6, 12):
+            ref = blk(x[:, t:t + 1], eager)
+            out = step(x[:, t:t + 1])
+            assert torch.equal(out, ref), t
+        assert torch.equal(graphed.conv_state, eager.conv_state)
+        assert torch.equal(graphed.rec_state, eager.rec_state)

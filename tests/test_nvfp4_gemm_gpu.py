@@ -94,3 +94,20 @@ def test_fp4_linear_fwd_bwd():
     y.backward(dy)
     exact = (dy.float().reshape(-1, 512) @ w.float()).cpu().numpy()
     assert x.grad.shape == x.shape and _rel(x.grad.float().reshape(-1, 256).cpu().numpy(), exact) < 0.2
+
+
+@pytest.mark.parametrize("M,N,K", [(257, 384, 320), (1, 4096, 4096), (64, 100, 64)])
+def test_gemm_with_cached_weight_images_is_identical(M, N, K):
+    """B's scale images built once (rb2_nvfp4_gemm_b_images, kept on the weight) give bit-for-bit the
+    result of building them inside every call."""
+    from recant_b200 import gemm_b200
+    from recant_b200.nvfp4 import gemm_images
+    gen = torch.Generator().manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    a, b = _fp4(x), _fp4(w)
+    plain = gemm_b200(a, b)
+    gemm_images(b)
+    assert b.gemm_images is not None
+    cached = gemm_b200(a, b)
+    assert torch.equal(plain, cached)
