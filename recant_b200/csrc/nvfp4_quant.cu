@@ -193,23 +193,36 @@ quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divide
     }
   }
   uint32_t packed[2] = {0u, 0u};
+  if (stochastic) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float q = __fdiv_rn(v[i], denom);
-    const float a = fminf(fabsf(q), 6.0f);
-    int idx;
-    if (stochastic) {
+    for (int i = 0; i < 16; ++i) {
+      const float q = __fdiv_rn(v[i], denom);
+      const float a = fminf(fabsf(q), 6.0f);
       int hi = (a > 0.f) + (a > 0.5f) + (a > 1.f) + (a > 1.5f) + (a > 2.f) + (a > 3.f) + (a > 4.f);
       hi = hi < 1 ? 1 : hi;
       const float glo = grid_value(hi - 1), ghi = grid_value(hi);
       const float p = __fdiv_rn(__fsub_rn(a, glo), __fsub_rn(ghi, glo));
       const float u = float(rnd[i] >> 8) * (1.0f / 16777216.0f);
-      idx = (u < p) ? hi : hi - 1;
-    } else {
-      idx = e2m1_index(a);
+      const int idx = (u < p) ? hi : hi - 1;
+      packed[i >> 3] |= uint32_t(idx + (q < 0.f ? 8 : 0)) << (4 * (i & 7));
     }
-    const uint32_t code = uint32_t(idx + (q < 0.f ? 8 : 0));
-    packed[i >> 3] |= code << (4 * (i & 7));
+  } else {
+    // Round to nearest without a division per element. a' = |x| RN(1/denom) is within 2.5 ulp of the
+    // correctly rounded |x| / denom (two roundings of relative size 2^-24 each, plus the quotient's
+    // own half ulp). Every decision point of e2m1_index lies on a multiple of 2^21 in the bit
+    // pattern, so when the bits of a' are more than 8 away from such a multiple, a' and the exact
+    // quotient fall on the same side of every point and give the same index; otherwise (about one
+    // element in 1.3e5) the exact quotient is computed. q < 0 <=> x < 0 since denom > 0 (and -0
+    // gives +0 / no sign bit in both).
+    const float rinv = __frcp_rn(denom);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float a = __fmul_rn(fabsf(v[i]), rinv);
+      const uint32_t u = __float_as_uint(a);
+      if (u != 0u && ((u + 8u) & 0x1FFFFFu) <= 16u) a = fabsf(__fdiv_rn(v[i], denom));
+      const int idx = e2m1_index(fminf(a, 6.0f));
+      packed[i >> 3] |= uint32_t(idx + (v[i] < 0.f ? 8 : 0)) << (4 * (i & 7));
+    }
   }
   reinterpret_cast<uint2*>(codes)[b] = make_uint2(packed[0], packed[1]);
   scales[b] = uint8_t(s8);
