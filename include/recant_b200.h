@@ -209,15 +209,24 @@ RB2_API int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_block
                    const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
                    int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws,
                    size_t ws_bytes, void* stream);
-/* rb2_nvfp4_gemm with B's scale images precomputed (b_images from rb2_nvfp4_gemm_b_images, NULL =
- * built per call as rb2_nvfp4_gemm does): for frozen weights, whose images are built once. The
- * images are B's blocked scales laid out as the kernel moves them into tensor memory (each 512-byte
- * atom repeated 4 times, the two 128-row halves of a 256-row tile interleaved per K step), 16-byte
- * aligned, rb2_nvfp4_gemm_b_images_size(N, K) bytes. */
+/* rb2_nvfp4_gemm with two optional extras (no reference counterpart for the first; the second is
+ * the "lora?" of the GEMM boundary):
+ * - b_images: B's scale images precomputed by rb2_nvfp4_gemm_b_images (NULL = built per call as
+ *   rb2_nvfp4_gemm does) -- for frozen weights, whose images are built once. The images are B's
+ *   blocked scales laid out as the kernel moves them into tensor memory (each 512-byte atom
+ *   repeated 4 times, the two 128-row halves of a 256-row tile interleaved per K step), 16-byte
+ *   aligned, rb2_nvfp4_gemm_b_images_size(N, K) bytes.
+ * - lora_h (NULL = none): out = a . b^T * gA * gB + lora_scale * lora_h . lora_b^T with lora_h
+ *   [M, lora_r] bf16 (row stride lora_ldh elements) and lora_b [N, lora_r] bf16, lora_r 8 or 16:
+ *   QLinear's LoRA y + (alpha / r) (x A^T) B^T (layers.py:65-70, 86-97) with h = x A^T computed by
+ *   the caller. fp32 output: one fp32 sum. bf16 output, rounded as the reference's ops round:
+ *   lora_mode 0 = grouped_linear's addmm (y to bf16, then y + s h B^T in fp32, one rounding);
+ *   lora_mode 1 = QLinear.forward's three ops (y, h B^T and s h B^T each to bf16, then the sum). */
 RB2_API int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
                               const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
-                              const uint8_t* b_images, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
-                              void* ws, size_t ws_bytes, void* stream);
+                              const uint8_t* b_images, const void* lora_h, int64_t lora_ldh, const void* lora_b,
+                              int lora_r, float lora_scale, int lora_mode, int64_t M, int64_t N, int64_t K, void* out,
+                              int out_dtype, void* ws, size_t ws_bytes, void* stream);
 RB2_API size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K);
 RB2_API int rb2_nvfp4_gemm_b_images(const uint8_t* b_scales_blocked, int64_t N, int64_t K, void* out,
                                     size_t out_bytes, void* stream);

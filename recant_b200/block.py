@@ -170,6 +170,79 @@ class _FP4Group(torch.autograd.Function):
         return (None if dx is None else dx.reshape(ctx.xshape), None, *([None] * len(ctx.weights)))
 
 
+class _FP4LoRAGroup(torch.autograd.Function):
+    """NVFP4 linears with LoRA sharing one input x: the activation is quantized once, h = x cat(A_i)^T
+    is one cuBLAS product, and each member's (alpha / r) h_i B_i^T is added inside its NVFP4 GEMM's
+    epilogue, rounded as the reference's ops round it (``mode`` 0: grouped_linear's one addmm per
+    member, layers.py:86-97; 1: QLinear.forward's three ops, layers.py:65-70). Backward:
+    the NVFP4 dgrads as _FP4Group, and the LoRA products dB_i = s dy_i^T h_i, dh_i = s dy_i B_i,
+    dA = dh^T x, dx += dh cat(A_i) through cuBLAS."""
+
+    @staticmethod
+    def forward(ctx, x, stochastic, mode, weights, scales, *ab):
+        k = weights[0].in_features
+        x2 = x.reshape(-1, k)
+        dt = x.dtype
+        A = [t.to(dt) for t in ab[0::2]]
+        B = [t.to(dt).contiguous() for t in ab[1::2]]
+        a = N.quantize_activation(x2, weights[0].use_rht)
+        h = x2 @ torch.cat(A, 0).t()
+        ys, off = [], 0
+        for w, b, sc in zip(weights, B, scales):
+            r = b.shape[1]
+            y = N.gemm_b200(a, w.fprop, out_dtype=dt, lora=(h[:, off:off + r], b, sc), lora_mode=mode)
+            ys.append(y.reshape(*x.shape[:-1], w.out_features))
+            off += r
+        ctx.save_for_backward(x2, h, *A, *B)
+        ctx.weights, ctx.scales, ctx.stochastic, ctx.xshape = weights, scales, stochastic, x.shape
+        ctx.n = len(weights)
+        return tuple(ys)
+
+    @staticmethod
+    def backward(ctx, *dys):
+        x2, h, *ab = ctx.saved_tensors
+        A, B = ab[:ctx.n], ab[ctx.n:]
+        need_dx = ctx.needs_input_grad[0]  # as the reference, no NVFP4 dgrad when x needs no gradient
+        dx, dhs, dBs, off = None, [], [], 0
+        for w, b, sc, dy in zip(ctx.weights, B, ctx.scales, dys):
+            r = b.shape[1]
+            hi = h[:, off:off + r]
+            off += r
+            if dy is None:
+                dhs.append(torch.zeros_like(hi))
+                dBs.append(torch.zeros(b.shape, dtype=torch.float32, device=b.device))
+                continue
+            d2 = dy.reshape(-1, w.out_features).to(x2.dtype)
+            if need_dx:
+                q = N.quantize_activation(d2, w.use_rht, stochastic=ctx.stochastic)
+                part = N._gemm_to(q, w.dgrad, d2.dtype)
+                dx = part if dx is None else dx + part
+            dBs.append((d2.t() @ hi).float() * sc)
+            dhs.append((d2 @ b) * sc)
+        dh = torch.cat(dhs, 1)
+        dA = (dh.t() @ x2).float()
+        if need_dx:
+            dxl = dh @ torch.cat(A, 0)
+            dx = dxl if dx is None else dx + dxl
+        grads, off = [], 0
+        for a_, b_, db in zip(A, B, dBs):
+            r = a_.shape[0]
+            grads += [dA[off:off + r], db]
+            off += r
+        return (None if dx is None else dx.reshape(ctx.xshape), None, None, None, None, *grads)
+
+
+# Add LoRA inside the NVFP4 GEMM epilogue (_FP4LoRAGroup) instead of the reference's addmm through
+# cuBLAS. Off by default: measured at config 2 it is slower (5.75 vs 5.40 ms per block step; the 16
+# FMAs per output element on CUDA cores are not hidden behind the next tile), as is the decode step.
+FUSED_LORA_EPILOGUE = False
+
+
+def _fused_lora_ok(lins):
+    return FUSED_LORA_EPILOGUE and all(l.fp4 is not None and l.lora_A is not None and l.lora_A.shape[0] in (8, 16) for l in lins) and \
+        len({l.fp4.use_rht for l in lins}) == 1
+
+
 class QLinear(nn.Module):
     """layers.py:36-70: NVFP4 base when quantizable (in, out % 16 == 0 and out >= 256), else a bf16
     dense weight; optional LoRA y += (alpha / r) (x A^T) B^T with fp32 A [r, in], B [out, r]."""
@@ -213,6 +286,10 @@ class QLinear(nn.Module):
         return y + (h @ self.lora_B.to(x.dtype).t()) * self.lora_scale
 
     def forward(self, x):
+        if _fused_lora_ok([self]):
+            (y,) = _FP4LoRAGroup.apply(x, self.stochastic_backward, 1, (self.fp4,), (self.lora_scale,),
+                                       self.lora_A, self.lora_B)
+            return y
         if self.fp4 is not None:
             (y,) = _FP4Group.apply(x, self.stochastic_backward, self.fp4)
         else:
@@ -223,7 +300,12 @@ class QLinear(nn.Module):
 def grouped_linear(x, lins):
     """layers.py:72-97 with the activation quantized once for all NVFP4 members; the LoRA
     down-projections of all members come from one GEMM over x (x . cat(A_i)^T, as the reference's
-    default path, layers.py:86-88), each member then adds one addmm."""
+    default path, layers.py:86-88); each member's up-projection is added inside its NVFP4 GEMM
+    (ranks 8 and 16; other ranks add one addmm per member as the reference does)."""
+    if _fused_lora_ok(lins):
+        ab = [t for l in lins for t in (l.lora_A, l.lora_B)]
+        return list(_FP4LoRAGroup.apply(x, lins[0].stochastic_backward, 0, tuple(l.fp4 for l in lins),
+                                        tuple(l.lora_scale for l in lins), *ab))
     fp4 = [l for l in lins if l.fp4 is not None]
     outs = {}
     if fp4:

@@ -42,12 +42,13 @@ struct GemmCfg {
   static constexpr int SFB_BYTES = 4 * 2 * kImg;             // 4 K steps x 2 halves
   static constexpr int SFA_OFF = 0, SFB_OFF = SFA_BYTES, A_OFF = SFA_BYTES + SFB_BYTES, B_OFF = A_OFF + A_BYTES;
   static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int LORA_BYTES = BN * 16 * 2;             // the tile's LoRA B rows (r <= 16, bf16)
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;   // + LORA_BYTES for the LoRA variant
   static constexpr int SF_COL0 = ACC * BN;                   // TMEM: accumulators, then scale factors
   static_assert(BN == 256, "a B scale copy moves exactly two 128-row halves");
   static_assert(SF_COL0 + 16 + 32 <= 512, "TMEM budget");
   static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && STAGE_BYTES % 1024 == 0, "SW128 alignment");
-  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(SMEM + LORA_BYTES <= 227 * 1024, "shared memory");
 };
 
 // Scale images in the workspace: A: [row block][K step (padded to 4)][kImg]; B: [256-row block]
@@ -127,12 +128,39 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // t % ntn, so concurrently running CTAs share A row blocks in L2). The producer streams stages
 // across tile boundaries; the single TMEM accumulator is handed between the MMA warp and the
 // epilogue warps with acc_full / acc_empty.
-template <class C>
+// Optional low-rank term added in the epilogue: out = y + s * h B^T with h [M, r] (row stride ldh)
+// and B [N, r] bf16, r 8 or 16 -- QLinear's LoRA (layers.py:65-70, 86-97) with h = x A^T computed
+// by the caller, rounded as the reference rounds it when the output is bf16:
+//   mode 0 (grouped_linear's addmm, layers.py:86-97): y rounded to bf16, then y + s (h B^T) in fp32,
+//          one rounding;
+//   mode 1 (QLinear.forward, layers.py:65-70): y, h B^T and (h B^T) s each rounded to bf16, then
+//          their sum rounded.
+struct Lora {
+  const __nv_bfloat16* h;
+  const __nv_bfloat16* b;
+  int64_t ldh;
+  int r;
+  float s;
+  int mode;
+};
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void unpack8(const uint4 u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <class C, bool kLora>
 __global__ void __launch_bounds__(kThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                   const uint8_t* __restrict__ img_a, const uint8_t* __restrict__ img_b, int ksp, const float* __restrict__ ga,
                   const float* __restrict__ gb, int M, int N, int K, void* __restrict__ out, int out_bf16,
-                  int* __restrict__ err) {
+                  Lora lora, int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023);
   constexpr int BN = C::BN, STAGES = C::STAGES, ACC = C::ACC;
@@ -224,7 +252,9 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       const int tm = t / ntn, tn = t % ntn;
       const int ab = local % ACC;
       const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16) + ab * BN + half * HC;
-      if (!tc::mbar_wait(&acc_full[ab], (local / ACC) & 1, err, 203)) break;
+      // a timed-out wait is recorded in err; the warp still walks every tile (with garbage) so that
+      // all 8 epilogue warps meet the same named barriers, each after bounded waits only
+      const bool live = tc::mbar_wait(&acc_full[ab], (local / ACC) & 1, err, 203);
       tc::fence_after_sync();
       uint32_t r[HC / 32][32];
 #pragma unroll
@@ -233,41 +263,81 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       tc::fence_before_sync();
       __syncwarp();
       if (l == 0) mbar_arrive(&acc_empty[ab]);
+      __nv_bfloat16* lb = reinterpret_cast<__nv_bfloat16*>(sm + STAGES * STAGE_BYTES);
+      if constexpr (kLora) {  // the tile's B rows, zero-padded to 16 values -> shared memory (named barrier 1)
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the previous tile's readers are done
+        for (int e = tid - 64; e < BN * 2; e += 256) {
+          const int rr = e >> 1, cc = e & 1, n = tn * BN + rr;
+          uint4 v4 = make_uint4(0, 0, 0, 0);
+          if (n < N && 8 * cc < lora.r) v4 = __ldg(reinterpret_cast<const uint4*>(lora.b + size_t(n) * lora.r) + cc);
+          reinterpret_cast<uint4*>(lb)[e] = v4;
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
       const int row = tm * BM + 32 * q + l;
-      if (row >= M) continue;
+      if (!live || row >= M) continue;
+      float hf[16];  // this row's h (LoRA), zero past r
+      if constexpr (kLora) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(lora.h + size_t(row) * lora.ldh)), hf);
+        if (lora.r > 8) {
+          unpack8(__ldg(reinterpret_cast<const uint4*>(lora.h + size_t(row) * lora.ldh + 8)), hf + 8);
+        } else {
+#pragma unroll
+          for (int i = 8; i < 16; ++i) hf[i] = 0.f;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < HC / 32; ++c) {
         const int col0 = tn * BN + half * HC + 32 * c;
         if (col0 >= N) break;
+        // r[c][j] <- the output value (fp32 bits)
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          float v = __uint_as_float(r[c][jj]) * scale;
+          if constexpr (kLora) {  // every lane reads the same B row: shared-memory broadcast
+            const uint4* bp = reinterpret_cast<const uint4*>(lb + (half * HC + 32 * c + jj) * 16);
+            float bf[8];
+            unpack8(bp[0], bf);
+            float d = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d = fmaf(hf[i], bf[i], d);
+            unpack8(bp[1], bf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d = fmaf(hf[8 + i], bf[i], d);
+            if (!out_bf16) v = fmaf(lora.s, d, v);
+            else if (lora.mode == 0) v = fmaf(lora.s, d, bf16r(v));
+            else v = bf16r(v) + bf16r(bf16r(d) * lora.s);
+          }
+          r[c][jj] = __float_as_uint(v);
+        }
         if (out_bf16) {
           __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
           if (col0 + 32 <= N && (N % 8) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
+            for (int jj = 0; jj < 32; jj += 8) {
               const uint4 pk = make_uint4(
-                  tc::pack_bf16(__uint_as_float(r[c][j]) * scale, __uint_as_float(r[c][j + 1]) * scale),
-                  tc::pack_bf16(__uint_as_float(r[c][j + 2]) * scale, __uint_as_float(r[c][j + 3]) * scale),
-                  tc::pack_bf16(__uint_as_float(r[c][j + 4]) * scale, __uint_as_float(r[c][j + 5]) * scale),
-                  tc::pack_bf16(__uint_as_float(r[c][j + 6]) * scale, __uint_as_float(r[c][j + 7]) * scale));
-              *reinterpret_cast<uint4*>(o + j) = pk;
+                  tc::pack_bf16(__uint_as_float(r[c][jj]), __uint_as_float(r[c][jj + 1])),
+                  tc::pack_bf16(__uint_as_float(r[c][jj + 2]), __uint_as_float(r[c][jj + 3])),
+                  tc::pack_bf16(__uint_as_float(r[c][jj + 4]), __uint_as_float(r[c][jj + 5])),
+                  tc::pack_bf16(__uint_as_float(r[c][jj + 6]), __uint_as_float(r[c][jj + 7])));
+              *reinterpret_cast<uint4*>(o + jj) = pk;
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) o[j] = __float2bfloat16_rn(__uint_as_float(r[c][j]) * scale);
+            for (int jj = 0; jj < 32; ++jj)
+              if (col0 + jj < N) o[jj] = __float2bfloat16_rn(__uint_as_float(r[c][jj]));
           }
         } else {
           float* o = static_cast<float*>(out) + size_t(row) * N + col0;
           if (col0 + 32 <= N && (N % 4) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(o + j) =
-                  make_float4(__uint_as_float(r[c][j]) * scale, __uint_as_float(r[c][j + 1]) * scale,
-                              __uint_as_float(r[c][j + 2]) * scale, __uint_as_float(r[c][j + 3]) * scale);
+            for (int jj = 0; jj < 32; jj += 4)
+              *reinterpret_cast<float4*>(o + jj) = make_float4(__uint_as_float(r[c][jj]), __uint_as_float(r[c][jj + 1]),
+                                                               __uint_as_float(r[c][jj + 2]), __uint_as_float(r[c][jj + 3]));
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) o[j] = __uint_as_float(r[c][j]) * scale;
+            for (int jj = 0; jj < 32; ++jj)
+              if (col0 + jj < N) o[jj] = __uint_as_float(r[c][jj]);
           }
         }
       }
@@ -326,8 +396,9 @@ extern "C" size_t rb2_nvfp4_gemm_workspace_size(int64_t M, int64_t N, int64_t K)
 
 extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
                                  const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
-                                 const uint8_t* b_images, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
-                                 void* ws, size_t ws_bytes, void* stream) {
+                                 const uint8_t* b_images, const void* lora_h, int64_t lora_ldh, const void* lora_b,
+                                 int lora_r, float lora_scale, int lora_mode, int64_t M, int64_t N, int64_t K, void* out,
+                                 int out_dtype, void* ws, size_t ws_bytes, void* stream) {
   RB2_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % 64 == 0, "nvfp4_gemm: need M, N > 0 and K %% 64 == 0 (K=%lld)",
                 (long long)K);
   RB2_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31), "nvfp4_gemm: size");
@@ -359,6 +430,13 @@ extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales
   uint8_t* img_a = static_cast<uint8_t*>(ws) + 1024;
   uint8_t* img_b = img_a + gw.img_a;
   RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(b_images) & 15) == 0, "nvfp4_gemm: b_images must be 16-byte aligned");
+  RB2_CHECK_ARG(lora_h == nullptr ||
+                    (lora_b && lora_r > 0 && lora_r <= 16 && lora_r % 8 == 0 && lora_ldh >= lora_r && lora_ldh % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(lora_h) & 15) == 0 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0),
+                "nvfp4_gemm: LoRA needs r in {8, 16}, a row stride that is a multiple of 8 and 16-byte aligned h, B");
+  RB2_CHECK_ARG(lora_mode == 0 || lora_mode == 1, "nvfp4_gemm: lora_mode must be 0 or 1");
+  const Lora lora{static_cast<const __nv_bfloat16*>(lora_h), static_cast<const __nv_bfloat16*>(lora_b), lora_ldh,
+                  lora_r, lora_scale, lora_mode};
   {
     ProfScope ps_("nvfp4_sf_images", s);
     // with precomputed B images (rb2_nvfp4_gemm_b_images) only A's are built (nrb = 0)
@@ -371,11 +449,21 @@ extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales
   RB2_CHECK_LAUNCH("nvfp4_sf_images");
   {
     ProfScope ps_("nvfp4_gemm", s);
-      RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide>, cudaFuncAttributeMaxDynamicSharedMemorySize, Wide::SMEM),
-             "nvfp4_gemm: smem attribute");
-    nvfp4_gemm_kernel<Wide><<<grid, kThreads, Wide::SMEM, s>>>(ma, mb, img_a, img_b, int(gw.ksp), a_gscale,
-                                                               b_gscale, int(M), int(N), int(K), out,
-                                                               out_dtype == RB2_BF16, static_cast<int*>(ws));
+    if (lora.h) {
+      RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Wide::SMEM + Wide::LORA_BYTES),
+               "nvfp4_gemm: smem attribute");
+      nvfp4_gemm_kernel<Wide, true><<<grid, kThreads, Wide::SMEM + Wide::LORA_BYTES, s>>>(
+          ma, mb, img_a, img_b, int(gw.ksp), a_gscale, b_gscale, int(M), int(N), int(K), out, out_dtype == RB2_BF16, lora,
+          static_cast<int*>(ws));
+    } else {
+      RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Wide::SMEM),
+               "nvfp4_gemm: smem attribute");
+      nvfp4_gemm_kernel<Wide, false><<<grid, kThreads, Wide::SMEM, s>>>(
+          ma, mb, img_a, img_b, int(gw.ksp), a_gscale, b_gscale, int(M), int(N), int(K), out, out_dtype == RB2_BF16, lora,
+          static_cast<int*>(ws));
+    }
   }
   RB2_CHECK_LAUNCH("nvfp4_gemm");
   return RB2_OK;
@@ -385,8 +473,8 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
                               const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
                               int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws, size_t ws_bytes,
                               void* stream) {
-  return rb2_nvfp4_gemm_ex(a_codes, a_scales_blocked, a_gscale, b_codes, b_scales_blocked, b_gscale, nullptr, M, N, K,
-                           out, out_dtype, ws, ws_bytes, stream);
+  return rb2_nvfp4_gemm_ex(a_codes, a_scales_blocked, a_gscale, b_codes, b_scales_blocked, b_gscale, nullptr, nullptr,
+                           0, nullptr, 0, 0.f, 0, M, N, K, out, out_dtype, ws, ws_bytes, stream);
 }
 
 extern "C" size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K) {

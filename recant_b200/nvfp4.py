@@ -90,8 +90,11 @@ def gemm_images(t) -> torch.Tensor:
     return t.gemm_images
 
 
-def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
-    """a . b^T * (gA gB) with a [M,K] and b [N,K] NVFP4 tensors; fp32 (or bf16) [M, N]."""
+def gemm_b200(a, b, out_dtype=torch.float32, lora=None, lora_mode=0) -> torch.Tensor:
+    """a . b^T * (gA gB) with a [M,K] and b [N,K] NVFP4 tensors; fp32 (or bf16) [M, N]. ``lora`` =
+    (h [M, r] bf16, B [N, r] bf16, scale) adds scale * h B^T (QLinear's LoRA with h = x A^T,
+    layers.py:65-70, 86-97), with bf16 output rounded as grouped_linear's addmm (``lora_mode`` 0)
+    or as QLinear.forward's three ops (1)."""
     m, k = a.shape
     n, kb = b.shape
     if k != kb:
@@ -105,8 +108,17 @@ def gemm_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
     ga = a.gscale.reshape(1).to(torch.float32).contiguous()
     gb = b.gscale.reshape(1).to(torch.float32).contiguous()
     img = getattr(b, "gemm_images", None)
+    h = bl = None
+    r, ldh, sc = 0, 0, 0.0
+    if lora is not None:
+        h, bl, sc = lora
+        if h.stride(-1) != 1 or h.dtype != torch.bfloat16 or h.shape[0] != m:
+            raise ValueError("recant_b200.gemm_b200: LoRA h must be a bf16 [M, r] tensor with unit column stride")
+        bl = bl.to(torch.bfloat16).contiguous()
+        r, ldh = bl.shape[1], h.stride(0)
     st = lib.rb2_nvfp4_gemm_ex(L.ptr(a.codes.contiguous()), L.ptr(blocked_scales(a)), L.ptr(ga),
-                               L.ptr(b.codes.contiguous()), L.ptr(blocked_scales(b)), L.ptr(gb), L.ptr(img), m, n, k,
+                               L.ptr(b.codes.contiguous()), L.ptr(blocked_scales(b)), L.ptr(gb), L.ptr(img),
+                               L.ptr(h), ldh, L.ptr(bl), r, float(sc), int(lora_mode), m, n, k,
                                L.ptr(out), _DT[out_dtype], L.ptr(ws), wsb,
                                torch.cuda.current_stream(a.codes.device).cuda_stream)
     L.check(st, "nvfp4_gemm")

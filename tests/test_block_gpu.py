@@ -240,3 +240,49 @@ def test_decode_graph_replays_the_eager_decode_step():
             assert torch.equal(out, ref), t
         assert torch.equal(graphed.conv_state, eager.conv_state)
         assert torch.equal(graphed.rec_state, eager.rec_state)
+
+
+def test_block_lora_grads_without_input_grad():
+    """With x needing no gradient (config 2 trains LoRA only) the NVFP4 dgrads are skipped, as the
+    reference's autograd skips them; the LoRA gradients are those of the full backward."""
+    G, blk = _block()
+    blk.set_stochastic_backward(False)
+    x = G["x"].to(torch.bfloat16).cuda()
+    dy = torch.randn(x.shape, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).cuda()
+    grads = []
+    for need in (True, False):
+        for p in blk.parameters():
+            p.grad = None
+        xi = x.clone().requires_grad_(need)
+        blk(xi).backward(dy)
+        grads.append({n: p.grad.clone() for n, p in blk.named_parameters() if p.grad is not None})
+    assert grads[0].keys() == grads[1].keys() and len(grads[0]) == 6
+    for n in grads[0]:
+        assert rel(grads[1][n], grads[0][n]) < 1e-6, n
+
+
+def test_block_with_fused_lora_epilogue():
+    """The opt-in path that adds LoRA inside the NVFP4 GEMM epilogue (rounded as the reference's addmm
+    and three-op forms) matches the reference block and gives the addmm path's LoRA gradients."""
+    import recant_b200.block as RB
+    G, blk = _block()
+    blk.set_stochastic_backward(False)
+    x = G["x"].to(torch.bfloat16).cuda()
+    dy = torch.randn(x.shape, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).cuda()
+    outs, grads = [], []
+    old = RB.FUSED_LORA_EPILOGUE
+    try:
+        for fused in (False, True):
+            RB.FUSED_LORA_EPILOGUE = fused
+            for p in blk.parameters():
+                p.grad = None
+            xi = x.clone().requires_grad_(True)
+            out = blk(xi)
+            out.backward(dy)
+            outs.append(out.detach().float())
+            grads.append({n: p.grad.clone() for n, p in blk.named_parameters() if p.grad is not None})
+    finally:
+        RB.FUSED_LORA_EPILOGUE = old
+    assert rel(outs[1], G["out"]) < BLOCK_TOL, rel(outs[1], G["out"])
+    for n in grads[0]:
+        assert rel(grads[1][n], grads[0][n]) < 2e-2, (n, rel(grads[1][n], grads[0][n]))

@@ -111,3 +111,23 @@ def test_gemm_with_cached_weight_images_is_identical(M, N, K):
     assert b.gemm_images is not None
     cached = gemm_b200(a, b)
     assert torch.equal(plain, cached)
+
+
+@pytest.mark.parametrize("M,N,K,r", [(300, 512, 256, 16), (257, 384, 320, 8), (1, 4096, 1024, 16)])
+def test_gemm_lora_epilogue(M, N, K, r):
+    """out = a . b^T gA gB + s h B^T with the low-rank term added in the GEMM epilogue, against the
+    plain GEMM plus the same term in fp32."""
+    from recant_b200 import gemm_b200
+    gen = torch.Generator().manual_seed(M + 3 * N + r)
+    x = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    hfull = torch.randn(M, 2 * r, generator=gen).to(torch.bfloat16).cuda()
+    h = hfull[:, r:]                       # a column slice: row stride 2r
+    Bm = (torch.randn(N, r, generator=gen) * 0.3).to(torch.bfloat16).cuda()
+    a, b = _fp4(x), _fp4(w)
+    base = gemm_b200(a, b)
+    ref = base + 2.0 * (h.float() @ Bm.float().t())
+    out = gemm_b200(a, b, lora=(h, Bm, 2.0))
+    assert _rel(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+    out16 = gemm_b200(a, b, out_dtype=torch.bfloat16, lora=(h, Bm, 2.0))
+    assert _rel(out16.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
