@@ -223,7 +223,6 @@ constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  /
               YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
 constexpr int QB2 = VT;                                                        // over V once consumed
 constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 is issued
-constexpr int GQS = 163840;  // GQA dq then dk rows, fp32 [64][128], over the fp32 scratch after G5
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
 constexpr int VEC = DAQF + 16640;                                              // 14 x 64 floats
 constexpr int RED = VEC + 14 * 256;                                            // 5 x 4 x 64 floats
@@ -275,7 +274,15 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   const int q4 = w & 3, hh = w >> 2, r = 32 * q4 + l, c0 = 32 * hh;
   const bool mrow = l < 16;            // this lane holds a row of an M=64 accumulator
   const int i64 = 16 * q4 + l;          // ... and it is token row i64
-  const int64_t n_items = int64_t(*ws.ct.n_chunks) * p.Hv;  // (chunk, head) pairs, head fastest
+  // Work: (chunk, key head) groups, each the p.group value heads that share the key head, walked
+  // group after group by one CTA (grid-strided over groups) so that the group's dq / dk can be summed
+  // in this CTA's slice of the scratch; item = chunk * Hv + value head.
+  const int64_t n_groups = int64_t(*ws.ct.n_chunks) * p.Hk;
+  auto seq_item = [&](int64_t k) -> int64_t {  // this CTA's k-th item, or -1
+    const int64_t G = int64_t(blockIdx.x) + (k / p.group) * gridDim.x;
+    if (G >= n_groups) return -1;
+    return (G / p.Hk) * p.Hv + (G % p.Hk) * p.group + k % p.group;
+  };
 
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
   if (tid == 0) {
@@ -303,12 +310,13 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::fence_before_sync();
   __syncthreads();  // barrier init and the TMEM address visible
   tc::fence_after_sync();
-  if (int64_t(blockIdx.x) < n_items) issue_phase1(blockIdx.x);
+  if (seq_item(0) >= 0) issue_phase1(seq_item(0));
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
-  int it = 0;
-  for (int64_t item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+  for (int64_t it = 0;; ++it) {
+  const int64_t item = seq_item(it);
+  if (item < 0) break;
   const uint32_t ph = uint32_t(it & 1);  // parity of every barrier (each completes once per item)
   const int ci = int(item / p.Hv), h = int(item % p.Hv);
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
@@ -556,7 +564,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::mbar_wait(&bar[4], ph, ws.err, 135);
   tc::fence_after_sync();
   __syncthreads();  // region A (the phase-2 tiles) is free once G5 has completed
-  if (item + gridDim.x < n_items) issue_phase1(item + gridDim.x);  // next item's tiles, behind this epilogue
+  if (seq_item(it + 1) >= 0) issue_phase1(seq_item(it + 1));  // next item's tiles, behind this epilogue
   // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j; q[i][r], k[i][r] read from the
   // [K;Q] tile (consecutive lanes read consecutive columns of one row: no bank conflicts) -----------
   float xr[32];
@@ -625,16 +633,28 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       const int64_t row = int64_t(p.Hk) * 128;
       store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
       store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
-    } else {  // per-value-head fp32 rows, staged for coalesced 16-byte stores (dq, then dk)
-      const int64_t rs = int64_t(p.Hv) * 512;
-      float* stg = reinterpret_cast<float*>(sm + lay::GQS);
-      stage_cols32(stg, r, c0, gq);
-      __syncthreads();
-      copy_rows_out(ws.dqh + (int64_t(t0) * p.Hv + h) * 128, rs, stg, 512, L, 0, 256);
-      __syncthreads();
-      stage_cols32(stg, r, c0, gk);
-      __syncthreads();
-      copy_rows_out(ws.dkh + (int64_t(t0) * p.Hv + h) * 128, rs, stg, 512, L, 0, 256);
+    } else {  // GQA: the group's sum, in fp32 in this CTA's scratch slice until its last value head
+      float* pq = ws.dqh + size_t(blockIdx.x) * 8192;  // [64 tokens][128], written and read by this thread
+      float* pk = ws.dkh + size_t(blockIdx.x) * 8192;
+      const int g = h % p.group;
+      if (g > 0) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          gq[j] = pq[(c0 + j) * 128 + r] + gq[j];
+          gk[j] = pk[(c0 + j) * 128 + r] + gk[j];
+        }
+      }
+      if (g + 1 < p.group) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          pq[(c0 + j) * 128 + r] = gq[j];
+          pk[(c0 + j) * 128 + r] = gk[j];
+        }
+      } else {
+        const int64_t row = int64_t(p.Hk) * 128;
+        store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
+        store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
+      }
     }
   }
   // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------
@@ -666,21 +686,6 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   if (w == 0) tc::tmem_dealloc(tbase, 512);
 }
 
-__global__ void __launch_bounds__(256) fast_gqa_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ dq,
-                                                       bf16* __restrict__ dk) {
-  const int64_t n = p.tokens * p.Hk * 128;
-  for (int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x; idx < n; idx += int64_t(gridDim.x) * 256) {
-    const int64_t c = idx & 127, th = idx >> 7, hk = th % p.Hk, tok = th / p.Hk;
-    float aq = 0.f, ak = 0.f;
-    for (int g = 0; g < p.group; ++g) {
-      const int64_t src = (tok * p.Hv + hk * p.group + g) * 128 + c;
-      aq += ws.dqh[src];
-      ak += ws.dkh[src];
-    }
-    dq[idx] = __float2bfloat16_rn(aq);
-    dk[idx] = __float2bfloat16_rn(ak);
-  }
-}
 
 template <typename K>
 int smem_attr_b(K kernel, int bytes) {
@@ -717,7 +722,7 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
       int dev = 0, sms = 148;
       RB2_CUDA(cudaGetDevice(&dev), "gdn fast chunk bwd: device");
       RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "gdn fast chunk bwd: SM count");
-      const int64_t items = int64_t(p.max_chunks) * p.Hv;
+      const int64_t items = int64_t(p.max_chunks) * p.Hk;  // (chunk, key head) groups
       CUtensorMap mq, mk, mv, mdo;
       if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk)) ||
           (rc = make_rows_map(&mv, p.v, p.tokens, p.Hv)) || (rc = make_rows_map(&mdo, d_o, p.tokens, p.Hv)))
@@ -726,11 +731,6 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
           p, w, static_cast<const bf16*>(d_o), static_cast<bf16*>(dq), static_cast<bf16*>(dk), static_cast<bf16*>(dv), dg,
           static_cast<bf16*>(dbeta), mq, mk, mv, mdo);
       RB2_CHECK_LAUNCH("gdn fast chunk bwd");
-    }
-    if (p.group > 1) {
-      ProfScope ps_("gdn_fast_gqa", s);
-      fast_gqa_kernel<<<148 * 8, 256, 0, s>>>(p, w, static_cast<bf16*>(dq), static_cast<bf16*>(dk));
-      RB2_CHECK_LAUNCH("gdn fast gqa");
     }
   }
   return RB2_OK;
