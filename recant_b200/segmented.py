@@ -21,7 +21,8 @@ normal reversed walk from the true dS_out; chunk backward.
 With a process group (context parallelism), each rank passes its contiguous token shard of the
 sequence; only rank 0's ``initial_state`` and the last rank's final-state gradient are used.
 The collectives per layer are one all_gather of 2 x Hv x 128 x 128 fp32 in the forward and one
-of Hv x 128 x 128 fp32 in the backward.
+of Hv x 128 x 128 fp32 in the backward, plus, only when the final state is requested, its broadcast
+from the last rank and the broadcast of its gradient.
 """
 from __future__ import annotations
 
@@ -49,7 +50,7 @@ def state_fold(M, c=None, s0=None, *, transpose=False, identity=False, states=Tr
 
 class _SegmentedGDN(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, initial_state, seg_len, group, scale):
+    def forward(ctx, q, k, v, g, beta, initial_state, seg_len, group, scale, want_final):
         if q.shape[0] != 1 or q.dtype != torch.bfloat16:
             raise ValueError("recant_b200.gdn_segmented: needs B == 1 and bfloat16 inputs (tensor-core path)")
         if seg_len % 64:
@@ -106,14 +107,17 @@ class _SegmentedGDN(torch.autograd.Function):
         hT = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
         fwd(S_in, o, hT, 2, 0)            # normal walk from the true segment inputs
         final = hT[n - 1].unsqueeze(0).clone()
-        if world > 1:
+        if world > 1 and want_final:  # the whole sequence's final state lives on the last rank
             import torch.distributed as dist
             dist.broadcast(final, src=world - 1, group=group)
         ctx.save_for_backward(q, k, v, g, beta, cu, S_in)
         ctx.ws, ctx.wsb, ctx.scratch_bytes, ctx.Ms, ctx.M_all = ws, wsb, scratch.value, Ms, M_all
         ctx.dims, ctx.n, ctx.group, ctx.world, ctx.rank = dims, n, group, world, rank
         ctx.has_h0 = initial_state is not None
+        ctx.want_final = want_final
         ctx.set_materialize_grads(False)
+        if not want_final:
+            ctx.mark_non_differentiable(final)
         return o, final
 
     @staticmethod
@@ -147,7 +151,8 @@ class _SegmentedGDN(torch.autograd.Function):
             d_last = dfinal.reshape(Hv, dk, dv).to(torch.float32).clone()
         if ctx.world > 1:
             import torch.distributed as dist
-            dist.broadcast(d_last, src=ctx.world - 1, group=ctx.group)
+            if ctx.want_final:  # (every rank decides alike: the final state was requested or not)
+                dist.broadcast(d_last, src=ctx.world - 1, group=ctx.group)
             # this rank's left-boundary gradient for a zero right-boundary gradient
             _, d = state_fold(Ms, dS0, transpose=True, states=False)
             d_all = torch.empty(ctx.world, Hv, dk, dv, dtype=torch.float32, device=dev)
@@ -159,7 +164,7 @@ class _SegmentedGDN(torch.autograd.Function):
         bwd(dS_out, dh0, 1, 0)            # normal reversed walk
         bwd(None, None, 2, 0)             # chunk backward
         d_init = dh0[0].unsqueeze(0) if (ctx.has_h0 and ctx.rank == 0) else None
-        return dq, dkk, dvv, dg, dbeta, d_init, None, None, None
+        return dq, dkk, dvv, dg, dbeta, d_init, None, None, None, None
 
 
 def gdn_segmented(q, k, v, g, beta, initial_state=None, output_final_state=False, *, segment_len=1024,
@@ -167,5 +172,6 @@ def gdn_segmented(q, k, v, g, beta, initial_state=None, output_final_state=False
     """GDN over one long sequence (B == 1) in chunk-aligned segments processed in parallel, with
     the affine hand-off; with ``group`` (a torch.distributed process group) the sequence is
     context-parallel: every rank passes its contiguous shard. Same semantics as ``gdn_b200``."""
-    o, final = _SegmentedGDN.apply(q, k, v, g, beta, initial_state, int(segment_len), group, scale)
+    o, final = _SegmentedGDN.apply(q, k, v, g, beta, initial_state, int(segment_len), group, scale,
+                                   bool(output_final_state))
     return o, (final if output_final_state else None)
