@@ -120,6 +120,15 @@ RB2_API int rb2_gdn_bwd_ex(const void* q, const void* k, const void* v, const fl
 RB2_API int rb2_gdn_state_fold(const float* M, const float* c, const float* s0, int64_t n, int H, int d,
                                int transpose, int identity_init, float* states, float* final_out, void* stream);
 
+/* rb2_gdn_state_fold with a prefix run and an explicit mode. mode 0: ascending k, x <- M_k x + c_k;
+ * mode 1: descending k, x <- M_k^T x + c_k (= transpose 1); mode 2: ascending k, x <- M_k^T x + c_k
+ * (pass transposed maps G_k = M_k^T to apply M_k: the fastest form). The np maps (Mp, cp) are applied
+ * first, in the same mode and order, their entering values not recorded; states records the values
+ * entering the n main maps. */
+RB2_API int rb2_gdn_state_fold_ex(const float* M, const float* c, int64_t n, const float* Mp, const float* cp,
+                                  int64_t np, const float* s0, int H, int d, int mode, int identity_init,
+                                  float* states, float* final_out, void* stream);
+
 /* Recurrent (token-by-token) forward for short calls with a carried state: the decode step of
  * GatedDeltaNet.forward with a LayerCache (layers.py:177-180; serve/engine.py:107-119), the same
  * arithmetic as gdn_torch on one padded chunk (ops.py:21-54). Arguments as rb2_gdn_fwd without

@@ -32,6 +32,7 @@ SIGNATURES = {
     "rb2_gdn_bwd_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _f,
                             _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p, _sz, _p, _i, _i]),
     "rb2_gdn_state_fold": (_i, [_p, _p, _p, _i64, _i, _i, _i, _i, _p, _p, _p]),
+    "rb2_gdn_state_fold_ex": (_i, [_p, _p, _i64, _p, _p, _i64, _p, _i, _i, _i, _i, _p, _p, _p]),
     "rb2_gdn_recurrent_fwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _f, _p, _p, _p]),
     "rb2_conv_silu_fwd": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _p]),
     "rb2_conv_silu_bwd": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),

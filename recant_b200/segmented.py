@@ -34,18 +34,30 @@ from . import _lib as L
 from .gdn import _PATHS, _stream
 
 
-def state_fold(M, c=None, s0=None, *, transpose=False, identity=False, states=True):
+def state_fold(M, c=None, s0=None, *, transpose=False, identity=False, states=True, mode=None, prefix=None):
     """Fold the affine maps M [n, H, 128, 128] (offsets c, same shape, None = 0) from the start
     value s0 [H, 128, 128] (None = zero, or the identity with ``identity``) on the GPU.
     Forward: x_0 = s0, x_{k+1} = M_k x_k + c_k; transposed: from k = n-1 down, x = M_k^T x + c_k.
+    ``mode`` 2: forward order applying M_k^T (pass transposed maps to apply the originals; the
+    fastest form). ``prefix`` = (Mp, cp): maps applied first, in the same mode, values not recorded.
     Returns (values entering every map [n, H, 128, 128] or None, value after the last map)."""
     n, H = int(M.shape[0]), int(M.shape[1])
     dev = M.device
+    if mode is None:
+        mode = 1 if transpose else 0
+    Mp, cp = prefix if prefix is not None else (None, None)
+    n_p = 0 if Mp is None else int(Mp.shape[0])
     out_states = torch.empty_like(M) if states else None
     out_final = torch.empty(H, 128, 128, dtype=torch.float32, device=dev)
-    L.check(L.lib().rb2_gdn_state_fold(L.ptr(M), L.ptr(c), L.ptr(s0), n, H, 128, int(transpose), int(identity),
-                                       L.ptr(out_states), L.ptr(out_final), _stream(dev)), "gdn_state_fold")
+    L.check(L.lib().rb2_gdn_state_fold_ex(L.ptr(M), L.ptr(c), n, L.ptr(Mp if n_p else None), L.ptr(cp if n_p else None),
+                                          n_p, L.ptr(s0), H, 128, int(mode), int(identity), L.ptr(out_states),
+                                          L.ptr(out_final), _stream(dev)), "gdn_state_fold")
     return out_states, out_final
+
+
+def _t(M):
+    """Maps with their last two dimensions transposed (contiguous): mode-2 folds apply the originals."""
+    return M.transpose(-1, -2).contiguous()
 
 
 class _SegmentedGDN(torch.autograd.Function):
@@ -92,17 +104,26 @@ class _SegmentedGDN(torch.autograd.Function):
         if initial_state is not None and rank == 0:
             s0 = initial_state.reshape(Hv, dk, dv).to(torch.float32)
         M_all = None
+        MsT = _t(Ms)
+        s0 = s0.contiguous()
         if world > 1:
             import torch.distributed as dist
             packed = torch.empty(2, Hv, dk, dk, dtype=torch.float32, device=dev)
-            _, packed[0] = state_fold(Ms, identity=True, states=False)      # M_r = M_{n-1} ... M_0
-            _, packed[1] = state_fold(Ms, S0, states=False)                 # c_r = S_out(S_in = 0)
+            # the rank's composed map M_r = M_{n-1} ... M_0 and its output c_r for its true input
+            # (rank 0: the initial state; others: zero)
+            _, packed[0] = state_fold(MsT, identity=True, states=False, mode=2)
+            _, packed[1] = state_fold(MsT, S0, s0, states=False, mode=2)
             gathered = torch.empty(world, 2, Hv, dk, dk, dtype=torch.float32, device=dev)
             dist.all_gather_into_tensor(gathered, packed, group=group)
             M_all = gathered[:, 0].contiguous()
             c_all = gathered[:, 1].contiguous()
-            _, s0 = state_fold(M_all[:rank], c_all[:rank], s0.contiguous(), states=False)
-        S_in, _ = state_fold(Ms, S0, s0.contiguous())
+            # this rank's input: the preceding ranks' maps from zero (rank 0's output already holds
+            # the initial state), then its own segments, in one launch
+            if rank > 0:
+                s0 = torch.zeros_like(s0)
+            S_in, _ = state_fold(MsT, S0, s0, mode=2, prefix=(_t(M_all[:rank]), c_all[:rank]) if rank else None)
+        else:
+            S_in, _ = state_fold(MsT, S0, s0, mode=2)
         o = torch.empty(1, T, Hv, dv, dtype=torch.bfloat16, device=dev)
         hT = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
         fwd(S_in, o, hT, 2, 0)            # normal walk from the true segment inputs
@@ -157,9 +178,12 @@ class _SegmentedGDN(torch.autograd.Function):
             _, d = state_fold(Ms, dS0, transpose=True, states=False)
             d_all = torch.empty(ctx.world, Hv, dk, dv, dtype=torch.float32, device=dev)
             dist.all_gather_into_tensor(d_all, d, group=ctx.group)
-            _, d_last = state_fold(ctx.M_all[ctx.rank + 1:], d_all[ctx.rank + 1:], d_last, transpose=True,
-                                   states=False)
-        dS_out, _ = state_fold(Ms, dS0, d_last, transpose=True)
+            # the following ranks' maps (transposed, last rank first), then this rank's segments
+            later = ctx.world - 1 - ctx.rank
+            pre = (ctx.M_all[ctx.rank + 1:], d_all[ctx.rank + 1:]) if later else None
+            dS_out, _ = state_fold(Ms, dS0, d_last, transpose=True, prefix=pre)
+        else:
+            dS_out, _ = state_fold(Ms, dS0, d_last, transpose=True)
         dh0 = torch.empty(n, Hv, dk, dv, dtype=torch.float32, device=dev)
         bwd(dS_out, dh0, 1, 0)            # normal reversed walk
         bwd(None, None, 2, 0)             # chunk backward

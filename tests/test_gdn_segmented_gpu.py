@@ -101,3 +101,35 @@ def test_state_fold_kernel_matches_oracle(n, transpose):
         _, prod = state_fold(M.cuda(), identity=True, states=False, transpose=transpose)
         eye = torch.eye(128, dtype=torch.float64).expand(H, 128, 128)
         assert rel(prod, OS.fold(M.double(), None, eye, transpose=transpose)[1]) < 1e-5
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("n_pre,n", [(0, 4), (3, 4), (2, 0)])
+def test_state_fold_modes_and_prefix_run(mode, n_pre, n):
+    """rb2_gdn_state_fold_ex: mode 2 (ascending, applying the transpose of the given maps) and a prefix
+    run applied first without recording its entering values, against the oracle fold of the
+    concatenated maps."""
+    from oracle import segments as OS
+    from recant_b200.segmented import state_fold
+    gen = torch.Generator().manual_seed(31 * mode + 7 * n_pre + n)
+    H = 2
+    Mp = torch.randn(n_pre, H, 128, 128, generator=gen) / 128 ** 0.5
+    cp = torch.randn(n_pre, H, 128, 128, generator=gen)
+    M = torch.randn(n, H, 128, 128, generator=gen) / 128 ** 0.5
+    c = torch.randn(n, H, 128, 128, generator=gen)
+    s0 = torch.randn(H, 128, 128, generator=gen)
+    pre = (Mp.cuda(), cp.cuda()) if n_pre else None
+    states, final = state_fold(M.cuda(), c.cuda(), s0.cuda(), mode=mode, prefix=pre)
+    # the same walk in the oracle: mode 2 applies M^T in forward order
+    A = lambda t: t.transpose(-1, -2).contiguous() if mode == 2 else t
+    if mode == 1:  # descending: the prefix runs first, i.e. it is the tail of the concatenation
+        allM, allc = torch.cat([M, Mp]), torch.cat([c, cp])
+        rs, rf = OS.fold(allM.double(), allc.double(), s0.double(), transpose=True)
+        ref_states = rs[:n]
+    else:
+        allM, allc = torch.cat([A(Mp), A(M)]), torch.cat([cp, c])
+        rs, rf = OS.fold(allM.double(), allc.double(), s0.double())
+        ref_states = rs[n_pre:]
+    assert rel(final, rf) < 1e-5
+    if n:
+        assert rel(states, ref_states) < 1e-5
