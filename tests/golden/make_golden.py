@@ -163,7 +163,9 @@ def decode_main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference RECANT checkout>")
+    root = sys.argv[1]
     main(root)
     block_main(root)
     decode_main(root)
