@@ -236,6 +236,14 @@ RB2_API int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_bl
                               const uint8_t* b_images, const void* lora_h, int64_t lora_ldh, const void* lora_b,
                               int lora_r, float lora_scale, int lora_mode, int64_t M, int64_t N, int64_t K, void* out,
                               int out_dtype, void* ws, size_t ws_bytes, void* stream);
+/* rb2_nvfp4_gemm for M <= 4 rows of A (the decode step: one token per sequence; no counterpart in
+ * the reference, whose GEMM backends serve every M alike, nvfp4.py:108-125): reads each row of B
+ * once, one warp per row, instead of 128-row tensor-core tiles. Scales are the row-major e4m3 bytes
+ * [rows, K/16] (FP4Tensor.scales), not the blocked layout. K % 32 == 0, M x K within shared memory
+ * (about 12k columns at M = 4); out [M, N] fp32 or bf16. */
+RB2_API int rb2_nvfp4_gemv(const uint8_t* a_codes, const uint8_t* a_scales, const float* a_gscale,
+                           const uint8_t* b_codes, const uint8_t* b_scales, const float* b_gscale, int64_t M,
+                           int64_t N, int64_t K, void* out, int out_dtype, void* stream);
 RB2_API size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K);
 RB2_API int rb2_nvfp4_gemm_b_images(const uint8_t* b_scales_blocked, int64_t N, int64_t K, void* out,
                                     size_t out_bytes, void* stream);

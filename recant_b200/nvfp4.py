@@ -19,6 +19,10 @@ import torch
 from . import _lib as L
 
 BLOCK = 16
+# Up to this many rows of A the GEMM runs as rb2_nvfp4_gemv (each row of B read once by one warp),
+# as long as A, dequantized with padding (K + K/8 floats per row), fits the kernel's shared memory
+GEMV_MAX_M = 4
+GEMV_MAX_ELEMS = 50_000
 # Frozen weights keep the GEMM's B-operand scale images (built once at quantisation) instead of
 # rebuilding them every call
 CACHE_WEIGHT_IMAGES = True
@@ -103,6 +107,15 @@ def gemm_b200(a, b, out_dtype=torch.float32, lora=None, lora_mode=0) -> torch.Te
         raise ValueError("recant_b200.gemm_b200: operands must be CUDA tensors (no CPU path)")
     out = torch.empty(m, n, dtype=out_dtype, device=a.codes.device)
     lib = L.lib()
+    if lora is None and m <= GEMV_MAX_M and k % 32 == 0 and m * (k + k // 8) <= GEMV_MAX_ELEMS:
+        # a few rows of A (the decode step): read B once, one warp per row
+        ga = a.gscale.reshape(1).to(torch.float32).contiguous()
+        gb = b.gscale.reshape(1).to(torch.float32).contiguous()
+        st = lib.rb2_nvfp4_gemv(L.ptr(a.codes.contiguous()), L.ptr(a.scales.contiguous().view(torch.uint8)), L.ptr(ga),
+                                L.ptr(b.codes.contiguous()), L.ptr(b.scales.contiguous().view(torch.uint8)), L.ptr(gb),
+                                m, n, k, L.ptr(out), _DT[out_dtype], torch.cuda.current_stream(a.codes.device).cuda_stream)
+        L.check(st, "nvfp4_gemv")
+        return out
     wsb = lib.rb2_nvfp4_gemm_workspace_size(m, n, k)
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=a.codes.device)
     ga = a.gscale.reshape(1).to(torch.float32).contiguous()

@@ -131,3 +131,33 @@ def test_gemm_lora_epilogue(M, N, K, r):
     assert _rel(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
     out16 = gemm_b200(a, b, out_dtype=torch.bfloat16, lora=(h, Bm, 2.0))
     assert _rel(out16.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (2, 300, 512), (3, 12288, 1024), (4, 7, 32), (1, 129, 4128)])
+def test_gemv_matches_emulated_and_tensor_core_gemm(M, N, K):
+    """rb2_nvfp4_gemv (M <= 4, the decode step) against the emulated reference GEMM and against the
+    tensor-core kernel on the same operands (that path forced with GEMV_MAX_M = 0)."""
+    from recant_b200 import _lib as L
+    from recant_b200 import gemm_b200
+    from recant_b200 import nvfp4 as N_
+    gen = torch.Generator().manual_seed(M * 1000 + N + K)
+    x = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    a, b = _fp4(x), _fp4(w)
+    prof = L.LaunchProfiler(capacity=64)
+    prof.start()
+    out = gemm_b200(a, b)
+    out16 = gemm_b200(a, b, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert {n for n, _ in prof.read()[0]} == {"nvfp4_gemv"}
+    ref = ON.gemm_emulated(_oracle(a, K), _oracle(b, K))
+    assert _rel(out.cpu().numpy(), ref) < 1e-5, _rel(out.cpu().numpy(), ref)
+    assert _rel(out16.float().cpu().numpy(), ref) < 1e-2
+    if K % 64 == 0:
+        old = N_.GEMV_MAX_M
+        try:
+            N_.GEMV_MAX_M = 0
+            tc_out = gemm_b200(a, b)
+        finally:
+            N_.GEMV_MAX_M = old
+        assert _rel(out.cpu().numpy(), tc_out.cpu().numpy()) < 1e-5
