@@ -71,39 +71,70 @@ __device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 
 
 // (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65); `nthr` threads
 // (a multiple of 128). The four 16x16 diagonal blocks by forward substitution (warps 0-3, lane =
-// column), then the off-diagonal blocks by block rows: T_ij = -T_ii sum_{j<=m<i} L_im T_mj.
+// column) while warps 4-7 zero the blocks above the diagonal; then the off-diagonal blocks by block
+// rows, T_ij = -T_ii X_j with X_j = sum_{j<=m<i} L_im T_mj. Each thread of a block-row step owns a
+// 2x2 tile of one X_j and then of T_ij (a warp: one j, 4 x 8 tiles), so that every shared-memory
+// value it loads feeds two FMAs; every element is still one fma chain in ascending m.
 __device__ inline void unit_lower_inverse(const float* lm, float* tm, float* xbuf, int nthr) {
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
-  for (int idx = tid; idx < 64 * 65; idx += nthr) tm[idx] = 0.f;
-  __syncthreads();
-  if (w < 4 && l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
-    const int o = 16 * w;
-    float col[16];
+  if (w < 4) {
+    if (l < 16) {  // warp w inverts diagonal block w by forward substitution, lane = column
+      const int o = 16 * w;
+      float col[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float t = (i == l) ? 1.f : 0.f;
+      for (int i = 0; i < 16; ++i) {
+        float t = (i == l) ? 1.f : 0.f;
 #pragma unroll
-      for (int m = 0; m < i; ++m) t = fmaf(-lm[(o + i) * 65 + o + m], col[m], t);
-      col[i] = t;
+        for (int m = 0; m < i; ++m) t = fmaf(-lm[(o + i) * 65 + o + m], col[m], t);
+        col[i] = t;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tm[(o + i) * 65 + o + l] = col[i];
     }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) tm[(o + i) * 65 + o + l] = col[i];
+  } else {
+    for (int idx = tid - 128; idx < 6 * 256; idx += nthr - 128) {  // the six blocks above the diagonal
+      const int b = idx >> 8, bi = b < 3 ? 0 : (b < 5 ? 1 : 2), bj = b < 3 ? b + 1 : (b < 5 ? b - 1 : 3);
+      tm[(16 * bi + ((idx >> 4) & 15)) * 65 + 16 * bj + (idx & 15)] = 0.f;
+    }
   }
   __syncthreads();
   for (int bi = 1; bi < 4; ++bi) {
-    for (int e = tid; e < bi * 256; e += nthr) {  // X_bj = sum_{m in [16bj, 16bi)} L[16bi+r][m] T[m][16bj+c]
-      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      float x = 0.f;
-      for (int m = 16 * bj; m < 16 * bi; ++m) x = fmaf(lm[(16 * bi + r) * 65 + m], tm[m * 65 + 16 * bj + c], x);
-      xbuf[e] = x;
+    for (int t = tid; t < 64 * bi; t += nthr) {  // X_bj rows 2 r2, 2 r2 + 1, columns 2 cc, 2 cc + 1
+      const int bj = t >> 6, r2 = (t >> 3) & 7, cc = t & 7;
+      const float* a = lm + (16 * bi + 2 * r2) * 65;
+      const float* b = tm + 16 * bj + 2 * cc;
+      float x00 = 0.f, x01 = 0.f, x10 = 0.f, x11 = 0.f;
+      for (int m = 16 * bj; m < 16 * bi; ++m) {
+        const float a0 = a[m], a1 = a[65 + m], b0 = b[m * 65], b1 = b[m * 65 + 1];
+        x00 = fmaf(a0, b0, x00);
+        x01 = fmaf(a0, b1, x01);
+        x10 = fmaf(a1, b0, x10);
+        x11 = fmaf(a1, b1, x11);
+      }
+      float* xo = xbuf + bj * 256 + 2 * r2 * 16 + 2 * cc;
+      *reinterpret_cast<float2*>(xo) = make_float2(x00, x01);
+      *reinterpret_cast<float2*>(xo + 16) = make_float2(x10, x11);
     }
     __syncthreads();
-    for (int e = tid; e < bi * 256; e += nthr) {  // T_bi,bj = -T_bi,bi X_bj
-      const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      float t = 0.f;
+    for (int t = tid; t < 64 * bi; t += nthr) {  // T_bi,bj = -T_bi,bi X_bj, same tiles
+      const int bj = t >> 6, r2 = (t >> 3) & 7, cc = t & 7;
+      const float* a = tm + (16 * bi + 2 * r2) * 65 + 16 * bi;
+      const float* xb = xbuf + bj * 256 + 2 * cc;
+      float t00 = 0.f, t01 = 0.f, t10 = 0.f, t11 = 0.f;
 #pragma unroll
-      for (int m = 0; m < 16; ++m) t = fmaf(tm[(16 * bi + r) * 65 + 16 * bi + m], xbuf[bj * 256 + m * 16 + c], t);
-      tm[(16 * bi + r) * 65 + 16 * bj + c] = -t;
+      for (int m = 0; m < 16; ++m) {
+        const float a0 = a[m], a1 = a[65 + m];
+        const float2 x = *reinterpret_cast<const float2*>(xb + m * 16);
+        t00 = fmaf(a0, x.x, t00);
+        t01 = fmaf(a0, x.y, t01);
+        t10 = fmaf(a1, x.x, t10);
+        t11 = fmaf(a1, x.y, t11);
+      }
+      float* to = tm + (16 * bi + 2 * r2) * 65 + 16 * bj + 2 * cc;
+      to[0] = -t00;
+      to[1] = -t01;
+      to[65] = -t10;
+      to[66] = -t11;
     }
     __syncthreads();
   }

@@ -226,7 +226,8 @@ constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
 constexpr int VEC = DAQF + 16640;                                              // 14 x 64 floats
 constexpr int RED = VEC + 14 * 256;                                            // 5 x 4 x 64 floats
-constexpr int END = RED + 5 * 1024 + 64;
+constexpr int STATS = RED + 5 * 1024 + 64;  // the next item's per-token stats, fp32 [4][64], by bulk copy
+constexpr int END = STATS + 1024;
 }  // namespace lay
 constexpr int kBChunkSmem = lay::END + 1024;
 
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
         *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [4][64] */, *scal = vec + 768;
   float* red = reinterpret_cast<float*>(sm + lay::RED);  // [5][4][64]
   __shared__ uint64_t bar[5];
-  __shared__ uint64_t ldbar[3];   // loads: phase-1 tiles (bulk + TMA), T, [K;Q] (TMA)
+  __shared__ uint64_t ldbar[3];   // loads: phase-1 tiles and stats (bulk + TMA), T, [K;Q] (TMA)
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
@@ -291,52 +292,70 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     tc::fence_mbar_init();
   }
   // Phase-1 tiles of one (chunk, head) other than [K;Q], issued by thread 0 on ldbar[0]: the
-  // workspace images by bulk copy and the caller's v, dO rows by TMA (rows past the sequence are
-  // zeroed after the wait).
+  // workspace images and the per-token stats by bulk copy and the caller's v, dO rows by TMA (rows
+  // past the sequence are zeroed after the wait).
   auto issue_phase1 = [&](int64_t item) {
     if (tid != 0) return;
     const int ci_ = int(item / p.Hv), h_ = int(item % p.Hv);
     const int64_t ch_ = int64_t(ci_) * p.Hv + h_;
     const int t0_ = ws.ct.tok0[ci_];
     tc::fence_proxy_async();
-    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2 + 2 * 16384);
+    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2 + 2 * 16384 + 1024);
     tc::bulk_load(sm + lay::DVP, ws.dvp + ch_ * 8192, 16384, &ldbar[0]);
     tc::bulk_load(sm + lay::ST, ws.hs + ch_ * 16384, 32768, &ldbar[0]);
     tc::bulk_load(sm + lay::DHT, ws.dh + ch_ * 16384, 32768, &ldbar[0]);
     tc::bulk_load(sm + lay::VPT, ws.vp + ch_ * 8192, 16384, &ldbar[0]);
     tc::tma_rows128(sm + lay::VT, 8192, 0, &map_v, h_, t0_, &ldbar[0]);
     tc::tma_rows128(sm + lay::DOT, 8192, 0, &map_do, h_, t0_, &ldbar[0]);
+    tc::bulk_load(sm + lay::STATS, ws.stats + ch_ * 256, 1024, &ldbar[0]);
   };
+  // [K;Q] rows of one (chunk, key head) by TMA on ldbar[2]. The value heads of a group share them,
+  // so they are fetched only when the (chunk, key head) changes, during the previous item's final
+  // epilogue once its reads of the region are done.
+  auto issue_kq = [&](int64_t item) {
+    if (tid != 0) return;
+    const int ci_ = int(item / p.Hv), hk_ = int(item % p.Hv) / p.group;
+    const int t0_ = ws.ct.tok0[ci_];
+    tc::fence_proxy_async();
+    tc::mbar_expect_tx(&ldbar[2], 32768);
+    tc::tma_rows128(sm + lay::KQ, 16384, 0, &map_k, hk_, t0_, &ldbar[2]);
+    tc::tma_rows128(sm + lay::KQ, 16384, 64, &map_q, hk_, t0_, &ldbar[2]);
+  };
+  // items a and b read the same [K;Q] rows
+  auto same_kq = [&](int64_t a, int64_t b) { return a / p.Hv == b / p.Hv && (a % p.Hv) / p.group == (b % p.Hv) / p.group; };
   tc::fence_before_sync();
   __syncthreads();  // barrier init and the TMEM address visible
   tc::fence_after_sync();
-  if (seq_item(0) >= 0) issue_phase1(seq_item(0));
+  if (seq_item(0) >= 0) {
+    issue_phase1(seq_item(0));
+    issue_kq(seq_item(0));
+  }
+  uint32_t kq_ph = 0;     // parity of the next [K;Q] load to wait for
+  int64_t prev_item = -1;
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
   for (int64_t it = 0;; ++it) {
   const int64_t item = seq_item(it);
   if (item < 0) break;
-  const uint32_t ph = uint32_t(it & 1);  // parity of every barrier (each completes once per item)
+  const uint32_t ph = uint32_t(it & 1);  // parity of the barriers that complete once per item
   const int ci = int(item / p.Hv), h = int(item % p.Hv);
   const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
   const int64_t ch = int64_t(ci) * p.Hv + h;
-  if (tid == 0) {  // [K;Q] rows of this chunk by TMA (the previous item's final epilogue read this region)
-    tc::fence_proxy_async();
-    tc::mbar_expect_tx(&ldbar[2], 32768);
-    tc::tma_rows128(sm + lay::KQ, 16384, 0, &map_k, hk, t0, &ldbar[2]);
-    tc::tma_rows128(sm + lay::KQ, 16384, 64, &map_q, hk, t0, &ldbar[2]);
+  if (prev_item < 0 || !same_kq(prev_item, item)) {  // issued at the start or by the previous item
+    tc::mbar_wait(&ldbar[2], kq_ph, ws.err, 137);
+    kq_ph ^= 1u;
   }
+  prev_item = item;
+  tc::mbar_wait(&ldbar[0], ph, ws.err, 130);
   if (tid < 64) {
-    const float* st = ws.stats + ch * 256;
+    const float* st = reinterpret_cast<const float*>(sm + lay::STATS);
     cum[tid] = st[tid]; rq[tid] = st[64 + tid]; rk[tid] = st[128 + tid]; beta[tid] = st[192 + tid];
     ecum[tid] = expf(st[tid]);
     edec[tid] = expf(st[63] - st[tid]);
     dbeta_acc[tid] = 0.f;
     dcum_acc[tid] = 0.f;
   }
-  tc::mbar_wait(&ldbar[2], ph, ws.err, 137);
-  tc::mbar_wait(&ldbar[0], ph, ws.err, 130);
   if (L < 64) {  // rows past the end of the sequence: zero (TMA fills only past the tensor's end)
     tc::zero_rows_tail(sm + lay::KQ, 16384, 0, L, 256);
     tc::zero_rows_tail(sm + lay::KQ, 16384, 64, L, 256);
@@ -611,7 +630,11 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     for (int j = 0; j < 32; ++j) t2[j] = dkh[j] * kr_[j];
     red5[q4 * 64 + c0 + l] = warp_colsum32(t2);
   }
-  __syncthreads();
+  __syncthreads();  // every thread holds its q and k rows (xr, kr_): [K;Q] may be refilled
+  {
+    const int64_t next = seq_item(it + 1);
+    if (next >= 0 && !same_kq(item, next)) issue_kq(next);
+  }
   if (tid < 64) {  // combine the four lane quarters
 #pragma unroll
     for (int b = 0; b < 5; ++b) {
