@@ -15,6 +15,7 @@
 // Pass 2 re-reads x in REVERSE block order so that the tail of x that pass 1 left in the
 // 126 MB L2 is consumed first, recomputes the transform and writes codes and scales.
 // One thread owns one 16-element block: a warp covers 512 contiguous elements of a row.
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include "common.cuh"
@@ -24,26 +25,32 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// The raw bytes of one 16-element block (32 for bf16, 64 for fp32): loaded one block ahead of the
+// block being transformed, so that every thread keeps a load in flight while it computes.
 template <typename T>
-__device__ __forceinline__ void load16(const T* __restrict__ p, float v[16]);
+struct Raw16 {
+  uint4 w[sizeof(T) * 16 / 16];
+};
 
-template <>
-__device__ __forceinline__ void load16<float>(const float* __restrict__ p, float v[16]) {
-  const float4* p4 = reinterpret_cast<const float4*>(p);
+template <typename T>
+__device__ __forceinline__ void load_raw(const T* __restrict__ p, Raw16<T>& r) {
+  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < int(sizeof(T)); ++i) r.w[i] = __ldg(p4 + i);
+}
+
+__device__ __forceinline__ void unpack16(const Raw16<float>& r, float v[16]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float4 t = __ldg(p4 + i);
-    v[4 * i + 0] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    v[4 * i + 0] = __uint_as_float(r.w[i].x); v[4 * i + 1] = __uint_as_float(r.w[i].y);
+    v[4 * i + 2] = __uint_as_float(r.w[i].z); v[4 * i + 3] = __uint_as_float(r.w[i].w);
   }
 }
 
-template <>
-__device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* __restrict__ p, float v[16]) {
-  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void unpack16(const Raw16<__nv_bfloat16>& r, float v[16]) {
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    uint4 t = __ldg(p4 + i);
-    uint32_t w[4] = {t.x, t.y, t.z, t.w};
+    const uint32_t w[4] = {r.w[i].x, r.w[i].y, r.w[i].z, r.w[i].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       v[8 * i + 2 * j + 0] = __uint_as_float(w[j] << 16);
@@ -73,9 +80,14 @@ __device__ __forceinline__ void transform16(float v[16], bool rot) {
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], 0.25f);
-    if (sizeof(T) == 2) {
+    if (sizeof(T) == 2) {  // one paired conversion per two elements
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+      for (int i = 0; i < 16; i += 2) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v[i], v[i + 1]);
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+        v[i] = __uint_as_float(u << 16);
+        v[i + 1] = __uint_as_float(u & 0xffff0000u);
+      }
     }
   }
 }
@@ -83,17 +95,25 @@ __device__ __forceinline__ void transform16(float v[16], bool rot) {
 __global__ void __launch_bounds__(kThreads)
 zero_word_kernel(unsigned int* w) { *w = 0u; }
 
+// Pass 1: a grid-stride sweep (forward) over the blocks, one block in flight per thread ahead of
+// the one being transformed; one atomicMax per CTA.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 amax_kernel(const T* __restrict__ x, int64_t n_blocks, int rot, unsigned int* __restrict__ gmax_bits) {
-  const int64_t b = int64_t(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t stride = int64_t(gridDim.x) * kThreads;
+  int64_t b = int64_t(blockIdx.x) * kThreads + threadIdx.x;
   float m = 0.f;
-  if (b < n_blocks) {
+  Raw16<T> cur;
+  if (b < n_blocks) load_raw(x + b * 16, cur);
+  for (; b < n_blocks; b += stride) {
+    Raw16<T> nxt;
+    if (b + stride < n_blocks) load_raw(x + (b + stride) * 16, nxt);
     float v[16];
-    load16<T>(x + b * 16, v);
+    unpack16(cur, v);
     transform16<T>(v, rot != 0);
 #pragma unroll
     for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+    cur = nxt;
   }
   m = warp_max(m);
   __shared__ float red[kThreads / 32];
@@ -135,11 +155,6 @@ __device__ __forceinline__ int e2m1_index(float a) {
   return k < 16 ? int((lo >> (4 * k)) & 0xF) : int((hi >> (4 * (k - 16))) & 0xF);
 }
 
-__device__ __forceinline__ float grid_value(int i) {
-  // e2m1 magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6
-  return i < 4 ? 0.5f * float(i) : (i == 4 ? 2.f : (i == 5 ? 3.f : (i == 6 ? 4.f : 6.f)));
-}
-
 // floor(n / d) for n < 2^32 by one multiply and shift (Granlund & Montgomery, PLDI 1994):
 // s = ceil(log2 d), m = ceil(2^(32+s) / d)
 struct Divider {
@@ -158,21 +173,24 @@ __device__ __forceinline__ uint32_t divide(uint32_t n, Divider dv) {
   return uint32_t(hi32 >> dv.s);
 }
 
+// SR: the upper of the two grid neighbours of a in [0, 6], as the index of the first of 0, .5, 1,
+// 1.5, 2, 3, 4 that is not below a (at least 1): every such point is a multiple of 2^21 in the bit
+// pattern, so with key = ceil(bits(a) / 2^21) the count is a step function of key in [504, 518],
+// read from a packed table of 4-bit entries.
+__device__ __forceinline__ int sr_upper(float a) {
+  const uint32_t key = (__float_as_uint(a) + 0x1FFFFFu) >> 21;
+  const uint32_t k = min(max(key, 504u), 518u) - 504u;  // 0 .. 14
+  return int((0x776655443322221ull >> (4 * k)) & 0xFu);
+}
+
+// Codes and scale of block b from its raw bytes.
 template <typename T>
-__global__ void __launch_bounds__(kThreads)
-quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divider by_groups, int rot,
-             int stochastic, uint64_t seed, const unsigned int* __restrict__ gmax_bits,
-             uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
-             uint8_t* __restrict__ blocked, float* __restrict__ gscale_out) {
-  // reverse CTA order: consume what pass 1 left in L2 first
-  const uint32_t cta = gridDim.x - 1 - blockIdx.x;
-  const uint32_t b = cta * kThreads + threadIdx.x;
-  const float gmax = fmaxf(__uint_as_float(*gmax_bits), 1e-30f);
-  const float s_g = __fdiv_rn(gmax, 2688.0f);  // 6 * 448
-  if (blockIdx.x == 0 && threadIdx.x == 0) *gscale_out = s_g;
-  if (b >= n_blocks) return;
+__device__ __forceinline__ void quant_block(uint32_t b, const Raw16<T>& raw, int rot, int stochastic, uint64_t seed,
+                                            float s_g, uint32_t groups, Divider by_groups,
+                                            uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+                                            uint8_t* __restrict__ blocked) {
   float v[16];
-  load16<T>(x + size_t(b) * 16, v);
+  unpack16(raw, v);
   transform16<T>(v, rot != 0);
   float amax = 0.f;
 #pragma unroll
@@ -182,46 +200,56 @@ quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divide
   const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
   const float sq = __half2float(__half(hr));
   const float denom = __fmul_rn(sq == 0.f ? 1.f : sq, s_g);
-
-  uint32_t rnd[16];
+  // a' = |x| RN(1/denom) is within 2.5 ulp of the correctly rounded |x| / denom (two roundings of
+  // relative size 2^-24 each, plus the quotient's own half ulp). Every decision point of the
+  // rounding (RN: 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5; SR: the grid 0.5, 1, 1.5, 2, 3, 4, 6) lies on
+  // a multiple of 2^21 in the bit pattern, so when the bits of a' are more than 8 away from such a
+  // multiple, a' and the exact quotient fall on the same side of every point; otherwise (about one
+  // element in 1.3e5) the exact quotient is computed. q < 0 <=> x < 0 since denom > 0 (and -0
+  // gives +0 / no sign bit in both); the sign is bit 3 of each nibble.
+  const float rinv = __frcp_rn(denom);
+  uint32_t packed[2] = {0u, 0u};
   if (stochastic) {
+    // Unbiased choice between the grid neighbours lo < a <= hi with p = (a - lo) / (hi - lo); the
+    // spacing hi - lo is a power of two, so the division is an exact multiply. p from a' differs from
+    // p of the exact quotient by a few ulps, which moves no choice's probability by more than that.
+    uint32_t rnd[16];
     const uint2 key = make_uint2(uint32_t(seed), uint32_t(seed >> 32));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint4 r = philox4x32_10(make_uint4(b, 0u, uint32_t(j), 0u), key);
       rnd[4 * j + 0] = r.x; rnd[4 * j + 1] = r.y; rnd[4 * j + 2] = r.z; rnd[4 * j + 3] = r.w;
     }
-  }
-  uint32_t packed[2] = {0u, 0u};
-  if (stochastic) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float q = __fdiv_rn(v[i], denom);
-      const float a = fminf(fabsf(q), 6.0f);
-      int hi = (a > 0.f) + (a > 0.5f) + (a > 1.f) + (a > 1.5f) + (a > 2.f) + (a > 3.f) + (a > 4.f);
-      hi = hi < 1 ? 1 : hi;
-      const float glo = grid_value(hi - 1), ghi = grid_value(hi);
-      const float p = __fdiv_rn(__fsub_rn(a, glo), __fsub_rn(ghi, glo));
-      const float u = float(rnd[i] >> 8) * (1.0f / 16777216.0f);
-      const int idx = (u < p) ? hi : hi - 1;
-      packed[i >> 3] |= uint32_t(idx + (q < 0.f ? 8 : 0)) << (4 * (i & 7));
-    }
-  } else {
-    // Round to nearest without a division per element. a' = |x| RN(1/denom) is within 2.5 ulp of the
-    // correctly rounded |x| / denom (two roundings of relative size 2^-24 each, plus the quotient's
-    // own half ulp). Every decision point of e2m1_index lies on a multiple of 2^21 in the bit
-    // pattern, so when the bits of a' are more than 8 away from such a multiple, a' and the exact
-    // quotient fall on the same side of every point and give the same index; otherwise (about one
-    // element in 1.3e5) the exact quotient is computed. q < 0 <=> x < 0 since denom > 0 (and -0
-    // gives +0 / no sign bit in both).
-    const float rinv = __frcp_rn(denom);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       float a = __fmul_rn(fabsf(v[i]), rinv);
       const uint32_t u = __float_as_uint(a);
       if (u != 0u && ((u + 8u) & 0x1FFFFFu) <= 16u) a = fabsf(__fdiv_rn(v[i], denom));
-      const int idx = e2m1_index(fminf(a, 6.0f));
+      a = fminf(a, 6.0f);
+      const int hi = sr_upper(a);
+      const float glo = hi <= 4 ? 0.5f * float(hi - 1) : float(hi - 3);
+      const float inv = hi <= 4 ? 2.f : (hi < 7 ? 1.f : 0.5f);
+      const float pr = __fmul_rn(__fsub_rn(a, glo), inv);
+      const float r = float(rnd[i] >> 8) * (1.0f / 16777216.0f);
+      const int idx = (r < pr) ? hi : hi - 1;
       packed[i >> 3] |= uint32_t(idx + (v[i] < 0.f ? 8 : 0)) << (4 * (i & 7));
+    }
+  } else {
+    // RN: away from the decision points the index is the nearest grid point, which the hardware
+    // pair conversion (cvt.rn.satfinite.e2m1x2, values above 6 saturating to 6) gives for two
+    // magnitudes at once; at a decision point it rounds ties to even where the reference rounds
+    // them toward zero, and those pairs take the exact path, which counts the points.
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const float a0 = __fmul_rn(fabsf(v[i]), rinv), a1 = __fmul_rn(fabsf(v[i + 1]), rinv);
+      const uint32_t u0 = __float_as_uint(a0), u1 = __float_as_uint(a1);
+      uint32_t nib = __nv_cvt_float2_to_fp4x2(make_float2(a0, a1), __NV_E2M1, cudaRoundNearest);  // a0 low
+      if ((u0 != 0u && ((u0 + 8u) & 0x1FFFFFu) <= 16u) || (u1 != 0u && ((u1 + 8u) & 0x1FFFFFu) <= 16u)) {
+        const float e0 = fabsf(__fdiv_rn(v[i], denom)), e1 = fabsf(__fdiv_rn(v[i + 1], denom));
+        nib = uint32_t(e2m1_index(fminf(e0, 6.0f))) | (uint32_t(e2m1_index(fminf(e1, 6.0f))) << 4);
+      }
+      nib |= (v[i] < 0.f ? 8u : 0u) | (v[i + 1] < 0.f ? 0x80u : 0u);
+      packed[i >> 3] |= (nib & 0xFFu) << (4 * (i & 7));
     }
   }
   reinterpret_cast<uint2*>(codes)[b] = make_uint2(packed[0], packed[1]);
@@ -232,6 +260,46 @@ quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divide
     const size_t off = ((r >> 7) * ncb + (c >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
     blocked[off] = uint8_t(s8);
   }
+}
+
+// Pass 2: a grid-stride sweep in REVERSE block order (the j-th block from the end), so that what
+// pass 1 left in L2 is consumed first, with the next block's load in flight during each block.
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 4)
+quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divider by_groups, int rot,
+             int stochastic, uint64_t seed, const unsigned int* __restrict__ gmax_bits,
+             uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+             uint8_t* __restrict__ blocked, float* __restrict__ gscale_out) {
+  const float gmax = fmaxf(__uint_as_float(*gmax_bits), 1e-30f);
+  const float s_g = __fdiv_rn(gmax, 2688.0f);  // 6 * 448
+  if (blockIdx.x == 0 && threadIdx.x == 0) *gscale_out = s_g;
+  const uint32_t stride = gridDim.x * kThreads;
+  uint32_t j = blockIdx.x * kThreads + threadIdx.x;
+  Raw16<T> cur;
+  if (j < n_blocks) load_raw(x + size_t(n_blocks - 1 - j) * 16, cur);
+  for (; j < n_blocks; j += stride) {
+    Raw16<T> nxt;
+    if (j + stride < n_blocks) load_raw(x + size_t(n_blocks - 1 - (j + stride)) * 16, nxt);
+    quant_block<T>(n_blocks - 1 - j, cur, rot, stochastic, seed, s_g, groups, by_groups, codes, scales, blocked);
+    cur = nxt;
+  }
+}
+
+// CTAs of kThreads that fit on one SM (the persistent grids are SMs x this).
+template <typename K>
+int resident_ctas(K kernel) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, 0) != cudaSuccess || n < 1) n = 1;
+  return n;
+}
+
+template <typename T>
+void sweep_grids(int sms, int64_t n_blocks, unsigned* g_amax, unsigned* g_quant) {
+  static const int occ_a = resident_ctas(amax_kernel<T>);
+  static const int occ_q = resident_ctas(quant_kernel<T>);
+  const int64_t need = (n_blocks + kThreads - 1) / kThreads;
+  *g_amax = unsigned(need < int64_t(sms) * occ_a ? need : int64_t(sms) * occ_a);
+  *g_quant = unsigned(need < int64_t(sms) * occ_q ? need : int64_t(sms) * occ_q);
 }
 
 }  // namespace
@@ -270,21 +338,26 @@ extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype
     const size_t nb = size_t((M + 127) / 128) * size_t((groups + 3) / 4) * 512;
     RB2_CUDA(cudaMemsetAsync(scales_blocked, 0, nb, s), "nvfp4_quantize: clear blocked pads");
   }
-  const unsigned grid = unsigned((n_blocks + kThreads - 1) / kThreads);
   const Divider div = make_divider(uint32_t(groups));
+  int dev = 0, sms = 148;
+  RB2_CUDA(cudaGetDevice(&dev), "nvfp4_quantize: device");
+  RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "nvfp4_quantize: SM count");
+  unsigned ga = 1, gq = 1;
   if (dtype == RB2_BF16) {
     auto xp = static_cast<const __nv_bfloat16*>(x);
-    { ProfScope ps_("nvfp4_amax", s); amax_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
+    sweep_grids<__nv_bfloat16>(sms, n_blocks, &ga, &gq);
+    { ProfScope ps_("nvfp4_amax", s); amax_kernel<__nv_bfloat16><<<ga, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
     ProfScope ps_("nvfp4_quant", s);
-    quant_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(xp, uint32_t(n_blocks), uint32_t(groups), div, use_rht,
-                                                          stochastic, seed, gmax, codes, scales, scales_blocked,
-                                                          gscale);
+    quant_kernel<__nv_bfloat16><<<gq, kThreads, 0, s>>>(xp, uint32_t(n_blocks), uint32_t(groups), div, use_rht,
+                                                        stochastic, seed, gmax, codes, scales, scales_blocked,
+                                                        gscale);
   } else {
     auto xp = static_cast<const float*>(x);
-    { ProfScope ps_("nvfp4_amax", s); amax_kernel<float><<<grid, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
+    sweep_grids<float>(sms, n_blocks, &ga, &gq);
+    { ProfScope ps_("nvfp4_amax", s); amax_kernel<float><<<ga, kThreads, 0, s>>>(xp, n_blocks, use_rht, gmax); }
     ProfScope ps_("nvfp4_quant", s);
-    quant_kernel<float><<<grid, kThreads, 0, s>>>(xp, uint32_t(n_blocks), uint32_t(groups), div, use_rht, stochastic,
-                                                  seed, gmax, codes, scales, scales_blocked, gscale);
+    quant_kernel<float><<<gq, kThreads, 0, s>>>(xp, uint32_t(n_blocks), uint32_t(groups), div, use_rht, stochastic,
+                                                seed, gmax, codes, scales, scales_blocked, gscale);
   }
   RB2_CHECK_LAUNCH("nvfp4_quantize");
   return RB2_OK;
