@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     if (tid == 0) tc::bulk_wait_read();  // the S^T and V'^T tiles are rewritten next step
     tc::fence_before_sync();
     __syncthreads();
-    if (outs) store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 128, r, 32 * hh, L, ox);
+    if (outs) store_cols32(o + (int64_t(t0) * p.Hv + h) * 128, p.Hv * 128, r, 32 * hh, L, ox);
     phase ^= 1;
   }
   if (hT) {

@@ -162,14 +162,16 @@ __device__ __forceinline__ void store_row16(unsigned char* tile, int rows, int r
 
 // Write 32 per-token values of head-dim column r (tokens 32 hh + j) as bf16 to dst[(tok) * row + r],
 // pairing lanes r, r^1 so that every store is one 4-byte bf16x2.
-__device__ __forceinline__ void store_cols32(bf16* dst, int64_t row, int r, int t_base, int L, const float (&v)[32]) {
+// `row` elements between tokens; the 64 tokens of a chunk span less than 2^31 elements.
+__device__ __forceinline__ void store_cols32(bf16* dst, int row, int r, int t_base, int L, const float (&v)[32]) {
   const bool odd = (r & 1) != 0;
+  const int t_odd = t_base + (odd ? 1 : 0);
+  uint32_t* base = reinterpret_cast<uint32_t*>(dst + t_odd * row + (r & ~1));
 #pragma unroll
   for (int j = 0; j < 32; j += 2) {
     const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
-    const int tk = t_base + j + (odd ? 1 : 0);
     const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
-    if (tk < L) *reinterpret_cast<uint32_t*>(dst + int64_t(tk) * row + (r & ~1)) = tc::pack_bf16(lo, hi);
+    if (t_odd + j < L) base[(j * row) >> 1] = tc::pack_bf16(lo, hi);
   }
 }
 

@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     const uint32_t id_ss = tc::idesc_bf16(128, 64, true, true);
     const uint32_t id_sn = tc::idesc_bf16(128, 64, true, true, true);
     const uint32_t id_64 = tc::idesc_bf16(64, 64, false, true);
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 128; k0 += 16) {
       const uint32_t o16 = (k0 >> 6) * 16384 + (k0 & 63) * 2, o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
       const bool acc = k0 > 0;
@@ -448,19 +448,19 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   if (tid == 0) {  // ---- G2 ----
     const uint32_t dva = tc::smem_u32(sm + lay::DVP), bva = tc::smem_u32(sm + lay::BV), bka = tc::smem_u32(sm + lay::BK);
     const uint32_t id_t1 = tc::idesc_bf16(64, 64, true, false), id_t2 = tc::idesc_bf16(64, 64, true, false);
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 128; k0 += 16) {  // dT = dV' (beta V)^T, dV' read MN-major from the dV'^T tile
       const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
       tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dva + k0 * 128, 8192), tc::desc_kmajor_sw128(bva + o8), id_t1,
                    k0 > 0);
     }
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 128; k0 += 16) {
       const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
       tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dwa + k0 * 128, 16384), tc::desc_kmajor_sw128(bka + o8), id_t2, true);
     }
     const uint32_t id_bv = tc::idesc_bf16(128, 64, false, true), id_bk = tc::idesc_bf16(128, 64, false, true);
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16) {
       tc::mma_bf16(tbase + 384, tc::desc_kmajor_sw128(dva + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bv,
                    k0 > 0);
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   if (tid == 0) {  // ---- G3: Y = T^T dT ----
     const uint32_t dta = tc::smem_u32(sm + lay::DTT);
     const uint32_t id_y = tc::idesc_bf16(64, 64, true, true);
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16)
       tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), tc::desc_mnmajor_sw128(dta + k0 * 128, 8192),
                    id_y, k0 > 0);
@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   if (tid == 0) {  // ---- G4: dL' = Y T^T ----
     const uint32_t ya = tc::smem_u32(sm + lay::YT);
     const uint32_t id_l = tc::idesc_bf16(128, 64, false, false);
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16)
       tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
     tc::mma_commit(&bar[3]);
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     const uint32_t p1 = tc::smem_u32(sm + lay::PB1), p2 = tc::smem_u32(sm + lay::PB2), q1 = tc::smem_u32(sm + lay::QB1),
                    q2 = tc::smem_u32(sm + lay::QB2);
     const uint32_t id_k = tc::idesc_bf16(128, 64, true, false), id_m = tc::idesc_bf16(128, 64, true, true);
-#pragma unroll
+#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16) {
       const uint64_t ka = tc::desc_mnmajor_sw128(kqa + k0 * 128, 16384);         // K rows as (M = dk, K = j)
       const uint64_t qa = tc::desc_mnmajor_sw128(kqa + 8192 + k0 * 128, 16384);  // Q rows (start at row 64)
@@ -652,11 +652,8 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       gq[j] = rqi * dqh[j] - xr[j] * rqi * rqi * rqi * red2[i];
       gk[j] = rki * dkh[j] - kr_[j] * rki * rki * rki * red5[i];
     }
-    if (p.group == 1) {
-      const int64_t row = int64_t(p.Hk) * 128;
-      store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
-      store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
-    } else {  // GQA: the group's sum, in fp32 in this CTA's scratch slice until its last value head
+    bool last = true;  // this value head completes dq / dk of its key head
+    if (p.group > 1) {  // GQA: the group's sum, in fp32 in this CTA's scratch slice until its last value head
       float* pq = ws.dqh + size_t(blockIdx.x) * 8192;  // [64 tokens][128], written and read by this thread
       float* pk = ws.dkh + size_t(blockIdx.x) * 8192;
       const int g = h % p.group;
@@ -673,11 +670,13 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
           pq[(c0 + j) * 128 + r] = gq[j];
           pk[(c0 + j) * 128 + r] = gk[j];
         }
-      } else {
-        const int64_t row = int64_t(p.Hk) * 128;
-        store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
-        store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
+        last = false;
       }
+    }
+    if (last) {
+      const int row = p.Hk * 128;
+      store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
+      store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
     }
   }
   // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------

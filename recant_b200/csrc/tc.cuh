@@ -132,6 +132,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait: gives up after ~2^26 polls (seconds), records `code` in *err and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+#pragma unroll 1  // one copy of the poll per call site: unrolled, the polls of a kernel outgrow the I-cache
   for (uint32_t i = 0; i < (1u << 26); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 64) __nanosleep(32);
