@@ -49,8 +49,8 @@ KERNEL_FLOPS_PER_CH = {
 # DRAM bytes (read + write) per chunk-head of each tensor-core kernel, from the ncu capture in
 # profiles/gdn_fast_kernels_B1T4096_ncu.md (per launch at B1 T4096 / 2048 chunk-heads); traffic scales
 # with the number of chunk-heads
-TRAFFIC_PER_CH = {"gdn_fast_prep": 183.47392e6 / 2048, "gdn_fast_state_fwd": 245.305088e6 / 2048,
-                  "gdn_fast_state_bwd": 218.57152e6 / 2048, "gdn_fast_chunk_bwd": 381.587712e6 / 2048}
+TRAFFIC_PER_CH = {"gdn_fast_prep": 184.964864e6 / 2048, "gdn_fast_state_fwd": 247.328512e6 / 2048,
+                  "gdn_fast_state_bwd": 218.171904e6 / 2048, "gdn_fast_chunk_bwd": 379.720704e6 / 2048}
 
 
 def peaks():
