@@ -822,33 +822,63 @@ def main():
     value = total_tokens / (ms / 1e3)
 
     # ---- end to end through the public op with host buffers ------------------------------
+    # Steps are double-buffered as a caller streaming batches would run them: step k+1's inputs go
+    # up on one copy stream while step k computes, and step k's results come down on another while
+    # step k+1 computes (PCIe carries both directions at once). Every step still moves all of its
+    # own inputs and results; the timed region ends when the last results are in host memory.
     host_in = {n: t.detach().cpu().pin_memory() for n, t in inp.items()}
     host_do = do.cpu().pin_memory()
     outs_host = {n: torch.empty_like(t.detach().cpu()).pin_memory() for n, t in inp.items()}
     o_host = torch.empty(B, T, Hv, d, dtype=torch.bfloat16).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host_in.values()) + host_do.numel() * host_do.element_size()
     d2h = o_host.numel() * o_host.element_size() + sum(t.numel() * t.element_size() for t in outs_host.values())
+    slots = [({n: torch.empty(t.shape, dtype=t.dtype, device=dev) for n, t in host_in.items()},
+              torch.empty(host_do.shape, dtype=host_do.dtype, device=dev)) for _ in range(2)]
+    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_up = [torch.cuda.Event() for _ in range(2)]    # a slot's inputs are on the device
+    ev_used = [torch.cuda.Event() for _ in range(2)]  # a slot's inputs have been consumed
 
-    def e2e_step():
-        dev_in = {n: t.to(dev, non_blocking=True).requires_grad_(True) for n, t in host_in.items()}
-        ddo = host_do.to(dev, non_blocking=True)
+    def upload(k):
+        ins, ddo = slots[k % 2]
+        with torch.cuda.stream(s_up):
+            s_up.wait_event(ev_used[k % 2])  # the step two back has finished reading this slot
+            for n, t in host_in.items():
+                ins[n].copy_(t, non_blocking=True)
+            ddo.copy_(host_do, non_blocking=True)
+            ev_up[k % 2].record(s_up)
+
+    def compute_and_download(k):
+        ins, ddo = slots[k % 2]
+        stream.wait_event(ev_up[k % 2])
+        dev_in = {n: t.detach().requires_grad_(True) for n, t in ins.items()}
         o, _ = gdn_b200(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], cu_seqlens=cu,
                         path=args.path)
         o.backward(ddo)
+        ev_used[k % 2].record(stream)
         if bucket is not None and world > 1:
             dist.all_reduce(bucket)
-        o_host.copy_(o.detach(), non_blocking=True)
-        for n, t in dev_in.items():
-            outs_host[n].copy_(t.grad, non_blocking=True)
+        results = [(o_host, o.detach())] + [(outs_host[n], t.grad) for n, t in dev_in.items()]
+        s_down.wait_stream(stream)
+        with torch.cuda.stream(s_down):
+            for host, r in results:
+                host.copy_(r, non_blocking=True)
+                r.record_stream(s_down)  # the allocator keeps r until its copy is done
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_run(steps):
+        s_up.wait_stream(stream)
+        upload(0)
+        for k in range(steps):
+            if k + 1 < steps:
+                upload(k + 1)
+            compute_and_download(k)
+        stream.wait_stream(s_down)
+
+    e2e_run(2)
     torch.cuda.synchronize()
     barrier()
     e0.record(stream)
     e2e_steps = max(3, args.steps // 2)
-    for _ in range(e2e_steps):
-        e2e_step()
+    e2e_run(e2e_steps)
     e1.record(stream)
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / e2e_steps
