@@ -12,7 +12,8 @@ divided by the slowest rank's time (weak scaling).
 Prints ONE JSON line (rank 0). `value` is device-timed with inputs resident in HBM (inputs are
 larger than L2, so no flush is needed); `e2e` is the same metric through the public op with
 inputs copied from pinned host memory and o plus all gradients copied back inside the timed
-region; `roofline` is for the dominant kernel, timed live with CUDA events on its stream;
+region, every step, with the copies of neighbouring steps overlapped on their own streams;
+`roofline` is for the dominant kernel, timed live with CUDA events on its stream;
 `cpu_baseline` is the CPU port of the reference op (oracle/gdn.py, the restatement of
 recant.model.ops.gdn_torch + autograd) on a bounded sample, on the host's cores.
 """
@@ -191,7 +192,7 @@ def nvfp4_leg(dev, pk, reps=10):
     torch.cuda.synchronize()
     recs, _ = prof.read()
     del y
-    q_ms = sum(t for n, t in recs if n in ("nvfp4_amax", "nvfp4_quant", "nvfp4_zero")) / reps
+    q_ms = sum(t for n, t in recs if n in ("nvfp4_amax", "nvfp4_quant", "nvfp4_zero", "nvfp4_quant_small")) / reps
     g_ms = sum(t for n, t in recs if n == "nvfp4_gemm") / reps
     gbs = M * K * 2.5625 / (q_ms / 1e3) / 1e9
     tfl = 2.0 * M * Nn * K / (g_ms / 1e3) / 1e12

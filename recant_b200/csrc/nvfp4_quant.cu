@@ -285,6 +285,44 @@ quant_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divide
   }
 }
 
+// Inputs of at most kSmallBlocks blocks (the decode step quantizes one token per sequence): one CTA
+// takes the amax and then quantizes, so the call is one launch instead of three. The same
+// per-block code as the two passes; max is exact in any order, so the result is identical.
+constexpr uint32_t kSmallBlocks = 2048;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+quant_small_kernel(const T* __restrict__ x, uint32_t n_blocks, uint32_t groups, Divider by_groups, int rot,
+                   int stochastic, uint64_t seed, uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+                   uint8_t* __restrict__ blocked, size_t clear_bytes, float* __restrict__ gscale_out) {
+  // zero the blocked scales first (their pads); the scales themselves are written after the barrier
+  for (size_t i = threadIdx.x; i < clear_bytes; i += kThreads) blocked[i] = 0;
+  float m = 0.f;
+  for (uint32_t b = threadIdx.x; b < n_blocks; b += kThreads) {
+    Raw16<T> raw;
+    load_raw(x + size_t(b) * 16, raw);
+    float v[16];
+    unpack16(raw, v);
+    transform16<T>(v, rot != 0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+  }
+  m = warp_max(m);
+  __shared__ float red[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float gm = 0.f;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) gm = fmaxf(gm, red[i]);
+  const float s_g = __fdiv_rn(fmaxf(gm, 1e-30f), 2688.0f);  // 6 * 448
+  if (threadIdx.x == 0) *gscale_out = s_g;
+  for (uint32_t b = threadIdx.x; b < n_blocks; b += kThreads) {
+    Raw16<T> raw;
+    load_raw(x + size_t(b) * 16, raw);
+    quant_block<T>(b, raw, rot, stochastic, seed, s_g, groups, by_groups, codes, scales, blocked);
+  }
+}
+
 // CTAs of kThreads that fit on one SM (the persistent grids are SMs x this).
 template <typename K>
 int resident_ctas(K kernel) {
@@ -332,13 +370,28 @@ extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype
   unsigned int* gmax = static_cast<unsigned int*>(ws);
   const int64_t n_blocks = M * (K / 16);
   const int64_t groups = K / 16;
+  const Divider div = make_divider(uint32_t(groups));
+  // the blocked layout pads rows to 128 and scale columns to 4; the pads must read as zero
+  const bool pads = scales_blocked && (M % 128 != 0 || groups % 4 != 0);
+  const size_t nb = size_t((M + 127) / 128) * size_t((groups + 3) / 4) * 512;
+  if (n_blocks <= int64_t(kSmallBlocks)) {
+    ProfScope ps_("nvfp4_quant_small", s);
+    const size_t clear = pads ? nb : 0;
+    if (dtype == RB2_BF16)
+      quant_small_kernel<__nv_bfloat16><<<1, kThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                               uint32_t(n_blocks), uint32_t(groups), div, use_rht,
+                                                               stochastic, seed, codes, scales, scales_blocked, clear,
+                                                               gscale);
+    else
+      quant_small_kernel<float><<<1, kThreads, 0, s>>>(static_cast<const float*>(x), uint32_t(n_blocks),
+                                                       uint32_t(groups), div, use_rht, stochastic, seed, codes, scales,
+                                                       scales_blocked, clear, gscale);
+    RB2_CHECK_LAUNCH("nvfp4_quantize: small");
+    return RB2_OK;
+  }
   { ProfScope ps_("nvfp4_zero", s); zero_word_kernel<<<1, 1, 0, s>>>(gmax); }
   RB2_CHECK_LAUNCH("nvfp4_quantize: zero");
-  if (scales_blocked && (M % 128 != 0 || groups % 4 != 0)) {
-    const size_t nb = size_t((M + 127) / 128) * size_t((groups + 3) / 4) * 512;
-    RB2_CUDA(cudaMemsetAsync(scales_blocked, 0, nb, s), "nvfp4_quantize: clear blocked pads");
-  }
-  const Divider div = make_divider(uint32_t(groups));
+  if (pads) RB2_CUDA(cudaMemsetAsync(scales_blocked, 0, nb, s), "nvfp4_quantize: clear blocked pads");
   int dev = 0, sms = 148;
   RB2_CUDA(cudaGetDevice(&dev), "nvfp4_quantize: device");
   RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "nvfp4_quantize: SM count");
