@@ -69,9 +69,9 @@ __device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int
 __device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
 
-// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65); `nthr` threads
-// (a multiple of 128). The four 16x16 diagonal blocks by forward substitution (warps 0-3, lane =
-// column) while warps 4-7 zero the blocks above the diagonal; then the off-diagonal blocks by block
+// (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65); `nthr` threads, a
+// multiple of 128 and at least 256. The four 16x16 diagonal blocks by forward substitution (warps
+// 0-3, lane = column) while warps 4-7 zero the blocks above the diagonal; then the off-diagonal blocks by block
 // rows, T_ij = -T_ii X_j with X_j = sum_{j<=m<i} L_im T_mj. Each thread of a block-row step owns a
 // 2x2 tile of one X_j and then of T_ij (a warp: one j, 4 x 8 tiles), so that every shared-memory
 // value it loads feeds two FMAs; every element is still one fma chain in ascending m.
