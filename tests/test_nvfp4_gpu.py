@@ -75,3 +75,28 @@ def test_stochastic_rounding_unbiased_and_neighbouring():
     acc /= 64
     assert np.abs(acc - target).mean() / np.abs(target).mean() < 0.03
     assert len(codes_seen) > 1
+
+
+@pytest.mark.parametrize("shape", [(1, 4096), (3, 48), (8, 4096), (9, 4096), (129, 256)])
+@pytest.mark.parametrize("dtype,rht", [("bf16", True), ("bf16", False), ("f32", True)])
+def test_quantize_single_launch_and_sweep_paths_bit_exact(shape, dtype, rht):
+    """Up to 2048 blocks of 16 take the one-CTA kernel, more take the two sweeps: shapes on both
+    sides of the boundary (8 x 4096 = 2048 blocks, 9 x 4096 = 2304), a decode-sized row, and ragged
+    ones whose blocked scales have pad rows and columns. Rows of exact rounding midpoints are mixed in
+    so that ties take the exact path. The pads must come back zero even over dirty memory."""
+    from recant_b200 import quantize_fast
+    m, k = shape
+    gen = torch.Generator().manual_seed(m * 7 + k)
+    x = torch.randn(m, k, generator=gen) * 2
+    ties = torch.tensor([6.0, 0.75, 1.75, 3.5, 0.25, 1.25, 2.5, 5.0, -0.75, -1.75, -3.5, -5.0, 0.0, -0.0, 3.0, -6.0])
+    x[::2] = ties.repeat(k // 16)[None, :].expand(x[::2].shape) * (1.0 + torch.arange(x[::2].shape[0])[:, None])
+    td = torch.bfloat16 if dtype == "bf16" else torch.float32
+    x = x.to(td)
+    dirty = torch.full((1 << 22,), 255, dtype=torch.uint8, device="cuda")
+    del dirty
+    fp = quantize_fast(x.cuda(), rht, False)
+    c, s, g = ON.quantize_activation(x.float().numpy(), dtype, rht)
+    assert np.array_equal(fp.codes.cpu().numpy(), c)
+    assert np.array_equal(fp.scales.view(torch.uint8).cpu().numpy(), s)
+    assert np.array_equal(fp.blocked.cpu().numpy(), ON.to_blocked(s))
+    assert float(fp.gscale.cpu()) == float(g)
