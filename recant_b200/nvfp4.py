@@ -107,7 +107,7 @@ def gemm_b200(a, b, out_dtype=torch.float32, lora=None, lora_mode=0) -> torch.Te
         raise ValueError("recant_b200.gemm_b200: operands must be CUDA tensors (no CPU path)")
     out = torch.empty(m, n, dtype=out_dtype, device=a.codes.device)
     lib = L.lib()
-    if lora is None and m <= GEMV_MAX_M and k % 32 == 0 and m * (k + k // 8) <= GEMV_MAX_ELEMS:
+    if lora is None and 0 < m <= GEMV_MAX_M and n > 0 and k % 32 == 0 and m * (k + k // 8) <= GEMV_MAX_ELEMS:
         # a few rows of A (the decode step): read B once, one warp per row
         ga = a.gscale.reshape(1).to(torch.float32).contiguous()
         gb = b.gscale.reshape(1).to(torch.float32).contiguous()
