@@ -124,3 +124,17 @@ def test_gdn_fast_path_rejects_misaligned_pointers():
     st = lib.rb2_gdn_fwd(bad, ok, ok, ok, ok, None, None, 1, 64, 1, 1, 1, 128, 128, L.BF16, L.GDN_FAST, 1.0,
                          ok, ok, ok, 1 << 40, None)
     assert st == L.EINVAL and b"aligned" in lib.rb2_last_error()
+
+
+def test_gemv_dispatch_bound_fits_the_kernel_and_larger_shapes_are_refused():
+    """gemm_b200 sends A of at most GEMV_MAX_M rows to rb2_nvfp4_gemv only while A, dequantized with
+    4 floats of padding per 32 (K + K/8 per row), plus the kernel's 272-float lookup tables fit its
+    200 KB of shared memory; the C entry refuses anything larger before touching the device."""
+    from recant_b200 import nvfp4 as N
+    assert 4 * (256 + 16 + N.GEMV_MAX_ELEMS) <= 200 * 1024
+    m, k = N.GEMV_MAX_M, 16384
+    assert m * (k + k // 8) > N.GEMV_MAX_ELEMS          # the dispatch keeps this shape on the tile GEMM
+    lib = L.lib()
+    fake = 1 << 20                                       # never dereferenced: refused before any launch
+    st = lib.rb2_nvfp4_gemv(fake, fake, fake, fake, fake, fake, m, 256, k, fake, L.F32, None)
+    assert st != 0 and "shared memory" in lib.rb2_last_error().decode()
