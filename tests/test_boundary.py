@@ -138,3 +138,42 @@ def test_gemv_dispatch_bound_fits_the_kernel_and_larger_shapes_are_refused():
     fake = 1 << 20                                       # never dereferenced: refused before any launch
     st = lib.rb2_nvfp4_gemv(fake, fake, fake, fake, fake, fake, m, 256, k, fake, L.F32, None)
     assert st != 0 and "shared memory" in lib.rb2_last_error().decode()
+
+
+def test_quantizer_index_tables_follow_from_the_e2m1_grid():
+    """The quantize kernel picks e2m1 indices from packed 4-bit tables keyed by
+    ceil(bits(a) / 2^21): round-to-nearest counts the midpoints strictly below a, stochastic
+    rounding takes the first grid point not below a (at least 1). Rebuild both tables from the grid
+    and the key rule, and check them against the constants in the kernel source."""
+    import struct
+
+    import numpy as np
+    with open(os.path.join(ROOT, "recant_b200", "csrc", "nvfp4_quant.cu")) as f:
+        src = f.read()
+    grid = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+    mids = [(a + b) / 2 for a, b in zip(grid, grid[1:])]
+
+    def bits(x):
+        return struct.unpack("<I", struct.pack("<f", x))[0]
+
+    def key(x):
+        return (bits(x) + 0x1FFFFF) >> 21
+    # every decision point sits on a multiple of 2^21 in the bit pattern, so key order = value order
+    assert all(bits(p) % (1 << 21) == 0 for p in mids + grid[1:])
+    rn = [sum(key(p) < 500 + k for p in mids) for k in range(19)]
+    lo = sum(v << (4 * k) for k, v in enumerate(rn[:16]))
+    hi = sum(v << (4 * (k - 16)) for k, v in enumerate(rn[16:], start=16))
+    assert f"0x{lo:X}ull" in src and f"0x{hi:X}u" in src, (hex(lo), hex(hi))
+    sr = [max(sum(key(p) < 504 + k for p in grid[:7]), 1) for k in range(15)]
+    packed = sum(v << (4 * k) for k, v in enumerate(sr))
+    assert f"0x{packed:X}ull" in src, hex(packed)
+    # and the tables reproduce the reference's rules on every float32 in [0, 6] near a decision point
+    for p in mids + grid:
+        for x in np.nextafter(np.float32(p), np.float32([-1, 7])).tolist() + [p]:
+            a = min(float(np.float32(x)), 6.0)
+            if a < 0:
+                continue
+            k_rn = min(max(key(a), 500), 518) - 500
+            assert rn[k_rn] == sum(a > m for m in mids)
+            k_sr = min(max(key(a), 504), 518) - 504
+            assert sr[k_sr] == max(sum(a > g for g in grid[:7]), 1)
