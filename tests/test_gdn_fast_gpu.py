@@ -93,3 +93,24 @@ def test_fast_backward_varlen():
     h0 = torch.randn(len(lengths), 4, 128, 128, generator=gen) * 0.1
     dht = torch.randn(len(lengths), 4, 128, 128, generator=gen) * 0.1
     _check_grads(inp, do, h0, dht, cu)
+
+
+def test_outputs_fully_written_over_nan_poisoned_memory():
+    """Every element of o, the final state and all input gradients is written by the kernels: the
+    caching allocator's free blocks (small and large pools) are filled with NaN before the op runs,
+    so anything the kernels leave unwritten or read uninitialised shows up as non-finite. Ragged
+    last chunk (T = 130), GQA, an initial state that needs a gradient."""
+    from recant_b200 import gdn_b200
+    poison = [torch.full((n,), float("nan"), device="cuda") for n in [1 << 26] + [1 << 17] * 64 + [1 << 14] * 64]
+    del poison
+    inp = I.gdn_inputs(2, 130, 2, 4, 128, dtype=torch.bfloat16, seed=77)
+    leaves = {n: t.cuda().requires_grad_(True) for n, t in inp.items()}
+    h0 = (torch.randn(2, 4, 128, 128, generator=torch.Generator().manual_seed(78)) * 0.1).cuda().requires_grad_(True)
+    o, hT = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], h0, True, path="fast")
+    do = torch.randn(o.shape, generator=torch.Generator().manual_seed(79)).to(o.dtype).cuda()
+    dhT = torch.randn(hT.shape, generator=torch.Generator().manual_seed(80)).cuda() * 0.1
+    torch.autograd.backward([o, hT], [do, dhT])
+    torch.cuda.synchronize()
+    outs = {"o": o, "hT": hT, "dh0": h0.grad, **{"d" + n: t.grad for n, t in leaves.items()}}
+    for name, t in outs.items():
+        assert t is not None and bool(torch.isfinite(t.float()).all()), name
