@@ -10,11 +10,13 @@
 //                          SR: unbiased choice between the two neighbouring grid points
 //   _pack          :73-74  even element in the low nibble
 //
-// Design (HBM-bound, 2.5625 B/elt algorithmic for bf16): the global amax forces two passes.
+// Design (2.5625 B/elt algorithmic for bf16): the global amax forces two passes.
 // Pass 1 reads x, transforms each 16-block in registers and reduces the amax to one word.
 // Pass 2 re-reads x in REVERSE block order so that the tail of x that pass 1 left in the
 // 126 MB L2 is consumed first, recomputes the transform and writes codes and scales.
-// One thread owns one 16-element block: a warp covers 512 contiguous elements of a row.
+// Both passes are persistent grid-stride sweeps (SMs x resident CTAs): a thread handles one
+// 16-element block at a time (a warp covers 512 contiguous elements) with the next block's load
+// already in flight. Inputs of at most 2048 blocks run both passes in one CTA and one launch.
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
