@@ -15,7 +15,14 @@ inputs copied from pinned host memory and o plus all gradients copied back insid
 region, every step, with the copies of neighbouring steps overlapped on their own streams;
 `roofline` is for the dominant kernel, timed live with CUDA events on its stream;
 `cpu_baseline` is the CPU port of the reference op (oracle/gdn.py, the restatement of
-recant.model.ops.gdn_torch + autograd) on a bounded sample, on the host's cores.
+recant.model.ops.gdn_torch + autograd) on a bounded sample (one of config 1's four sequences, at
+the full T), on the host's cores. Inputs are seeded as the spec states (seed 0; dO seed 1).
+
+The same line also carries `config3` and `config4`: the packed varlen batch data-parallel over the
+N ranks (LPT token balance + NCCL all-reduce of the LoRA-gradient bucket) and the 8-layer
+T = 131072 stack context-parallel over them (affine state hand-off by all_gather), each timed on
+the device (max over ranks) and, for N > 1, with its per-GPU efficiency against the same config
+run on one GPU inside the same job (`--no-extras` skips them).
 """
 from __future__ import annotations
 
@@ -47,11 +54,25 @@ KERNEL_FLOPS_PER_CH = {
 }
 
 
-# DRAM bytes (read + write) per chunk-head of each tensor-core kernel, from the ncu capture in
-# profiles/gdn_fast_kernels_B1T4096_ncu.md (per launch at B1 T4096 / 2048 chunk-heads); traffic scales
-# with the number of chunk-heads
-TRAFFIC_PER_CH = {"gdn_fast_prep": 184.964864e6 / 2048, "gdn_fast_state_fwd": 247.328512e6 / 2048,
-                  "gdn_fast_state_bwd": 218.171904e6 / 2048, "gdn_fast_chunk_bwd": 379.720704e6 / 2048}
+# DRAM traffic of the GDN kernels at the benchmark shape, from the ncu capture summarised in this
+# text file (one line per kernel: dram bytes read / written per launch and the chunk-heads of that
+# launch); traffic scales with the number of chunk-heads
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "gdn_fast_traffic_config1.txt")
+
+
+def traffic_per_ch():
+    """{kernel: DRAM bytes (read + write) per chunk-head} from TRAFFIC_FILE, or {} when absent."""
+    out = {}
+    try:
+        with open(TRAFFIC_FILE) as f:
+            for line in f:
+                t = line.split()
+                if len(t) >= 9 and t[0] == "kernel":
+                    kv = dict(zip(t[2::2], t[3::2]))
+                    out[t[1]] = (float(kv["dram_read_bytes"]) + float(kv["dram_write_bytes"])) / float(kv["chunk_heads"])
+    except (OSError, KeyError, ValueError):
+        return {}
+    return out
 
 
 def peaks():
@@ -121,19 +142,24 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(sm), "source": "NVML, 2 ms polling"}
 
 
-def make_inputs(dev, rank, B, T, Hk, Hv, d):
+def make_inputs(dev, B, T, Hk, Hv, d, seed=0):
+    """The benchmark spec's inputs: one CPU generator seeded with 0, drawn in the order q, k ~ N(0,1)
+    [B,T,Hk,d], v ~ N(0,1) [B,T,Hv,d], beta = sigmoid(N(0,1)), A_log = log U(1,16) per head, a ~ N(0,1),
+    g = -exp(A_log) softplus(a) (fp32); upstream dO ~ N(0,1) from a generator seeded with 1. bf16 on
+    the device."""
     import torch
     import torch.nn.functional as F
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    gen = torch.Generator().manual_seed(seed)
     bf = torch.bfloat16
-    q = torch.randn(B, T, Hk, d, device=dev, generator=gen).to(bf)
-    k = torch.randn(B, T, Hk, d, device=dev, generator=gen).to(bf)
-    v = torch.randn(B, T, Hv, d, device=dev, generator=gen).to(bf)
-    beta = torch.sigmoid(torch.randn(B, T, Hv, device=dev, generator=gen)).to(bf)
-    a_log = torch.log(torch.empty(Hv, device=dev).uniform_(1.0, 16.0, generator=gen))
-    g = (-a_log.exp() * F.softplus(torch.randn(B, T, Hv, device=dev, generator=gen))).float()
-    do = torch.randn(B, T, Hv, d, device=dev, generator=gen).to(bf)
-    return dict(q=q, k=k, v=v, g=g, beta=beta), do
+    q = torch.randn(B, T, Hk, d, generator=gen).to(bf)
+    k = torch.randn(B, T, Hk, d, generator=gen).to(bf)
+    v = torch.randn(B, T, Hv, d, generator=gen).to(bf)
+    beta = torch.sigmoid(torch.randn(B, T, Hv, generator=gen)).to(bf)
+    a_log = torch.log(torch.empty(Hv).uniform_(1.0, 16.0, generator=gen))
+    g = (-a_log.exp() * F.softplus(torch.randn(B, T, Hv, generator=gen))).float()
+    do = torch.randn(B, T, Hv, d, generator=torch.Generator().manual_seed(seed + 1)).to(bf)
+    inp = {n: t.to(dev) for n, t in dict(q=q, k=k, v=v, g=g, beta=beta).items()}
+    return inp, do.to(dev)
 
 
 def config3_lengths(n=64, lo=128, hi=8192, seed=0):
@@ -144,9 +170,86 @@ def config3_lengths(n=64, lo=128, hi=8192, seed=0):
     return torch.randint(lo, hi + 1, (n,), generator=gen).tolist()
 
 
-def cpu_reference_sample(B, T, Hk, Hv, d, reps):
-    """The reference op's CPU path (oracle port of gdn_torch + autograd) on a bounded sample.
-    Returns tokens/s, threads, the sample description and seconds."""
+def measure_config3(rank, world, dev, steps, warmup):
+    """Config 3 on ``world`` ranks (world = 1: the whole pack on this GPU, no collective): the 64
+    packed sequences assigned to ranks by LPT on token count, each rank's varlen GDN forward +
+    backward over its own cu_seqlens pack, then the NCCL all-reduce of the 44 MB fp32 LoRA-gradient
+    bucket. Device time per step, max over ranks; value = all 64 sequences' tokens / that time."""
+    import torch
+    import torch.distributed as dist
+
+    from recant_b200 import gdn_b200
+    from recant_b200 import parallel as P
+    lengths = config3_lengths()
+    parts, loads = P.lpt_partition(lengths, world)
+    mine = [lengths[i] for i in parts[rank]]
+    cu = P.cu_seqlens_of(mine, device=dev)
+    inp, do = make_inputs(dev, 1, sum(mine), CFG["Hk"], CFG["Hv"], CFG["d"])
+    leaves = {n: t.clone().requires_grad_(True) for n, t in inp.items()}
+    bucket = torch.ones(P.lora_bucket_numel(), dtype=torch.float32, device=dev)
+
+    def step():
+        for t in leaves.values():
+            t.grad = None
+        o, _ = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], cu_seqlens=cu)
+        o.backward(do)
+        if world > 1:
+            dist.all_reduce(bucket)
+
+    for _ in range(warmup):
+        step()
+    ms = _timed(step, steps, torch.cuda.current_stream(), world, dev)
+    total = sum(lengths)
+    return {"value": round(total / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3), "n_gpus": world,
+            "tokens": total, "max_rank_tokens": max(loads), "load_imbalance": round(max(loads) * world / total, 4),
+            "parallelism": f"dp{world}", "steps": steps, "warmup": warmup}
+
+
+def multi_gpu_extras(args, rank, world, local, dev):
+    """Configs 3 (data parallel) and 4 (context parallel) on the same ranks as the headline line, with
+    their real collectives, plus, when world > 1, the same configs on rank 0's GPU alone (the others
+    wait at a barrier), so that the line carries the per-GPU efficiency value_N / (N x value_1)."""
+    import torch
+    import torch.distributed as dist
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    steps, warmup = max(3, min(args.steps, 10)), 3
+    out = {}
+    c3 = measure_config3(rank, world, dev, steps, warmup)
+    torch.cuda.empty_cache()
+    barrier()
+    c4 = run_config4(args, rank, world, local, dev, emit=False, steps=max(3, min(args.steps, 5)), warmup=warmup,
+                     with_e2e=False)
+    c4 = {"value": c4["value"], "unit": "tokens/s", "ms_per_step": c4["ms_per_step"], "n_gpus": world,
+          "parallelism": c4["config"]["parallelism"], "workload": c4["config"]["workload"],
+          "steps": c4["steps"], "warmup": c4["warmup"], "phases_ms_per_step_rank0": c4["phases_ms_per_step"]}
+    torch.cuda.empty_cache()
+    barrier()
+    if world > 1:
+        if rank == 0:
+            one3 = measure_config3(0, 1, dev, steps, warmup)
+            torch.cuda.empty_cache()
+            one4 = run_config4(args, 0, 1, local, dev, emit=False, steps=max(3, min(args.steps, 5)), warmup=warmup,
+                               with_e2e=False)
+            torch.cuda.empty_cache()
+            c3["value_1gpu"], c4["value_1gpu"] = one3["value"], one4["value"]
+            c3["efficiency_per_gpu"] = round(c3["value"] / (world * one3["value"]), 4)
+            c4["efficiency_per_gpu"] = round(c4["value"] / (world * one4["value"]), 4)
+        barrier()
+    else:
+        c3["efficiency_per_gpu"] = c4["efficiency_per_gpu"] = 1.0
+    c4["efficiency_target"] = 0.85
+    out["config3"], out["config4"] = c3, c4
+    return out
+
+
+def cpu_reference_runner(B, T, Hk, Hv, d):
+    """The reference op's CPU path (oracle port of gdn_torch + autograd) on a bounded sample: the
+    seeded inputs are made once; the returned callable runs one forward + backward and returns its
+    seconds. Also returns the thread count and the sample description."""
     import torch
 
     from oracle import gdn as OG
@@ -154,15 +257,16 @@ def cpu_reference_sample(B, T, Hk, Hv, d, reps):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     inp = I.gdn_inputs(B, T, Hk, Hv, d, dtype=torch.bfloat16, seed=0)
-    do = I.grad_output(B, T, Hv, d, dtype=torch.bfloat16)
+    do = I.grad_output(B, T, Hv, d, dtype=torch.bfloat16).float()
     f32 = {n: t.float() for n, t in inp.items()}   # the reference upcasts to fp32 (ops.py:25)
     OG.gdn_fwd_bwd(f32["q"][:, :64], f32["k"][:, :64], f32["v"][:, :64], f32["g"][:, :64],
-                   f32["beta"][:, :64], do[:, :64].float())
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        OG.gdn_fwd_bwd(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], do.float())
-    dt = (time.perf_counter() - t0) / reps
-    return B * T / dt, threads, f"B{B} T{T} Hk{Hk} Hv{Hv} d{d} fwd+bwd, fp32 compute, {reps} reps", dt
+                   f32["beta"][:, :64], do[:, :64])
+
+    def run():
+        t0 = time.perf_counter()
+        OG.gdn_fwd_bwd(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], do)
+        return time.perf_counter() - t0
+    return run, threads, f"B{B} T{T} Hk{Hk} Hv{Hv} d{d} fwd+bwd, fp32 compute"
 
 
 def nvfp4_leg(dev, pk, reps=10):
@@ -205,28 +309,36 @@ def nvfp4_leg(dev, pk, reps=10):
                      "peak_source": f"4 x {pk['source']} bf16 burst (MEASURED_PEAKS.json)"}}
 
 
+CONFIG1 = {"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",
+           "global_batch": 4, "seq_len": 4096,
+           "l2": "inputs (q,k,v,dO ~ 470 MB) exceed the 126 MB L2; no flush"}
+# the CPU sample: one of config 1's four independent sequences, at the full T (the reference op's
+# cost per token grows with the number of chunks, so T is kept and only B is sampled)
+CPU_SAMPLE = dict(B=1, T=4096)
+
+
 def reference_arm(args, rank, world):
     """--impl reference: the reference's own CPU implementation of the path (its torch op
-    restated in oracle/gdn.py) timed on the host cores. Rank 0 only."""
+    recant.model.ops.gdn_torch + autograd, restated in oracle/gdn.py) timed on the host cores, with
+    all host threads. Each step is one sequence of config 1 (B1 T4096 Hk16 Hv32), forward +
+    backward; tokens/s is per sequence token. Rank 0 only; the other ranks exit without work."""
     if rank != 0:
         return 0
     c = CFG
-    sample_T = 1024
-    steps = []
-    for i in range(args.warmup + args.steps):
-        tps, threads, sample, dt = cpu_reference_sample(1, sample_T, c["Hk"], c["Hv"], c["d"], 1)
-        if i >= args.warmup:
-            steps.append(dt)
-    dt = statistics.mean(steps)
-    value = sample_T / dt
+    run, threads, _ = cpu_reference_runner(CPU_SAMPLE["B"], CPU_SAMPLE["T"], c["Hk"], c["Hv"], c["d"])
+    for _ in range(args.warmup):
+        run()
+    dt = statistics.mean(run() for _ in range(args.steps))
+    value = CPU_SAMPLE["B"] * CPU_SAMPLE["T"] / dt
+    sample = (f"B{CPU_SAMPLE['B']} T{CPU_SAMPLE['T']} Hk16 Hv32 d128 fwd+bwd per step: one of config 1's four "
+              f"sequences (oracle/gdn.py, the reference's gdn_torch + autograd, fp32 compute)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "config1-sample: GDN fwd+bwd, B1 T1024 Hk16 Hv32 d128 "
-                                        "(a bounded sample of B4 T4096; tokens/s is size-independent for O(T) GDN)"},
+        "data": "synthetic", "config": dict(CONFIG1, global_batch=4 * world, parallelism=f"replicas x{world}", path="auto"),
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"B1 T{sample_T} Hk16 Hv32 d128 fwd+bwd per step (oracle/gdn.py)"},
+                         "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -272,7 +384,7 @@ def comparator_arm(args):
 
     c = CFG
     B, T, Hk, Hv, d = c["B"], c["T"], c["Hk"], c["Hv"], c["d"]
-    inp, do = make_inputs(dev, 0, B, T, Hk, Hv, d)
+    inp, do = make_inputs(dev, B, T, Hk, Hv, d)
     rep = Hv // Hk
     rq, rk = (inp[n].repeat_interleave(rep, dim=2).contiguous() for n in ("q", "k"))
     out = {"impl": "comparators", "config": "config1 B4 T4096 Hk16 Hv32 d128 fwd+bwd; config2 in_proj GEMM",
@@ -592,14 +704,18 @@ def run_config2(args, rank, world, local, dev):
     return 0
 
 
-def run_config4(args, rank, world, local, dev):
+def run_config4(args, rank, world, local, dev, *, emit=True, steps=None, warmup=None, with_e2e=True):
     """Config 4: 8 stacked layers, each a chunked GDN whose values are the previous layer's output
     (v = x viewed as [1, T, Hv, d]) followed by an NVFP4 4096x4096 out_proj, on one sequence of
     131072 tokens split into contiguous shards of T / N tokens (context parallelism). Per layer and
     rank the GDN runs as segmented walks with the affine state hand-off (segments_per_rank
     segments per shard); the ranks exchange their composed state maps with one all_gather in the
     forward and one in the backward. A step is the forward of all layers plus the backward from a
-    synthetic upstream gradient, computing dq, dk, dv, dg, dbeta of every layer and dx of the input."""
+    synthetic upstream gradient, computing dq, dk, dv, dg, dbeta of every layer and dx of the input.
+
+    With ``emit`` the JSON line is printed by rank 0 and the process group is torn down; otherwise
+    the result dict is returned (the multi-GPU extras of the headline line). ``world`` = 1 inside a
+    multi-rank job runs the whole sequence on this GPU alone, with no collective."""
     import torch
     import torch.distributed as dist
 
@@ -608,6 +724,8 @@ def run_config4(args, rank, world, local, dev):
     from recant_b200 import nvfp4 as N
 
     c = C4
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     T, Hk, Hv, d, layers = c["T"], c["Hk"], c["Hv"], c["d"], c["layers"]
     if T % (64 * world):
         raise SystemExit(f"config 4: T={T} does not split into {world} chunk-aligned shards")
@@ -653,14 +771,14 @@ def run_config4(args, rank, world, local, dev):
         clear_grads()
         forward_backward(x_leaf, leaves, dy)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     stream = torch.cuda.current_stream()
     clocks = ClockSampler(local)
     clocks.start()
-    prof = L.LaunchProfiler(capacity=256 * layers * (args.steps + 1))
+    prof = L.LaunchProfiler(capacity=256 * layers * (steps + 1))
     prof.start()
-    ms = _timed(step, args.steps, stream, world, dev)
+    ms = _timed(step, steps, stream, world, dev)
     records, dropped = prof.read()
     clock_info = clocks.stop()
     value = T / (ms / 1e3)
@@ -686,9 +804,11 @@ def run_config4(args, rank, world, local, dev):
         out_host.copy_(out.detach(), non_blocking=True)
         dx_host.copy_(xl.grad, non_blocking=True)
 
-    e2e_step()
-    e2e_steps = max(2, args.steps // 2)
-    ms_e2e = _timed(e2e_step, e2e_steps, stream, world, dev)
+    ms_e2e = None
+    if with_e2e:
+        e2e_step()
+        e2e_steps = max(2, steps // 2)
+        ms_e2e = _timed(e2e_step, e2e_steps, stream, world, dev)
 
     pk = peaks()
     per_kernel = {}
@@ -719,16 +839,16 @@ def run_config4(args, rank, world, local, dev):
     f_gemm = layers * 2 * (2.0 * T * c["hidden"] * c["hidden"])   # fprop + dgrad
     t_roof = f_gdn / (pk["bf16"] * 1e12) + f_gemm / (pk["bf16"] * FP4_PER_BF16 * 1e12)
     line = {
-        "metric": METRIC4, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "metric": METRIC4, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "config4: 8 x (GDN Hk16 Hv32 d128 chunk64 + NVFP4 4096x4096 out_proj) fwd+bwd "
                                "on one sequence, B1 T131072, context-parallel in contiguous shards",
                    "seq_len": T, "layers": layers, "tokens_this_rank": Tr, "segment_len": seg,
                    "parallelism": f"cp{world}", "layer_tokens_per_s": round(value * layers, 1),
                    "l2": "per-rank inputs exceed the 126 MB L2; no flush"},
-        "e2e": {"value": round(T / (ms_e2e / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "e2e": None if ms_e2e is None else {"value": round(T / (ms_e2e / 1e3), 1), "unit": "tokens/s",
+                                            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": roof,
         "path_roofline": {"flops_gdn": f_gdn, "flops_fp4_gemm": f_gemm, "t_roof_ms": round(t_roof * 1e3 / world, 3),
                           "frac": round(t_roof * 1e3 / world / ms, 4),
@@ -737,6 +857,14 @@ def run_config4(args, rank, world, local, dev):
         "kernels": kernels,
         "clocks": clock_info,
     }
+    # where the step goes on this rank: the library's kernels (CUDA events around each launch),
+    # the fold kernels of the hand-off among them, and the rest (NCCL gathers, torch ops, gaps)
+    k_ms = sum(v[1] for v in per_kernel.values()) / steps
+    fold_ms = sum(v[1] for n, v in per_kernel.items() if "fold" in n) / steps
+    line["phases_ms_per_step"] = {"library_kernels": round(k_ms, 3), "of_which_fold": round(fold_ms, 3),
+                                  "other": round(ms - k_ms, 3)}
+    if not emit:
+        return line
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -753,6 +881,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "exact", "fast"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="config 1: skip the configs 3 and 4 keys (their real collectives at the same N)")
     ap.add_argument("--decode", action="store_true",
                     help="time the GDN block's decode step (one token per sequence with a cache) at B = 1 and 64 "
                          "(one JSON line; outside the driver contract)")
@@ -809,7 +939,7 @@ def main():
         cu = P.cu_seqlens_of(mine, device=dev)
         total_tokens = sum(lengths)
         bucket = torch.ones(P.lora_bucket_numel(), dtype=torch.float32, device=dev)
-    inp, do = make_inputs(dev, rank, B, T, Hk, Hv, d)
+    inp, do = make_inputs(dev, B, T, Hk, Hv, d)
     leaves = {n: t.clone().requires_grad_(True) for n, t in inp.items()}
 
     def step():
@@ -936,12 +1066,12 @@ def main():
         avg_s = tot / launches / 1e3
         flops = KERNEL_FLOPS_PER_CH.get(top, 0) * n_ch
         achieved = flops / avg_s / 1e12
-        traffic = TRAFFIC_PER_CH.get(top)
+        traffic = traffic_per_ch().get(top) if args.config == 1 else None
         roof = {"kernel": top, "bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16"],
                 "unit": "TFLOP/s", "frac": round(achieved / pk["bf16"], 4),
                 "traffic": None if traffic is None else round(traffic * n_ch),
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per chunk-head x chunk-heads "
-                                  "(profiles/gdn_fast_kernels_B1T4096_ncu.md)",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at this shape "
+                                  f"({os.path.relpath(TRAFFIC_FILE, ROOT)})" if traffic is not None else None,
                 "dram_gbs_at_traffic": None if traffic is None else round(traffic * n_ch / avg_s / 1e9, 1),
                 "peak_source": f"{pk['source']} bf16 burst (MEASURED_PEAKS.json)",
                 "share_of_kernel_time": round(tot / total_k, 3), "avg_launch_ms": round(avg_s * 1e3, 4)}
@@ -956,9 +1086,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak" if args.config == 1 else "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": ({"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",
-                    "global_batch": B * world, "seq_len": T, "parallelism": f"replicas x{world}",
-                    "path": args.path, "l2": "inputs (q,k,v,dO ~ 470 MB) exceed the 126 MB L2; no flush"}
+        "config": (dict(CONFIG1, global_batch=B * world, seq_len=T, parallelism=f"replicas x{world}", path=args.path)
                    if args.config == 1 else
                    {"workload": "config3: packed varlen GDN fwd+bwd, 64 sequences U[128,8192] (243,613 tokens), "
                                 "Hk16 Hv32 d128, LPT token balance + 44 MB fp32 LoRA-bucket NCCL all-reduce per step",
@@ -978,9 +1106,13 @@ def main():
     if rank == 0 and world == 1 and args.config == 1:
         line["nvfp4"] = nvfp4_leg(dev, pk)
     if rank == 0 and world == 1 and args.config == 1 and not args.no_cpu_baseline:
-        tps, threads, sample, _ = cpu_reference_sample(1, 2048, Hk, Hv, d, 1)
+        run, threads, sample = cpu_reference_runner(CPU_SAMPLE["B"], CPU_SAMPLE["T"], Hk, Hv, d)
+        tps = CPU_SAMPLE["B"] * CPU_SAMPLE["T"] / run()
         line["cpu_baseline"] = {"value": round(tps, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": sample}
+                                "sample": sample + " (one of config 1's four sequences), 1 run"}
+    if args.config == 1 and not args.no_extras and args.batch is None:
+        line.update(multi_gpu_extras(args, rank, world, local, dev))
+        line["extra_keys"] = ["config3", "config4"]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

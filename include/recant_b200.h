@@ -192,9 +192,11 @@ RB2_API int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype, i
  * allocator is frozen, code where a cudaMalloc would synchronise or break a memory cap -- the
  * quantizer's one scratch word (the global |x| maximum) lives in a 256-byte file-scope device
  * array that every GPU loading the library keeps until exit. Same arguments and results as
- * rb2_nvfp4_quantize minus ws/ws_bytes; returns RB2_EWORKSPACE if a size would need more than the
- * 256-byte buffer. The first call on each device looks the buffer's address up (make it before any
- * stream capture). All calls share the buffer and each call clears it first; calls that overlap on
+ * rb2_nvfp4_quantize minus ws/ws_bytes. The scratch is one word for every shape, so no size is
+ * rejected today (RB2_EWORKSPACE stays as a guard should a shape ever need more than the 256-byte
+ * array). The first call on each device, and the first after that device's context is replaced
+ * (e.g. by cudaDeviceReset), looks the array's address up; make that call before any stream
+ * capture. All calls share the array and each call clears the word first; calls that overlap on
  * the GPU (concurrent streams) race on it. Never allocates or frees device memory. */
 RB2_API int rb2_nvfp4_quantize_noalloc(const void* x, int64_t M, int64_t K, int dtype, int use_rht, int stochastic,
                                        uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,

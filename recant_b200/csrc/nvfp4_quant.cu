@@ -455,7 +455,10 @@ extern "C" int rb2_nvfp4_block_scales(const uint8_t* scales, int64_t rows, int64
 // file-scope device array instead. That array exists once per GPU that loads the library and stays
 // allocated until the process exits. Every call shares it: the kernel clears the word at the start
 // of each call, and calls whose kernels overlap on the GPU (two streams at once) race on it.
+// The scratch is one word for every shape, so no size is rejected today; the size check below
+// guards the array's stated maximum should the quantizer ever need more.
 // ------------------------------------------------------------------------------------------------
+#include <cudaTypedefs.h>
 #include <mutex>
 
 namespace rb2 {
@@ -464,12 +467,40 @@ constexpr size_t kQuantStaticScratchBytes = 256;
 __device__ __align__(256) unsigned char g_quant_scratch[kQuantStaticScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchSlot {
+  unsigned long long ctx_id = 0;  // the CUDA context the address belongs to (0: none yet)
+  void* ptr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
 std::mutex g_scratch_mu;
 
-// Device address of g_quant_scratch on the current device. The name g_quant_scratch is only a
-// host-side stand-in in host code, so the address is looked up once per device, with that device
-// current, on the first call that runs there.
+// Unique id of the calling thread's current context (ids are never reused, unlike handles), or 0.
+unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_quant_scratch in the current context. In host code the name g_quant_scratch
+// is only a host-side stand-in, so the address is looked up with cudaGetSymbolAddress on the first
+// call that runs on a device, and again whenever that device's context has changed since (after a
+// cudaDeviceReset the module is loaded anew and the old address is gone).
 int static_scratch(void** out) {
   int dev = 0;
   RB2_CUDA(cudaGetDevice(&dev), "nvfp4_quantize_noalloc: cudaGetDevice");
@@ -477,13 +508,17 @@ int static_scratch(void** out) {
     set_error("nvfp4_quantize_noalloc: device ordinal %d out of range", dev);
     return RB2_EINVAL;
   }
+  const unsigned long long ctx = current_context_id();  // 0 before the thread's first CUDA call
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  ScratchSlot& slot = g_scratch[dev];
+  if (!slot.ptr || ctx == 0 || slot.ctx_id != ctx) {
     void* p = nullptr;
+    // (this also makes the device's primary context current if the thread had none yet)
     RB2_CUDA(cudaGetSymbolAddress(&p, g_quant_scratch), "nvfp4_quantize_noalloc: cudaGetSymbolAddress");
-    g_scratch_ptr[dev] = p;
+    slot.ptr = p;
+    slot.ctx_id = current_context_id();
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return RB2_OK;
 }
 }  // namespace
@@ -493,7 +528,7 @@ extern "C" int rb2_nvfp4_quantize_noalloc(const void* x, int64_t M, int64_t K, i
                                           int stochastic, uint64_t seed, uint8_t* codes, uint8_t* scales,
                                           uint8_t* scales_blocked, float* gscale, void* stream) {
   const size_t need = rb2_nvfp4_quantize_workspace_size(M, K);
-  if (need > rb2::kQuantStaticScratchBytes) {
+  if (need > rb2::kQuantStaticScratchBytes) {  // unreachable today (one word for every shape); a guard
     rb2::set_error("nvfp4_quantize_noalloc: M=%lld K=%lld needs %zu bytes of scratch, more than the %zu-byte static "
                    "buffer; use rb2_nvfp4_quantize with a workspace",
                    (long long)M, (long long)K, need, rb2::kQuantStaticScratchBytes);

@@ -166,9 +166,14 @@ def gdn_b200(q, k, v, g, beta, initial_state=None, output_final_state=False, *, 
              scale=None, path="auto"):
     """GDN on B200 with gdn_torch's contract (recant/model/ops.py:21-54): the chunked op, or for a
     call of at most RECURRENT_MAX_T tokens that needs no gradient (``path="auto"``), or always with
-    ``path="recurrent"``, the token-by-token forward."""
-    if path == "recurrent" or (path == "auto" and q.shape[1] <= RECURRENT_MAX_T
-                               and not _needs_grad(q, k, v, g, beta, initial_state)):
+    ``path="recurrent"``, the token-by-token forward. That kernel builds no autograd graph, so
+    ``path="recurrent"`` on inputs that need a gradient raises ValueError instead of silently
+    returning an output that gradients cannot flow through."""
+    needs_grad = _needs_grad(q, k, v, g, beta, initial_state)
+    if path == "recurrent" and needs_grad:
+        raise ValueError("recant_b200.gdn_b200: path='recurrent' is forward-only and the inputs require grad; "
+                         "use path='auto' or 'fast' for training, or call it under torch.no_grad()")
+    if path == "recurrent" or (path == "auto" and q.shape[1] <= RECURRENT_MAX_T and not needs_grad):
         o, hT = gdn_recurrent(q, k, v, g, beta, initial_state, output_final_state, cu_seqlens=cu_seqlens,
                               scale=scale)
         return o, (hT if output_final_state else None)

@@ -221,8 +221,31 @@ def quantize_activation(x: torch.Tensor, use_rht: bool = True, stochastic: bool 
         return quantize_fast(x.contiguous(), use_rht, stochastic)
 
 
-def register(ref_nvfp4_module, select: bool = False) -> None:
-    """Add ``'b200'`` to the reference's GEMM_BACKENDS and install the fast quantizer hook."""
+def register(ref_nvfp4_module, select: bool = False, quantizer: bool = True) -> None:
+    """Plug this package into the reference's ``recant.model.nvfp4`` module.
+
+    * Adds ``'b200'`` to its ``GEMM_BACKENDS`` (nvfp4.py:125) and, with ``select``, makes it the
+      active backend through ``set_gemm_backend`` (nvfp4.py:128-131).
+    * With ``quantizer`` (the default), installs :func:`quantize_fast` as the fast quantizer hook:
+      the reference's ``quantize_activation`` (nvfp4.py:144-149) calls
+      ``fp4_kernels.quantize_fast(x, use_rht, stochastic)`` from its sibling module once
+      ``_fast['quantize']`` is on, so this sets ``quantize_fast`` on that module (created as a
+      plain module when the Triton one has not been imported, so Triton is never needed) and turns
+      the switch on with ``set_fast_quantizer(True)`` (nvfp4.py:139-142)."""
     ref_nvfp4_module.GEMM_BACKENDS["b200"] = gemm_b200
     if select:
         ref_nvfp4_module.set_gemm_backend("b200")
+    if quantizer:
+        import sys
+        import types
+        pkg_name = ref_nvfp4_module.__name__.rpartition(".")[0]
+        mod_name = (pkg_name + "." if pkg_name else "") + "fp4_kernels"
+        mod = sys.modules.get(mod_name)
+        if mod is None:
+            mod = types.ModuleType(mod_name, "recant_b200 quantizer installed as the fast NVFP4 quantizer hook")
+            sys.modules[mod_name] = mod
+            pkg = sys.modules.get(pkg_name)
+            if pkg is not None:
+                setattr(pkg, "fp4_kernels", mod)
+        mod.quantize_fast = quantize_fast
+        ref_nvfp4_module.set_fast_quantizer(True)

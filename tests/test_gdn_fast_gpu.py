@@ -114,3 +114,21 @@ def test_outputs_fully_written_over_nan_poisoned_memory():
     outs = {"o": o, "hT": hT, "dh0": h0.grad, **{"d" + n: t.grad for n, t in leaves.items()}}
     for name, t in outs.items():
         assert t is not None and bool(torch.isfinite(t.float()).all()), name
+
+
+def test_fast_headline_shape_parity():
+    """One batch row of the benchmark's headline shape: T = 4096 (64 chunks walked per sequence),
+    Hk = 16, Hv = 32 (GQA group 2), bf16 inputs from the benchmark's seeded distributions, forward
+    and backward against the fp32 oracle. The per-chunk bf16 roundings of the state and of the chunk
+    operands compound along the 64-chunk walk; every output and gradient must stay within 2e-2."""
+    inp = I.gdn_inputs(1, 4096, 16, 32, 128, dtype=torch.bfloat16, seed=0)
+    do = I.grad_output(1, 4096, 32, 128, dtype=torch.bfloat16, seed=1)
+    from gpu_util import run_b200
+    f32 = {n: t.float() for n, t in inp.items()}
+    ro, rhT, rg = OG.gdn_fwd_bwd(f32["q"], f32["k"], f32["v"], f32["g"], f32["beta"], do.float())
+    o, hT, gr = run_b200(inp, do, path="fast")
+    errs = {"o": rel(o, ro), "hT": rel(hT, rhT)}
+    errs.update({"d" + n: rel(gr[n], rg[n]) for n in ("q", "k", "v", "g", "beta")})
+    print("headline-shape errors", {k: f"{v:.2e}" for k, v in errs.items()})
+    bad = {k: v for k, v in errs.items() if not v < TOL}
+    assert not bad, (bad, errs)

@@ -161,3 +161,27 @@ def test_gemv_matches_emulated_and_tensor_core_gemm(M, N, K):
         finally:
             N_.GEMV_MAX_M = old
         assert _rel(out.cpu().numpy(), tc_out.cpu().numpy()) < 1e-5
+
+
+def test_gemm_config2_in_proj_shape():
+    """The fused in_proj fprop of the block benchmark at full size: A = Q(rht(x)) for x [16384, 4096]
+    bf16 ~ N(0, 1), B = the fprop copy of a [12288, 4096] weight ~ N(0, 0.02) from quantize_weight
+    (qkv 8192 rows + z 4096 rows). The whole 16384 x 12288 product runs on the GPU (every output tile
+    of the persistent schedule); 256 rows drawn from the first, middle and last row tiles are checked
+    against the emulated GEMM of those rows."""
+    from recant_b200 import gemm_b200, quantize_fast
+    from recant_b200 import nvfp4 as N
+    M, Nn, K = 16384, 12288, 4096
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(M, K, device="cuda", generator=gen).to(torch.bfloat16)
+    W = N.quantize_weight(torch.randn(Nn, K, device="cuda", generator=gen) * 0.02)
+    a = quantize_fast(x, True, False)
+    out = gemm_b200(a, W.fprop)
+    rows = torch.cat([torch.arange(0, 64), torch.arange(M // 2 - 64, M // 2 + 64), torch.arange(M - 64, M)])
+    ac = a.codes[rows.cuda()].cpu().numpy()
+    asc = a.scales.view(torch.uint8)[rows.cuda()].cpu().numpy()
+    ref = ON.gemm_emulated((ac, asc, float(a.gscale.cpu()), (len(rows), K)), _oracle(W.fprop, K))
+    got = out[rows.cuda()].cpu().numpy()
+    assert _rel(got, ref) < TOL, _rel(got, ref)
+    out16 = gemm_b200(a, W.fprop, out_dtype=torch.bfloat16)[rows.cuda()].float().cpu().numpy()
+    assert _rel(out16, ref) < 1e-2

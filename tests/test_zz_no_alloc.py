@@ -21,26 +21,31 @@ def _outputs(m, k, device):
             torch.empty(1, dtype=torch.float32, device=device))
 
 
-def _with_workspace(x, rht, sr, seed):
+_DT = {torch.bfloat16: L.BF16, torch.float32: L.F32}
+
+
+def _with_workspace(x, rht, sr, seed, blocked=True):
     lib = L.lib()
     m, k = x.shape
     c, s, b, g = _outputs(m, k, x.device)
     wsb = lib.rb2_nvfp4_quantize_workspace_size(m, k)
     ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
-    st = lib.rb2_nvfp4_quantize(x.data_ptr(), m, k, L.BF16, rht, sr, seed, c.data_ptr(), s.data_ptr(), b.data_ptr(),
-                                g.data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream)
+    st = lib.rb2_nvfp4_quantize(x.data_ptr(), m, k, _DT[x.dtype], rht, sr, seed, c.data_ptr(), s.data_ptr(),
+                                b.data_ptr() if blocked else None, g.data_ptr(), ws.data_ptr(), wsb,
+                                torch.cuda.current_stream().cuda_stream)
     L.check(st, "nvfp4_quantize")
-    return c, s, b, g
+    return (c, s, b, g) if blocked else (c, s, g)
 
 
-def _no_alloc(x, rht, sr, seed):
+def _no_alloc(x, rht, sr, seed, blocked=True):
     lib = L.lib()
     m, k = x.shape
     c, s, b, g = _outputs(m, k, x.device)
-    st = lib.rb2_nvfp4_quantize_noalloc(x.data_ptr(), m, k, L.BF16, rht, sr, seed, c.data_ptr(), s.data_ptr(),
-                                        b.data_ptr(), g.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    st = lib.rb2_nvfp4_quantize_noalloc(x.data_ptr(), m, k, _DT[x.dtype], rht, sr, seed, c.data_ptr(), s.data_ptr(),
+                                        b.data_ptr() if blocked else None, g.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream)
     L.check(st, "nvfp4_quantize_noalloc")
-    return c, s, b, g
+    return (c, s, b, g) if blocked else (c, s, g)
 
 
 @pytest.mark.parametrize("rht,sr", [(1, 0), (0, 0), (1, 1)])
@@ -53,6 +58,24 @@ def test_noalloc_matches_workspace_entry_point_twice(rht, sr):
         seed = 1234 + call
         ref = _with_workspace(x, rht, sr, seed)
         got = _no_alloc(x, rht, sr, seed)
+        torch.cuda.synchronize()
+        for a, b in zip(ref, got):
+            assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype,shapes,blocked", [
+    (torch.bfloat16, ((8, 2048), (3, 512)), True),      # at most 2048 blocks: the one-CTA path
+    (torch.float32, ((300, 2048), (5, 160)), True),     # f32 input, both paths
+    (torch.bfloat16, ((257, 6144), (130, 64)), False),  # no blocked-scale output
+])
+def test_noalloc_small_f32_and_unblocked_twice(dtype, shapes, blocked):
+    """The same comparison on the single-CTA path (which needs no scratch word), on f32 input and
+    with scales_blocked = NULL; two calls in a row, each bit-exact with the workspace entry point."""
+    gen = torch.Generator().manual_seed(41)
+    for call, (m, k) in enumerate(shapes):
+        x = (torch.randn(m, k, generator=gen) * (4.0 if call == 0 else 0.25)).to(dtype).cuda()
+        ref = _with_workspace(x, 1, 0, 0, blocked)
+        got = _no_alloc(x, 1, 0, 0, blocked)
         torch.cuda.synchronize()
         for a, b in zip(ref, got):
             assert torch.equal(a, b)
