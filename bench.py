@@ -67,7 +67,7 @@ def traffic_per_ch():
         with open(TRAFFIC_FILE) as f:
             for line in f:
                 t = line.split()
-                if len(t) >= 9 and t[0] == "kernel":
+                if len(t) >= 8 and t[0] == "kernel":
                     kv = dict(zip(t[2::2], t[3::2]))
                     out[t[1]] = (float(kv["dram_read_bytes"]) + float(kv["dram_write_bytes"])) / float(kv["chunk_heads"])
     except (OSError, KeyError, ValueError):
