@@ -275,14 +275,31 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   const int q4 = w & 3, hh = w >> 2, r = 32 * q4 + l, c0 = 32 * hh;
   const bool mrow = l < 16;            // this lane holds a row of an M=64 accumulator
   const int i64 = 16 * q4 + l;          // ... and it is token row i64
-  // Work: (chunk, key head) groups, each the p.group value heads that share the key head, walked
-  // group after group by one CTA (grid-strided over groups) so that the group's dq / dk can be summed
-  // in this CTA's slice of the scratch; item = chunk * Hv + value head.
-  const int64_t n_groups = int64_t(*ws.ct.n_chunks) * p.Hk;
-  auto seq_item = [&](int64_t k) -> int64_t {  // this CTA's k-th item, or -1
-    const int64_t G = int64_t(blockIdx.x) + (k / p.group) * gridDim.x;
-    if (G >= n_groups) return -1;
-    return (G / p.Hk) * p.Hv + (G % p.Hk) * p.group + k % p.group;
+  // Work: (chunk, key head) groups G = chunk * Hk + key head, each the p.group value heads that share
+  // the key head, walked group after group by one CTA (grid-strided over groups) so that the group's
+  // dq / dk can be summed in this CTA's slice of the scratch. An item is one (chunk, value head); the
+  // sequence is advanced incrementally in 32-bit arithmetic (one division per group).
+  const int n_groups = *ws.ct.n_chunks * p.Hk;
+  struct Item {
+    int G, gi, ci, hk, h;  // group, index in the group, chunk, key head, value head
+  };
+  auto group_item = [&](int G) {
+    Item x;
+    x.G = G;
+    x.gi = 0;
+    x.ci = G / p.Hk;
+    x.hk = G - x.ci * p.Hk;
+    x.h = x.hk * p.group;
+    return x;
+  };
+  auto next_item = [&](const Item& x) {
+    if (x.gi + 1 < p.group) {
+      Item y = x;
+      ++y.gi;
+      ++y.h;
+      return y;
+    }
+    return group_item(x.G + int(gridDim.x));
   };
 
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
@@ -294,9 +311,9 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   // Phase-1 tiles of one (chunk, head) other than [K;Q], issued by thread 0 on ldbar[0]: the
   // workspace images and the per-token stats by bulk copy and the caller's v, dO rows by TMA (rows
   // past the sequence are zeroed after the wait).
-  auto issue_phase1 = [&](int64_t item) {
+  auto issue_phase1 = [&](const Item& x) {
     if (tid != 0) return;
-    const int ci_ = int(item / p.Hv), h_ = int(item % p.Hv);
+    const int ci_ = x.ci, h_ = x.h;
     const int64_t ch_ = int64_t(ci_) * p.Hv + h_;
     const int t0_ = ws.ct.tok0[ci_];
     tc::fence_proxy_async();
@@ -312,41 +329,40 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   // [K;Q] rows of one (chunk, key head) by TMA on ldbar[2]. The value heads of a group share them,
   // so they are fetched only when the (chunk, key head) changes, during the previous item's final
   // epilogue once its reads of the region are done.
-  auto issue_kq = [&](int64_t item) {
+  auto issue_kq = [&](const Item& x) {
     if (tid != 0) return;
-    const int ci_ = int(item / p.Hv), hk_ = int(item % p.Hv) / p.group;
+    const int ci_ = x.ci, hk_ = x.hk;
     const int t0_ = ws.ct.tok0[ci_];
     tc::fence_proxy_async();
     tc::mbar_expect_tx(&ldbar[2], 32768);
     tc::tma_rows128(sm + lay::KQ, 16384, 0, &map_k, hk_, t0_, &ldbar[2]);
     tc::tma_rows128(sm + lay::KQ, 16384, 64, &map_q, hk_, t0_, &ldbar[2]);
   };
-  // items a and b read the same [K;Q] rows
-  auto same_kq = [&](int64_t a, int64_t b) { return a / p.Hv == b / p.Hv && (a % p.Hv) / p.group == (b % p.Hv) / p.group; };
   tc::fence_before_sync();
   __syncthreads();  // barrier init and the TMEM address visible
   tc::fence_after_sync();
-  if (seq_item(0) >= 0) {
-    issue_phase1(seq_item(0));
-    issue_kq(seq_item(0));
+  Item cur = group_item(int(blockIdx.x));
+  if (cur.G < n_groups) {
+    issue_phase1(cur);
+    issue_kq(cur);
   }
   uint32_t kq_ph = 0;     // parity of the next [K;Q] load to wait for
-  int64_t prev_item = -1;
+  int prev_G = -1;        // the group whose [K;Q] rows are in shared memory
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
-  for (int64_t it = 0;; ++it) {
-  const int64_t item = seq_item(it);
-  if (item < 0) break;
-  const uint32_t ph = uint32_t(it & 1);  // parity of the barriers that complete once per item
-  const int ci = int(item / p.Hv), h = int(item % p.Hv);
-  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
+  for (uint32_t it = 0; cur.G < n_groups; ++it, cur = next_item(cur)) {
+  const Item nxt = next_item(cur);
+  const bool has_next = nxt.G < n_groups;
+  const uint32_t ph = it & 1u;  // parity of the barriers that complete once per item
+  const int ci = cur.ci, h = cur.h, hk = cur.hk;
+  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
   const int64_t ch = int64_t(ci) * p.Hv + h;
-  if (prev_item < 0 || !same_kq(prev_item, item)) {  // issued at the start or by the previous item
+  if (prev_G != cur.G) {  // issued at the start or by the previous item
     tc::mbar_wait(&ldbar[2], kq_ph, ws.err, 137);
     kq_ph ^= 1u;
   }
-  prev_item = item;
+  prev_G = cur.G;
   tc::mbar_wait(&ldbar[0], ph, ws.err, 130);
   if (tid < 64) {
     const float* st = reinterpret_cast<const float*>(sm + lay::STATS);
@@ -583,7 +599,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::mbar_wait(&bar[4], ph, ws.err, 135);
   tc::fence_after_sync();
   __syncthreads();  // region A (the phase-2 tiles) is free once G5 has completed
-  if (seq_item(it + 1) >= 0) issue_phase1(seq_item(it + 1));  // next item's tiles, behind this epilogue
+  if (has_next) issue_phase1(nxt);  // next item's tiles, behind this epilogue
   // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j; q[i][r], k[i][r] read from the
   // [K;Q] tile (consecutive lanes read consecutive columns of one row: no bank conflicts) -----------
   float xr[32];
@@ -632,8 +648,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   __syncthreads();  // every thread holds its q and k rows (xr, kr_): [K;Q] may be refilled
   {
-    const int64_t next = seq_item(it + 1);
-    if (next >= 0 && !same_kq(item, next)) issue_kq(next);
+    if (has_next && nxt.G != cur.G) issue_kq(nxt);
   }
   if (tid < 64) {  // combine the four lane quarters
 #pragma unroll
@@ -745,6 +760,8 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
       RB2_CUDA(cudaGetDevice(&dev), "gdn fast chunk bwd: device");
       RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "gdn fast chunk bwd: SM count");
       const int64_t items = int64_t(p.max_chunks) * p.Hk;  // (chunk, key head) groups
+      RB2_CHECK_ARG(items + sms < (int64_t(1) << 31), "gdn fast chunk bwd: %lld (chunk, key head) groups exceed 2^31",
+                    (long long)items);
       CUtensorMap mq, mk, mv, mdo;
       if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk)) ||
           (rc = make_rows_map(&mv, p.v, p.tokens, p.Hv)) || (rc = make_rows_map(&mdo, d_o, p.tokens, p.Hv)))
