@@ -46,10 +46,8 @@ size_t carve_fast_scratch(Carver& c, FastWs& w, int64_t tokens, int Hv, int max_
   const size_t nch = size_t(max_chunks) * Hv;
   w.dh = c.take<__nv_bfloat16>(nch * 16384);
   w.dvp = c.take<__nv_bfloat16>(nch * 8192);
-  // GQA: one [64][128] fp32 slice per chunk-backward CTA (at most one CTA per SM; 1024 covers any GPU)
-  const size_t slices = gqa ? size_t(std::min<int64_t>(nch, 1024)) : 0;
-  w.dqh = c.take<float>(slices * 8192);
-  w.dkh = c.take<float>(slices * 8192);
+  (void)tokens;
+  (void)gqa;  // the GQA group sums of dq / dk stay in the chunk backward's tensor memory
   return c.bytes();
 }
 

@@ -19,14 +19,12 @@ struct FastWs {
   __nv_bfloat16* vp;     // [ch][128][64]  V'^T [dv][tok] (tile image)
   __nv_bfloat16* dh;     // [ch][128][128] dS^T of the state leaving the chunk, [dv][dk] (image)
   __nv_bfloat16* dvp;    // [ch][128][64]  dV'^T [dv][tok] (tile image)
-  float* dqh;            // [tokens][Hv][128] per-value-head dq (GQA only)
-  float* dkh;            // [tokens][Hv][128]
   int* err;              // device status word
 };
 
 // The workspace has two parts: "saved" (written by the forward, read by the backward: chunk table,
-// status word, per-chunk prep outputs, states and V') and "scratch" (backward only: dS, dV' and the
-// per-value-head dq / dk of GQA), which the caller may pass separately and reuse across layers.
+// status word, per-chunk prep outputs, states and V') and "scratch" (backward only: dS and dV'),
+// which the caller may pass separately and reuse across layers.
 size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_chunks);
 size_t carve_fast_scratch(Carver& c, FastWs& w, int64_t tokens, int Hv, int max_chunks, bool gqa);
 

@@ -215,6 +215,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
 // chunk backward: one CTA (256 threads) per (chunk, value head). Thread (w, l): TMEM lane quarter
 // q = w & 3, lane r = 32 q + l (head-dim row of an M=128 accumulator; for M=64 accumulators lanes
 // l < 16 hold token rows 16 q + l), column half hh = w >> 2 (columns [32 hh, 32 hh + 32)).
+// TMEM columns (64-column blocks): G1 writes [K;Q]K^T 0, dq~^T 64, dW^T 128, dk~^T 192, dA_qk 256;
+// E1 frees 0, 128, 256; G2 writes dT 320, dBv^T 128, dBk^T 256; G3 Y 0; G4 dL' 128; G5 320 and 0.
+// Columns [384, 512) are never written by an MMA: they carry the GQA group's running dq / dk sums
+// (fp32) from one value head of the group to the next.
 // ------------------------------------------------------------------------------------------------
 namespace lay {  // shared-memory map (bytes from the 1024-aligned base)
 constexpr int KQ = 0, VT = 32768, DVP = 49152;
@@ -478,9 +482,9 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     const uint32_t id_bv = tc::idesc_bf16(128, 64, false, true), id_bk = tc::idesc_bf16(128, 64, false, true);
 #pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16) {
-      tc::mma_bf16(tbase + 384, tc::desc_kmajor_sw128(dva + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bv,
+      tc::mma_bf16(tbase + 128, tc::desc_kmajor_sw128(dva + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bv,
                    k0 > 0);
-      tc::mma_bf16(tbase + 448, tc::desc_kmajor_sw128(dwa + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bk,
+      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(dwa + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bk,
                    k0 > 0);
     }
     tc::mma_commit(&bar[1]);
@@ -496,7 +500,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       for (int j = 0; j < 32; ++j) v[j] = c0 + j <= i64 ? v[j] : 0.f;
       store_row32(sm + lay::DTT, 64, i64, c0, v);
     }
-    tmem_ld32f(lane_addr + 384, v);  // dBv^T row dv = r, columns m = c0 + j
+    tmem_ld32f(lane_addr + 128, v);  // dBv^T row dv = r, columns m = c0 + j
     float x[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -535,7 +539,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     const uint32_t id_l = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16)
-      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
+      tc::mma_bf16(tbase + 128, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
     tc::mma_commit(&bar[3]);
   }
   tc::mbar_wait(&bar[3], ph, ws.err, 134);
@@ -545,7 +549,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   {
     const int i = r & 63, cb = c0 + 16 * (q4 >> 1);
     float v[16];
-    tc::tmem_ld16(tbase + (uint32_t(32 * q4) << 16) + 256 + cb, v);
+    tc::tmem_ld16(tbase + (uint32_t(32 * q4) << 16) + 128 + cb, v);
     const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
     float db = 0.f;
     float pb1[16], qb1[16], pb2[16], qb2[16];
@@ -632,7 +636,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     float t2[32], t3[32];
     tmem_ld32f(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
     tmem_ld32f(lane_addr + 192, t2);   // dk~^T
-    tmem_ld32f(lane_addr + 448, t3);   // dBk^T
+    tmem_ld32f(lane_addr + 256, t3);   // dBk^T
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int i = c0 + j;
@@ -668,23 +672,19 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       gk[j] = rki * dkh[j] - kr_[j] * rki * rki * rki * red5[i];
     }
     bool last = true;  // this value head completes dq / dk of its key head
-    if (p.group > 1) {  // GQA: the group's sum, in fp32 in this CTA's scratch slice until its last value head
-      float* pq = ws.dqh + size_t(blockIdx.x) * 8192;  // [64 tokens][128], written and read by this thread
-      float* pk = ws.dkh + size_t(blockIdx.x) * 8192;
-      const int g = h % p.group;
-      if (g > 0) {
+    if (p.group > 1) {  // GQA: the group's running sum in fp32, kept in TMEM columns [384, 512) until its last value head
+      if (cur.gi > 0) {
+        float pq[32];
+        tmem_ld32f(lane_addr + 384, pq);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          gq[j] = pq[(c0 + j) * 128 + r] + gq[j];
-          gk[j] = pk[(c0 + j) * 128 + r] + gk[j];
-        }
+        for (int j = 0; j < 32; ++j) gq[j] += pq[j];
+        tmem_ld32f(lane_addr + 448, pq);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) gk[j] += pq[j];
       }
-      if (g + 1 < p.group) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          pq[(c0 + j) * 128 + r] = gq[j];
-          pk[(c0 + j) * 128 + r] = gk[j];
-        }
+      if (cur.gi + 1 < p.group) {
+        tc::tmem_st32(lane_addr + 384, gq);
+        tc::tmem_st32(lane_addr + 448, gk);
         last = false;
       }
     }
