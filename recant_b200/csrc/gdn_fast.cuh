@@ -158,6 +158,25 @@ __device__ __forceinline__ void store_row16(unsigned char* tile, int rows, int r
   }
 }
 
+// 8 values of row r starting at element e0 (a multiple of 8) of a K-major SW128 tile -> bf16
+__device__ __forceinline__ void store_row8(unsigned char* tile, int rows, int r, int e0, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0, rows)) =
+      make_uint4(tc::pack_bf16(v[0], v[1]), tc::pack_bf16(v[2], v[3]), tc::pack_bf16(v[4], v[5]), tc::pack_bf16(v[6], v[7]));
+}
+
+// store_cols32 for 16 tokens (t_base + j, j < 16)
+__device__ __forceinline__ void store_cols16(bf16* dst, int row, int r, int t_base, int L, const float (&v)[16]) {
+  const bool odd = (r & 1) != 0;
+  const int t_odd = t_base + (odd ? 1 : 0);
+  uint32_t* base = reinterpret_cast<uint32_t*>(dst + t_odd * row + (r & ~1));
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
+    if (t_odd + j < L) base[(j * row) >> 1] = tc::pack_bf16(lo, hi);
+  }
+}
+
 // Write 32 per-token values of head-dim column r (tokens 32 hh + j) as bf16 to dst[(tok) * row + r],
 // pairing lanes r, r^1 so that every store is one 4-byte bf16x2.
 // `row` elements between tokens; the 64 tokens of a chunk span less than 2^31 elements.
@@ -184,6 +203,16 @@ __device__ __forceinline__ void stage_cols32(bf16* tile, int r, int t_base, cons
   const bool odd = (r & 1) != 0;
 #pragma unroll
   for (int j = 0; j < 32; j += 2) {
+    const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+    const int tk = t_base + j + (odd ? 1 : 0);
+    const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;
+    *reinterpret_cast<uint32_t*>(tile + tk * 128 + (r & ~1)) = tc::pack_bf16(lo, hi);
+  }
+}
+__device__ __forceinline__ void stage_cols16(bf16* tile, int r, int t_base, const float (&v)[16]) {
+  const bool odd = (r & 1) != 0;
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
     const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
     const int tk = t_base + j + (odd ? 1 : 0);
     const float lo = odd ? other : v[j], hi = odd ? v[j + 1] : other;

@@ -212,9 +212,11 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
 }
 
 // ------------------------------------------------------------------------------------------------
-// chunk backward: one CTA (256 threads) per (chunk, value head). Thread (w, l): TMEM lane quarter
-// q = w & 3, lane r = 32 q + l (head-dim row of an M=128 accumulator; for M=64 accumulators lanes
-// l < 16 hold token rows 16 q + l), column half hh = w >> 2 (columns [32 hh, 32 hh + 32)).
+// chunk backward: persistent, one CTA of 512 threads (16 warps) per SM. Thread (w, l): TMEM lane
+// quarter q = w & 3, lane r = 32 q + l (head-dim row of an M=128 accumulator; for M=64 accumulators
+// lanes l < 16 hold token rows 16 q + l), column quarter cq = w >> 2 (columns [16 cq, 16 cq + 16)).
+// Sixteen warps (four per scheduler) hide the latency of the epilogues' shared-memory and TMEM
+// traffic; each thread holds 16 columns of an accumulator row, so 128 registers suffice.
 // TMEM columns (64-column blocks): G1 writes [K;Q]K^T 0, dq~^T 64, dW^T 128, dk~^T 192, dA_qk 256;
 // E1 frees 0, 128, 256; G2 writes dT 320, dBv^T 128, dBk^T 256; G3 Y 0; G4 dL' 128; G5 320 and 0.
 // Columns [384, 512) are never written by an MMA: they carry the GQA group's running dq / dk sums
@@ -228,12 +230,13 @@ constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  /
 constexpr int QB2 = VT;                                                        // over V once consumed
 constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 is issued
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
-constexpr int VEC = DAQF + 16640;                                              // 14 x 64 floats
-constexpr int RED = VEC + 14 * 256;                                            // 5 x 4 x 64 floats
+constexpr int VEC = DAQF + 16640;                                              // 18 x 64 floats
+constexpr int RED = VEC + 18 * 256;                                            // 16 + 5 x 4 x 64 floats
 constexpr int STATS = RED + 5 * 1024 + 64;  // the next item's per-token stats, fp32 [4][64], by bulk copy
 constexpr int END = STATS + 1024;
 }  // namespace lay
 constexpr int kBChunkSmem = lay::END + 1024;
+constexpr int kBThreads = 512;
 
 // Sum v[0..31] over the 32 lanes; afterwards lane l holds the total of column l.
 __device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
@@ -252,9 +255,26 @@ __device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
   return v[0];
 }
 
-__device__ __forceinline__ void tmem_ld32f(uint32_t addr, float (&v)[32]) { tc::tmem_ld32(addr, v); }
+// Sum v[0..15] over the 32 lanes; afterwards lanes 2c and 2c + 1 hold the total of column c.
+__device__ __forceinline__ float warp_colsum16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int step = 0; step < 4; ++step) {
+    const int s = 16 >> step, c = 16 >> step;
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < c / 2; ++j) {
+      const float send = up ? v[j] : v[j + c / 2];
+      const float keep = up ? v[j + c / 2] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
 
-__global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
+__device__ __forceinline__ void tmem_ld16f(uint32_t addr, float (&v)[16]) { tc::tmem_ld16(addr, v); }
+
+__global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  bf16* __restrict__ dq, bf16* __restrict__ dk,
                                                                  bf16* __restrict__ dv, float* __restrict__ dg,
                                                                  bf16* __restrict__ dbeta,
@@ -269,14 +289,14 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   float* daqf = reinterpret_cast<float*>(sm + lay::DAQF);
   float* vec = reinterpret_cast<float*>(sm + lay::VEC);
   float *cum = vec, *rq = vec + 64, *rk = vec + 128, *beta = vec + 192, *ecum = vec + 256, *edec = vec + 320,
-        *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [4][64] */, *scal = vec + 768;
-  float* red = reinterpret_cast<float*>(sm + lay::RED);  // [5][4][64]
+        *dbeta_acc = vec + 384, *dcum_acc = vec + 448, *dbp = vec + 512 /* [8][64] */, *scal = vec + 1024;
+  float* red = reinterpret_cast<float*>(sm + lay::RED);  // [5][4][64]; the first 16 also per-warp partials
   __shared__ uint64_t bar[5];
   __shared__ uint64_t ldbar[3];   // loads: phase-1 tiles and stats (bulk + TMA), T, [K;Q] (TMA)
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
-  const int q4 = w & 3, hh = w >> 2, r = 32 * q4 + l, c0 = 32 * hh;
+  const int q4 = w & 3, cq = w >> 2, r = 32 * q4 + l, c0 = 16 * cq;
   const bool mrow = l < 16;            // this lane holds a row of an M=64 accumulator
   const int i64 = 16 * q4 + l;          // ... and it is token row i64
   // Work: (chunk, key head) groups G = chunk * Hk + key head, each the p.group value heads that share
@@ -353,7 +373,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   uint32_t kq_ph = 0;     // parity of the next [K;Q] load to wait for
   int prev_G = -1;        // the group whose [K;Q] rows are in shared memory
   const uint32_t tbase = tmem_base;
-  const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column half
+  const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column quarter
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
   for (uint32_t it = 0; cur.G < n_groups; ++it, cur = next_item(cur)) {
   const Item nxt = next_item(cur);
@@ -377,10 +397,10 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     dcum_acc[tid] = 0.f;
   }
   if (L < 64) {  // rows past the end of the sequence: zero (TMA fills only past the tensor's end)
-    tc::zero_rows_tail(sm + lay::KQ, 16384, 0, L, 256);
-    tc::zero_rows_tail(sm + lay::KQ, 16384, 64, L, 256);
-    tc::zero_rows_tail(sm + lay::VT, 8192, 0, L, 256);
-    tc::zero_rows_tail(sm + lay::DOT, 8192, 0, L, 256);
+    tc::zero_rows_tail(sm + lay::KQ, 16384, 0, L, kBThreads);
+    tc::zero_rows_tail(sm + lay::KQ, 16384, 64, L, kBThreads);
+    tc::zero_rows_tail(sm + lay::VT, 8192, 0, L, kBThreads);
+    tc::zero_rows_tail(sm + lay::DOT, 8192, 0, L, kBThreads);
   }
   sync_for_mma();
   if (tid == 0) {  // ---- G1 ----
@@ -408,7 +428,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   {  // dgamma = sum S^T * dS^T while G1 runs (both tiles share one layout); warp 0 issues G1
     float part = 0.f;
-    for (int idx = tid - 32; w > 0 && idx < 128 * 16; idx += 224) {
+    for (int idx = tid - 32; w > 0 && idx < 128 * 16; idx += kBThreads - 32) {
       const uint32_t off = uint32_t(idx) * 16;
       const uint4 a = *reinterpret_cast<const uint4*>(sm + lay::ST + off);
       const uint4 b = *reinterpret_cast<const uint4*>(sm + lay::DHT + off);
@@ -422,7 +442,7 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   __syncthreads();
   if (tid == 0) {
     float t = 0.f;
-    for (int i = 0; i < 8; ++i) t += red[i];
+    for (int i = 0; i < kBThreads / 32; ++i) t += red[i];
     scal[0] = t;
   }
   tc::mbar_wait(&bar[0], ph, ws.err, 131);
@@ -434,20 +454,20 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   // ---- E1 ------------------------------------------------------------------------------------
   {
-    float v[32];
-    tmem_ld32f(lane_addr + 0, v);  // lanes 0-63: kk rows, 64-127: qk rows
+    float v[16];
+    tmem_ld16f(lane_addr + 0, v);  // lanes 0-63: kk rows, 64-127: qk rows
     float* dstf = r < 64 ? kkf + r * 65 + c0 : qkf + (r - 64) * 65 + c0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) dstf[j] = v[j];
-    tmem_ld32f(lane_addr + 128, v);  // dW^T row dk = r
-    store_row32(sm + lay::DWT, 128, r, c0, v);
-    tmem_ld32f(lane_addr + 256, v);  // dA_qk (M = 64)
+    for (int j = 0; j < 16; ++j) dstf[j] = v[j];
+    tmem_ld16f(lane_addr + 128, v);  // dW^T row dk = r
+    store_row16(sm + lay::DWT, 128, r, c0, v);
+    tmem_ld16f(lane_addr + 256, v);  // dA_qk (M = 64)
     if (mrow) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) daqf[i64 * 65 + c0 + j] = c0 + j <= i64 ? v[j] : 0.f;
+      for (int j = 0; j < 16; ++j) daqf[i64 * 65 + c0 + j] = c0 + j <= i64 ? v[j] : 0.f;
     }
   }
-  for (int idx = tid; idx < 64 * 16; idx += 256) {  // beta V and beta e^cum rk K (rows m)
+  for (int idx = tid; idx < 64 * 16; idx += kBThreads) {  // beta V and beta e^cum rk K (rows m)
     const int m = idx >> 4, c8 = (idx & 15) * 8;
     const uint4 xv = *reinterpret_cast<const uint4*>(sm + lay::VT + tc::sw128_offset(m, c8, 64));
     const uint4 xk = *reinterpret_cast<const uint4*>(sm + lay::KQ + tc::sw128_offset(m, c8, 128));
@@ -493,23 +513,24 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::fence_after_sync();
   // ---- E2 ------------------------------------------------------------------------------------
   {
-    float v[32];
-    tmem_ld32f(lane_addr + 320, v);  // dT (M = 64)
+    float v[16];
+    tmem_ld16f(lane_addr + 320, v);  // dT (M = 64)
     if (mrow) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = c0 + j <= i64 ? v[j] : 0.f;
-      store_row32(sm + lay::DTT, 64, i64, c0, v);
+      for (int j = 0; j < 16; ++j) v[j] = c0 + j <= i64 ? v[j] : 0.f;
+      store_row16(sm + lay::DTT, 64, i64, c0, v);
     }
-    tmem_ld32f(lane_addr + 128, v);  // dBv^T row dv = r, columns m = c0 + j
-    float x[32];
+    tmem_ld16f(lane_addr + 128, v);  // dBv^T row dv = r, columns m = c0 + j
+    float x[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       x[j] = beta[c0 + j] * v[j];
       v[j] *= tile_elem(sm + lay::VT, 64, c0 + j, r);
     }
     // dv rows are staged over dW^T (dead after G2) and written out after the last proxy fence
-    stage_cols32(reinterpret_cast<bf16*>(sm + lay::DVS), r, c0, x);
-    red[q4 * 64 + c0 + l] = warp_colsum32(v);
+    stage_cols16(reinterpret_cast<bf16*>(sm + lay::DVS), r, c0, x);
+    const float cs = warp_colsum16(v);
+    if ((l & 1) == 0) red[q4 * 64 + c0 + (l >> 1)] = cs;
   }
   __syncthreads();
   if (tid < 64) dbeta_acc[tid] += red[tid] + red[64 + tid] + red[128 + tid] + red[192 + tid];
@@ -526,11 +547,11 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::mbar_wait(&bar[2], ph, ws.err, 133);
   tc::fence_after_sync();
   {
-    float v[32];
-    tmem_ld32f(lane_addr + 0, v);
+    float v[16];
+    tmem_ld16f(lane_addr + 0, v);
     if (mrow) {  // [Y; Y]: G4 runs with M = 128 so that E4 has a row in every lane
-      store_row32(sm + lay::YT, 128, i64, c0, v);
-      store_row32(sm + lay::YT, 128, 64 + i64, c0, v);
+      store_row16(sm + lay::YT, 128, i64, c0, v);
+      store_row16(sm + lay::YT, 128, 64 + i64, c0, v);
     }
   }
   sync_for_mma();
@@ -545,16 +566,16 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   tc::mbar_wait(&bar[3], ph, ws.err, 134);
   tc::fence_after_sync();
   // ---- E4: P, Qm, R and the B operands of G5. dL' is an M = 128 accumulator of [Y; Y] T^T, so
-  // lane 32 q4 + l holds token row i = (32 q4 + l) & 63; the thread takes 16 columns, cb..cb+15.
+  // lane 32 q4 + l holds token row i = (32 q4 + l) & 63; the thread takes 8 columns, cb..cb+7.
   {
-    const int i = r & 63, cb = c0 + 16 * (q4 >> 1);
-    float v[16];
-    tc::tmem_ld16(tbase + (uint32_t(32 * q4) << 16) + 128 + cb, v);
+    const int i = r & 63, cb = c0 + 8 * (q4 >> 1);
+    float v[8];
+    tc::tmem_ld8(tbase + (uint32_t(32 * q4) << 16) + 128 + cb, v);
     const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
     float db = 0.f;
-    float pb1[16], qb1[16], pb2[16], qb2[16];
+    float pb1[8], qb1[8], pb2[8], qb2[8];
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
+    for (int jj = 0; jj < 8; ++jj) {
       const int j = cb + jj;
       const float gam = j <= i ? __expf(ci_ - cum[j]) : 0.f;
       const float P = j < i ? -v[jj] * gam : 0.f;
@@ -569,15 +590,16 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
       pb2[jj] = bi * rki * P;
       qb2[jj] = sqi * qm;
     }
-    dbp[(2 * hh + (q4 >> 1)) * 64 + i] = db;
-    store_row16(sm + lay::PB1, 64, i, cb, pb1);
-    store_row16(sm + lay::QB1, 64, i, cb, qb1);
-    store_row16(sm + lay::PB2, 64, i, cb, pb2);
-    store_row16(sm + lay::QB2, 64, i, cb, qb2);
+    dbp[(2 * cq + (q4 >> 1)) * 64 + i] = db;
+    store_row8(sm + lay::PB1, 64, i, cb, pb1);
+    store_row8(sm + lay::QB1, 64, i, cb, qb1);
+    store_row8(sm + lay::PB2, 64, i, cb, pb2);
+    store_row8(sm + lay::QB2, 64, i, cb, qb2);
   }
   sync_for_mma();
-  // dv rows of the chunk: coalesced 16-byte stores by warps 4-7 while G5 runs
-  copy_rows_out(dv + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 256, sm + lay::DVS, 256, L, 128, 128);
+  // dv rows of the chunk: coalesced 16-byte stores by warps 8-15 while G5 runs
+  copy_rows_out(dv + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 256, sm + lay::DVS, 256, L, kBThreads / 2,
+                kBThreads / 2);
   if (tid == 0) {  // ---- G5 ----
     const uint32_t p1 = tc::smem_u32(sm + lay::PB1), p2 = tc::smem_u32(sm + lay::PB2), q1 = tc::smem_u32(sm + lay::QB1),
                    q2 = tc::smem_u32(sm + lay::QB2);
@@ -593,62 +615,77 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     }
     tc::mma_commit(&bar[4]);
   }
-  if (tid >= 64 && tid < 128) {  // dcum_i += sum_j R_ij - sum_j R_ji; dbeta partials (warp 0 issues G5)
-    const int i = tid - 64;
+  constexpr int kParts = (kBThreads - 64) / 64;  // dcum row / column sums split over warps 2..15
+  if (tid >= 64) {  // dcum_i += sum_j R_ij - sum_j R_ji, in kParts ranges of j (warp 0 issues G5)
+    const int i = (tid - 64) & 63, part = (tid - 64) >> 6;
+    const int j0 = (64 * part) / kParts, j1 = (64 * (part + 1)) / kParts;
     float a = 0.f;
-    for (int j = 0; j < 64; ++j) a += kkf[i * 65 + j] - kkf[j * 65 + i];
-    dcum_acc[i] += a;
-    dbeta_acc[i] += dbp[i] + dbp[64 + i] + dbp[128 + i] + dbp[192 + i];
+    for (int j = j0; j < j1; ++j) a += kkf[i * 65 + j] - kkf[j * 65 + i];
+    daqf[part * 64 + i] = a;  // dA_qk (E4's input) is dead
+    if (part == 0) {
+      float d = 0.f;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) d += dbp[b * 64 + i];
+      dbeta_acc[i] += d;
+    }
   }
   tc::mbar_wait(&bar[4], ph, ws.err, 135);
   tc::fence_after_sync();
   __syncthreads();  // region A (the phase-2 tiles) is free once G5 has completed
   if (has_next) issue_phase1(nxt);  // next item's tiles, behind this epilogue
+  if (tid < 64) {
+    float a = 0.f;
+#pragma unroll
+    for (int b = 0; b < kParts; ++b) a += daqf[b * 64 + tid];
+    dcum_acc[tid] += a;
+  }
   // ---- final epilogue: thread = head-dim row r, tokens i = c0 + j; q[i][r], k[i][r] read from the
   // [K;Q] tile (consecutive lanes read consecutive columns of one row: no bank conflicts) -----------
-  float xr[32];
+  float xr[16];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) xr[j] = tile_elem(sm + lay::KQ, 128, 64 + c0 + j, r);
+  for (int j = 0; j < 16; ++j) xr[j] = tile_elem(sm + lay::KQ, 128, 64 + c0 + j, r);
   float* red1 = red;            // a1: sum_r dq~^T q
   float* red2 = red + 256;      // a4: sum_r dq^^T q   (l2norm)
   float* red3 = red + 512;      // a2: sum_r dk~^T k
   float* red4 = red + 768;      // a3: sum_r dBk^T k
   float* red5 = red + 1024;     // a5: sum_r dk^^T k   (l2norm)
-  float dqh[32];
+  const int rslot = q4 * 64 + c0 + (l >> 1);  // this lane's column of a warp_colsum16 (even lanes write it)
+  const bool wr = (l & 1) == 0;
+  float dqh[16];
   {
-    float t1[32], v[32];
-    tmem_ld32f(lane_addr + 0, dqh);   // (Qm k^)^T
-    tmem_ld32f(lane_addr + 64, t1);   // dq~^T
+    float t1[16], v[16];
+    tmem_ld16f(lane_addr + 0, dqh);   // (Qm k^)^T
+    tmem_ld16f(lane_addr + 64, t1);   // dq~^T
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       dqh[j] = p.scale * fmaf(ecum[c0 + j], t1[j], dqh[j]);
       v[j] = t1[j] * xr[j];
       t1[j] = dqh[j] * xr[j];
     }
-    red1[q4 * 64 + c0 + l] = warp_colsum32(v);
-    red2[q4 * 64 + c0 + l] = warp_colsum32(t1);
+    const float s1 = warp_colsum16(v), s2 = warp_colsum16(t1);
+    if (wr) { red1[rslot] = s1; red2[rslot] = s2; }
   }
-  float kr_[32];
+  float kr_[16];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) kr_[j] = tile_elem(sm + lay::KQ, 128, c0 + j, r);
-  float dkh[32];
+  for (int j = 0; j < 16; ++j) kr_[j] = tile_elem(sm + lay::KQ, 128, c0 + j, r);
+  float dkh[16];
   {
-    float t2[32], t3[32];
-    tmem_ld32f(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
-    tmem_ld32f(lane_addr + 192, t2);   // dk~^T
-    tmem_ld32f(lane_addr + 256, t3);   // dBk^T
+    float t2[16], t3[16];
+    tmem_ld16f(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
+    tmem_ld16f(lane_addr + 192, t2);   // dk~^T
+    tmem_ld16f(lane_addr + 256, t3);   // dBk^T
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       const int i = c0 + j;
       dkh[j] = fmaf(edec[i], t2[j], fmaf(beta[i] * ecum[i], t3[j], dkh[j]));
       t2[j] *= kr_[j];
       t3[j] *= kr_[j];
     }
-    red3[q4 * 64 + c0 + l] = warp_colsum32(t2);
-    red4[q4 * 64 + c0 + l] = warp_colsum32(t3);
+    const float s3 = warp_colsum16(t2), s4 = warp_colsum16(t3);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) t2[j] = dkh[j] * kr_[j];
-    red5[q4 * 64 + c0 + l] = warp_colsum32(t2);
+    for (int j = 0; j < 16; ++j) t2[j] = dkh[j] * kr_[j];
+    const float s5 = warp_colsum16(t2);
+    if (wr) { red3[rslot] = s3; red4[rslot] = s4; red5[rslot] = s5; }
   }
   __syncthreads();  // every thread holds its q and k rows (xr, kr_): [K;Q] may be refilled
   {
@@ -663,9 +700,9 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
   }
   __syncthreads();
   {
-    float gq[32], gk[32];
+    float gq[16], gk[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       const int i = c0 + j;
       const float rqi = rq[i], rki = rk[i];
       gq[j] = rqi * dqh[j] - xr[j] * rqi * rqi * rqi * red2[i];
@@ -674,24 +711,24 @@ __global__ void __launch_bounds__(256, 1) fast_chunk_bwd_kernel(GdnProblem p, Fa
     bool last = true;  // this value head completes dq / dk of its key head
     if (p.group > 1) {  // GQA: the group's running sum in fp32, kept in TMEM columns [384, 512) until its last value head
       if (cur.gi > 0) {
-        float pq[32];
-        tmem_ld32f(lane_addr + 384, pq);
+        float pq[16];
+        tmem_ld16f(lane_addr + 384, pq);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) gq[j] += pq[j];
-        tmem_ld32f(lane_addr + 448, pq);
+        for (int j = 0; j < 16; ++j) gq[j] += pq[j];
+        tmem_ld16f(lane_addr + 448, pq);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) gk[j] += pq[j];
+        for (int j = 0; j < 16; ++j) gk[j] += pq[j];
       }
       if (cur.gi + 1 < p.group) {
-        tc::tmem_st32(lane_addr + 384, gq);
-        tc::tmem_st32(lane_addr + 448, gk);
+        tc::tmem_st16(lane_addr + 384, gq);
+        tc::tmem_st16(lane_addr + 448, gk);
         last = false;
       }
     }
     if (last) {
       const int row = p.Hk * 128;
-      store_cols32(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
-      store_cols32(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
+      store_cols16(dq + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gq);
+      store_cols16(dk + (int64_t(t0) * p.Hk + hk) * 128, row, r, c0, L, gk);
     }
   }
   // ---- per-token scalars: dcum, dbeta, dg -----------------------------------------------------
@@ -766,7 +803,7 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
       if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk)) ||
           (rc = make_rows_map(&mv, p.v, p.tokens, p.Hv)) || (rc = make_rows_map(&mdo, d_o, p.tokens, p.Hv)))
         return rc;
-      fast_chunk_bwd_kernel<<<unsigned(items < sms ? items : sms), 256, kBChunkSmem, s>>>(
+      fast_chunk_bwd_kernel<<<unsigned(items < sms ? items : sms), kBThreads, kBChunkSmem, s>>>(
           p, w, static_cast<const bf16*>(d_o), static_cast<bf16*>(dq), static_cast<bf16*>(dk), static_cast<bf16*>(dv), dg,
           static_cast<bf16*>(dbeta), mq, mk, mv, mdo);
       RB2_CHECK_LAUNCH("gdn fast chunk bwd");
