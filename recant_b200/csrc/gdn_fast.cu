@@ -56,31 +56,168 @@ namespace {
 using namespace fast;
 
 // ------------------------------------------------------------------------------------------------
-// prep: one CTA (256 threads) per (chunk, value head). Thread (w, l): TMEM lane r = 32 (w & 3) + l,
-// column half hh = w >> 2 (columns [32 hh, 32 hh + 32) of the 64-wide accumulators). 128 TMEM columns:
-// [K;Q] K^T in [0, 64) is read before U^T / W^T overwrite [0, 128), so two CTAs share an SM.
+// Triangular inverse T = (I + L)^-1 of a strictly lower 64x64 L, in place (fp32, stride 65): L on
+// entry, T on exit. 256 threads. The 16x16 diagonal blocks by forward substitution on CUDA cores;
+// the 16x16 blocks below them inside each 32x32 diagonal block as T_10 = -T_11 (L_10 T_00) on CUDA
+// cores; the 32x32 bottom-left block as T_BA = -T_B (L_BA T_A) by two tcgen05 MMAs:
+//   X = P D   and   Y = P X'   (M = N = K = 64, bf16 operands, fp32 accumulators in TMEM)
+// where P is the working matrix at that point (T_A, T_B on the diagonal, L_BA below), D the same
+// with L_BA zeroed (block-diagonal T_A, T_B), and X' = X with its top 32 rows zeroed, so that
+// X[B][A] = L_BA T_A and Y[B][A] = T_B X[B][A]. ptile, dtile: 8 KB SW128 tiles (1024-aligned);
+// TMEM columns [tcol, tcol + 128) are used; bars: two mbarriers (phase 0) for the two MMAs.
 // ------------------------------------------------------------------------------------------------
-constexpr int kPrepSmem = 32768 + 16384 + 8192 + 8192 + 2 * 64 * 65 * 4 + 768 * 4 + 6 * 64 * 4 + 2048;
+__device__ void inverse_lower64_tc(float* lt, float* xbuf, unsigned char* ptile, unsigned char* dtile, uint32_t tbase,
+                                   uint32_t tcol, uint64_t* bars, int* err) {
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, q4 = w & 3, hh = w >> 2;
+  if (w < 4 && l < 16) {  // warp w: diagonal block w by forward substitution, lane = column
+    const int o = 16 * w;
+    float col[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float t = (i == l) ? 1.f : 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) t = fmaf(-lt[(o + i) * 65 + o + m], col[m], t);
+      col[i] = t;
+    }
+    __syncwarp(0x0000ffffu);  // every lane has read the block before any lane overwrites it
+#pragma unroll
+    for (int i = 0; i < 16; ++i) lt[(o + i) * 65 + o + l] = col[i];
+  }
+  __syncthreads();
+  // blocks (1, 0) and (3, 2): X_b = L_{2b+1,2b} T_{2b,2b}, then T_{2b+1,2b} = -T_{2b+1,2b+1} X_b; a thread
+  // owns a 2x2 tile (rows 2 r2, 2 r2 + 1, columns 2 cc, 2 cc + 1) of one block
+  const int bq = tid >> 6, r2 = (tid >> 3) & 7, cc = tid & 7;
+  const int rb = 16 * (2 * bq + 1), cb = 32 * bq;  // block row / column origin
+  if (tid < 128) {
+    const float* av = lt + (rb + 2 * r2) * 65 + cb;
+    const float* bv = lt + cb * 65 + cb + 2 * cc;
+    float x00 = 0.f, x01 = 0.f, x10 = 0.f, x11 = 0.f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const float a0 = av[m], a1 = av[65 + m], b0 = bv[m * 65], b1 = bv[m * 65 + 1];
+      x00 = fmaf(a0, b0, x00);
+      x01 = fmaf(a0, b1, x01);
+      x10 = fmaf(a1, b0, x10);
+      x11 = fmaf(a1, b1, x11);
+    }
+    float* xo = xbuf + bq * 256 + 2 * r2 * 16 + 2 * cc;
+    *reinterpret_cast<float2*>(xo) = make_float2(x00, x01);
+    *reinterpret_cast<float2*>(xo + 16) = make_float2(x10, x11);
+  }
+  __syncthreads();
+  if (tid < 128) {
+    const float* av = lt + (rb + 2 * r2) * 65 + rb;
+    const float* xb = xbuf + bq * 256 + 2 * cc;
+    float t00 = 0.f, t01 = 0.f, t10 = 0.f, t11 = 0.f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const float a0 = av[m], a1 = av[65 + m];
+      const float2 x = *reinterpret_cast<const float2*>(xb + m * 16);
+      t00 = fmaf(a0, x.x, t00);
+      t01 = fmaf(a0, x.y, t01);
+      t10 = fmaf(a1, x.x, t10);
+      t11 = fmaf(a1, x.y, t11);
+    }
+    float* to = lt + (rb + 2 * r2) * 65 + cb + 2 * cc;
+    to[0] = -t00;
+    to[1] = -t01;
+    to[65] = -t10;
+    to[66] = -t11;
+  }
+  __syncthreads();
+  // P (all of the working matrix) and D (its block diagonal) as bf16 images, rows i, columns j
+  for (int idx = tid; idx < 512; idx += 256) {
+    const int i = idx >> 3, c8 = (idx & 7) * 8;
+    const float* t = lt + i * 65 + c8;
+    const uint4 v = make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
+                               tc::pack_bf16(t[6], t[7]));
+    *reinterpret_cast<uint4*>(ptile + tc::sw128_offset(i, c8, 64)) = v;
+    *reinterpret_cast<uint4*>(dtile + tc::sw128_offset(i, c8, 64)) = (i >= 32 && c8 < 32) ? make_uint4(0, 0, 0, 0) : v;
+  }
+  tc::fence_proxy_async();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t pa = tc::smem_u32(ptile), da = tc::smem_u32(dtile);
+  const uint32_t idesc = tc::idesc_bf16(64, 64, false, true);  // A = P K-major (rows i), B row-major (MN-major)
+  if (tid == 0) {
+#pragma unroll 1
+    for (int k0 = 0; k0 < 64; k0 += 16)
+      tc::mma_bf16(tbase + tcol, tc::desc_kmajor_sw128(pa + k0 * 2), tc::desc_mnmajor_sw128(da + k0 * 128, 8192), idesc,
+                   k0 > 0);
+    tc::mma_commit(&bars[0]);
+  }
+  tc::mbar_wait(&bars[0], 0, err, 103);
+  tc::fence_after_sync();
+  {  // X' into the D tile: rows i = 16 q4 + l (lanes l < 16 of an M = 64 accumulator), zero above row 32
+    float x[32];
+    tc::tmem_ld32(tbase + (uint32_t(32 * q4) << 16) + tcol + 32 * hh, x);
+    if (l < 16) {
+      const int i = 16 * q4 + l;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = i >= 32 ? make_uint4(tc::pack_bf16(x[8 * j], x[8 * j + 1]), tc::pack_bf16(x[8 * j + 2], x[8 * j + 3]),
+                                             tc::pack_bf16(x[8 * j + 4], x[8 * j + 5]),
+                                             tc::pack_bf16(x[8 * j + 6], x[8 * j + 7]))
+                                : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dtile + tc::sw128_offset(i, 32 * hh + 8 * j, 64)) = v;
+      }
+    }
+  }
+  tc::fence_proxy_async();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (tid == 0) {
+#pragma unroll 1
+    for (int k0 = 0; k0 < 64; k0 += 16)
+      tc::mma_bf16(tbase + tcol + 64, tc::desc_kmajor_sw128(pa + k0 * 2), tc::desc_mnmajor_sw128(da + k0 * 128, 8192),
+                   idesc, k0 > 0);
+    tc::mma_commit(&bars[1]);
+  }
+  tc::mbar_wait(&bars[1], 0, err, 104);
+  tc::fence_after_sync();
+  if (q4 >= 2 && hh == 0) {  // T_BA = -Y[B][A]: rows 32..63 (quarters 2, 3), columns 0..31
+    float y[32];
+    tc::tmem_ld32(tbase + (uint32_t(32 * q4) << 16) + tcol + 64, y);
+    if (l < 16) {
+      float* to = lt + (16 * q4 + l) * 65;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) to[j] = -y[j];
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+}
 
-__global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws, const __grid_constant__ CUtensorMap map_q,
-                                                        const __grid_constant__ CUtensorMap map_k,
-                                                        const __grid_constant__ CUtensorMap map_v) {
+// ------------------------------------------------------------------------------------------------
+// prep: one CTA (256 threads) per (chunk, value head), three CTAs per SM. Thread (w, l): TMEM lane
+// r = 32 (w & 3) + l, column half hh = w >> 2 (columns [32 hh, 32 hh + 32) of the 64-wide
+// accumulators). 128 TMEM columns: [K;Q] K^T in [0, 128) is read before the inverse's two products
+// and then U^T / W^T reuse them. Shared memory: the [K;Q] tile, whose Q rows (bytes [8K, 16K) and
+// [24K, 32K): rows 64-127 of both 64-column slabs) are free once q~ has been written and hold first
+// the inverse's operand tiles and then T beta and T beta e^cum r_k; V; L / T in place (fp32).
+// ------------------------------------------------------------------------------------------------
+constexpr int kPrepSmem = 32768 + 16384 + 64 * 65 * 4 + 512 * 4 + 6 * 64 * 4 + 2048;
+
+__global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs ws, const __grid_constant__ CUtensorMap map_q,
+                                                           const __grid_constant__ CUtensorMap map_k,
+                                                           const __grid_constant__ CUtensorMap map_v) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* kq = sm;                  // [K;Q] K-major SW128, 128 rows x 128   (32 KB)
   unsigned char* vt = kq + 32768;          // V, 64 rows x 128 (as MN-major A)     (16 KB)
-  unsigned char* tb1 = vt + 16384;         // T diag(beta), 64 x 64 K-major         (8 KB)
-  unsigned char* tb2 = tb1 + 8192;         // T diag(beta e^cum rk)                 (8 KB)
-  float* lm = reinterpret_cast<float*>(tb2 + 8192);
-  float* tm = lm + 64 * 65;
-  float* xbuf = tm + 64 * 65;
-  float* cum = xbuf + 768;
+  unsigned char* tb1 = kq + 8192;          // over Q, slab 0: P, then T diag(beta)                  (8 KB)
+  unsigned char* tb2 = kq + 24576;         // over Q, slab 1: D / X', then T diag(beta e^cum rk)   (8 KB)
+  float* lt = reinterpret_cast<float*>(vt + 16384);  // L, then T (fp32 64 x 65)
+  float* xbuf = lt + 64 * 65;
+  float* cum = xbuf + 512;
   float* rq = cum + 64;
   float* rk = rq + 64;
   float* beta = rk + 64;
   float* ecum = beta + 64;
   float* gv = ecum + 64;
-  __shared__ uint64_t bar[3];  // [K;Q] K^T, U/W, loads
+  __shared__ uint64_t bar[5];  // [K;Q] K^T, U/W, loads, the inverse's two products
   __shared__ uint32_t tmem_base;
 
   const int ci = blockIdx.x, h = blockIdx.y;
@@ -95,9 +232,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws,
     tc::tmem_relinquish();
   }
   if (tid == 0) {  // k, q, v rows of the chunk by TMA
-    tc::mbar_init(&bar[0], 1);
-    tc::mbar_init(&bar[1], 1);
-    tc::mbar_init(&bar[2], 1);
+    for (int b = 0; b < 5; ++b) tc::mbar_init(&bar[b], 1);
     tc::fence_mbar_init();
     tc::mbar_expect_tx(&bar[2], 3 * 16384);
     tc::tma_rows128(kq, 16384, 0, &map_k, hk, t0, &bar[2]);
@@ -173,6 +308,17 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws,
   if (tid < 64) ecum[tid] = __expf(cum[tid]);
   float* st = ws.stats + ch * 256;
   if (tid < 64) { st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid]; }
+  // q~ rows now (the Q rows' shared memory is reused below): half-warp per row, 8 elements per lane
+  for (int row_ = w * 2 + (l >> 4); row_ < 64; row_ += 16) {
+    const int c8 = (l & 15) * 8;
+    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(64 + row_, c8, 128));
+    const float f = p.scale * rq[row_] * __expf(cum[row_]);
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
+    *reinterpret_cast<uint4*>(img(ws.qt + ch * 8192) + tc::sw128_offset(row_, c8, 64)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
   uint32_t apk[16];  // A_qk row i (bf16 pairs), stored after the proxy fence below
   {
     const int i = r & 63;
@@ -182,7 +328,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws,
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         const int j = c0 + jj;
-        lm[i * 65 + j] = j < i ? bi * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
+        lt[i * 65 + j] = j < i ? bi * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
       }
     } else {
       const float si = p.scale * rq[i];
@@ -196,8 +342,8 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws,
     }
   }
   tc::fence_before_sync();
-  __syncthreads();
-  unit_lower_inverse(lm, tm, xbuf, 256);
+  __syncthreads();  // L complete; the Q rows and the [K;Q] K^T accumulator are consumed
+  inverse_lower64_tc(lt, xbuf, tb1, tb2, tbase, 0, &bar[3], ws.err);
   {
     const int i = tid & 63, which = (tid >> 6) & 1, m0 = 32 * (tid >> 7);
     unsigned char* dst = which == 0 ? tb1 : tb2;
@@ -207,7 +353,7 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws,
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         const int m = m0 + mb + j;
-        float f0 = tm[i * 65 + m] * beta[m], f1 = tm[i * 65 + m + 1] * beta[m + 1];
+        float f0 = lt[i * 65 + m] * beta[m], f1 = lt[i * 65 + m + 1] * beta[m + 1];
         if (which) { f0 *= ecum[m] * rk[m]; f1 *= ecum[m + 1] * rk[m + 1]; }
         pk[j >> 1] = tc::pack_bf16(f0, f1);
       }
@@ -240,23 +386,21 @@ __global__ void __launch_bounds__(256) fast_prep_kernel(GdnProblem p, FastWs ws,
   }
   for (int idx = tid; idx < 512; idx += 256) {
     const int i = idx >> 3, c8 = (idx & 7) * 8;
-    const float* t = tm + i * 65 + c8;
+    const float* t = lt + i * 65 + c8;
     *reinterpret_cast<uint4*>(img(ws.tinv + ch * 4096) + tc::sw128_offset(i, c8, 64)) =
         make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
                    tc::pack_bf16(t[6], t[7]));
   }
-  // q~ and k~ rows while the MMAs run: half-warp per row, 8 elements per lane (warps 1-7)
-  for (int row = (w - 1) * 2 + (l >> 4); w > 0 && row < 128; row += 14) {
+  // k~ rows while the MMAs run: half-warp per row, 8 elements per lane (warps 1-7)
+  for (int row_ = (w - 1) * 2 + (l >> 4); w > 0 && row_ < 64; row_ += 14) {
     const int c8 = (l & 15) * 8;
-    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row, c8, 128));
-    const int i = row & 63;
-    const float f = row < 64 ? __expf(cum[63] - cum[i]) * rk[i] : p.scale * rq[i] * ecum[i];
+    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row_, c8, 128));
+    const float f = __expf(cum[63] - cum[row_]) * rk[row_];
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
-    unsigned char* dst = img((row < 64 ? ws.kt : ws.qt) + ch * 8192) + tc::sw128_offset(i, c8, 64);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(img(ws.kt + ch * 8192) + tc::sw128_offset(row_, c8, 64)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   tc::mbar_wait(&bar[1], 0, ws.err, 102);
   tc::fence_after_sync();
@@ -497,6 +641,9 @@ int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_
   }
   if ((p.stages & 1) && p.max_chunks > 0) {
     if ((rc = smem_attr(fast_prep_kernel, kPrepSmem))) return rc;
+    // all of the SM's unified memory as shared memory, so that three prep CTAs fit on one SM
+    RB2_CUDA(cudaFuncSetAttribute(fast_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+             "gdn fast prep: carveout");
     ProfScope ps_("gdn_fast_prep", s);
     CUtensorMap mq, mk, mv;
     if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk)) ||
