@@ -202,6 +202,17 @@ RB2_API int rb2_nvfp4_quantize_noalloc(const void* x, int64_t M, int64_t K, int 
                                        uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,
                                        float* gscale, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Narrow bf16 projection: out[M,N] = A[M,K] . B[N,K]^T, fp32 accumulation, out bf16 (RB2_BF16) or
+ * fp32 (RB2_F32) with row stride ldo. Replaces the block's dense projections that are too narrow for
+ * NVFP4 -- in_proj_b / in_proj_a (recant/model/layers.py:154-155; QLinear keeps N < 256 unquantized,
+ * layers.py:47-48) -- and the LoRA down-projections x A^T (layers.py:65-69, 86-88), concatenated
+ * along N so that one pass over x yields all of them. B contiguous [N][K]; A row stride lda
+ * (elements). Needs 16 <= N <= 256 with N % 16 == 0, K % 64 == 0, lda and ldo multiples of 8, A, B
+ * and out 16-byte aligned. */
+RB2_API int rb2_skinny_gemm(const void* A, int64_t lda, const void* B, int64_t M, int64_t N, int64_t K, void* out,
+                            int64_t ldo, int out_dtype, void* stream);
+
 /* Scale bytes [rows, cols] (e4m3) -> the 128x4 blocked swizzle of nvfp4._to_blocked
  * (recant/model/nvfp4.py:112-119), ceil(rows/128)*ceil(cols/4)*512 bytes, pad bytes zero. Lets
  * FP4 tensors quantized elsewhere (e.g. by the reference's quantize_weight) feed the GEMM. */

@@ -16,8 +16,10 @@ x [B, T, hidden] bf16 ->
   y           = out_proj(RMSNormGated(core, z))  (NVFP4 + LoRA)            (layers.py:23-34,181)
 
 Kernels: ``rb2_conv_silu_*``, ``rb2_gdn_gates_*``, ``rb2_gated_rmsnorm_*`` (csrc/gdn_block.cu), the
-NVFP4 quantizer and GEMM, the GDN op; the LoRA products (rank 16) and the N = Hv projections are
-plain GEMMs through torch (cuBLAS). Frozen weights get no gradients; LoRA A and B do.
+NVFP4 quantizer and GEMM, the GDN op, and ``rb2_skinny_gemm`` (csrc/skinny_gemm.cu) for the narrow
+projections of x: in_proj_b, in_proj_a and the LoRA down-projections of in_proj_qkv / in_proj_z
+come from one pass over x (:class:`_XProjections`). The LoRA up-projections and the LoRA weight
+gradients are plain GEMMs through torch (cuBLAS). Frozen weights get no gradients; LoRA A and B do.
 """
 from __future__ import annotations
 
@@ -34,6 +36,64 @@ from .gdn import RECURRENT_MAX_T, _stream, gdn_b200, gdn_recurrent
 
 def _p(t):
     return L.ptr(t)
+
+
+# The narrow projections of x run on rb2_skinny_gemm from this many rows on; shorter calls (the
+# decode step's few rows) keep the cuBLAS GEMV-like path, which has less latency for one tile.
+NARROW_MIN_ROWS = 65
+
+
+def narrow_product(x2, w):
+    """x2 [M, K] bf16 . w [N, K]^T bf16 -> bf16 [M, N] on the library's tcgen05 kernel (N <= 256, K a
+    multiple of 64; N is padded to a multiple of 16 with zero rows)."""
+    M, K = x2.shape
+    n = w.shape[0]
+    npad = -(-n // 16) * 16
+    if npad != n:
+        w = torch.cat([w, w.new_zeros(npad - n, K)], 0)
+    w = w.contiguous()
+    out = torch.empty(M, npad, dtype=torch.bfloat16, device=x2.device)
+    L.check(L.lib().rb2_skinny_gemm(_p(x2), x2.stride(0), _p(w), M, npad, K, _p(out), npad, L.BF16,
+                                    _stream(x2.device)), "skinny_gemm")
+    return out[:, :n]
+
+
+def _narrow_ok(x, n):
+    x2_rows = x.numel() // x.shape[-1]
+    return (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 64 == 0 and 0 < n <= 256
+            and x2_rows >= NARROW_MIN_ROWS)
+
+
+class _XProjections(torch.autograd.Function):
+    """The block's narrow projections of x in one pass: [x W_f^T | x A_1^T | x A_2^T ...] with W_f the
+    frozen bf16 rows (in_proj_b, in_proj_a; layers.py:154-155) and A_i the LoRA down-projection
+    weights of the grouped in_proj (layers.py:86-88, cast to bf16 as the reference casts them).
+    Backward: dx = dout . [W_f; A_i] and dA_i = (dh_i^T x) in bf16 then fp32, the gradient the
+    reference's autograd gives through ``A.to(x.dtype)``; W_f gets none."""
+
+    @staticmethod
+    def forward(ctx, x, w_frozen, *As):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+        W = torch.cat([w_frozen.to(torch.bfloat16)] + [a.to(torch.bfloat16) for a in As], 0).contiguous()
+        out = narrow_product(x2, W)
+        ctx.save_for_backward(x2, W)
+        ctx.n_frozen = w_frozen.shape[0]
+        ctx.ranks = [a.shape[0] for a in As]
+        ctx.xshape = x.shape
+        return out.reshape(*x.shape[:-1], W.shape[0])
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, W = ctx.saved_tensors
+        d2 = dout.reshape(-1, dout.shape[-1]).to(torch.bfloat16)
+        dx = (d2 @ W).reshape(ctx.xshape) if ctx.needs_input_grad[0] else None
+        grads, off = [], ctx.n_frozen
+        for i, r in enumerate(ctx.ranks):
+            grads.append((d2[:, off:off + r].t() @ x2).float() if ctx.needs_input_grad[2 + i] else None)
+            off += r
+        return (dx, None, *grads)
 
 
 class _ConvSiLU(torch.autograd.Function):
@@ -297,11 +357,12 @@ class QLinear(nn.Module):
         return self.lora(x, y)
 
 
-def grouped_linear(x, lins):
+def grouped_linear(x, lins, h=None):
     """layers.py:72-97 with the activation quantized once for all NVFP4 members; the LoRA
     down-projections of all members come from one GEMM over x (x . cat(A_i)^T, as the reference's
-    default path, layers.py:86-88); each member's up-projection is added inside its NVFP4 GEMM
-    (ranks 8 and 16; other ranks add one addmm per member as the reference does)."""
+    default path, layers.py:86-88), or are given as ``h`` (the members' x A_i^T side by side, e.g.
+    from :class:`_XProjections`); each member's up-projection is one addmm as the reference's, or,
+    with the fused LoRA epilogue switched on, is added inside its NVFP4 GEMM (ranks 8 and 16)."""
     if _fused_lora_ok(lins):
         ab = [t for l in lins for t in (l.lora_A, l.lora_B)]
         return list(_FP4LoRAGroup.apply(x, lins[0].stochastic_backward, 0, tuple(l.fp4 for l in lins),
@@ -315,7 +376,8 @@ def grouped_linear(x, lins):
     act = [l for l in lins if l.lora_A is not None]
     if not act:
         return base
-    h = x @ torch.cat([l.lora_A for l in act], 0).to(x.dtype).t()
+    if h is None:
+        h = x @ torch.cat([l.lora_A for l in act], 0).to(x.dtype).t()
     res, off = [], 0
     for l, y in zip(lins, base):
         if l.lora_A is None:
@@ -406,12 +468,23 @@ class GDNBlock(nn.Module):
         graph needs). ``pos_offset`` is accepted for the reference's signature and unused."""
         B, T, _ = x.shape
         d = self.d
-        qkv, z = grouped_linear(x, [self.in_proj_qkv, self.in_proj_z])
-        if self.in_proj_b.weight is not None and self.in_proj_a.weight is not None:  # one N = 2 Hv GEMM
-            ba = x @ torch.cat([self.in_proj_b.weight, self.in_proj_a.weight], 0).t()
-            b_lin, a = ba[..., :self.Hv], ba[..., self.Hv:]
+        ins = [self.in_proj_qkv, self.in_proj_z]
+        lora_ins = [l for l in ins if l.lora_A is not None]
+        dense_ba = self.in_proj_b.weight is not None and self.in_proj_a.weight is not None
+        if (dense_ba and not _fused_lora_ok(ins)
+                and _narrow_ok(x, 2 * self.Hv + sum(l.lora_A.shape[0] for l in lora_ins))):
+            # one pass over x: b, a and the LoRA down-projections of in_proj_qkv / in_proj_z
+            proj = _XProjections.apply(x, torch.cat([self.in_proj_b.weight, self.in_proj_a.weight], 0),
+                                       *[l.lora_A for l in lora_ins])
+            b_lin, a = proj[..., :self.Hv], proj[..., self.Hv:2 * self.Hv]
+            qkv, z = grouped_linear(x, ins, h=proj[..., 2 * self.Hv:] if lora_ins else None)
         else:
-            b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
+            qkv, z = grouped_linear(x, ins)
+            if dense_ba:  # one N = 2 Hv GEMM
+                ba = x @ torch.cat([self.in_proj_b.weight, self.in_proj_a.weight], 0).t()
+                b_lin, a = ba[..., :self.Hv], ba[..., self.Hv:]
+            else:
+                b_lin, a = self.in_proj_b(x), self.in_proj_a(x)
         inplace = (inplace_cache and cache is not None and cache.conv_state is not None
                    and cache.rec_state is not None and T <= RECURRENT_MAX_T and not torch.is_grad_enabled())
         if cache is None:
