@@ -202,6 +202,17 @@ RB2_API int rb2_nvfp4_quantize_noalloc(const void* x, int64_t M, int64_t K, int 
                                        uint64_t seed, uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked,
                                        float* gscale, void* stream);
 
+/* Gated RMSNorm (as rb2_gated_rmsnorm_fwd) fused with the NVFP4 quantize of its output: y = the
+ * norm of x gated by z (fused_ops.py:11-16) and rstd as rb2_gated_rmsnorm_fwd, plus codes / scales /
+ * blocked scales / gscale of quantize(rht(y)) (RN) as rb2_nvfp4_quantize on y viewed as [M, K]
+ * (rows * 128 == M * K) -- the out_proj input of GatedDeltaNet.forward (layers.py:181, QLinear ->
+ * quantize_activation, nvfp4.py:144-149). The global amax is reduced in the norm's own pass, so y
+ * is read once more (by the code pass) instead of twice. ws: rb2_nvfp4_quantize_workspace_size(M, K). */
+RB2_API int rb2_gated_rmsnorm_nvfp4_fwd(const void* x, const void* z, const float* w, int64_t rows, int dim, float eps,
+                                        void* y, float* rstd, int64_t M, int64_t K, int use_rht, uint8_t* codes,
+                                        uint8_t* scales, uint8_t* scales_blocked, float* gscale, void* ws,
+                                        size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Narrow bf16 projection: out[M,N] = A[M,K] . B[N,K]^T, fp32 accumulation, out bf16 (RB2_BF16) or
  * fp32 (RB2_F32) with row stride ldo. Replaces the block's dense projections that are too narrow for

@@ -52,6 +52,8 @@ SIGNATURES = {
     "rb2_nvfp4_gemv": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "rb2_nvfp4_gemm_b_images": (_i, [_p, _i64, _i64, _p, _sz, _p]),
     "rb2_skinny_gemm": (_i, [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _i, _p]),
+    "rb2_gated_rmsnorm_nvfp4_fwd": (_i, [_p, _p, _p, _i64, _i, _f, _p, _p, _i64, _i64, _i, _p, _p, _p, _p, _p, _sz,
+                                         _p]),
     "rb2_profile_enable": (_i, [_i]),
     "rb2_profile_disable": (_i, []),
     "rb2_profile_read": (_i, [_i, C.c_char_p, _sz, C.POINTER(C.c_float)]),

@@ -38,6 +38,12 @@ def _p(t):
     return L.ptr(t)
 
 
+# The gated norm reduces out_proj's quantizer amax in its own pass (rb2_gated_rmsnorm_nvfp4_fwd) when
+# y has more blocks of 16 than the quantizer's single-launch limit; smaller calls (the decode step)
+# keep the norm and the one-launch quantizer.
+FUSE_NORM_QUANT = True
+NORM_QUANT_MIN_BLOCKS = 2048
+
 # The narrow projections of x run on rb2_skinny_gemm from this many rows on; shorter calls (the
 # decode step's few rows) keep the cuBLAS GEMV-like path, which has less latency for one tile.
 NARROW_MIN_ROWS = 65
@@ -186,6 +192,49 @@ class _GatedRMSNorm(torch.autograd.Function):
         return dx, dz, None, None
 
 
+class _GatedRMSNormQuant(torch.autograd.Function):
+    """The gated RMSNorm whose output feeds an NVFP4 projection, fused with that projection's
+    activation quantize (rb2_gated_rmsnorm_nvfp4_fwd): returns y and the NVFP4 codes, scales,
+    blocked scales and global scale of quantize(rht(y)) for y viewed as [M, K] (RN, as
+    quantize_activation in the forward, nvfp4.py:144-149). The quantized parts get no gradient;
+    y's backward is the gated norm's."""
+
+    @staticmethod
+    def forward(ctx, x, z, w, eps, K, use_rht):
+        x, z = x.to(torch.bfloat16).contiguous(), z.to(torch.bfloat16).contiguous()
+        wf = w.float().contiguous()
+        rows = x.numel() // 128
+        M = rows * 128 // K
+        y = torch.empty_like(x)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        codes = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device)
+        scales = torch.empty(M, K // 16, dtype=torch.uint8, device=x.device)
+        blocked = torch.empty(N.blocked_size(M, K // 16), dtype=torch.uint8, device=x.device)
+        gscale = torch.empty((), dtype=torch.float32, device=x.device)
+        lib = L.lib()
+        wsb = lib.rb2_nvfp4_quantize_workspace_size(M, K)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=x.device)
+        L.check(lib.rb2_gated_rmsnorm_nvfp4_fwd(_p(x), _p(z), _p(wf), rows, 128, float(eps), _p(y), _p(rstd), M, K,
+                                                int(use_rht), _p(codes), _p(scales), _p(blocked), _p(gscale), _p(ws),
+                                                wsb, _stream(x.device)), "gated_rmsnorm_nvfp4_fwd")
+        ctx.save_for_backward(x, z, wf, rstd)
+        ctx.mark_non_differentiable(codes, scales, blocked, gscale)
+        return y, codes, scales, blocked, gscale
+
+    @staticmethod
+    def backward(ctx, dy, *unused):
+        dx, dz, _, _ = _GatedRMSNorm.backward(ctx, dy)
+        return dx, dz, None, None, None, None
+
+
+def gated_rmsnorm_quant(x, z, weight, K, use_rht=True, eps=1e-6):
+    """RMSNormGated over rows of 128 and the NVFP4 quantize of its output viewed as [M, K]:
+    (y, FP4Tensor) -- what ``out_proj(gated_rmsnorm(...))`` computes in two passes."""
+    y, codes, scales, blocked, gscale = _GatedRMSNormQuant.apply(x, z, weight, eps, K, use_rht)
+    M = codes.shape[0]
+    return y, N.FP4Tensor(codes, scales.view(torch.float8_e4m3fn), gscale, (M, K), blocked)
+
+
 def conv_silu(x, weight, s1, s2, prev=None, want_state=False, state_out=None):
     """silu(causal depthwise conv1d(x, weight [C, 1, 4])), x [B, T, C] bf16 (layers.py:157-168), split
     into channels [0, s1), [s1, s2), [s2, C) as three contiguous tensors (layers.py:169). ``prev``:
@@ -211,9 +260,10 @@ class _FP4Group(torch.autograd.Function):
     Q(rht(dy_i)) . dgrad_i^T with stochastic rounding, as FP4Linear (nvfp4.py:151-170)."""
 
     @staticmethod
-    def forward(ctx, x, stochastic, *weights):
+    def forward(ctx, x, stochastic, a_pre, *weights):
         x2 = x.reshape(-1, weights[0].in_features)
-        a = N.quantize_activation(x2, weights[0].use_rht)
+        # a_pre: x already quantized by its producer (gated_rmsnorm_quant), else quantized here
+        a = N.quantize_activation(x2, weights[0].use_rht) if a_pre is None else a_pre
         ys = tuple(N._gemm_to(a, w.fprop, x.dtype).reshape(*x.shape[:-1], w.out_features) for w in weights)
         ctx.weights, ctx.stochastic, ctx.xshape = weights, stochastic, x.shape
         return ys
@@ -227,7 +277,7 @@ class _FP4Group(torch.autograd.Function):
             d = N.quantize_activation(dy.reshape(-1, w.out_features), w.use_rht, stochastic=ctx.stochastic)
             part = N._gemm_to(d, w.dgrad, dy.dtype)
             dx = part if dx is None else dx + part
-        return (None if dx is None else dx.reshape(ctx.xshape), None, *([None] * len(ctx.weights)))
+        return (None if dx is None else dx.reshape(ctx.xshape), None, None, *([None] * len(ctx.weights)))
 
 
 class _FP4LoRAGroup(torch.autograd.Function):
@@ -345,13 +395,15 @@ class QLinear(nn.Module):
             return o.reshape(*y.shape)
         return y + (h @ self.lora_B.to(x.dtype).t()) * self.lora_scale
 
-    def forward(self, x):
+    def forward(self, x, a_pre=None):
+        """``a_pre``: x already quantized (the FP4Tensor of x, RN, with this weight's RHT setting),
+        as the fused gated norm produces it; used by the NVFP4 base only."""
         if _fused_lora_ok([self]):
             (y,) = _FP4LoRAGroup.apply(x, self.stochastic_backward, 1, (self.fp4,), (self.lora_scale,),
                                        self.lora_A, self.lora_B)
             return y
         if self.fp4 is not None:
-            (y,) = _FP4Group.apply(x, self.stochastic_backward, self.fp4)
+            (y,) = _FP4Group.apply(x, self.stochastic_backward, a_pre, self.fp4)
         else:
             y = x @ self.weight.t()
         return self.lora(x, y)
@@ -370,7 +422,7 @@ def grouped_linear(x, lins, h=None):
     fp4 = [l for l in lins if l.fp4 is not None]
     outs = {}
     if fp4:
-        ys = _FP4Group.apply(x, fp4[0].stochastic_backward, *[l.fp4 for l in fp4])
+        ys = _FP4Group.apply(x, fp4[0].stochastic_backward, None, *[l.fp4 for l in fp4])
         outs = {id(l): y for l, y in zip(fp4, ys)}
     base = [outs[id(l)] if id(l) in outs else x @ l.weight.t() for l in lins]
     act = [l for l in lins if l.lora_A is not None]
@@ -506,8 +558,15 @@ class GDNBlock(nn.Module):
         else:
             core, rec = gdn_b200(q, k, v, g, beta, initial_state=cache.rec_state, output_final_state=True)
             cache.rec_state = rec.detach()
+        op = self.out_proj
+        if (FUSE_NORM_QUANT and op.fp4 is not None and not _fused_lora_ok([op]) and core.dtype == torch.bfloat16
+                and core.numel() // 16 > NORM_QUANT_MIN_BLOCKS):
+            # the norm's pass also reduces the quantizer's global amax; out_proj gets the codes
+            y, a = gated_rmsnorm_quant(core.reshape(-1, d), z.reshape(-1, d), self.norm_weight, op.in_features,
+                                       op.fp4.use_rht, self.eps)
+            return op(y.reshape(B, T, -1), a_pre=a)
         y = gated_rmsnorm(core.reshape(-1, d), z.reshape(-1, d), self.norm_weight, self.eps)
-        return self.out_proj(y.reshape(B, T, -1))
+        return op(y.reshape(B, T, -1))
 
 
 @dataclass

@@ -7,6 +7,7 @@
 // gradients). All are HBM-bound: 16-byte loads and stores, fp32 arithmetic, the reference's
 // roundings to bf16 where its eager code casts.
 #include "common.cuh"
+#include "gated_norm.cuh"
 
 namespace rb2 {
 namespace {
@@ -267,26 +268,34 @@ __global__ void __launch_bounds__(256) gates_bwd_kernel(const bf16* __restrict__
 __global__ void __launch_bounds__(256) gated_norm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z,
                                                              const float* __restrict__ w, int64_t rows, float eps,
                                                              bf16* __restrict__ y, float* __restrict__ rstd) {
-  const int lane = threadIdx.x & 31;
-  const float4 wv = reinterpret_cast<const float4*>(w)[lane];
-  for (int64_t row = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5; row < rows; row += int64_t(gridDim.x) * 8) {
-    const uint2 ux = reinterpret_cast<const uint2*>(x + row * 128)[lane];
-    const uint2 uz = reinterpret_cast<const uint2*>(z + row * 128)[lane];
-    const float xv[4] = {__uint_as_float(ux.x << 16), __uint_as_float(ux.x & 0xffff0000u),
-                         __uint_as_float(ux.y << 16), __uint_as_float(ux.y & 0xffff0000u)};
-    const float zv[4] = {__uint_as_float(uz.x << 16), __uint_as_float(uz.x & 0xffff0000u),
-                         __uint_as_float(uz.y << 16), __uint_as_float(uz.y & 0xffff0000u)};
-    float ss = xv[0] * xv[0] + xv[1] * xv[1] + xv[2] * xv[2] + xv[3] * xv[3];
-    ss = warp_sum(ss);
-    const float r = rsqrtf(ss * (1.f / 128.f) + eps);
-    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
-    float o[4];
+  // 16 threads per row (gated_norm.cuh), two rows per warp, two row pairs per warp and step
+  const int lane = threadIdx.x & 31, hl = lane & 15;
+  float w8[8];
+  {
+    const float4 a = reinterpret_cast<const float4*>(w)[2 * hl], b = reinterpret_cast<const float4*>(w)[2 * hl + 1];
+    w8[0] = a.x; w8[1] = a.y; w8[2] = a.z; w8[3] = a.w; w8[4] = b.x; w8[5] = b.y; w8[6] = b.z; w8[7] = b.w;
+  }
+  const int64_t warp = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5, nwarps = int64_t(gridDim.x) * 8;
+  for (int64_t row0 = warp * 4 + (lane >> 4); row0 - (lane >> 4) < rows; row0 += nwarps * 4) {
+    uint4 ux[2], uz[2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = bfr(wa[i] * bfr(xv[i] * r)) * silu(zv[i]);
-    const __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]), p1 = __floats2bfloat162_rn(o[2], o[3]);
-    reinterpret_cast<uint2*>(y + row * 128)[lane] =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1));
-    if (lane == 0 && rstd) rstd[row] = r;
+    for (int u = 0; u < 2; ++u) {
+      const int64_t row = row0 + 2 * u;
+      ux[u] = row < rows ? reinterpret_cast<const uint4*>(x + row * 128)[hl] : make_uint4(0, 0, 0, 0);
+      uz[u] = row < rows ? reinterpret_cast<const uint4*>(z + row * 128)[hl] : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t row = row0 + 2 * u;
+      float x8[8], z8[8], o[8];
+      gn_unpack8(ux[u], x8);
+      gn_unpack8(uz[u], z8);
+      const float r = gated_norm8(x8, z8, w8, eps, o);
+      if (row < rows) {
+        reinterpret_cast<uint4*>(y + row * 128)[hl] = gn_pack8(o);
+        if (hl == 0 && rstd) rstd[row] = r;
+      }
+    }
   }
 }
 // out = bf16(w n) silu(z), n = bf16(x r): dz = dout bf16(w n) silu'(z); dn = dout w silu(z);
@@ -298,36 +307,53 @@ __global__ void __launch_bounds__(256) gated_norm_bwd_kernel(const bf16* __restr
   const int lane = threadIdx.x & 31;
   const float4 wv = reinterpret_cast<const float4*>(w)[lane];
   const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
-  for (int64_t row = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5; row < rows; row += int64_t(gridDim.x) * 8) {
-    const uint2 ux = reinterpret_cast<const uint2*>(x + row * 128)[lane];
-    const uint2 uz = reinterpret_cast<const uint2*>(z + row * 128)[lane];
-    const uint2 ud = reinterpret_cast<const uint2*>(dout + row * 128)[lane];
-    const float xv[4] = {__uint_as_float(ux.x << 16), __uint_as_float(ux.x & 0xffff0000u),
-                         __uint_as_float(ux.y << 16), __uint_as_float(ux.y & 0xffff0000u)};
-    const float zv[4] = {__uint_as_float(uz.x << 16), __uint_as_float(uz.x & 0xffff0000u),
-                         __uint_as_float(uz.y << 16), __uint_as_float(uz.y & 0xffff0000u)};
-    const float gv[4] = {__uint_as_float(ud.x << 16), __uint_as_float(ud.x & 0xffff0000u),
-                         __uint_as_float(ud.y << 16), __uint_as_float(ud.y & 0xffff0000u)};
-    const float r = rstd[row];
-    float dn[4], dzv[4], dot = 0.f;
+  // four rows per warp and step, their loads issued together (the rows are short: 256 bytes each)
+  constexpr int kU = 4;
+  const int64_t warp = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5, nwarps = int64_t(gridDim.x) * 8;
+  for (int64_t row0 = warp * kU; row0 < rows; row0 += nwarps * kU) {
+    uint2 uxs[kU], uzs[kU], uds[kU];
+    float rs[kU];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float s = sigm(zv[i]);
-      const float wn = bfr(wa[i] * bfr(xv[i] * r));
-      dzv[i] = gv[i] * wn * s * (1.f + zv[i] * (1.f - s));
-      dn[i] = gv[i] * wa[i] * zv[i] * s;
-      dot += dn[i] * xv[i] * r;
+    for (int u = 0; u < kU; ++u) {
+      if (row0 + u < rows) {
+        uxs[u] = reinterpret_cast<const uint2*>(x + (row0 + u) * 128)[lane];
+        uzs[u] = reinterpret_cast<const uint2*>(z + (row0 + u) * 128)[lane];
+        uds[u] = reinterpret_cast<const uint2*>(dout + (row0 + u) * 128)[lane];
+        rs[u] = rstd[row0 + u];
+      }
     }
-    dot = warp_sum(dot) * (1.f / 128.f);
-    float dxv[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) dxv[i] = r * (dn[i] - xv[i] * r * dot);
-    const __nv_bfloat162 a0 = __floats2bfloat162_rn(dxv[0], dxv[1]), a1 = __floats2bfloat162_rn(dxv[2], dxv[3]);
-    const __nv_bfloat162 b0 = __floats2bfloat162_rn(dzv[0], dzv[1]), b1 = __floats2bfloat162_rn(dzv[2], dzv[3]);
-    reinterpret_cast<uint2*>(dx + row * 128)[lane] =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&a0), *reinterpret_cast<const uint32_t*>(&a1));
-    reinterpret_cast<uint2*>(dz + row * 128)[lane] =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
+    for (int u = 0; u < kU; ++u) {
+      const int64_t row = row0 + u;
+      if (row >= rows) break;
+      const uint2 ux = uxs[u], uz = uzs[u], ud = uds[u];
+      const float xv[4] = {__uint_as_float(ux.x << 16), __uint_as_float(ux.x & 0xffff0000u),
+                           __uint_as_float(ux.y << 16), __uint_as_float(ux.y & 0xffff0000u)};
+      const float zv[4] = {__uint_as_float(uz.x << 16), __uint_as_float(uz.x & 0xffff0000u),
+                           __uint_as_float(uz.y << 16), __uint_as_float(uz.y & 0xffff0000u)};
+      const float gv[4] = {__uint_as_float(ud.x << 16), __uint_as_float(ud.x & 0xffff0000u),
+                           __uint_as_float(ud.y << 16), __uint_as_float(ud.y & 0xffff0000u)};
+      const float r = rs[u];
+      float dn[4], dzv[4], dot = 0.f;
+  #pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float s = sigm(zv[i]);
+        const float wn = bfr(wa[i] * bfr(xv[i] * r));
+        dzv[i] = gv[i] * wn * s * (1.f + zv[i] * (1.f - s));
+        dn[i] = gv[i] * wa[i] * zv[i] * s;
+        dot += dn[i] * xv[i] * r;
+      }
+      dot = warp_sum(dot) * (1.f / 128.f);
+      float dxv[4];
+  #pragma unroll
+      for (int i = 0; i < 4; ++i) dxv[i] = r * (dn[i] - xv[i] * r * dot);
+      const __nv_bfloat162 a0 = __floats2bfloat162_rn(dxv[0], dxv[1]), a1 = __floats2bfloat162_rn(dxv[2], dxv[3]);
+      const __nv_bfloat162 b0 = __floats2bfloat162_rn(dzv[0], dzv[1]), b1 = __floats2bfloat162_rn(dzv[2], dzv[3]);
+      reinterpret_cast<uint2*>(dx + row * 128)[lane] =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&a0), *reinterpret_cast<const uint32_t*>(&a1));
+      reinterpret_cast<uint2*>(dz + row * 128)[lane] =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
+    }
   }
 }
 
@@ -439,7 +465,7 @@ extern "C" int rb2_gated_rmsnorm_fwd(const void* x, const void* z, const float* 
                 "gated_rmsnorm: null or misaligned pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   ProfScope ps_("block_gated_norm_fwd", s);
-  gated_norm_fwd_kernel<<<grid_for(rows, 8), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(z), w,
+  gated_norm_fwd_kernel<<<grid_for(rows, 32), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(z), w,
                                                            rows, eps, static_cast<bf16*>(y), rstd);
   RB2_CHECK_LAUNCH("gated_rmsnorm_fwd");
   return RB2_OK;
@@ -454,7 +480,7 @@ extern "C" int rb2_gated_rmsnorm_bwd(const void* x, const void* z, const float* 
                 "gated_rmsnorm: null or misaligned pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   ProfScope ps_("block_gated_norm_bwd", s);
-  gated_norm_bwd_kernel<<<grid_for(rows, 8), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(z), w,
+  gated_norm_bwd_kernel<<<grid_for(rows, 32), 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(z), w,
                                                            rstd, static_cast<const bf16*>(dout), rows,
                                                            static_cast<bf16*>(dx), static_cast<bf16*>(dz));
   RB2_CHECK_LAUNCH("gated_rmsnorm_bwd");

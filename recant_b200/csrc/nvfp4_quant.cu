@@ -21,6 +21,7 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "gated_norm.cuh"
 
 namespace rb2 {
 namespace {
@@ -415,6 +416,144 @@ extern "C" int rb2_nvfp4_quantize(const void* x, int64_t M, int64_t K, int dtype
                                                 seed, gmax, codes, scales, scales_blocked, gscale);
   }
   RB2_CHECK_LAUNCH("nvfp4_quantize");
+  return RB2_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// The block's gated RMSNorm (RMSNormGated, recant/model/fused_ops.py:11-16: y = bf16(w bf16(x r))
+// silu(z) over rows of 128, r = rsqrt(mean x^2 + eps)) fused with the first pass of the NVFP4
+// quantizer of y, the out_proj input (layers.py:181 -> QLinear -> quantize_activation,
+// nvfp4.py:144-149): the kernel writes y and r and reduces the global amax of rht(y) in the same
+// pass, so the quantizer's second pass is the only other read of y.
+// 16 threads per row (gated_norm.cuh: thread h holds elements 8h .. 8h + 7, the same arithmetic as
+// the stand-alone norm kernel), so each 16-element block of the transform spans lanes 2b, 2b + 1:
+// butterflies of stride 1, 2 and 4 stay in the thread, stride 8 pairs lanes l, l ^ 1 by a shuffle;
+// the operations and their order are the reference's (as in transform16), so the amax is
+// bit-identical to the stand-alone pass.
+// ------------------------------------------------------------------------------------------------
+namespace rb2 {
+namespace {
+__global__ void __launch_bounds__(256) gated_norm_amax_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              const __nv_bfloat16* __restrict__ z,
+                                                              const float* __restrict__ w, int64_t rows, float eps,
+                                                              int rot, __nv_bfloat16* __restrict__ y,
+                                                              float* __restrict__ rstd, unsigned int* __restrict__ gmax_bits) {
+  const int lane = threadIdx.x & 31, hl = lane & 15, jj = hl & 1;
+  float w8[8];
+  {
+    const float4 a = reinterpret_cast<const float4*>(w)[2 * hl], b = reinterpret_cast<const float4*>(w)[2 * hl + 1];
+    w8[0] = a.x; w8[1] = a.y; w8[2] = a.z; w8[3] = a.w; w8[4] = b.x; w8[5] = b.y; w8[6] = b.z; w8[7] = b.w;
+  }
+  // _SIGNS of elements 8 jj .. 8 jj + 7 of the block (negative at 2, 4, 5, 6, 12, 13, 15), bit t = element 8 jj + t
+  const uint32_t neg = jj ? 0xB0u : 0x74u;
+  float m = 0.f;
+  const int64_t warp = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5, nwarps = int64_t(gridDim.x) * 8;
+  for (int64_t row0 = warp * 4 + (lane >> 4); row0 - (lane >> 4) < rows; row0 += nwarps * 4) {
+    uint4 ux[2], uz[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t row = row0 + 2 * u;
+      ux[u] = row < rows ? reinterpret_cast<const uint4*>(x + row * 128)[hl] : make_uint4(0, 0, 0, 0);
+      uz[u] = row < rows ? reinterpret_cast<const uint4*>(z + row * 128)[hl] : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t row = row0 + 2 * u;
+      float x8[8], z8[8], v[8];
+      gn_unpack8(ux[u], x8);
+      gn_unpack8(uz[u], z8);
+      const float r = gated_norm8(x8, z8, w8, eps, v);
+      if (row < rows) {
+        reinterpret_cast<uint4*>(y + row * 128)[hl] = gn_pack8(v);
+        if (hl == 0 && rstd) rstd[row] = r;
+      }
+      if (rot) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = (neg >> t) & 1u ? -v[t] : v[t];
+#pragma unroll
+        for (int st = 1; st < 8; st <<= 1) {  // strides 1, 2, 4 inside the thread
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            if ((t & st) == 0) {
+              const float a = v[t], b = v[t + st];
+              v[t] = __fadd_rn(a, b);
+              v[t + st] = __fsub_rn(a, b);
+            }
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {  // stride 8: lanes l, l ^ 1; the lower lane keeps a + b
+          const float o = __shfl_xor_sync(0xffffffffu, v[t], 1);
+          v[t] = jj ? __fsub_rn(o, v[t]) : __fadd_rn(v[t], o);
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = gn_bf16_round(__fmul_rn(v[t], 0.25f));
+      }
+      if (row < rows) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) m = fmaxf(m, fabsf(v[t]));
+      }
+    }
+  }
+  m = warp_max(m);
+  __shared__ float red[8];
+  if (lane == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float q = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    q = warp_max(q);
+    if (threadIdx.x == 0 && q > 0.f) atomicMax(gmax_bits, __float_as_uint(q));
+  }
+}
+}  // namespace
+}  // namespace rb2
+
+extern "C" int rb2_gated_rmsnorm_nvfp4_fwd(const void* x, const void* z, const float* w, int64_t rows, int dim,
+                                           float eps, void* y, float* rstd, int64_t M, int64_t K, int use_rht,
+                                           uint8_t* codes, uint8_t* scales, uint8_t* scales_blocked, float* gscale,
+                                           void* ws, size_t ws_bytes, void* stream) {
+  RB2_CHECK_ARG(dim == 128, "gated_rmsnorm_nvfp4: row length must be 128 (got %d)", dim);
+  RB2_CHECK_ARG(rows > 0 && M > 0 && K > 0 && K % 16 == 0 && rows * 128 == M * K,
+                "gated_rmsnorm_nvfp4: rows x 128 must equal M x K with K %% 16 == 0 (rows=%lld M=%lld K=%lld)",
+                (long long)rows, (long long)M, (long long)K);
+  RB2_CHECK_ARG(M * (K / 16) < (int64_t(1) << 31), "gated_rmsnorm_nvfp4: more than 2^31 blocks of 16");
+  RB2_CHECK_ARG(x && z && w && y && rstd && codes && scales && gscale && ws, "gated_rmsnorm_nvfp4: null pointer");
+  RB2_CHECK_ARG(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) | reinterpret_cast<uintptr_t>(w) |
+                  reinterpret_cast<uintptr_t>(y)) & 15) == 0 && (reinterpret_cast<uintptr_t>(codes) & 7) == 0,
+                "gated_rmsnorm_nvfp4: x, z, w, y must be 16-byte and codes 8-byte aligned");
+  if (ws_bytes < rb2_nvfp4_quantize_workspace_size(M, K)) {
+    set_error("gated_rmsnorm_nvfp4: workspace too small");
+    return RB2_EWORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned int* gmax = static_cast<unsigned int*>(ws);
+  const int64_t n_blocks = M * (K / 16), groups = K / 16;
+  const Divider div = make_divider(uint32_t(groups));
+  const bool pads = scales_blocked && (M % 128 != 0 || groups % 4 != 0);
+  const size_t nb = size_t((M + 127) / 128) * size_t((groups + 3) / 4) * 512;
+  { ProfScope ps_("nvfp4_zero", s); zero_word_kernel<<<1, 1, 0, s>>>(gmax); }
+  RB2_CHECK_LAUNCH("gated_rmsnorm_nvfp4: zero");
+  if (pads) RB2_CUDA(cudaMemsetAsync(scales_blocked, 0, nb, s), "gated_rmsnorm_nvfp4: clear blocked pads");
+  int dev = 0, sms = 148;
+  RB2_CUDA(cudaGetDevice(&dev), "gated_rmsnorm_nvfp4: device");
+  RB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "gated_rmsnorm_nvfp4: SM count");
+  {
+    ProfScope ps_("block_gated_norm_amax", s);
+    const int64_t need = (rows + 31) / 32;  // 8 warps x 4 rows per CTA step
+    const unsigned g = unsigned(need < int64_t(sms) * 8 ? need : int64_t(sms) * 8);
+    gated_norm_amax_kernel<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z),
+                                             w, rows, eps, use_rht, static_cast<__nv_bfloat16*>(y), rstd, gmax);
+  }
+  RB2_CHECK_LAUNCH("gated_rmsnorm_nvfp4: norm + amax");
+  unsigned ga = 1, gq = 1;
+  sweep_grids<__nv_bfloat16>(sms, n_blocks, &ga, &gq);
+  {
+    ProfScope ps_("nvfp4_quant", s);
+    quant_kernel<__nv_bfloat16><<<gq, kThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(y), uint32_t(n_blocks),
+                                                        uint32_t(groups), div, use_rht, 0, 0, gmax, codes, scales,
+                                                        scales_blocked, gscale);
+  }
+  RB2_CHECK_LAUNCH("gated_rmsnorm_nvfp4: quantize");
   return RB2_OK;
 }
 

@@ -286,3 +286,62 @@ def test_block_with_fused_lora_epilogue():
     assert rel(outs[1], G["out"]) < BLOCK_TOL, rel(outs[1], G["out"])
     for n in grads[0]:
         assert rel(grads[1][n], grads[0][n]) < 2e-2, (n, rel(grads[1][n], grads[0][n]))
+
+
+@pytest.mark.parametrize("rht", [True, False])
+def test_gated_rmsnorm_quant_equals_norm_then_quantize(rht):
+    """The fused gated norm + NVFP4 quantize (rb2_gated_rmsnorm_nvfp4_fwd) gives bit-identical y, codes,
+    scales, blocked scales and global scale to the norm followed by the stand-alone quantizer, and the
+    same input gradients."""
+    from recant_b200 import block as BL
+    from recant_b200 import nvfp4 as N
+    gen = torch.Generator().manual_seed(11 + rht)
+    M, K = 300, 4096
+    x = (torch.randn(M * K // 128, 128, generator=gen) * 2).to(torch.bfloat16).cuda().requires_grad_(True)
+    z = torch.randn(M * K // 128, 128, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(128, generator=gen)).cuda()
+    y1, a1 = BL.gated_rmsnorm_quant(x, z, w, K, rht)
+    x2, z2 = x.detach().clone().requires_grad_(True), z.detach().clone().requires_grad_(True)
+    y2 = BL.gated_rmsnorm(x2, z2, w)
+    a2 = N.quantize_fast(y2.detach().reshape(M, K), rht, False)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert torch.equal(a1.codes, a2.codes) and torch.equal(a1.scales.view(torch.uint8), a2.scales.view(torch.uint8))
+    assert torch.equal(a1.blocked, a2.blocked) and torch.equal(a1.gscale, a2.gscale)
+    dy = torch.randn(y1.shape, generator=gen).to(torch.bfloat16).cuda()
+    y1.backward(dy)
+    y2.backward(dy)
+    assert torch.equal(x.grad, x2.grad) and torch.equal(z.grad, z2.grad)
+
+
+def test_block_with_and_without_norm_quant_fusion_agree():
+    """A block large enough for the fused norm + quantize path gives the same output and LoRA
+    gradients with the fusion switched off (the stand-alone norm and quantizer)."""
+    from recant_b200 import block as BL
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    blk = BL.GDNBlock(512, 2, 4).cuda()
+    for lin in blk.projections():
+        lin.load_weight(torch.randn(lin.out_features, lin.in_features, device="cuda", generator=gen) * 0.02)
+    for lin in (blk.in_proj_qkv, blk.in_proj_z, blk.out_proj):
+        lin.add_lora(16, 32, "cuda")
+        with torch.no_grad():
+            lin.lora_B.normal_(0, 0.01, generator=gen)
+    x = torch.randn(2, 600, 512, device="cuda", generator=gen).to(torch.bfloat16)
+    dy = torch.randn(2, 600, 512, device="cuda", generator=gen).to(torch.bfloat16)
+    outs, grads = [], []
+    for fuse in (True, False):
+        BL.FUSE_NORM_QUANT = fuse
+        try:
+            for p in blk.parameters():
+                p.grad = None
+            for lin in blk.projections():
+                lin.stochastic_backward = False
+            y = blk(x)
+            y.backward(dy)
+            outs.append(y.detach())
+            grads.append([blk.out_proj.lora_A.grad.clone(), blk.in_proj_qkv.lora_A.grad.clone()])
+        finally:
+            BL.FUSE_NORM_QUANT = True
+    assert torch.equal(outs[0], outs[1])
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
