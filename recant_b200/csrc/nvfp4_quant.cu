@@ -62,28 +62,45 @@ __device__ __forceinline__ void unpack16(const Raw16<__nv_bfloat16>& r, float v[
   }
 }
 
-// The 16-point randomized Hadamard transform of one block, with the reference's exact
-// operation order, followed by re-rounding to the input dtype.
+// Two butterflies at once: (a0, a1) <- (a0, a1) + (b0, b1), (b0, b1) <- (a0, a1) - (b0, b1) as paired
+// f32x2 operations (sm_100), each lane rounded exactly as the scalar add / sub.
+__device__ __forceinline__ void bfly2(float& a0, float& a1, float& b0, float& b1) {
+  unsigned long long a, b, sm, df;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(sm) : "l"(a), "l"(b));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(df) : "l"(a), "l"(b));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(sm));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(b0), "=f"(b1) : "l"(df));
+}
+__device__ __forceinline__ void mul2(float& a0, float& a1, float c) {
+  unsigned long long a, k, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(k) : "f"(c));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(k));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(r));
+}
+
+// The 16-point randomized Hadamard transform of one block with the reference's operations in the
+// reference's order (every element is the same chain of IEEE adds / subtracts as nvfp4.rht), the
+// butterflies paired two at a time; `reround`: round the result to the input dtype, as rht does.
 template <typename T>
-__device__ __forceinline__ void transform16(float v[16], bool rot) {
+__device__ __forceinline__ void transform16(float v[16], bool rot, bool reround = true) {
   if (rot) {
     // _SIGNS = [1,1,-1,1,-1,-1,-1,1,1,1,1,1,-1,-1,1,-1]
     v[2] = -v[2]; v[4] = -v[4]; v[5] = -v[5]; v[6] = -v[6];
     v[12] = -v[12]; v[13] = -v[13]; v[15] = -v[15];
 #pragma unroll
-    for (int s = 1; s < 16; s <<= 1) {
+    for (int i = 0; i < 16; i += 4) bfly2(v[i], v[i + 2], v[i + 1], v[i + 3]);  // stride 1: (i, i+1), (i+2, i+3)
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if ((i & s) == 0) {
-          float a = v[i], b = v[i + s];
-          v[i] = __fadd_rn(a, b);
-          v[i + s] = __fsub_rn(a, b);
-        }
-      }
+    for (int s = 2; s < 16; s <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 2)
+        if ((i & s) == 0) bfly2(v[i], v[i + 1], v[i + s], v[i + s + 1]);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], 0.25f);
-    if (sizeof(T) == 2) {  // one paired conversion per two elements
+    for (int i = 0; i < 16; i += 2) mul2(v[i], v[i + 1], 0.25f);
+    if (sizeof(T) == 2 && reround) {  // one paired conversion per two elements
 #pragma unroll
       for (int i = 0; i < 16; i += 2) {
         const __nv_bfloat162 h = __floats2bfloat162_rn(v[i], v[i + 1]);
@@ -113,11 +130,14 @@ amax_kernel(const T* __restrict__ x, int64_t n_blocks, int rot, unsigned int* __
     if (b + stride < n_blocks) load_raw(x + (b + stride) * 16, nxt);
     float v[16];
     unpack16(cur, v);
-    transform16<T>(v, rot != 0);
+    transform16<T>(v, rot != 0, false);
 #pragma unroll
     for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
     cur = nxt;
   }
+  // rht re-rounds to the input dtype; rounding to nearest is monotone and symmetric, so the max of
+  // the rounded magnitudes is the rounded max
+  if (sizeof(T) == 2 && rot) m = __bfloat162float(__float2bfloat16_rn(m));
   m = warp_max(m);
   __shared__ float red[kThreads / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
