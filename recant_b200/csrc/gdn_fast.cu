@@ -30,13 +30,12 @@ size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_ch
   w.ct.seq_chunk0 = c.take<int>(n_seqs + 1);
   w.ct.n_chunks = c.take<int>(1);
   w.err = c.take<int>(1);
-  w.stats = c.take<float>(nch * 256);
+  w.stats = c.take<float>(nch * 384);
   w.tinv = c.take<__nv_bfloat16>(nch * 4096);
   w.aqk = c.take<__nv_bfloat16>(nch * 4096);
   w.w = c.take<__nv_bfloat16>(nch * 8192);
   w.u = c.take<__nv_bfloat16>(nch * 8192);
   w.qt = c.take<__nv_bfloat16>(nch * 8192);
-  w.kt = c.take<__nv_bfloat16>(nch * 8192);
   w.hs = c.take<__nv_bfloat16>(nch * 16384);
   w.vp = c.take<__nv_bfloat16>(nch * 8192);
   return c.bytes();
@@ -195,8 +194,10 @@ __device__ void inverse_lower64_tc(float* lt, float* xbuf, unsigned char* ptile,
 // r = 32 (w & 3) + l, column half hh = w >> 2 (columns [32 hh, 32 hh + 32) of the 64-wide
 // accumulators). 128 TMEM columns: [K;Q] K^T in [0, 128) is read before the inverse's two products
 // and then U^T / W^T reuse them. Shared memory: the [K;Q] tile, whose Q rows (bytes [8K, 16K) and
-// [24K, 32K): rows 64-127 of both 64-column slabs) are free once q~ has been written and hold first
-// the inverse's operand tiles and then T beta and T beta e^cum r_k; V; L / T in place (fp32).
+// [24K, 32K): rows 64-127 of both 64-column slabs) are free once the [K;Q] K^T product is done and
+// hold first the inverse's operand tiles and then T beta and T beta e^cum r_k; V; L / T in place
+// (fp32). Only the backward walk takes a q~ tile; the forward walk reads the caller's q rows and both
+// walks the caller's k rows, with the per-token factors f_q, f_k kept in the stats.
 // ------------------------------------------------------------------------------------------------
 constexpr int kPrepSmem = 32768 + 16384 + 64 * 65 * 4 + 512 * 4 + 6 * 64 * 4 + 2048;
 
@@ -306,9 +307,14 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
   }
   __syncthreads();  // cum, rk, rq
   if (tid < 64) ecum[tid] = __expf(cum[tid]);
-  float* st = ws.stats + ch * 256;
-  if (tid < 64) { st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid]; }
-  // q~ rows now (the Q rows' shared memory is reused below): half-warp per row, 8 elements per lane
+  float* st = ws.stats + ch * 384;
+  if (tid < 64) {  // stats: cum, r_q, r_k, beta and the per-token factors f_q of q~ and f_k of k~
+    st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid];
+    st[256 + tid] = p.scale * rq[tid] * __expf(cum[tid]);
+    st[320 + tid] = __expf(cum[63] - cum[tid]) * rk[tid];
+  }
+  // q~ rows for the backward walk now (the Q rows' shared memory is reused below): half-warp per row,
+  // 8 elements per lane
   for (int row_ = w * 2 + (l >> 4); row_ < 64; row_ += 16) {
     const int c8 = (l & 15) * 8;
     const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(64 + row_, c8, 128));
@@ -391,17 +397,6 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
         make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
                    tc::pack_bf16(t[6], t[7]));
   }
-  // k~ rows while the MMAs run: half-warp per row, 8 elements per lane (warps 1-7)
-  for (int row_ = (w - 1) * 2 + (l >> 4); w > 0 && row_ < 64; row_ += 14) {
-    const int c8 = (l & 15) * 8;
-    const uint4 x = *reinterpret_cast<const uint4*>(kq + tc::sw128_offset(row_, c8, 128));
-    const float f = __expf(cum[63] - cum[row_]) * rk[row_];
-    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
-    *reinterpret_cast<uint4*>(img(ws.kt + ch * 8192) + tc::sw128_offset(row_, c8, 64)) = make_uint4(o[0], o[1], o[2], o[3]);
-  }
   tc::mbar_wait(&bar[1], 0, ws.err, 102);
   tc::fence_after_sync();
   {
@@ -421,16 +416,20 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
 // forward state walk: one CTA (256 threads) per (sequence, value head)
 //   thread (w, l): TMEM lane / dv row r = 32 (w & 3) + l, dk half hh = w >> 2
 // ------------------------------------------------------------------------------------------------
-constexpr int kStageBytes = 16384 * 4 + 8192 + 1024;  // W, q~, k~, U, A_qk, cum (1024-byte multiple)
-constexpr int kStateSmem = 32768 + 16384 + 2 * kStageBytes + 2048;
+constexpr int kStageBytes = 16384 * 4 + 8192 + 2048;  // W, q, k, U, A_qk, stats (1024-byte multiple)
+constexpr int kStateSmem = 32768 + 16384 + 16384 + 2 * kStageBytes + 2048;
 
+// The caller's q and k rows come by TMA and are used raw: q~ = f_q q and k~ = f_k k with per-token
+// f_q = scale r_q e^cum and f_k = r_k e^(cum_last - cum) (the prep's l2-norm and decay factors), so
+// S^T q~^T = (S^T q^T) diag(f_q) is scaled in the output epilogue and V'^T k~ = (V'^T diag(f_k)) k
+// takes a second, scaled V'^T tile.
 struct FwdStage {
   unsigned char* wt;   // W   64 rows (tok) x 128 (dk)        16 KB
-  unsigned char* qt;   // q~  64 x 128                         16 KB
-  unsigned char* kt;   // k~  64 x 128 (used MN-major: N = dk) 16 KB
+  unsigned char* qt;   // q   64 x 128 (the caller's rows)     16 KB
+  unsigned char* kt;   // k   64 x 128 (used MN-major: N = dk) 16 KB
   bf16* us;            // U plain [64][128]                    16 KB
   unsigned char* at;   // A_qk 64 (i) x 64 (j)                  8 KB
-  float* cum;          // 64 floats
+  float* cum;          // stats: cum, r_q, r_k, beta, f_q, f_k (64 floats each)
 };
 
 __device__ __forceinline__ FwdStage fwd_stage(unsigned char* base, int stg) {
@@ -445,33 +444,38 @@ __device__ __forceinline__ FwdStage fwd_stage(unsigned char* base, int stg) {
   return st;
 }
 
-// One thread: bulk copies of the chunk's tile images (and U, cum) into a stage, counted on `bar`.
-__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch, int walk, uint64_t* bar) {
-  const uint32_t bytes = 16384 * 2 + 256 + (walk == 0 ? 16384 + 8192 : 0) + (walk != 2 ? 16384 : 0);
+// One thread: the chunk's q, k rows by TMA and its workspace tile images (W, U, A_qk) and stats by
+// bulk copies into a stage, counted on `bar`.
+__device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, int64_t ch, int walk, int hk, int t0,
+                                          const CUtensorMap* map_q, const CUtensorMap* map_k, uint64_t* bar) {
+  const uint32_t bytes = 16384 * 2 + 1536 + (walk == 0 ? 16384 + 8192 : 0) + (walk != 2 ? 16384 : 0);
   tc::fence_proxy_async();  // the stage's previous generic reads are ordered before these writes
   tc::mbar_expect_tx(bar, bytes);
   tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
-  tc::bulk_load(st.kt, ws.kt + ch * 8192, 16384, bar);
-  if (walk == 0) {  // outputs need q~ and A_qk
-    tc::bulk_load(st.qt, ws.qt + ch * 8192, 16384, bar);
+  tc::tma_rows128(st.kt, 8192, 0, map_k, hk, t0, bar);
+  if (walk == 0) {  // outputs need q and A_qk
+    tc::tma_rows128(st.qt, 8192, 0, map_q, hk, t0, bar);
     tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
   }
   if (walk != 2) tc::bulk_load(st.us, ws.u + ch * 8192, 16384, bar);
-  tc::bulk_load(st.cum, ws.stats + ch * 256, 256, bar);
+  tc::bulk_load(st.cum, ws.stats + ch * 384, 1536, bar);
 }
 
 __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ o,
-                                                                 float* __restrict__ hT) {
+                                                                 float* __restrict__ hT,
+                                                                 const __grid_constant__ CUtensorMap map_q,
+                                                                 const __grid_constant__ CUtensorMap map_k) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* st = sm;                   // S^T bf16, K-major 128 rows (dv) x 128 (dk)   32 KB
   unsigned char* vpt = st + 32768;          // V'^T 128 rows (dv) x 64 (tok)                16 KB
-  unsigned char* stages = vpt + 16384;      // 2 x FwdStage
+  unsigned char* vpk = vpt + 16384;         // V'^T diag(f_k), the S update's operand      16 KB
+  unsigned char* stages = vpk + 16384;      // 2 x FwdStage
   __shared__ uint64_t bar[2];
   __shared__ uint64_t ldbar[2];   // stage loads
   __shared__ uint32_t tmem_base;
 
-  const int h = blockIdx.x, s = blockIdx.y;
+  const int h = blockIdx.x, s = blockIdx.y, hk = h / p.group;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int r = 32 * (w & 3) + l, hh = w >> 2;
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
@@ -482,7 +486,8 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     tc::mbar_init(&ldbar[0], 1);
     tc::mbar_init(&ldbar[1], 1);
     tc::fence_mbar_init();
-    if (c0 < c1) fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h, p.walk, &ldbar[0]);
+    if (c0 < c1)
+      fwd_issue(fwd_stage(stages, 0), ws, int64_t(c0) * p.Hv + h, p.walk, hk, ws.ct.tok0[c0], &map_q, &map_k, &ldbar[0]);
   }
   // S^T[r][dk] for dk in [64 hh, 64 hh + 64): S[dk][r] of the [dk][dv] state
   float S[64];
@@ -501,8 +506,14 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
     const int stg = (ci - c0) & 1;
     const FwdStage cur = fwd_stage(stages, stg);
-    if (tid == 0 && ci + 1 < c1) fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv, p.walk, &ldbar[stg ^ 1]);
+    if (tid == 0 && ci + 1 < c1)
+      fwd_issue(fwd_stage(stages, stg ^ 1), ws, ch + p.Hv, p.walk, hk, ws.ct.tok0[ci + 1], &map_q, &map_k,
+                &ldbar[stg ^ 1]);
     tc::mbar_wait(&ldbar[stg], ((ci - c0) >> 1) & 1, ws.err, 110);
+    if (L < 64) {  // the caller's rows past the end of the sequence (another sequence's, or the TMA fill)
+      tc::zero_rows_tail(cur.kt, 8192, 0, L, 256);
+      if (outs) tc::zero_rows_tail(cur.qt, 8192, 0, L, 256);
+    }
     // S^T (bf16) -> smem operand and -> workspace (state entering this chunk)
     {
       uint32_t pk[32];
@@ -518,7 +529,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {
-      // D_vp = S^T W^T (cols [0,64)), D_o = S^T q~^T (cols [64,128)): M=128, N=64, K=128
+      // D_vp = S^T W^T (cols [0,64)), D_o = S^T q^T (cols [64,128), scaled by f_q later): M=128, N=64, K=128
       const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
       const uint32_t sa = tc::smem_u32(st), wa = tc::smem_u32(cur.wt), qa = tc::smem_u32(cur.qt);
 #pragma unroll
@@ -553,20 +564,30 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
             make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+#pragma unroll
+      const float* fk = cur.cum + 320;  // f_k = r_k e^(cum_last - cum)
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j] * fk[32 * hh + j], x[j + 1] * fk[32 * hh + j + 1]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(vpk + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
+            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
     }
     tc::fence_proxy_async();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {
-      // D_o += V'^T A_qk^T (M=128, N=64, K=64); D_s = V'^T k~ (M=128, N=128, K=64, k~ MN-major)
-      const uint32_t va = tc::smem_u32(vpt), aa = tc::smem_u32(cur.at), ka = tc::smem_u32(cur.kt);
+      // D_o2 = V'^T A_qk^T (cols [128, 192); M=128, N=64, K=64); D_s = (V'^T diag(f_k)) k (M=128, N=128, K=64,
+      // k MN-major)
+      const uint32_t va = tc::smem_u32(vpt), vk = tc::smem_u32(vpk), aa = tc::smem_u32(cur.at), ka = tc::smem_u32(cur.kt);
       const uint32_t id_o = tc::idesc_bf16(128, 64, false, false);
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
 #pragma unroll
       for (int k0 = 0; k0 < 64; k0 += 16) {
-        if (outs) tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_kmajor_sw128(aa + k0 * 2), id_o, true);
-        tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_mnmajor_sw128(ka + k0 * 128, 8192), id_s,
+        if (outs)
+          tc::mma_bf16(tbase + 128, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_kmajor_sw128(aa + k0 * 2), id_o, k0 > 0);
+        tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(vk + k0 * 2), tc::desc_mnmajor_sw128(ka + k0 * 128, 8192), id_s,
                      k0 > 0);
       }
       tc::mma_commit(&bar[1]);
@@ -580,7 +601,12 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     float ox[32];  // o rows of this chunk, stored after the barrier below (stores ahead of a fence stall it)
     {
       float x[32];
-      if (outs) tc::tmem_ld32(lane_addr + 64 + 32 * hh, ox);
+      if (outs) {  // o^T = (S^T q^T) diag(f_q) + V'^T A_qk^T
+        tc::tmem_ld32(lane_addr + 64 + 32 * hh, ox);
+        tc::tmem_ld32(lane_addr + 128 + 32 * hh, x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ox[j] = fmaf(cur.cum[256 + 32 * hh + j], ox[j], x[j]);
+      }
       const float gamma = expf(cur.cum[63]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -656,7 +682,10 @@ int fast_forward(const GdnProblem& p, void* wsp, void* o, float* hT, cudaStream_
   if ((rc = smem_attr(fast_state_fwd_kernel, kStateSmem))) return rc;
   {
     ProfScope ps_("gdn_fast_state_fwd", s);
-    fast_state_fwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kStateSmem, s>>>(p, w, static_cast<bf16*>(o), hT);
+    CUtensorMap mq, mk;
+    if ((rc = make_rows_map(&mq, p.q, p.tokens, p.Hk)) || (rc = make_rows_map(&mk, p.k, p.tokens, p.Hk))) return rc;
+    fast_state_fwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kStateSmem, s>>>(p, w, static_cast<bf16*>(o), hT, mq,
+                                                                                    mk);
     RB2_CHECK_LAUNCH("gdn fast state fwd");
   }
   return check_err_word(w, s, false);

@@ -8,13 +8,12 @@ namespace rb2 {
 
 struct FastWs {
   ChunkTable ct;
-  float* stats;          // [ch][4][64] cum, rq, rk, beta
+  float* stats;          // [ch][6][64] cum, rq, rk, beta, f_q = scale rq e^cum, f_k = rk e^(cl - cum)
   __nv_bfloat16* tinv;   // [ch][64][64]   T = (I + L)^-1                      (tile image)
   __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal (image)
   __nv_bfloat16* w;      // [ch][64][128]                                      (tile image)
   __nv_bfloat16* u;      // [ch][64][128]   plain row-major
-  __nv_bfloat16* qt;     // [ch][64][128]  q~ = scale rq e^cum q           (tile image)
-  __nv_bfloat16* kt;     // [ch][64][128]  k~ = e^(cl - cum) rk k          (tile image)
+  __nv_bfloat16* qt;     // [ch][64][128]  q~ = f_q q, for the backward walk (tile image)
   __nv_bfloat16* hs;     // [ch][128][128] S^T entering the chunk, [dv][dk] (tile image)
   __nv_bfloat16* vp;     // [ch][128][64]  V'^T [dv][tok] (tile image)
   __nv_bfloat16* dh;     // [ch][128][128] dS^T of the state leaving the chunk, [dv][dk] (image)

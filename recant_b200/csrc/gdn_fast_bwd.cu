@@ -36,16 +36,19 @@ __device__ __forceinline__ void sync_for_mma() {
 // ------------------------------------------------------------------------------------------------
 // reversed state walk: one CTA (256 threads) per (sequence, value head); thread = (dv row, dk half)
 // ------------------------------------------------------------------------------------------------
-constexpr int kBStageBytes = 16384 * 4 + 8192 + 1024;  // dO, k~, q~, W, A_qk, cum (1024-byte multiple)
+constexpr int kBStageBytes = 16384 * 4 + 8192 + 2048;  // dO, k, q~, W, A_qk, stats (1024-byte multiple)
 constexpr int kBStateSmem = 32768 + 16384 + 2 * kBStageBytes + 2048;
 
+// The caller's k rows are used raw, as in the forward walk: dS^T k~^T = (dS^T k^T) diag(f_k) is scaled
+// in the dV' epilogue with the prep's f_k; q~ comes from the prep as a tile image (scaling dO instead
+// would put a pass over it on the walk's critical path).
 struct BwdStage {
   unsigned char* dot;  // dO rows tok (64) x dv
-  unsigned char* kt;   // k~ rows tok x dk
-  unsigned char* qt;   // q~
+  unsigned char* kt;   // k rows tok x dk (the caller's)
+  unsigned char* qt;   // q~ rows (tile image)
   unsigned char* wt;   // W
   unsigned char* at;   // A_qk rows i x c
-  float* cum;
+  float* cum;          // stats: cum, r_q, r_k, beta, f_q, f_k
 };
 
 __device__ __forceinline__ BwdStage bwd_stage(unsigned char* base, int stg) {
@@ -60,26 +63,28 @@ __device__ __forceinline__ BwdStage bwd_stage(unsigned char* base, int stg) {
   return st;
 }
 
-// Thread 0: the chunk's dO rows by TMA (rows past the sequence are zeroed after the wait) and the
-// workspace tile images (k~, q~, W, A_qk, cum) by bulk copies, counted on `bar`.
+// Thread 0: the chunk's dO and k rows by TMA (rows past the sequence are zeroed after the wait)
+// and the workspace tile images (q~, W, A_qk) and stats by bulk copies, counted on `bar`.
 __device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& p, const FastWs& ws,
-                                          const CUtensorMap* map_do, int ci, int h, uint64_t* bar) {
+                                          const CUtensorMap* map_do, const CUtensorMap* map_k, int ci, int h,
+                                          uint64_t* bar) {
   const int64_t ch = int64_t(ci) * p.Hv + h;
-  const int t0 = ws.ct.tok0[ci];
+  const int t0 = ws.ct.tok0[ci], hk = h / p.group;
   if (threadIdx.x == 0) {
     tc::fence_proxy_async();
-    tc::mbar_expect_tx(bar, 4 * 16384 + 8192 + 256);
+    tc::mbar_expect_tx(bar, 4 * 16384 + 8192 + 1536);
     tc::tma_rows128(st.dot, 8192, 0, map_do, h, t0, bar);
-    tc::bulk_load(st.kt, ws.kt + ch * 8192, 16384, bar);
+    tc::tma_rows128(st.kt, 8192, 0, map_k, hk, t0, bar);
     tc::bulk_load(st.qt, ws.qt + ch * 8192, 16384, bar);
     tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
     tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
-    tc::bulk_load(st.cum, ws.stats + ch * 256, 256, bar);
+    tc::bulk_load(st.cum, ws.stats + ch * 384, 1536, bar);
   }
 }
 
 __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, FastWs ws, const __grid_constant__ CUtensorMap map_do,
-                                                                 const float* __restrict__ dhT, float* __restrict__ dh0) {
+                                                                 const float* __restrict__ dhT, float* __restrict__ dh0,
+                                                                 const __grid_constant__ CUtensorMap map_k) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   unsigned char* dst = sm;              // dS^T bf16, rows dv (128) x dk               32 KB
@@ -101,7 +106,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     tc::fence_mbar_init();
   }
   const int c0 = ws.ct.seq_chunk0[s], c1 = ws.ct.seq_chunk0[s + 1];
-  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, &map_do, c1 - 1, h, &ldbar[0]);
+  if (c0 < c1) bwd_issue(bwd_stage(stages, 0), p, ws, &map_do, &map_k, c1 - 1, h, &ldbar[0]);
   float dS[64];
   const int64_t sbase = (int64_t(s) * p.Hv + h) * 16384;
 #pragma unroll
@@ -115,10 +120,13 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     const int64_t ch = int64_t(ci) * p.Hv + h;
     const int stg = (c1 - 1 - ci) & 1;
     const BwdStage cur = bwd_stage(stages, stg);
-    if (ci - 1 >= c0) bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, &map_do, ci - 1, h, &ldbar[stg ^ 1]);
+    if (ci - 1 >= c0) bwd_issue(bwd_stage(stages, stg ^ 1), p, ws, &map_do, &map_k, ci - 1, h, &ldbar[stg ^ 1]);
     tc::mbar_wait(&ldbar[stg], ((c1 - 1 - ci) >> 1) & 1, ws.err, 120);
     const int Lc = ws.ct.len[ci];
-    if (Lc < 64) tc::zero_rows_tail(cur.dot, 8192, 0, Lc, 256);  // dO rows past the sequence
+    if (Lc < 64) {  // dO and k rows past the sequence
+      tc::zero_rows_tail(cur.dot, 8192, 0, Lc, 256);
+      tc::zero_rows_tail(cur.kt, 8192, 0, Lc, 256);
+    }
     {
       uint32_t pk[32];
 #pragma unroll
@@ -139,12 +147,13 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       for (int k0 = 0; k0 < 64; k0 += 16)
         tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(doa + k0 * 128, 8192), tc::desc_mnmajor_sw128(aa + k0 * 128, 8192),
                      id_a, k0 > 0);
-      // dV'^T += dS^T k~^T (A = dS^T K-major: M = dv, K = dk; B = k~ K-major: N = tok, K = dk)
+      // D_k = dS^T k^T into columns [64, 128), scaled by f_k in the epilogue (A = dS^T K-major: M = dv,
+      // K = dk; B = k K-major: N = tok, K = dk)
       const uint32_t id_b = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16)
-        tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(da + (k0 >> 6) * 16384 + (k0 & 63) * 2),
-                     tc::desc_kmajor_sw128(ka + (k0 >> 6) * 8192 + (k0 & 63) * 2), id_b, true);
+        tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(da + (k0 >> 6) * 16384 + (k0 & 63) * 2),
+                     tc::desc_kmajor_sw128(ka + (k0 >> 6) * 8192 + (k0 & 63) * 2), id_b, k0 > 0);
       // D_s = dO^T q~ (A = dO MN-major; B = q~ MN-major: N = dk, K = tok)
       const uint32_t id_s = tc::idesc_bf16(128, 128, true, true);
 #pragma unroll
@@ -160,8 +169,12 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     tc::mbar_wait(&bar[0], phase, ws.err, 121);
     tc::fence_after_sync();
     {
-      float x[32];
+      float x[32], xk[32];  // dV'^T = dO^T A_qk + (dS^T k^T) diag(f_k)
       tc::tmem_ld32(lane_addr + 32 * hh, x);
+      tc::tmem_ld32(lane_addr + 64 + 32 * hh, xk);
+      const float* fk = cur.cum + 320;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = fmaf(fk[32 * hh + j], xk[j], x[j]);
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
@@ -348,7 +361,7 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
     tc::bulk_load(sm + lay::VPT, ws.vp + ch_ * 8192, 16384, &ldbar[0]);
     tc::tma_rows128(sm + lay::VT, 8192, 0, &map_v, h_, t0_, &ldbar[0]);
     tc::tma_rows128(sm + lay::DOT, 8192, 0, &map_do, h_, t0_, &ldbar[0]);
-    tc::bulk_load(sm + lay::STATS, ws.stats + ch_ * 256, 1024, &ldbar[0]);
+    tc::bulk_load(sm + lay::STATS, ws.stats + ch_ * 384, 1024, &ldbar[0]);
   };
   // [K;Q] rows of one (chunk, key head) by TMA on ldbar[2]. The value heads of a group share them,
   // so they are fetched only when the (chunk, key head) changes, during the previous item's final
@@ -786,7 +799,9 @@ int fast_backward(const GdnProblem& p, void* wsp, void* scratch, const void* d_o
     ProfScope ps_("gdn_fast_state_bwd", s);
     CUtensorMap mdo;
     if ((rc = make_rows_map(&mdo, d_o, p.tokens, p.Hv))) return rc;
-    fast_state_bwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kBStateSmem, s>>>(p, w, mdo, dhT, dh0);
+    CUtensorMap mk;
+    if ((rc = make_rows_map(&mk, p.k, p.tokens, p.Hk))) return rc;
+    fast_state_bwd_kernel<<<dim3(p.Hv, unsigned(p.n_seqs)), 256, kBStateSmem, s>>>(p, w, mdo, dhT, dh0, mk);
     RB2_CHECK_LAUNCH("gdn fast state bwd");
   }
   if ((p.stages & 2) && p.max_chunks > 0) {
