@@ -140,10 +140,9 @@ __device__ void inverse_lower64_tc(float* lt, float* xbuf, unsigned char* ptile,
   const uint32_t pa = tc::smem_u32(ptile), da = tc::smem_u32(dtile);
   const uint32_t idesc = tc::idesc_bf16(64, 64, false, true);  // A = P K-major (rows i), B row-major (MN-major)
   if (tid == 0) {
+    const uint64_t d_p = tc::desc_kmajor_sw128(pa), d_d = tc::desc_mnmajor_sw128(da, 8192);
 #pragma unroll 1
-    for (int k0 = 0; k0 < 64; k0 += 16)
-      tc::mma_bf16(tbase + tcol, tc::desc_kmajor_sw128(pa + k0 * 2), tc::desc_mnmajor_sw128(da + k0 * 128, 8192), idesc,
-                   k0 > 0);
+    for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + tcol, d_p + (k0 >> 3), d_d + k0 * 8, idesc, k0 > 0);
     tc::mma_commit(&bars[0]);
   }
   tc::mbar_wait(&bars[0], 0, err, 103);
@@ -168,10 +167,9 @@ __device__ void inverse_lower64_tc(float* lt, float* xbuf, unsigned char* ptile,
   __syncthreads();
   tc::fence_after_sync();
   if (tid == 0) {
+    const uint64_t d_p = tc::desc_kmajor_sw128(pa), d_d = tc::desc_mnmajor_sw128(da, 8192);
 #pragma unroll 1
-    for (int k0 = 0; k0 < 64; k0 += 16)
-      tc::mma_bf16(tbase + tcol + 64, tc::desc_kmajor_sw128(pa + k0 * 2), tc::desc_mnmajor_sw128(da + k0 * 128, 8192),
-                   idesc, k0 > 0);
+    for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + tcol + 64, d_p + (k0 >> 3), d_d + k0 * 8, idesc, k0 > 0);
     tc::mma_commit(&bars[1]);
   }
   tc::mbar_wait(&bars[1], 0, err, 104);
@@ -258,12 +256,12 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * (w & 3)) << 16) + c0;
   if (tid == 0) {  // [K;Q][K;Q]^T: M=128, N=128, K=128 -> TMEM cols [0, 128)
-    const uint32_t a0 = tc::smem_u32(kq);
+    const uint64_t d_kq = tc::desc_kmajor_sw128(tc::smem_u32(kq));
     const uint32_t idesc = tc::idesc_bf16(128, 128, false, false);
 #pragma unroll
     for (int k0 = 0; k0 < 128; k0 += 16) {
-      const uint32_t off = (k0 >> 6) * 16384 + (k0 & 63) * 2;
-      tc::mma_bf16(tbase, tc::desc_kmajor_sw128(a0 + off), tc::desc_kmajor_sw128(a0 + off), idesc, k0 > 0);
+      const uint32_t off = ((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4;
+      tc::mma_bf16(tbase, d_kq + off, d_kq + off, idesc, k0 > 0);
     }
     tc::mma_commit(&bar[0]);
   }
@@ -373,11 +371,12 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
     // U^T = V^T (T beta)^T: A = V as MN-major (M = dv, K = tok), B = tb1 K-major (N = 64, K = 64)
     // W^T = K^T (T beta e^cum rk)^T: A = rows 0-63 of [K;Q] as MN-major (slab stride 16 KB)
     const uint32_t idesc = tc::idesc_bf16(128, 64, true, false);
-    const uint32_t va = tc::smem_u32(vt), ka = tc::smem_u32(kq), b1 = tc::smem_u32(tb1), b2 = tc::smem_u32(tb2);
+    const uint64_t d_v = tc::desc_mnmajor_sw128(tc::smem_u32(vt), 8192), d_k = tc::desc_mnmajor_sw128(tc::smem_u32(kq), 16384),
+                   d_1 = tc::desc_kmajor_sw128(tc::smem_u32(tb1)), d_2 = tc::desc_kmajor_sw128(tc::smem_u32(tb2));
 #pragma unroll
     for (int k0 = 0; k0 < 64; k0 += 16) {
-      tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(va + k0 * 128, 8192), tc::desc_kmajor_sw128(b1 + k0 * 2), idesc, k0 > 0);
-      tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(ka + k0 * 128, 16384), tc::desc_kmajor_sw128(b2 + k0 * 2), idesc, k0 > 0);
+      tc::mma_bf16(tbase + 0, d_v + k0 * 8, d_1 + (k0 >> 3), idesc, k0 > 0);
+      tc::mma_bf16(tbase + 64, d_k + k0 * 8, d_2 + (k0 >> 3), idesc, k0 > 0);
     }
     tc::mma_commit(&bar[1]);
   }
@@ -531,12 +530,13 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     if (tid == 0) {
       // D_vp = S^T W^T (cols [0,64)), D_o = S^T q^T (cols [64,128), scaled by f_q later): M=128, N=64, K=128
       const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
-      const uint32_t sa = tc::smem_u32(st), wa = tc::smem_u32(cur.wt), qa = tc::smem_u32(cur.qt);
+      const uint64_t d_s = tc::desc_kmajor_sw128(tc::smem_u32(st)), d_w = tc::desc_kmajor_sw128(tc::smem_u32(cur.wt)),
+                     d_q = tc::desc_kmajor_sw128(tc::smem_u32(cur.qt));
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16) {
-        const uint32_t aoff = (k0 >> 6) * 16384 + (k0 & 63) * 2, boff = (k0 >> 6) * 8192 + (k0 & 63) * 2;
-        tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(wa + boff), idesc, k0 > 0);
-        if (outs) tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(sa + aoff), tc::desc_kmajor_sw128(qa + boff), idesc, k0 > 0);
+        const uint32_t aoff = ((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4, boff = ((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4;
+        tc::mma_bf16(tbase + 0, d_s + aoff, d_w + boff, idesc, k0 > 0);
+        if (outs) tc::mma_bf16(tbase + 64, d_s + aoff, d_q + boff, idesc, k0 > 0);
       }
       tc::mma_commit(&bar[0]);
       if (outs) {  // the state entering the chunk: the S^T tile is its workspace image
@@ -580,15 +580,14 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     if (tid == 0) {
       // D_o2 = V'^T A_qk^T (cols [128, 192); M=128, N=64, K=64); D_s = (V'^T diag(f_k)) k (M=128, N=128, K=64,
       // k MN-major)
-      const uint32_t va = tc::smem_u32(vpt), vk = tc::smem_u32(vpk), aa = tc::smem_u32(cur.at), ka = tc::smem_u32(cur.kt);
+      const uint64_t d_v = tc::desc_kmajor_sw128(tc::smem_u32(vpt)), d_vk = tc::desc_kmajor_sw128(tc::smem_u32(vpk)),
+                     d_a = tc::desc_kmajor_sw128(tc::smem_u32(cur.at)), d_k = tc::desc_mnmajor_sw128(tc::smem_u32(cur.kt), 8192);
       const uint32_t id_o = tc::idesc_bf16(128, 64, false, false);
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
 #pragma unroll
       for (int k0 = 0; k0 < 64; k0 += 16) {
-        if (outs)
-          tc::mma_bf16(tbase + 128, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_kmajor_sw128(aa + k0 * 2), id_o, k0 > 0);
-        tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(vk + k0 * 2), tc::desc_mnmajor_sw128(ka + k0 * 128, 8192), id_s,
-                     k0 > 0);
+        if (outs) tc::mma_bf16(tbase + 128, d_v + (k0 >> 3), d_a + (k0 >> 3), id_o, k0 > 0);
+        tc::mma_bf16(tbase + 256, d_vk + (k0 >> 3), d_k + k0 * 8, id_s, k0 > 0);
       }
       tc::mma_commit(&bar[1]);
       if (outs) {  // V'^T [dv][tok]: the tile is the workspace image

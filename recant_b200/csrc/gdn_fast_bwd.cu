@@ -139,27 +139,25 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     }
     sync_for_mma();
     if (tid == 0) {
-      const uint32_t doa = tc::smem_u32(cur.dot), aa = tc::smem_u32(cur.at), da = tc::smem_u32(dst),
-                     ka = tc::smem_u32(cur.kt), qa = tc::smem_u32(cur.qt);
+      const uint64_t d_do = tc::desc_mnmajor_sw128(tc::smem_u32(cur.dot), 8192),
+                     d_a = tc::desc_mnmajor_sw128(tc::smem_u32(cur.at), 8192), d_ds = tc::desc_kmajor_sw128(tc::smem_u32(dst)),
+                     d_k = tc::desc_kmajor_sw128(tc::smem_u32(cur.kt)),
+                     d_q = tc::desc_mnmajor_sw128(tc::smem_u32(cur.qt), 8192);
       // dV'^T = dO^T A_qk (A = dO MN-major: M = dv, K = tok; B = A_qk MN-major: N = c, K = i)
       const uint32_t id_a = tc::idesc_bf16(128, 64, true, true);
 #pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16)
-        tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(doa + k0 * 128, 8192), tc::desc_mnmajor_sw128(aa + k0 * 128, 8192),
-                     id_a, k0 > 0);
+      for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + 0, d_do + k0 * 8, d_a + k0 * 8, id_a, k0 > 0);
       // D_k = dS^T k^T into columns [64, 128), scaled by f_k in the epilogue (A = dS^T K-major: M = dv,
       // K = dk; B = k K-major: N = tok, K = dk)
       const uint32_t id_b = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16)
-        tc::mma_bf16(tbase + 64, tc::desc_kmajor_sw128(da + (k0 >> 6) * 16384 + (k0 & 63) * 2),
-                     tc::desc_kmajor_sw128(ka + (k0 >> 6) * 8192 + (k0 & 63) * 2), id_b, k0 > 0);
+        tc::mma_bf16(tbase + 64, d_ds + (((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4),
+                       d_k + (((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4), id_b, k0 > 0);
       // D_s = dO^T q~ (A = dO MN-major; B = q~ MN-major: N = dk, K = tok)
       const uint32_t id_s = tc::idesc_bf16(128, 128, true, true);
 #pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16)
-        tc::mma_bf16(tbase + 256, tc::desc_mnmajor_sw128(doa + k0 * 128, 8192), tc::desc_mnmajor_sw128(qa + k0 * 128, 8192),
-                     id_s, k0 > 0);
+      for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + 256, d_do + k0 * 8, d_q + k0 * 8, id_s, k0 > 0);
       tc::mma_commit(&bar[0]);
       if (p.walk == 0) {  // the gradient of the state leaving the chunk: the dS^T tile is its image
         tc::bulk_store(ws.dh + ch * 16384, dst, 32768);
@@ -186,11 +184,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
     sync_for_mma();
     if (tid == 0) {
       // D_s -= dV'^T W (A = dV'^T K-major: M = dv, K = tok, negated; B = W MN-major: N = dk, K = tok)
-      const uint32_t va = tc::smem_u32(dvt), wa = tc::smem_u32(cur.wt);
+      const uint64_t d_v = tc::desc_kmajor_sw128(tc::smem_u32(dvt)), d_w = tc::desc_mnmajor_sw128(tc::smem_u32(cur.wt), 8192);
       const uint32_t id_w = tc::idesc_bf16(128, 128, false, true, true);
 #pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16)
-        tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(va + k0 * 2), tc::desc_mnmajor_sw128(wa + k0 * 128, 8192), id_w, true);
+      for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + 256, d_v + (k0 >> 3), d_w + k0 * 8, id_w, true);
       tc::mma_commit(&bar[1]);
       if (p.walk == 0) {  // dV'^T [dv][tok]: the tile is the workspace image
         tc::bulk_store(ws.dvp + ch * 8192, dvt, 16384);
@@ -417,9 +414,12 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   }
   sync_for_mma();
   if (tid == 0) {  // ---- G1 ----
-    const uint32_t sta = tc::smem_u32(sm + lay::ST), dha = tc::smem_u32(sm + lay::DHT), doa = tc::smem_u32(sm + lay::DOT),
-                   vpa = tc::smem_u32(sm + lay::VPT), dva = tc::smem_u32(sm + lay::DVP);
     // V'^T and dV'^T arrive as [dv][tok] tiles: read MN-major as the N = tok operand
+    const uint64_t d_kq = tc::desc_kmajor_sw128(kqa), d_s = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::ST), 16384),
+                   d_dh = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::DHT), 16384),
+                   d_do = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::DOT)),
+                   d_vp = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::VPT), 8192),
+                   d_dv = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::DVP), 8192);
     const uint32_t id_kk = tc::idesc_bf16(128, 64, false, false);
     const uint32_t id_s = tc::idesc_bf16(128, 64, true, false);
     const uint32_t id_ss = tc::idesc_bf16(128, 64, true, true);
@@ -427,15 +427,16 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
     const uint32_t id_64 = tc::idesc_bf16(64, 64, false, true);
 #pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 128; k0 += 16) {
-      const uint32_t o16 = (k0 >> 6) * 16384 + (k0 & 63) * 2, o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
+      // descriptor address fields advance in 16-byte units: K-major by the k offset within the slab,
+      // MN-major by k0 rows of 128 bytes
+      const uint32_t o16 = ((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4, o8 = ((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4,
+                     om = k0 * 8;
       const bool acc = k0 > 0;
-      tc::mma_bf16(tbase + 0, tc::desc_kmajor_sw128(kqa + o16), tc::desc_kmajor_sw128(kqa + o16), id_kk, acc);
-      tc::mma_bf16(tbase + 64, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_kmajor_sw128(doa + o8), id_s, acc);
-      tc::mma_bf16(tbase + 128, tc::desc_mnmajor_sw128(sta + k0 * 128, 16384), tc::desc_mnmajor_sw128(dva + k0 * 128, 8192),
-                   id_sn, acc);
-      tc::mma_bf16(tbase + 192, tc::desc_mnmajor_sw128(dha + k0 * 128, 16384), tc::desc_mnmajor_sw128(vpa + k0 * 128, 8192),
-                   id_ss, acc);
-      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(doa + o8), tc::desc_mnmajor_sw128(vpa + k0 * 128, 8192), id_64, acc);
+      tc::mma_bf16(tbase + 0, d_kq + o16, d_kq + o16, id_kk, acc);
+      tc::mma_bf16(tbase + 64, d_s + om, d_do + o8, id_s, acc);
+      tc::mma_bf16(tbase + 128, d_s + om, d_dv + om, id_sn, acc);
+      tc::mma_bf16(tbase + 192, d_dh + om, d_vp + om, id_ss, acc);
+      tc::mma_bf16(tbase + 256, d_do + o8, d_vp + om, id_64, acc);
     }
     tc::mma_commit(&bar[0]);
   }
@@ -499,26 +500,23 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   tc::mbar_wait(&ldbar[1], ph, ws.err, 136);
   const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
   if (tid == 0) {  // ---- G2 ----
-    const uint32_t dva = tc::smem_u32(sm + lay::DVP), bva = tc::smem_u32(sm + lay::BV), bka = tc::smem_u32(sm + lay::BK);
-    const uint32_t id_t1 = tc::idesc_bf16(64, 64, true, false), id_t2 = tc::idesc_bf16(64, 64, true, false);
-#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
-    for (int k0 = 0; k0 < 128; k0 += 16) {  // dT = dV' (beta V)^T, dV' read MN-major from the dV'^T tile
-      const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
-      tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dva + k0 * 128, 8192), tc::desc_kmajor_sw128(bva + o8), id_t1,
-                   k0 > 0);
-    }
-#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
-    for (int k0 = 0; k0 < 128; k0 += 16) {
-      const uint32_t o8 = (k0 >> 6) * 8192 + (k0 & 63) * 2;
-      tc::mma_bf16(tbase + 320, tc::desc_mnmajor_sw128(dwa + k0 * 128, 16384), tc::desc_kmajor_sw128(bka + o8), id_t2, true);
-    }
-    const uint32_t id_bv = tc::idesc_bf16(128, 64, false, true), id_bk = tc::idesc_bf16(128, 64, false, true);
-#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
-    for (int k0 = 0; k0 < 64; k0 += 16) {
-      tc::mma_bf16(tbase + 128, tc::desc_kmajor_sw128(dva + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bv,
-                   k0 > 0);
-      tc::mma_bf16(tbase + 256, tc::desc_kmajor_sw128(dwa + k0 * 2), tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), id_bk,
-                   k0 > 0);
+    const uint32_t dva = tc::smem_u32(sm + lay::DVP);
+    const uint64_t d_dvm = tc::desc_mnmajor_sw128(dva, 8192), d_dwm = tc::desc_mnmajor_sw128(dwa, 16384),
+                   d_bv = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::BV)),
+                   d_bk = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::BK));
+    const uint32_t id_t = tc::idesc_bf16(64, 64, true, false);
+#pragma unroll 4
+    for (int k0 = 0; k0 < 128; k0 += 16)  // dT = dV' (beta V)^T, dV' read MN-major from the dV'^T tile
+      tc::mma_bf16(tbase + 320, d_dvm + k0 * 8, d_bv + (((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4), id_t, k0 > 0);
+#pragma unroll 4
+    for (int k0 = 0; k0 < 128; k0 += 16)  // dT += dW (beta e^cum r_k K)^T
+      tc::mma_bf16(tbase + 320, d_dwm + k0 * 8, d_bk + (((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4), id_t, true);
+    const uint64_t d_dvk = tc::desc_kmajor_sw128(dva), d_dwk = tc::desc_kmajor_sw128(dwa), d_t = tc::desc_mnmajor_sw128(tta, 8192);
+    const uint32_t id_b = tc::idesc_bf16(128, 64, false, true);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16) {  // dBv^T = dV'^T T, dBk^T = dW^T T
+      tc::mma_bf16(tbase + 128, d_dvk + (k0 >> 3), d_t + k0 * 8, id_b, k0 > 0);
+      tc::mma_bf16(tbase + 256, d_dwk + (k0 >> 3), d_t + k0 * 8, id_b, k0 > 0);
     }
     tc::mma_commit(&bar[1]);
   }
@@ -549,12 +547,10 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   if (tid < 64) dbeta_acc[tid] += red[tid] + red[64 + tid] + red[128 + tid] + red[192 + tid];
   sync_for_mma();
   if (tid == 0) {  // ---- G3: Y = T^T dT ----
-    const uint32_t dta = tc::smem_u32(sm + lay::DTT);
+    const uint64_t d_t = tc::desc_mnmajor_sw128(tta, 8192), d_dt = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::DTT), 8192);
     const uint32_t id_y = tc::idesc_bf16(64, 64, true, true);
-#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
-    for (int k0 = 0; k0 < 64; k0 += 16)
-      tc::mma_bf16(tbase + 0, tc::desc_mnmajor_sw128(tta + k0 * 128, 8192), tc::desc_mnmajor_sw128(dta + k0 * 128, 8192),
-                   id_y, k0 > 0);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + 0, d_t + k0 * 8, d_dt + k0 * 8, id_y, k0 > 0);
     tc::mma_commit(&bar[2]);
   }
   tc::mbar_wait(&bar[2], ph, ws.err, 133);
@@ -569,11 +565,10 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   }
   sync_for_mma();
   if (tid == 0) {  // ---- G4: dL' = Y T^T ----
-    const uint32_t ya = tc::smem_u32(sm + lay::YT);
+    const uint64_t d_y = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::YT)), d_t = tc::desc_kmajor_sw128(tta);
     const uint32_t id_l = tc::idesc_bf16(128, 64, false, false);
-#pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
-    for (int k0 = 0; k0 < 64; k0 += 16)
-      tc::mma_bf16(tbase + 128, tc::desc_kmajor_sw128(ya + k0 * 2), tc::desc_kmajor_sw128(tta + k0 * 2), id_l, k0 > 0);
+#pragma unroll
+    for (int k0 = 0; k0 < 64; k0 += 16) tc::mma_bf16(tbase + 128, d_y + (k0 >> 3), d_t + (k0 >> 3), id_l, k0 > 0);
     tc::mma_commit(&bar[3]);
   }
   tc::mbar_wait(&bar[3], ph, ws.err, 134);
@@ -614,17 +609,19 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   copy_rows_out(dv + (int64_t(t0) * p.Hv + h) * 128, int64_t(p.Hv) * 256, sm + lay::DVS, 256, L, kBThreads / 2,
                 kBThreads / 2);
   if (tid == 0) {  // ---- G5 ----
-    const uint32_t p1 = tc::smem_u32(sm + lay::PB1), p2 = tc::smem_u32(sm + lay::PB2), q1 = tc::smem_u32(sm + lay::QB1),
-                   q2 = tc::smem_u32(sm + lay::QB2);
+    const uint64_t d_k = tc::desc_mnmajor_sw128(kqa, 16384),         // K rows as (M = dk, K = j)
+        d_q = tc::desc_mnmajor_sw128(kqa + 8192, 16384),              // Q rows (start at row 64)
+        d_p1 = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::PB1)), d_q1 = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::QB1)),
+                   d_p2 = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::PB2), 8192),
+                   d_q2 = tc::desc_mnmajor_sw128(tc::smem_u32(sm + lay::QB2), 8192);
     const uint32_t id_k = tc::idesc_bf16(128, 64, true, false), id_m = tc::idesc_bf16(128, 64, true, true);
 #pragma unroll 1  // issue loops stay rolled: the kernel is larger than the instruction cache
     for (int k0 = 0; k0 < 64; k0 += 16) {
-      const uint64_t ka = tc::desc_mnmajor_sw128(kqa + k0 * 128, 16384);         // K rows as (M = dk, K = j)
-      const uint64_t qa = tc::desc_mnmajor_sw128(kqa + 8192 + k0 * 128, 16384);  // Q rows (start at row 64)
-      tc::mma_bf16(tbase + 320, ka, tc::desc_kmajor_sw128(p1 + k0 * 2), id_k, k0 > 0);
-      tc::mma_bf16(tbase + 320, ka, tc::desc_mnmajor_sw128(p2 + k0 * 128, 8192), id_m, true);
-      tc::mma_bf16(tbase + 320, qa, tc::desc_mnmajor_sw128(q2 + k0 * 128, 8192), id_m, true);
-      tc::mma_bf16(tbase + 0, ka, tc::desc_kmajor_sw128(q1 + k0 * 2), id_k, k0 > 0);
+      const uint32_t om = k0 * 8, ok = k0 >> 3;
+      tc::mma_bf16(tbase + 320, d_k + om, d_p1 + ok, id_k, k0 > 0);
+      tc::mma_bf16(tbase + 320, d_k + om, d_p2 + om, id_m, true);
+      tc::mma_bf16(tbase + 320, d_q + om, d_q2 + om, id_m, true);
+      tc::mma_bf16(tbase + 0, d_k + om, d_q1 + ok, id_k, k0 > 0);
     }
     tc::mma_commit(&bar[4]);
   }
