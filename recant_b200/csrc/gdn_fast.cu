@@ -30,7 +30,7 @@ size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_ch
   w.ct.seq_chunk0 = c.take<int>(n_seqs + 1);
   w.ct.n_chunks = c.take<int>(1);
   w.err = c.take<int>(1);
-  w.stats = c.take<float>(nch * 384);
+  w.stats = c.take<float>(nch * 512);
   w.tinv = c.take<__nv_bfloat16>(nch * 4096);
   w.aqk = c.take<__nv_bfloat16>(nch * 4096);
   w.w = c.take<__nv_bfloat16>(nch * 8192);
@@ -305,11 +305,14 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
   }
   __syncthreads();  // cum, rk, rq
   if (tid < 64) ecum[tid] = __expf(cum[tid]);
-  float* st = ws.stats + ch * 384;
-  if (tid < 64) {  // stats: cum, r_q, r_k, beta and the per-token factors f_q of q~ and f_k of k~
+  float* st = ws.stats + ch * 512;
+  if (tid < 64) {  // stats: cum, r_q, r_k, beta, the per-token factors f_q of q~ and f_k of k~, and the
+                   // chunk backward's decay factors e^cum, e^(cum_last - cum) (accurate expf)
     st[tid] = cum[tid]; st[64 + tid] = rq[tid]; st[128 + tid] = rk[tid]; st[192 + tid] = beta[tid];
     st[256 + tid] = p.scale * rq[tid] * __expf(cum[tid]);
     st[320 + tid] = __expf(cum[63] - cum[tid]) * rk[tid];
+    st[384 + tid] = expf(cum[tid]);
+    st[448 + tid] = expf(cum[63] - cum[tid]);
   }
   // q~ rows for the backward walk now (the Q rows' shared memory is reused below): half-warp per row,
   // 8 elements per lane
@@ -457,7 +460,7 @@ __device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, 
     tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
   }
   if (walk != 2) tc::bulk_load(st.us, ws.u + ch * 8192, 16384, bar);
-  tc::bulk_load(st.cum, ws.stats + ch * 384, 1536, bar);
+  tc::bulk_load(st.cum, ws.stats + ch * 512, 1536, bar);
 }
 
 __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, FastWs ws, bf16* __restrict__ o,

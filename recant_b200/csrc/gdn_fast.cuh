@@ -8,7 +8,7 @@ namespace rb2 {
 
 struct FastWs {
   ChunkTable ct;
-  float* stats;          // [ch][6][64] cum, rq, rk, beta, f_q = scale rq e^cum, f_k = rk e^(cl - cum)
+  float* stats;          // [ch][8][64] cum, rq, rk, beta, f_q = scale rq e^cum, f_k = rk e^(cl - cum), e^cum, e^(cl - cum)
   __nv_bfloat16* tinv;   // [ch][64][64]   T = (I + L)^-1                      (tile image)
   __nv_bfloat16* aqk;    // [ch][64][64]   (q k^T) Gamma * scales, lower incl. diagonal (image)
   __nv_bfloat16* w;      // [ch][64][128]                                      (tile image)

@@ -78,7 +78,7 @@ __device__ __forceinline__ void bwd_issue(const BwdStage& st, const GdnProblem& 
     tc::bulk_load(st.qt, ws.qt + ch * 8192, 16384, bar);
     tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
     tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
-    tc::bulk_load(st.cum, ws.stats + ch * 384, 1536, bar);
+    tc::bulk_load(st.cum, ws.stats + ch * 512, 1536, bar);
   }
 }
 
@@ -242,8 +242,8 @@ constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 
 constexpr int KKF = 163840, QKF = KKF + 16640, DAQF = QKF + 16640;             // fp32 [64][65]
 constexpr int VEC = DAQF + 16640;                                              // 18 x 64 floats
 constexpr int RED = VEC + 18 * 256;                                            // 16 + 5 x 4 x 64 floats
-constexpr int STATS = RED + 5 * 1024 + 64;  // the next item's per-token stats, fp32 [4][64], by bulk copy
-constexpr int END = STATS + 1024;
+constexpr int STATS = RED + 5 * 1024 + 64;  // the next item's per-token stats, fp32 [8][64], by bulk copy
+constexpr int END = STATS + 2048;
 }  // namespace lay
 constexpr int kBChunkSmem = lay::END + 1024;
 constexpr int kBThreads = 512;
@@ -311,11 +311,13 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   const int i64 = 16 * q4 + l;          // ... and it is token row i64
   // Work: (chunk, key head) groups G = chunk * Hk + key head, each the p.group value heads that share
   // the key head, walked group after group by one CTA (grid-strided over groups) so that the group's
-  // dq / dk can be summed in this CTA's slice of the scratch. An item is one (chunk, value head); the
-  // sequence is advanced incrementally in 32-bit arithmetic (one division per group).
+  // dq / dk can be summed in tensor memory. An item is one (chunk, value head); the sequence is
+  // advanced incrementally in 32-bit arithmetic (one division per group), and an item's chunk-table
+  // entries are read when it becomes the next item, a whole item ahead of their use.
   const int n_groups = *ws.ct.n_chunks * p.Hk;
   struct Item {
     int G, gi, ci, hk, h;  // group, index in the group, chunk, key head, value head
+    int t0, L;             // the chunk's first token and length
   };
   auto group_item = [&](int G) {
     Item x;
@@ -324,6 +326,12 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
     x.ci = G / p.Hk;
     x.hk = G - x.ci * p.Hk;
     x.h = x.hk * p.group;
+    x.t0 = 0;
+    x.L = 0;
+    if (G < n_groups) {
+      x.t0 = ws.ct.tok0[x.ci];
+      x.L = ws.ct.len[x.ci];
+    }
     return x;
   };
   auto next_item = [&](const Item& x) {
@@ -349,24 +357,24 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
     if (tid != 0) return;
     const int ci_ = x.ci, h_ = x.h;
     const int64_t ch_ = int64_t(ci_) * p.Hv + h_;
-    const int t0_ = ws.ct.tok0[ci_];
+    const int t0_ = x.t0;
     tc::fence_proxy_async();
-    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2 + 2 * 16384 + 1024);
+    tc::mbar_expect_tx(&ldbar[0], 2 * 8192 * 2 + 2 * 16384 * 2 + 2 * 16384 + 2048);
     tc::bulk_load(sm + lay::DVP, ws.dvp + ch_ * 8192, 16384, &ldbar[0]);
     tc::bulk_load(sm + lay::ST, ws.hs + ch_ * 16384, 32768, &ldbar[0]);
     tc::bulk_load(sm + lay::DHT, ws.dh + ch_ * 16384, 32768, &ldbar[0]);
     tc::bulk_load(sm + lay::VPT, ws.vp + ch_ * 8192, 16384, &ldbar[0]);
     tc::tma_rows128(sm + lay::VT, 8192, 0, &map_v, h_, t0_, &ldbar[0]);
     tc::tma_rows128(sm + lay::DOT, 8192, 0, &map_do, h_, t0_, &ldbar[0]);
-    tc::bulk_load(sm + lay::STATS, ws.stats + ch_ * 384, 1024, &ldbar[0]);
+    tc::bulk_load(sm + lay::STATS, ws.stats + ch_ * 512, 2048, &ldbar[0]);
   };
   // [K;Q] rows of one (chunk, key head) by TMA on ldbar[2]. The value heads of a group share them,
   // so they are fetched only when the (chunk, key head) changes, during the previous item's final
   // epilogue once its reads of the region are done.
   auto issue_kq = [&](const Item& x) {
     if (tid != 0) return;
-    const int ci_ = x.ci, hk_ = x.hk;
-    const int t0_ = ws.ct.tok0[ci_];
+    const int hk_ = x.hk;
+    const int t0_ = x.t0;
     tc::fence_proxy_async();
     tc::mbar_expect_tx(&ldbar[2], 32768);
     tc::tma_rows128(sm + lay::KQ, 16384, 0, &map_k, hk_, t0_, &ldbar[2]);
@@ -385,12 +393,12 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   const uint32_t tbase = tmem_base;
   const uint32_t lane_addr = tbase + (uint32_t(32 * q4) << 16) + c0;  // this thread's lane and column quarter
   const uint32_t kqa = tc::smem_u32(sm + lay::KQ);
-  for (uint32_t it = 0; cur.G < n_groups; ++it, cur = next_item(cur)) {
+  for (uint32_t it = 0; cur.G < n_groups; ++it) {
   const Item nxt = next_item(cur);
   const bool has_next = nxt.G < n_groups;
   const uint32_t ph = it & 1u;  // parity of the barriers that complete once per item
   const int ci = cur.ci, h = cur.h, hk = cur.hk;
-  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];
+  const int t0 = cur.t0, L = cur.L;
   const int64_t ch = int64_t(ci) * p.Hv + h;
   if (prev_G != cur.G) {  // issued at the start or by the previous item
     tc::mbar_wait(&ldbar[2], kq_ph, ws.err, 137);
@@ -401,8 +409,8 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   if (tid < 64) {
     const float* st = reinterpret_cast<const float*>(sm + lay::STATS);
     cum[tid] = st[tid]; rq[tid] = st[64 + tid]; rk[tid] = st[128 + tid]; beta[tid] = st[192 + tid];
-    ecum[tid] = expf(st[tid]);
-    edec[tid] = expf(st[63] - st[tid]);
+    ecum[tid] = st[384 + tid];  // e^cum
+    edec[tid] = st[448 + tid];  // e^(cum_last - cum)
     dbeta_acc[tid] = 0.f;
     dcum_acc[tid] = 0.f;
   }
@@ -766,6 +774,7 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   if (tid < L && tid < 64) dbeta[int64_t(t0 + tid) * p.Hv + h] = __float2bfloat16_rn(dbeta_acc[tid]);
   tc::fence_before_sync();
   __syncthreads();  // this item's TMEM and shared reads are done before the next item's MMAs and loads
+  cur = nxt;
   }
   if (w == 0) tc::tmem_dealloc(tbase, 512);
 }

@@ -228,13 +228,27 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
           const uint32_t sa = st + C::A_OFF, sb = st + C::B_OFF, ssfa = st + C::SFA_OFF, ssfb = st + C::SFB_OFF;
           const int steps = min(4, ksteps - 4 * kt);
-          for (int kk = 0; kk < steps; kk += 2)  // A: K steps kk, kk + 1 -> columns 4kk .. 4kk + 7
-            tmem_cp_sf_pair(t_sfa + 4 * kk, desc_sf_pair(ssfa + kk * kImg));
-          for (int kk = 0; kk < steps; ++kk)     // B: both halves of K step kk -> columns 8kk .. 8kk + 7
-            tmem_cp_sf_pair(t_sfb + 8 * kk, desc_sf_pair(ssfb + 2 * kk * kImg));
-          for (int kk = 0; kk < steps; ++kk)
-            mma_nvf4(t_acc, tc::desc_kmajor_sw128(sa + 32 * kk), tc::desc_kmajor_sw128(sb + 32 * kk), idesc,
-                     t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
+          // descriptors built once per stage; their address fields advance in 16-byte units
+          const uint64_t d_sfa = desc_sf_pair(ssfa), d_sfb = desc_sf_pair(ssfb), d_a = tc::desc_kmajor_sw128(sa),
+                         d_b = tc::desc_kmajor_sw128(sb);
+          if (steps == 4) {  // every stage but a ragged last one: straight-line issue
+#pragma unroll
+            for (int kk = 0; kk < 4; kk += 2)  // A: K steps kk, kk + 1 -> columns 4kk .. 4kk + 7
+              tmem_cp_sf_pair(t_sfa + 4 * kk, d_sfa + uint32_t(kk * kImg >> 4));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)     // B: both halves of K step kk -> columns 8kk .. 8kk + 7
+              tmem_cp_sf_pair(t_sfb + 8 * kk, d_sfb + uint32_t(2 * kk * kImg >> 4));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_nvf4(t_acc, d_a + 2 * kk, d_b + 2 * kk, idesc, t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
+          } else {
+            for (int kk = 0; kk < steps; kk += 2)
+              tmem_cp_sf_pair(t_sfa + 4 * kk, d_sfa + uint32_t(kk * kImg >> 4));
+            for (int kk = 0; kk < steps; ++kk)
+              tmem_cp_sf_pair(t_sfb + 8 * kk, d_sfb + uint32_t(2 * kk * kImg >> 4));
+            for (int kk = 0; kk < steps; ++kk)
+              mma_nvf4(t_acc, d_a + 2 * kk, d_b + 2 * kk, idesc, t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
+          }
           tc::mma_commit(&empty[s]);
         }
         tc::mma_commit(&acc_full[ab]);
