@@ -269,10 +269,11 @@ def cpu_reference_runner(B, T, Hk, Hv, d):
     return run, threads, f"B{B} T{T} Hk{Hk} Hv{Hv} d{d} fwd+bwd, fp32 compute"
 
 
-def nvfp4_leg(dev, pk, reps=10):
+def nvfp4_leg(dev, pk, reps=10, gemm_reps=40):
     """The NVFP4 half of the path at config 2's in_proj shapes: quantize (RHT, round-to-nearest) of a
     [16384, 4096] bf16 activation and the fprop GEMM [16384 x 4096] . [12288 x 4096]^T (qkv + z)
-    with a bf16 epilogue, each timed from the library's per-launch CUDA events. Quantize bytes are
+    with a bf16 epilogue, each timed from the library's per-launch CUDA events, with the SM clock
+    sampled during each loop (a back-to-back GEMM loop runs into the power cap). Quantize bytes are
     the algorithmic 2.5625 per element (2 read, 0.5 codes, 1/16 scales); GEMM FLOPs are 2MNK
     against 4 x the measured dense bf16 peak (the tcgen05 FP4 : bf16 rate)."""
     import torch
@@ -287,26 +288,33 @@ def nvfp4_leg(dev, pk, reps=10):
         a = N.quantize_fast(x)
         y = N.gemm_b200(a, W.fprop, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
-    prof = L.LaunchProfiler(capacity=16 * reps)
+    prof = L.LaunchProfiler(capacity=16 * (reps + gemm_reps))
     prof.start()
+    cq = ClockSampler(dev.index or 0)
+    cq.start()
     for _ in range(reps):
         a = N.quantize_fast(x)
-    for _ in range(reps):
+    torch.cuda.synchronize()
+    q_clk = cq.stop()
+    cg = ClockSampler(dev.index or 0)
+    cg.start()
+    for _ in range(gemm_reps):
         y = N.gemm_b200(a, W.fprop, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
+    g_clk = cg.stop()
     recs, _ = prof.read()
     del y
     q_ms = sum(t for n, t in recs if n in ("nvfp4_amax", "nvfp4_quant", "nvfp4_zero", "nvfp4_quant_small")) / reps
-    g_ms = sum(t for n, t in recs if n == "nvfp4_gemm") / reps
+    g_ms = sum(t for n, t in recs if n == "nvfp4_gemm") / gemm_reps
     gbs = M * K * 2.5625 / (q_ms / 1e3) / 1e9
     tfl = 2.0 * M * Nn * K / (g_ms / 1e3) / 1e12
     fp4_peak = FP4_PER_BF16 * pk["bf16"]
     return {"quantize": {"shape": [M, K], "ms": round(q_ms, 4), "achieved": round(gbs, 1), "unit": "GB/s",
                          "peak": pk["hbm"], "frac": round(gbs / pk["hbm"], 4), "bytes_per_elt": 2.5625,
-                         "peak_source": f"{pk['source']} HBM copy (MEASURED_PEAKS.json)"},
+                         "peak_source": f"{pk['source']} HBM copy (MEASURED_PEAKS.json)", "clocks": q_clk},
             "gemm": {"shape": [M, Nn, K], "ms": round(g_ms, 4), "achieved": round(tfl, 1), "unit": "TFLOP/s",
                      "peak": round(fp4_peak, 1), "frac": round(tfl / fp4_peak, 4),
-                     "peak_source": f"4 x {pk['source']} bf16 burst (MEASURED_PEAKS.json)"}}
+                     "peak_source": f"4 x {pk['source']} bf16 burst (MEASURED_PEAKS.json)", "clocks": g_clk}}
 
 
 CONFIG1 = {"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",
@@ -426,16 +434,23 @@ def comparator_arm(args):
         y_ref = smm_backend()
         y_ours = N.gemm_b200(a, b)
         agree = float((y_ours - y_ref).norm() / y_ref.norm())
-        ms_k, ms_b = med(smm, args.steps), med(smm_backend, args.steps)
+        ck = ClockSampler(0)
+        ck.start()
+        ms_k = med(smm, args.steps)
+        clk_k = ck.stop()
+        ms_b = med(smm_backend, args.steps)
         out["scaled_mm_nvfp4"] = {"ms": round(ms_k, 4), "tflops": round(flop / ms_k / 1e9, 1),
                                   "ms_with_fp32_epilogue": round(ms_b, 4),
-                                  "rel_diff_vs_b200_fp32": agree}
+                                  "rel_diff_vs_b200_fp32": agree, "clocks": clk_k}
     except Exception as e:
         out["scaled_mm_nvfp4"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+    co = ClockSampler(0)
+    co.start()
     ms_o = med(lambda: N.gemm_b200(a, b, out_dtype=torch.bfloat16), args.steps)
+    clk_o = co.stop()
     ms_of = med(lambda: N.gemm_b200(a, b), args.steps)
     out["b200_nvfp4_gemm"] = {"ms": round(ms_o, 4), "tflops": round(flop / ms_o / 1e9, 1),
-                              "ms_fp32_out": round(ms_of, 4)}
+                              "ms_fp32_out": round(ms_of, 4), "clocks": clk_o}
     print(json.dumps(out), flush=True)
     return 0
 

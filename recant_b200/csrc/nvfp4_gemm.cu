@@ -5,19 +5,18 @@
 // _to_blocked, nvfp4.py:112-119). A = codes [M, K/2] (two e2m1 per byte, even element in the low
 // nibble), B = codes [N, K/2]; per-16 e4m3 scales in the blocked layout; fp32 accumulation.
 //
-// Persistent CTAs (one per SM) walk 128 x 256 output tiles, warp-specialised:
-//   (before)   a small kernel expands both operands' blocked scales into workspace images: every
-//              512-byte atom (32 rows x 16 bytes: row r = the 4 scales of rows r, r+32, r+64, r+96 for
-//              one 64-element K step) written 4 times in a row, i.e. the 128-lane picture the MMA
-//              reads (row m of the image = atom row m % 32); B's two 128-row halves interleaved per
-//              K step;
+// Persistent CTAs (one per SM) walk 128 x 256 output tiles, warp-specialised. The scales are read
+// in the blocked layout itself: its 512-byte atom (32 rows x 16 bytes: row r = the 4 scales of rows
+// r, r+32, r+64, r+96 for one 64-element K step) is what each 32-lane quarter of the tensor memory
+// holds, so one tcgen05.cp.32x128b.warpx4 (the copy engine writes the atom to all four quarters)
+// moves a K step of one 128-row block, and no expanded image is built or read:
 //   warp 0     producer: TMA (cp.async.bulk.tensor, SW128, no multicast) of the A and B code tiles
-//              (128 bytes = 256 K-elements per row per stage) and one 1-D bulk copy per operand of
-//              its scale images into a 3-stage ring; completion via mbarrier transaction counts;
-//   warp 1     MMA: tcgen05.cp.128x256b of the images into TMEM (lane m, 32-bit column m / 32 of a
-//              4-column group holds row m's scales; one copy fills two groups: two K steps of A,
-//              or both halves of B for one K step: 6 copies per 4 K steps), then one
-//              tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64) per K step;
+//              (128 bytes = 256 K-elements per row per stage) and 1-D bulk copies of the stage's
+//              scale atoms (A's row block; B's two 128-row halves) into a 4-stage ring; completion
+//              via mbarrier transaction counts;
+//   warp 1     MMA: the atom copies into TMEM (lane m, 32-bit column m / 32 of a 4-column group holds
+//              row m's scales: A one group per K step, B two (its halves); 12 copies per 4 K steps),
+//              then one tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=256, K=64) per K step;
 //   warps 2-9  epilogue: TMEM -> registers (each warp: its sub-partition's 32 rows x 128 columns),
 //              accumulator released, then * gA gB -> fp32 or bf16 rows while the next tile runs.
 
@@ -30,48 +29,26 @@ constexpr int BM = 128, BKB = 128;  // tile rows, K bytes per stage (= 256 e2m1)
 constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 
 // Tile shape: BN output columns, STAGES smem stages, ACC TMEM accumulator buffers. A stage is
-// [A scale images | B scale images | A codes | B codes]: the images first, so that every scale
-// copy reads well inside its own stage.
-constexpr int kImg = 4 * 512;  // one atom repeated over 128 rows
+// [A scale atoms | B scale atoms | A codes | B codes]: the atoms first, so that every scale copy
+// reads well inside its own stage.
+constexpr int kAtom = 512;  // the scales of one 128-row block for one 64-element K step
 
 template <int BN_, int STAGES_, int ACC_>
 struct GemmCfg {
   static constexpr int BN = BN_, STAGES = STAGES_, ACC = ACC_;
   static constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;
-  static constexpr int SFA_BYTES = 4 * kImg;                 // 4 K steps
-  static constexpr int SFB_BYTES = 4 * 2 * kImg;             // 4 K steps x 2 halves
+  static constexpr int SFA_BYTES = 4 * kAtom;                // [4 K steps][atom]
+  static constexpr int SFB_BYTES = 2 * 4 * kAtom;            // [2 halves][4 K steps][atom]
   static constexpr int SFA_OFF = 0, SFB_OFF = SFA_BYTES, A_OFF = SFA_BYTES + SFB_BYTES, B_OFF = A_OFF + A_BYTES;
   static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
   static constexpr int LORA_BYTES = BN * 16 * 2;             // the tile's LoRA B rows (r <= 16, bf16)
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;   // + LORA_BYTES for the LoRA variant
   static constexpr int SF_COL0 = ACC * BN;                   // TMEM: accumulators, then scale factors
-  static_assert(BN == 256, "a B scale copy moves exactly two 128-row halves");
+  static_assert(BN == 256, "B's scales are two 128-row halves");
   static_assert(SF_COL0 + 16 + 32 <= 512, "TMEM budget");
   static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && STAGE_BYTES % 1024 == 0, "SW128 alignment");
   static_assert(SMEM + LORA_BYTES <= 227 * 1024, "shared memory");
 };
-
-// Scale images in the workspace: A: [row block][K step (padded to 4)][kImg]; B: [256-row block]
-// [K step (padded to 4)][half][kImg]. ksp = K steps rounded up to a multiple of 4.
-__global__ void sf_images_kernel(const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int ntm, int nrb,
-                                 int ncb, int ksp, uint8_t* __restrict__ img_a, uint8_t* __restrict__ img_b) {
-  const int64_t na = int64_t(ntm) * ksp * (kImg / 16), nb = int64_t((nrb + 1) / 2) * ksp * 2 * (kImg / 16);
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < na + nb; i += int64_t(gridDim.x) * blockDim.x) {
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (i < na) {
-      const int within = int(i % 32), ks = int((i / 128) % ksp);
-      const int64_t tm = i / (int64_t(128) * ksp);
-      if (ks < ncb) v = reinterpret_cast<const uint4*>(sfa + (tm * ncb + ks) * 512)[within];
-      reinterpret_cast<uint4*>(img_a)[i] = v;
-    } else {
-      const int64_t j = i - na;
-      const int within = int(j % 32), h = int((j / 128) % 2), ks = int((j / 256) % ksp);
-      const int64_t rb = (j / (int64_t(256) * ksp)) * 2 + h;
-      if (ks < ncb && rb < nrb) v = reinterpret_cast<const uint4*>(sfb + (rb * ncb + ks) * 512)[within];
-      reinterpret_cast<uint4*>(img_b)[j] = v;
-    }
-  }
-}
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -80,19 +57,20 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "l"(map), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
       : "memory");
 }
-// smem descriptor of a 128-row x 32-byte scale source for tcgen05.cp.128x256b, no swizzle: 8-row x
-// 16-byte core matrices, consecutive row groups 128 bytes apart (SBO), the second 16-byte column
-// kImg bytes after the first (LBO)
-__device__ __forceinline__ uint64_t desc_sf_pair(uint32_t saddr) {
+// smem descriptor of one scale atom (32 rows x 16 bytes) as the source of tcgen05.cp.32x128b, no
+// swizzle: 8-row x 16-byte core matrices, consecutive row groups 128 bytes apart (SBO); a single
+// 16-byte column, so the leading-dimension offset is unused
+__device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
   uint64_t d = 0;
   d |= uint64_t((saddr >> 4) & 0x3FFF);
-  d |= uint64_t((kImg >> 4) & 0x3FFF) << 16;  // LBO
+  d |= uint64_t(1) << 16;                     // LBO (unused)
   d |= uint64_t(128 >> 4) << 32;              // SBO
   d |= uint64_t(1) << 46;
   return d;                                   // layout type 0 = no swizzle
 }
-__device__ __forceinline__ void tmem_cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+// the atom into 4 consecutive columns of all 128 lanes: lane 32 q + r gets atom row r, q = 0..3
+__device__ __forceinline__ void tmem_cp_sf_atom(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 // kind::mxf4nvf4 instruction descriptor: e2m1 x e2m1, ue4m3 scales, K-major A and B, dense K=64
 __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
@@ -158,7 +136,7 @@ __device__ __forceinline__ void unpack8(const uint4 u, float* f) {
 template <class C, bool kLora>
 __global__ void __launch_bounds__(kThreads, 1)
 nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                  const uint8_t* __restrict__ img_a, const uint8_t* __restrict__ img_b, int ksp, const float* __restrict__ ga,
+                  const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int nrb_b, const float* __restrict__ ga,
                   const float* __restrict__ gb, int M, int N, int K, void* __restrict__ out, int out_bf16,
                   Lora lora, int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -202,11 +180,17 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           if (!(ok = tc::mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, err, 201))) break;
           unsigned char* st = sm + s * STAGE_BYTES;
           const int steps = min(4, ksteps - 4 * kt);
-          tc::mbar_expect_tx(&full[s], A_BYTES + B_BYTES + uint32_t(steps) * 3 * kImg);
+          // blocked scales: atom (row block, K step) at (row block * K steps + K step) * 512; B's second
+          // half is absent past the last row block (its output columns are not stored)
+          const uint32_t sf = uint32_t(steps) * kAtom;
+          const bool half1 = 2 * tn + 1 < nrb_b;
+          tc::mbar_expect_tx(&full[s], A_BYTES + B_BYTES + sf * (half1 ? 3u : 2u));
           tma_load_2d(st + C::A_OFF, &map_a, kt * BKB, tm * BM, &full[s]);
           tma_load_2d(st + C::B_OFF, &map_b, kt * BKB, tn * BN, &full[s]);
-          tc::bulk_load(st + C::SFA_OFF, img_a + (size_t(tm) * ksp + 4 * kt) * kImg, steps * kImg, &full[s]);
-          tc::bulk_load(st + C::SFB_OFF, img_b + (size_t(tn) * ksp + 4 * kt) * 2 * kImg, steps * 2 * kImg, &full[s]);
+          tc::bulk_load(st + C::SFA_OFF, sfa + (size_t(tm) * ksteps + 4 * kt) * kAtom, sf, &full[s]);
+          tc::bulk_load(st + C::SFB_OFF, sfb + (size_t(2 * tn) * ksteps + 4 * kt) * kAtom, sf, &full[s]);
+          if (half1)
+            tc::bulk_load(st + C::SFB_OFF + 4 * kAtom, sfb + (size_t(2 * tn + 1) * ksteps + 4 * kt) * kAtom, sf, &full[s]);
         }
       }
     }
@@ -226,26 +210,27 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           if (!(ok = tc::mbar_wait(&full[s], (g / STAGES) & 1, err, 202))) break;
           tc::fence_after_sync();
           const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
-          const uint32_t sa = st + C::A_OFF, sb = st + C::B_OFF, ssfa = st + C::SFA_OFF, ssfb = st + C::SFB_OFF;
           const int steps = min(4, ksteps - 4 * kt);
           // descriptors built once per stage; their address fields advance in 16-byte units
-          const uint64_t d_sfa = desc_sf_pair(ssfa), d_sfb = desc_sf_pair(ssfb), d_a = tc::desc_kmajor_sw128(sa),
-                         d_b = tc::desc_kmajor_sw128(sb);
+          const uint64_t d_sfa = desc_sf_atom(st + C::SFA_OFF), d_sfb = desc_sf_atom(st + C::SFB_OFF),
+                         d_a = tc::desc_kmajor_sw128(st + C::A_OFF), d_b = tc::desc_kmajor_sw128(st + C::B_OFF);
+          constexpr uint32_t kA = kAtom >> 4, kH = 4 * kAtom >> 4;  // one atom; one B half (16-byte units)
           if (steps == 4) {  // every stage but a ragged last one: straight-line issue
 #pragma unroll
-            for (int kk = 0; kk < 4; kk += 2)  // A: K steps kk, kk + 1 -> columns 4kk .. 4kk + 7
-              tmem_cp_sf_pair(t_sfa + 4 * kk, d_sfa + uint32_t(kk * kImg >> 4));
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)     // B: both halves of K step kk -> columns 8kk .. 8kk + 7
-              tmem_cp_sf_pair(t_sfb + 8 * kk, d_sfb + uint32_t(2 * kk * kImg >> 4));
+            for (int kk = 0; kk < 4; ++kk) {   // K step kk: A -> columns 4kk .. 4kk + 3, B halves -> 8kk .. 8kk + 7
+              tmem_cp_sf_atom(t_sfa + 4 * kk, d_sfa + kk * kA);
+              tmem_cp_sf_atom(t_sfb + 8 * kk, d_sfb + kk * kA);
+              tmem_cp_sf_atom(t_sfb + 8 * kk + 4, d_sfb + kH + kk * kA);
+            }
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               mma_nvf4(t_acc, d_a + 2 * kk, d_b + 2 * kk, idesc, t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
           } else {
-            for (int kk = 0; kk < steps; kk += 2)
-              tmem_cp_sf_pair(t_sfa + 4 * kk, d_sfa + uint32_t(kk * kImg >> 4));
-            for (int kk = 0; kk < steps; ++kk)
-              tmem_cp_sf_pair(t_sfb + 8 * kk, d_sfb + uint32_t(2 * kk * kImg >> 4));
+            for (int kk = 0; kk < steps; ++kk) {
+              tmem_cp_sf_atom(t_sfa + 4 * kk, d_sfa + kk * kA);
+              tmem_cp_sf_atom(t_sfb + 8 * kk, d_sfb + kk * kA);
+              tmem_cp_sf_atom(t_sfb + 8 * kk + 4, d_sfb + kH + kk * kA);
+            }
             for (int kk = 0; kk < steps; ++kk)
               mma_nvf4(t_acc, d_a + 2 * kk, d_b + 2 * kk, idesc, t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
           }
@@ -389,23 +374,14 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_byte
 using namespace rb2;
 
 namespace {
-// workspace: [status word, padded to 1 KB][A scale images][B scale images]
-struct GemmWs {
-  int64_t ksp, img_a, img_b, total;
-};
-GemmWs gemm_ws(int64_t M, int64_t N, int64_t K) {
-  GemmWs w;
-  w.ksp = (K / 64 + 3) / 4 * 4;
-  w.img_a = (M + 127) / 128 * w.ksp * kImg;
-  w.img_b = (N + 255) / 256 * w.ksp * 2 * kImg;
-  w.total = 1024 + w.img_a + w.img_b;
-  return w;
-}
+// the blocked scale layout: [row block of 128][K step of 64][512-byte atom]
+int64_t blocked_bytes(int64_t rows, int64_t K) { return (rows + 127) / 128 * (K / 64) * kAtom; }
 }  // namespace
 
+// workspace: the kernel's status word (the scales are read in place)
 extern "C" size_t rb2_nvfp4_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
-  if (M <= 0 || N <= 0 || K <= 0) return 1024;
-  return size_t(gemm_ws(M, N, K).total);
+  (void)M; (void)N; (void)K;
+  return 1024;
 }
 
 extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
@@ -430,7 +406,7 @@ extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CUtensorMap ma, mb;
   int rc;
-  using Wide = GemmCfg<256, 3, 1>;
+  using Wide = GemmCfg<256, 4, 1>;
   const int BN = Wide::BN;
   if ((rc = make_map(&ma, a_codes, M, K / 2, BM))) return rc;
   if ((rc = make_map(&mb, b_codes, N, K / 2, BN))) return rc;
@@ -440,9 +416,8 @@ extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t ntiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   dim3 grid(unsigned(ntiles < sms ? ntiles : sms));
-  const GemmWs gw = gemm_ws(M, N, K);
-  uint8_t* img_a = static_cast<uint8_t*>(ws) + 1024;
-  uint8_t* img_b = img_a + gw.img_a;
+  // B's precomputed scales (rb2_nvfp4_gemm_b_images) are its blocked scales, read in place like A's
+  const uint8_t* sfb = b_images ? b_images : b_scales_blocked;
   RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(b_images) & 15) == 0, "nvfp4_gemm: b_images must be 16-byte aligned");
   RB2_CHECK_ARG(lora_h == nullptr ||
                     (lora_b && lora_r > 0 && lora_r <= 16 && lora_r % 8 == 0 && lora_ldh >= lora_r && lora_ldh % 8 == 0 &&
@@ -452,30 +427,22 @@ extern "C" int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales
   const Lora lora{static_cast<const __nv_bfloat16*>(lora_h), static_cast<const __nv_bfloat16*>(lora_b), lora_ldh,
                   lora_r, lora_scale, lora_mode};
   {
-    ProfScope ps_("nvfp4_sf_images", s);
-    // with precomputed B images (rb2_nvfp4_gemm_b_images) only A's are built (nrb = 0)
-    const int64_t n16 = (gw.img_a + (b_images ? 0 : gw.img_b)) / 16;
-    sf_images_kernel<<<unsigned(std::min<int64_t>((n16 + 255) / 256, int64_t(sms) * 16)), 256, 0, s>>>(
-        a_scales_blocked, b_scales_blocked, int((M + 127) / 128), b_images ? 0 : int((N + 127) / 128), int(K / 64),
-        int(gw.ksp), img_a, img_b);
-  }
-  if (b_images) img_b = const_cast<uint8_t*>(b_images);
-  RB2_CHECK_LAUNCH("nvfp4_sf_images");
-  {
     ProfScope ps_("nvfp4_gemm", s);
     if (lora.h) {
       RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     Wide::SMEM + Wide::LORA_BYTES),
                "nvfp4_gemm: smem attribute");
       nvfp4_gemm_kernel<Wide, true><<<grid, kThreads, Wide::SMEM + Wide::LORA_BYTES, s>>>(
-          ma, mb, img_a, img_b, int(gw.ksp), a_gscale, b_gscale, int(M), int(N), int(K), out, out_dtype == RB2_BF16, lora,
+          ma, mb, a_scales_blocked, sfb, int((N + 127) / 128), a_gscale, b_gscale, int(M), int(N), int(K), out,
+          out_dtype == RB2_BF16, lora,
           static_cast<int*>(ws));
     } else {
       RB2_CUDA(cudaFuncSetAttribute(nvfp4_gemm_kernel<Wide, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     Wide::SMEM),
                "nvfp4_gemm: smem attribute");
       nvfp4_gemm_kernel<Wide, false><<<grid, kThreads, Wide::SMEM, s>>>(
-          ma, mb, img_a, img_b, int(gw.ksp), a_gscale, b_gscale, int(M), int(N), int(K), out, out_dtype == RB2_BF16, lora,
+          ma, mb, a_scales_blocked, sfb, int((N + 127) / 128), a_gscale, b_gscale, int(M), int(N), int(K), out,
+          out_dtype == RB2_BF16, lora,
           static_cast<int*>(ws));
     }
   }
@@ -493,9 +460,11 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
 
 extern "C" size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K) {
   if (N <= 0 || K <= 0) return 0;
-  return size_t(gemm_ws(1, N, K).img_b);
+  return size_t(blocked_bytes(N, K));
 }
 
+// The B operand's scales as the kernel reads them, kept with a frozen weight: the kernel reads the
+// blocked layout in place, so this is a copy of the blocked scales (kept for callers that cache it).
 extern "C" int rb2_nvfp4_gemm_b_images(const uint8_t* b_scales_blocked, int64_t N, int64_t K, void* out,
                                        size_t out_bytes, void* stream) {
   RB2_CHECK_ARG(N > 0 && K > 0 && K % 64 == 0 && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
@@ -503,17 +472,12 @@ extern "C" int rb2_nvfp4_gemm_b_images(const uint8_t* b_scales_blocked, int64_t 
   RB2_CHECK_ARG(b_scales_blocked && out && (reinterpret_cast<uintptr_t>(b_scales_blocked) & 15) == 0 &&
                     (reinterpret_cast<uintptr_t>(out) & 15) == 0,
                 "nvfp4_gemm_b_images: null or misaligned pointer");
-  const GemmWs gw = gemm_ws(1, N, K);
-  if (out_bytes < size_t(gw.img_b)) {
+  const size_t nb = size_t(blocked_bytes(N, K));
+  if (out_bytes < nb) {
     set_error("nvfp4_gemm_b_images: output too small");
     return RB2_EWORKSPACE;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t n16 = gw.img_b / 16;
-  ProfScope ps_("nvfp4_sf_images", s);
-  // the prep kernel with no A rows: only the B part
-  sf_images_kernel<<<unsigned(std::min<int64_t>((n16 + 255) / 256, int64_t(148) * 16)), 256, 0, s>>>(
-      nullptr, b_scales_blocked, 0, int((N + 127) / 128), int(K / 64), int(gw.ksp), nullptr, static_cast<uint8_t*>(out));
-  RB2_CHECK_LAUNCH("nvfp4_gemm_b_images");
+  RB2_CUDA(cudaMemcpyAsync(out, b_scales_blocked, nb, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)),
+           "nvfp4_gemm_b_images: copy");
   return RB2_OK;
 }

@@ -23,8 +23,8 @@ BLOCK = 16
 # as long as A, dequantized with padding (K + K/8 floats per row), fits the kernel's shared memory
 GEMV_MAX_M = 4
 GEMV_MAX_ELEMS = 50_000
-# Frozen weights keep the GEMM's B-operand scale images (built once at quantisation) instead of
-# rebuilding them every call
+# Frozen weights keep the scales the GEMM reads for its B operand (the blocked layout, built once at
+# quantisation) instead of rebuilding them every call
 CACHE_WEIGHT_IMAGES = True
 _DT = {torch.float32: L.F32, torch.bfloat16: L.BF16}
 
@@ -36,7 +36,7 @@ class FP4Tensor:
     gscale: torch.Tensor
     shape: tuple
     blocked: torch.Tensor | None = field(default=None, repr=False)
-    gemm_images: torch.Tensor | None = field(default=None, repr=False)  # B-operand scale images
+    gemm_images: torch.Tensor | None = field(default=None, repr=False)  # B-operand scales as the GEMM reads them
 
 
 def blocked_size(rows: int, cols: int) -> int:
@@ -80,17 +80,10 @@ def blocked_scales(t) -> torch.Tensor:
 
 
 def gemm_images(t) -> torch.Tensor:
-    """The scale images the GEMM kernel reads for ``t`` as its B operand, built once and kept on the
-    tensor (frozen weights; about 4x the size of the scales)."""
+    """The scales the GEMM kernel reads for ``t`` as its B operand, kept on the tensor (frozen
+    weights). The kernel reads the blocked layout in place, so these are the blocked scales."""
     if t.gemm_images is None:
-        rows, k = t.shape
-        lib = L.lib()
-        nb = lib.rb2_nvfp4_gemm_b_images_size(rows, k)
-        img = torch.empty(nb, dtype=torch.uint8, device=t.codes.device)
-        L.check(lib.rb2_nvfp4_gemm_b_images(L.ptr(blocked_scales(t)), rows, k, L.ptr(img), nb,
-                                            torch.cuda.current_stream(t.codes.device).cuda_stream),
-                "nvfp4_gemm_b_images")
-        t.gemm_images = img
+        t.gemm_images = blocked_scales(t)
     return t.gemm_images
 
 

@@ -98,10 +98,11 @@ def test_fp4_linear_fwd_bwd():
 
 @pytest.mark.parametrize("M,N,K", [(257, 384, 320), (1, 4096, 4096), (64, 100, 64)])
 def test_gemm_with_cached_weight_images_is_identical(M, N, K):
-    """B's scale images built once (rb2_nvfp4_gemm_b_images, kept on the weight) give bit-for-bit the
-    result of building them inside every call."""
+    """B's scales kept on the weight (gemm_images), or copied once through rb2_nvfp4_gemm_b_images and
+    passed as the precomputed B operand, give bit-for-bit the result of the plain call."""
+    from recant_b200 import _lib as L
     from recant_b200 import gemm_b200
-    from recant_b200.nvfp4 import gemm_images
+    from recant_b200.nvfp4 import blocked_scales, gemm_images
     gen = torch.Generator().manual_seed(M * 7 + N + K)
     x = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
     w = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
@@ -111,6 +112,14 @@ def test_gemm_with_cached_weight_images_is_identical(M, N, K):
     assert b.gemm_images is not None
     cached = gemm_b200(a, b)
     assert torch.equal(plain, cached)
+    lib = L.lib()
+    nb = lib.rb2_nvfp4_gemm_b_images_size(N, K)
+    img = torch.full((nb,), 0xAB, dtype=torch.uint8, device="cuda")
+    L.check(lib.rb2_nvfp4_gemm_b_images(L.ptr(blocked_scales(b)), N, K, L.ptr(img), nb,
+                                        torch.cuda.current_stream().cuda_stream), "nvfp4_gemm_b_images")
+    b.gemm_images = img
+    copied = gemm_b200(a, b)
+    assert torch.equal(plain, copied)
 
 
 @pytest.mark.parametrize("M,N,K,r", [(300, 512, 256, 16), (257, 384, 320, 8), (1, 4096, 1024, 16)])
