@@ -125,8 +125,8 @@ __device__ void inverse_lower64_tc(float* lt, float* xbuf, unsigned char* ptile,
   }
   __syncthreads();
   // P (all of the working matrix) and D (its block diagonal) as bf16 images, rows i, columns j
-  for (int idx = tid; idx < 512; idx += 256) {
-    const int i = idx >> 3, c8 = (idx & 7) * 8;
+  for (int idx = tid; idx < 512; idx += 256) {  // consecutive lanes take consecutive rows: no bank conflicts
+    const int i = idx & 63, c8 = (idx >> 6) * 8;
     const float* t = lt + i * 65 + c8;
     const uint4 v = make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
                                tc::pack_bf16(t[6], t[7]));
@@ -392,8 +392,8 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
       *reinterpret_cast<uint4*>(dst + tc::sw128_offset(i, c0 + 8 * j, 64)) =
           make_uint4(apk[4 * j], apk[4 * j + 1], apk[4 * j + 2], apk[4 * j + 3]);
   }
-  for (int idx = tid; idx < 512; idx += 256) {
-    const int i = idx >> 3, c8 = (idx & 7) * 8;
+  for (int idx = tid; idx < 512; idx += 256) {  // consecutive lanes take consecutive rows: no bank conflicts
+    const int i = idx & 63, c8 = (idx >> 6) * 8;
     const float* t = lt + i * 65 + c8;
     *reinterpret_cast<uint4*>(img(ws.tinv + ch * 4096) + tc::sw128_offset(i, c8, 64)) =
         make_uint4(tc::pack_bf16(t[0], t[1]), tc::pack_bf16(t[2], t[3]), tc::pack_bf16(t[4], t[5]),
@@ -426,8 +426,8 @@ constexpr int kStateSmem = 32768 + 16384 + 16384 + 2 * kStageBytes + 2048;
 // S^T q~^T = (S^T q^T) diag(f_q) is scaled in the output epilogue and V'^T k~ = (V'^T diag(f_k)) k
 // takes a second, scaled V'^T tile.
 struct FwdStage {
-  unsigned char* wt;   // W   64 rows (tok) x 128 (dk)        16 KB
-  unsigned char* qt;   // q   64 x 128 (the caller's rows)     16 KB
+  unsigned char* wt;   // [W; q]: one 128-row K-major tile (slab stride 16 KB), rows 0-63 W, 64-127 the
+                       // caller's q rows, so S^T [W; q]^T is one N = 128 product              32 KB
   unsigned char* kt;   // k   64 x 128 (used MN-major: N = dk) 16 KB
   bf16* us;            // U plain [64][128]                    16 KB
   unsigned char* at;   // A_qk 64 (i) x 64 (j)                  8 KB
@@ -438,7 +438,6 @@ __device__ __forceinline__ FwdStage fwd_stage(unsigned char* base, int stg) {
   unsigned char* b = base + stg * kStageBytes;
   FwdStage st;
   st.wt = b;
-  st.qt = b + 16384;
   st.kt = b + 32768;
   st.us = reinterpret_cast<bf16*>(b + 49152);
   st.at = b + 65536;
@@ -453,10 +452,11 @@ __device__ __forceinline__ void fwd_issue(const FwdStage& st, const FastWs& ws, 
   const uint32_t bytes = 16384 * 2 + 1536 + (walk == 0 ? 16384 + 8192 : 0) + (walk != 2 ? 16384 : 0);
   tc::fence_proxy_async();  // the stage's previous generic reads are ordered before these writes
   tc::mbar_expect_tx(bar, bytes);
-  tc::bulk_load(st.wt, ws.w + ch * 8192, 16384, bar);
+  tc::bulk_load(st.wt, ws.w + ch * 8192, 8192, bar);                  // W image slab 0 -> rows 0-63
+  tc::bulk_load(st.wt + 16384, ws.w + ch * 8192 + 4096, 8192, bar);   // slab 1
   tc::tma_rows128(st.kt, 8192, 0, map_k, hk, t0, bar);
   if (walk == 0) {  // outputs need q and A_qk
-    tc::tma_rows128(st.qt, 8192, 0, map_q, hk, t0, bar);
+    tc::tma_rows128(st.wt, 16384, 64, map_q, hk, t0, bar);
     tc::bulk_load(st.at, ws.aqk + ch * 4096, 8192, bar);
   }
   if (walk != 2) tc::bulk_load(st.us, ws.u + ch * 8192, 16384, bar);
@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     tc::mbar_wait(&ldbar[stg], ((ci - c0) >> 1) & 1, ws.err, 110);
     if (L < 64) {  // the caller's rows past the end of the sequence (another sequence's, or the TMA fill)
       tc::zero_rows_tail(cur.kt, 8192, 0, L, 256);
-      if (outs) tc::zero_rows_tail(cur.qt, 8192, 0, L, 256);
+      if (outs) tc::zero_rows_tail(cur.wt, 16384, 64, L, 256);
     }
     // S^T (bf16) -> smem operand and -> workspace (state entering this chunk)
     {
@@ -531,15 +531,14 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {
-      // D_vp = S^T W^T (cols [0,64)), D_o = S^T q^T (cols [64,128), scaled by f_q later): M=128, N=64, K=128
-      const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
-      const uint64_t d_s = tc::desc_kmajor_sw128(tc::smem_u32(st)), d_w = tc::desc_kmajor_sw128(tc::smem_u32(cur.wt)),
-                     d_q = tc::desc_kmajor_sw128(tc::smem_u32(cur.qt));
+      // [D_vp D_o] = S^T [W; q]^T: D_vp in columns [0,64), D_o = S^T q^T (scaled by f_q later) in [64,128);
+      // M=128, N=128 (N=64, W only, without outputs), K=128
+      const uint32_t idesc = tc::idesc_bf16(128, outs ? 128 : 64, false, false);
+      const uint64_t d_s = tc::desc_kmajor_sw128(tc::smem_u32(st)), d_wq = tc::desc_kmajor_sw128(tc::smem_u32(cur.wt));
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16) {
-        const uint32_t aoff = ((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4, boff = ((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4;
-        tc::mma_bf16(tbase + 0, d_s + aoff, d_w + boff, idesc, k0 > 0);
-        if (outs) tc::mma_bf16(tbase + 64, d_s + aoff, d_q + boff, idesc, k0 > 0);
+        const uint32_t off = ((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4;  // both operands: 16 KB slabs
+        tc::mma_bf16(tbase + 0, d_s + off, d_wq + off, idesc, k0 > 0);
       }
       tc::mma_commit(&bar[0]);
       if (outs) {  // the state entering the chunk: the S^T tile is its workspace image
