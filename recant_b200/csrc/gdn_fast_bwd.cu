@@ -228,14 +228,15 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
 // Sixteen warps (four per scheduler) hide the latency of the epilogues' shared-memory and TMEM
 // traffic; each thread holds 16 columns of an accumulator row, so 128 registers suffice.
 // TMEM columns (64-column blocks): G1 writes [K;Q]K^T 0, dq~^T 64, dW^T 128, dk~^T 192, dA_qk 256;
-// E1 frees 0, 128, 256; G2 writes dT 320, dBv^T 128, dBk^T 256; G3 Y 0; G4 dL' 128; G5 320 and 0.
+// E1 frees 0, 128, 256; G2 writes dV' V^T 320, dW K^T 0 (the two parts of dT, combined with the
+// per-token factors in E2), dBv^T 128, dBk^T 256; G3 Y 0; G4 dL' 128; G5 320 and 0.
 // Columns [384, 512) are never written by an MMA: they carry the GQA group's running dq / dk sums
 // (fp32) from one value head of the group to the next.
 // ------------------------------------------------------------------------------------------------
 namespace lay {  // shared-memory map (bytes from the 1024-aligned base)
 constexpr int KQ = 0, VT = 32768, DVP = 49152;
 constexpr int ST = 65536, DHT = 98304, DOT = 131072, VPT = 147456;           // phase 1
-constexpr int DWT = 65536, BV = 81920, BK = 98304, TT = 114688, DTT = 122880,  // phase 2 (over phase 1)
+constexpr int DWT = 65536, TT = 114688, DTT = 122880,                        // phase 2 (over phase 1)
               YT = 131072, PB1 = 139264, PB2 = 147456, QB1 = 155648;
 constexpr int QB2 = VT;                                                        // over V once consumed
 constexpr int DVS = DWT;     // dv rows, bf16 [64][128], from E2 until after G5 is issued
@@ -489,36 +490,23 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
       for (int j = 0; j < 16; ++j) daqf[i64 * 65 + c0 + j] = c0 + j <= i64 ? v[j] : 0.f;
     }
   }
-  for (int idx = tid; idx < 64 * 16; idx += kBThreads) {  // beta V and beta e^cum rk K (rows m)
-    const int m = idx >> 4, c8 = (idx & 15) * 8;
-    const uint4 xv = *reinterpret_cast<const uint4*>(sm + lay::VT + tc::sw128_offset(m, c8, 64));
-    const uint4 xk = *reinterpret_cast<const uint4*>(sm + lay::KQ + tc::sw128_offset(m, c8, 128));
-    const float fv = beta[m], fk = beta[m] * ecum[m] * rk[m];
-    const uint32_t av[4] = {xv.x, xv.y, xv.z, xv.w}, ak[4] = {xk.x, xk.y, xk.z, xk.w};
-    uint32_t ov[4], ok[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      ov[j] = tc::pack_bf16(bf_lo(av[j]) * fv, bf_hi(av[j]) * fv);
-      ok[j] = tc::pack_bf16(bf_lo(ak[j]) * fk, bf_hi(ak[j]) * fk);
-    }
-    *reinterpret_cast<uint4*>(sm + lay::BV + tc::sw128_offset(m, c8, 64)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
-    *reinterpret_cast<uint4*>(sm + lay::BK + tc::sw128_offset(m, c8, 64)) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
-  }
   sync_for_mma();
   tc::mbar_wait(&ldbar[1], ph, ws.err, 136);
   const uint32_t tta = tc::smem_u32(sm + lay::TT), dwa = tc::smem_u32(sm + lay::DWT);
   if (tid == 0) {  // ---- G2 ----
     const uint32_t dva = tc::smem_u32(sm + lay::DVP);
     const uint64_t d_dvm = tc::desc_mnmajor_sw128(dva, 8192), d_dwm = tc::desc_mnmajor_sw128(dwa, 16384),
-                   d_bv = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::BV)),
-                   d_bk = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::BK));
+                   d_v = tc::desc_kmajor_sw128(tc::smem_u32(sm + lay::VT));
     const uint32_t id_t = tc::idesc_bf16(64, 64, true, false);
+    // dT = dV' (beta V)^T + dW (beta e^cum r_k K)^T = (dV' V^T + dW K^T diag(e^cum r_k)) diag(beta): the two
+    // products on the raw V and K rows, the per-token factors in E2's fp32 epilogue
 #pragma unroll 4
-    for (int k0 = 0; k0 < 128; k0 += 16)  // dT = dV' (beta V)^T, dV' read MN-major from the dV'^T tile
-      tc::mma_bf16(tbase + 320, d_dvm + k0 * 8, d_bv + (((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4), id_t, k0 > 0);
+    for (int k0 = 0; k0 < 128; k0 += 16)  // dV' V^T, dV' read MN-major from the dV'^T tile
+      tc::mma_bf16(tbase + 320, d_dvm + k0 * 8, d_v + (((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4), id_t, k0 > 0);
 #pragma unroll 4
-    for (int k0 = 0; k0 < 128; k0 += 16)  // dT += dW (beta e^cum r_k K)^T
-      tc::mma_bf16(tbase + 320, d_dwm + k0 * 8, d_bk + (((k0 >> 6) * 8192 + (k0 & 63) * 2) >> 4), id_t, true);
+    for (int k0 = 0; k0 < 128; k0 += 16)  // dW K^T, K = rows 0-63 of the [K;Q] tile
+      tc::mma_bf16(tbase + 0, d_dwm + k0 * 8, tc::desc_kmajor_sw128(kqa) + (((k0 >> 6) * 16384 + (k0 & 63) * 2) >> 4), id_t,
+                   k0 > 0);
     const uint64_t d_dvk = tc::desc_kmajor_sw128(dva), d_dwk = tc::desc_kmajor_sw128(dwa), d_t = tc::desc_mnmajor_sw128(tta, 8192);
     const uint32_t id_b = tc::idesc_bf16(128, 64, false, true);
 #pragma unroll
@@ -533,11 +521,24 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   // ---- E2 ------------------------------------------------------------------------------------
   {
     float v[16];
-    tmem_ld16f(lane_addr + 320, v);  // dT (M = 64)
-    if (mrow) {
+    tmem_ld16f(lane_addr + 320, v);  // dV' V^T (M = 64)
+    {
+      float z[16];
+      tmem_ld16f(lane_addr + 0, z);  // dW K^T
+      if (mrow) {  // dT[i][m] = beta_m (dV' V^T + e^cum_m r_k,m dW K^T)[i][m], lower triangle
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = c0 + j <= i64 ? v[j] : 0.f;
-      store_row16(sm + lay::DTT, 64, i64, c0, v);
+        for (int j4 = 0; j4 < 16; j4 += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(beta + c0 + j4), e4 = *reinterpret_cast<const float4*>(ecum + c0 + j4),
+                       k4 = *reinterpret_cast<const float4*>(rk + c0 + j4);
+          const float bs[4] = {b4.x, b4.y, b4.z, b4.w}, es[4] = {e4.x, e4.y, e4.z, e4.w}, ks[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int j = j4 + u;
+            v[j] = c0 + j <= i64 ? bs[u] * fmaf(es[u] * ks[u], z[j], v[j]) : 0.f;
+          }
+        }
+        store_row16(sm + lay::DTT, 64, i64, c0, v);
+      }
     }
     tmem_ld16f(lane_addr + 128, v);  // dBv^T row dv = r, columns m = c0 + j
     float x[16];
