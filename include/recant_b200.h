@@ -244,11 +244,10 @@ RB2_API int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_block
                    size_t ws_bytes, void* stream);
 /* rb2_nvfp4_gemm with two optional extras (no reference counterpart for the first; the second is
  * the "lora?" of the GEMM boundary):
- * - b_images: B's scale images precomputed by rb2_nvfp4_gemm_b_images (NULL = built per call as
- *   rb2_nvfp4_gemm does) -- for frozen weights, whose images are built once. The images are B's
- *   blocked scales laid out as the kernel moves them into tensor memory (each 512-byte atom
- *   repeated 4 times, the two 128-row halves of a 256-row tile interleaved per K step), 16-byte
- *   aligned, rb2_nvfp4_gemm_b_images_size(N, K) bytes.
+ * - b_images: B's scales as the kernel reads them, prepared by rb2_nvfp4_gemm_b_images for frozen
+ *   weights (NULL = read b_scales_blocked). The kernel reads the 128x4 blocked layout in place
+ *   (one 512-byte atom per 128-row block and 64-element K step), so these are a copy of B's
+ *   blocked scales: 16-byte aligned, rb2_nvfp4_gemm_b_images_size(N, K) bytes.
  * - lora_h (NULL = none): out = a . b^T * gA * gB + lora_scale * lora_h . lora_b^T with lora_h
  *   [M, lora_r] bf16 (row stride lora_ldh elements) and lora_b [N, lora_r] bf16, lora_r 8 or 16:
  *   QLinear's LoRA y + (alpha / r) (x A^T) B^T (layers.py:65-70, 86-97) with h = x A^T computed by
