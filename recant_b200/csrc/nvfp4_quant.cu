@@ -227,8 +227,8 @@ __device__ __forceinline__ void quant_block(uint32_t b, const Raw16<T>& raw, int
   // relative size 2^-24 each, plus the quotient's own half ulp). Every decision point of the
   // rounding (RN: 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5; SR: the grid 0.5, 1, 1.5, 2, 3, 4, 6) lies on
   // a multiple of 2^21 in the bit pattern, so when the bits of a' are more than 8 away from such a
-  // multiple, a' and the exact quotient fall on the same side of every point; otherwise (about one
-  // element in 1.3e5) the exact quotient is computed. q < 0 <=> x < 0 since denom > 0 (and -0
+  // multiple (SR; RN tests the points themselves, below), a' and the exact quotient fall on the same
+  // side of every point; otherwise the exact quotient is computed. q < 0 <=> x < 0 since denom > 0 (and -0
   // gives +0 / no sign bit in both); the sign is bit 3 of each nibble.
   const float rinv = __frcp_rn(denom);
   uint32_t packed[2] = {0u, 0u};
@@ -261,13 +261,20 @@ __device__ __forceinline__ void quant_block(uint32_t b, const Raw16<T>& raw, int
     // RN: away from the decision points the index is the nearest grid point, which the hardware
     // pair conversion (cvt.rn.satfinite.e2m1x2, values above 6 saturating to 6) gives for two
     // magnitudes at once; at a decision point it rounds ties to even where the reference rounds
-    // them toward zero, and those pairs take the exact path, which counts the points.
+    // them toward zero, and those pairs take the exact path, which counts the points. A pair is near
+    // a decision point when a' (1 - e) and a' (1 + e), e = 2^-19 (16 ulps, against a' being within
+    // 2.5 ulps of the exact quotient), convert differently: the two then lie on either side of a
+    // point; grid points and zeros convert alike on both sides and do not trigger.
 #pragma unroll
     for (int i = 0; i < 16; i += 2) {
       const float a0 = __fmul_rn(fabsf(v[i]), rinv), a1 = __fmul_rn(fabsf(v[i + 1]), rinv);
-      const uint32_t u0 = __float_as_uint(a0), u1 = __float_as_uint(a1);
       uint32_t nib = __nv_cvt_float2_to_fp4x2(make_float2(a0, a1), __NV_E2M1, cudaRoundNearest);  // a0 low
-      if ((u0 != 0u && ((u0 + 8u) & 0x1FFFFFu) <= 16u) || (u1 != 0u && ((u1 + 8u) & 0x1FFFFFu) <= 16u)) {
+      float l0 = a0, l1 = a1, h0 = a0, h1 = a1;
+      mul2(l0, l1, 1.0f - 0x1p-19f);
+      mul2(h0, h1, 1.0f + 0x1p-19f);
+      const uint32_t nl = __nv_cvt_float2_to_fp4x2(make_float2(l0, l1), __NV_E2M1, cudaRoundNearest),
+                     nh = __nv_cvt_float2_to_fp4x2(make_float2(h0, h1), __NV_E2M1, cudaRoundNearest);
+      if (((nl ^ nh) & 0xFFu) != 0u) {
         const float e0 = fabsf(__fdiv_rn(v[i], denom)), e1 = fabsf(__fdiv_rn(v[i + 1], denom));
         nib = uint32_t(e2m1_index(fminf(e0, 6.0f))) | (uint32_t(e2m1_index(fminf(e1, 6.0f))) << 4);
       }
