@@ -302,10 +302,15 @@ def nvfp4_leg(dev, pk, reps=10, gemm_reps=40):
         y = N.gemm_b200(a, W.fprop, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     g_clk = cg.stop()
+    pair_reps = gemm_reps // 4  # the SM-pair alternative (rb2_nvfp4_gemm_pair), for comparison
+    for _ in range(pair_reps):
+        y = N.gemm_pair_b200(a, W.fprop, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
     recs, _ = prof.read()
     del y
     q_ms = sum(t for n, t in recs if n in ("nvfp4_amax", "nvfp4_quant", "nvfp4_zero", "nvfp4_quant_small")) / reps
     g_ms = sum(t for n, t in recs if n == "nvfp4_gemm") / gemm_reps
+    p_ms = sum(t for n, t in recs if n == "nvfp4_gemm_pair") / pair_reps
     gbs = M * K * 2.5625 / (q_ms / 1e3) / 1e9
     tfl = 2.0 * M * Nn * K / (g_ms / 1e3) / 1e12
     fp4_peak = FP4_PER_BF16 * pk["bf16"]
@@ -314,7 +319,8 @@ def nvfp4_leg(dev, pk, reps=10, gemm_reps=40):
                          "peak_source": f"{pk['source']} HBM copy (MEASURED_PEAKS.json)", "clocks": q_clk},
             "gemm": {"shape": [M, Nn, K], "ms": round(g_ms, 4), "achieved": round(tfl, 1), "unit": "TFLOP/s",
                      "peak": round(fp4_peak, 1), "frac": round(tfl / fp4_peak, 4),
-                     "peak_source": f"4 x {pk['source']} bf16 burst (MEASURED_PEAKS.json)", "clocks": g_clk}}
+                     "peak_source": f"4 x {pk['source']} bf16 burst (MEASURED_PEAKS.json)", "clocks": g_clk,
+                     "sm_pair_alternative_ms": round(p_ms, 4)}}
 
 
 CONFIG1 = {"workload": "config1: GDN chunked fwd+bwd, B4 T4096 Hk16 Hv32 d128 chunk64, bf16 in / fp32 state",

@@ -259,6 +259,14 @@ RB2_API int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_bl
                               const uint8_t* b_images, const void* lora_h, int64_t lora_ldh, const void* lora_b,
                               int lora_r, float lora_scale, int lora_mode, int64_t M, int64_t N, int64_t K, void* out,
                               int out_dtype, void* ws, size_t ws_bytes, void* stream);
+/* rb2_nvfp4_gemm on SM pairs: two-CTA clusters (tcgen05 cta_group::2) computing 256 x 256 tiles, each
+ * CTA holding its own 128 rows of A and half of B's 256 rows (no multicast loads). Same arguments,
+ * layouts and results as rb2_nvfp4_gemm (no LoRA, no b_images); an alternative kept for measurement:
+ * at 16384 x 12288 x 4096 it takes 0.56 ms against rb2_nvfp4_gemm's 0.46 ms. */
+RB2_API int rb2_nvfp4_gemm_pair(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                                const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                                int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws,
+                                size_t ws_bytes, void* stream);
 /* rb2_nvfp4_gemm for M <= 4 rows of A (the decode step: one token per sequence; no counterpart in
  * the reference, whose GEMM backends serve every M alike, nvfp4.py:108-125): reads each row of B
  * once, one warp per row, instead of 128-row tensor-core tiles. Scales are the row-major e4m3 bytes

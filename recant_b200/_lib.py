@@ -46,6 +46,7 @@ SIGNATURES = {
     "rb2_nvfp4_block_scales": (_i, [_p, _i64, _i64, _p, _p]),
     "rb2_nvfp4_gemm_workspace_size": (_sz, [_i64, _i64, _i64]),
     "rb2_nvfp4_gemm": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _p]),
+    "rb2_nvfp4_gemm_pair": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _p]),
     "rb2_nvfp4_gemm_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i, _f, _i, _i64, _i64, _i64, _p, _i, _p,
                                _sz, _p]),
     "rb2_nvfp4_gemm_b_images_size": (_sz, [_i64, _i64]),

@@ -347,6 +347,301 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
   if (w == 1) tc::tmem_dealloc(tbase, 512);
 }
 
+// ------------------------------------------------------------------------------------------------
+// SM-pair variant (cta_group::2): a cluster of two CTAs computes one 256 x 256 output tile. Each CTA
+// holds its own 128 rows of A and its own 128-row half of B in shared memory; the pair's MMA
+// (M = 256, N = 256, K = 64), issued by the even CTA, reads both CTAs' operands and writes each CTA's
+// 128 accumulator rows (all 256 columns) into that CTA's tensor memory. A CTA thus reads only half of
+// B from L2 where a one-SM 128 x 256 tile reads all of it: 8 KB instead of 12 KB of codes per 128 x
+// 256 x 64 MMA step, and L2 -> SM traffic is what bounds the one-SM kernel at large shapes.
+//   both CTAs, warp 0: TMA of the CTA's A rows, B half and scale atoms (A: its own row block; B: both
+//     128-row halves, since each CTA's accumulator spans all 256 columns); the .cta_group::2 loads
+//     count their bytes on the even CTA's `full` barrier (plain loads, no multicast);
+//   even CTA, warp 10: per K step three atom copies into both CTAs' tensor memory
+//     (tcgen05.cp.cta_group::2), into one of NSF scale sets in turn, handed to the MMA thread
+//     through `sf_full` / `sf_free` (issued from one thread, copies and MMAs run one after the
+//     other; from two threads the copies of later stages overlap the MMAs);
+//   even CTA, warp 1: one pair MMA per K step; commits arrive on both CTAs' `empty`, `acc_full`;
+//   both CTAs, warps 2-9: the epilogue of the CTA's 128 rows; each warp releases the accumulator by
+//     an arrival on the even CTA's `acc_empty` (8 warps x 2 CTAs).
+// The scale atoms are read through 3-D tensor maps over the blocked layout, [row block][K step][128
+// u32]: a stage's 4 K steps of one row block are one box, and K steps or row blocks past the end
+// read as zero.
+namespace pair {
+constexpr int ROWS = 128;                                   // rows of A and of B per CTA
+constexpr int STAGES = 5;
+constexpr int A_BYTES = ROWS * BKB, B_BYTES = ROWS * BKB;
+constexpr int SFA_OFF = 0, SFB_OFF = 4 * kAtom, A_OFF = SFB_OFF + 8 * kAtom, B_OFF = A_OFF + A_BYTES;
+constexpr int STAGE_BYTES = B_OFF + B_BYTES;                // 38 KB
+constexpr int STAGE_TX = A_BYTES + B_BYTES + 12 * kAtom;    // bytes one CTA loads per stage
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+constexpr int NSF = 4;         // scale sets in tensor memory (stage g uses set g % NSF)
+constexpr int SF_COL0 = 256;  // TMEM: accumulator 0-255, scale sets of 48 columns from 256
+static_assert(SF_COL0 + NSF * 48 <= 512, "TMEM budget");
+constexpr int THREADS = kThreads + 32;                      // + warp 10: the scale-copy issuer
+static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && STAGE_BYTES % 1024 == 0, "SW128 alignment");
+static_assert(SMEM <= 227 * 1024, "shared memory");
+}  // namespace pair
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// the shared::cluster address of the variable at local shared address `saddr` in CTA `rank`
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+// every thread of both CTAs
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_u32(smem_dst)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+// tile of this CTA's rows into its own shared memory; the bytes are counted on `bar`, a
+// shared::cluster address (the even CTA's barrier)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_cp_sf_atom_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void mma_nvf4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t sfa_tmem, uint32_t sfb_tmem, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+// arrives on `bar` (same shared offset) in both CTAs of the pair once the issuing thread's earlier
+// pair MMAs and copies have completed
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          tc::smem_u32(bar)),
+      "h"(uint16_t(3))
+      : "memory");
+}
+// arrives on `bar` in this CTA only
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tc::smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// scales 32 accumulator values (fp32 bits) and stores them to out[row][col0 ...], columns < N
+__device__ __forceinline__ void store_out32(uint32_t (&r)[32], float scale, void* out, int out_bf16, int row, int col0,
+                                            int N) {
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) r[jj] = __float_as_uint(__uint_as_float(r[jj]) * scale);
+  if (out_bf16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + size_t(row) * N + col0;
+    if (col0 + 32 <= N && (N % 8) == 0) {
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 8)
+        *reinterpret_cast<uint4*>(o + jj) = make_uint4(
+            tc::pack_bf16(__uint_as_float(r[jj]), __uint_as_float(r[jj + 1])),
+            tc::pack_bf16(__uint_as_float(r[jj + 2]), __uint_as_float(r[jj + 3])),
+            tc::pack_bf16(__uint_as_float(r[jj + 4]), __uint_as_float(r[jj + 5])),
+            tc::pack_bf16(__uint_as_float(r[jj + 6]), __uint_as_float(r[jj + 7])));
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj)
+        if (col0 + jj < N) o[jj] = __float2bfloat16_rn(__uint_as_float(r[jj]));
+    }
+  } else {
+    float* o = static_cast<float*>(out) + size_t(row) * N + col0;
+    if (col0 + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 4)
+        *reinterpret_cast<float4*>(o + jj) = make_float4(__uint_as_float(r[jj]), __uint_as_float(r[jj + 1]),
+                                                         __uint_as_float(r[jj + 2]), __uint_as_float(r[jj + 3]));
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj)
+        if (col0 + jj < N) o[jj] = __uint_as_float(r[jj]);
+    }
+  }
+}
+
+// Persistent: cluster c (CTAs 2c, 2c + 1) handles 256 x 256 tiles c, c + clusters, ... (row-major
+// over the tile grid). Every wait is bounded; a timed-out wait records its code in *err.
+__global__ void __launch_bounds__(pair::THREADS, 1)
+nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ CUtensorMap map_sfa, const __grid_constant__ CUtensorMap map_sfb,
+                       const float* __restrict__ ga, const float* __restrict__ gb, int M, int N, int K,
+                       void* __restrict__ out, int out_bf16, int* __restrict__ err) {
+  using namespace pair;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023);
+  __shared__ uint64_t full[STAGES], empty[STAGES], acc_full, acc_empty, drain, sf_full[NSF], sf_free[NSF], cp_drain;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const uint32_t rank = cta_rank_in_cluster();
+  const int cluster = int(blockIdx.x >> 1), nclusters = int(gridDim.x >> 1);
+  const int ksteps = K / 64, nstages = (ksteps + 3) / 4;
+  const int ntn = (N + 255) / 256, ntiles = ((M + 255) / 256) * ntn;
+
+  if (w == 1) {  // the same warp in both CTAs: the pair's allocation covers both tensor memories
+    tmem_alloc_pair(&tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(&acc_full, 1);
+    tc::mbar_init(&acc_empty, 16);
+    tc::mbar_init(&drain, 1);
+    for (int b = 0; b < NSF; ++b) {
+      tc::mbar_init(&sf_full[b], 1);
+      tc::mbar_init(&sf_free[b], 1);
+    }
+    tc::mbar_init(&cp_drain, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised before any load or arrival can reach them
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+
+  if (w == 0) {
+    if (l == 0) {  // ---------------- producer (both CTAs) ----------------
+      int g = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters) {
+        const int tm = t / ntn, tn = t % ntn;
+        for (int kt = 0; kt < nstages; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = tc::mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, err, 211))) break;
+          const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES), fb = cluster_addr(tc::smem_u32(&full[s]), 0);
+          if (rank == 0) tc::mbar_expect_tx(&full[s], 2 * STAGE_TX);  // both CTAs' bytes
+          tma_load_2d_pair(st + A_OFF, &map_a, kt * BKB, tm * 256 + ROWS * int(rank), fb);
+          tma_load_2d_pair(st + B_OFF, &map_b, kt * BKB, tn * 256 + ROWS * int(rank), fb);
+          tma_load_3d_pair(st + SFA_OFF, &map_sfa, 0, 4 * kt, 2 * tm + int(rank), fb);
+          tma_load_3d_pair(st + SFB_OFF, &map_sfb, 0, 4 * kt, 2 * tn, fb);
+          tma_load_3d_pair(st + SFB_OFF + 4 * kAtom, &map_sfb, 0, 4 * kt, 2 * tn + 1, fb);
+        }
+      }
+    }
+  } else if (w == 1) {
+    if (l == 0 && rank == 0) {  // ---------------- MMA issuer (even CTA) ----------------
+      constexpr uint32_t idesc = idesc_nvf4(256, 256);
+      int g = 0, local = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters, ++local) {
+        if (!(ok = tc::mbar_wait(&acc_empty, (local & 1) ^ 1, err, 214))) break;
+        tc::fence_after_sync();
+        for (int kt = 0; kt < nstages; ++kt, ++g) {
+          const int s = g % STAGES, b = g % NSF;
+          if (!(ok = tc::mbar_wait(&full[s], (g / STAGES) & 1, err, 212))) break;
+          if (!(ok = tc::mbar_wait(&sf_full[b], (g / NSF) & 1, err, 216))) break;  // the stage's scales are in TMEM
+          tc::fence_after_sync();
+          const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
+          const int steps = min(4, ksteps - 4 * kt);
+          const uint32_t t_sfa = tbase + SF_COL0 + b * 48, t_sfb = t_sfa + 16;
+          const uint64_t d_a = tc::desc_kmajor_sw128(st + A_OFF), d_b = tc::desc_kmajor_sw128(st + B_OFF);
+          for (int kk = 0; kk < steps; ++kk)
+            mma_nvf4_pair(tbase, d_a + 2 * kk, d_b + 2 * kk, idesc, t_sfa + 4 * kk, t_sfb + 8 * kk, kt > 0 || kk > 0);
+          mma_commit_pair(&empty[s]);
+          mma_commit_pair_local(&sf_free[b]);  // the scale set may be overwritten once these MMAs are done
+        }
+        mma_commit_pair(&acc_full);
+      }
+      mma_commit_pair(&drain);  // completes once every MMA issued above has
+    }
+  } else if (w == 10) {
+    if (l == 0 && rank == 0) {  // ---------------- scale-copy issuer (even CTA) ----------------
+      // copies a stage's scale atoms into scale set g % NSF of both CTAs' tensor memory, up to NSF - 1
+      // stages ahead of the MMAs
+      int g = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters) {
+        for (int kt = 0; kt < nstages; ++kt, ++g) {
+          const int s = g % STAGES, b = g % NSF;
+          if (!(ok = tc::mbar_wait(&full[s], (g / STAGES) & 1, err, 217))) break;
+          if (!(ok = tc::mbar_wait(&sf_free[b], ((g / NSF) & 1) ^ 1, err, 218))) break;
+          tc::fence_after_sync();
+          const uint32_t st = tc::smem_u32(sm + s * STAGE_BYTES);
+          const int steps = min(4, ksteps - 4 * kt);
+          const uint32_t t_sfa = tbase + SF_COL0 + b * 48, t_sfb = t_sfa + 16;
+          const uint64_t d_sfa = desc_sf_atom(st + SFA_OFF), d_sfb = desc_sf_atom(st + SFB_OFF);
+          constexpr uint32_t kA = kAtom >> 4, kH = 4 * kAtom >> 4;  // one atom; one B half (16-byte units)
+          for (int kk = 0; kk < steps; ++kk) {  // K step kk: A -> columns 4kk .. 4kk + 3, B halves -> 8kk .. 8kk + 7
+            tmem_cp_sf_atom_pair(t_sfa + 4 * kk, d_sfa + kk * kA);
+            tmem_cp_sf_atom_pair(t_sfb + 8 * kk, d_sfb + kk * kA);
+            tmem_cp_sf_atom_pair(t_sfb + 8 * kk + 4, d_sfb + kH + kk * kA);
+          }
+          mma_commit_pair_local(&sf_full[b]);
+        }
+      }
+      mma_commit_pair_local(&cp_drain);
+      tc::mbar_wait(&cp_drain, 0, err, 219);  // no copy of this thread is still in flight
+    }
+  } else {  // ---------------- epilogue: warps 2..9 of both CTAs ----------------
+    static_assert(pair::THREADS == 11 * 32, "warps 0, 1 and 10 are handled above");
+    const int q = w & 3, half = (w - 2) >> 2;
+    const float scale = ga[0] * gb[0];
+    const uint32_t ae = cluster_addr(tc::smem_u32(&acc_empty), 0);
+    int local = 0;
+    for (int t = cluster; t < ntiles; t += nclusters, ++local) {
+      const int tm = t / ntn, tn = t % ntn;
+      const uint32_t lane_addr = tbase + (uint32_t(32 * q) << 16) + half * 128;
+      if (!tc::mbar_wait(&acc_full, local & 1, err, 213)) break;  // (no named barriers: leaving is safe)
+      tc::fence_after_sync();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_raw(lane_addr + 32 * c, r[c]);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      tc::fence_before_sync();
+      __syncwarp();
+      if (l == 0) mbar_arrive_cluster(ae);
+      const int row = tm * 256 + ROWS * int(rank) + 32 * q + l;
+      if (row >= M) continue;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int col0 = tn * 256 + half * 128 + 32 * c;
+        if (col0 >= N) break;
+        store_out32(r[c], scale, out, out_bf16, row, col0, N);
+      }
+    }
+  }
+  if (w == 1 && l == 0) tc::mbar_wait(&drain, 0, err, 215);  // the pair's MMAs no longer touch either CTA
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the other may still signal its barriers
+  tc::fence_after_sync();
+  if (w == 1) tmem_dealloc_pair(tbase, 512);
+}
+
 // 2-D byte tensor [rows][cols_bytes], box [box_rows][128 bytes], 128-byte swizzle.
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_bytes, int box_rows) {
   auto fn = tmap_encoder();
@@ -366,6 +661,62 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols_byte
     return RB2_ECUDA;
   }
   return RB2_OK;
+}
+
+// The blocked scales of `rows` rows as a 3-D u32 tensor [row block][K step][128] (one 512-byte atom
+// per (row block, K step)), box [1][4][128]: the four K steps of one row block that a stage uses.
+int make_map_sf(CUtensorMap* map, const void* base, int64_t rows, int64_t K) {
+  auto fn = tmap_encoder();
+  if (!fn) {
+    set_error("nvfp4_gemm: cuTensorMapEncodeTiled unavailable");
+    return RB2_ECUDA;
+  }
+  const int64_t nrb = (rows + 127) / 128, ks = K / 64;
+  cuuint64_t dims[3] = {128u, cuuint64_t(ks), cuuint64_t(nrb)};
+  cuuint64_t strides[2] = {cuuint64_t(kAtom), cuuint64_t(ks) * kAtom};
+  cuuint32_t box[3] = {128u, 4u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("nvfp4_gemm: cuTensorMapEncodeTiled (scales) failed (%d)", int(r));
+    return RB2_ECUDA;
+  }
+  return RB2_OK;
+}
+
+// How many two-CTA clusters of the pair kernel can be resident at once on device `dev` (queried
+// once per device; 0 if the query fails, in which case the one-SM kernel is used).
+int pair_clusters(int dev) {
+  static int cache[64];
+  static bool have[64];
+  if (dev < 0 || dev >= 64) return 0;
+  if (have[dev]) return cache[dev];
+  int n = 0;
+  bool failed = true;
+  if (cudaFuncSetAttribute(nvfp4_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::SMEM) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(pair::THREADS);
+    cfg.dynamicSmemBytes = pair::SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    failed = cudaOccupancyMaxActiveClusters(&n, nvfp4_gemm_pair_kernel, &cfg) != cudaSuccess;
+  }
+  if (failed) {
+    n = 0;
+    cudaGetLastError();  // the failed query's error is not left for the next launch check
+  }
+  cache[dev] = n;
+  have[dev] = true;
+  return n;
 }
 
 }  // namespace
@@ -456,6 +807,65 @@ extern "C" int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_bl
                               void* stream) {
   return rb2_nvfp4_gemm_ex(a_codes, a_scales_blocked, a_gscale, b_codes, b_scales_blocked, b_gscale, nullptr, nullptr,
                            0, nullptr, 0, 0.f, 0, M, N, K, out, out_dtype, ws, ws_bytes, stream);
+}
+
+// The same product on SM pairs (cta_group::2, 256 x 256 tiles). Correct at every shape the one-SM
+// kernel takes, but slower at the shapes measured (16384 x 12288 x 4096: 0.56 ms against 0.46 ms):
+// per SM it moves the same tensor-memory scale copies as the one-SM kernel, and its pair MMA and
+// copies each take longer per SM than their one-SM counterparts.
+extern "C" int rb2_nvfp4_gemm_pair(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
+                                   const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,
+                                   int64_t M, int64_t N, int64_t K, void* out, int out_dtype, void* ws, size_t ws_bytes,
+                                   void* stream) {
+  RB2_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % 64 == 0, "nvfp4_gemm_pair: need M, N > 0 and K %% 64 == 0 (K=%lld)",
+                (long long)K);
+  RB2_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31), "nvfp4_gemm_pair: size");
+  RB2_CHECK_ARG(a_codes && b_codes && a_scales_blocked && b_scales_blocked && a_gscale && b_gscale && out && ws,
+                "nvfp4_gemm_pair: null pointer");
+  RB2_CHECK_ARG(out_dtype == RB2_F32 || out_dtype == RB2_BF16, "nvfp4_gemm_pair: out_dtype");
+  RB2_CHECK_ARG((reinterpret_cast<uintptr_t>(a_codes) & 15) == 0 && (reinterpret_cast<uintptr_t>(b_codes) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(a_scales_blocked) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(b_scales_blocked) & 15) == 0,
+                "nvfp4_gemm_pair: operands must be 16-byte aligned");
+  if (ws_bytes < rb2_nvfp4_gemm_workspace_size(M, N, K)) {
+    set_error("nvfp4_gemm_pair: workspace too small");
+    return RB2_EWORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int clusters = pair_clusters(dev);
+  if (clusters <= 0) {
+    set_error("nvfp4_gemm_pair: no two-CTA cluster of this kernel fits on the device");
+    return RB2_ECUDA;
+  }
+  int rc;
+  CUtensorMap pa, pb, psa, psb;
+  if ((rc = make_map(&pa, a_codes, M, K / 2, pair::ROWS)) || (rc = make_map(&pb, b_codes, N, K / 2, pair::ROWS)) ||
+      (rc = make_map_sf(&psa, a_scales_blocked, M, K)) || (rc = make_map_sf(&psb, b_scales_blocked, N, K)))
+    return rc;
+  RB2_CUDA(cudaMemsetAsync(ws, 0, sizeof(int), s), "nvfp4_gemm_pair: clear status");
+  const int64_t ptiles = ((M + 255) / 256) * ((N + 255) / 256);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(2 * (ptiles < clusters ? ptiles : clusters)));
+  cfg.blockDim = dim3(pair::THREADS);
+  cfg.dynamicSmemBytes = pair::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  {
+    ProfScope ps_("nvfp4_gemm_pair", s);
+    RB2_CUDA(cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel, pa, pb, psa, psb, a_gscale, b_gscale, int(M), int(N),
+                                int(K), out, int(out_dtype == RB2_BF16), static_cast<int*>(ws)),
+             "nvfp4_gemm_pair: launch");
+  }
+  RB2_CHECK_LAUNCH("nvfp4_gemm_pair");
+  return RB2_OK;
 }
 
 extern "C" size_t rb2_nvfp4_gemm_b_images_size(int64_t N, int64_t K) {

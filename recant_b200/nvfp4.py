@@ -131,6 +131,30 @@ def gemm_b200(a, b, out_dtype=torch.float32, lora=None, lora_mode=0) -> torch.Te
     return out
 
 
+def gemm_pair_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
+    """The product of :func:`gemm_b200` (no LoRA) on SM pairs: two-CTA clusters computing 256 x 256
+    tiles (rb2_nvfp4_gemm_pair). Same results; slower than the one-SM kernel at the shapes measured,
+    kept as the measured alternative."""
+    m, k = a.shape
+    n, kb = b.shape
+    if k != kb:
+        raise ValueError(f"recant_b200.gemm_pair_b200: K mismatch {k} vs {kb}")
+    if not a.codes.is_cuda:
+        raise ValueError("recant_b200.gemm_pair_b200: operands must be CUDA tensors (no CPU path)")
+    out = torch.empty(m, n, dtype=out_dtype, device=a.codes.device)
+    lib = L.lib()
+    wsb = lib.rb2_nvfp4_gemm_workspace_size(m, n, k)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=a.codes.device)
+    ga = a.gscale.reshape(1).to(torch.float32).contiguous()
+    gb = b.gscale.reshape(1).to(torch.float32).contiguous()
+    st = lib.rb2_nvfp4_gemm_pair(L.ptr(a.codes.contiguous()), L.ptr(blocked_scales(a)), L.ptr(ga),
+                                 L.ptr(b.codes.contiguous()), L.ptr(blocked_scales(b)), L.ptr(gb), m, n, k,
+                                 L.ptr(out), _DT[out_dtype], L.ptr(ws), wsb,
+                                 torch.cuda.current_stream(a.codes.device).cuda_stream)
+    L.check(st, "nvfp4_gemm_pair")
+    return out
+
+
 @dataclass
 class FP4Weight:
     """Frozen NVFP4 weight with its fprop (Q(rht(W)) [N,K]) and dgrad (Q(rht(W^T)) [K,N]) copies,

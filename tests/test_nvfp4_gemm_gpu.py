@@ -39,6 +39,25 @@ def test_gemm_matches_emulated(M, N, K):
     assert _rel(out16, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (300, 2048, 1024), (257, 384, 320), (64, 100, 64), (512, 1024, 4096)])
+def test_gemm_pair_matches_emulated_and_one_sm(M, N, K):
+    """The SM-pair kernel (cta_group::2, 256 x 256 tiles): rows past M, columns past N and a ragged
+    last K stage as above; against the emulated GEMM and against the one-SM kernel's output."""
+    from recant_b200 import gemm_b200
+    from recant_b200.nvfp4 import gemm_pair_b200
+    gen = torch.Generator().manual_seed(M + N + K + 1)
+    x = torch.randn(M, K, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=gen) * 0.05).to(torch.bfloat16).cuda()
+    a, b = _fp4(x), _fp4(w)
+    out = gemm_pair_b200(a, b)
+    ref = ON.gemm_emulated(_oracle(a, K), _oracle(b, K))
+    assert _rel(out.cpu().numpy(), ref) < TOL
+    one = gemm_b200(a, b)
+    assert _rel(out.cpu().numpy(), one.cpu().numpy()) < 1e-6
+    out16 = gemm_pair_b200(a, b, out_dtype=torch.bfloat16).float().cpu().numpy()
+    assert _rel(out16, ref) < 1e-2
+
+
 def test_gemm_on_reference_layout_scales():
     """Operands without pre-blocked scales (e.g. quantized by the reference) get blocked on the GPU."""
     from recant_b200 import nvfp4 as N
