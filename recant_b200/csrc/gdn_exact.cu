@@ -146,6 +146,13 @@ __global__ void chunk_table_kernel(const int64_t* __restrict__ cu, int64_t n_seq
     ct.seq_chunk0[n_seqs] = carry;
     *ct.n_chunks = carry;
   }
+  // entries past the last chunk read as empty (len 0): a kernel launched over max_chunks can skip
+  // its chunk from its own entry, without first reading n_chunks
+  for (int idx = carry + int(threadIdx.x); idx < max_chunks; idx += 1024) {
+    ct.tok0[idx] = 0;
+    ct.len[idx] = 0;
+    ct.seq[idx] = 0;
+  }
 }
 
 // ------------------------------------------------------------------------------------------

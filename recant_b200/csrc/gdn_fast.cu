@@ -220,10 +220,11 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
   __shared__ uint32_t tmem_base;
 
   const int ci = blockIdx.x, h = blockIdx.y;
-  if (ci >= *ws.ct.n_chunks) return;
+  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci];  // len 0: past the last chunk (the grid is max_chunks)
+  if (L <= 0) return;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int r = 32 * (w & 3) + l, hh = w >> 2, c0 = 32 * hh;
-  const int t0 = ws.ct.tok0[ci], L = ws.ct.len[ci], hk = h / p.group;
+  const int hk = h / p.group;
   const int64_t ch = int64_t(ci) * p.Hv + h;
 
   if (w == 0) {
@@ -238,12 +239,19 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
     tc::tma_rows128(kq, 16384, 64, &map_q, hk, t0, &bar[2]);
     tc::tma_rows128(vt, 8192, 0, &map_v, h, t0, &bar[2]);
   }
-  if (tid < 64) {
-    gv[tid] = tid < L ? p.g[int64_t(t0 + tid) * p.Hv + h] : 0.f;
-    beta[tid] = tid < L ? __bfloat162float(static_cast<const bf16*>(p.beta)[int64_t(t0 + tid) * p.Hv + h]) : 0.f;
+  // per-token g and beta: loaded into registers now, stored to shared memory after the TMA wait, so
+  // that their latency overlaps the row loads instead of holding up the barrier-init sync
+  float g_r = 0.f, beta_r = 0.f;
+  if (tid < 64 && tid < L) {
+    g_r = p.g[int64_t(t0 + tid) * p.Hv + h];
+    beta_r = __bfloat162float(static_cast<const bf16*>(p.beta)[int64_t(t0 + tid) * p.Hv + h]);
   }
   __syncthreads();  // barrier init visible
   tc::mbar_wait(&bar[2], 0, ws.err, 100);
+  if (tid < 64) {
+    gv[tid] = g_r;
+    beta[tid] = beta_r;
+  }
   if (L < 64) {  // rows past the end of the sequence
     tc::zero_rows_tail(kq, 16384, 0, L, 256);
     tc::zero_rows_tail(kq, 16384, 64, L, 256);

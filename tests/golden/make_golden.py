@@ -126,14 +126,19 @@ def _reference_block(ref_root: str):
 
 
 def block_main(ref_root: str) -> None:
-    """``tests/golden/block_golden.npz``: the reference block's weights, a seeded input [1, 70, 256]
-    and the forward output."""
+    """``tests/golden/block_golden.npz``: the reference block's weights, a seeded input [1, 70, 256],
+    the forward output and out_proj's input ``y`` (the gated norm's output, before out_proj quantizes
+    it to NVFP4), captured by a forward pre-hook on the reference's out_proj."""
     blk, arrays, gen, _ = _reference_block(ref_root)
     x = torch.randn(1, 70, 256, generator=gen).to(torch.bfloat16)
+    seen = {}
+    hook = blk.out_proj.register_forward_pre_hook(lambda mod, args: seen.setdefault("y", args[0].detach().clone()))
     with torch.no_grad():
         out = blk(x)
+    hook.remove()
     arrays["x"] = x.float().numpy()
     arrays["out"] = out.float().numpy()
+    arrays["y"] = seen["y"].float().numpy()
     np.savez_compressed(os.path.join(HERE, "block_golden.npz"), **arrays)
     print("block golden: out", tuple(out.shape), float(out.float().abs().mean()))
 
@@ -142,21 +147,26 @@ def decode_main(ref_root: str) -> None:
     """``tests/golden/block_decode_golden.npz``: the same reference block (weights in
     block_golden.npz) driven as the serving engine drives it (serve/engine.py:107-119), with a
     ``LayerCache`` (layers.py:111-130) over 2 sequences of a seeded input [2, 48, 256]: a 40-token
-    prefill, three single-token steps, then a 5-token chunk. Stores every output, the cache's conv
-    state after each call and its recurrent state after the prefill and at the end."""
+    prefill, three single-token steps, then a 5-token chunk. Stores every output, out_proj's input
+    ``y`` of every call (forward pre-hook), the cache's conv state after each call and its
+    recurrent state after the prefill and at the end."""
     blk, _, _, layers = _reference_block(ref_root)
     gen = torch.Generator().manual_seed(12)
     x = torch.randn(2, 48, 256, generator=gen).to(torch.bfloat16)
     cache = layers.LayerCache()
     calls = [(0, 40), (40, 41), (41, 42), (42, 43), (43, 48)]
     arrays = {"x": x.float().numpy()}
+    seen = []
+    hook = blk.out_proj.register_forward_pre_hook(lambda mod, args: seen.append(args[0].detach().clone()))
     with torch.no_grad():
         for i, (s, e) in enumerate(calls):
             out = blk(x[:, s:e], cache, s)
             arrays[f"out{i}"] = out.float().numpy()
+            arrays[f"y{i}"] = seen[-1].float().numpy()
             arrays[f"conv_state{i}"] = cache.conv_state.float().numpy()
             if i in (0, len(calls) - 1):  # after the prefill and at the end
                 arrays[f"rec_state{i}"] = cache.rec_state.float().numpy()
+    hook.remove()
     arrays["calls"] = np.array(calls, dtype=np.int64)
     np.savez_compressed(os.path.join(HERE, "block_decode_golden.npz"), **arrays)
     print("decode golden:", [tuple(arrays[f"out{i}"].shape) for i in range(len(calls))])
