@@ -1,6 +1,8 @@
 """NVFP4 block-scaled GEMM parity: tcgen05 kind::mxf4nvf4 vs the emulated reference GEMM
 (dequantise both operands, fp32 matmul; recant/model/nvfp4.py:108-110). Tolerance 5e-3 relative
 Frobenius (the reference's own check, recant/backends.py:21-35, allows 3e-2)."""
+import random
+
 import numpy as np
 import pytest
 import torch
@@ -110,9 +112,18 @@ def test_fp4_linear_fwd_bwd():
     ref = ON.gemm_emulated(_oracle(N.quantize_fast(x.detach().reshape(-1, 256), True, False), 256), _oracle(W.fprop, 256))
     assert _rel(y.detach().float().reshape(-1, 512).cpu().numpy(), ref) < 1e-2
     dy = torch.randn(4, 32, 512, generator=gen).to(torch.bfloat16).cuda()
+    random.seed(1234)  # the backward's stochastic-rounding seed comes from random.getrandbits
     y.backward(dy)
     exact = (dy.float().reshape(-1, 512) @ w.float()).cpu().numpy()
+    # against the exact product: within NVFP4's own quantization error
     assert x.grad.shape == x.shape and _rel(x.grad.float().reshape(-1, 256).cpu().numpy(), exact) < 0.2
+    # against the same SR codes (re-drawn with the same seed) through the emulated GEMM: the dgrad
+    # itself, pinned at the bf16 output rounding
+    random.seed(1234)
+    d = N.quantize_fast(dy.reshape(-1, 512), True, True)
+    ref_dx = ON.gemm_emulated(_oracle(d, 512), _oracle(W.dgrad, 512))
+    assert _rel(x.grad.float().reshape(-1, 256).cpu().numpy(), ref_dx) < 5e-3
+    assert torch.equal(x.grad.reshape(-1, 256), N.gemm_b200(d, W.dgrad, out_dtype=torch.bfloat16))
 
 
 @pytest.mark.parametrize("M,N,K", [(257, 384, 320), (1, 4096, 4096), (64, 100, 64)])
