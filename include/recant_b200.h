@@ -290,6 +290,26 @@ RB2_API int rb2_profile_disable(void);
 RB2_API int rb2_profile_read(int max_records, char* names, size_t name_stride, float* ms);
 RB2_API int rb2_profile_dropped(void);
 
+/* ---------------------------------------------------------------------------------------------
+ * Device status words (the reference's wrapper contract: device-side guards write an error word
+ * that the wrapper checks). Every mbarrier wait in this library's kernels is bounded: when one runs
+ * out (a load or a product that never completes), the kernel records a nonzero code in its op's
+ * status word, skips the rest of its work and returns, so the context stays usable. The word is the
+ * first 4 bytes of the op's workspace for rb2_gdn_fwd / rb2_gdn_bwd (of the saved part, with
+ * rb2_gdn_workspace_split), rb2_nvfp4_gemm / _ex / _pair; the operation clears it when it starts
+ * (the GDN forward; the GEMM calls). rb2_skinny_gemm keeps its word in the library.
+ * ------------------------------------------------------------------------------------------- */
+/* Synchronises `stream`, copies the status word at device address `status_word` to *code and, with
+ * `clear`, zeroes it. */
+RB2_API int rb2_status_read(const void* status_word, int* code, int clear, void* stream);
+/* rb2_skinny_gemm's status word (synchronises the device; `clear` zeroes it). */
+RB2_API int rb2_skinny_gemm_status(int* code, int clear);
+/* Self-test of the bounded wait: one kernel waits on an mbarrier that one arrival completed (it must
+ * return at once; if not, code 902) and then on one that nothing completes, which must give up after
+ * `max_polls` polls (0 < max_polls <= 2^24; 2^14 polls take well under a millisecond) and record 901
+ * in the device int `*status`. Afterwards the context is usable as before. */
+RB2_API int rb2_selftest_wait(int* status, unsigned int max_polls, void* stream);
+
 /* Diagnostic (no counterpart in the reference): one-tile tcgen05 product D[M,N] = A . B^T with
  * bf16 A, B given K-major (a_mn/b_mn = 0: A[m*K+k]) or MN-major (1: A[k*M+m]); M in {64,128},
  * N, K in {64,128}; fp32 D. Validates the tensor-core operand layouts on this device. */

@@ -6,12 +6,14 @@ host side that mirrors the reference's backend registries (recant/model/ops.py a
 recant/model/nvfp4.py) so the reference's callers can use it unchanged.
 """
 from . import _lib
+from ._lib import DeviceStatusError, set_status_checks
 from .gdn import GDN_BACKENDS, gdn_b200, gdn_core, gdn_recurrent, get_gdn_backend, set_gdn_backend
 from .nvfp4 import FP4Tensor, gemm_b200, quantize_activation, quantize_fast
 from .segmented import gdn_segmented
 
 __all__ = ["GDN_BACKENDS", "gdn_b200", "gdn_core", "gdn_recurrent", "get_gdn_backend", "set_gdn_backend", "FP4Tensor",
-           "gemm_b200", "quantize_activation", "quantize_fast", "gdn_segmented"]
+           "gemm_b200", "quantize_activation", "quantize_fast", "gdn_segmented", "set_status_checks",
+           "DeviceStatusError"]
 
 
 def library_version() -> str:

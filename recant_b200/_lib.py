@@ -47,6 +47,9 @@ SIGNATURES = {
     "rb2_nvfp4_gemm_workspace_size": (_sz, [_i64, _i64, _i64]),
     "rb2_nvfp4_gemm": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _p]),
     "rb2_nvfp4_gemm_pair": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _p]),
+    "rb2_status_read": (_i, [_p, C.POINTER(_i), _i, _p]),
+    "rb2_skinny_gemm_status": (_i, [C.POINTER(_i), _i]),
+    "rb2_selftest_wait": (_i, [_p, C.c_uint, _p]),
     "rb2_nvfp4_gemm_ex": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i, _f, _i, _i64, _i64, _i64, _p, _i, _p,
                                _sz, _p]),
     "rb2_nvfp4_gemm_b_images_size": (_sz, [_i64, _i64]),
@@ -95,6 +98,58 @@ def check(status: int, what: str) -> None:
         import torch
         raise torch.cuda.OutOfMemoryError(f"recant_b200 {what}: {msg}")
     raise LibraryError(f"recant_b200 {what} failed (status {status}): {msg}")
+
+
+# Device status words. Every bounded wait in the library's kernels gives up after a limit instead of
+# spinning for ever, records a code in its op's status word (the first 4 bytes of the op's workspace;
+# the narrow projection's is a device variable) and lets the kernel finish. Reading a word
+# synchronises, so the wrappers read them only when status checks are on.
+_status_checks = [False]
+
+
+def set_status_checks(on: bool) -> None:
+    """After every GDN, NVFP4 GEMM and narrow-projection call, read the op's device status word
+    (synchronising the stream) and raise DeviceStatusError if a bounded wait ran out."""
+    _status_checks[0] = bool(on)
+
+
+def status_checks() -> bool:
+    return _status_checks[0]
+
+
+class DeviceStatusError(RuntimeError):
+    """A bounded device wait ran out: the kernel recorded ``code`` and returned without finishing."""
+
+    def __init__(self, what: str, code: int):
+        super().__init__(f"recant_b200 {what}: a bounded device wait ran out (code {code}); the kernel "
+                         f"returned early and its outputs are not valid")
+        self.code = code
+
+
+def check_status(ws, what: str) -> None:
+    """Raise DeviceStatusError if the status word at the start of ``ws`` (a device tensor holding an
+    op's workspace) is non-zero. Only when status checks are on."""
+    if not _status_checks[0]:
+        return
+    code = C.c_int(0)
+    check(lib().rb2_status_read(ws.data_ptr(), C.byref(code), 0, _current_stream(ws)), "status_read")
+    if code.value:
+        raise DeviceStatusError(what, code.value)
+
+
+def check_skinny_status(what: str = "skinny_gemm") -> None:
+    """As check_status for the narrow projection, whose status word is a device variable (cleared when read)."""
+    if not _status_checks[0]:
+        return
+    code = C.c_int(0)
+    check(lib().rb2_skinny_gemm_status(C.byref(code), 1), "skinny_gemm_status")
+    if code.value:
+        raise DeviceStatusError(what, code.value)
+
+
+def _current_stream(t):
+    import torch
+    return torch.cuda.current_stream(t.device).cuda_stream
 
 
 class LaunchProfiler:

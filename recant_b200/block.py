@@ -61,6 +61,7 @@ def narrow_product(x2, w):
     out = torch.empty(M, npad, dtype=torch.bfloat16, device=x2.device)
     L.check(L.lib().rb2_skinny_gemm(_p(x2), x2.stride(0), _p(w), M, npad, K, _p(out), npad, L.BF16,
                                     _stream(x2.device)), "skinny_gemm")
+    L.check_skinny_status()
     return out[:, :n]
 
 

@@ -84,6 +84,16 @@ size_t exact_ws_bytes(const GdnProblem& p, ExactWs* out, void* base) {
 using namespace rb2;
 
 extern "C" const char* rb2_last_error(void) { return g_err; }
+
+extern "C" int rb2_status_read(const void* status_word, int* code, int clear, void* stream) {
+  RB2_CHECK_ARG(status_word && code && (reinterpret_cast<uintptr_t>(status_word) & 3) == 0,
+                "status_read: null or misaligned pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RB2_CUDA(cudaStreamSynchronize(s), "status_read: synchronize");
+  RB2_CUDA(cudaMemcpy(code, status_word, sizeof(int), cudaMemcpyDeviceToHost), "status_read: copy");
+  if (clear) RB2_CUDA(cudaMemset(const_cast<void*>(status_word), 0, sizeof(int)), "status_read: clear");
+  return RB2_OK;
+}
 extern "C" const char* rb2_version(void) { return "recant_b200 0.1 (sm_100a)"; }
 
 namespace rb2 {

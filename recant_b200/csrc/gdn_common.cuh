@@ -30,6 +30,7 @@ struct ChunkTable {
 
 // fp32 workspace of the exact path; every per-(chunk, head) array is indexed by ch = ci*Hv + h.
 struct ExactWs {
+  int* err;       // the op's device status word, the first 4 bytes of the (saved) workspace: 0 here
   ChunkTable ct;
   float* stats;   // [ch][4][64]: cum, rq, rk, beta
   float* qn;      // [ch][64][128]  q * rsqrt(|q|^2 + eps) * scale
@@ -59,6 +60,7 @@ inline int gdn_max_chunks(int64_t tokens, int64_t n_seqs) {
 template <typename Ws>
 size_t carve_exact(Carver& c, Ws& w, int64_t tokens, int64_t n_seqs, int Hv, int max_chunks, bool gqa) {
   const size_t nch = size_t(max_chunks) * Hv;
+  w.err = c.template take<int>(1);  // first: every GDN workspace starts with its status word
   w.ct.tok0 = c.template take<int>(max_chunks);
   w.ct.len = c.template take<int>(max_chunks);
   w.ct.seq = c.template take<int>(max_chunks);

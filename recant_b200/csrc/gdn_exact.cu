@@ -815,6 +815,7 @@ template <typename TIn>
 int exact_forward(const GdnProblem& p, ExactWs& ws, TIn* o, float* hT, cudaStream_t s) {
   int rc = launch_chunk_table(p, ws.ct, s);
   if (rc) return rc;
+  RB2_CUDA(cudaMemsetAsync(ws.err, 0, sizeof(int), s), "gdn exact: clear status");  // no bounded waits here
   if (p.max_chunks > 0) {
     if ((rc = set_smem(fwd_prep_kernel<TIn>, sizeof(PrepSmem)))) return rc;
     ProfScope ps_("gdn_exact_fwd_prep", s);

@@ -24,12 +24,12 @@ namespace rb2 {
 
 size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_chunks) {
   const size_t nch = size_t(max_chunks) * Hv;
+  w.err = c.take<int>(1);  // first: every GDN workspace starts with its status word
   w.ct.tok0 = c.take<int>(max_chunks);
   w.ct.len = c.take<int>(max_chunks);
   w.ct.seq = c.take<int>(max_chunks);
   w.ct.seq_chunk0 = c.take<int>(n_seqs + 1);
   w.ct.n_chunks = c.take<int>(1);
-  w.err = c.take<int>(1);
   w.stats = c.take<float>(nch * 512);
   w.tinv = c.take<__nv_bfloat16>(nch * 4096);
   w.aqk = c.take<__nv_bfloat16>(nch * 4096);

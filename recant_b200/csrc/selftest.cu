@@ -70,8 +70,35 @@ __global__ void __launch_bounds__(128) selftest_mma_kernel(const __nv_bfloat16* 
   if (tid < 32) tc::tmem_dealloc(tbase, 128);
 }
 
+// The bounded wait that every kernel's mbarrier waits use, made to run out on purpose: a barrier that
+// one arrival completes must be seen complete (else code 902 is recorded), and a barrier that nothing
+// arrives on must give up after max_polls polls and record 901, after which the kernel returns.
+__global__ void selftest_wait_kernel(int* __restrict__ status, uint32_t max_polls) {
+  __shared__ uint64_t bar[2];
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&bar[1])) : "memory");
+    tc::mbar_wait_polls(&bar[1], 0, status, 902, max_polls);  // phase 0 of bar[1] has completed
+    tc::mbar_wait_polls(&bar[0], 0, status, 901, max_polls);  // nothing completes phase 0 of bar[0]
+  }
+}
+
 }  // namespace
 }  // namespace rb2
+
+extern "C" RB2_API int rb2_selftest_wait(int* status, unsigned int max_polls, void* stream) {
+  using namespace rb2;
+  RB2_CHECK_ARG(status && max_polls > 0 && max_polls <= (1u << 24), "selftest_wait: status and 0 < max_polls <= 2^24");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  selftest_wait_kernel<<<1, 32, 0, s>>>(status, max_polls);
+  RB2_CHECK_LAUNCH("selftest_wait");
+  return RB2_OK;
+}
 
 extern "C" RB2_API int rb2_selftest_mma(const void* A, const void* B, float* D, int a_mn, int b_mn, int M, int N,
                                         int K, int* err, void* stream) {

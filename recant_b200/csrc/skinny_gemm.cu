@@ -169,3 +169,14 @@ extern "C" int rb2_skinny_gemm(const void* a, int64_t lda, const void* b, int64_
   RB2_CHECK_LAUNCH("skinny_gemm");
   return RB2_OK;
 }
+
+extern "C" int rb2_skinny_gemm_status(int* code, int clear) {
+  RB2_CHECK_ARG(code, "skinny_gemm_status: null pointer");
+  RB2_CUDA(cudaDeviceSynchronize(), "skinny_gemm_status: synchronize");
+  RB2_CUDA(cudaMemcpyFromSymbol(code, g_skinny_err, sizeof(int)), "skinny_gemm_status: read");
+  if (clear) {
+    const int zero = 0;
+    RB2_CUDA(cudaMemcpyToSymbol(g_skinny_err, &zero, sizeof(int)), "skinny_gemm_status: clear");
+  }
+  return RB2_OK;
+}

@@ -180,6 +180,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// As mbar_wait, with the number of polls given (the self-test of the bounded wait uses a short one).
+__device__ __forceinline__ bool mbar_wait_polls(uint64_t* bar, uint32_t parity, int* err, int code, uint32_t max_polls) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  if (err) atomicExch(err, code);
+  return false;
+}
+
 // ----- bulk copies (TMA engine): 1-D global -> shared, completion counted on an mbarrier ----------
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");

@@ -84,6 +84,7 @@ class _GDNFunction(torch.autograd.Function):
         st = L.lib().rb2_gdn_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(beta_k), L.ptr(h0), L.ptr(cu),
                                  *pb.args(), L.ptr(o), L.ptr(hT), L.ptr(ws), pb.ws_bytes, _stream(q.device))
         L.check(st, "gdn_fwd")
+        L.check_status(ws, "gdn_fwd")
         ctx.set_materialize_grads(False)  # an unused final state needs no zero gradient
         ctx.save_for_backward(q, k, v, g, beta_k, h0, cu)
         ctx.pb, ctx.ws = pb, ws
@@ -109,6 +110,7 @@ class _GDNFunction(torch.autograd.Function):
                                     L.ptr(dbeta), L.ptr(dh0), L.ptr(ws), pb.ws_bytes, L.ptr(scratch),
                                     pb.scratch_bytes, _stream(q.device), 3, 0)
         L.check(st, "gdn_bwd")
+        L.check_status(ws, "gdn_bwd")
         return dq, dk, dv, dg, dbeta.to(ctx.beta_dtype), dh0, None, None, None, None
 
 

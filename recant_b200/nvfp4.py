@@ -128,6 +128,7 @@ def gemm_b200(a, b, out_dtype=torch.float32, lora=None, lora_mode=0) -> torch.Te
                                L.ptr(out), _DT[out_dtype], L.ptr(ws), wsb,
                                torch.cuda.current_stream(a.codes.device).cuda_stream)
     L.check(st, "nvfp4_gemm")
+    L.check_status(ws, "nvfp4_gemm")
     return out
 
 
@@ -152,6 +153,7 @@ def gemm_pair_b200(a, b, out_dtype=torch.float32) -> torch.Tensor:
                                  L.ptr(out), _DT[out_dtype], L.ptr(ws), wsb,
                                  torch.cuda.current_stream(a.codes.device).cuda_stream)
     L.check(st, "nvfp4_gemm_pair")
+    L.check_status(ws, "nvfp4_gemm_pair")
     return out
 
 
