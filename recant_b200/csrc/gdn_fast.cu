@@ -321,6 +321,9 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
     st[320 + tid] = __expf(cum[63] - cum[tid]) * rk[tid];
     st[384 + tid] = expf(cum[tid]);
     st[448 + tid] = expf(cum[63] - cum[tid]);
+    // per token j, c_j log2(e) - log2(r_k,j), so that r_k,j e^(c_i - c_j) = 2^(c_i log2(e) - that) in the
+    // L / A_qk build below (into g's place: the cumulative sum has consumed it)
+    gv[tid] = cum[tid] * kLog2e - __log2f(rk[tid]);
   }
   // q~ rows for the backward walk now (the Q rows' shared memory is reused below): half-warp per row,
   // 8 elements per lane
@@ -334,24 +337,35 @@ __global__ void __launch_bounds__(256, 3) fast_prep_kernel(GdnProblem p, FastWs 
     for (int j = 0; j < 4; ++j) o[j] = tc::pack_bf16(bf_lo(xs[j]) * f, bf_hi(xs[j]) * f);
     *reinterpret_cast<uint4*>(img(ws.qt + ch * 8192) + tc::sw128_offset(row_, c8, 64)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  __syncthreads();  // the per-token exponents in gv
   uint32_t apk[16];  // A_qk row i (bf16 pairs), stored after the proxy fence below
   {
+    // the masked elements (j > i) may overflow the power of two; they are selected away, not used
     const int i = r & 63;
-    const float ci_ = cum[i];
+    const float ci2 = cum[i] * kLog2e;
+    float ex[32];
+#pragma unroll
+    for (int j4 = 0; j4 < 32; j4 += 4) {
+      const float4 e4 = *reinterpret_cast<const float4*>(gv + c0 + j4);
+      ex[j4] = ex2_approx(ci2 - e4.x);
+      ex[j4 + 1] = ex2_approx(ci2 - e4.y);
+      ex[j4 + 2] = ex2_approx(ci2 - e4.z);
+      ex[j4 + 3] = ex2_approx(ci2 - e4.w);
+    }
     if (r < 64) {
       const float bi = beta[i] * rk[i];
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         const int j = c0 + jj;
-        lt[i * 65 + j] = j < i ? bi * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
+        lt[i * 65 + j] = j < i ? bi * row[jj] * ex[jj] : 0.f;
       }
     } else {
       const float si = p.scale * rq[i];
 #pragma unroll
       for (int jj = 0; jj < 32; jj += 2) {
         const int j = c0 + jj;
-        const float a = j <= i ? si * rk[j] * row[jj] * __expf(ci_ - cum[j]) : 0.f;
-        const float b = j + 1 <= i ? si * rk[j + 1] * row[jj + 1] * __expf(ci_ - cum[j + 1]) : 0.f;
+        const float a = j <= i ? si * row[jj] * ex[jj] : 0.f;
+        const float b = j + 1 <= i ? si * row[jj + 1] * ex[jj + 1] : 0.f;
         apk[jj >> 1] = tc::pack_bf16(a, b);
       }
     }

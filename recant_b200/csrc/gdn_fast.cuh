@@ -64,6 +64,13 @@ __device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int
 }
 
 __device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
+// 2^x by the hardware approximation (MUFU.EX2; denormal results flush to zero)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float bf_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
 
 // (I + L)^-1 for strictly-lower L (fp32 64x64, stride 65) into T (stride 65); `nthr` threads, a
