@@ -591,19 +591,26 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
     const float bi = beta[i], rki = rk[i], sqi = p.scale * rq[i], ci_ = cum[i];
     float db = 0.f;
     float pb1[8], qb1[8], pb2[8], qb2[8];
+    float cj[8], rkj[8], ex[8];  // the columns' cum and r_k (16-byte loads) and e^(c_i - c_j), all first
+    *reinterpret_cast<float4*>(cj) = *reinterpret_cast<const float4*>(cum + cb);
+    *reinterpret_cast<float4*>(cj + 4) = *reinterpret_cast<const float4*>(cum + cb + 4);
+    *reinterpret_cast<float4*>(rkj) = *reinterpret_cast<const float4*>(rk + cb);
+    *reinterpret_cast<float4*>(rkj + 4) = *reinterpret_cast<const float4*>(rk + cb + 4);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) ex[jj] = __expf(ci_ - cj[jj]);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
       const int j = cb + jj;
-      const float gam = j <= i ? __expf(ci_ - cum[j]) : 0.f;
+      const float gam = j <= i ? ex[jj] : 0.f;
       const float P = j < i ? -v[jj] * gam : 0.f;
-      const float kkn = kkf[i * 65 + j] * rki * rk[j];
-      const float qkn = qkf[i * 65 + j] * sqi * rk[j];
+      const float kkn = kkf[i * 65 + j] * rki * rkj[jj];
+      const float qkn = qkf[i * 65 + j] * sqi * rkj[jj];
       const float daq = daqf[i * 65 + j];
       const float qm = daq * gam;
       db = fmaf(P, kkn, db);
       kkf[i * 65 + j] = P * bi * kkn + daq * qkn * gam;  // R
-      pb1[jj] = bi * rk[j] * P;
-      qb1[jj] = rk[j] * qm;
+      pb1[jj] = bi * rkj[jj] * P;
+      qb1[jj] = rkj[jj] * qm;
       pb2[jj] = bi * rki * P;
       qb2[jj] = sqi * qm;
     }
