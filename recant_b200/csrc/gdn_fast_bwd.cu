@@ -285,6 +285,13 @@ __device__ __forceinline__ float warp_colsum16(float (&v)[16]) {
 
 __device__ __forceinline__ void tmem_ld16f(uint32_t addr, float (&v)[16]) { tc::tmem_ld16(addr, v); }
 
+// N consecutive floats of a per-token vector in shared memory (16-byte aligned) by 16-byte loads
+template <int N>
+__device__ __forceinline__ void lds_vec(const float* p, float (&out)[N]) {
+#pragma unroll
+  for (int k = 0; k < N; k += 4) *reinterpret_cast<float4*>(out + k) = *reinterpret_cast<const float4*>(p + k);
+}
+
 __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  bf16* __restrict__ dq, bf16* __restrict__ dk,
                                                                  bf16* __restrict__ dv, float* __restrict__ dg,
@@ -679,12 +686,13 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   const bool wr = (l & 1) == 0;
   float dqh[16];
   {
-    float t1[16], v[16];
+    float t1[16], v[16], ec[16];
     tmem_ld16f(lane_addr + 0, dqh);   // (Qm k^)^T
     tmem_ld16f(lane_addr + 64, t1);   // dq~^T
+    lds_vec(ecum + c0, ec);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      dqh[j] = p.scale * fmaf(ecum[c0 + j], t1[j], dqh[j]);
+      dqh[j] = p.scale * fmaf(ec[j], t1[j], dqh[j]);
       v[j] = t1[j] * xr[j];
       t1[j] = dqh[j] * xr[j];
     }
@@ -696,14 +704,16 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   for (int j = 0; j < 16; ++j) kr_[j] = tile_elem(sm + lay::KQ, 128, c0 + j, r);
   float dkh[16];
   {
-    float t2[16], t3[16];
+    float t2[16], t3[16], ed[16], bt[16], ec[16];
     tmem_ld16f(lane_addr + 320, dkh);  // diag(beta) P k^ + P^T diag(beta) k^ + Qm^T q^   (transposed)
     tmem_ld16f(lane_addr + 192, t2);   // dk~^T
     tmem_ld16f(lane_addr + 256, t3);   // dBk^T
+    lds_vec(edec + c0, ed);
+    lds_vec(beta + c0, bt);
+    lds_vec(ecum + c0, ec);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const int i = c0 + j;
-      dkh[j] = fmaf(edec[i], t2[j], fmaf(beta[i] * ecum[i], t3[j], dkh[j]));
+      dkh[j] = fmaf(ed[j], t2[j], fmaf(bt[j] * ec[j], t3[j], dkh[j]));
       t2[j] *= kr_[j];
       t3[j] *= kr_[j];
     }
@@ -727,12 +737,18 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
   __syncthreads();
   {
     float gq[16], gk[16];
+    {
+      float rqv[16], rkv[16], a4[16], a5[16];
+      lds_vec(rq + c0, rqv);
+      lds_vec(rk + c0, rkv);
+      lds_vec(red2 + c0, a4);
+      lds_vec(red5 + c0, a5);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int i = c0 + j;
-      const float rqi = rq[i], rki = rk[i];
-      gq[j] = rqi * dqh[j] - xr[j] * rqi * rqi * rqi * red2[i];
-      gk[j] = rki * dkh[j] - kr_[j] * rki * rki * rki * red5[i];
+      for (int j = 0; j < 16; ++j) {
+        const float rqi = rqv[j], rki = rkv[j];
+        gq[j] = rqi * dqh[j] - xr[j] * rqi * rqi * rqi * a4[j];
+        gk[j] = rki * dkh[j] - kr_[j] * rki * rki * rki * a5[j];
+      }
     }
     bool last = true;  // this value head completes dq / dk of its key head
     if (p.group > 1) {  // GQA: the group's running sum in fp32, kept in TMEM columns [384, 512) until its last value head
