@@ -589,9 +589,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
         *reinterpret_cast<uint4*>(vpt + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
             make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
 #pragma unroll
-      const float* fk = cur.cum + 320;  // f_k = r_k e^(cum_last - cum)
+      float fk[32];
+      lds_vec(cur.cum + 320 + 32 * hh, fk);  // f_k = r_k e^(cum_last - cum)
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j] * fk[32 * hh + j], x[j + 1] * fk[32 * hh + j + 1]);
+      for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j] * fk[j], x[j + 1] * fk[j + 1]);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(vpk + tc::sw128_offset(r, 32 * hh + 8 * j, 128)) =
@@ -627,8 +628,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
       if (outs) {  // o^T = (S^T q^T) diag(f_q) + V'^T A_qk^T
         tc::tmem_ld32(lane_addr + 64 + 32 * hh, ox);
         tc::tmem_ld32(lane_addr + 128 + 32 * hh, x);
+        float fq[32];
+        lds_vec(cur.cum + 256 + 32 * hh, fq);  // f_q
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ox[j] = fmaf(cur.cum[256 + 32 * hh + j], ox[j], x[j]);
+        for (int j = 0; j < 32; ++j) ox[j] = fmaf(fq[j], ox[j], x[j]);
       }
       const float gamma = expf(cur.cum[63]);
 #pragma unroll

@@ -64,6 +64,12 @@ __device__ __forceinline__ void load_rows_plain(bf16* tile, const bf16* src, int
 }
 
 __device__ __forceinline__ float bf_lo(uint32_t x) { return __uint_as_float(x << 16); }
+// N consecutive floats of a per-token vector in shared memory (16-byte aligned) by 16-byte loads
+template <int N>
+__device__ __forceinline__ void lds_vec(const float* p, float (&out)[N]) {
+#pragma unroll
+  for (int k = 0; k < N; k += 4) *reinterpret_cast<float4*>(out + k) = *reinterpret_cast<const float4*>(p + k);
+}
 constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
 // 2^x by the hardware approximation (MUFU.EX2; denormal results flush to zero)
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -170,9 +170,10 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
       float x[32], xk[32];  // dV'^T = dO^T A_qk + (dS^T k^T) diag(f_k)
       tc::tmem_ld32(lane_addr + 32 * hh, x);
       tc::tmem_ld32(lane_addr + 64 + 32 * hh, xk);
-      const float* fk = cur.cum + 320;
+      float fk[32];
+      lds_vec(cur.cum + 320 + 32 * hh, fk);  // f_k
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = fmaf(fk[32 * hh + j], xk[j], x[j]);
+      for (int j = 0; j < 32; ++j) x[j] = fmaf(fk[j], xk[j], x[j]);
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) pk[j >> 1] = tc::pack_bf16(x[j], x[j + 1]);
@@ -285,12 +286,6 @@ __device__ __forceinline__ float warp_colsum16(float (&v)[16]) {
 
 __device__ __forceinline__ void tmem_ld16f(uint32_t addr, float (&v)[16]) { tc::tmem_ld16(addr, v); }
 
-// N consecutive floats of a per-token vector in shared memory (16-byte aligned) by 16-byte loads
-template <int N>
-__device__ __forceinline__ void lds_vec(const float* p, float (&out)[N]) {
-#pragma unroll
-  for (int k = 0; k < N; k += 4) *reinterpret_cast<float4*>(out + k) = *reinterpret_cast<const float4*>(p + k);
-}
 
 __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem p, FastWs ws, const bf16* __restrict__ d_o,
                                                                  bf16* __restrict__ dq, bf16* __restrict__ dk,
@@ -548,10 +543,11 @@ __global__ void __launch_bounds__(kBThreads, 1) fast_chunk_bwd_kernel(GdnProblem
       }
     }
     tmem_ld16f(lane_addr + 128, v);  // dBv^T row dv = r, columns m = c0 + j
-    float x[16];
+    float x[16], bt[16];
+    lds_vec(beta + c0, bt);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      x[j] = beta[c0 + j] * v[j];
+      x[j] = bt[j] * v[j];
       v[j] *= tile_elem(sm + lay::VT, 64, c0 + j, r);
     }
     // dv rows are staged over dW^T (dead after G2) and written out after the last proxy fence
