@@ -20,6 +20,8 @@
 //   warps 2-9  epilogue: TMEM -> registers (each warp: its sub-partition's 32 rows x 128 columns),
 //              accumulator released, then * gA gB -> fp32 or bf16 rows while the next tile runs.
 
+#include <atomic>
+
 #include "tmap.cuh"
 
 namespace rb2 {
@@ -689,10 +691,10 @@ int make_map_sf(CUtensorMap* map, const void* base, int64_t rows, int64_t K) {
 // How many two-CTA clusters of the pair kernel can be resident at once on device `dev` (queried
 // once per device; 0 if the query fails, in which case the one-SM kernel is used).
 int pair_clusters(int dev) {
-  static int cache[64];
-  static bool have[64];
+  static std::atomic<int> cache[64];  // value + 1; 0 = not yet queried (concurrent first calls agree)
   if (dev < 0 || dev >= 64) return 0;
-  if (have[dev]) return cache[dev];
+  const int known = cache[dev].load(std::memory_order_relaxed);
+  if (known > 0) return known - 1;
   int n = 0;
   bool failed = true;
   if (cudaFuncSetAttribute(nvfp4_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::SMEM) ==
@@ -714,8 +716,7 @@ int pair_clusters(int dev) {
     n = 0;
     cudaGetLastError();  // the failed query's error is not left for the next launch check
   }
-  cache[dev] = n;
-  have[dev] = true;
+  cache[dev].store(n + 1, std::memory_order_relaxed);
   return n;
 }
 
