@@ -192,9 +192,13 @@ def measure_config3(rank, world, dev, steps, warmup):
         for t in leaves.values():
             t.grad = None
         o, _ = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], cu_seqlens=cu)
+        # the bucket stands for the other layers' LoRA gradients: its all-reduce runs on NCCL's stream
+        # during this backward, as data-parallel training overlaps gradient buckets with the backward,
+        # and the step waits for it before it ends
+        work = dist.all_reduce(bucket, async_op=True) if world > 1 else None
         o.backward(do)
-        if world > 1:
-            dist.all_reduce(bucket)
+        if work is not None:
+            work.wait()
 
     for _ in range(warmup):
         step()
@@ -968,9 +972,12 @@ def main():
             t.grad = None
         o, _ = gdn_b200(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], cu_seqlens=cu,
                         path=args.path)
+        # config 3: the LoRA-gradient bucket's all-reduce overlaps this backward (NCCL's stream); the
+        # step waits for it before it ends
+        work = dist.all_reduce(bucket, async_op=True) if bucket is not None and world > 1 else None
         o.backward(do)
-        if bucket is not None and world > 1:
-            dist.all_reduce(bucket)
+        if work is not None:
+            work.wait()
 
     def barrier():
         if world > 1:
@@ -1036,10 +1043,11 @@ def main():
         dev_in = {n: t.detach().requires_grad_(True) for n, t in ins.items()}
         o, _ = gdn_b200(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], cu_seqlens=cu,
                         path=args.path)
+        work = dist.all_reduce(bucket, async_op=True) if bucket is not None and world > 1 else None
         o.backward(ddo)
         ev_used[k % 2].record(stream)
-        if bucket is not None and world > 1:
-            dist.all_reduce(bucket)
+        if work is not None:
+            work.wait()
         results = [(o_host, o.detach())] + [(outs_host[n], t.grad) for n, t in dev_in.items()]
         s_down.wait_stream(stream)
         with torch.cuda.stream(s_down):
@@ -1110,7 +1118,8 @@ def main():
         "config": (dict(CONFIG1, global_batch=B * world, seq_len=T, parallelism=f"replicas x{world}", path=args.path)
                    if args.config == 1 else
                    {"workload": "config3: packed varlen GDN fwd+bwd, 64 sequences U[128,8192] (243,613 tokens), "
-                                "Hk16 Hv32 d128, LPT token balance + 44 MB fp32 LoRA-bucket NCCL all-reduce per step",
+                                "Hk16 Hv32 d128, LPT token balance + 44 MB fp32 LoRA-bucket NCCL all-reduce per step "
+                                "(overlapped with the backward)",
                     "global_batch": 64, "tokens": total_tokens, "tokens_this_rank": tokens,
                     "parallelism": f"dp{world}", "path": args.path,
                     "l2": "per-rank inputs exceed the 126 MB L2; no flush"}),
