@@ -26,6 +26,7 @@ struct GdnProblem {
 // [seq_chunk0[s], seq_chunk0[s+1]).
 struct ChunkTable {
   int* tok0; int* len; int* seq; int* seq_chunk0; int* n_chunks;
+  int* order;  // [n_seqs] sequences longest first (ties: lower index); the walks take them in this order
 };
 
 // fp32 workspace of the exact path; every per-(chunk, head) array is indexed by ch = ci*Hv + h.
@@ -65,6 +66,7 @@ size_t carve_exact(Carver& c, Ws& w, int64_t tokens, int64_t n_seqs, int Hv, int
   w.ct.len = c.template take<int>(max_chunks);
   w.ct.seq = c.template take<int>(max_chunks);
   w.ct.seq_chunk0 = c.template take<int>(n_seqs + 1);
+  w.ct.order = c.template take<int>(n_seqs);
   w.ct.n_chunks = c.template take<int>(1);
   w.stats = c.template take<float>(nch * 4 * 64);
   w.qn = c.template take<float>(nch * 64 * 128);

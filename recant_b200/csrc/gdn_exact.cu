@@ -146,6 +146,28 @@ __global__ void chunk_table_kernel(const int64_t* __restrict__ cu, int64_t n_seq
     ct.seq_chunk0[n_seqs] = carry;
     *ct.n_chunks = carry;
   }
+  // The walks' order of the sequences: longest first (ties: lower index), so that the CTAs of the
+  // long ones start in the first wave and a short one, not a long one, finishes last (packs of up to
+  // 1024 sequences, ranked from shared memory; larger packs and equal lengths keep the given order).
+  __shared__ int len_s[1024];
+  const bool rank_them = cu != nullptr && n_seqs <= 1024;
+  for (int64_t i = threadIdx.x; i < n_seqs; i += 1024) {
+    if (!rank_them) {
+      ct.order[i] = int(i);
+      continue;
+    }
+    len_s[i] = int(cu[i + 1] - cu[i]);
+  }
+  __syncthreads();
+  if (rank_them && int64_t(threadIdx.x) < n_seqs) {
+    const int i = int(threadIdx.x), li = len_s[i];
+    int rank = 0;
+    for (int j = 0; j < int(n_seqs); ++j) {
+      const int lj = len_s[j];
+      rank += (lj > li || (lj == li && j < i)) ? 1 : 0;
+    }
+    ct.order[rank] = i;
+  }
   // entries past the last chunk read as empty (len 0): a kernel launched over max_chunks can skip
   // its chunk from its own entry, without first reading n_chunks
   for (int idx = carry + int(threadIdx.x); idx < max_chunks; idx += 1024) {

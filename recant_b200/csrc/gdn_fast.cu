@@ -29,6 +29,7 @@ size_t carve_fast_saved(Carver& c, FastWs& w, int64_t n_seqs, int Hv, int max_ch
   w.ct.len = c.take<int>(max_chunks);
   w.ct.seq = c.take<int>(max_chunks);
   w.ct.seq_chunk0 = c.take<int>(n_seqs + 1);
+  w.ct.order = c.take<int>(n_seqs);
   w.ct.n_chunks = c.take<int>(1);
   w.stats = c.take<float>(nch * 512);
   w.tinv = c.take<__nv_bfloat16>(nch * 4096);
@@ -499,7 +500,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_fwd_kernel(GdnProblem p, Fa
   __shared__ uint64_t ldbar[2];   // stage loads
   __shared__ uint32_t tmem_base;
 
-  const int h = blockIdx.x, s = blockIdx.y, hk = h / p.group;
+  const int h = blockIdx.x, s = ws.ct.order[blockIdx.y], hk = h / p.group;  // longest sequences first
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int r = 32 * (w & 3) + l, hh = w >> 2;
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(256, 1) fast_state_bwd_kernel(GdnProblem p, Fa
   __shared__ uint64_t ldbar[2];   // stage loads (bulk part)
   __shared__ uint32_t tmem_base;
 
-  const int h = blockIdx.x, s = blockIdx.y;
+  const int h = blockIdx.x, s = ws.ct.order[blockIdx.y];  // longest sequences first
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int r = 32 * (w & 3) + l, hh = w >> 2;
   if (w == 0) tc::tmem_alloc(&tmem_base, 512);
