@@ -224,6 +224,26 @@ RB2_API int rb2_gated_rmsnorm_nvfp4_fwd(const void* x, const void* z, const floa
 RB2_API int rb2_skinny_gemm(const void* A, int64_t lda, const void* B, int64_t M, int64_t N, int64_t K, void* out,
                             int64_t ldo, int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * LoRA weight gradient: out(n, r) = bf16(bf16(sum_m D[m, n] H[m, r]) * scale) as fp32, for
+ * n < N, r < R, the sum over the M tokens. Replaces the cuBLAS products that torch's autograd runs
+ * for the gradients of the block's fp32 LoRA factors (recant/model/layers.py:65-70, 86-97): for
+ * dB = s dy^T h (the mat2 gradient of grouped_linear's addmm(y, h, B^T, alpha=s), or of QLinear's
+ * (h B^T) * s) pass D = dy [M, out], H = h [M, r], scale = s; for dA = (x^T dh)^T (the gradient of
+ * x A^T) pass D = x [M, in], H = dh [M, r], scale = 1. The roundings are the reference's: the bf16
+ * product, the bf16 multiply by alpha, and the cast back to the fp32 parameter; only the order of
+ * the fp32 sum over tokens differs. D, H bf16 with row strides ldd, ldh (multiples of 8 elements,
+ * 16-byte aligned bases; H's columns past R are not read); 1 <= R <= 64. out fp32 at
+ * out[n * ld_n + r * ld_r], either [N, R] (ld_r = 1) or [R, N] (ld_n = 1). M = 0 writes zeros (D and H
+ * may then be NULL).
+ * ws: rb2_lora_wgrad_workspace_size(M, N, R) bytes, 256-byte aligned; its first 4 bytes are the
+ * op's status word (cleared by the call). Deterministic: the token splits are summed in a fixed
+ * order. */
+RB2_API size_t rb2_lora_wgrad_workspace_size(int64_t M, int64_t N, int R);
+RB2_API int rb2_lora_wgrad(const void* D, int64_t ldd, const void* H, int64_t ldh, int64_t M, int64_t N, int R,
+                           float scale, float* out, int64_t ld_n, int64_t ld_r, void* ws, size_t ws_bytes,
+                           void* stream);
+
 /* Scale bytes [rows, cols] (e4m3) -> the 128x4 blocked swizzle of nvfp4._to_blocked
  * (recant/model/nvfp4.py:112-119), ceil(rows/128)*ceil(cols/4)*512 bytes, pad bytes zero. Lets
  * FP4 tensors quantized elsewhere (e.g. by the reference's quantize_weight) feed the GEMM. */

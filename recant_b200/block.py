@@ -65,6 +65,40 @@ def narrow_product(x2, w):
     return out[:, :n]
 
 
+def _wgrad_ok(d2, h):
+    """Both operands as rb2_lora_wgrad reads them: CUDA bf16 rows (unit column stride, row strides
+    multiples of 8 elements, 16-byte aligned) and a rank of at most 64."""
+    return (d2.is_cuda and d2.dtype == torch.bfloat16 and h.dtype == torch.bfloat16 and d2.dim() == 2 and h.dim() == 2
+            and d2.shape[0] == h.shape[0] and 1 <= h.shape[1] <= 64 and d2.shape[1] >= 1
+            and d2.stride(1) == 1 and h.stride(1) == 1 and d2.stride(0) % 8 == 0 and h.stride(0) % 8 == 0
+            and d2.stride(0) >= d2.shape[1] and h.stride(0) >= h.shape[1]
+            and d2.data_ptr() % 16 == 0 and h.data_ptr() % 16 == 0)
+
+
+def lora_wgrad(d2, h, scale=1.0, transposed=False):
+    """fp32 LoRA factor gradient from the library's tcgen05 kernel: out[n, r] = bf16(bf16(d2^T h) * scale)
+    over the M rows of d2 [M, N] and h [M, R] (bf16), as [N, R], or [R, N] with ``transposed`` --
+    the gradients torch's autograd gives the fp32 factors through their bf16 casts (dB = s dy^T h for
+    h B^T; dA = (x^T dh)^T for x A^T; layers.py:65-70, 86-97)."""
+    if not _wgrad_ok(d2, h):
+        raise ValueError("recant_b200.lora_wgrad: needs CUDA bf16 [M, N] and [M, R <= 64] rows with unit column "
+                         "stride, row strides a multiple of 8 elements and 16-byte aligned bases")
+    M, n = d2.shape
+    R = h.shape[1]
+    out = torch.empty((R, n) if transposed else (n, R), dtype=torch.float32, device=d2.device)
+    ws = torch.empty(L.lib().rb2_lora_wgrad_workspace_size(M, n, R), dtype=torch.uint8, device=d2.device)
+    ld_n, ld_r = (1, n) if transposed else (R, 1)
+    L.check(L.lib().rb2_lora_wgrad(_p(d2), d2.stride(0), _p(h), h.stride(0), M, n, R, float(scale), _p(out), ld_n,
+                                   ld_r, _p(ws), ws.numel(), _stream(d2.device)), "lora_wgrad")
+    L.check_status(ws, "lora_wgrad")
+    return out
+
+
+# The LoRA factor gradients (dA, dB) run on rb2_lora_wgrad; off, torch's autograd computes them with
+# cuBLAS as the reference does.
+LORA_WGRAD = True
+
+
 def _narrow_ok(x, n):
     x2_rows = x.numel() // x.shape[-1]
     return (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 64 == 0 and 0 < n <= 256
@@ -97,8 +131,16 @@ class _XProjections(torch.autograd.Function):
         d2 = dout.reshape(-1, dout.shape[-1]).to(torch.bfloat16)
         dx = (d2 @ W).reshape(ctx.xshape) if ctx.needs_input_grad[0] else None
         grads, off = [], ctx.n_frozen
+        need = [ctx.needs_input_grad[2 + i] for i in range(len(ctx.ranks))]
+        dh_all = d2[:, off:off + sum(ctx.ranks)]
+        if LORA_WGRAD and any(need) and _wgrad_ok(x2, dh_all):
+            dA = lora_wgrad(x2, dh_all, 1.0, transposed=True)  # every member's dA in one pass over x
+            for i, r in enumerate(ctx.ranks):
+                grads.append(dA[off - ctx.n_frozen:off - ctx.n_frozen + r] if need[i] else None)
+                off += r
+            return (dx, None, *grads)
         for i, r in enumerate(ctx.ranks):
-            grads.append((d2[:, off:off + r].t() @ x2).float() if ctx.needs_input_grad[2 + i] else None)
+            grads.append((d2[:, off:off + r].t() @ x2).float() if need[i] else None)
             off += r
         return (dx, None, *grads)
 
@@ -343,6 +385,68 @@ class _FP4LoRAGroup(torch.autograd.Function):
         return (None if dx is None else dx.reshape(ctx.xshape), None, None, None, None, *grads)
 
 
+class _LoRAAddmm(torch.autograd.Function):
+    """grouped_linear's LoRA up-projection, one addmm per member as the reference's (layers.py:86-97):
+    y2 + s h2 B^T with B the fp32 factor cast to bf16. Forward as torch.addmm; backward as its
+    autograd (dy to y2, dh = (dy B) s in bf16) with dB from rb2_lora_wgrad."""
+
+    @staticmethod
+    def forward(ctx, y2, h2, B, s):
+        b = B.to(y2.dtype)
+        ctx.save_for_backward(h2, b)
+        ctx.s = s
+        return torch.addmm(y2, h2, b.t(), alpha=s)
+
+    @staticmethod
+    def backward(ctx, dout):
+        h2, b = ctx.saved_tensors
+        s = ctx.s
+        dh = _alpha(dout @ b, s) if ctx.needs_input_grad[1] else None
+        dB = None
+        if ctx.needs_input_grad[2]:
+            dB = lora_wgrad(dout, h2, s) if _wgrad_ok(dout, h2) else _alpha(h2.t() @ dout, s).t().float()
+        return (dout if ctx.needs_input_grad[0] else None), dh, dB, None
+
+
+class _LoRAQLinear(torch.autograd.Function):
+    """QLinear.forward's LoRA term as the reference's three bf16 ops (layers.py:65-70): h = x2 A^T,
+    y2 + (h B^T) s, with A, B the fp32 factors cast to bf16. Forward bit-identical to those ops;
+    backward as their autograd, with dA and dB from rb2_lora_wgrad."""
+
+    @staticmethod
+    def forward(ctx, x2, y2, A, B, s):
+        a, b = A.to(x2.dtype), B.to(x2.dtype)
+        h = x2 @ a.t()
+        ctx.save_for_backward(x2, h, a, b)
+        ctx.s = s
+        return y2 + (h @ b.t()) * s
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, h, a, b = ctx.saved_tensors
+        dt = dout * ctx.s                      # the gradient of (h B^T) in bf16
+        dB = None
+        if ctx.needs_input_grad[3]:
+            dB = lora_wgrad(dt, h, 1.0) if _wgrad_ok(dt, h) else (h.t() @ dt).t().float()
+        dx = dA = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[2]:
+            dh = dt @ b
+            if ctx.needs_input_grad[2]:
+                dA = lora_wgrad(x2, dh, 1.0, transposed=True) if _wgrad_ok(x2, dh) else (x2.t() @ dh).t().float()
+            if ctx.needs_input_grad[0]:
+                dx = dh @ a
+        return dx, (dout if ctx.needs_input_grad[1] else None), dA, dB, None
+
+
+def _alpha(t, s):
+    """torch's maybe_multiply: the product times alpha unless alpha is 1."""
+    return t if s == 1 else t * s
+
+
+def _lora_kernels_ok(x):
+    return LORA_WGRAD and x.is_cuda and x.dtype == torch.bfloat16
+
+
 # Add LoRA inside the NVFP4 GEMM epilogue (_FP4LoRAGroup) instead of the reference's addmm through
 # cuBLAS. Off by default: measured at config 2 it is slower (5.75 vs 5.40 ms per block step; the 16
 # FMAs per output element on CUDA cores are not hidden behind the next tile), as is the decode step.
@@ -389,6 +493,10 @@ class QLinear(nn.Module):
         addmm as grouped_linear's default path (layers.py:86-97)."""
         if self.lora_A is None:
             return y
+        if not grouped and _lora_kernels_ok(x) and y.shape == x.shape[:-1] + (self.out_features,):
+            x2 = x.reshape(-1, self.in_features)
+            o = _LoRAQLinear.apply(x2, y.reshape(-1, self.out_features), self.lora_A, self.lora_B, self.lora_scale)
+            return o.reshape(*y.shape)
         h = x @ self.lora_A.to(x.dtype).t()
         if grouped:
             o = torch.addmm(y.reshape(-1, y.shape[-1]), h.reshape(-1, h.shape[-1]), self.lora_B.to(x.dtype).t(),
@@ -439,7 +547,10 @@ def grouped_linear(x, lins, h=None):
         r = l.lora_A.shape[0]
         hi = h[..., off:off + r].reshape(-1, r)
         off += r
-        o = torch.addmm(y.reshape(-1, l.out_features), hi, l.lora_B.to(x.dtype).t(), alpha=l.lora_scale)
+        if _lora_kernels_ok(x):
+            o = _LoRAAddmm.apply(y.reshape(-1, l.out_features), hi, l.lora_B, l.lora_scale)
+        else:
+            o = torch.addmm(y.reshape(-1, l.out_features), hi, l.lora_B.to(x.dtype).t(), alpha=l.lora_scale)
         res.append(o.reshape(*y.shape))
     return res
 
