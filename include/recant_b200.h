@@ -225,6 +225,19 @@ RB2_API int rb2_skinny_gemm(const void* A, int64_t lda, const void* B, int64_t M
                             int64_t ldo, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * LoRA up-projection added to a base output: out[m, n] = y[m, n] + s * sum_k h[m, k] B[n, k] over
+ * k < r (1 <= r <= 64), fp32 accumulation, rounded as the reference's ops round it on the GPU --
+ * mode 0: grouped_linear's torch.addmm(y, h, B^T, alpha=s) (recant/model/layers.py:86-97), which
+ * cuBLAS computes as bf16(y + bf16(s * acc)); mode 1: QLinear.forward's y + (h B^T) * s
+ * (layers.py:65-70), the product, its scaling and the sum each rounded to bf16. y, h, B, out bf16 with row strides ldy, ldh, ldb, ldo (multiples
+ * of 8 elements, 16-byte aligned bases; h's and B's columns past r are not read); out may be y. ws:
+ * rb2_lora_up_workspace_size() bytes (the op's status word, cleared by the call). */
+RB2_API size_t rb2_lora_up_workspace_size(void);
+RB2_API int rb2_lora_up(const void* y, int64_t ldy, const void* h, int64_t ldh, const void* B, int64_t ldb, int64_t M,
+                        int64_t N, int r, float scale, int mode, void* out, int64_t ldo, void* ws, size_t ws_bytes,
+                        void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * LoRA weight gradient: out(n, r) = bf16(bf16(sum_m D[m, n] H[m, r]) * scale) as fp32, for
  * n < N, r < R, the sum over the M tokens. Replaces the cuBLAS products that torch's autograd runs
  * for the gradients of the block's fp32 LoRA factors (recant/model/layers.py:65-70, 86-97): for

@@ -56,6 +56,8 @@ SIGNATURES = {
     "rb2_nvfp4_gemv": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "rb2_nvfp4_gemm_b_images": (_i, [_p, _i64, _i64, _p, _sz, _p]),
     "rb2_skinny_gemm": (_i, [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _i, _p]),
+    "rb2_lora_up_workspace_size": (_sz, []),
+    "rb2_lora_up": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i, _f, _i, _p, _i64, _p, _sz, _p]),
     "rb2_lora_wgrad_workspace_size": (_sz, [_i64, _i64, _i]),
     "rb2_lora_wgrad": (_i, [_p, _i64, _p, _i64, _i64, _i64, _i, _f, _p, _i64, _i64, _p, _sz, _p]),
     "rb2_gated_rmsnorm_nvfp4_fwd": (_i, [_p, _p, _p, _i64, _i, _f, _p, _p, _i64, _i64, _i, _p, _p, _p, _p, _p, _sz,

@@ -94,6 +94,42 @@ def lora_wgrad(d2, h, scale=1.0, transposed=False):
     return out
 
 
+def _up_ok(y2, h, b):
+    """Operands as rb2_lora_up reads them: CUDA bf16 rows with unit column stride, row strides
+    multiples of 8 elements, 16-byte aligned bases, rank at most 64."""
+    ts = (y2, h, b)
+    return (all(t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0
+                and t.stride(0) >= t.shape[1] and t.data_ptr() % 16 == 0 for t in ts)
+            and h.shape[0] == y2.shape[0] and b.shape[0] == y2.shape[1] and h.shape[1] == b.shape[1]
+            and 1 <= h.shape[1] <= 64)
+
+
+def lora_up(y2, h, b, scale, mode):
+    """y2 + scale (h b^T) on the library's tcgen05 kernel, rounded as the reference's ops round it on
+    the GPU: ``mode`` 0 as torch.addmm(y2, h, b^T, alpha=scale) (layers.py:86-97; cuBLAS rounds the
+    scaled product to bf16, then adds), 1 as QLinear's three bf16 ops (layers.py:65-70);
+    y2 [M, N], h [M, r], b [N, r] bf16, r <= 64. Returns a new [M, N] bf16 tensor."""
+    if not _up_ok(y2, h, b):
+        raise ValueError("recant_b200.lora_up: needs CUDA bf16 [M, N], [M, r], [N, r] rows (r <= 64) with unit "
+                         "column stride, row strides a multiple of 8 elements and 16-byte aligned bases")
+    M, n = y2.shape
+    out = torch.empty(M, n, dtype=torch.bfloat16, device=y2.device)
+    ws = torch.empty(L.lib().rb2_lora_up_workspace_size(), dtype=torch.uint8, device=y2.device)
+    L.check(L.lib().rb2_lora_up(_p(y2), y2.stride(0), _p(h), h.stride(0), _p(b), b.stride(0), M, n, h.shape[1],
+                                float(scale), int(mode), _p(out), n, _p(ws), ws.numel(), _stream(y2.device)),
+            "lora_up")
+    L.check_status(ws, "lora_up")
+    return out
+
+
+def _pow2(s):
+    """Whether scaling by s is exact in binary floating point (s a power of two)."""
+    return s > 0 and math.frexp(s)[0] == 0.5
+
+
+# The LoRA up-projection (y + s h B^T) runs on rb2_lora_up; off, as the reference's torch ops.
+LORA_UP = True
+
 # The LoRA factor gradients (dA, dB) run on rb2_lora_wgrad; off, torch's autograd computes them with
 # cuBLAS as the reference does.
 LORA_WGRAD = True
@@ -387,14 +423,16 @@ class _FP4LoRAGroup(torch.autograd.Function):
 
 class _LoRAAddmm(torch.autograd.Function):
     """grouped_linear's LoRA up-projection, one addmm per member as the reference's (layers.py:86-97):
-    y2 + s h2 B^T with B the fp32 factor cast to bf16. Forward as torch.addmm; backward as its
-    autograd (dy to y2, dh = (dy B) s in bf16) with dB from rb2_lora_wgrad."""
+    y2 + s h2 B^T with B the fp32 factor cast to bf16, on rb2_lora_up (mode 0: addmm's rounding);
+    backward as addmm's autograd (dy to y2, dh = (dy B) s in bf16) with dB from rb2_lora_wgrad."""
 
     @staticmethod
     def forward(ctx, y2, h2, B, s):
         b = B.to(y2.dtype)
         ctx.save_for_backward(h2, b)
         ctx.s = s
+        if LORA_UP and _up_ok(y2, h2, b):
+            return lora_up(y2, h2, b, s, 0)
         return torch.addmm(y2, h2, b.t(), alpha=s)
 
     @staticmethod
@@ -404,14 +442,15 @@ class _LoRAAddmm(torch.autograd.Function):
         dh = _alpha(dout @ b, s) if ctx.needs_input_grad[1] else None
         dB = None
         if ctx.needs_input_grad[2]:
-            dB = lora_wgrad(dout, h2, s) if _wgrad_ok(dout, h2) else _alpha(h2.t() @ dout, s).t().float()
+            dB = lora_wgrad(dout, h2, s) if LORA_WGRAD and _wgrad_ok(dout, h2) else _alpha(h2.t() @ dout, s).t().float()
         return (dout if ctx.needs_input_grad[0] else None), dh, dB, None
 
 
 class _LoRAQLinear(torch.autograd.Function):
     """QLinear.forward's LoRA term as the reference's three bf16 ops (layers.py:65-70): h = x2 A^T,
-    y2 + (h B^T) s, with A, B the fp32 factors cast to bf16. Forward bit-identical to those ops;
-    backward as their autograd, with dA and dB from rb2_lora_wgrad."""
+    y2 + (h B^T) s, with A, B the fp32 factors cast to bf16; the up-projection and the add in one
+    pass on rb2_lora_up (mode 1: the three ops' roundings). Backward as their autograd, with dA and
+    dB from rb2_lora_wgrad."""
 
     @staticmethod
     def forward(ctx, x2, y2, A, B, s):
@@ -419,20 +458,31 @@ class _LoRAQLinear(torch.autograd.Function):
         h = x2 @ a.t()
         ctx.save_for_backward(x2, h, a, b)
         ctx.s = s
+        if LORA_UP and _up_ok(y2, h, b):
+            return lora_up(y2, h, b, s, 1)
         return y2 + (h @ b.t()) * s
 
     @staticmethod
     def backward(ctx, dout):
         x2, h, a, b = ctx.saved_tensors
-        dt = dout * ctx.s                      # the gradient of (h B^T) in bf16
+        s = ctx.s
+        # the gradient of (h B^T) is dt = dout * s in bf16; when s is a power of two that scaling is
+        # exact and commutes with every rounding below, so it is applied to the products instead of
+        # materialising dt (the same values, one pass over [M, N] fewer)
+        fold = LORA_WGRAD and _pow2(s) and _wgrad_ok(dout, h)
+        dt = None if fold else dout * s
         dB = None
         if ctx.needs_input_grad[3]:
-            dB = lora_wgrad(dt, h, 1.0) if _wgrad_ok(dt, h) else (h.t() @ dt).t().float()
+            if fold:
+                dB = lora_wgrad(dout, h, s)
+            else:
+                dB = lora_wgrad(dt, h, 1.0) if LORA_WGRAD and _wgrad_ok(dt, h) else (h.t() @ dt).t().float()
         dx = dA = None
         if ctx.needs_input_grad[0] or ctx.needs_input_grad[2]:
-            dh = dt @ b
+            dh = (dout @ b) * s if fold else dt @ b
             if ctx.needs_input_grad[2]:
-                dA = lora_wgrad(x2, dh, 1.0, transposed=True) if _wgrad_ok(x2, dh) else (x2.t() @ dh).t().float()
+                dA = (lora_wgrad(x2, dh, 1.0, transposed=True) if LORA_WGRAD and _wgrad_ok(x2, dh)
+                      else (x2.t() @ dh).t().float())
             if ctx.needs_input_grad[0]:
                 dx = dh @ a
         return dx, (dout if ctx.needs_input_grad[1] else None), dA, dB, None
@@ -444,7 +494,7 @@ def _alpha(t, s):
 
 
 def _lora_kernels_ok(x):
-    return LORA_WGRAD and x.is_cuda and x.dtype == torch.bfloat16
+    return (LORA_WGRAD or LORA_UP) and x.is_cuda and x.dtype == torch.bfloat16
 
 
 # Add LoRA inside the NVFP4 GEMM epilogue (_FP4LoRAGroup) instead of the reference's addmm through

@@ -262,9 +262,6 @@ extern "C" int rb2_lora_wgrad(const void* D, int64_t ldd, const void* H, int64_t
     RB2_CHECK_LAUNCH("lora_wgrad zero");
     return RB2_OK;
   }
-  CUtensorMap md, mh;
-  int rc;
-  if ((rc = make_map(&md, D, M, N, ldd)) || (rc = make_map(&mh, H, M, R, ldh))) return rc;
   int n_tiles, n_splits, tok;
   plan(M, N, &n_tiles, &n_splits, &tok);
   // workspace: status word | the column tiles' arrival counters | per-split partials
@@ -272,8 +269,13 @@ extern "C" int rb2_lora_wgrad(const void* D, int64_t ldd, const void* H, int64_t
   int* arrivals = n_splits > 1 ? reinterpret_cast<int*>(static_cast<char*>(ws) + kStatusBytes) : nullptr;
   float* partial =
       n_splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(ws) + kStatusBytes + counters) : nullptr;
-  // one memset clears the status word and the counters
+  // one memset clears the status word and the counters; as the call's first CUDA call it also makes
+  // the device's context current on a thread that has not used it yet (an autograd worker), which
+  // the tensor-map encoding below needs
   RB2_CUDA(cudaMemsetAsync(ws, 0, n_splits > 1 ? kStatusBytes + counters : sizeof(int), s), "lora_wgrad: clear");
+  CUtensorMap md, mh;
+  int rc;
+  if ((rc = make_map(&md, D, M, N, ldd)) || (rc = make_map(&mh, H, M, R, ldh))) return rc;
   cudaError_t e = cudaFuncSetAttribute(lora_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) {
     set_error("lora_wgrad: cudaFuncSetAttribute: %s", cudaGetErrorString(e));

@@ -149,18 +149,20 @@ extern "C" int rb2_skinny_gemm(const void* a, int64_t lda, const void* b, int64_
                     (reinterpret_cast<uintptr_t>(out) & 15) == 0,
                 "skinny_gemm: A, B and out must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap ma, mb;
-  int rc;
-  if ((rc = make_map_bf16(&ma, a, M, K, lda, kRows)) || (rc = make_map_bf16(&mb, b, N, K, K, int(N)))) return rc;
   const int b_pad = (int(N) * 128 + 1023) & ~1023;
   const int smem = kStages * (kRows * 128 + b_pad) + 1024;
   int tmem_cols = 32;
   while (tmem_cols < N) tmem_cols <<= 1;
+  // the first CUDA call also makes the device's context current on a thread that has not used it yet,
+  // which the tensor-map encoding below needs
   cudaError_t e = cudaFuncSetAttribute(skinny_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_error("skinny_gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     return RB2_ECUDA;
   }
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_map_bf16(&ma, a, M, K, lda, kRows)) || (rc = make_map_bf16(&mb, b, N, K, K, int(N)))) return rc;
   {
     ProfScope ps_("skinny_gemm", s);
     skinny_gemm_kernel<<<unsigned((M + kRows - 1) / kRows), 128, smem, s>>>(ma, mb, int(M), int(N), int(K), tmem_cols,

@@ -70,10 +70,11 @@ def test_lora_wgrad_rejects_bad_operands():
 
 
 def test_block_lora_gradients_kernel_vs_cublas(monkeypatch):
-    """The GDN block's LoRA gradients (in_proj_qkv, in_proj_z through the grouped addmm and the
-    shared down-projection; out_proj through QLinear's three ops) with rb2_lora_wgrad against the
-    same backward with torch's cuBLAS products, on the golden block's input and one upstream
-    gradient (round-to-nearest backward quantization, so both runs see the same codes)."""
+    """The GDN block's output and LoRA gradients (in_proj_qkv, in_proj_z through the grouped addmm
+    and the shared down-projection; out_proj through QLinear's three ops) with rb2_lora_up and
+    rb2_lora_wgrad against the same forward and backward as the reference's torch ops (cuBLAS), on
+    the golden block's input and one upstream gradient (round-to-nearest backward quantization, so
+    both runs see the same codes)."""
     import recant_b200.block as blk
     from block_util import HIDDEN, HK, HV, golden
 
@@ -86,13 +87,15 @@ def test_block_lora_gradients_kernel_vs_cublas(monkeypatch):
 
     def grads(on):
         monkeypatch.setattr(blk, "LORA_WGRAD", on)
+        monkeypatch.setattr(blk, "LORA_UP", on)
         for name in ("in_proj_qkv", "in_proj_z", "out_proj"):
             lin = getattr(block, name)
             lin.lora_A.grad = lin.lora_B.grad = None
         xd = x.clone().requires_grad_(True)
-        block(xd).backward(dy)
+        y = block(xd)
+        y.backward(dy)
         torch.cuda.synchronize()
-        out = {"dx": xd.grad.float().cpu()}
+        out = {"dx": xd.grad.float().cpu(), "y": y.detach().float().cpu()}
         for name in ("in_proj_qkv", "in_proj_z", "out_proj"):
             lin = getattr(block, name)
             out[name + ".A"] = lin.lora_A.grad.cpu().clone()
@@ -100,8 +103,46 @@ def test_block_lora_gradients_kernel_vs_cublas(monkeypatch):
         return out
 
     on, off = grads(True), grads(False)
+    assert rel(on["y"], off["y"]) < 1e-2, rel(on["y"], off["y"])
     assert rel(on["dx"], off["dx"]) < 1e-2
     for k in off:
-        if k != "dx":
+        if k not in ("dx", "y"):
             assert off[k].abs().sum() > 0, k
             assert rel(on[k], off[k]) < 1e-3, (k, rel(on[k], off[k]))
+
+
+def _up_reference(y, h, b, s, mode):
+    acc = (h.double() @ b.double().t()).float()
+    if mode == 0:  # torch.addmm on the GPU: the scaled product rounded to bf16, then added
+        return (y.float() + (acc * s).to(torch.bfloat16).float()).to(torch.bfloat16)
+    t = acc.to(torch.bfloat16)
+    return (y.float() + (t.float() * s).to(torch.bfloat16).float()).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,r,mode", [(16384, 4096, 16, 1), (16384, 8192, 16, 0), (1000, 200, 32, 1),
+                                        (77, 136, 8, 0), (129, 4096, 64, 1), (300, 256, 48, 0)])
+def test_lora_up_matches_reference_ops(M, N, r, mode):
+    """rb2_lora_up against the reference's ops on the same bf16 operands: mode 1 (QLinear's three
+    ops) and mode 0 (grouped_linear's addmm, which cuBLAS computes as bf16(y + bf16(s acc))) equal a
+    float64-accumulated restatement of those roundings within 1e-3 (relative Frobenius), and torch's
+    own ops on this GPU element for element (all but 1e-4 of the elements, for fp32 sums that round
+    differently)."""
+    from recant_b200.block import lora_up
+    gen = torch.Generator().manual_seed(M + N + r + mode)
+    y = torch.randn(M, N, generator=gen).to(torch.bfloat16).cuda()
+    h = torch.randn(M, r, generator=gen).to(torch.bfloat16).cuda()
+    b = (torch.randn(N, r, generator=gen) * 0.1).to(torch.bfloat16).cuda()
+    out = lora_up(y, h, b, 2.0, mode)
+    torch.cuda.synchronize()
+    ref = _up_reference(y.cpu(), h.cpu(), b.cpu(), 2.0, mode)
+    assert rel(out.float().cpu(), ref.float()) < 1e-3
+    torch_ops = torch.addmm(y, h, b.t(), alpha=2.0) if mode == 0 else y + (h @ b.t()) * 2.0
+    assert rel(out.float(), torch_ops.float()) < 1e-3
+    assert (out == torch_ops).float().mean().item() > 0.9999
+    # a strided y (a column slice) and an output row stride equal to N
+    if N >= 136:
+        wide = torch.randn(M, N + 8, generator=gen).to(torch.bfloat16).cuda()
+        y2 = wide[:, 8:]
+        out2 = lora_up(y2, h, b, 2.0, mode)
+        torch.cuda.synchronize()
+        assert rel(out2.float().cpu(), _up_reference(y2.cpu(), h.cpu(), b.cpu(), 2.0, mode).float()) < 1e-3
