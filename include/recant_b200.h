@@ -284,8 +284,8 @@ RB2_API int rb2_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales_block
  * - lora_h (NULL = none): out = a . b^T * gA * gB + lora_scale * lora_h . lora_b^T with lora_h
  *   [M, lora_r] bf16 (row stride lora_ldh elements) and lora_b [N, lora_r] bf16, lora_r 8 or 16:
  *   QLinear's LoRA y + (alpha / r) (x A^T) B^T (layers.py:65-70, 86-97) with h = x A^T computed by
- *   the caller. fp32 output: one fp32 sum. bf16 output, rounded as the reference's ops round:
- *   lora_mode 0 = grouped_linear's addmm (y to bf16, then y + s h B^T in fp32, one rounding);
+ *   the caller. fp32 output: one fp32 sum. bf16 output, rounded as the reference's ops round on
+ *   the GPU: lora_mode 0 = grouped_linear's addmm (y to bf16, s h B^T to bf16, their sum rounded);
  *   lora_mode 1 = QLinear.forward's three ops (y, h B^T and s h B^T each to bf16, then the sum). */
 RB2_API int rb2_nvfp4_gemm_ex(const uint8_t* a_codes, const uint8_t* a_scales_blocked, const float* a_gscale,
                               const uint8_t* b_codes, const uint8_t* b_scales_blocked, const float* b_gscale,

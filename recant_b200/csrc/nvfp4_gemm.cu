@@ -111,8 +111,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // Optional low-rank term added in the epilogue: out = y + s * h B^T with h [M, r] (row stride ldh)
 // and B [N, r] bf16, r 8 or 16 -- QLinear's LoRA (layers.py:65-70, 86-97) with h = x A^T computed
 // by the caller, rounded as the reference rounds it when the output is bf16:
-//   mode 0 (grouped_linear's addmm, layers.py:86-97): y rounded to bf16, then y + s (h B^T) in fp32,
-//          one rounding;
+//   mode 0 (grouped_linear's addmm, layers.py:86-97): y rounded to bf16, plus s (h B^T) rounded to
+//          bf16, the sum rounded (torch.addmm on the GPU: cuBLAS rounds the scaled product first);
 //   mode 1 (QLinear.forward, layers.py:65-70): y, h B^T and (h B^T) s each rounded to bf16, then
 //          their sum rounded.
 struct Lora {
@@ -306,7 +306,7 @@ nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
 #pragma unroll
             for (int i = 0; i < 8; ++i) d = fmaf(hf[8 + i], bf[i], d);
             if (!out_bf16) v = fmaf(lora.s, d, v);
-            else if (lora.mode == 0) v = fmaf(lora.s, d, bf16r(v));
+            else if (lora.mode == 0) v = bf16r(v) + bf16r(lora.s * d);  // addmm as cuBLAS rounds it
             else v = bf16r(v) + bf16r(bf16r(d) * lora.s);
           }
           r[c][jj] = __float_as_uint(v);

@@ -170,6 +170,10 @@ def test_gemm_lora_epilogue(M, N, K, r):
     assert _rel(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
     out16 = gemm_b200(a, b, out_dtype=torch.bfloat16, lora=(h, Bm, 2.0))
     assert _rel(out16.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
+    # bf16 output against grouped_linear's own op on this GPU, torch.addmm over the bf16 base output
+    # (the low-rank sum runs on CUDA cores here, in another order: a few elements may round apart)
+    addmm = torch.addmm(base.to(torch.bfloat16), h, Bm.t(), alpha=2.0)
+    assert (out16 == addmm).float().mean().item() > 0.995
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (2, 300, 512), (3, 12288, 1024), (4, 7, 32), (1, 129, 4128)])
