@@ -488,6 +488,50 @@ class _LoRAQLinear(torch.autograd.Function):
         return dx, (dout if ctx.needs_input_grad[1] else None), dA, dB, None
 
 
+class _FP4QLinear(torch.autograd.Function):
+    """QLinear.forward with an NVFP4 base and LoRA (layers.py:62-70) as one function: y = Q(x) W^T
+    (the activation quantized once, or given as ``a_pre``), then y + (h B^T) s on rb2_lora_up with
+    h = x A^T, rounded as the reference's three ops. Backward: the NVFP4 dgrad as FP4Linear's
+    (nvfp4.py:151-170) and the LoRA gradients as _LoRAQLinear's; x's two gradient contributions are
+    summed inside rb2_lora_up (dx = bf16(dx_base + bf16(dh A)), the sum autograd would form from
+    the two ops) instead of materialising dh A and adding it in another pass."""
+
+    @staticmethod
+    def forward(ctx, x2, stochastic, a_pre, w, A, B, s):
+        a, b = A.to(x2.dtype), B.to(x2.dtype)
+        q = N.quantize_activation(x2, w.use_rht) if a_pre is None else a_pre
+        y = N._gemm_to(q, w.fprop, x2.dtype).to(x2.dtype)
+        h = x2 @ a.t()
+        ctx.save_for_backward(x2, h, a, b)
+        ctx.s, ctx.w, ctx.stochastic = s, w, stochastic
+        return lora_up(y, h, b, s, 1) if _up_ok(y, h, b) else y + (h @ b.t()) * s
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, h, a, b = ctx.saved_tensors
+        s, w = ctx.s, ctx.w
+        fold = LORA_WGRAD and _pow2(s) and _wgrad_ok(dout, h)
+        dt = None if fold else dout * s
+        dB = None
+        if ctx.needs_input_grad[5]:
+            if fold:
+                dB = lora_wgrad(dout, h, s)
+            else:
+                dB = lora_wgrad(dt, h, 1.0) if LORA_WGRAD and _wgrad_ok(dt, h) else (h.t() @ dt).t().float()
+        dx = dA = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[4]:
+            dh = (dout @ b) * s if fold else dt @ b
+            if ctx.needs_input_grad[4]:
+                dA = (lora_wgrad(x2, dh, 1.0, transposed=True) if LORA_WGRAD and _wgrad_ok(x2, dh)
+                      else (x2.t() @ dh).t().float())
+            if ctx.needs_input_grad[0]:
+                d = N.quantize_activation(dout, w.use_rht, stochastic=ctx.stochastic)
+                dx_base = N._gemm_to(d, w.dgrad, dout.dtype).to(dout.dtype)
+                at = a.t().contiguous()  # [in, r]: A's rows as the up-projection's B operand
+                dx = lora_up(dx_base, dh, at, 1.0, 1) if _up_ok(dx_base, dh, at) else dx_base + dh @ a
+        return dx, None, None, None, dA, dB, None
+
+
 def _alpha(t, s):
     """torch's maybe_multiply: the product times alpha unless alpha is 1."""
     return t if s == 1 else t * s
@@ -557,6 +601,12 @@ class QLinear(nn.Module):
     def forward(self, x, a_pre=None):
         """``a_pre``: x already quantized (the FP4Tensor of x, RN, with this weight's RHT setting),
         as the fused gated norm produces it; used by the NVFP4 base only."""
+        if (self.fp4 is not None and self.lora_A is not None and LORA_UP and not _fused_lora_ok([self])
+                and x.is_cuda and x.dtype == torch.bfloat16 and self.lora_A.shape[0] <= 64):
+            x2 = x.reshape(-1, self.in_features)
+            y = _FP4QLinear.apply(x2, self.stochastic_backward, a_pre, self.fp4, self.lora_A, self.lora_B,
+                                  self.lora_scale)
+            return y.reshape(*x.shape[:-1], self.out_features)
         if _fused_lora_ok([self]):
             (y,) = _FP4LoRAGroup.apply(x, self.stochastic_backward, 1, (self.fp4,), (self.lora_scale,),
                                        self.lora_A, self.lora_B)
