@@ -554,17 +554,19 @@ C4 = dict(T=131072, layers=8, Hk=16, Hv=32, d=128, hidden=4096, segments_per_ran
 FP4_PER_BF16 = 4.0
 
 
-def host_link_probe(dev, h2d, d2h, world, reps=2):
-    """The host link's rates for the end-to-end leg's byte counts: one pinned-host -> device copy of
-    `h2d` bytes alone, one device -> pinned-host copy of `d2h` bytes alone, and both at once on two
-    streams (CUDA events, best of `reps`, max over ranks). The end-to-end step cannot beat the
-    duplex time, so this says how much of the end-to-end figure is the box's link."""
+def host_link_probe(dev, h2d, d2h, world, reps=2, cap=128 << 20):
+    """The host link's rates for the end-to-end leg: pinned-host -> device copies alone, device ->
+    pinned-host copies alone, and both at once on two streams (CUDA events, best of `reps`, max over
+    ranks), each of min(bytes, `cap`) so that N ranks pin little extra host memory; `*_ms` are the
+    times the step's own byte counts take at those rates. The end-to-end step cannot beat the duplex
+    time, so this says how much of the end-to-end figure is the box's link."""
     import torch
     import torch.distributed as dist
-    hin = torch.empty(h2d, dtype=torch.uint8).pin_memory()
-    din = torch.empty(h2d, dtype=torch.uint8, device=dev)
-    hout = torch.empty(d2h, dtype=torch.uint8).pin_memory()
-    dout = torch.empty(d2h, dtype=torch.uint8, device=dev)
+    ph, pd = min(h2d, cap), min(d2h, cap)
+    hin = torch.empty(ph, dtype=torch.uint8).pin_memory()
+    din = torch.empty(ph, dtype=torch.uint8, device=dev)
+    hout = torch.empty(pd, dtype=torch.uint8).pin_memory()
+    dout = torch.empty(pd, dtype=torch.uint8, device=dev)
     s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     cur = torch.cuda.current_stream(dev)
 
@@ -595,10 +597,13 @@ def host_link_probe(dev, h2d, d2h, world, reps=2):
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
-        res[name + "_ms"] = round(ms, 3)
-    res["h2d_gbs"] = round(h2d / res["h2d_ms"] / 1e6, 1)
-    res["d2h_gbs"] = round(d2h / res["d2h_ms"] / 1e6, 1)
-    res["duplex_gbs"] = round((h2d + d2h) / res["duplex_ms"] / 1e6, 1)
+        moved = (ph if up else 0) + (pd if down else 0)
+        res[name + "_gbs"] = round(moved / ms / 1e6, 1)
+    # the step's bytes at those rates (the duplex rate applied to both directions together)
+    res["h2d_ms"] = round(h2d / res["h2d_gbs"] / 1e6, 3)
+    res["d2h_ms"] = round(d2h / res["d2h_gbs"] / 1e6, 3)
+    res["duplex_ms"] = round((h2d + d2h) / res["duplex_gbs"] / 1e6, 3)
+    res["probe_bytes"] = [ph, pd]
     del hin, din, hout, dout
     return res
 

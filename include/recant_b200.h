@@ -226,7 +226,7 @@ RB2_API int rb2_skinny_gemm(const void* A, int64_t lda, const void* B, int64_t M
 
 /* ---------------------------------------------------------------------------------------------
  * LoRA up-projection added to a base output: out[m, n] = y[m, n] + s * sum_k h[m, k] B[n, k] over
- * k < r (1 <= r <= 64), fp32 accumulation, rounded as the reference's ops round it on the GPU --
+ * k < r (1 <= r <= 128), fp32 accumulation, rounded as the reference's ops round it on the GPU --
  * mode 0: grouped_linear's torch.addmm(y, h, B^T, alpha=s) (recant/model/layers.py:86-97), which
  * cuBLAS computes as bf16(y + bf16(s * acc)); mode 1: QLinear.forward's y + (h B^T) * s
  * (layers.py:65-70), the product, its scaling and the sum each rounded to bf16. y, h, B, out bf16 with row strides ldy, ldh, ldb, ldo (multiples

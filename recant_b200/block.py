@@ -96,21 +96,21 @@ def lora_wgrad(d2, h, scale=1.0, transposed=False):
 
 def _up_ok(y2, h, b):
     """Operands as rb2_lora_up reads them: CUDA bf16 rows with unit column stride, row strides
-    multiples of 8 elements, 16-byte aligned bases, rank at most 64."""
+    multiples of 8 elements, 16-byte aligned bases, rank at most 128."""
     ts = (y2, h, b)
     return (all(t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0
                 and t.stride(0) >= t.shape[1] and t.data_ptr() % 16 == 0 for t in ts)
             and h.shape[0] == y2.shape[0] and b.shape[0] == y2.shape[1] and h.shape[1] == b.shape[1]
-            and 1 <= h.shape[1] <= 64)
+            and 1 <= h.shape[1] <= 128)
 
 
 def lora_up(y2, h, b, scale, mode):
     """y2 + scale (h b^T) on the library's tcgen05 kernel, rounded as the reference's ops round it on
     the GPU: ``mode`` 0 as torch.addmm(y2, h, b^T, alpha=scale) (layers.py:86-97; cuBLAS rounds the
     scaled product to bf16, then adds), 1 as QLinear's three bf16 ops (layers.py:65-70);
-    y2 [M, N], h [M, r], b [N, r] bf16, r <= 64. Returns a new [M, N] bf16 tensor."""
+    y2 [M, N], h [M, r], b [N, r] bf16, r <= 128. Returns a new [M, N] bf16 tensor."""
     if not _up_ok(y2, h, b):
-        raise ValueError("recant_b200.lora_up: needs CUDA bf16 [M, N], [M, r], [N, r] rows (r <= 64) with unit "
+        raise ValueError("recant_b200.lora_up: needs CUDA bf16 [M, N], [M, r], [N, r] rows (r <= 128) with unit "
                          "column stride, row strides a multiple of 8 elements and 16-byte aligned bases")
     M, n = y2.shape
     out = torch.empty(M, n, dtype=torch.bfloat16, device=y2.device)
@@ -179,6 +179,72 @@ class _XProjections(torch.autograd.Function):
             grads.append((d2[:, off:off + r].t() @ x2).float() if need[i] else None)
             off += r
         return (dx, None, *grads)
+
+
+class _InProj(torch.autograd.Function):
+    """The block's input projections of x as one function (layers.py:86-97, 154-155): the NVFP4
+    products of in_proj_qkv / in_proj_z from one activation quantize (as _FP4Group) and the narrow
+    projections [x W_b^T | x W_a^T | x A_i^T] from one pass over x (as _XProjections). Backward:
+    dx = sum_i Q(dy_i) dgrad_i^T + dproj [W_b; W_a; A_i], the second term added by rb2_lora_up in
+    one pass over the first (no [M, hidden] product of its own and no autograd add), and the LoRA
+    down-projections' dA_i as _XProjections computes them."""
+
+    @staticmethod
+    def forward(ctx, x, stochastic, w_frozen, weights, *As):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+        q = N.quantize_activation(x2, weights[0].use_rht)
+        ys = tuple(N._gemm_to(q, w.fprop, x.dtype).reshape(*x.shape[:-1], w.out_features) for w in weights)
+        W = torch.cat([w_frozen.to(torch.bfloat16)] + [a.to(torch.bfloat16) for a in As], 0).contiguous()
+        proj = narrow_product(x2, W)
+        ctx.save_for_backward(x2, W)
+        ctx.weights, ctx.stochastic, ctx.xshape = weights, stochastic, x.shape
+        ctx.n_frozen, ctx.ranks = w_frozen.shape[0], [a.shape[0] for a in As]
+        return (*ys, proj.reshape(*x.shape[:-1], W.shape[0]))
+
+    @staticmethod
+    def backward(ctx, *grads):
+        x2, W = ctx.saved_tensors
+        dys, dproj = grads[:-1], grads[-1]
+        need_dx = ctx.needs_input_grad[0]
+        dx = None
+        if need_dx:  # as the reference, no NVFP4 dgrad when x needs no gradient
+            for w, dy in zip(ctx.weights, dys):
+                if dy is None:
+                    continue
+                d = N.quantize_activation(dy.reshape(-1, w.out_features), w.use_rht, stochastic=ctx.stochastic)
+                part = N._gemm_to(d, w.dgrad, dy.dtype)
+                dx = part if dx is None else dx + part
+        gA = [None] * len(ctx.ranks)
+        if dproj is not None:
+            d2 = dproj.reshape(-1, dproj.shape[-1]).to(torch.bfloat16)
+            off = ctx.n_frozen
+            need = [ctx.needs_input_grad[4 + i] for i in range(len(ctx.ranks))]
+            dh_all = d2[:, off:off + sum(ctx.ranks)]
+            if any(need):
+                if LORA_WGRAD and _wgrad_ok(x2, dh_all):
+                    dA = lora_wgrad(x2, dh_all, 1.0, transposed=True)
+                    o = 0
+                    for i, r in enumerate(ctx.ranks):
+                        gA[i] = dA[o:o + r] if need[i] else None
+                        o += r
+                else:
+                    for i, r in enumerate(ctx.ranks):
+                        gA[i] = (d2[:, off:off + r].t() @ x2).float() if need[i] else None
+                        off += r
+            if need_dx:
+                wt = W.t().contiguous()  # [hidden, n]: the narrow weights as the up-projection's B
+                if dx is not None and _up_ok(dx, d2, wt):
+                    dx = lora_up(dx, d2, wt, 1.0, 1)
+                else:
+                    dx = d2 @ W if dx is None else dx + d2 @ W
+        return (None if dx is None else dx.reshape(ctx.xshape), None, None, None, *gA)
+
+
+# The block's input projections as one function (_InProj) when both in_proj_qkv and in_proj_z are
+# NVFP4; off, _FP4Group and _XProjections with autograd summing their input gradients.
+FUSED_IN_PROJ = True
 
 
 class _ConvSiLU(torch.autograd.Function):
@@ -618,19 +684,22 @@ class QLinear(nn.Module):
         return self.lora(x, y)
 
 
-def grouped_linear(x, lins, h=None):
+def grouped_linear(x, lins, h=None, base=None):
     """layers.py:72-97 with the activation quantized once for all NVFP4 members; the LoRA
     down-projections of all members come from one GEMM over x (x . cat(A_i)^T, as the reference's
     default path, layers.py:86-88), or are given as ``h`` (the members' x A_i^T side by side, e.g.
     from :class:`_XProjections`); each member's up-projection is one addmm as the reference's, or,
-    with the fused LoRA epilogue switched on, is added inside its NVFP4 GEMM (ranks 8 and 16)."""
+    with the fused LoRA epilogue switched on, is added inside its NVFP4 GEMM (ranks 8 and 16).
+    ``base``: the NVFP4 members' products of x, in order, when already computed."""
     if _fused_lora_ok(lins):
         ab = [t for l in lins for t in (l.lora_A, l.lora_B)]
         return list(_FP4LoRAGroup.apply(x, lins[0].stochastic_backward, 0, tuple(l.fp4 for l in lins),
                                         tuple(l.lora_scale for l in lins), *ab))
     fp4 = [l for l in lins if l.fp4 is not None]
     outs = {}
-    if fp4:
+    if base is not None:  # the NVFP4 products, already computed (by _InProj)
+        outs = {id(l): y for l, y in zip(fp4, base)}
+    elif fp4:
         ys = _FP4Group.apply(x, fp4[0].stochastic_backward, None, *[l.fp4 for l in fp4])
         outs = {id(l): y for l, y in zip(fp4, ys)}
     base = [outs[id(l)] if id(l) in outs else x @ l.weight.t() for l in lins]
@@ -738,10 +807,15 @@ class GDNBlock(nn.Module):
         if (dense_ba and not _fused_lora_ok(ins)
                 and _narrow_ok(x, 2 * self.Hv + sum(l.lora_A.shape[0] for l in lora_ins))):
             # one pass over x: b, a and the LoRA down-projections of in_proj_qkv / in_proj_z
-            proj = _XProjections.apply(x, torch.cat([self.in_proj_b.weight, self.in_proj_a.weight], 0),
-                                       *[l.lora_A for l in lora_ins])
+            wba = torch.cat([self.in_proj_b.weight, self.in_proj_a.weight], 0)
+            base = None
+            if FUSED_IN_PROJ and LORA_UP and all(l.fp4 is not None for l in ins):
+                *base, proj = _InProj.apply(x, ins[0].stochastic_backward, wba, tuple(l.fp4 for l in ins),
+                                            *[l.lora_A for l in lora_ins])
+            else:
+                proj = _XProjections.apply(x, wba, *[l.lora_A for l in lora_ins])
             b_lin, a = proj[..., :self.Hv], proj[..., self.Hv:2 * self.Hv]
-            qkv, z = grouped_linear(x, ins, h=proj[..., 2 * self.Hv:] if lora_ins else None)
+            qkv, z = grouped_linear(x, ins, h=proj[..., 2 * self.Hv:] if lora_ins else None, base=base)
         else:
             qkv, z = grouped_linear(x, ins)
             if dense_ba:  # one N = 2 Hv GEMM

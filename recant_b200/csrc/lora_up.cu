@@ -2,20 +2,24 @@
 // reference's ops round it.
 //
 // The LoRA term of the GDN block's projections (recant/model/layers.py:65-70, 86-97) is
-// y + (alpha / r) (h B^T) with h = x A^T [M, r] and B [N, r], r <= 64. torch runs it as one
+// y + (alpha / r) (h B^T) with h = x A^T [M, r] and B [N, r], r <= 128. torch runs it as one
 // addmm (grouped_linear's default, layers.py:86-97: mode 0) or as three bf16 ops (QLinear.forward,
 // layers.py:65-70: mode 1), which for out_proj read and write [M, N] bf16 tensors five times. Here
-// one pass reads y, writes out, and the K = r product runs on the tensor core:
+// one pass reads y, writes out, and the K = r product runs on the tensor core. The same pass also
+// adds a narrow product to another output: the block's input gradient, dx + dproj [W_b; W_a; A]
+// (r = 96), with mode 1 and s = 1.
+//
 //   mode 0: out = bf16(y + bf16(s * acc))                 (torch.addmm on the GPU: cuBLAS rounds the
 //                                                          scaled product to bf16 before adding y)
 //   mode 1: out = bf16(y + bf16(bf16(acc) * s))           (h B^T, * s, + y: three roundings)
 // with acc = sum_k h[m, k] B[n, k] in fp32. Both are bit-identical to the reference's ops run by
 // torch on a B200 (tests/test_lora_wgrad_gpu.py compares every element).
 //
-// One CTA (128 threads) per 128 x 128 output tile, three CTAs per SM. Thread 0 loads the tile's h
-// rows and B rows (one 64-column box each, columns past r zero-filled by TMA; 128-byte swizzle, no
-// multicast) and, on a second barrier, y's tile (two 64-column boxes); it issues ceil(r / 16)
-// tcgen05.mma (M = N = 128, K = 16, both operands K-major) as soon as h and B are in. Each thread
+// One CTA (128 threads) per 128 x 128 output tile, three CTAs per SM for r <= 64, two above. Thread
+// 0 loads the tile's h rows and B rows (one 64-column box each per 64 of r, columns past r
+// zero-filled by TMA; 128-byte swizzle, no multicast) and, on a second barrier, y's tile (two
+// 64-column boxes); it issues ceil(r / 16) tcgen05.mma (M = N = 128, K = 16, both operands K-major)
+// as soon as h and B are in. Each thread
 // then takes one output row: its accumulator columns from TMEM, y from the swizzled tile, the
 // result written back over y in shared memory, and the tile leaves by two TMA stores (rows and
 // columns past the tensor are clipped by TMA). Every mbarrier wait is bounded; a wait that runs out
@@ -26,10 +30,10 @@ namespace rb2 {
 namespace {
 
 constexpr int kTile = 128;
-constexpr int kHBytes = kTile * 128;          // h rows: 128 x 64 bf16 (one SW128 slab)
-constexpr int kBBytes = kTile * 128;          // B rows
-constexpr int kYBytes = 2 * kTile * 128;      // y / out tile: two 64-column slabs
-constexpr int kSmem = kHBytes + kBBytes + kYBytes + 1024;
+constexpr int kSlab = kTile * 128;            // 128 rows x 64 bf16: one SW128 slab of h, of B or of y
+constexpr int kYBytes = 2 * kSlab;            // y / out tile: two 64-column slabs
+constexpr int kMaxRank = 128;                 // h and B: one slab per 64 of r
+inline int smem_bytes(int nslab) { return 2 * nslab * kSlab + kYBytes + 1024; }
 constexpr size_t kStatusBytes = 256;
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -69,15 +73,16 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__global__ void __launch_bounds__(128, 3)
+__global__ void __launch_bounds__(128, 2)
 lora_up_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_b,
                const __grid_constant__ CUtensorMap map_y, const __grid_constant__ CUtensorMap map_out, int r,
                int n_tiles_n, float s, int mode, int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023);
+  const int nslab = (r + 63) / 64;
   unsigned char* th = sm;
-  unsigned char* tb = sm + kHBytes;
-  unsigned char* ty = tb + kBBytes;
+  unsigned char* tb = sm + nslab * kSlab;
+  unsigned char* ty = tb + nslab * kSlab;
   __shared__ uint64_t bar_hb, bar_y, bar_mma;
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
@@ -99,9 +104,11 @@ lora_up_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant_
   const uint32_t tbase = tmem_base;
   bool ok = true;
   if (tid == 0) {
-    tc::mbar_expect_tx(&bar_hb, uint32_t(kHBytes + kBBytes));
-    tma_load_2d(th, &map_h, 0, m0, &bar_hb);
-    tma_load_2d(tb, &map_b, 0, n0, &bar_hb);
+    tc::mbar_expect_tx(&bar_hb, uint32_t(2 * nslab * kSlab));
+    for (int j = 0; j < nslab; ++j) {
+      tma_load_2d(th + j * kSlab, &map_h, 64 * j, m0, &bar_hb);
+      tma_load_2d(tb + j * kSlab, &map_b, 64 * j, n0, &bar_hb);
+    }
     tc::mbar_expect_tx(&bar_y, uint32_t(kYBytes));
     tma_load_2d(ty, &map_y, n0, m0, &bar_y);
     tma_load_2d(ty + kYBytes / 2, &map_y, n0 + 64, m0, &bar_y);
@@ -110,8 +117,10 @@ lora_up_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant_
     if (ok) {
       constexpr uint32_t idesc = tc::idesc_bf16(kTile, kTile, false, false);
       const uint32_t sa = tc::smem_u32(th), sb = tc::smem_u32(tb);
-      for (int k = 0; k * 16 < r; ++k)  // 16 k = 32 bytes along a swizzled row
-        tc::mma_bf16(tbase, tc::desc_kmajor_sw128(sa + 32 * k), tc::desc_kmajor_sw128(sb + 32 * k), idesc, k > 0);
+      for (int k = 0; k * 16 < r; ++k) {  // 16 k = 32 bytes along a swizzled row; 64 k per slab
+        const uint32_t off = uint32_t((k >> 2) * kSlab + (k & 3) * 32);
+        tc::mma_bf16(tbase, tc::desc_kmajor_sw128(sa + off), tc::desc_kmajor_sw128(sb + off), idesc, k > 0);
+      }
     }
     tc::mma_commit(&bar_mma);
   }
@@ -178,7 +187,7 @@ extern "C" int rb2_lora_up(const void* y, int64_t ldy, const void* h, int64_t ld
   RB2_CHECK_ARG(ws, "lora_up: null workspace");
   RB2_CHECK_ARG(M >= 0 && M < (int64_t(1) << 31) && N > 0 && N < (int64_t(1) << 31),
                 "lora_up: need 0 <= M < 2^31 and 0 < N < 2^31 (M=%lld N=%lld)", (long long)M, (long long)N);
-  RB2_CHECK_ARG(r >= 1 && r <= 64, "lora_up: rank must be in [1, 64] (r=%d)", r);
+  RB2_CHECK_ARG(r >= 1 && r <= kMaxRank, "lora_up: rank must be in [1, 128] (r=%d)", r);
   RB2_CHECK_ARG(mode == 0 || mode == 1, "lora_up: mode must be 0 (addmm) or 1 (three ops)");
   RB2_CHECK_ARG(ws_bytes >= kStatusBytes && (reinterpret_cast<uintptr_t>(ws) & 15) == 0,
                 "lora_up: workspace of at least %zu bytes, 16-byte aligned", kStatusBytes);
@@ -200,14 +209,15 @@ extern "C" int rb2_lora_up(const void* y, int64_t ldy, const void* h, int64_t ld
     return rc;
   const int64_t tn = (N + kTile - 1) / kTile, tm = (M + kTile - 1) / kTile;
   RB2_CHECK_ARG(tn * tm < (int64_t(1) << 31), "lora_up: too many tiles");
-  cudaError_t e = cudaFuncSetAttribute(lora_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  const int smem = smem_bytes((r + 63) / 64);
+  cudaError_t e = cudaFuncSetAttribute(lora_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(2));
   if (e != cudaSuccess) {
     set_error("lora_up: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     return RB2_ECUDA;
   }
   {
     ProfScope ps_("lora_up", s);
-    lora_up_kernel<<<unsigned(tn * tm), 128, kSmem, s>>>(mh, mb, my, mo, r, int(tn), scale, mode, err);
+    lora_up_kernel<<<unsigned(tn * tm), 128, smem, s>>>(mh, mb, my, mo, r, int(tn), scale, mode, err);
   }
   RB2_CHECK_LAUNCH("lora_up");
   return RB2_OK;

@@ -171,8 +171,8 @@ def test_block_backward_split_at_the_in_proj_dgrad(monkeypatch):
     kept = {}
     gl, gg = BM.grouped_linear, BM.gdn_gates
 
-    def grouped_kept(x_, lins, h=None):
-        out = gl(x_, lins, h=h)
+    def grouped_kept(x_, lins, h=None, base=None):
+        out = gl(x_, lins, h=h, base=base)
         for t in out:
             t.retain_grad()
         kept["qkv"], kept["z"] = out

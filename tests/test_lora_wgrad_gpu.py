@@ -120,7 +120,8 @@ def _up_reference(y, h, b, s, mode):
 
 
 @pytest.mark.parametrize("M,N,r,mode", [(16384, 4096, 16, 1), (16384, 8192, 16, 0), (1000, 200, 32, 1),
-                                        (77, 136, 8, 0), (129, 4096, 64, 1), (300, 256, 48, 0)])
+                                        (77, 136, 8, 0), (129, 4096, 64, 1), (300, 256, 48, 0),
+                                        (4096, 4096, 96, 1), (300, 256, 128, 0)])
 def test_lora_up_matches_reference_ops(M, N, r, mode):
     """rb2_lora_up against the reference's ops on the same bf16 operands: mode 1 (QLinear's three
     ops) and mode 0 (grouped_linear's addmm, which cuBLAS computes as bf16(y + bf16(s acc))) equal a
