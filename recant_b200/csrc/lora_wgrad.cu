@@ -6,18 +6,20 @@
 //   dA = (x^T dh)^T    (D = x [M, in],   H = dh [M, r];       autograd of x A^T)
 // with r <= 64. Each is bound by reading D once (M x N bf16); H is M x r and mostly comes from L2.
 //
-// One CTA (128 threads) per (128 columns of D, split of the tokens). Thread 0 streams 64-token
-// stages by TMA (two 64 x 64 boxes of D, one 64 x 64 box of H, 128-byte swizzle, no multicast)
-// through a 4-stage ring; thread 32 issues four tcgen05.mma (M = 128 columns n, N = 64 columns r,
-// K = 16 tokens) per stage with both operands MN-major -- the tiles land token-major, as D and H
-// are stored, and are read transposed by the descriptors, so nothing is transposed in memory. The
-// fp32 accumulator (TMEM lanes = n, columns = r) goes to a per-split partial in the workspace; the
-// last split of a column tile to arrive (an atomic counter per tile) sums the tile's partials in split
-// order (deterministic) and rounds as the reference does: the bf16 product, then times s in bf16,
-// stored as fp32 (the fp32 parameter's gradient through its bf16 cast, layers.py:69, 86, 95). The
-// splits fill at most one wave of two CTAs per SM. Columns of H past r, and tokens past M, read as
-// zero (TMA fill). Every mbarrier wait is bounded; a wait that runs out writes its code to the status
-// word (the first 4 bytes of the workspace) and the kernel finishes.
+// One CTA (128 threads) per (256 columns of D, split of the tokens), one CTA per SM. Thread 0 streams
+// 64-token stages by TMA (four 64 x 64 boxes of D -- 512-byte runs of each row, which the DRAM
+// pages serve better than 256-byte ones -- and one 64 x 64 box of H; 128-byte swizzle, no multicast)
+// through a 4-stage ring; thread 32 issues, per stage and per 128-column half, four tcgen05.mma
+// (M = 128 columns n, N = 64 columns r, K = 16 tokens) with both operands MN-major -- the tiles
+// land token-major, as D and H are stored, and are read transposed by the descriptors, so nothing
+// is transposed in memory. The fp32 accumulators (TMEM lanes = n, 64 columns per half) go to a
+// per-split partial in the workspace; the last split of a column tile to arrive (an atomic counter
+// per tile) sums the tile's partials in split order (deterministic) and rounds as the reference
+// does: the bf16 product, then times s in bf16, stored as fp32 (the fp32 parameter's gradient
+// through its bf16 cast, layers.py:69, 86, 95). The splits fill at most one wave. Columns of H
+// past r, and tokens past M, read as zero (TMA fill). Every mbarrier wait is bounded; a wait that
+// runs out writes its code to the status word (the first 4 bytes of the workspace) and the kernel
+// finishes.
 #include "tmap.cuh"
 
 namespace rb2 {
@@ -25,11 +27,13 @@ namespace {
 
 constexpr int kTok = 64;                      // tokens per stage
 constexpr int kStages = 4;
-constexpr int kDBytes = 2 * 64 * 128;         // D: two 64-column slabs of 64 token rows
+constexpr int kHalves = 2;                    // 128-column halves of a tile: 256 columns of D per CTA
+constexpr int kTileN = 128 * kHalves;
+constexpr int kDBytes = kHalves * 2 * 64 * 128;  // D: four 64-column slabs of 64 token rows
 constexpr int kHBytes = 64 * 128;             // H: one 64-column slab
 constexpr int kStageBytes = kDBytes + kHBytes;
 constexpr int kSmem = kStages * kStageBytes + 1024;
-constexpr int kCols = 64;                     // accumulator columns (r padded to 64)
+constexpr int kCols = 64;                     // accumulator columns per half (r padded to 64)
 constexpr size_t kStatusBytes = 256;
 constexpr int kMaxSplits = 16;                // token splits per column tile, at most
 
@@ -68,7 +72,7 @@ __device__ __forceinline__ float finish(float acc, float s) {
   return __bfloat162float(__float2bfloat16_rn(p * s));
 }
 
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(128, 1)
 lora_wgrad_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_constant__ CUtensorMap map_h, int M, int N,
                   int R, int tok_per_split, int n_tiles, int n_splits, float s, float* __restrict__ partial,
                   int* __restrict__ arrivals, float* __restrict__ out, int64_t ld_n, int64_t ld_r,
@@ -80,12 +84,12 @@ lora_wgrad_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_consta
   __shared__ int last;
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
   const int tile = int(blockIdx.x) % n_tiles, split = int(blockIdx.x) / n_tiles;
-  const int n0 = tile * 128, m0 = split * tok_per_split;
+  const int n0 = tile * kTileN, m0 = split * tok_per_split;
   const int m1 = min(M, m0 + tok_per_split);
   const int nk = (m1 - m0 + kTok - 1) / kTok;  // >= 1: the host sizes the splits so that none is empty
 
   if (w == 0) {
-    tc::tmem_alloc(&tmem_base, kCols);
+    tc::tmem_alloc(&tmem_base, kCols * kHalves);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
@@ -107,8 +111,8 @@ lora_wgrad_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_consta
       unsigned char* b = sm + st * kStageBytes;
       const int y = m0 + kt * kTok;
       tc::mbar_expect_tx(&full[st], uint32_t(kStageBytes));
-      tma_load_2d(b, &map_d, n0, y, &full[st]);
-      tma_load_2d(b + kDBytes / 2, &map_d, n0 + 64, y, &full[st]);
+#pragma unroll
+      for (int j = 0; j < 2 * kHalves; ++j) tma_load_2d(b + j * 8192, &map_d, n0 + 64 * j, y, &full[st]);
       tma_load_2d(b + kDBytes, &map_h, 0, y, &full[st]);
     }
   } else if (tid == 32) {  // MMA issuer: C[n][r] += D^T H over 16 tokens per instruction
@@ -118,11 +122,17 @@ lora_wgrad_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_consta
       if (!tc::mbar_wait(&full[st], (kt / kStages) & 1, err, 402)) break;
       tc::fence_after_sync();
       const uint32_t sa = tc::smem_u32(sm + st * kStageBytes), sb = sa + uint32_t(kDBytes);
-      // MN-major operands: the two 64-column slabs of D are 8 KB apart (LBO); 16 tokens = 2 KB
-      const uint64_t da = tc::desc_mnmajor_sw128(sa, kDBytes / 2), db = tc::desc_mnmajor_sw128(sb, kHBytes);
+      // MN-major operands: a half's two 64-column slabs of D are 8 KB apart (LBO); 16 tokens = 2 KB;
+      // half hv accumulates in TMEM columns 64 hv ..
+      const uint64_t db = tc::desc_mnmajor_sw128(sb, kHBytes);
 #pragma unroll
-      for (int kk = 0; kk < kTok / 16; ++kk)
-        tc::mma_bf16(tbase, da + uint64_t(kk * 128), db + uint64_t(kk * 128), idesc, kt > 0 || kk > 0);
+      for (int hv = 0; hv < kHalves; ++hv) {
+        const uint64_t da = tc::desc_mnmajor_sw128(sa + uint32_t(hv * 16384), 8192);
+#pragma unroll
+        for (int kk = 0; kk < kTok / 16; ++kk)
+          tc::mma_bf16(tbase + uint32_t(kCols * hv), da + uint64_t(kk * 128), db + uint64_t(kk * 128), idesc,
+                       kt > 0 || kk > 0);
+      }
       tc::mma_commit(&empty[st]);
     }
     tc::mma_commit(&done);
@@ -130,29 +140,32 @@ lora_wgrad_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_consta
   __syncwarp();
   const bool ok = tc::mbar_wait(&done, 0, err, 403);
   tc::fence_after_sync();
-  // warp w holds TMEM lanes 32 w .. 32 w + 31: column n = n0 + 32 w + l of D, 64 accumulator columns
-  const int n = n0 + 32 * w + l;
-  const int64_t npad = int64_t(n_tiles) * 128;
+  // warp w holds TMEM lanes 32 w .. 32 w + 31: column n0 + 128 hv + 32 w + l of D in half hv
+  const int64_t npad = int64_t(n_tiles) * kTileN;
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    float v[32];
-    tc::tmem_ld32(tbase + (uint32_t(32 * w) << 16) + uint32_t(32 * half), v);
-    if (!ok) continue;
-    if (partial) {
-      float4* p = reinterpret_cast<float4*>(partial + (int64_t(split) * npad + n) * kCols + 32 * half);
+  for (int hv = 0; hv < kHalves; ++hv) {
+    const int n = n0 + 128 * hv + 32 * w + l;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else if (n < N) {  // a single split: finish here
+    for (int half = 0; half < 2; ++half) {
+      float v[32];
+      tc::tmem_ld32(tbase + (uint32_t(32 * w) << 16) + uint32_t(kCols * hv + 32 * half), v);
+      if (!ok) continue;
+      if (partial) {
+        float4* p = reinterpret_cast<float4*>(partial + (int64_t(split) * npad + n) * kCols + 32 * half);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int r = 32 * half + j;
-        if (r < R) out[int64_t(n) * ld_n + int64_t(r) * ld_r] = finish(v[j], s);
+        for (int j = 0; j < 8; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      } else if (n < N) {  // a single split: finish here
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int r = 32 * half + j;
+          if (r < R) out[int64_t(n) * ld_n + int64_t(r) * ld_r] = finish(v[j], s);
+        }
       }
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (w == 0) tc::tmem_dealloc(tbase, kCols);
+  if (w == 0) tc::tmem_dealloc(tbase, kCols * kHalves);
   if (!partial) return;
   // The last split of this column tile to finish sums all splits' partials, in split order (so the
   // result does not depend on which CTA came last), and writes the tile's output columns.
@@ -162,33 +175,36 @@ lora_wgrad_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_consta
   __syncthreads();
   if (!last) return;
   __threadfence();
-  if (n >= N) return;
-  // all splits' partials of two 4-column groups in flight at once (independent loads), then summed in
-  // split order: a serial load-add chain over the splits would add one L2 round trip per partial
-  for (int r8 = 0; r8 < R; r8 += 8) {
-    float4 v[2][kMaxSplits];
+  for (int hv = 0; hv < kHalves; ++hv) {
+    const int n = n0 + 128 * hv + 32 * w + l;
+    if (n >= N) break;
+    // all splits' partials of two 4-column groups in flight at once (independent loads), then summed
+    // in split order: a serial load-add chain over the splits would add one L2 round trip per partial
+    for (int r8 = 0; r8 < R; r8 += 8) {
+      float4 v[2][kMaxSplits];
 #pragma unroll
-    for (int g = 0; g < 2; ++g)
+      for (int g = 0; g < 2; ++g)
 #pragma unroll
-      for (int sp = 0; sp < kMaxSplits; ++sp)
-        if (sp < n_splits && r8 + 4 * g < R)
-          v[g][sp] = __ldcg(reinterpret_cast<const float4*>(partial + (int64_t(sp) * npad + n) * kCols + r8 + 4 * g));
+        for (int sp = 0; sp < kMaxSplits; ++sp)
+          if (sp < n_splits && r8 + 4 * g < R)
+            v[g][sp] = __ldcg(reinterpret_cast<const float4*>(partial + (int64_t(sp) * npad + n) * kCols + r8 + 4 * g));
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int g = 0; g < 2; ++g) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int sp = 0; sp < kMaxSplits; ++sp)
-        if (sp < n_splits) {
-          acc.x += v[g][sp].x;
-          acc.y += v[g][sp].y;
-          acc.z += v[g][sp].z;
-          acc.w += v[g][sp].w;
+        for (int sp = 0; sp < kMaxSplits; ++sp)
+          if (sp < n_splits) {
+            acc.x += v[g][sp].x;
+            acc.y += v[g][sp].y;
+            acc.z += v[g][sp].z;
+            acc.w += v[g][sp].w;
+          }
+        const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = r8 + 4 * g + j;
+          if (r < R) out[int64_t(n) * ld_n + int64_t(r) * ld_r] = finish(a[j], s);
         }
-      const float a[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = r8 + 4 * g + j;
-        if (r < R) out[int64_t(n) * ld_n + int64_t(r) * ld_r] = finish(a[j], s);
       }
     }
   }
@@ -203,12 +219,12 @@ __global__ void lora_wgrad_zero_kernel(int N, int R, float s, float* __restrict_
   }
 }
 
-// Token splits: as many as fit in one wave of two CTAs on each of B200's 148 SMs (a second, partial
+// Token splits: as many as fit in one wave of one CTA on each of B200's 148 SMs (a second, partial
 // wave would nearly double the time of a bandwidth-bound pass), whole 64-token stages per split.
 void plan(int64_t M, int64_t N, int* n_tiles, int* n_splits, int* tok_per_split) {
-  *n_tiles = int((N + 127) / 128);
+  *n_tiles = int((N + kTileN - 1) / kTileN);
   const int64_t stages = (M + kTok - 1) / kTok;
-  int want = (2 * 148) / *n_tiles;
+  int want = 148 / *n_tiles;
   if (want > kMaxSplits) want = kMaxSplits;
   if (want < 1) want = 1;
   if (want > stages) want = int(stages);
@@ -229,7 +245,7 @@ extern "C" size_t rb2_lora_wgrad_workspace_size(int64_t M, int64_t N, int R) {
   plan(M, N, &n_tiles, &n_splits, &tok);
   if (n_splits == 1) return kStatusBytes;
   const size_t counters = (size_t(n_tiles) * sizeof(int) + 255) & ~size_t(255);
-  return kStatusBytes + counters + size_t(n_splits) * size_t(n_tiles) * 128 * kCols * sizeof(float);
+  return kStatusBytes + counters + size_t(n_splits) * size_t(n_tiles) * kTileN * kCols * sizeof(float);
 }
 
 extern "C" int rb2_lora_wgrad(const void* D, int64_t ldd, const void* H, int64_t ldh, int64_t M, int64_t N, int R,
