@@ -175,3 +175,44 @@ def test_quantizer_index_tables_follow_from_the_e2m1_grid():
             assert rn[k_rn] == sum(a > m for m in mids)
             k_sr = min(max(key(a), 504), 518) - 504
             assert sr[k_sr] == max(sum(a > g for g in grid[:7]), 1)
+
+
+def test_lora_wgrad_workspace_and_argument_checks():
+    """rb2_lora_wgrad: the workspace holds the status word, the tiles' counters and the per-split
+    partials (growing with N); bad ranks, strides, alignment and short workspaces are refused
+    before any CUDA call."""
+    lib = L.lib()
+    assert lib.rb2_lora_wgrad_workspace_size(0, 4096, 16) == 256
+    small = lib.rb2_lora_wgrad_workspace_size(16384, 4096, 16)
+    big = lib.rb2_lora_wgrad_workspace_size(16384, 8192, 16)
+    assert 256 < small < big
+    p, ws = C.c_void_p(4096), C.c_void_p(1 << 20)
+    args = dict(ldd=256, ldh=16, M=128, N=256, R=16)
+
+    def call(ws_bytes=1 << 30, **kw):
+        a = {**args, **kw}
+        return lib.rb2_lora_wgrad(p, a["ldd"], p, a["ldh"], a["M"], a["N"], a["R"], 1.0, p, a["R"], 1, ws, ws_bytes,
+                                  None)
+
+    assert call(R=0) == L.EINVAL and b"rank" in lib.rb2_last_error()
+    assert call(R=65) == L.EINVAL
+    assert call(ldd=250) == L.EINVAL and b"strides" in lib.rb2_last_error()
+    assert call(ws_bytes=16) == L.EINVAL and b"workspace" in lib.rb2_last_error()
+    assert lib.rb2_lora_wgrad(C.c_void_p(4100), 256, p, 16, 128, 256, 16, 1.0, p, 16, 1, ws, 1 << 30,
+                              None) == L.EINVAL
+
+
+def test_lora_up_argument_checks():
+    """rb2_lora_up refuses ranks outside [1, 128], unknown rounding modes and a short workspace before
+    any CUDA call."""
+    lib = L.lib()
+    assert lib.rb2_lora_up_workspace_size() >= 4
+    p, ws = C.c_void_p(4096), C.c_void_p(1 << 20)
+
+    def call(r=16, mode=0, ws_bytes=256):
+        return lib.rb2_lora_up(p, 256, p, 16, p, 16, 128, 256, r, 2.0, mode, p, 256, ws, ws_bytes, None)
+
+    assert call(r=0) == L.EINVAL and b"rank" in lib.rb2_last_error()
+    assert call(r=129) == L.EINVAL
+    assert call(mode=2) == L.EINVAL and b"mode" in lib.rb2_last_error()
+    assert call(ws_bytes=8) == L.EINVAL and b"workspace" in lib.rb2_last_error()
